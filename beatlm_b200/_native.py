@@ -1,0 +1,89 @@
+"""ctypes binding of ``libbeatlm_b200.so`` (the C ABI in
+``include/beatlm_b200.h``).
+
+The library is loaded from this directory only; there is no fallback: if it
+is missing or fails to load, every call raises. Build it with
+``python -m beatlm_b200.build``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libbeatlm_b200.so")
+
+BL_OK = 0
+BL_F32, BL_F16, BL_BF16 = 0, 1, 2
+
+_lock = threading.Lock()
+_lib = None
+
+
+class BackendError(RuntimeError):
+    """A C-ABI call returned a non-zero status."""
+
+    def __init__(self, code: int, message: str):
+        super().__init__("beatlm_b200 error %d: %s" % (code, message))
+        self.code = code
+
+
+class AttentionArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_uint32), ("tokens", ctypes.c_uint32), ("heads", ctypes.c_uint32),
+        ("head_dim", ctypes.c_uint32), ("head_begin", ctypes.c_uint32),
+        ("head_end", ctypes.c_uint32), ("row_begin", ctypes.c_uint32),
+        ("row_end", ctypes.c_uint32), ("scale", ctypes.c_float), ("qk_dtype", ctypes.c_int32),
+        ("v_dtype", ctypes.c_int32), ("out_dtype", ctypes.c_int32), ("qkv", ctypes.c_void_p),
+        ("qkv_row_stride", ctypes.c_uint64), ("out", ctypes.c_void_p),
+        ("out_row_stride", ctypes.c_uint64), ("out_head_base", ctypes.c_uint32),
+    ]
+
+
+class Status(ctypes.Structure):
+    _fields_ = [("code", ctypes.c_uint32), ("block", ctypes.c_uint32),
+                ("where", ctypes.c_uint32), ("count", ctypes.c_uint32)]
+
+
+# name -> (restype, argtypes), every symbol include/beatlm_b200.h declares.
+SIGNATURES = {
+    "bl_last_error": (ctypes.c_size_t, [ctypes.c_char_p, ctypes.c_size_t]),
+    "bl_version": (ctypes.c_char_p, []),
+    "bl_status": (ctypes.c_int, [ctypes.POINTER(Status), ctypes.c_int]),
+    "bl_attention": (ctypes.c_int, [ctypes.POINTER(AttentionArgs), ctypes.c_void_p]),
+}
+
+
+def lib():
+    """The loaded library (raises if it is missing)."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise ImportError("beatlm_b200: %s is missing; build it with "
+                                  "`python -m beatlm_b200.build`" % LIB_PATH)
+            L = ctypes.CDLL(LIB_PATH)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(L, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    buf = ctypes.create_string_buffer(1024)
+    lib().bl_last_error(buf, len(buf))
+    return buf.value.decode(errors="replace")
+
+
+def check(rc: int) -> None:
+    if rc != BL_OK:
+        raise BackendError(rc, last_error())
+
+
+def status(reset: bool = False) -> Status:
+    s = Status()
+    check(lib().bl_status(ctypes.byref(s), 1 if reset else 0))
+    return s

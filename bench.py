@@ -1,0 +1,305 @@
+#!/usr/bin/env python
+"""Benchmark of the ViT attention hot path on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload attention]
+
+Workloads (synthetic data, seeded):
+  attention  config 1: one ViT-S self-attention op, batch 1, 6 heads x 64,
+             1370 tokens, Q/K/V ~ N(0,1), scale 1/8; f16 Q/K/V, f32 output.
+
+A step is one pass of the hot path over one batch. `value` is whole-job
+throughput (all ranks) with the inputs resident in HBM; L2 is flushed (a
+256 MiB write) before every timed launch and the flush is outside the timed
+events. `e2e` is the same metric through the public call with host buffers:
+the H2D copy of the packed Q/K/V from pinned memory and the D2H copy of the
+output are inside its timed region. Multi-GPU: one process per GPU (torchrun),
+replicas only (config 1 does not shard), times are the max over ranks.
+
+`--impl reference` times the reference's CPU path (the C restatement of its
+f64 interpreter, oracle/, all host threads) on the same workload, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "ViT attention TFLOP/s (% of B200 bf16 peak); DA-V2-S 518² encoder frames/s"
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons during timing."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.FIELDS,
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.summary = {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        if self.proc is None:
+            return
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [r.split(", ") for r in out.strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return
+        sm = sorted(float(r[1]) for r in rows)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4)
+                          if r[5 + i].strip().lower() == "active"})
+        self.summary = {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": float(rows[0][2]),
+                        "reasons": reasons, "samples": len(rows)}
+
+
+# ------------------------------------------------------------------ workloads
+
+class AttentionWorkload:
+    """Config 1: one ViT-S attention op (T=1370, H=6, hd=64), batch 1."""
+
+    name = "attention"
+
+    def __init__(self, rank: int, batch: int = 1):
+        import numpy as np
+        import torch
+        import beatlm_b200 as bl
+        self.bl = bl
+        self.t, self.h, self.batch = 1370, 6, batch
+        rng = np.random.default_rng(1234 + rank)
+        qkv = rng.standard_normal((batch, self.t, 3, self.h, 64), dtype=np.float32)
+        self.dev = bl.pack_qkv(qkv, "f16")
+        self.host = self.dev.cpu().pin_memory()
+        self.out = torch.empty((batch, self.t, self.h * 64), dtype=torch.float32, device="cuda")
+        self.out_host = torch.empty(self.out.shape, dtype=torch.float32).pin_memory()
+        self.flops = 4.0 * self.t * self.t * self.h * 64 * batch
+        self.unit_bytes = self.dev.numel() * 2 + self.out.numel() * 4
+        self.launches_per_step = 1
+
+    def config(self):
+        return {"workload": "vit_s_attention_op (config 1)", "batch": self.batch,
+                "tokens": self.t, "heads": self.h, "head_dim": 64,
+                "qkv_dtype": "f16", "out_dtype": "f32",
+                "l2": "flushed before every timed launch (256 MiB write)"}
+
+    def step(self, stream):
+        self.bl.attention(self.dev, tokens=self.t, heads=self.h, batch=self.batch,
+                          out=self.out, stream=stream)
+
+    def step_e2e(self, stream):
+        self.dev.copy_(self.host, non_blocking=True)
+        self.step(stream)
+        self.out_host.copy_(self.out, non_blocking=True)
+
+    def e2e_bytes(self):
+        return self.host.numel() * 2, self.out_host.numel() * 4
+
+    def units(self):
+        return self.flops / 1e12  # TFLOP per step
+
+    def cpu_baseline(self, threads: int, budget_s: float = 15.0):
+        """The reference's CPU path (oracle/, a C restatement of
+        reference.rs:437-494) on a bounded sample of query rows."""
+        import torch
+        import oracle
+        t, h = self.t, self.h
+        qkv = self.host[0].view(torch.float16).float().numpy().reshape(t, -1)
+        rows = 64
+        t0 = time.perf_counter()
+        oracle.attention(qkv, t, h, 64, rows=(0, rows), threads=threads)
+        dt = time.perf_counter() - t0
+        rows = int(min(t, max(rows, rows * budget_s / max(dt, 1e-6) / 4)))
+        t0 = time.perf_counter()
+        n = 0
+        while time.perf_counter() - t0 < budget_s / 2 or n == 0:
+            oracle.attention(qkv, t, h, 64, rows=(0, rows), threads=threads)
+            n += 1
+        dt = time.perf_counter() - t0
+        flops = 4.0 * rows * t * h * 64 * n
+        return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                "sample": "%d of %d query rows x %d heads, %d repeats (f64 accumulation, "
+                          "oracle/oracle.c)" % (rows, t, h, n)}
+
+
+WORKLOADS = {"attention": AttentionWorkload}
+
+
+# ------------------------------------------------------------------ timing
+
+def time_device(fn, steps, warmup, stream, flush):
+    import torch
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            flush.zero_()
+            fn(stream)
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    with torch.cuda.stream(stream):
+        for i in range(steps):
+            flush.zero_()
+            starts[i].record(stream)
+            fn(stream)
+            ends[i].record(stream)
+    torch.cuda.synchronize()
+    return [s.elapsed_time(e) for s, e in zip(starts, ends)]
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="attention", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-cpu-baseline", action="store_true",
+                    help="skip the cpu_baseline leg (profiling runs)")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        return run_reference(args, world, rank)
+
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    wl = WORKLOADS[args.workload](rank)
+    stream = torch.cuda.Stream()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # device-resident timing
+    barrier()
+    with Clocks(local) as clk:
+        times = time_device(wl.step, args.steps, args.warmup, stream, flush)
+    barrier()
+    total_ms = sum(times)
+    # e2e through the public call with host buffers
+    barrier()
+    e2e_times = time_device(wl.step_e2e, args.steps, args.warmup, stream, flush)
+    barrier()
+    e2e_ms = sum(e2e_times)
+    if world > 1:
+        t = torch.tensor([total_ms, e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms, e2e_ms = float(t[0]), float(t[1])
+    value = wl.units() * args.steps * world / (total_ms / 1e3)
+    e2e_value = wl.units() * args.steps * world / (e2e_ms / 1e3)
+
+    if rank == 0:
+        pk = peaks()
+        avg_ms = total_ms / args.steps
+        achieved = wl.flops / (avg_ms / 1e3) / 1e12
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(avg_ms, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16 (Q/K/V, P); f32 accumulate", "data": "synthetic N(0,1), seeded",
+            "config": dict(wl.config(), parallelism="replicas x%d" % world),
+            "e2e": {"value": round(e2e_value, 3), "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": wl.e2e_bytes()[0],
+                    "d2h_bytes_per_step": wl.e2e_bytes()[1]},
+            "gpu_launches": wl.launches_per_step * args.steps,
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 2),
+                         "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": round(achieved / pk["bf16_tflops"], 4),
+                         "peak_source": pk["source"] + " (burst bf16, MEASURED_PEAKS.json)",
+                         "traffic": None, "kernel": "bl::attn::attention_fwd"},
+            "clocks": clk.summary,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = wl.cpu_baseline(threads=os.cpu_count() or 1)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_reference(args, world, rank):
+    """The reference's CPU implementation of the path (the oracle port; the
+    Rust reference has no toolchain here), all host threads, rank 0 only."""
+    if rank != 0:
+        return
+    import numpy as np
+    import oracle
+    threads = os.cpu_count() or 1
+    t, h = 1370, 6
+    rng = np.random.default_rng(1234)
+    qkv = oracle.round_f16(rng.standard_normal((t, 3 * h * 64), dtype=np.float32))
+    # bound each step to about 1 s of CPU work
+    rows = 32
+    t0 = time.perf_counter()
+    oracle.attention(qkv, t, h, 64, rows=(0, rows), threads=threads)
+    per_row = (time.perf_counter() - t0) / rows
+    rows = int(max(16, min(t, 1.0 / max(per_row, 1e-9))))
+    for _ in range(1):
+        oracle.attention(qkv, t, h, 64, rows=(0, rows), threads=threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.attention(qkv, t, h, 64, rows=(0, rows), threads=threads)
+    dt = time.perf_counter() - t0
+    flops = 4.0 * rows * t * h * 64 * args.steps
+    value = flops / dt / 1e12
+    line = {"metric": METRIC, "impl": "reference", "value": value, "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f64 accumulate, f32 storage",
+            "data": "synthetic N(0,1), seeded",
+            "config": {"workload": "vit_s_attention_op (config 1)", "tokens": t, "heads": h,
+                       "head_dim": 64},
+            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads,
+                             "kind": "port",
+                             "sample": "%d of %d query rows x %d heads per step" % (rows, t, h)},
+            "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()
