@@ -87,3 +87,45 @@ def status(reset: bool = False) -> Status:
     s = Status()
     check(lib().bl_status(ctypes.byref(s), 1 if reset else 0))
     return s
+
+
+class GemmArgs(ctypes.Structure):
+    _fields_ = [
+        ("m", ctypes.c_uint32), ("n", ctypes.c_uint32), ("k", ctypes.c_uint32),
+        ("ab_dtype", ctypes.c_int32), ("a", ctypes.c_void_p), ("lda", ctypes.c_uint64),
+        ("b", ctypes.c_void_p), ("ldb", ctypes.c_uint64), ("ln_x", ctypes.c_void_p),
+        ("ln_ldx", ctypes.c_uint64), ("ln_gamma", ctypes.c_void_p), ("ln_beta", ctypes.c_void_p),
+        ("ln_eps", ctypes.c_float), ("bias", ctypes.c_void_p), ("act", ctypes.c_int32),
+        ("scale", ctypes.c_float), ("chan_scale", ctypes.c_void_p), ("residual", ctypes.c_void_p),
+        ("res_dtype", ctypes.c_int32), ("res_ld", ctypes.c_uint64), ("res_period", ctypes.c_uint32),
+        ("out", ctypes.c_void_p), ("out_dtype", ctypes.c_int32), ("out_ld", ctypes.c_uint64),
+        ("split_col", ctypes.c_uint32), ("out_dtype_hi", ctypes.c_int32),
+        ("out_row_offset", ctypes.c_uint32), ("out_group_rows", ctypes.c_uint32),
+        ("out_group_gap", ctypes.c_uint32), ("tile_n", ctypes.c_uint32),
+    ]
+
+
+class LayerNormArgs(ctypes.Structure):
+    _fields_ = [
+        ("rows", ctypes.c_uint32), ("cols", ctypes.c_uint32), ("x", ctypes.c_void_p),
+        ("ldx", ctypes.c_uint64), ("gamma", ctypes.c_void_p), ("beta", ctypes.c_void_p),
+        ("eps", ctypes.c_float), ("out", ctypes.c_void_p), ("out_dtype", ctypes.c_int32),
+        ("ldo", ctypes.c_uint64), ("in_row_offset", ctypes.c_uint32),
+        ("in_group_rows", ctypes.c_uint32), ("in_group_gap", ctypes.c_uint32),
+    ]
+
+
+class PatchifyArgs(ctypes.Structure):
+    _fields_ = [
+        ("frames", ctypes.c_uint32), ("side", ctypes.c_uint32), ("patch", ctypes.c_uint32),
+        ("cin", ctypes.c_uint32), ("k_pad", ctypes.c_uint32), ("dim", ctypes.c_uint32),
+        ("image", ctypes.c_void_p), ("a", ctypes.c_void_p), ("a_dtype", ctypes.c_int32),
+        ("cls", ctypes.c_void_p), ("pos", ctypes.c_void_p), ("x", ctypes.c_void_p),
+    ]
+
+
+SIGNATURES.update({
+    "bl_gemm": (ctypes.c_int, [ctypes.POINTER(GemmArgs), ctypes.c_void_p]),
+    "bl_layernorm": (ctypes.c_int, [ctypes.POINTER(LayerNormArgs), ctypes.c_void_p]),
+    "bl_patchify": (ctypes.c_int, [ctypes.POINTER(PatchifyArgs), ctypes.c_void_p]),
+})

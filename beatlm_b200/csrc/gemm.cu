@@ -1,0 +1,515 @@
+// tcgen05 GEMM for the ViT linear layers, with the reference's fusions:
+//   C[M][N] = epilogue(A[M][K] . B[N][K]^T)
+// A is either a 16-bit activation loaded by TMA, or produced in the kernel by
+// a LayerNorm prologue from the f32 residual stream (the LN before the QKV
+// projection and before fc1), so the normalised activation never reaches
+// memory. B is the weight in [out][in] order (K-major), loaded by TMA.
+// The epilogue chain is the reference's Epilogue (kernel.rs:1595-1615) in
+// its canonical order: + bias (the MatMul's own), activation (ReLU, GELU
+// tanh, GELU erf), Scale, ChannelScale (LayerScale), Add (residual), then a
+// store in f32, f16 or bf16 (optionally a second type from a given column,
+// for the packed Q|K|V rows whose V part is f16).
+//
+// CTA: warp 0 TMA producer, warp 1 MMA issuer (M=128, N=BN, K=16 steps,
+// f32 accumulator in TMEM), warps 2..5 LN producers (LN mode) and then the
+// epilogue, one accumulator row (TMEM lane) per thread. Tiles 128 x BN x 64,
+// a 4-stage ring.
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+
+#include "host.h"
+
+namespace bl {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int STAGES = 4;
+constexpr int kThreads = 192;
+constexpr uint32_t kTileA = BM * BK * 2;  // 16 KiB
+
+struct Params {
+    int M, N, K;
+    int ab_fmt;  // 0 = f16, 1 = bf16 (A and B)
+    // LayerNorm prologue (LN mode only)
+    const float* x;
+    long long ldx;
+    const float* gamma;
+    const float* beta;
+    float eps;
+    // epilogue
+    const float* bias;
+    int act;
+    float scale;
+    const float* chan_scale;
+    const void* residual;
+    int res_dtype;
+    long long res_ld;
+    int res_period;  // residual row = out_row % res_period (0: out_row)
+    void* out;
+    int out_dtype;
+    int out_dtype_hi;
+    int split_col;
+    long long out_ld;
+    int out_row_offset;
+    int out_group_rows;  // out_row = m + (m / group_rows) * group_gap + offset
+    int out_group_gap;
+    Status* status;
+};
+
+template <int BN>
+struct Layout {
+    static constexpr uint32_t kTileB = BN * BK * 2;
+    static constexpr uint32_t kStage = kTileA + kTileB;
+    static constexpr uint32_t kTmemCols = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+};
+
+struct Tail {
+    uint64_t full[STAGES];
+    uint64_t empty[STAGES];
+    uint64_t acc_full;
+    uint64_t drain;
+    uint32_t tmem_base;
+    int abort;
+};
+
+template <int BN>
+constexpr size_t smem_bytes() {
+    return 1024 + STAGES * Layout<BN>::kStage + sizeof(Tail);
+}
+
+__device__ __forceinline__ uint64_t desc_k(uint32_t addr) { return sdesc_sw128(addr, 16, 1024); }
+
+__device__ __forceinline__ uint32_t pack2(float a, float b, int dt) {
+    return dt == BL_BF16 ? pack_bf16x2(a, b) : pack_f16x2(a, b);
+}
+
+// GELU through erf, Abramowitz and Stegun 7.1.26 (the reference's
+// GELU_ERF_P / GELU_ERF_A, kernel.rs:355-372), in f32 as its kernels do.
+__device__ __forceinline__ float gelu_erf(float x) {
+    const float p = 0.3275911f;
+    const float a1 = 0.254829592f, a2 = -0.284496736f, a3 = 1.421413741f, a4 = -1.453152027f,
+                a5 = 1.061405429f;
+    const float z = fabsf(x) * 0.70710678118654752f;
+    const float t = 1.0f / (1.0f + p * z);
+    const float poly = t * (a1 + t * (a2 + t * (a3 + t * (a4 + t * a5))));
+    const float q = 0.5f * poly * ex2(-z * z * 1.4426950408889634f);
+    return x * (x >= 0.0f ? 1.0f - q : q);
+}
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+    const float k = 0.7978845608028654f;
+    return 0.5f * x * (1.0f + tanhf(k * (x + 0.044715f * x * x * x)));
+}
+
+__device__ __forceinline__ void load16(const void* base, int dt, float* v) {
+    // 16 consecutive values of a residual row
+    if (dt == BL_F32) {
+        const float4* p = static_cast<const float4*>(base);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float4 q = p[i];
+            v[4 * i] = q.x; v[4 * i + 1] = q.y; v[4 * i + 2] = q.z; v[4 * i + 3] = q.w;
+        }
+    } else {
+        const uint4* p = static_cast<const uint4*>(base);
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            uint4 q = p[i];
+            uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if (dt == BL_BF16) {
+                    __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&w[j]);
+                    float2 f = __bfloat1622float2(h);
+                    v[8 * i + 2 * j] = f.x; v[8 * i + 2 * j + 1] = f.y;
+                } else {
+                    __half2 h = *reinterpret_cast<__half2*>(&w[j]);
+                    float2 f = __half22float2(h);
+                    v[8 * i + 2 * j] = f.x; v[8 * i + 2 * j + 1] = f.y;
+                }
+            }
+        }
+    }
+}
+
+template <int BN, bool kLn>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                const Params p) {
+    using L = Layout<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    Tail* tail = reinterpret_cast<Tail*>(smem + STAGES * L::kStage);
+    volatile int* abort = &tail->abort;
+    auto sA = [&](int s) { return smem + s * L::kStage; };
+    auto sB = [&](int s) { return smem + s * L::kStage + kTileA; };
+
+    const int warp = warp_id();
+    const int lane = lane_id();
+    const int m0 = blockIdx.x * BM;
+    const int n0 = blockIdx.y * BN;
+    const int nk = p.K / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(smem_u32(&tail->full[s]), kLn ? 1 + 4 : 1);
+            mbar_init(smem_u32(&tail->empty[s]), 1);
+        }
+        mbar_init(smem_u32(&tail->acc_full), 1);
+        mbar_init(smem_u32(&tail->drain), 1);
+        tail->abort = 0;
+        fence_barrier_init();
+        fence_proxy_async_smem();
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(&tail->tmem_base), L::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tail->tmem_base;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            tma_prefetch_desc(&tm_b);
+            if (!kLn) tma_prefetch_desc(&tm_a);
+            int issued[STAGES];
+#pragma unroll
+            for (int s = 0; s < STAGES; ++s) issued[s] = 0;
+            for (int kb = 0; kb < nk; ++kb) {
+                const int s = kb % STAGES;
+                if (kb >= STAGES &&
+                    !mbar_wait(smem_u32(&tail->empty[s]), ((kb / STAGES) - 1) & 1, abort, p.status,
+                               ST_TIMEOUT_TMA, kb))
+                    break;
+                const uint32_t bar = smem_u32(&tail->full[s]);
+                mbar_arrive_expect_tx(bar, (kLn ? 0u : kTileA) + L::kTileB);
+                if (!kLn) tma_load_2d(smem_u32(sA(s)), &tm_a, kb * BK, m0, bar);
+                tma_load_2d(smem_u32(sB(s)), &tm_b, kb * BK, n0, bar);
+                issued[s] += 1;
+            }
+            if (*abort) {
+                for (int s = 0; s < STAGES; ++s)
+                    if (issued[s] > 0)
+                        mbar_wait(smem_u32(&tail->full[s]), (issued[s] - 1) & 1, nullptr,
+                                  p.status, ST_TIMEOUT_DRAIN, s);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc = idesc_f16(BM, BN, p.ab_fmt, p.ab_fmt, 0, 0);
+            bool ok = true;
+            for (int kb = 0; kb < nk; ++kb) {
+                const int s = kb % STAGES;
+                ok = mbar_wait(smem_u32(&tail->full[s]), (kb / STAGES) & 1, abort, p.status,
+                               ST_TIMEOUT_MMA, kb);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t a = smem_u32(sA(s)), b = smem_u32(sB(s));
+#pragma unroll
+                for (int k = 0; k < BK / 16; ++k)
+                    mma_ss(tmem, desc_k(a + 32 * k), desc_k(b + 32 * k), idesc,
+                           (kb > 0 || k > 0) ? 1u : 0u);
+                // Release the stage only if the producers will refill it, so no
+                // arrival lands after the CTA has finished.
+                if (kb + STAGES < nk) mma_commit(smem_u32(&tail->empty[s]));
+            }
+            if (ok) {
+                mma_commit(smem_u32(&tail->acc_full));
+            } else {
+                mma_commit(smem_u32(&tail->drain));
+                mbar_wait(smem_u32(&tail->drain), 0, nullptr, p.status, ST_TIMEOUT_DRAIN, 0xD);
+            }
+        }
+    } else {
+        constexpr unsigned kFull = 0xFFFFFFFFu;
+        const int sub = warp & 3;
+        const int row = sub * 32 + lane;
+        const int grow = m0 + row;
+        bool ok = true;
+        if (kLn) {
+            // ---------------------------------------------- LayerNorm prologue
+            // Row statistics, one thread per row: a one-pass sum and sum of
+            // squares shifted by the row's first element (so a large mean does
+            // not cancel), the biased variance of reference.rs:247-270.
+            float mean = 0.0f, rstd = 0.0f;
+            const float* xr = p.x + static_cast<long long>(grow) * p.ldx;
+            if (grow < p.M) {
+                const float x0 = xr[0];
+                float s1 = 0.0f, s2 = 0.0f;
+                for (int k = 0; k < p.K; k += 4) {
+                    const float4 v = *reinterpret_cast<const float4*>(xr + k);
+                    const float d0 = v.x - x0, d1 = v.y - x0, d2 = v.z - x0, d3 = v.w - x0;
+                    s1 += (d0 + d1) + (d2 + d3);
+                    s2 += (d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3);
+                }
+                const float inv_k = 1.0f / static_cast<float>(p.K);
+                const float dm = s1 * inv_k;
+                const float var = fmaxf(s2 * inv_k - dm * dm, 0.0f);
+                mean = x0 + dm;
+                rstd = rsqrtf(var + p.eps);
+            }
+            for (int kb = 0; kb < nk; ++kb) {
+                const int s = kb % STAGES;
+                if (kb >= STAGES) {
+                    ok = mbar_wait(smem_u32(&tail->empty[s]), ((kb / STAGES) - 1) & 1, abort,
+                                   p.status, ST_TIMEOUT_SOFTMAX, kb);
+                    ok = __all_sync(kFull, ok);
+                    if (!ok) break;
+                }
+                uint8_t* arow = sA(s) + row * 128;
+#pragma unroll
+                for (int ch = 0; ch < 8; ++ch) {
+                    const int k = kb * BK + ch * 8;
+                    uint4 w = make_uint4(0, 0, 0, 0);
+                    if (grow < p.M) {
+                        const float4 v0 = *reinterpret_cast<const float4*>(xr + k);
+                        const float4 v1 = *reinterpret_cast<const float4*>(xr + k + 4);
+                        const float4 g0 = __ldg(reinterpret_cast<const float4*>(p.gamma + k));
+                        const float4 g1 = __ldg(reinterpret_cast<const float4*>(p.gamma + k + 4));
+                        const float4 b0 = __ldg(reinterpret_cast<const float4*>(p.beta + k));
+                        const float4 b1 = __ldg(reinterpret_cast<const float4*>(p.beta + k + 4));
+                        const int dt = p.ab_fmt ? BL_BF16 : BL_F16;
+                        w.x = pack2((v0.x - mean) * rstd * g0.x + b0.x,
+                                    (v0.y - mean) * rstd * g0.y + b0.y, dt);
+                        w.y = pack2((v0.z - mean) * rstd * g0.z + b0.z,
+                                    (v0.w - mean) * rstd * g0.w + b0.w, dt);
+                        w.z = pack2((v1.x - mean) * rstd * g1.x + b1.x,
+                                    (v1.y - mean) * rstd * g1.y + b1.y, dt);
+                        w.w = pack2((v1.z - mean) * rstd * g1.z + b1.z,
+                                    (v1.w - mean) * rstd * g1.w + b1.w, dt);
+                    }
+                    // 128-byte swizzle: 16-byte chunk index XOR (row % 8).
+                    *reinterpret_cast<uint4*>(arow + ((ch ^ (row & 7)) << 4)) = w;
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&tail->full[s]));
+            }
+        }
+        // -------------------------------------------------------- epilogue
+        if (ok) ok = mbar_wait(smem_u32(&tail->acc_full), 0, abort, p.status, ST_TIMEOUT_SOFTMAX,
+                               0xE);
+        ok = __all_sync(kFull, ok);
+        if (ok) {
+            tc_fence_after();
+            const uint32_t t_lane = tmem + (static_cast<uint32_t>(sub * 32) << 16);
+            const bool live = grow < p.M;
+            long long orow = grow;
+            if (p.out_group_rows > 0)
+                orow = grow + static_cast<long long>(grow / p.out_group_rows) * p.out_group_gap;
+            orow += p.out_row_offset;
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld32(t_lane + c * 32, r);
+                tmem_wait_ld();
+                if (!live) continue;
+                const int col = n0 + c * 32;
+                float v[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+                if (p.bias != nullptr) {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4) {
+                        const float4 b = __ldg(reinterpret_cast<const float4*>(p.bias + col + i));
+                        v[i] += b.x; v[i + 1] += b.y; v[i + 2] += b.z; v[i + 3] += b.w;
+                    }
+                }
+                if (p.act == 1) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] = fmaxf(v[i], 0.0f);
+                } else if (p.act == 2) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
+                } else if (p.act == 3) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+                }
+                if (p.scale != 1.0f) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] *= p.scale;
+                }
+                if (p.chan_scale != nullptr) {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4) {
+                        const float4 s =
+                            __ldg(reinterpret_cast<const float4*>(p.chan_scale + col + i));
+                        v[i] *= s.x; v[i + 1] *= s.y; v[i + 2] *= s.z; v[i + 3] *= s.w;
+                    }
+                }
+                if (p.residual != nullptr) {
+                    const long long rrow = p.res_period > 0 ? orow % p.res_period : orow;
+                    const size_t esz = p.res_dtype == BL_F32 ? 4 : 2;
+                    const uint8_t* rb = static_cast<const uint8_t*>(p.residual) +
+                                        esz * (rrow * p.res_ld + col);
+                    float rv[16];
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        load16(rb + esz * 16 * h, p.res_dtype, rv);
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) v[16 * h + i] += rv[i];
+                    }
+                }
+                const int dt = col >= p.split_col ? p.out_dtype_hi : p.out_dtype;
+                if (dt == BL_F32) {
+                    float4* o = reinterpret_cast<float4*>(static_cast<float*>(p.out) +
+                                                          orow * p.out_ld + col);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        o[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+                } else {
+                    uint4* o = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) +
+                                                        orow * p.out_ld + col);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        o[i] = make_uint4(pack2(v[8 * i], v[8 * i + 1], dt),
+                                          pack2(v[8 * i + 2], v[8 * i + 3], dt),
+                                          pack2(v[8 * i + 4], v[8 * i + 5], dt),
+                                          pack2(v[8 * i + 6], v[8 * i + 7], dt));
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, L::kTmemCols);
+    }
+}
+
+template <int BN, bool kLn>
+int launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaStream_t stream) {
+    auto kern = gemm_kernel<BN, kLn>;
+    constexpr size_t smem = smem_bytes<BN>();
+    BL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(smem)));
+    dim3 grid((p.M + BM - 1) / BM, p.N / BN);
+    kern<<<grid, kThreads, smem, stream>>>(ta, tb, p);
+    BL_CUDA_TRY(cudaGetLastError());
+    return BL_OK;
+}
+
+int pick_bn(const bl_gemm_args& g) {
+    if (g.tile_n) return static_cast<int>(g.tile_n);
+    // Fill the 148 SMs: the widest tile whose grid still covers them.
+    const int mt = static_cast<int>((g.m + BM - 1) / BM);
+    const int cands[4] = {128, 96, 64, 32};
+    for (int bn : cands)
+        if (g.n % bn == 0 && mt * static_cast<int>(g.n / bn) >= 120) return bn;
+    for (int i = 3; i >= 0; --i)
+        if (g.n % cands[i] == 0) return cands[i];
+    return 0;
+}
+
+int launch(const bl_gemm_args& g, cudaStream_t stream) {
+    if (g.m == 0 || g.n == 0 || g.k == 0) return fail(BL_ERR_INVALID, "gemm: zero dimension");
+    if (g.k % BK != 0) return fail(BL_ERR_UNSUPPORTED, "gemm: K=%u is not a multiple of 64", g.k);
+    if (g.ab_dtype != BL_F16 && g.ab_dtype != BL_BF16)
+        return fail(BL_ERR_UNSUPPORTED, "gemm: operand dtype %d (f16 or bf16)", g.ab_dtype);
+    const int bn = pick_bn(g);
+    if (bn == 0 || g.n % bn != 0 || (bn != 32 && bn != 64 && bn != 96 && bn != 128))
+        return fail(BL_ERR_UNSUPPORTED, "gemm: N=%u has no tile width (32/64/96/128)", g.n);
+    const bool ln = g.ln_x != nullptr;
+    if (!ln && g.a == nullptr) return fail(BL_ERR_INVALID, "gemm: no A operand");
+    if (ln && (g.ln_gamma == nullptr || g.ln_beta == nullptr || !(g.ln_eps > 0.0f)))
+        return fail(BL_ERR_INVALID, "gemm: LayerNorm prologue needs gamma, beta and eps > 0");
+    if (ln && ((reinterpret_cast<uintptr_t>(g.ln_x) & 15) || (g.ln_ldx % 4) || g.ln_ldx < g.k))
+        return fail(BL_ERR_INVALID, "gemm: LayerNorm input must be 16-byte aligned rows");
+    if (g.out == nullptr) return fail(BL_ERR_INVALID, "gemm: null output");
+    const bool split = g.split_col > 0 && g.split_col < g.n;
+    const int dts[2] = {g.out_dtype, split ? g.out_dtype_hi : g.out_dtype};
+    for (int dt : dts)
+        if (dt != BL_F32 && dt != BL_F16 && dt != BL_BF16)
+            return fail(BL_ERR_INVALID, "gemm: output dtype %d", dt);
+    const uint64_t out_ld = g.out_ld ? g.out_ld : g.n;
+    if ((reinterpret_cast<uintptr_t>(g.out) & 15) || (out_ld * 2) % 16 ||
+        (g.out_dtype == BL_F32 && (out_ld * 4) % 16))
+        return fail(BL_ERR_INVALID, "gemm: output must be 16-byte aligned rows");
+    if (split && g.split_col % 32)
+        return fail(BL_ERR_INVALID, "gemm: split column must be a multiple of 32");
+    if ((g.bias && (reinterpret_cast<uintptr_t>(g.bias) & 15)) ||
+        (g.chan_scale && (reinterpret_cast<uintptr_t>(g.chan_scale) & 15)))
+        return fail(BL_ERR_INVALID, "gemm: bias/scale vectors must be 16-byte aligned");
+    if (g.act < 0 || g.act > 3) return fail(BL_ERR_INVALID, "gemm: activation %d", g.act);
+    if (ln && ((reinterpret_cast<uintptr_t>(g.ln_gamma) & 15) ||
+               (reinterpret_cast<uintptr_t>(g.ln_beta) & 15)))
+        return fail(BL_ERR_INVALID, "gemm: LayerNorm gamma/beta must be 16-byte aligned");
+    if (g.residual != nullptr) {
+        const uint64_t rld = g.res_ld ? g.res_ld : g.n;
+        const uint64_t esz = g.res_dtype == BL_F32 ? 4 : 2;
+        if ((reinterpret_cast<uintptr_t>(g.residual) & 15) || (rld * esz) % 16 ||
+            (g.res_dtype != BL_F32 && g.res_dtype != BL_F16 && g.res_dtype != BL_BF16))
+            return fail(BL_ERR_INVALID, "gemm: residual must be 16-byte aligned rows");
+    }
+
+    CUtensorMap ta{}, tb{};
+    int rc;
+    if (!ln) {
+        const uint64_t lda = g.lda ? g.lda : g.k;
+        const uint64_t dims[2] = {g.k, g.m};
+        const uint32_t box[2] = {BK, BM};
+        if ((rc = make_tmap_16bit_2d(&ta, g.a, dims, lda * 2, box)) != BL_OK) return rc;
+    }
+    {
+        const uint64_t ldb = g.ldb ? g.ldb : g.k;
+        const uint64_t dims[2] = {g.k, g.n};
+        const uint32_t box[2] = {BK, static_cast<uint32_t>(bn)};
+        if ((rc = make_tmap_16bit_2d(&tb, g.b, dims, ldb * 2, box)) != BL_OK) return rc;
+    }
+    Params p{};
+    p.M = static_cast<int>(g.m);
+    p.N = static_cast<int>(g.n);
+    p.K = static_cast<int>(g.k);
+    p.ab_fmt = g.ab_dtype == BL_BF16 ? 1 : 0;
+    p.x = static_cast<const float*>(g.ln_x);
+    p.ldx = static_cast<long long>(g.ln_ldx ? g.ln_ldx : g.k);
+    p.gamma = g.ln_gamma;
+    p.beta = g.ln_beta;
+    p.eps = g.ln_eps;
+    p.bias = g.bias;
+    p.act = g.act;
+    p.scale = g.scale == 0.0f ? 1.0f : g.scale;
+    p.chan_scale = g.chan_scale;
+    p.residual = g.residual;
+    p.res_dtype = g.res_dtype;
+    p.res_ld = static_cast<long long>(g.res_ld ? g.res_ld : g.n);
+    p.res_period = static_cast<int>(g.res_period);
+    p.out = g.out;
+    p.out_dtype = g.out_dtype;
+    p.out_dtype_hi = split ? g.out_dtype_hi : g.out_dtype;
+    p.split_col = split ? static_cast<int>(g.split_col) : static_cast<int>(g.n);
+    p.out_ld = static_cast<long long>(out_ld);
+    p.out_row_offset = static_cast<int>(g.out_row_offset);
+    p.out_group_rows = static_cast<int>(g.out_group_rows);
+    p.out_group_gap = static_cast<int>(g.out_group_gap);
+    p.status = status_ptr();
+    if (ln) {
+        switch (bn) {
+            case 32: return launch_t<32, true>(ta, tb, p, stream);
+            case 64: return launch_t<64, true>(ta, tb, p, stream);
+            case 96: return launch_t<96, true>(ta, tb, p, stream);
+            default: return launch_t<128, true>(ta, tb, p, stream);
+        }
+    }
+    switch (bn) {
+        case 32: return launch_t<32, false>(ta, tb, p, stream);
+        case 64: return launch_t<64, false>(ta, tb, p, stream);
+        case 96: return launch_t<96, false>(ta, tb, p, stream);
+        default: return launch_t<128, false>(ta, tb, p, stream);
+    }
+}
+
+}  // namespace gemm
+}  // namespace bl
+
+extern "C" int bl_gemm(const bl_gemm_args* args, void* stream) {
+    if (args == nullptr) return bl::fail(BL_ERR_INVALID, "gemm: null args");
+    return bl::gemm::launch(*args, static_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,168 @@
+// Memory-bound helpers of the encoder: the standalone LayerNorm (the final
+// norm, with TokensToMap folded in) and the embedding front (patch matrix for
+// the patch-embedding GEMM, class token + position embedding).
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+
+#include "host.h"
+
+namespace bl {
+namespace misc {
+
+__device__ __forceinline__ uint16_t to16(float v, int dt) {
+    if (dt == BL_BF16) {
+        __nv_bfloat16 h = __float2bfloat16_rn(v);
+        return *reinterpret_cast<uint16_t*>(&h);
+    }
+    __half h = __float2half_rn(v);
+    return *reinterpret_cast<uint16_t*>(&h);
+}
+
+// One warp per output row. Two passes over the row held in registers
+// (mean, then the biased variance of the deviations), as reference.rs:247-270
+// defines the layer norm; f32 arithmetic.
+template <int kPerLane>
+__global__ void __launch_bounds__(256) layernorm_kernel(bl_layernorm_args a) {
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= static_cast<int>(a.rows)) return;
+    long long in_row = row;
+    if (a.in_group_rows > 0) in_row += static_cast<long long>(row / a.in_group_rows) * a.in_group_gap;
+    in_row += a.in_row_offset;
+    const float* x = a.x + in_row * static_cast<long long>(a.ldx);
+    const int cols = static_cast<int>(a.cols);
+    float v[kPerLane];
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kPerLane; ++i) {
+        const int c = lane + 32 * i;
+        v[i] = c < cols ? x[c] : 0.0f;
+        s += v[i];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
+    const float mean = s / static_cast<float>(cols);
+    float q = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kPerLane; ++i) {
+        const int c = lane + 32 * i;
+        const float d = c < cols ? v[i] - mean : 0.0f;
+        q += d * d;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xFFFFFFFFu, q, o);
+    const float rstd = rsqrtf(q / static_cast<float>(cols) + a.eps);
+    const long long orow = static_cast<long long>(row) * static_cast<long long>(a.ldo);
+#pragma unroll
+    for (int i = 0; i < kPerLane; ++i) {
+        const int c = lane + 32 * i;
+        if (c >= cols) break;
+        const float y = (v[i] - mean) * rstd * a.gamma[c] + a.beta[c];
+        if (a.out_dtype == BL_F32)
+            static_cast<float*>(a.out)[orow + c] = y;
+        else
+            static_cast<uint16_t*>(a.out)[orow + c] = to16(y, a.out_dtype);
+    }
+}
+
+// Patch matrix: one thread per (patch, 8 consecutive taps). Tap t of a patch
+// is (ky, kx, ci) = (t / (p*cin), (t / cin) % p, t % cin), the HWIO order of
+// the reference's patch weights, so row . weight[cout][t] is its patch_embed.
+__global__ void patchify_kernel(bl_patchify_args a, int grid_side, int taps) {
+    const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int groups = static_cast<int>(a.k_pad / 8);
+    const long long patches = static_cast<long long>(a.frames) * grid_side * grid_side;
+    if (idx >= patches * groups) return;
+    const long long patch = idx / groups;
+    const int g = static_cast<int>(idx % groups);
+    const int f = static_cast<int>(patch / (grid_side * grid_side));
+    const int pp = static_cast<int>(patch % (grid_side * grid_side));
+    const int gy = pp / grid_side, gx = pp % grid_side;
+    const int P = static_cast<int>(a.patch), C = static_cast<int>(a.cin);
+    const float* img = a.image + static_cast<long long>(f) * a.side * a.side * C;
+    uint16_t h[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int t = g * 8 + j;
+        float v = 0.0f;
+        if (t < taps) {
+            const int ky = t / (P * C), kx = (t / C) % P, ci = t % C;
+            v = img[(static_cast<long long>(gy * P + ky) * a.side + gx * P + kx) * C + ci];
+        }
+        h[j] = to16(v, a.a_dtype);
+    }
+    uint4 w;
+    w.x = h[0] | (static_cast<uint32_t>(h[1]) << 16);
+    w.y = h[2] | (static_cast<uint32_t>(h[3]) << 16);
+    w.z = h[4] | (static_cast<uint32_t>(h[5]) << 16);
+    w.w = h[6] | (static_cast<uint32_t>(h[7]) << 16);
+    reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.a) + patch * a.k_pad)[g] = w;
+}
+
+// Class-token rows: x[f][0][c] = cls[c] + pos[0][c] (f64-free f32 add, as a
+// fused epilogue Add would do).
+__global__ void cls_rows_kernel(bl_patchify_args a, int tokens) {
+    const int f = blockIdx.x;
+    for (int c = threadIdx.x; c < static_cast<int>(a.dim); c += blockDim.x)
+        a.x[static_cast<long long>(f) * tokens * a.dim + c] = a.cls[c] + a.pos[c];
+}
+
+}  // namespace misc
+}  // namespace bl
+
+extern "C" int bl_layernorm(const bl_layernorm_args* args, void* stream) {
+    using namespace bl;
+    if (args == nullptr) return fail(BL_ERR_INVALID, "layernorm: null args");
+    const bl_layernorm_args& a = *args;
+    if (a.rows == 0 || a.cols == 0 || a.x == nullptr || a.out == nullptr || a.gamma == nullptr ||
+        a.beta == nullptr)
+        return fail(BL_ERR_INVALID, "layernorm: empty shape or null pointer");
+    if (!(a.eps > 0.0f)) return fail(BL_ERR_INVALID, "layernorm: epsilon must be positive");
+    if (a.cols > 1024) return fail(BL_ERR_UNSUPPORTED, "layernorm: %u columns (max 1024)", a.cols);
+    if (a.out_dtype != BL_F32 && a.out_dtype != BL_F16 && a.out_dtype != BL_BF16)
+        return fail(BL_ERR_INVALID, "layernorm: output dtype %d", a.out_dtype);
+    bl_layernorm_args b = a;
+    if (b.ldx == 0) b.ldx = b.cols;
+    if (b.ldo == 0) b.ldo = b.cols;
+    dim3 grid((a.rows + 7) / 8);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (a.cols <= 128)
+        misc::layernorm_kernel<4><<<grid, 256, 0, s>>>(b);
+    else if (a.cols <= 384)
+        misc::layernorm_kernel<12><<<grid, 256, 0, s>>>(b);
+    else if (a.cols <= 512)
+        misc::layernorm_kernel<16><<<grid, 256, 0, s>>>(b);
+    else
+        misc::layernorm_kernel<32><<<grid, 256, 0, s>>>(b);
+    BL_CUDA_TRY(cudaGetLastError());
+    return BL_OK;
+}
+
+extern "C" int bl_patchify(const bl_patchify_args* args, void* stream) {
+    using namespace bl;
+    if (args == nullptr) return fail(BL_ERR_INVALID, "patchify: null args");
+    const bl_patchify_args& a = *args;
+    if (a.frames == 0 || a.patch == 0 || a.cin == 0 || a.side == 0 || a.side % a.patch != 0)
+        return fail(BL_ERR_INVALID, "patchify: side %u is not whole patches of %u", a.side, a.patch);
+    const uint32_t taps = a.patch * a.patch * a.cin;
+    if (a.k_pad < taps || a.k_pad % 64 != 0)
+        return fail(BL_ERR_INVALID, "patchify: k_pad %u must cover %u taps and be a multiple of 64",
+                    a.k_pad, taps);
+    if (a.image == nullptr || a.a == nullptr || (reinterpret_cast<uintptr_t>(a.a) & 15))
+        return fail(BL_ERR_INVALID, "patchify: null or misaligned buffers");
+    if (a.a_dtype != BL_F16 && a.a_dtype != BL_BF16)
+        return fail(BL_ERR_INVALID, "patchify: A dtype %d", a.a_dtype);
+    const int g = static_cast<int>(a.side / a.patch);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const long long work = static_cast<long long>(a.frames) * g * g * (a.k_pad / 8);
+    misc::patchify_kernel<<<static_cast<unsigned>((work + 255) / 256), 256, 0, s>>>(
+        a, g, static_cast<int>(taps));
+    BL_CUDA_TRY(cudaGetLastError());
+    if (a.x != nullptr) {
+        if (a.cls == nullptr || a.pos == nullptr || a.dim == 0)
+            return fail(BL_ERR_INVALID, "patchify: class-token rows need cls, pos and dim");
+        misc::cls_rows_kernel<<<a.frames, 128, 0, s>>>(a, g * g + 1);
+        BL_CUDA_TRY(cudaGetLastError());
+    }
+    return BL_OK;
+}

@@ -1,0 +1,268 @@
+"""The ViT encoder of Depth-Anything-V2 on the B200 backend.
+
+Mirrors the reference's graph builders
+(``crates/beatlm/src/model/depth_anything_v2.rs``: ``block``/``layer_of``
+252-427, ``encoder`` 435-545) as fused launches of ``libbeatlm_b200.so``:
+
+    per block (5 launches; the reference lowers the same block to 9 kernels,
+    kernel.rs:3796-3844):
+      qkv  = LN1(x) . Wqkv + b        GEMM, LayerNorm prologue, packed Q|K|V
+                                      (Q/K in the model dtype, V in f16)
+      o    = attention(qkv)           fused flash kernel (scores never stored)
+      x    = x + ls1 * (o . Wo + bo)  GEMM, LayerScale + residual epilogue
+      h    = gelu_erf(LN2(x) . W1 + b1)  GEMM, LayerNorm prologue, GELU epilogue
+      x    = x + ls2 * (h . W2 + b2)  GEMM, LayerScale + residual epilogue
+    embedding: patch matrix + class rows (1 launch pair), patch GEMM with the
+    position-embedding Add in its epilogue; features: final LayerNorm with
+    TokensToMap folded in.
+
+Weights are given in the reference's layouts (linear weights ``[in][out]``,
+``model/mod.rs:274-353``) as f32 and uploaded once, transposed to
+``[out][in]`` and rounded to the compute type. All activation buffers are
+allocated once per (frames) shape, so a forward pass allocates nothing.
+"""
+from __future__ import annotations
+
+import dataclasses
+import math
+
+import numpy as np
+
+from . import ops
+
+
+@dataclasses.dataclass(frozen=True)
+class ViTConfig:
+    dim: int = 384
+    heads: int = 6
+    mlp: int = 1536
+    layers: int = 12
+    patch: int = 14
+    side: int = 518
+    cin: int = 3
+    eps: float = 1e-6  # DINOV2_LAYER_NORM_EPSILON, depth_anything_v2.rs:114
+    out_indices: tuple = (3, 6, 9, 12)
+
+    @property
+    def grid(self) -> int:
+        return self.side // self.patch
+
+    @property
+    def tokens(self) -> int:
+        return self.grid * self.grid + 1
+
+    @property
+    def head_dim(self) -> int:
+        return self.dim // self.heads
+
+    @property
+    def taps(self) -> int:
+        return self.patch * self.patch * self.cin
+
+    @property
+    def k_pad(self) -> int:
+        return (self.taps + 63) // 64 * 64
+
+    @staticmethod
+    def small(**kw) -> "ViTConfig":
+        """Depth-Anything-V2-Small (load/depth_anything_v2.rs:126-147)."""
+        return ViTConfig(**kw)
+
+    @staticmethod
+    def large(**kw) -> "ViTConfig":
+        """ViT-L/14 shape of BASELINE config 4."""
+        base = dict(dim=1024, heads=16, mlp=4096, layers=24, out_indices=(6, 12, 18, 24))
+        base.update(kw)
+        return ViTConfig(**base)
+
+    def flops_per_frame(self) -> dict:
+        t, d, m = self.tokens, self.dim, self.mlp
+        linear = 2.0 * t * d * (3 * d + d + 2 * m) * self.layers
+        attn = 4.0 * t * t * d * self.layers
+        patch = 2.0 * (t - 1) * self.taps * d
+        return {"linear": linear, "attention": attn, "patch": patch,
+                "total": linear + attn + patch}
+
+
+BLOCK_NAMES = ("norm1_g", "norm1_b", "qkv_w", "qkv_b", "proj_w", "proj_b", "ls1",
+               "norm2_g", "norm2_b", "fc1_w", "fc1_b", "fc2_w", "fc2_b", "ls2")
+
+
+def _lcg_uniform(seed, count, low, high):
+    """The reference's seeded generator (net.rs:183-203), in numpy."""
+    s = np.uint64(seed)
+    mul, inc = np.uint64(6364136223846793005), np.uint64(1442695040888963407)
+    out = np.empty(count, np.float32)
+    # vectorised by jumping: sequential is fine at these sizes
+    vals = np.empty(count, np.uint64)
+    with np.errstate(over="ignore"):
+        for i in range(count):
+            s = s * mul + inc
+            vals[i] = s
+    out[:] = (vals >> np.uint64(40)).astype(np.float32) / np.float32(1 << 24)
+    return (np.float32(low) + np.float32(high - low) * out).astype(np.float32)
+
+
+def block_weights_by_role(seed: int, dim: int, mlp: int, uniform=None) -> dict:
+    """Random block weights drawn as the reference's block test draws them
+    (crates/beatlm-bench/src/vit.rs:203-238): gamma U(0.8,1.2), LayerScale
+    U(0.1,1), linear weights U(+-1/sqrt(fan_in)), the rest U(+-0.1); linear
+    weights in the reference's [in][out] layout."""
+    u = uniform or _lcg_uniform
+    fan = lambda s, n, f: u(s, n, -1 / math.sqrt(f), 1 / math.sqrt(f))
+    return {
+        "norm1_g": u(seed, dim, 0.8, 1.2), "norm1_b": u(seed + 1, dim, -0.1, 0.1),
+        "qkv_w": fan(seed + 2, dim * 3 * dim, dim), "qkv_b": u(seed + 3, 3 * dim, -0.1, 0.1),
+        "proj_w": fan(seed + 4, dim * dim, dim), "proj_b": u(seed + 5, dim, -0.1, 0.1),
+        "ls1": u(seed + 6, dim, 0.1, 1.0),
+        "norm2_g": u(seed + 7, dim, 0.8, 1.2), "norm2_b": u(seed + 8, dim, -0.1, 0.1),
+        "fc1_w": fan(seed + 9, dim * mlp, dim), "fc1_b": u(seed + 10, mlp, -0.1, 0.1),
+        "fc2_w": fan(seed + 11, mlp * dim, mlp), "fc2_b": u(seed + 12, dim, -0.1, 0.1),
+        "ls2": u(seed + 13, dim, 0.1, 1.0),
+    }
+
+
+def block_weights_normal(rng: np.random.Generator, dim: int, mlp: int, std=0.02,
+                         layer_scale=1.0) -> dict:
+    """linear weights N(0, std), biases 0, LayerNorm
+    gamma 1 / beta 0, LayerScale `layer_scale` (BASELINE gives no value; 1)."""
+    n = lambda *s: (rng.standard_normal(int(np.prod(s)), dtype=np.float32) * std)
+    z = lambda k: np.zeros(k, np.float32)
+    one = lambda k: np.ones(k, np.float32)
+    return {"norm1_g": one(dim), "norm1_b": z(dim), "qkv_w": n(dim, 3 * dim),
+            "qkv_b": z(3 * dim), "proj_w": n(dim, dim), "proj_b": z(dim),
+            "ls1": one(dim) * layer_scale, "norm2_g": one(dim), "norm2_b": z(dim),
+            "fc1_w": n(dim, mlp), "fc1_b": z(mlp), "fc2_w": n(mlp, dim), "fc2_b": z(dim),
+            "ls2": one(dim) * layer_scale}
+
+
+def _round(x: np.ndarray, dtype: str) -> np.ndarray:
+    import torch
+    t = torch.from_numpy(np.ascontiguousarray(x, np.float32))
+    return t.to(torch.bfloat16 if dtype == "bf16" else torch.float16).float().numpy()
+
+
+class DeviceBlock:
+    """One block's weights on the device: linear weights [out][in] in the
+    compute type, vectors in f32."""
+
+    def __init__(self, w: dict, dim: int, mlp: int, dtype: str = "bf16", device="cuda"):
+        import torch
+        td = torch.bfloat16 if dtype == "bf16" else torch.float16
+        self.dtype, self.dim, self.mlp = dtype, dim, mlp
+        f32 = lambda k: torch.from_numpy(np.ascontiguousarray(w[k], np.float32)).to(device)
+
+        def lin(k, fan_in, fan_out):
+            m = np.asarray(w[k], np.float32).reshape(fan_in, fan_out).T
+            return torch.from_numpy(np.ascontiguousarray(m)).to(td).to(device)
+
+        self.norm1 = (f32("norm1_g"), f32("norm1_b"))
+        self.qkv_w, self.qkv_b = lin("qkv_w", dim, 3 * dim), f32("qkv_b")
+        self.proj_w, self.proj_b = lin("proj_w", dim, dim), f32("proj_b")
+        self.ls1 = f32("ls1")
+        self.norm2 = (f32("norm2_g"), f32("norm2_b"))
+        self.fc1_w, self.fc1_b = lin("fc1_w", dim, mlp), f32("fc1_b")
+        self.fc2_w, self.fc2_b = lin("fc2_w", mlp, dim), f32("fc2_b")
+        self.ls2 = f32("ls2")
+
+    @staticmethod
+    def rounded(w: dict, dtype: str) -> dict:
+        """The weights as the device holds them, back in f32 and the
+        reference layout: what an oracle comparison must be given."""
+        out = dict(w)
+        for k in ("qkv_w", "proj_w", "fc1_w", "fc2_w"):
+            out[k] = _round(w[k], dtype)
+        return out
+
+
+class Buffers:
+    """Activation buffers for `frames` frames of `tokens` tokens, allocated
+    once (zero allocation in the forward pass)."""
+
+    def __init__(self, cfg: ViTConfig, frames: int, dtype: str, tokens: int | None = None,
+                 device="cuda", features: bool = True):
+        import torch
+        td = torch.bfloat16 if dtype == "bf16" else torch.float16
+        t = cfg.tokens if tokens is None else tokens
+        rows = frames * t
+        self.frames, self.tokens, self.rows = frames, t, rows
+        self.x = torch.empty((rows, cfg.dim), dtype=torch.float32, device=device)
+        self.qkv = torch.empty((rows, 3 * cfg.dim), dtype=torch.int16, device=device)
+        self.o = torch.empty((rows, cfg.dim), dtype=td, device=device)
+        self.h = torch.empty((rows, cfg.mlp), dtype=td, device=device)
+        self.patches = torch.empty((frames * (t - 1), cfg.k_pad), dtype=td, device=device)
+        self.features = ([torch.empty((frames * (t - 1), cfg.dim), dtype=torch.float32,
+                                      device=device) for _ in cfg.out_indices]
+                         if features else [])
+
+
+def run_block(blk: DeviceBlock, cfg: ViTConfig, buf: Buffers, stream=None):
+    """One pre-norm block in place on ``buf.x`` (reference.rs:520-544):
+    x1 = x + ls1 * proj(attention(norm1(x))); x = x1 + ls2 * fc2(gelu(fc1(norm2(x1))))."""
+    d = cfg.dim
+    ops.linear(blk.qkv_w, ln=(buf.x, blk.norm1[0], blk.norm1[1], cfg.eps), bias=blk.qkv_b,
+               out=buf.qkv, out_dtype=blk.dtype, out_split=(2 * d, "f16"), stream=stream)
+    ops.attention(buf.qkv, tokens=buf.tokens, heads=cfg.heads, head_dim=cfg.head_dim,
+                  batch=buf.frames, qk_dtype=blk.dtype, out=buf.o.view(buf.frames, buf.tokens, d),
+                  out_dtype=blk.dtype, stream=stream)
+    ops.linear(blk.proj_w, a=buf.o, bias=blk.proj_b, chan_scale=blk.ls1, residual=buf.x,
+               out=buf.x, stream=stream)
+    ops.linear(blk.fc1_w, ln=(buf.x, blk.norm2[0], blk.norm2[1], cfg.eps), bias=blk.fc1_b,
+               act="gelu_erf", out=buf.h, stream=stream)
+    ops.linear(blk.fc2_w, a=buf.h, bias=blk.fc2_b, chan_scale=blk.ls2, residual=buf.x,
+               out=buf.x, stream=stream)
+
+
+class Encoder:
+    """The DA-V2 ViT encoder (depth_anything_v2.rs:435-545) on the device."""
+
+    def __init__(self, cfg: ViTConfig, weights: dict, dtype: str = "bf16", device="cuda"):
+        """``weights``: ``blocks`` (list of per-block dicts in the reference
+        layout), ``patch_w`` [patch][patch][cin][dim] (HWIO), ``patch_b`` [dim],
+        ``cls`` [dim], ``pos`` [tokens][dim], ``norm_g``/``norm_b`` [dim]."""
+        import torch
+        td = torch.bfloat16 if dtype == "bf16" else torch.float16
+        self.cfg, self.dtype = cfg, dtype
+        self.blocks = [DeviceBlock(w, cfg.dim, cfg.mlp, dtype, device) for w in weights["blocks"]]
+        pw = np.zeros((cfg.dim, cfg.k_pad), np.float32)
+        pw[:, :cfg.taps] = np.asarray(weights["patch_w"], np.float32).reshape(cfg.taps, cfg.dim).T
+        f32 = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(device)
+        self.patch_w = torch.from_numpy(pw).to(td).to(device)
+        self.patch_b = f32(weights["patch_b"])
+        self.cls = f32(weights["cls"])
+        self.pos = f32(np.asarray(weights["pos"], np.float32).reshape(cfg.tokens, cfg.dim))
+        self.norm = (f32(weights["norm_g"]), f32(weights["norm_b"]))
+        self._buffers = {}
+
+    def buffers(self, frames: int) -> Buffers:
+        if frames not in self._buffers:
+            self._buffers[frames] = Buffers(self.cfg, frames, self.dtype)
+        return self._buffers[frames]
+
+    def forward(self, image, frames: int = 1, stream=None, layers: int | None = None):
+        """``image``: device f32 NHWC [frames][side][side][cin]. Returns the
+        feature maps (device f32 [frames * grid^2][dim] each) of the layers in
+        ``out_indices`` (those within ``layers``)."""
+        cfg, buf = self.cfg, self.buffers(frames)
+        t = cfg.tokens
+        ops.patchify(image, frames=frames, side=cfg.side, patch=cfg.patch, cin=cfg.cin,
+                     k_pad=cfg.k_pad, a_out=buf.patches, a_dtype=self.dtype, cls=self.cls,
+                     pos=self.pos, x=buf.x, stream=stream)
+        ops.linear(self.patch_w, a=buf.patches, bias=self.patch_b, residual=self.pos,
+                   res_period=t, out=buf.x, out_row_offset=1, out_group=(t - 1, 1),
+                   stream=stream)
+        n = cfg.layers if layers is None else layers
+        feats = []
+        for i in range(n):
+            run_block(self.blocks[i], cfg, buf, stream)
+            if (i + 1) in cfg.out_indices:
+                f = buf.features[cfg.out_indices.index(i + 1)]
+                ops.layernorm(buf.x, self.norm[0], self.norm[1], cfg.eps, out=f,
+                              in_row_offset=1, in_group=(t - 1, 1), stream=stream)
+                feats.append(f)
+        return feats
+
+    def launches_per_frame_batch(self, layers: int | None = None) -> int:
+        n = self.cfg.layers if layers is None else layers
+        taken = sum(1 for i in self.cfg.out_indices if i <= n)
+        return 3 + 5 * n + taken  # patchify (2) + patch GEMM, 5 per block, final norms

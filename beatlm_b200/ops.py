@@ -9,9 +9,6 @@ import numpy as np
 
 from . import _native as N
 
-_TORCH_DTYPE_CODE = {}
-
-
 def _dtype_code(name: str) -> int:
     return {"f32": N.BL_F32, "f16": N.BL_F16, "bf16": N.BL_BF16}[name]
 
@@ -60,3 +57,77 @@ def attention(qkv, *, tokens: int, heads: int, head_dim: int = 64, batch: int = 
                         out_head_base=out_head_base)
     N.check(N.lib().bl_attention(ctypes.byref(a), _stream_ptr(stream)))
     return out
+
+
+ACT = {None: 0, "none": 0, "relu": 1, "gelu_tanh": 2, "gelu_erf": 3}
+_TD = {"f32": N.BL_F32, "f16": N.BL_F16, "bf16": N.BL_BF16}
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _dt(t):
+    import torch
+    return {torch.float32: N.BL_F32, torch.float16: N.BL_F16, torch.bfloat16: N.BL_BF16}[t.dtype]
+
+
+def linear(w, *, a=None, ln=None, bias=None, act=None, scale=None, chan_scale=None,
+           residual=None, res_period=0, out, out_dtype=None, out_split=None, m=None,
+           out_row_offset=0, out_group=(0, 0), tile_n=0, stream=None):
+    """``out = epilogue(A . w^T)`` on the tensor cores (``bl_gemm``).
+
+    ``w`` is the 16-bit weight ``[n][k]`` (f16 or bf16; A is converted to the
+    same type); A is the 16-bit ``a`` ``[m][k]`` or, with
+    ``ln=(x, gamma, beta, eps)``, LayerNorm of the f32 rows ``x`` computed
+    inside the kernel. ``out_dtype`` defaults to ``out``'s own type;
+    ``out_split=(col, dtype)`` stores columns from ``col`` on as ``dtype``
+    (the f16 V part of packed Q|K|V rows)."""
+    import torch
+    n, k = w.shape
+    ab = {torch.float16: "f16", torch.bfloat16: "bf16"}[w.dtype]
+    if ln is not None:
+        x, gamma, beta, eps = ln
+        m = x.shape[0] if m is None else m
+    else:
+        m = a.shape[0] if m is None else m
+    odt = _TD[out_dtype] if out_dtype is not None else _dt(out)
+    g = N.GemmArgs(m=m, n=n, k=k, ab_dtype=_TD[ab], a=_ptr(a),
+                   lda=0 if a is None else a.stride(0), b=w.data_ptr(), ldb=w.stride(0),
+                   act=ACT[act], scale=0.0 if scale is None else scale,
+                   bias=_ptr(bias), chan_scale=_ptr(chan_scale), residual=_ptr(residual),
+                   res_dtype=N.BL_F32 if residual is None else _dt(residual),
+                   res_ld=0 if residual is None else residual.stride(0), res_period=res_period,
+                   out=out.data_ptr(), out_dtype=odt, out_ld=out.stride(0),
+                   out_row_offset=out_row_offset, out_group_rows=out_group[0],
+                   out_group_gap=out_group[1], tile_n=tile_n)
+    if out_split is not None:
+        g.split_col, g.out_dtype_hi = out_split[0], _TD[out_split[1]]
+    if ln is not None:
+        g.ln_x, g.ln_ldx, g.ln_gamma, g.ln_beta, g.ln_eps = (x.data_ptr(), x.stride(0),
+                                                             gamma.data_ptr(), beta.data_ptr(),
+                                                             eps)
+    N.check(N.lib().bl_gemm(ctypes.byref(g), _stream_ptr(stream)))
+    return out
+
+
+def layernorm(x, gamma, beta, eps, *, out, rows=None, in_row_offset=0, in_group=(0, 0),
+              stream=None):
+    rows = out.shape[0] if rows is None else rows
+    a = N.LayerNormArgs(rows=rows, cols=x.shape[1], x=x.data_ptr(), ldx=x.stride(0),
+                        gamma=gamma.data_ptr(), beta=beta.data_ptr(), eps=eps,
+                        out=out.data_ptr(), out_dtype=_dt(out), ldo=out.stride(0),
+                        in_row_offset=in_row_offset, in_group_rows=in_group[0],
+                        in_group_gap=in_group[1])
+    N.check(N.lib().bl_layernorm(ctypes.byref(a), _stream_ptr(stream)))
+    return out
+
+
+def patchify(image, *, frames, side, patch, cin, k_pad, a_out, a_dtype="bf16", cls=None,
+             pos=None, x=None, stream=None):
+    a = N.PatchifyArgs(frames=frames, side=side, patch=patch, cin=cin, k_pad=k_pad,
+                       dim=0 if cls is None else cls.numel(), image=image.data_ptr(),
+                       a=a_out.data_ptr(), a_dtype=_TD[a_dtype], cls=_ptr(cls), pos=_ptr(pos),
+                       x=_ptr(x))
+    N.check(N.lib().bl_patchify(ctypes.byref(a), _stream_ptr(stream)))
+    return a_out

@@ -106,6 +106,112 @@ typedef struct bl_attention_args {
 
 int bl_attention(const bl_attention_args* args, void* stream);
 
+/* ------------------------------------------------------------------ linear */
+
+enum { BL_ACT_NONE = 0, BL_ACT_RELU = 1, BL_ACT_GELU_TANH = 2, BL_ACT_GELU_ERF = 3 };
+
+/*
+ * A linear layer with the reference's fusions, on the tensor cores:
+ *   out = epilogue(A . W^T)   A [m][k], W [n][k] (out x in), f32 accumulate.
+ * Replaces the MatMul kernel with its fused epilogue chain
+ * (kernel.rs:781-794 MatMul, 1595-1615 Epilogue; WGSL tiled/matmul at
+ * crates/beatlm/src/codegen/wgsl.rs:744-932, epilogue hook 297-326), and adds
+ * the LayerNorm prologue of the QKV and fc1 projections.
+ *
+ * A: a 16-bit activation `a` (row stride lda), or, when ln_x != NULL,
+ * LayerNorm(ln_x) computed inside the kernel from the f32 rows ln_x (stride
+ * ln_ldx) with ln_gamma/ln_beta [k] and ln_eps (reference.rs:247-270), so the
+ * normalised rows never reach memory. A and W are `ab_dtype` (f16 or bf16).
+ *
+ * Epilogue, in this order: + bias[n]; act; * scale (0 or 1 = none);
+ * * chan_scale[n] (LayerScale, the reference's ChannelScale); + residual
+ * (res_dtype, row stride res_ld, row index out_row % res_period when
+ * res_period > 0). Stored as out_dtype, or as out_dtype_hi from column
+ * split_col on (0 < split_col < n; used for packed Q|K|V rows with f16 V).
+ * Output row of A-row r: r + (r / out_group_rows) * out_group_gap +
+ * out_row_offset (out_group_rows = 0: r + out_row_offset), which places the
+ * patch tokens of a frame after its class token.
+ *
+ * k must be a multiple of 64 and n a multiple of the tile width (32, 64, 96 or
+ * 128; tile_n = 0 chooses). Pointers 16-byte aligned, row strides 16-byte
+ * multiples. Enqueues on `stream`; allocates nothing.
+ */
+typedef struct bl_gemm_args {
+    uint32_t m, n, k;
+    int32_t ab_dtype;
+    const void* a;
+    uint64_t lda;
+    const void* b;
+    uint64_t ldb;
+    const float* ln_x;
+    uint64_t ln_ldx;
+    const float* ln_gamma;
+    const float* ln_beta;
+    float ln_eps;
+    const float* bias;
+    int32_t act;
+    float scale;
+    const float* chan_scale;
+    const void* residual;
+    int32_t res_dtype;
+    uint64_t res_ld;
+    uint32_t res_period;
+    void* out;
+    int32_t out_dtype;
+    uint64_t out_ld;
+    uint32_t split_col;
+    int32_t out_dtype_hi;
+    uint32_t out_row_offset, out_group_rows, out_group_gap;
+    uint32_t tile_n;
+} bl_gemm_args;
+
+int bl_gemm(const bl_gemm_args* args, void* stream);
+
+/*
+ * Standalone LayerNorm over rows of `cols` f32 values (reference.rs:247-270;
+ * OpKind::LayerNorm kernel.rs:644-659, WGSL layer_norm wgsl.rs:519-585), with
+ * the reference's TokensToMap (kernel.rs:703-720) folded in: input row of
+ * output row r is r + (r / in_group_rows) * in_group_gap + in_row_offset
+ * (in_group_rows = 0: r + in_row_offset), so the final norm can skip each
+ * frame's class token. One warp per row; out is f32/f16/bf16.
+ */
+typedef struct bl_layernorm_args {
+    uint32_t rows, cols;
+    const float* x;
+    uint64_t ldx;
+    const float* gamma;
+    const float* beta;
+    float eps;
+    void* out;
+    int32_t out_dtype;
+    uint64_t ldo;
+    uint32_t in_row_offset, in_group_rows, in_group_gap;
+} bl_layernorm_args;
+
+int bl_layernorm(const bl_layernorm_args* args, void* stream);
+
+/*
+ * The embedding front of the ViT encoder for `frames` images (NHWC f32,
+ * [frames][side][side][cin]): writes the patch matrix A
+ * [frames * grid^2][k_pad] (16-bit `a_dtype`, patches in row-major patch
+ * order, taps in (ky, kx, ci) order, zero-padded from patch^2*cin to k_pad)
+ * for the patch-embedding GEMM (the reference's PatchEmbed, kernel.rs:661-687,
+ * reference.rs:388-420), and the class-token rows of the residual stream x
+ * [frames][grid^2 + 1][dim] (f32): x[f][0] = cls + pos[0] (PrependToken and
+ * the position Add, kernel.rs:689-701).
+ */
+typedef struct bl_patchify_args {
+    uint32_t frames, side, patch, cin, k_pad, dim;
+    const float* image;
+    void* a;
+    int32_t a_dtype;
+    const float* cls;
+    const float* pos;
+    float* x;
+} bl_patchify_args;
+
+int bl_patchify(const bl_patchify_args* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

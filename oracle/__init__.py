@@ -79,6 +79,8 @@ def lib():
                                         ctypes.c_void_p, ctypes.c_void_p, F32P]
             L.orc_round_f16.argtypes = [F32P, sz, ctypes.c_void_p]
             L.orc_round_bf16.argtypes = [F32P, sz, ctypes.c_void_p]
+            L.orc_round_qkv_bf16.argtypes = [F32P, sz, ctypes.c_void_p]
+            L.orc_round_qkv_f16.argtypes = [F32P, sz, ctypes.c_void_p]
             _lib = L
     return _lib
 
@@ -231,17 +233,22 @@ WEIGHT_NAMES = ("norm1_g", "norm1_b", "qkv_w", "qkv_b", "proj_w", "proj_b", "ls1
 
 
 def vit_block(x, weights: dict, t, h, d, mlp, eps=1e-6, qkv_round=None, threads=None):
-    """``reference.rs:520-544``. ``qkv_round`` in {None, "f16", "bf16"} models
-    16-bit storage of the packed projection that attention reads."""
+    """``reference.rs:520-544``. ``qkv_round`` models 16-bit storage of the
+    packed projection that attention reads: None (f32, the reference), "f16" /
+    "bf16" (all of it), "qk_bf16" / "qk_f16" (Q and K in that type, V in f16:
+    the backend's packed layout)."""
     x = _f32(x)
     keep = {k: _f32(weights[k]) for k in WEIGHT_NAMES}
     bw = BlockWeights(**{k: _p(v) for k, v in keep.items()})
     out = np.empty_like(x)
     L = lib()
+    width = ctypes.c_size_t(h * d)
     fn = {None: None, "f16": ctypes.cast(L.orc_round_f16, ctypes.c_void_p),
-          "bf16": ctypes.cast(L.orc_round_bf16, ctypes.c_void_p)}[qkv_round]
+          "bf16": ctypes.cast(L.orc_round_bf16, ctypes.c_void_p),
+          "qk_bf16": ctypes.cast(L.orc_round_qkv_bf16, ctypes.c_void_p),
+          "qk_f16": ctypes.cast(L.orc_round_qkv_f16, ctypes.c_void_p)}[qkv_round]
     L.orc_vit_block(_p(x), ctypes.byref(bw), t, h, d, mlp, eps, threads or default_threads(),
-                    fn, None, _p(out))
+                    fn, ctypes.cast(ctypes.byref(width), ctypes.c_void_p), _p(out))
     return out
 
 

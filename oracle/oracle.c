@@ -350,3 +350,23 @@ void orc_round_bf16(float* values, size_t count, void* ctx) {
         memcpy(&values[i], &bits, 4);
     }
 }
+
+/* Models the backend's packed Q|K|V storage: in every row of 3 * width
+ * values, Q and K rounded to bf16 (ctx != NULL: *(size_t*)ctx = width) or
+ * f16, V always to f16. */
+static void round_qkv(float* values, size_t count, size_t width, int qk_bf16) {
+    size_t row = 3 * width;
+    for (size_t r = 0; r < count / row; ++r) {
+        float* v = values + r * row;
+        if (qk_bf16) orc_round_bf16(v, 2 * width, NULL); else orc_round_f16(v, 2 * width, NULL);
+        orc_round_f16(v + 2 * width, width, NULL);
+    }
+}
+
+void orc_round_qkv_bf16(float* values, size_t count, void* ctx) {
+    round_qkv(values, count, *(const size_t*)ctx, 1);
+}
+
+void orc_round_qkv_f16(float* values, size_t count, void* ctx) {
+    round_qkv(values, count, *(const size_t*)ctx, 0);
+}

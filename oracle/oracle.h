@@ -106,6 +106,10 @@ void orc_vit_block(const float* x, const orc_block_weights* w, size_t t, size_t 
  * binary16 / bfloat16 and back to f32. */
 void orc_round_f16(float* values, size_t count, void* ctx);
 void orc_round_bf16(float* values, size_t count, void* ctx);
+/* Packed Q|K|V rows of 3 * width values (ctx points to a size_t width):
+ * Q and K rounded to bf16 (resp. f16), V to f16. */
+void orc_round_qkv_bf16(float* values, size_t count, void* ctx);
+void orc_round_qkv_f16(float* values, size_t count, void* ctx);
 
 #ifdef __cplusplus
 }

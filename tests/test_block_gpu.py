@@ -1,0 +1,118 @@
+"""One pre-norm ViT block (5 fused launches) and the encoder against the
+oracle's forward pass (reference.rs:520-544 vit_block; encoder ops
+reference.rs:388-430), mirroring the reference's
+one_encoder_block_with_random_weights_matches_the_reference_block
+(crates/beatlm-bench/src/vit.rs:240-309): ViT-S shapes (T=1370, D=384, H=6,
+MLP=1536), weights by role, input U(-2, 2) from seed 20.
+
+The oracle is given the weights as the device holds them (rounded to the
+compute type) and the packed Q|K|V rounded as stored (Q/K compute type, V
+f16). The kernels additionally round three GEMM inputs to 16 bits (the
+normalised rows, the attention output and the GELU output) that the f32
+reference keeps in f32; those roundings are the stated difference. Bound:
+relative L2 <= 1e-3 (f16) and <= 4e-3 (bf16) on the block output."""
+import numpy as np
+import pytest
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+T, D, H, MLP = 1370, 384, 6, 1536
+REL = {"f16": 1e-3, "bf16": 4e-3}
+
+
+def _rel(got, want):
+    got, want = np.asarray(got, np.float64).ravel(), np.asarray(want, np.float64).ravel()
+    return float(np.linalg.norm(got - want) / np.linalg.norm(want)), float(
+        np.max(np.abs(got - want)))
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_one_block_matches_the_reference_block(dtype):
+    import torch
+    import beatlm_b200 as bl
+    from beatlm_b200.model import (Buffers, DeviceBlock, ViTConfig, block_weights_by_role,
+                                   run_block)
+    cfg = ViTConfig.small()
+    w = block_weights_by_role(100, D, MLP, uniform=oracle.uniform)
+    x = oracle.uniform(20, T * D, -2.0, 2.0)
+    blk = DeviceBlock(w, D, MLP, dtype)
+    buf = Buffers(cfg, 1, dtype, features=False)
+    buf.x.copy_(torch.from_numpy(x.reshape(T, D)))
+    run_block(blk, cfg, buf)
+    torch.cuda.synchronize()
+    st = bl.status(reset=True)
+    assert st.code == 0, hex(st.code)
+    got = buf.x.cpu().numpy()
+    want = oracle.vit_block(x, DeviceBlock.rounded(w, dtype), T, H, 64, MLP, 1e-6,
+                            qkv_round="qk_" + dtype)
+    rel, mx = _rel(got, want)
+    print("block %s: rel-L2 %.3e max-abs %.3e" % (dtype, rel, mx))
+    assert rel <= REL[dtype]
+
+
+def _encoder_weights(cfg, layers, seed=1):
+    rng = np.random.default_rng(seed)
+    from beatlm_b200.model import block_weights_normal
+    n = lambda *s: rng.standard_normal(int(np.prod(s)), dtype=np.float32) * 0.02
+    return {
+        "blocks": [block_weights_normal(rng, cfg.dim, cfg.mlp) for _ in range(layers)],
+        "patch_w": n(cfg.patch, cfg.patch, cfg.cin, cfg.dim), "patch_b": n(cfg.dim),
+        "cls": n(cfg.dim), "pos": n(cfg.tokens, cfg.dim),
+        "norm_g": np.ones(cfg.dim, np.float32), "norm_b": np.zeros(cfg.dim, np.float32),
+    }
+
+
+def imagenet_image(rng, side, frames=1):
+    """U[0,1] pixels normalised by the ImageNet mean/std
+    (load/depth_anything_v2/reference.rs:58-62), NHWC."""
+    mean = np.array([0.485, 0.456, 0.406], np.float32)
+    std = np.array([0.229, 0.224, 0.225], np.float32)
+    u = rng.random((frames, side, side, 3), dtype=np.float32)
+    return ((u - mean) / std).astype(np.float32)
+
+
+def oracle_encoder(cfg, w, image, layers, dtype):
+    """The reference's encoder chain (depth_anything_v2.rs:435-545) through the
+    oracle, with the weights rounded as the device holds them."""
+    from beatlm_b200.model import DeviceBlock
+    g = cfg.grid
+    rnd = oracle.round_bf16 if dtype == "bf16" else oracle.round_f16
+    patches = oracle.patch_embed(rnd(image), rnd(w["patch_w"]), w["patch_b"], g, g, cfg.patch,
+                                 cfg.cin, cfg.dim)
+    x = oracle.add(oracle.prepend_token(w["cls"], patches), w["pos"])
+    feats = []
+    for i in range(layers):
+        x = oracle.vit_block(x, DeviceBlock.rounded(w["blocks"][i], dtype), cfg.tokens,
+                             cfg.heads, cfg.head_dim, cfg.mlp, cfg.eps, qkv_round="qk_" + dtype)
+        if (i + 1) in cfg.out_indices:
+            n = oracle.layernorm(x, w["norm_g"], w["norm_b"], cfg.eps)
+            feats.append(oracle.tokens_to_map(n, cfg.dim))
+    return feats
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_encoder_features_match_the_reference_chain(dtype):
+    """Config-3 shapes (518 px, ViT-S) with 3 blocks and a feature taken after
+    blocks 1 and 3, batch 2 frames."""
+    import torch
+    import beatlm_b200 as bl
+    from beatlm_b200.model import Encoder, ViTConfig
+    layers = 3
+    cfg = ViTConfig.small(layers=layers, out_indices=(1, 3))
+    w = _encoder_weights(cfg, layers)
+    rng = np.random.default_rng(7)
+    image = imagenet_image(rng, cfg.side, frames=2)
+    enc = Encoder(cfg, w, dtype)
+    feats = enc.forward(torch.from_numpy(image).cuda(), frames=2)
+    torch.cuda.synchronize()
+    assert bl.status(reset=True).code == 0
+    for f in range(2):
+        want = oracle_encoder(cfg, w, image[f], layers, dtype)
+        for i, ft in enumerate(feats):
+            got = ft.cpu().numpy().reshape(2, -1)[f]
+            rel, mx = _rel(got, want[i])
+            print("encoder %s frame %d feature %d: rel-L2 %.3e max-abs %.3e" % (
+                dtype, f, i, rel, mx))
+            assert rel <= REL[dtype]

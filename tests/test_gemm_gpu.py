@@ -1,0 +1,196 @@
+"""The tcgen05 GEMM (bl_gemm) against the oracle's matmul (reference.rs:273-298)
+and its epilogue operations, through the C ABI.
+
+The oracle receives the same 16-bit-rounded A and W values the tensor cores
+read, so plain products differ only by f32 accumulation order: they must meet
+the reference's own per-element tolerance |d| <= 1e-4 + 1e-4 |ref|
+(reference.rs:17-24). With the LayerNorm prologue the normalised values are
+computed in f32 on the GPU and in f64 in the oracle before both round to 16
+bits, so a few elements round to neighbouring 16-bit values: there the bound
+is relative L2 <= 1e-3 (bf16) / 2e-4 (f16)."""
+import math
+
+import numpy as np
+import pytest
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+TOL_ABS, TOL_REL = 1e-4, 1e-4
+
+
+def _dev(a, dtype):
+    import torch
+    td = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32}[dtype]
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(td).cuda()
+
+
+def _rnd(a, dtype):
+    return oracle.round_bf16(a) if dtype == "bf16" else oracle.round_f16(a)
+
+
+def _close(got, want, what):
+    got = np.asarray(got, np.float32).ravel()
+    want = np.asarray(want, np.float32).ravel()
+    bad = np.abs(got - want) > TOL_ABS + TOL_REL * np.abs(want)
+    assert not bad.any(), "%s: %d mismatches, first at %d: %r vs %r" % (
+        what, bad.sum(), np.argmax(bad), got[np.argmax(bad)], want[np.argmax(bad)])
+
+
+def _rel(got, want):
+    got = np.asarray(got, np.float64).ravel()
+    want = np.asarray(want, np.float64).ravel()
+    return np.linalg.norm(got - want) / np.linalg.norm(want)
+
+
+def _check_status():
+    import beatlm_b200 as bl
+    st = bl.status(reset=True)
+    assert st.code == 0, hex(st.code)
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+@pytest.mark.parametrize("m,n,k,tile", [(1370, 1152, 384, 0), (1370, 384, 384, 32),
+                                        (1370, 1536, 384, 128), (1370, 384, 1536, 32),
+                                        (200, 192, 128, 96), (1, 64, 64, 64), (129, 128, 640, 64)])
+def test_plain_gemm_with_bias(dtype, m, n, k, tile):
+    import torch
+    import beatlm_b200 as bl
+    a = _rnd(oracle.normal(m + n, m * k), dtype)
+    w = _rnd(oracle.uniform(k, k * n, -1 / math.sqrt(k), 1 / math.sqrt(k)), dtype)  # [in][out]
+    b = oracle.uniform(n, n, -0.1, 0.1)
+    out = torch.zeros((m, n), dtype=torch.float32, device="cuda")
+    bl.ops.linear(_dev(w.reshape(k, n).T, dtype), a=_dev(a.reshape(m, k), dtype),
+                  bias=_dev(b, "f32"), out=out, tile_n=tile)
+    torch.cuda.synchronize()
+    _check_status()
+    want = oracle.matmul(a, w, b, m, k, n)
+    _close(out.cpu().numpy(), want, "gemm %dx%dx%d %s" % (m, n, k, dtype))
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_layerscale_residual_epilogue(dtype):
+    """x1 = x + ls * (A.W + b): ChannelScale then Add (reference.rs:379, 301),
+    in place on the f32 residual stream."""
+    import torch
+    import beatlm_b200 as bl
+    m, n, k = 1370, 384, 384
+    a = _rnd(oracle.normal(1, m * k), dtype)
+    w = _rnd(oracle.uniform(2, k * n, -0.05, 0.05), dtype)
+    b, ls = oracle.uniform(3, n, -0.1, 0.1), oracle.uniform(4, n, 0.1, 1.0)
+    x = oracle.uniform(5, m * n, -2, 2)
+    xd = _dev(x.reshape(m, n), "f32")
+    bl.ops.linear(_dev(w.reshape(k, n).T, dtype), a=_dev(a.reshape(m, k), dtype),
+                  bias=_dev(b, "f32"), chan_scale=_dev(ls, "f32"), residual=xd, out=xd)
+    torch.cuda.synchronize()
+    _check_status()
+    want = oracle.add(x, oracle.channel_scale(oracle.matmul(a, w, b, m, k, n), ls))
+    _close(xd.cpu().numpy(), want, "layerscale+residual")
+
+
+def test_gelu_erf_epilogue_and_16bit_store():
+    import torch
+    import beatlm_b200 as bl
+    m, n, k = 300, 1536, 384
+    a = _rnd(oracle.normal(6, m * k), "bf16")
+    w = _rnd(oracle.uniform(7, k * n, -0.1, 0.1), "bf16")
+    b = oracle.uniform(8, n, -0.1, 0.1)
+    out = torch.zeros((m, n), dtype=torch.bfloat16, device="cuda")
+    bl.ops.linear(_dev(w.reshape(k, n).T, "bf16"), a=_dev(a.reshape(m, k), "bf16"),
+                  bias=_dev(b, "f32"), act="gelu_erf", out=out)
+    torch.cuda.synchronize()
+    _check_status()
+    want = oracle.round_bf16(oracle.gelu_erf(oracle.matmul(a, w, b, m, k, n)))
+    got = out.float().cpu().numpy().ravel()
+    # one bf16 ulp of slack for values that sit on a rounding boundary
+    assert np.all(np.abs(got - want) <= 2 ** -7 * np.abs(want) + 1e-4)
+    assert _rel(got, want) < 2e-3
+
+
+def test_gelu_erf_on_the_gpu_is_within_its_stated_error():
+    """The reference's GPU test (vit.rs:175-199): GELU (erf) over [-10, 10] in
+    steps of 2^-12 within GELU_ERF_MAX_ERROR = 5e-7 of GELU through f64 erf.
+    The values enter as the bias of a zero product."""
+    import torch
+    import beatlm_b200 as bl
+    grid = (-10.0 + np.arange(81921, dtype=np.float32) / np.float32(4096)).astype(np.float32)
+    n = (grid.size + 127) // 128 * 128
+    bias = np.zeros(n, np.float32)
+    bias[:grid.size] = grid
+    out = torch.zeros((1, n), dtype=torch.float32, device="cuda")
+    bl.ops.linear(torch.zeros((n, 64), dtype=torch.float16, device="cuda"),
+                  a=torch.zeros((1, 64), dtype=torch.float16, device="cuda"),
+                  bias=_dev(bias, "f32"), act="gelu_erf", out=out, tile_n=128)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()[0, :grid.size].astype(np.float64)
+    exact = np.array([0.5 * float(v) * (1.0 + oracle.erf(float(v) / math.sqrt(2.0)))
+                      for v in grid])
+    worst = float(np.max(np.abs(got - exact)))
+    print("GELU (erf) on the GPU: max abs error %.3e" % worst)
+    assert worst <= 5e-7
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+@pytest.mark.parametrize("d", [384, 1024])
+def test_layernorm_prologue(dtype, d):
+    """QKV projection of LN(x): the LayerNorm (reference.rs:247-270) computed
+    inside the GEMM; Q|K stored in `dtype`, V in f16 (split store)."""
+    import torch
+    import beatlm_b200 as bl
+    m, n = 1370, 3 * d
+    x = oracle.uniform(9, m * d, -2, 2) + np.float32(0.7)  # a non-zero mean
+    g, be = oracle.uniform(10, d, 0.8, 1.2), oracle.uniform(11, d, -0.1, 0.1)
+    w = _rnd(oracle.uniform(12, d * n, -1 / math.sqrt(d), 1 / math.sqrt(d)), dtype)
+    b = oracle.uniform(13, n, -0.1, 0.1)
+    out = torch.zeros((m, n), dtype=torch.int16, device="cuda")
+    bl.ops.linear(_dev(w.reshape(d, n).T, dtype), ln=(_dev(x.reshape(m, d), "f32"),
+                  _dev(g, "f32"), _dev(be, "f32"), 1e-6), bias=_dev(b, "f32"), out=out,
+                  out_dtype=dtype, out_split=(2 * d, "f16"))
+    torch.cuda.synchronize()
+    _check_status()
+    o = out.cpu()
+    qk = o[:, :2 * d].view(torch.bfloat16 if dtype == "bf16" else torch.float16).float().numpy()
+    v = o[:, 2 * d:].view(torch.float16).float().numpy()
+    a = _rnd(oracle.layernorm(x, g, be, 1e-6), dtype)
+    want = oracle.matmul(a, w, b, m, d, n).reshape(m, n)
+    # the stored values are 16-bit: compare with the oracle rounded the same way
+    rel_qk = _rel(qk, _rnd(want[:, :2 * d], dtype))
+    rel_v = _rel(v, oracle.round_f16(want[:, 2 * d:]))
+    print("LN prologue %s D=%d: rel-L2 QK %.2e V %.2e" % (dtype, d, rel_qk, rel_v))
+    assert rel_qk < 2e-4 and rel_v < 2e-4
+
+
+def test_patch_rows_land_after_the_class_token():
+    """Output-row grouping (patch tokens after each frame's class token) and a
+    periodic residual (the position embedding)."""
+    import torch
+    import beatlm_b200 as bl
+    frames, t, n, k = 2, 10, 64, 64
+    rows = frames * (t - 1)
+    a = _rnd(oracle.normal(14, rows * k), "f16")
+    w = _rnd(oracle.uniform(15, k * n, -0.1, 0.1), "f16")
+    pos = oracle.uniform(16, t * n, -1, 1)
+    out = torch.full((frames * t, n), 7.0, dtype=torch.float32, device="cuda")
+    bl.ops.linear(_dev(w.reshape(k, n).T, "f16"), a=_dev(a.reshape(rows, k), "f16"),
+                  residual=_dev(pos.reshape(t, n), "f32"), res_period=t, out=out,
+                  out_row_offset=1, out_group=(t - 1, 1))
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().reshape(frames, t, n)
+    prod = oracle.matmul(a, w, None, rows, k, n).reshape(frames, t - 1, n)
+    want = prod + pos.reshape(t, n)[1:]
+    assert np.all(got[:, 0] == 7.0)
+    _close(got[:, 1:], want, "grouped rows")
+
+
+def test_bad_shapes_are_errors():
+    import torch
+    import beatlm_b200 as bl
+    w = torch.zeros((64, 60), dtype=torch.float16, device="cuda")
+    with pytest.raises(bl.BackendError, match="multiple of 64"):
+        bl.ops.linear(w, a=torch.zeros((4, 60), dtype=torch.float16, device="cuda"),
+                      out=torch.zeros((4, 64), device="cuda"))
+    w = torch.zeros((40, 64), dtype=torch.float16, device="cuda")
+    with pytest.raises(bl.BackendError, match="tile width"):
+        bl.ops.linear(w, a=torch.zeros((4, 64), dtype=torch.float16, device="cuda"),
+                      out=torch.zeros((4, 40), device="cuda"))
