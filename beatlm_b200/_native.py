@@ -124,7 +124,49 @@ class PatchifyArgs(ctypes.Structure):
     ]
 
 
+class KernelSpec(ctypes.Structure):
+    _fields_ = [("op", ctypes.c_int32), ("args", ctypes.c_void_p), ("label", ctypes.c_char_p),
+                ("parts", ctypes.c_uint32)]
+
+
+class SliceTime(ctypes.Structure):
+    _fields_ = [("frame", ctypes.c_uint64), ("slice", ctypes.c_uint32),
+                ("kernel", ctypes.c_uint32), ("begin_us", ctypes.c_double),
+                ("micros", ctypes.c_double)]
+
+
+class TimerStats(ctypes.Structure):
+    _fields_ = [("frames_skipped", ctypes.c_uint64), ("frames_collected", ctypes.c_uint64),
+                ("frames_failed", ctypes.c_uint64)]
+
+
+_vp, _sz, _u32, _i32 = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_uint32, ctypes.c_int32
 SIGNATURES.update({
+    "bl_split_edges": (_u32, [_u32, _u32, _u32, ctypes.POINTER(_u32)]),
+    "bl_parts_within": (_u32, [ctypes.c_uint64, ctypes.c_uint64, _u32]),
+    "bl_kernels_create": (ctypes.c_int, [ctypes.POINTER(KernelSpec), _sz,
+                                         ctypes.POINTER(_vp)]),
+    "bl_kernels_destroy": (None, [_vp]),
+    "bl_kernels_len": (_sz, [_vp]),
+    "bl_kernels_label": (ctypes.c_char_p, [_vp, _sz]),
+    "bl_kernels_encode": (ctypes.c_int, [_vp, _sz, _vp, _vp, _i32]),
+    "bl_kernels_encode_range": (ctypes.c_int, [_vp, _sz, _sz, _vp, _vp, _i32]),
+    "bl_kernels_capture": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(_vp)]),
+    "bl_graph_launch": (ctypes.c_int, [_vp, _vp]),
+    "bl_graph_destroy": (None, [_vp]),
+    "bl_timer_create": (ctypes.c_int, [_u32, ctypes.POINTER(_vp)]),
+    "bl_timer_destroy": (None, [_vp]),
+    "bl_timer_max_slices": (_u32, [_vp]),
+    "bl_timer_begin_frame": (ctypes.c_int, [_vp, ctypes.c_uint64, ctypes.POINTER(_i32)]),
+    "bl_timer_submitted": (ctypes.c_int, [_vp, _i32]),
+    "bl_timer_submitted_held": (ctypes.c_int, [_vp, _i32]),
+    "bl_timer_settle": (ctypes.c_int, [_vp, _i32, ctypes.c_int]),
+    "bl_timer_drop": (ctypes.c_int, [_vp, _i32]),
+    "bl_timer_invalidate_submitted": (_sz, [_vp]),
+    "bl_timer_in_flight": (_sz, [_vp]),
+    "bl_timer_collect_ready": (ctypes.c_int, [_vp, ctypes.POINTER(SliceTime), _sz,
+                                              ctypes.POINTER(_sz), ctypes.POINTER(_sz)]),
+    "bl_timer_get_stats": (ctypes.c_int, [_vp, ctypes.POINTER(TimerStats)]),
     "bl_gemm": (ctypes.c_int, [ctypes.POINTER(GemmArgs), ctypes.c_void_p]),
     "bl_layernorm": (ctypes.c_int, [ctypes.POINTER(LayerNormArgs), ctypes.c_void_p]),
     "bl_patchify": (ctypes.c_int, [ctypes.POINTER(PatchifyArgs), ctypes.c_void_p]),

@@ -358,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-int launch(const bl_attention_args& a, cudaStream_t stream) {
+int prepare(const bl_attention_args& a, Launch* out) {
     if (a.head_dim != HD) return fail(BL_ERR_UNSUPPORTED, "attention: head_dim %u (only 64)", a.head_dim);
     if (a.batch == 0 || a.tokens == 0 || a.heads == 0)
         return fail(BL_ERR_INVALID, "attention: zero dimension");
@@ -418,15 +418,23 @@ int launch(const bl_attention_args& a, cudaStream_t stream) {
                                         : attention_fwd<BL_BF16>;
     BL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(kSmemBytes)));
-    kern<<<grid, kThreads, kSmemBytes, stream>>>(tm, tm, tm, p);
-    BL_CUDA_TRY(cudaGetLastError());
+    out->op = 1;
+    out->run = [=](cudaStream_t s) {
+        kern<<<grid, kThreads, kSmemBytes, s>>>(tm, tm, tm, p);
+        return cudaGetLastError();
+    };
     return BL_OK;
 }
 
 }  // namespace attn
+
+int prepare_attention(const bl_attention_args& a, Launch* out) { return attn::prepare(a, out); }
+
 }  // namespace bl
 
 extern "C" int bl_attention(const bl_attention_args* args, void* stream) {
     if (args == nullptr) return bl::fail(BL_ERR_INVALID, "attention: null args");
-    return bl::attn::launch(*args, static_cast<cudaStream_t>(stream));
+    bl::Launch l;
+    int rc = bl::prepare_attention(*args, &l);
+    return rc != BL_OK ? rc : bl::enqueue(l, static_cast<cudaStream_t>(stream));
 }

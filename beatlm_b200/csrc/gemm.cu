@@ -17,6 +17,8 @@
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 
+#include <algorithm>
+
 #include "host.h"
 
 namespace bl {
@@ -54,6 +56,7 @@ struct Params {
     int out_row_offset;
     int out_group_rows;  // out_row = m + (m / group_rows) * group_gap + offset
     int out_group_gap;
+    int m_tile0, m_tiles;  // row tiles [m_tile0, m_tile0 + m_tiles) of this launch (a part)
     Status* status;
 };
 
@@ -148,7 +151,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = warp_id();
     const int lane = lane_id();
-    const int m0 = blockIdx.x * BM;
+    const int m0 = (p.m_tile0 + static_cast<int>(blockIdx.x)) * BM;
     const int n0 = blockIdx.y * BN;
     const int nk = p.K / BK;
 
@@ -385,14 +388,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <int BN, bool kLn>
-int launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaStream_t stream) {
+int prepare_t(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, Launch* out) {
     auto kern = gemm_kernel<BN, kLn>;
     constexpr size_t smem = smem_bytes<BN>();
     BL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(smem)));
-    dim3 grid((p.M + BM - 1) / BM, p.N / BN);
-    kern<<<grid, kThreads, smem, stream>>>(ta, tb, p);
-    BL_CUDA_TRY(cudaGetLastError());
+    const dim3 grid(p.m_tiles, p.N / BN);
+    out->op = 2;
+    out->run = [=](cudaStream_t s) {
+        kern<<<grid, kThreads, smem, s>>>(ta, tb, p);
+        return cudaGetLastError();
+    };
     return BL_OK;
 }
 
@@ -408,7 +414,7 @@ int pick_bn(const bl_gemm_args& g) {
     return 0;
 }
 
-int launch(const bl_gemm_args& g, cudaStream_t stream) {
+int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch* out) {
     if (g.m == 0 || g.n == 0 || g.k == 0) return fail(BL_ERR_INVALID, "gemm: zero dimension");
     if (g.k % BK != 0) return fail(BL_ERR_UNSUPPORTED, "gemm: K=%u is not a multiple of 64", g.k);
     if (g.ab_dtype != BL_F16 && g.ab_dtype != BL_BF16)
@@ -489,27 +495,39 @@ int launch(const bl_gemm_args& g, cudaStream_t stream) {
     p.out_row_offset = static_cast<int>(g.out_row_offset);
     p.out_group_rows = static_cast<int>(g.out_group_rows);
     p.out_group_gap = static_cast<int>(g.out_group_gap);
+    p.m_tile0 = static_cast<int>(row_begin / BM);
+    p.m_tiles = static_cast<int>((std::min(row_end, g.m) + BM - 1) / BM) - p.m_tile0;
+    if (row_begin % BM != 0 || row_begin >= row_end || p.m_tiles <= 0)
+        return fail(BL_ERR_INVALID, "gemm: row part [%u, %u) is not whole 128-row tiles", row_begin, row_end);
     p.status = status_ptr();
     if (ln) {
         switch (bn) {
-            case 32: return launch_t<32, true>(ta, tb, p, stream);
-            case 64: return launch_t<64, true>(ta, tb, p, stream);
-            case 96: return launch_t<96, true>(ta, tb, p, stream);
-            default: return launch_t<128, true>(ta, tb, p, stream);
+            case 32: return prepare_t<32, true>(ta, tb, p, out);
+            case 64: return prepare_t<64, true>(ta, tb, p, out);
+            case 96: return prepare_t<96, true>(ta, tb, p, out);
+            default: return prepare_t<128, true>(ta, tb, p, out);
         }
     }
     switch (bn) {
-        case 32: return launch_t<32, false>(ta, tb, p, stream);
-        case 64: return launch_t<64, false>(ta, tb, p, stream);
-        case 96: return launch_t<96, false>(ta, tb, p, stream);
-        default: return launch_t<128, false>(ta, tb, p, stream);
+        case 32: return prepare_t<32, false>(ta, tb, p, out);
+        case 64: return prepare_t<64, false>(ta, tb, p, out);
+        case 96: return prepare_t<96, false>(ta, tb, p, out);
+        default: return prepare_t<128, false>(ta, tb, p, out);
     }
 }
 
 }  // namespace gemm
+
+int prepare_gemm(const bl_gemm_args& g, Launch* out) { return gemm::prepare(g, 0, g.m, out); }
+int prepare_gemm_rows(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch* out) {
+    return gemm::prepare(g, row_begin, row_end, out);
+}
+
 }  // namespace bl
 
 extern "C" int bl_gemm(const bl_gemm_args* args, void* stream) {
     if (args == nullptr) return bl::fail(BL_ERR_INVALID, "gemm: null args");
-    return bl::gemm::launch(*args, static_cast<cudaStream_t>(stream));
+    bl::Launch l;
+    int rc = bl::prepare_gemm(*args, &l);
+    return rc != BL_OK ? rc : bl::enqueue(l, static_cast<cudaStream_t>(stream));
 }

@@ -7,6 +7,7 @@
 
 #include <cstdarg>
 #include <cstdint>
+#include <functional>
 
 #include "../../include/beatlm_b200.h"
 #include "sm100.cuh"
@@ -30,6 +31,30 @@ int make_tmap_16bit_2d(CUtensorMap* map, const void* base, const uint64_t dims[2
                        uint64_t row_stride_bytes, const uint32_t box[2]);
 
 inline size_t dtype_size(int dt) { return dt == BL_F32 ? 4 : 2; }
+
+// A validated, fully prepared launch: tensor maps encoded, parameters packed,
+// kernel attributes set. run() only enqueues (the reference's split between
+// Kernels::new, which builds, and Kernels::encode, which records).
+struct Launch {
+    std::function<cudaError_t(cudaStream_t)> run;
+    int op = 0;  // bl_op kind
+};
+
+int prepare_attention(const bl_attention_args& a, Launch* out);
+int prepare_gemm(const bl_gemm_args& g, Launch* out);
+// Rows [row_begin, row_end) of the output only (whole 128-row tiles): one
+// part of a split kernel.
+int prepare_gemm_rows(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch* out);
+int prepare_layernorm(const bl_layernorm_args& a, Launch* out);
+int prepare_layernorm_rows(const bl_layernorm_args& a, uint32_t row_begin, uint32_t row_end,
+                           Launch* out);
+int prepare_patchify(const bl_patchify_args& a, Launch* out);
+
+inline int enqueue(const Launch& l, cudaStream_t s) {
+    cudaError_t e = l.run(s);
+    if (e != cudaSuccess) return fail(BL_ERR_CUDA, "launch failed: %s", cudaGetErrorString(e));
+    return BL_OK;
+}
 
 }  // namespace bl
 

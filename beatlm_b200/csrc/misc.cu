@@ -22,10 +22,10 @@ __device__ __forceinline__ uint16_t to16(float v, int dt) {
 // (mean, then the biased variance of the deviations), as reference.rs:247-270
 // defines the layer norm; f32 arithmetic.
 template <int kPerLane>
-__global__ void __launch_bounds__(256) layernorm_kernel(bl_layernorm_args a) {
-    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+__global__ void __launch_bounds__(256) layernorm_kernel(bl_layernorm_args a, int row_begin, int row_end) {
+    const int row = row_begin + static_cast<int>(blockIdx.x) * 8 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
-    if (row >= static_cast<int>(a.rows)) return;
+    if (row >= row_end) return;
     long long in_row = row;
     if (a.in_group_rows > 0) in_row += static_cast<long long>(row / a.in_group_rows) * a.in_group_gap;
     in_row += a.in_row_offset;
@@ -110,10 +110,10 @@ __global__ void cls_rows_kernel(bl_patchify_args a, int tokens) {
 }  // namespace misc
 }  // namespace bl
 
-extern "C" int bl_layernorm(const bl_layernorm_args* args, void* stream) {
-    using namespace bl;
-    if (args == nullptr) return fail(BL_ERR_INVALID, "layernorm: null args");
-    const bl_layernorm_args& a = *args;
+namespace bl {
+
+int prepare_layernorm_rows(const bl_layernorm_args& a, uint32_t row_begin, uint32_t row_end,
+                           Launch* out) {
     if (a.rows == 0 || a.cols == 0 || a.x == nullptr || a.out == nullptr || a.gamma == nullptr ||
         a.beta == nullptr)
         return fail(BL_ERR_INVALID, "layernorm: empty shape or null pointer");
@@ -124,24 +124,27 @@ extern "C" int bl_layernorm(const bl_layernorm_args* args, void* stream) {
     bl_layernorm_args b = a;
     if (b.ldx == 0) b.ldx = b.cols;
     if (b.ldo == 0) b.ldo = b.cols;
-    dim3 grid((a.rows + 7) / 8);
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (a.cols <= 128)
-        misc::layernorm_kernel<4><<<grid, 256, 0, s>>>(b);
-    else if (a.cols <= 384)
-        misc::layernorm_kernel<12><<<grid, 256, 0, s>>>(b);
-    else if (a.cols <= 512)
-        misc::layernorm_kernel<16><<<grid, 256, 0, s>>>(b);
-    else
-        misc::layernorm_kernel<32><<<grid, 256, 0, s>>>(b);
-    BL_CUDA_TRY(cudaGetLastError());
+    if (row_begin >= row_end || row_end > a.rows)
+        return fail(BL_ERR_INVALID, "layernorm: row part [%u, %u) outside [0, %u)", row_begin, row_end, a.rows);
+    const dim3 grid((row_end - row_begin + 7) / 8);
+    const int r0 = static_cast<int>(row_begin), r1 = static_cast<int>(row_end);
+    void (*kern)(bl_layernorm_args, int, int) = a.cols <= 128   ? misc::layernorm_kernel<4>
+                                      : a.cols <= 384 ? misc::layernorm_kernel<12>
+                                      : a.cols <= 512 ? misc::layernorm_kernel<16>
+                                                      : misc::layernorm_kernel<32>;
+    out->op = 3;
+    out->run = [=](cudaStream_t s) {
+        kern<<<grid, 256, 0, s>>>(b, r0, r1);
+        return cudaGetLastError();
+    };
     return BL_OK;
 }
 
-extern "C" int bl_patchify(const bl_patchify_args* args, void* stream) {
-    using namespace bl;
-    if (args == nullptr) return fail(BL_ERR_INVALID, "patchify: null args");
-    const bl_patchify_args& a = *args;
+int prepare_layernorm(const bl_layernorm_args& a, Launch* out) {
+    return prepare_layernorm_rows(a, 0, a.rows, out);
+}
+
+int prepare_patchify(const bl_patchify_args& a, Launch* out) {
     if (a.frames == 0 || a.patch == 0 || a.cin == 0 || a.side == 0 || a.side % a.patch != 0)
         return fail(BL_ERR_INVALID, "patchify: side %u is not whole patches of %u", a.side, a.patch);
     const uint32_t taps = a.patch * a.patch * a.cin;
@@ -152,17 +155,32 @@ extern "C" int bl_patchify(const bl_patchify_args* args, void* stream) {
         return fail(BL_ERR_INVALID, "patchify: null or misaligned buffers");
     if (a.a_dtype != BL_F16 && a.a_dtype != BL_BF16)
         return fail(BL_ERR_INVALID, "patchify: A dtype %d", a.a_dtype);
+    if (a.x != nullptr && (a.cls == nullptr || a.pos == nullptr || a.dim == 0))
+        return fail(BL_ERR_INVALID, "patchify: class-token rows need cls, pos and dim");
     const int g = static_cast<int>(a.side / a.patch);
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
     const long long work = static_cast<long long>(a.frames) * g * g * (a.k_pad / 8);
-    misc::patchify_kernel<<<static_cast<unsigned>((work + 255) / 256), 256, 0, s>>>(
-        a, g, static_cast<int>(taps));
-    BL_CUDA_TRY(cudaGetLastError());
-    if (a.x != nullptr) {
-        if (a.cls == nullptr || a.pos == nullptr || a.dim == 0)
-            return fail(BL_ERR_INVALID, "patchify: class-token rows need cls, pos and dim");
-        misc::cls_rows_kernel<<<a.frames, 128, 0, s>>>(a, g * g + 1);
-        BL_CUDA_TRY(cudaGetLastError());
-    }
+    const unsigned blocks = static_cast<unsigned>((work + 255) / 256);
+    out->op = 4;
+    out->run = [=](cudaStream_t s) {
+        misc::patchify_kernel<<<blocks, 256, 0, s>>>(a, g, static_cast<int>(taps));
+        if (a.x != nullptr) misc::cls_rows_kernel<<<a.frames, 128, 0, s>>>(a, g * g + 1);
+        return cudaGetLastError();
+    };
     return BL_OK;
+}
+
+}  // namespace bl
+
+extern "C" int bl_layernorm(const bl_layernorm_args* args, void* stream) {
+    if (args == nullptr) return bl::fail(BL_ERR_INVALID, "layernorm: null args");
+    bl::Launch l;
+    int rc = bl::prepare_layernorm(*args, &l);
+    return rc != BL_OK ? rc : bl::enqueue(l, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int bl_patchify(const bl_patchify_args* args, void* stream) {
+    if (args == nullptr) return bl::fail(BL_ERR_INVALID, "patchify: null args");
+    bl::Launch l;
+    int rc = bl::prepare_patchify(*args, &l);
+    return rc != BL_OK ? rc : bl::enqueue(l, static_cast<cudaStream_t>(stream));
 }

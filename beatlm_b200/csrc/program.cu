@@ -1,0 +1,408 @@
+// The program of a model on the device: prepared launches (the reference's
+// Kernels), the row split of Program::split, CUDA-graph replay, and the
+// cudaEvent slice timer with the reference SliceTimer's semantics.
+#include <cstdio>
+#include <cstring>
+#include <deque>
+#include <string>
+#include <vector>
+
+#include "host.h"
+
+// ------------------------------------------------------------------ split
+
+extern "C" uint32_t bl_split_edges(uint32_t extent, uint32_t grain, uint32_t count,
+                                   uint32_t* edges) {
+    if (grain == 0) grain = 1;
+    const uint64_t blocks = (static_cast<uint64_t>(extent) + grain - 1) / grain;
+    const uint64_t maxp = blocks > 0 ? blocks : 1;
+    uint64_t c = count < 1 ? 1 : count;
+    if (c > maxp) c = maxp;
+    if (edges != nullptr) {
+        for (uint64_t i = 0; i <= c; ++i) {
+            const uint64_t unit = blocks * i / c * grain;
+            edges[i] = static_cast<uint32_t>(unit < extent ? unit : extent);
+        }
+    }
+    return static_cast<uint32_t>(c);
+}
+
+extern "C" uint32_t bl_parts_within(uint64_t duration_us, uint64_t bound_us, uint32_t max_parts) {
+    if (bound_us == 0) return 0;
+    uint64_t want = duration_us / bound_us + (duration_us % bound_us != 0 ? 1 : 0);
+    if (want < 1) want = 1;
+    const uint64_t cap = max_parts < 1 ? 1 : max_parts;
+    return static_cast<uint32_t>(want < cap ? want : cap);
+}
+
+// ------------------------------------------------------------------ timer
+
+namespace bl {
+
+enum class SlotState { Free, Recording, Submitted, Held, Rejected, Invalid };
+
+struct TimerSlot {
+    SlotState state = SlotState::Free;
+    uint64_t frame = 0;
+    uint64_t seq = 0;  // submission order
+    std::vector<cudaEvent_t> begin, end;
+    std::vector<uint32_t> kernel;
+    uint32_t used = 0;
+};
+
+}  // namespace bl
+
+struct bl_timer {
+    uint32_t max_slices = 0;
+    bl::TimerSlot slots[BL_TIMER_RING_DEPTH];
+    uint32_t next = 0;           // ring position of the next claim
+    uint64_t next_seq = 0;
+    std::deque<int> submitted;   // slot indices in submission order
+    bl_timer_stats stats{};
+};
+
+namespace {
+bool valid_handle(const bl_timer* t, int32_t h) {
+    return t != nullptr && h >= 0 && h < BL_TIMER_RING_DEPTH;
+}
+void release(bl_timer* t, int i) {
+    t->slots[i].state = bl::SlotState::Free;
+    t->slots[i].used = 0;
+}
+}  // namespace
+
+extern "C" int bl_timer_create(uint32_t max_slices, bl_timer** out) {
+    using namespace bl;
+    if (out == nullptr || max_slices == 0) return fail(BL_ERR_INVALID, "timer: max_slices must be > 0");
+    bl_timer* t = new bl_timer();
+    t->max_slices = max_slices;
+    for (auto& s : t->slots) {
+        s.begin.resize(max_slices);
+        s.end.resize(max_slices);
+        s.kernel.resize(max_slices);
+        for (uint32_t i = 0; i < max_slices; ++i) {
+            if (cudaEventCreate(&s.begin[i]) != cudaSuccess ||
+                cudaEventCreate(&s.end[i]) != cudaSuccess) {
+                bl_timer_destroy(t);
+                return fail(BL_ERR_CUDA, "timer: cudaEventCreate failed");
+            }
+        }
+    }
+    *out = t;
+    return BL_OK;
+}
+
+extern "C" void bl_timer_destroy(bl_timer* t) {
+    if (t == nullptr) return;
+    for (auto& s : t->slots) {
+        for (auto e : s.begin) if (e) cudaEventDestroy(e);
+        for (auto e : s.end) if (e) cudaEventDestroy(e);
+    }
+    delete t;
+}
+
+extern "C" uint32_t bl_timer_max_slices(const bl_timer* t) { return t ? t->max_slices : 0; }
+
+extern "C" int bl_timer_begin_frame(bl_timer* t, uint64_t frame, int32_t* handle) {
+    using namespace bl;
+    if (t == nullptr || handle == nullptr) return fail(BL_ERR_INVALID, "timer: null argument");
+    const int i = static_cast<int>(t->next);
+    if (t->slots[i].state != SlotState::Free) {
+        t->stats.frames_skipped += 1;
+        *handle = -1;
+        return BL_OK;
+    }
+    t->next = (t->next + 1) % BL_TIMER_RING_DEPTH;
+    t->slots[i].state = SlotState::Recording;
+    t->slots[i].frame = frame;
+    t->slots[i].used = 0;
+    *handle = i;
+    return BL_OK;
+}
+
+static int submit(bl_timer* t, int32_t h, bool held) {
+    using namespace bl;
+    if (t == nullptr) return fail(BL_ERR_INVALID, "timer: null timer");
+    if (h == -1) return BL_OK;
+    if (!valid_handle(t, h) || t->slots[h].state != SlotState::Recording)
+        return fail(BL_ERR_INVALID, "timer: handle %d is not a frame being recorded", h);
+    t->slots[h].state = held ? SlotState::Held : SlotState::Submitted;
+    t->slots[h].seq = t->next_seq++;
+    t->submitted.push_back(h);
+    return BL_OK;
+}
+
+extern "C" int bl_timer_submitted(bl_timer* t, int32_t h) { return submit(t, h, false); }
+extern "C" int bl_timer_submitted_held(bl_timer* t, int32_t h) { return submit(t, h, true); }
+
+extern "C" int bl_timer_settle(bl_timer* t, int32_t h, int accept) {
+    using namespace bl;
+    if (!valid_handle(t, h) || t->slots[h].state != SlotState::Held)
+        return fail(BL_ERR_INVALID, "timer: handle %d is not a held frame", h);
+    t->slots[h].state = accept ? SlotState::Submitted : SlotState::Rejected;
+    return BL_OK;
+}
+
+extern "C" int bl_timer_drop(bl_timer* t, int32_t h) {
+    using namespace bl;
+    if (t == nullptr) return fail(BL_ERR_INVALID, "timer: null timer");
+    if (h == -1) return BL_OK;
+    if (!valid_handle(t, h) || t->slots[h].state != SlotState::Recording)
+        return fail(BL_ERR_INVALID, "timer: handle %d is not a frame being recorded", h);
+    release(t, h);
+    return BL_OK;
+}
+
+extern "C" size_t bl_timer_invalidate_submitted(bl_timer* t) {
+    if (t == nullptr) return 0;
+    size_t n = 0;
+    for (int i : t->submitted) {
+        auto& s = t->slots[i];
+        if (s.state == bl::SlotState::Submitted || s.state == bl::SlotState::Held) {
+            s.state = bl::SlotState::Invalid;
+            ++n;
+        }
+    }
+    return n;
+}
+
+extern "C" size_t bl_timer_in_flight(const bl_timer* t) {
+    if (t == nullptr) return 0;
+    size_t n = 0;
+    for (const auto& s : t->slots) n += s.state != bl::SlotState::Free;
+    return n;
+}
+
+extern "C" int bl_timer_collect_ready(bl_timer* t, bl_slice_time* out, size_t cap, size_t* n,
+                                      size_t* frames) {
+    using namespace bl;
+    if (t == nullptr || n == nullptr) return fail(BL_ERR_INVALID, "timer: null argument");
+    size_t written = 0, done = 0;
+    while (!t->submitted.empty()) {
+        const int i = t->submitted.front();
+        TimerSlot& s = t->slots[i];
+        if (s.state == SlotState::Invalid || s.state == SlotState::Rejected) {
+            // Never decoded; a marked frame holds nothing back once its
+            // events can no longer be written (they may still be pending, but
+            // nothing reads them before the slot is re-recorded in order).
+            t->stats.frames_failed += 1;
+            t->submitted.pop_front();
+            release(t, i);
+            continue;
+        }
+        if (s.state == SlotState::Held) break;  // unsettled: later frames wait
+        bool failed = false;
+        if (s.used > 0) {
+            cudaError_t q = cudaEventQuery(s.end[s.used - 1]);
+            if (q == cudaErrorNotReady) break;
+            if (q != cudaSuccess) failed = true;
+        }
+        if (!failed && written + s.used > cap) break;  // whole frames only
+        float ms = 0.0f;
+        for (uint32_t k = 0; k < s.used && !failed; ++k) {
+            float b = 0.0f;
+            if (cudaEventElapsedTime(&ms, s.begin[k], s.end[k]) != cudaSuccess ||
+                cudaEventElapsedTime(&b, s.begin[0], s.begin[k]) != cudaSuccess) {
+                failed = true;
+                break;
+            }
+            out[written + k].frame = s.frame;
+            out[written + k].slice = k;
+            out[written + k].kernel = s.kernel[k];
+            out[written + k].begin_us = 1000.0 * b;
+            out[written + k].micros = 1000.0 * ms;
+        }
+        t->submitted.pop_front();
+        if (failed) {
+            cudaGetLastError();  // a failed query must not leak into later calls
+            t->stats.frames_failed += 1;
+        } else {
+            written += s.used;
+            done += 1;
+            t->stats.frames_collected += 1;
+        }
+        release(t, i);
+    }
+    *n = written;
+    if (frames != nullptr) *frames = done;
+    return BL_OK;
+}
+
+extern "C" int bl_timer_get_stats(const bl_timer* t, bl_timer_stats* out) {
+    if (t == nullptr || out == nullptr) return bl::fail(BL_ERR_INVALID, "timer: null argument");
+    *out = t->stats;
+    return BL_OK;
+}
+
+// ------------------------------------------------------------------ kernels
+
+struct bl_kernels {
+    std::vector<bl::Launch> launches;
+    std::vector<std::string> labels;
+};
+
+struct bl_graph {
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+};
+
+namespace {
+
+int add_spec(bl_kernels* k, const bl_kernel_spec& s, size_t index) {
+    using namespace bl;
+    if (s.args == nullptr) return fail(BL_ERR_INVALID, "kernel %zu: null args", index);
+    const std::string base = s.label ? s.label : ("kernel " + std::to_string(index));
+    uint32_t extent = 1, grain = 1;
+    switch (s.op) {
+        case BL_OP_ATTENTION: {
+            const auto& a = *static_cast<const bl_attention_args*>(s.args);
+            extent = a.row_end > a.row_begin ? a.row_end - a.row_begin : 0;
+            grain = 128;
+            break;
+        }
+        case BL_OP_GEMM: extent = static_cast<const bl_gemm_args*>(s.args)->m; grain = 128; break;
+        case BL_OP_LAYERNORM: extent = static_cast<const bl_layernorm_args*>(s.args)->rows; break;
+        case BL_OP_PATCHIFY: break;
+        default: return fail(BL_ERR_INVALID, "kernel %zu: unknown op %d", index, s.op);
+    }
+    std::vector<uint32_t> edges(static_cast<size_t>(s.parts > 1 ? s.parts : 1) + 1);
+    const uint32_t count = s.op == BL_OP_PATCHIFY ? 1 : bl_split_edges(extent, grain, s.parts, edges.data());
+    if (s.op == BL_OP_PATCHIFY) { edges[0] = 0; edges[1] = 1; }
+    for (uint32_t i = 0; i < count; ++i) {
+        Launch l;
+        int rc = BL_OK;
+        switch (s.op) {
+            case BL_OP_ATTENTION: {
+                bl_attention_args a = *static_cast<const bl_attention_args*>(s.args);
+                const uint32_t r0 = a.row_begin;
+                a.row_begin = r0 + edges[i];
+                a.row_end = r0 + edges[i + 1];
+                rc = prepare_attention(a, &l);
+                break;
+            }
+            case BL_OP_GEMM:
+                rc = prepare_gemm_rows(*static_cast<const bl_gemm_args*>(s.args), edges[i],
+                                       edges[i + 1], &l);
+                break;
+            case BL_OP_LAYERNORM:
+                rc = prepare_layernorm_rows(*static_cast<const bl_layernorm_args*>(s.args),
+                                            edges[i], edges[i + 1], &l);
+                break;
+            default:
+                rc = prepare_patchify(*static_cast<const bl_patchify_args*>(s.args), &l);
+        }
+        if (rc != BL_OK) return rc;
+        k->launches.push_back(std::move(l));
+        k->labels.push_back(count == 1 ? base
+                                       : base + " [" + std::to_string(i + 1) + "/" +
+                                             std::to_string(count) + "]");
+    }
+    return BL_OK;
+}
+
+int encode_one(const bl_kernels* k, size_t kernel, cudaStream_t s, bl_timer* t, int32_t h) {
+    using namespace bl;
+    if (kernel >= k->launches.size())
+        return fail(BL_ERR_INVALID, "encode: kernel %zu of %zu", kernel, k->launches.size());
+    TimerSlot* slot = nullptr;
+    if (t != nullptr && h >= 0) {
+        if (!valid_handle(t, h) || t->slots[h].state != SlotState::Recording)
+            return fail(BL_ERR_INVALID, "encode: timer handle %d is not being recorded", h);
+        slot = &t->slots[h];
+        if (slot->used >= t->max_slices)
+            return fail(BL_ERR_CAPACITY, "encode: more than %u timed passes in one frame",
+                        t->max_slices);
+        BL_CUDA_TRY(cudaEventRecord(slot->begin[slot->used], s));
+    }
+    int rc = enqueue(k->launches[kernel], s);
+    if (rc != BL_OK) return rc;
+    if (slot != nullptr) {
+        BL_CUDA_TRY(cudaEventRecord(slot->end[slot->used], s));
+        slot->kernel[slot->used] = static_cast<uint32_t>(kernel);
+        slot->used += 1;
+    }
+    return BL_OK;
+}
+
+}  // namespace
+
+extern "C" int bl_kernels_create(const bl_kernel_spec* specs, size_t n, bl_kernels** out) {
+    if (out == nullptr || (specs == nullptr && n > 0))
+        return bl::fail(BL_ERR_INVALID, "kernels: null argument");
+    bl_kernels* k = new bl_kernels();
+    for (size_t i = 0; i < n; ++i) {
+        int rc = add_spec(k, specs[i], i);
+        if (rc != BL_OK) {
+            delete k;
+            return rc;
+        }
+    }
+    *out = k;
+    return BL_OK;
+}
+
+extern "C" void bl_kernels_destroy(bl_kernels* k) { delete k; }
+
+extern "C" size_t bl_kernels_len(const bl_kernels* k) { return k ? k->launches.size() : 0; }
+
+extern "C" const char* bl_kernels_label(const bl_kernels* k, size_t kernel) {
+    if (k == nullptr || kernel >= k->labels.size()) return nullptr;
+    return k->labels[kernel].c_str();
+}
+
+extern "C" int bl_kernels_encode(const bl_kernels* k, size_t kernel, void* stream, bl_timer* t,
+                                 int32_t frame) {
+    if (k == nullptr) return bl::fail(BL_ERR_INVALID, "encode: null kernels");
+    return encode_one(k, kernel, static_cast<cudaStream_t>(stream), t, frame);
+}
+
+extern "C" int bl_kernels_encode_range(const bl_kernels* k, size_t begin, size_t end, void* stream,
+                                       bl_timer* t, int32_t frame) {
+    if (k == nullptr || begin > end || end > k->launches.size())
+        return bl::fail(BL_ERR_INVALID, "encode: range [%zu, %zu)", begin, end);
+    for (size_t i = begin; i < end; ++i) {
+        int rc = encode_one(k, i, static_cast<cudaStream_t>(stream), t, frame);
+        if (rc != BL_OK) return rc;
+    }
+    return BL_OK;
+}
+
+extern "C" int bl_kernels_capture(const bl_kernels* k, void* stream, bl_graph** out) {
+    using namespace bl;
+    if (k == nullptr || out == nullptr) return fail(BL_ERR_INVALID, "capture: null argument");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (s == nullptr) return fail(BL_ERR_INVALID, "capture: needs a non-default stream");
+    BL_CUDA_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeRelaxed));
+    int rc = BL_OK;
+    for (size_t i = 0; i < k->launches.size() && rc == BL_OK; ++i) rc = enqueue(k->launches[i], s);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(s, &g);
+    if (rc != BL_OK) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (e != cudaSuccess) return fail(BL_ERR_CUDA, "capture: %s", cudaGetErrorString(e));
+    bl_graph* gr = new bl_graph();
+    gr->graph = g;
+    e = cudaGraphInstantiate(&gr->exec, g, 0);
+    if (e != cudaSuccess) {
+        cudaGraphDestroy(g);
+        delete gr;
+        return fail(BL_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
+    }
+    *out = gr;
+    return BL_OK;
+}
+
+extern "C" int bl_graph_launch(const bl_graph* g, void* stream) {
+    if (g == nullptr) return bl::fail(BL_ERR_INVALID, "graph: null");
+    BL_CUDA_TRY(cudaGraphLaunch(g->exec, static_cast<cudaStream_t>(stream)));
+    return BL_OK;
+}
+
+extern "C" void bl_graph_destroy(bl_graph* g) {
+    if (g == nullptr) return;
+    if (g->exec) cudaGraphExecDestroy(g->exec);
+    if (g->graph) cudaGraphDestroy(g->graph);
+    delete g;
+}

@@ -177,7 +177,8 @@ class DeviceBlock:
 
 class Buffers:
     """Activation buffers for `frames` frames of `tokens` tokens, allocated
-    once (zero allocation in the forward pass)."""
+    once (zero allocation in the forward pass). The image buffer is what a
+    prebuilt program reads, so a caller writes each frame's pixels there."""
 
     def __init__(self, cfg: ViTConfig, frames: int, dtype: str, tokens: int | None = None,
                  device="cuda", features: bool = True):
@@ -186,6 +187,8 @@ class Buffers:
         t = cfg.tokens if tokens is None else tokens
         rows = frames * t
         self.frames, self.tokens, self.rows = frames, t, rows
+        self.image = torch.zeros((frames, cfg.side, cfg.side, cfg.cin), dtype=torch.float32,
+                                 device=device)
         self.x = torch.empty((rows, cfg.dim), dtype=torch.float32, device=device)
         self.qkv = torch.empty((rows, 3 * cfg.dim), dtype=torch.int16, device=device)
         self.o = torch.empty((rows, cfg.dim), dtype=td, device=device)
@@ -196,21 +199,36 @@ class Buffers:
                          if features else [])
 
 
-def run_block(blk: DeviceBlock, cfg: ViTConfig, buf: Buffers, stream=None):
-    """One pre-norm block in place on ``buf.x`` (reference.rs:520-544):
+def block_specs(blk: DeviceBlock, cfg: ViTConfig, buf: Buffers, layer: int = 0,
+                parts: int = 1) -> list:
+    """The five fused kernels of one pre-norm block (reference.rs:520-544),
+    in place on ``buf.x``:
     x1 = x + ls1 * proj(attention(norm1(x))); x = x1 + ls2 * fc2(gelu(fc1(norm2(x1))))."""
+    from .runtime import Spec
     d = cfg.dim
-    ops.linear(blk.qkv_w, ln=(buf.x, blk.norm1[0], blk.norm1[1], cfg.eps), bias=blk.qkv_b,
-               out=buf.qkv, out_dtype=blk.dtype, out_split=(2 * d, "f16"), stream=stream)
-    ops.attention(buf.qkv, tokens=buf.tokens, heads=cfg.heads, head_dim=cfg.head_dim,
-                  batch=buf.frames, qk_dtype=blk.dtype, out=buf.o.view(buf.frames, buf.tokens, d),
-                  out_dtype=blk.dtype, stream=stream)
-    ops.linear(blk.proj_w, a=buf.o, bias=blk.proj_b, chan_scale=blk.ls1, residual=buf.x,
-               out=buf.x, stream=stream)
-    ops.linear(blk.fc1_w, ln=(buf.x, blk.norm2[0], blk.norm2[1], cfg.eps), bias=blk.fc1_b,
-               act="gelu_erf", out=buf.h, stream=stream)
-    ops.linear(blk.fc2_w, a=buf.h, bias=blk.fc2_b, chan_scale=blk.ls2, residual=buf.x,
-               out=buf.x, stream=stream)
+    name = "block%d." % layer
+    return [
+        Spec(ops.gemm_args(blk.qkv_w, ln=(buf.x, blk.norm1[0], blk.norm1[1], cfg.eps),
+                           bias=blk.qkv_b, out=buf.qkv, out_dtype=blk.dtype,
+                           out_split=(2 * d, "f16")), name + "qkv", parts),
+        Spec(ops.attention_args(buf.qkv, tokens=buf.tokens, heads=cfg.heads,
+                                head_dim=cfg.head_dim, batch=buf.frames, qk_dtype=blk.dtype,
+                                out=buf.o), name + "attention", parts),
+        Spec(ops.gemm_args(blk.proj_w, a=buf.o, bias=blk.proj_b, chan_scale=blk.ls1,
+                           residual=buf.x, out=buf.x), name + "proj", parts),
+        Spec(ops.gemm_args(blk.fc1_w, ln=(buf.x, blk.norm2[0], blk.norm2[1], cfg.eps),
+                           bias=blk.fc1_b, act="gelu_erf", out=buf.h), name + "fc1", parts),
+        Spec(ops.gemm_args(blk.fc2_w, a=buf.h, bias=blk.fc2_b, chan_scale=blk.ls2,
+                           residual=buf.x, out=buf.x), name + "fc2", parts),
+    ]
+
+
+def run_block(blk: DeviceBlock, cfg: ViTConfig, buf: Buffers, stream=None, parts: int = 1):
+    """One block, built and encoded at once (tests; the encoder prebuilds)."""
+    from .runtime import Kernels
+    k = Kernels(block_specs(blk, cfg, buf, parts=parts))
+    k.encode_all(stream)
+    return k
 
 
 class Encoder:
@@ -233,36 +251,60 @@ class Encoder:
         self.pos = f32(np.asarray(weights["pos"], np.float32).reshape(cfg.tokens, cfg.dim))
         self.norm = (f32(weights["norm_g"]), f32(weights["norm_b"]))
         self._buffers = {}
+        self._programs = {}
 
     def buffers(self, frames: int) -> Buffers:
         if frames not in self._buffers:
             self._buffers[frames] = Buffers(self.cfg, frames, self.dtype)
         return self._buffers[frames]
 
-    def forward(self, image, frames: int = 1, stream=None, layers: int | None = None):
-        """``image``: device f32 NHWC [frames][side][side][cin]. Returns the
-        feature maps (device f32 [frames * grid^2][dim] each) of the layers in
-        ``out_indices`` (those within ``layers``)."""
+    def specs(self, frames: int, layers: int | None = None, parts: int = 1) -> list:
+        """The encoder as kernel specs over the buffers of `frames` frames."""
+        from .runtime import Spec
         cfg, buf = self.cfg, self.buffers(frames)
         t = cfg.tokens
-        ops.patchify(image, frames=frames, side=cfg.side, patch=cfg.patch, cin=cfg.cin,
-                     k_pad=cfg.k_pad, a_out=buf.patches, a_dtype=self.dtype, cls=self.cls,
-                     pos=self.pos, x=buf.x, stream=stream)
-        ops.linear(self.patch_w, a=buf.patches, bias=self.patch_b, residual=self.pos,
-                   res_period=t, out=buf.x, out_row_offset=1, out_group=(t - 1, 1),
-                   stream=stream)
+        out = [
+            Spec(ops.patchify_args(buf.image, frames=frames, side=cfg.side, patch=cfg.patch,
+                                   cin=cfg.cin, k_pad=cfg.k_pad, a_out=buf.patches,
+                                   a_dtype=self.dtype, cls=self.cls, pos=self.pos, x=buf.x),
+                 "embed.patchify"),
+            Spec(ops.gemm_args(self.patch_w, a=buf.patches, bias=self.patch_b, residual=self.pos,
+                               res_period=t, out=buf.x, out_row_offset=1, out_group=(t - 1, 1)),
+                 "embed.patch", parts),
+        ]
         n = cfg.layers if layers is None else layers
-        feats = []
         for i in range(n):
-            run_block(self.blocks[i], cfg, buf, stream)
+            out += block_specs(self.blocks[i], cfg, buf, i, parts)
             if (i + 1) in cfg.out_indices:
                 f = buf.features[cfg.out_indices.index(i + 1)]
-                ops.layernorm(buf.x, self.norm[0], self.norm[1], cfg.eps, out=f,
-                              in_row_offset=1, in_group=(t - 1, 1), stream=stream)
-                feats.append(f)
-        return feats
+                out.append(Spec(ops.layernorm_args(buf.x, self.norm[0], self.norm[1], cfg.eps,
+                                                   out=f, in_row_offset=1, in_group=(t - 1, 1)),
+                                "features.%d" % (i + 1), parts))
+        return out
+
+    def program(self, frames: int = 1, layers: int | None = None, parts: int = 1):
+        from .runtime import Kernels
+        key = (frames, layers, parts)
+        if key not in self._programs:
+            self._programs[key] = Kernels(self.specs(frames, layers, parts))
+        return self._programs[key]
+
+    def features(self, frames: int, layers: int | None = None) -> list:
+        n = self.cfg.layers if layers is None else layers
+        buf = self.buffers(frames)
+        return [buf.features[j] for j, i in enumerate(self.cfg.out_indices) if i <= n]
+
+    def forward(self, image, frames: int = 1, stream=None, layers: int | None = None):
+        """``image``: device f32 NHWC [frames][side][side][cin], copied into the
+        program's image buffer. Returns the feature maps (device f32
+        [frames * grid^2][dim] each) of the layers in ``out_indices`` (those
+        within ``layers``)."""
+        buf = self.buffers(frames)
+        buf.image.copy_(image)
+        self.program(frames, layers).encode_all(stream)
+        return self.features(frames, layers)
 
     def launches_per_frame_batch(self, layers: int | None = None) -> int:
         n = self.cfg.layers if layers is None else layers
         taken = sum(1 for i in self.cfg.out_indices if i <= n)
-        return 3 + 5 * n + taken  # patchify (2) + patch GEMM, 5 per block, final norms
+        return 3 + 5 * n + taken  # patchify (2 kernels) + patch GEMM, 5 per block, norms

@@ -1,5 +1,9 @@
-"""Host-side calls of the fused kernels, on device buffers (torch tensors are
-used only as device memory and for the current stream)."""
+"""Host-side calls of the fused kernels on device buffers.
+
+Torch tensors serve only as device memory and streams. Every op has two forms:
+``*_args(...)`` packs the C-ABI argument struct (for a prebuilt program, see
+``runtime.Kernels``), and the plain call packs and launches at once.
+"""
 from __future__ import annotations
 
 import ctypes
@@ -9,14 +13,23 @@ import numpy as np
 
 from . import _native as N
 
-def _dtype_code(name: str) -> int:
-    return {"f32": N.BL_F32, "f16": N.BL_F16, "bf16": N.BL_BF16}[name]
+_TD = {"f32": N.BL_F32, "f16": N.BL_F16, "bf16": N.BL_BF16}
+ACT = {None: 0, "none": 0, "relu": 1, "gelu_tanh": 2, "gelu_erf": 3}
 
 
 def _stream_ptr(stream):
     import torch
     s = stream if stream is not None else torch.cuda.current_stream()
     return ctypes.c_void_p(s.cuda_stream)
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _dt(t):
+    import torch
+    return {torch.float32: N.BL_F32, torch.float16: N.BL_F16, torch.bfloat16: N.BL_BF16}[t.dtype]
 
 
 def pack_qkv(qkv, qk_dtype: str = "f16", device="cuda"):
@@ -33,6 +46,25 @@ def pack_qkv(qkv, qk_dtype: str = "f16", device="cuda"):
     return out.to(device)
 
 
+# ------------------------------------------------------------------ attention
+
+def attention_args(qkv, *, tokens, heads, out, head_dim=64, batch=1, qk_dtype="f16",
+                   out_dtype=None, scale=None, rows=None, head_range=None, out_head_base=0,
+                   qkv_row_stride=0, out_row_stride=None):
+    if scale is None:
+        scale = 1.0 / math.sqrt(head_dim)
+    r0, r1 = rows or (0, tokens)
+    h0, h1 = head_range or (0, heads)
+    odt = _TD[out_dtype] if out_dtype is not None else _dt(out)
+    return N.AttentionArgs(batch=batch, tokens=tokens, heads=heads, head_dim=head_dim,
+                           head_begin=h0, head_end=h1, row_begin=r0, row_end=r1, scale=scale,
+                           qk_dtype=_TD[qk_dtype], v_dtype=N.BL_F16, out_dtype=odt,
+                           qkv=qkv.data_ptr(), qkv_row_stride=qkv_row_stride,
+                           out=out.data_ptr(),
+                           out_row_stride=out.shape[-1] if out_row_stride is None
+                           else out_row_stride, out_head_base=out_head_base)
+
+
 def attention(qkv, *, tokens: int, heads: int, head_dim: int = 64, batch: int = 1,
               qk_dtype: str = "f16", out=None, out_dtype: str = "f32", scale: float | None = None,
               rows: tuple[int, int] | None = None, head_range: tuple[int, int] | None = None,
@@ -41,48 +73,26 @@ def attention(qkv, *, tokens: int, heads: int, head_dim: int = 64, batch: int = 
     (reference kernel.rs:722-777) on packed ``[batch][tokens][3][heads][64]``
     16-bit ``qkv``; returns ``out`` ``[batch][tokens][heads * 64]``."""
     import torch
-    if scale is None:
-        scale = 1.0 / math.sqrt(head_dim)
-    r0, r1 = rows or (0, tokens)
     h0, h1 = head_range or (0, heads)
     width = (h1 - out_head_base) * head_dim if head_range else heads * head_dim
     if out is None:
         tdt = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[out_dtype]
         out = torch.zeros((batch, tokens, width), dtype=tdt, device=qkv.device)
-    a = N.AttentionArgs(batch=batch, tokens=tokens, heads=heads, head_dim=head_dim,
-                        head_begin=h0, head_end=h1, row_begin=r0, row_end=r1, scale=scale,
-                        qk_dtype=_dtype_code(qk_dtype), v_dtype=N.BL_F16,
-                        out_dtype=_dtype_code(out_dtype), qkv=qkv.data_ptr(), qkv_row_stride=0,
-                        out=out.data_ptr(), out_row_stride=out.shape[-1],
-                        out_head_base=out_head_base)
+        odt = None
+    else:  # a float tensor's own type decides; a 16-bit container takes out_dtype
+        odt = None if out.dtype.is_floating_point else out_dtype
+    a = attention_args(qkv, tokens=tokens, heads=heads, out=out, head_dim=head_dim, batch=batch,
+                       qk_dtype=qk_dtype, out_dtype=odt, scale=scale, rows=rows,
+                       head_range=head_range, out_head_base=out_head_base)
     N.check(N.lib().bl_attention(ctypes.byref(a), _stream_ptr(stream)))
     return out
 
 
-ACT = {None: 0, "none": 0, "relu": 1, "gelu_tanh": 2, "gelu_erf": 3}
-_TD = {"f32": N.BL_F32, "f16": N.BL_F16, "bf16": N.BL_BF16}
+# ------------------------------------------------------------------ linear
 
-
-def _ptr(t):
-    return None if t is None else t.data_ptr()
-
-
-def _dt(t):
-    import torch
-    return {torch.float32: N.BL_F32, torch.float16: N.BL_F16, torch.bfloat16: N.BL_BF16}[t.dtype]
-
-
-def linear(w, *, a=None, ln=None, bias=None, act=None, scale=None, chan_scale=None,
-           residual=None, res_period=0, out, out_dtype=None, out_split=None, m=None,
-           out_row_offset=0, out_group=(0, 0), tile_n=0, stream=None):
-    """``out = epilogue(A . w^T)`` on the tensor cores (``bl_gemm``).
-
-    ``w`` is the 16-bit weight ``[n][k]`` (f16 or bf16; A is converted to the
-    same type); A is the 16-bit ``a`` ``[m][k]`` or, with
-    ``ln=(x, gamma, beta, eps)``, LayerNorm of the f32 rows ``x`` computed
-    inside the kernel. ``out_dtype`` defaults to ``out``'s own type;
-    ``out_split=(col, dtype)`` stores columns from ``col`` on as ``dtype``
-    (the f16 V part of packed Q|K|V rows)."""
+def gemm_args(w, *, a=None, ln=None, bias=None, act=None, scale=None, chan_scale=None,
+              residual=None, res_period=0, out, out_dtype=None, out_split=None, m=None,
+              out_row_offset=0, out_group=(0, 0), tile_n=0):
     import torch
     n, k = w.shape
     ab = {torch.float16: "f16", torch.bfloat16: "bf16"}[w.dtype]
@@ -107,27 +117,49 @@ def linear(w, *, a=None, ln=None, bias=None, act=None, scale=None, chan_scale=No
         g.ln_x, g.ln_ldx, g.ln_gamma, g.ln_beta, g.ln_eps = (x.data_ptr(), x.stride(0),
                                                              gamma.data_ptr(), beta.data_ptr(),
                                                              eps)
+    return g
+
+
+def linear(w, *, stream=None, **kw):
+    """``out = epilogue(A . w^T)`` on the tensor cores (``bl_gemm``).
+
+    ``w`` is the 16-bit weight ``[n][k]`` (f16 or bf16; A is converted to the
+    same type); A is the 16-bit ``a`` ``[m][k]`` or, with
+    ``ln=(x, gamma, beta, eps)``, LayerNorm of the f32 rows ``x`` computed
+    inside the kernel. ``out_dtype`` defaults to ``out``'s own type;
+    ``out_split=(col, dtype)`` stores columns from ``col`` on as ``dtype``
+    (the f16 V part of packed Q|K|V rows)."""
+    g = gemm_args(w, **kw)
     N.check(N.lib().bl_gemm(ctypes.byref(g), _stream_ptr(stream)))
-    return out
+    return kw["out"]
 
 
-def layernorm(x, gamma, beta, eps, *, out, rows=None, in_row_offset=0, in_group=(0, 0),
-              stream=None):
+# ------------------------------------------------------------------ others
+
+def layernorm_args(x, gamma, beta, eps, *, out, rows=None, in_row_offset=0, in_group=(0, 0)):
     rows = out.shape[0] if rows is None else rows
-    a = N.LayerNormArgs(rows=rows, cols=x.shape[1], x=x.data_ptr(), ldx=x.stride(0),
-                        gamma=gamma.data_ptr(), beta=beta.data_ptr(), eps=eps,
-                        out=out.data_ptr(), out_dtype=_dt(out), ldo=out.stride(0),
-                        in_row_offset=in_row_offset, in_group_rows=in_group[0],
-                        in_group_gap=in_group[1])
+    return N.LayerNormArgs(rows=rows, cols=x.shape[1], x=x.data_ptr(), ldx=x.stride(0),
+                           gamma=gamma.data_ptr(), beta=beta.data_ptr(), eps=eps,
+                           out=out.data_ptr(), out_dtype=_dt(out), ldo=out.stride(0),
+                           in_row_offset=in_row_offset, in_group_rows=in_group[0],
+                           in_group_gap=in_group[1])
+
+
+def layernorm(x, gamma, beta, eps, *, out, stream=None, **kw):
+    a = layernorm_args(x, gamma, beta, eps, out=out, **kw)
     N.check(N.lib().bl_layernorm(ctypes.byref(a), _stream_ptr(stream)))
     return out
 
 
-def patchify(image, *, frames, side, patch, cin, k_pad, a_out, a_dtype="bf16", cls=None,
-             pos=None, x=None, stream=None):
-    a = N.PatchifyArgs(frames=frames, side=side, patch=patch, cin=cin, k_pad=k_pad,
-                       dim=0 if cls is None else cls.numel(), image=image.data_ptr(),
-                       a=a_out.data_ptr(), a_dtype=_TD[a_dtype], cls=_ptr(cls), pos=_ptr(pos),
-                       x=_ptr(x))
+def patchify_args(image, *, frames, side, patch, cin, k_pad, a_out, a_dtype="bf16", cls=None,
+                  pos=None, x=None):
+    return N.PatchifyArgs(frames=frames, side=side, patch=patch, cin=cin, k_pad=k_pad,
+                          dim=0 if cls is None else cls.numel(), image=image.data_ptr(),
+                          a=a_out.data_ptr(), a_dtype=_TD[a_dtype], cls=_ptr(cls),
+                          pos=_ptr(pos), x=_ptr(x))
+
+
+def patchify(image, *, stream=None, **kw):
+    a = patchify_args(image, **kw)
     N.check(N.lib().bl_patchify(ctypes.byref(a), _stream_ptr(stream)))
-    return a_out
+    return kw["a_out"]

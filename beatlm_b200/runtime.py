@@ -1,0 +1,184 @@
+"""Programs of prebuilt launches, CUDA-graph replay and the slice timer.
+
+Host mirror of the reference's ``Kernels`` (``crates/beatlm/src/codegen/
+kernels.rs:63-249``: build once, encode per frame) and ``SliceTimer``
+(``crates/beatlm/src/gpu/timer.rs:185-470``), over ``bl_kernels_*`` and
+``bl_timer_*``.
+"""
+from __future__ import annotations
+
+import ctypes
+import dataclasses
+
+from . import _native as N
+from .ops import _stream_ptr
+
+OP_ATTENTION, OP_GEMM, OP_LAYERNORM, OP_PATCHIFY = 1, 2, 3, 4
+_OP_OF = {N.AttentionArgs: OP_ATTENTION, N.GemmArgs: OP_GEMM,
+          N.LayerNormArgs: OP_LAYERNORM, N.PatchifyArgs: OP_PATCHIFY}
+
+
+@dataclasses.dataclass
+class Spec:
+    """One kernel of a program: its packed arguments, a label, its parts."""
+    args: ctypes.Structure
+    label: str
+    parts: int = 1
+
+    @property
+    def op(self) -> int:
+        return _OP_OF[type(self.args)]
+
+
+def split_edges(extent: int, grain: int, count: int) -> list[int]:
+    """Program::split's part edges (kernel.rs:2006-2029), from the library."""
+    edges = (ctypes.c_uint32 * (max(count, 1) + 1))()
+    c = N.lib().bl_split_edges(extent, grain, count, edges)
+    return list(edges[:c + 1])
+
+
+def parts_within(duration_us: int, bound_us: int, max_parts: int) -> int:
+    """KernelSpec::parts_within (kernel.rs:2048-2056); 0 for a zero bound."""
+    return N.lib().bl_parts_within(duration_us, bound_us, max_parts)
+
+
+class Kernels:
+    """Prebuilt launches of a program; ``len`` counts parts."""
+
+    def __init__(self, specs: list[Spec]):
+        arr = (N.KernelSpec * len(specs))()
+        self._labels = [s.label.encode() for s in specs]
+        for i, s in enumerate(specs):
+            arr[i] = N.KernelSpec(op=s.op, args=ctypes.cast(ctypes.pointer(s.args),
+                                                            ctypes.c_void_p),
+                                  label=self._labels[i], parts=s.parts)
+        h = ctypes.c_void_p()
+        N.check(N.lib().bl_kernels_create(arr, len(specs), ctypes.byref(h)))
+        self._h = h
+        self._graphs = []
+
+    def __len__(self) -> int:
+        return N.lib().bl_kernels_len(self._h)
+
+    def label(self, k: int) -> str:
+        s = N.lib().bl_kernels_label(self._h, k)
+        return s.decode() if s is not None else None
+
+    def encode(self, k: int, stream=None, timer: "SliceTimer | None" = None, frame: int = -1):
+        N.check(N.lib().bl_kernels_encode(self._h, k, _stream_ptr(stream),
+                                          timer._h if timer else None, frame))
+
+    def encode_all(self, stream=None, timer: "SliceTimer | None" = None, frame: int = -1,
+                   begin: int = 0, end: int | None = None):
+        end = len(self) if end is None else end
+        N.check(N.lib().bl_kernels_encode_range(self._h, begin, end, _stream_ptr(stream),
+                                                timer._h if timer else None, frame))
+
+    def capture(self, stream) -> "Graph":
+        g = ctypes.c_void_p()
+        N.check(N.lib().bl_kernels_capture(self._h, _stream_ptr(stream), ctypes.byref(g)))
+        graph = Graph(g)
+        self._graphs.append(graph)
+        return graph
+
+    def close(self):
+        for g in self._graphs:
+            g.close()
+        self._graphs = []
+        if self._h:
+            N.lib().bl_kernels_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Graph:
+    def __init__(self, h):
+        self._h = h
+
+    def launch(self, stream=None):
+        N.check(N.lib().bl_graph_launch(self._h, _stream_ptr(stream)))
+
+    def close(self):
+        if self._h:
+            N.lib().bl_graph_destroy(self._h)
+            self._h = None
+
+
+@dataclasses.dataclass
+class FrameTiming:
+    """What one frame's passes took (timer.rs:115): (kernel, micros) per
+    pass in encode order, and each pass's begin relative to the first."""
+    frame: int
+    compute: list
+    begin_us: list
+
+
+class SliceTimer:
+    RING_DEPTH = 3
+
+    def __init__(self, max_slices: int):
+        h = ctypes.c_void_p()
+        N.check(N.lib().bl_timer_create(max_slices, ctypes.byref(h)))
+        self._h = h
+        self.max_slices = max_slices
+
+    def begin_frame(self, frame: int) -> int:
+        """A handle for `frame`, or -1 when its ring slot is in flight."""
+        h = ctypes.c_int32()
+        N.check(N.lib().bl_timer_begin_frame(self._h, frame, ctypes.byref(h)))
+        return h.value
+
+    def submitted(self, handle: int):
+        N.check(N.lib().bl_timer_submitted(self._h, handle))
+
+    def submitted_held(self, handle: int):
+        N.check(N.lib().bl_timer_submitted_held(self._h, handle))
+
+    def settle(self, handle: int, accept: bool):
+        N.check(N.lib().bl_timer_settle(self._h, handle, 1 if accept else 0))
+
+    def drop(self, handle: int):
+        N.check(N.lib().bl_timer_drop(self._h, handle))
+
+    def invalidate_submitted(self) -> int:
+        return N.lib().bl_timer_invalidate_submitted(self._h)
+
+    def in_flight(self) -> int:
+        return N.lib().bl_timer_in_flight(self._h)
+
+    def collect_ready(self) -> list[FrameTiming]:
+        cap = self.max_slices * self.RING_DEPTH
+        buf = (N.SliceTime * cap)()
+        n, frames = ctypes.c_size_t(), ctypes.c_size_t()
+        N.check(N.lib().bl_timer_collect_ready(self._h, buf, cap, ctypes.byref(n),
+                                               ctypes.byref(frames)))
+        out: list[FrameTiming] = []
+        for i in range(n.value):
+            e = buf[i]
+            if not out or out[-1].frame != e.frame or e.slice == 0:
+                out.append(FrameTiming(e.frame, [], []))
+            out[-1].compute.append((e.kernel, e.micros))
+            out[-1].begin_us.append(e.begin_us)
+        return out
+
+    def stats(self) -> dict:
+        s = N.TimerStats()
+        N.check(N.lib().bl_timer_get_stats(self._h, ctypes.byref(s)))
+        return {"frames_skipped": s.frames_skipped, "frames_collected": s.frames_collected,
+                "frames_failed": s.frames_failed}
+
+    def close(self):
+        if self._h:
+            N.lib().bl_timer_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

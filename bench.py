@@ -94,6 +94,31 @@ class AttentionWorkload:
     """Config 1: one ViT-S attention op (T=1370, H=6, hd=64), batch 1."""
 
     name = "attention"
+    unit = "TFLOP/s"
+    dtype = "f16 Q/K/V and P; f32 scores, softmax and accumulator"
+    data = "synthetic Q/K/V ~ N(0,1), seeded"
+    workload_name = "vit_s_attention_op (config 1)"
+
+    def roofline(self, stream, avg_ms):
+        return {"achieved_tflops": self.flops / (avg_ms / 1e3) / 1e12,
+                "kernel": "bl::attn::attention_fwd",
+                "how": "CUDA events around every timed launch (a step is one launch)"}
+
+    @classmethod
+    def reference_step(cls, threads):
+        import numpy as np
+        import oracle
+        t, h = 1370, 6
+        rng = np.random.default_rng(1234)
+        qkv = oracle.round_f16(rng.standard_normal((t, 3 * h * 64), dtype=np.float32))
+        rows = 32
+        t0 = time.perf_counter()
+        oracle.attention(qkv, t, h, 64, rows=(0, rows), threads=threads)
+        per_row = (time.perf_counter() - t0) / rows
+        rows = int(max(16, min(t, 1.0 / max(per_row, 1e-9))))
+        fn = lambda: oracle.attention(qkv, t, h, 64, rows=(0, rows), threads=threads)
+        return fn, 4.0 * rows * t * h * 64 / 1e12, (
+            "%d of %d query rows x %d heads per step (oracle/oracle.c, f64)" % (rows, t, h))
 
     def __init__(self, rank: int, batch: int = 1):
         import numpy as np
@@ -156,7 +181,149 @@ class AttentionWorkload:
                           "oracle/oracle.c)" % (rows, t, h, n)}
 
 
-WORKLOADS = {"attention": AttentionWorkload}
+class EncoderWorkload:
+    """Config 3: the Depth-Anything-V2-Small ViT-S/14 encoder at 518 px, 12
+    blocks, bf16, random N(0, 0.02) weights (LayerNorm gamma 1 / beta 0,
+    LayerScale 1), one frame per forward (batch 1), input U[0,1] normalised by
+    the ImageNet mean/std. A step is one frame through a captured CUDA graph of
+    the whole encoder (patch embedding, 12 blocks of 5 fused kernels, the four
+    feature LayerNorms)."""
+
+    name = "encoder"
+    unit = "frames/s"
+    dtype = "bf16 (weights, activations, Q/K); f16 V and P; f32 accumulate and residual"
+    data = "synthetic: ImageNet-normalised U[0,1] 518x518x3 image, N(0,0.02) weights, seeded"
+    workload_name = "da_v2_small_encoder_518 (config 3)"
+
+    def roofline(self, stream, avg_ms):
+        prof = self.slice_profile(stream)
+        n, tot, avg_us = prof["attention"]
+        steps = n / self.cfg.layers
+        return {"achieved_tflops": self.attn_flops / (avg_us / 1e6) / 1e12,
+                "kernel": "bl::attn::attention_fwd (%d launches per frame)" % self.cfg.layers,
+                "how": "cudaEvent slice timer (bl_timer) around every kernel of 5 direct "
+                       "(non-graph) encodes after the timed region",
+                "kernels": {k: round(v[1] / steps, 2) for k, v in sorted(prof.items())}}
+
+    @classmethod
+    def reference_step(cls, threads):
+        """One encoder block of the oracle per step (a twelfth of a frame; the
+        patch embedding, under 1 % of a frame's arithmetic, is left out)."""
+        import numpy as np
+        import oracle
+        from beatlm_b200.model import ViTConfig, block_weights_normal
+        c = ViTConfig.small()
+        rng = np.random.default_rng(5)
+        w = block_weights_normal(rng, c.dim, c.mlp)
+        x = rng.standard_normal(c.tokens * c.dim, dtype=np.float32)
+        fn = lambda: oracle.vit_block(x, w, c.tokens, c.heads, c.head_dim, c.mlp, c.eps,
+                                      threads=threads)
+        return fn, 1.0 / c.layers, ("one ViT-S block (T=1370) per step = 1/12 frame, "
+                                    "f64 oracle, patch embedding excluded")
+
+    def __init__(self, rank: int, frames: int = 1, large: bool = False):
+        import numpy as np
+        import torch
+        from beatlm_b200.model import Encoder, ViTConfig, block_weights_normal
+        self.cfg = ViTConfig.large() if large else ViTConfig.small()
+        cfg = self.cfg
+        rng = np.random.default_rng(99 + rank)
+        n = lambda *s: rng.standard_normal(int(np.prod(s)), dtype=np.float32) * 0.02
+        w = {"blocks": [block_weights_normal(rng, cfg.dim, cfg.mlp) for _ in range(cfg.layers)],
+             "patch_w": n(cfg.patch, cfg.patch, cfg.cin, cfg.dim), "patch_b": n(cfg.dim),
+             "cls": n(cfg.dim), "pos": n(cfg.tokens, cfg.dim),
+             "norm_g": np.ones(cfg.dim, np.float32), "norm_b": np.zeros(cfg.dim, np.float32)}
+        self.frames = frames
+        self.enc = Encoder(cfg, w, "bf16")
+        mean = np.array([0.485, 0.456, 0.406], np.float32)
+        std = np.array([0.229, 0.224, 0.225], np.float32)
+        img = ((rng.random((frames, cfg.side, cfg.side, cfg.cin), dtype=np.float32) - mean)
+               / std).astype(np.float32)
+        self.host = torch.from_numpy(img).pin_memory()
+        self.buf = self.enc.buffers(frames)
+        self.buf.image.copy_(self.host)
+        self.prog = self.enc.program(frames)
+        self.graph = None
+        self.feats_host = [torch.empty(f.shape, dtype=f.dtype).pin_memory()
+                           for f in self.enc.features(frames)]
+        fl = cfg.flops_per_frame()
+        self.flops = fl["total"] * frames
+        self.attn_flops = 4.0 * cfg.tokens * cfg.tokens * cfg.dim * frames  # per layer launch
+        self.launches_per_step = self.enc.launches_per_frame_batch()
+
+    def config(self):
+        c = self.cfg
+        return {"workload": ("vit_l14_encoder (config 4)" if c.dim == 1024 else
+                             "da_v2_small_encoder_518 (config 3)"),
+                "frames_per_step": self.frames, "tokens": c.tokens, "dim": c.dim,
+                "heads": c.heads, "mlp": c.mlp, "layers": c.layers, "image": c.side,
+                "weights": "random N(0,0.02), LN gamma=1 beta=0, LayerScale=1",
+                "dtype": "bf16 weights/activations, f16 V and P, f32 residual",
+                "launch": "one CUDA graph per frame (%d kernels)" % self.launches_per_step,
+                "l2": "flushed before every timed step (256 MiB write)"}
+
+    def step(self, stream):
+        if self.graph is None:
+            self.graph = self.prog.capture(stream)
+        self.graph.launch(stream)
+
+    def step_e2e(self, stream):
+        self.buf.image.copy_(self.host, non_blocking=True)
+        self.step(stream)
+        for h, f in zip(self.feats_host, self.enc.features(self.frames)):
+            h.copy_(f, non_blocking=True)
+
+    def e2e_bytes(self):
+        return (self.host.numel() * 4, sum(h.numel() * 4 for h in self.feats_host))
+
+    def units(self):
+        return self.frames  # frames per step
+
+    def slice_profile(self, stream, frames: int = 5):
+        """Per-kernel durations from the cudaEvent slice timer over `frames`
+        direct (non-graph) encodes: {kind: (launches, total_us, avg_us)}."""
+        import torch
+        from beatlm_b200.runtime import SliceTimer
+        t = SliceTimer(max_slices=len(self.prog))
+        kinds = {}
+        for f in range(frames):
+            h = t.begin_frame(f)
+            self.prog.encode_all(stream, timer=t, frame=h)
+            t.submitted(h)
+            torch.cuda.synchronize()
+            for ft in t.collect_ready():
+                for k, us in ft.compute:
+                    kind = self.prog.label(k).split(".")[-1].split(" ")[0]
+                    n, tot = kinds.get(kind, (0, 0.0))
+                    kinds[kind] = (n + 1, tot + us)
+        t.close()
+        return {k: (n, tot, tot / n) for k, (n, tot) in kinds.items()}
+
+    def cpu_baseline(self, threads: int, budget_s: float = 15.0):
+        """One encoder block through the oracle (reference.rs:520-544) on all
+        host cores, scaled to a frame: 12 blocks plus the patch embedding."""
+        import oracle
+        from beatlm_b200.model import block_weights_normal
+        import numpy as np
+        c = self.cfg
+        rng = np.random.default_rng(5)
+        w = block_weights_normal(rng, c.dim, c.mlp)
+        x = rng.standard_normal(c.tokens * c.dim, dtype=np.float32)
+        t0 = time.perf_counter()
+        oracle.vit_block(x, w, c.tokens, c.heads, c.head_dim, c.mlp, c.eps, threads=threads)
+        t_block = time.perf_counter() - t0
+        img = self.host[0].numpy().ravel()
+        pw = rng.standard_normal(c.taps * c.dim, dtype=np.float32) * 0.02
+        t0 = time.perf_counter()
+        oracle.patch_embed(img, pw, None, c.grid, c.grid, c.patch, c.cin, c.dim, threads=threads)
+        t_embed = time.perf_counter() - t0
+        frame_s = c.layers * t_block + t_embed
+        return {"value": 1.0 / frame_s, "unit": "frames/s", "cores": threads, "kind": "port",
+                "sample": "1 block (%.2f s) x %d + patch embedding (%.2f s), f64 oracle, "
+                          "%d threads" % (t_block, c.layers, t_embed, threads)}
+
+
+WORKLOADS = {"attention": AttentionWorkload, "encoder": EncoderWorkload}
 
 
 # ------------------------------------------------------------------ timing
@@ -186,7 +353,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="attention", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="encoder", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true",
                     help="skip the cpu_baseline leg (profiling runs)")
     args = ap.parse_args()
@@ -232,28 +399,33 @@ def main():
         total_ms, e2e_ms = float(t[0]), float(t[1])
     value = wl.units() * args.steps * world / (total_ms / 1e3)
     e2e_value = wl.units() * args.steps * world / (e2e_ms / 1e3)
+    extra = wl.roofline(stream, total_ms / args.steps)
+    barrier()
 
     if rank == 0:
         pk = peaks()
         avg_ms = total_ms / args.steps
-        achieved = wl.flops / (avg_ms / 1e3) / 1e12
+        achieved, kernels = extra["achieved_tflops"], extra.get("kernels")
         line = {
-            "metric": METRIC, "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world,
+            "metric": METRIC, "value": round(value, 3), "unit": wl.unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(avg_ms, 5),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f16 (Q/K/V, P); f32 accumulate", "data": "synthetic N(0,1), seeded",
-            "config": dict(wl.config(), parallelism="replicas x%d" % world),
-            "e2e": {"value": round(e2e_value, 3), "unit": "TFLOP/s",
+            "dtype": wl.dtype, "data": wl.data,
+            "config": dict(wl.config(), parallelism="replicas x%d (no collective)" % world),
+            "e2e": {"value": round(e2e_value, 3), "unit": wl.unit,
                     "h2d_bytes_per_step": wl.e2e_bytes()[0],
                     "d2h_bytes_per_step": wl.e2e_bytes()[1]},
             "gpu_launches": wl.launches_per_step * args.steps,
             "roofline": {"bound": "tensor", "achieved": round(achieved, 2),
                          "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": round(achieved / pk["bf16_tflops"], 4),
-                         "peak_source": pk["source"] + " (burst bf16, MEASURED_PEAKS.json)",
-                         "traffic": None, "kernel": "bl::attn::attention_fwd"},
+                         "peak_source": pk["source"] + " burst bf16 (MEASURED_PEAKS.json)",
+                         "traffic": extra.get("traffic"), "kernel": extra["kernel"],
+                         "how": extra["how"]},
             "clocks": clk.summary,
         }
+        if kernels:
+            line["kernels_us_per_step"] = kernels
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = wl.cpu_baseline(threads=os.cpu_count() or 1)
         print(json.dumps(line), flush=True)
@@ -262,41 +434,28 @@ def main():
 
 
 def run_reference(args, world, rank):
-    """The reference's CPU implementation of the path (the oracle port; the
-    Rust reference has no toolchain here), all host threads, rank 0 only."""
+    """The reference's CPU implementation of the path: the oracle port (the
+    Rust reference has no toolchain here), all host threads, rank 0 only; each
+    step is a bounded sample of the workload (WORKLOADS[...].reference_step)."""
     if rank != 0:
         return
-    import numpy as np
-    import oracle
+    wl = WORKLOADS[args.workload]
     threads = os.cpu_count() or 1
-    t, h = 1370, 6
-    rng = np.random.default_rng(1234)
-    qkv = oracle.round_f16(rng.standard_normal((t, 3 * h * 64), dtype=np.float32))
-    # bound each step to about 1 s of CPU work
-    rows = 32
-    t0 = time.perf_counter()
-    oracle.attention(qkv, t, h, 64, rows=(0, rows), threads=threads)
-    per_row = (time.perf_counter() - t0) / rows
-    rows = int(max(16, min(t, 1.0 / max(per_row, 1e-9))))
-    for _ in range(1):
-        oracle.attention(qkv, t, h, 64, rows=(0, rows), threads=threads)
+    step, units_per_step, sample = wl.reference_step(threads)
+    step()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        oracle.attention(qkv, t, h, 64, rows=(0, rows), threads=threads)
+        step()
     dt = time.perf_counter() - t0
-    flops = 4.0 * rows * t * h * 64 * args.steps
-    value = flops / dt / 1e12
-    line = {"metric": METRIC, "impl": "reference", "value": value, "unit": "TFLOP/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+    value = units_per_step * args.steps / dt
+    line = {"metric": METRIC, "impl": "reference", "value": value, "unit": wl.unit,
+            "n_gpus": world, "steps": args.steps, "warmup": 1,
             "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f64 accumulate, f32 storage",
-            "data": "synthetic N(0,1), seeded",
-            "config": {"workload": "vit_s_attention_op (config 1)", "tokens": t, "heads": h,
-                       "head_dim": 64},
-            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads,
-                             "kind": "port",
-                             "sample": "%d of %d query rows x %d heads per step" % (rows, t, h)},
-            "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+            "data": "synthetic, seeded", "config": {"workload": wl.workload_name},
+            "cpu_baseline": {"value": value, "unit": wl.unit, "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": wl.unit, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 

@@ -212,6 +212,131 @@ typedef struct bl_patchify_args {
 
 int bl_patchify(const bl_patchify_args* args, void* stream);
 
+/* ------------------------------------------------------------------ splitting */
+
+/*
+ * Program::split's rule (crates/beatlm-core/src/kernel.rs:2006-2029, rule 6 at
+ * 133-149): a split dimension of `extent` units in blocks of `grain` units is
+ * cut into `count` parts, clamped to 1..=ceil(extent / grain); part i covers
+ * blocks [B*i/count, B*(i+1)/count), so no part is empty and none differs
+ * from another by more than one block. Writes count+1 unit edges (edges[0] =
+ * 0, edges[count] = extent) and returns the clamped count.
+ */
+uint32_t bl_split_edges(uint32_t extent, uint32_t grain, uint32_t count, uint32_t* edges);
+
+/* KernelSpec::parts_within (kernel.rs:2048-2056): ceil(duration / bound)
+ * clamped to [1, max_parts]; 0 when bound is 0 (the reference's ZeroBound). */
+uint32_t bl_parts_within(uint64_t duration_us, uint64_t bound_us, uint32_t max_parts);
+
+/* ------------------------------------------------------------------ kernels */
+
+enum { BL_OP_ATTENTION = 1, BL_OP_GEMM = 2, BL_OP_LAYERNORM = 3, BL_OP_PATCHIFY = 4 };
+
+/* One kernel of a program: an op and its arguments (the matching bl_*_args,
+ * read during bl_kernels_create only), a label, and the number of row parts
+ * it runs as (0 or 1 = whole). Split dimensions and grains: attention query
+ * rows in 128-row tiles (every frame of the batch), GEMM output rows in
+ * 128-row tiles, LayerNorm rows one by one; patchify is never split. */
+typedef struct bl_kernel_spec {
+    int32_t op;
+    const void* args;
+    const char* label;
+    uint32_t parts;
+} bl_kernel_spec;
+
+typedef struct bl_kernels bl_kernels;
+
+/*
+ * Builds every launch of a program once: validates each spec, splits it into
+ * its parts, encodes the TMA tensor maps and packs the kernel parameters
+ * (Kernels::new, crates/beatlm/src/codegen/kernels.rs:63-184). Afterwards
+ * encoding does no host work beyond the launch. Kernel i of the result is a
+ * part; bl_kernels_len counts parts.
+ */
+int bl_kernels_create(const bl_kernel_spec* specs, size_t n, bl_kernels** out);
+void bl_kernels_destroy(bl_kernels* k);
+size_t bl_kernels_len(const bl_kernels* k);
+/* The spec's label with " [i/n]" appended for a part; NULL out of range. */
+const char* bl_kernels_label(const bl_kernels* k, size_t kernel);
+
+typedef struct bl_timer bl_timer;
+
+/*
+ * Enqueues kernel `kernel` on `stream` (Kernels::encode, kernels.rs:217-233).
+ * When `timer` is non-NULL and `frame` >= 0 (a handle from
+ * bl_timer_begin_frame), the launch is bracketed by the frame's next pair of
+ * cudaEvents, the compute-pass timestamp writes of the reference
+ * (FrameTimestamps::compute_pass, gpu/timer.rs:507).
+ */
+int bl_kernels_encode(const bl_kernels* k, size_t kernel, void* stream, bl_timer* timer,
+                      int32_t frame);
+/* Kernels [begin, end) in order, each timed as bl_kernels_encode does. */
+int bl_kernels_encode_range(const bl_kernels* k, size_t begin, size_t end, void* stream,
+                            bl_timer* timer, int32_t frame);
+
+/* The whole program captured once into a CUDA graph (relaxed capture on
+ * `stream`), replayed with one launch: the launch-bound ViT-S encoder's way
+ * of paying the per-kernel launch cost once per frame instead of per kernel. */
+typedef struct bl_graph bl_graph;
+int bl_kernels_capture(const bl_kernels* k, void* stream, bl_graph** out);
+int bl_graph_launch(const bl_graph* g, void* stream);
+void bl_graph_destroy(bl_graph* g);
+
+/* ------------------------------------------------------------------ slice timer */
+
+/*
+ * Per-kernel GPU timing from cudaEvents, with the semantics of the
+ * reference's SliceTimer (crates/beatlm/src/gpu/timer.rs:185-470): a ring of
+ * BL_TIMER_RING_DEPTH frames; a frame whose slot is still in flight goes
+ * untimed and is counted as skipped; only frames handed back as submitted are
+ * read, in submission order; nothing ever blocks (cudaEventQuery).
+ */
+enum { BL_TIMER_RING_DEPTH = 3 };
+
+int bl_timer_create(uint32_t max_slices, bl_timer** out);
+void bl_timer_destroy(bl_timer* t);
+uint32_t bl_timer_max_slices(const bl_timer* t);
+
+/* SliceTimer::begin_frame (timer.rs:272): claims a ring slot for `frame` and
+ * sets *handle to it, or to -1 when the slot is in flight (frame skipped). */
+int bl_timer_begin_frame(bl_timer* t, uint64_t frame, int32_t* handle);
+/* SliceTimer::submitted (timer.rs:307): the frame's launches are enqueued;
+ * it becomes collectable. A handle of -1 is accepted and ignored. */
+int bl_timer_submitted(bl_timer* t, int32_t handle);
+/* SliceTimer::submitted_held (timer.rs:332): submitted, but collected only
+ * once bl_timer_settle accepts it; settle(accept = 0) rejects it. */
+int bl_timer_submitted_held(bl_timer* t, int32_t handle);
+int bl_timer_settle(bl_timer* t, int32_t handle, int accept);
+/* A begun frame dropped before submission (a ResolvedFrame dropped with its
+ * encoder): its slot is freed unread. */
+int bl_timer_drop(bl_timer* t, int32_t handle);
+/* SliceTimer::invalidate_submitted (timer.rs:445): marks every submitted,
+ * uncollected frame as failed; returns how many. */
+size_t bl_timer_invalidate_submitted(bl_timer* t);
+/* SliceTimer::in_flight (timer.rs:452). */
+size_t bl_timer_in_flight(const bl_timer* t);
+
+typedef struct bl_slice_time {
+    uint64_t frame;    /* the frame index given to begin_frame */
+    uint32_t slice;    /* order of the pass within the frame */
+    uint32_t kernel;   /* the kernel index that was encoded */
+    double begin_us;   /* pass begin, relative to the frame's first pass */
+    double micros;     /* pass duration */
+} bl_slice_time;
+
+/* SliceTimer::collect_ready (timer.rs:371): writes the passes of every frame
+ * whose events have completed, oldest submitted first, whole frames only, up
+ * to `cap` entries; *n = entries written, *frames = frames completed. */
+int bl_timer_collect_ready(bl_timer* t, bl_slice_time* out, size_t cap, size_t* n,
+                           size_t* frames);
+
+typedef struct bl_timer_stats {
+    uint64_t frames_skipped;   /* TimerStats (timer.rs:135) */
+    uint64_t frames_collected;
+    uint64_t frames_failed;
+} bl_timer_stats;
+int bl_timer_get_stats(const bl_timer* t, bl_timer_stats* out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,150 @@
+"""Programs of prebuilt launches on the GPU: split parts equal the whole
+kernel (Program::split, kernel.rs:2384-2408, rule 6), a captured CUDA graph
+equals direct encoding, and the cudaEvent slice timer keeps the reference
+SliceTimer's rules (crates/beatlm/src/gpu/timer.rs:185-470)."""
+import numpy as np
+import pytest
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+T, D, MLP = 1370, 384, 1536
+
+
+def _block(dtype="bf16", frames=1):
+    import torch
+    from beatlm_b200.model import Buffers, DeviceBlock, ViTConfig, block_weights_by_role
+    cfg = ViTConfig.small()
+    w = block_weights_by_role(100, D, MLP, uniform=oracle.uniform)
+    blk = DeviceBlock(w, D, MLP, dtype)
+    buf = Buffers(cfg, frames, dtype, features=False)
+    x0 = torch.from_numpy(oracle.uniform(20, frames * T * D, -2, 2).reshape(frames * T, D)).cuda()
+    return cfg, blk, buf, x0
+
+
+@pytest.mark.parametrize("parts", [3, 11, 200])
+def test_split_block_equals_the_whole_block(parts):
+    import torch
+    import beatlm_b200 as bl
+    from beatlm_b200.model import block_specs
+    from beatlm_b200.runtime import Kernels
+    cfg, blk, buf, x0 = _block(frames=2)
+    whole = Kernels(block_specs(blk, cfg, buf))
+    split = Kernels(block_specs(blk, cfg, buf, parts=parts))
+    assert len(whole) == 5
+    assert len(split) > 5
+    assert split.label(0).startswith("block0.qkv [1/")
+    buf.x.copy_(x0)
+    whole.encode_all()
+    torch.cuda.synchronize()
+    want = buf.x.clone()
+    buf.x.copy_(x0)
+    split.encode_all()
+    torch.cuda.synchronize()
+    assert torch.equal(buf.x, want)
+    assert bl.status(reset=True).code == 0
+
+
+def test_graph_replay_equals_direct_encoding():
+    import torch
+    from beatlm_b200.model import block_specs
+    from beatlm_b200.runtime import Kernels
+    cfg, blk, buf, x0 = _block()
+    k = Kernels(block_specs(blk, cfg, buf))
+    buf.x.copy_(x0)
+    k.encode_all()
+    torch.cuda.synchronize()
+    want = buf.x.clone()
+    s = torch.cuda.Stream()
+    g = k.capture(s)
+    buf.x.copy_(x0)
+    torch.cuda.synchronize()
+    g.launch(s)
+    s.synchronize()
+    assert torch.equal(buf.x, want)
+
+
+def test_slice_timer_rules():
+    import torch
+    from beatlm_b200.model import block_specs
+    from beatlm_b200.runtime import Kernels, SliceTimer
+    cfg, blk, buf, x0 = _block()
+    k = Kernels(block_specs(blk, cfg, buf))
+    t = SliceTimer(max_slices=8)
+    s = torch.cuda.current_stream()
+    handles = []
+    for frame in range(3):
+        h = t.begin_frame(frame)
+        assert h >= 0
+        k.encode_all(s, timer=t, frame=h)
+        t.submitted(h)
+        handles.append(h)
+    # every slot is in flight: the fourth frame goes untimed, counted
+    assert t.begin_frame(3) == -1
+    k.encode_all(s, timer=None)
+    t.submitted(-1)
+    assert t.stats()["frames_skipped"] == 1
+    torch.cuda.synchronize()
+    got = t.collect_ready()
+    assert [f.frame for f in got] == [0, 1, 2]           # submission order
+    for f in got:
+        assert [kernel for kernel, _ in f.compute] == [0, 1, 2, 3, 4]
+        assert all(us > 0 for _, us in f.compute)
+        assert f.begin_us[0] == 0.0 and f.begin_us == sorted(f.begin_us)
+    assert t.stats()["frames_collected"] == 3
+    assert t.in_flight() == 0
+
+    # a dropped frame is never read; an invalidated one is counted failed
+    h = t.begin_frame(10)
+    k.encode(0, s, timer=t, frame=h)
+    t.drop(h)
+    h = t.begin_frame(11)
+    k.encode(1, s, timer=t, frame=h)
+    t.submitted(h)
+    assert t.invalidate_submitted() == 1
+    torch.cuda.synchronize()
+    assert t.collect_ready() == []
+    assert t.stats()["frames_failed"] == 1
+
+    # a held frame holds back later frames until it is settled
+    h1 = t.begin_frame(20)
+    k.encode(2, s, timer=t, frame=h1)
+    t.submitted_held(h1)
+    h2 = t.begin_frame(21)
+    k.encode(3, s, timer=t, frame=h2)
+    t.submitted(h2)
+    torch.cuda.synchronize()
+    assert t.collect_ready() == []
+    t.settle(h1, accept=False)
+    got = t.collect_ready()
+    assert [f.frame for f in got] == [21]
+    assert t.stats()["frames_failed"] == 2
+
+    # more timed passes than the timer holds is an error, not a guess
+    small = SliceTimer(max_slices=2)
+    h = small.begin_frame(0)
+    import beatlm_b200 as bl
+    with pytest.raises(bl.BackendError, match="timed passes"):
+        k.encode_all(s, timer=small, frame=h)
+
+
+def test_encoder_program_graph_equals_direct():
+    import torch
+    from beatlm_b200.model import Encoder, ViTConfig
+    from test_block_gpu import _encoder_weights, imagenet_image
+    cfg = ViTConfig.small(layers=2, out_indices=(2,))
+    enc = Encoder(cfg, _encoder_weights(cfg, 2), "bf16")
+    image = torch.from_numpy(imagenet_image(np.random.default_rng(3), cfg.side)).cuda()
+    feats = enc.forward(image, frames=1)
+    torch.cuda.synchronize()
+    want = feats[0].clone()
+    prog = enc.program(1)
+    assert len(prog) == enc.launches_per_frame_batch() - 1  # patchify is one launch record
+    s = torch.cuda.Stream()
+    g = prog.capture(s)
+    enc.buffers(1).features[0].zero_()
+    torch.cuda.synchronize()
+    g.launch(s)
+    s.synchronize()
+    assert torch.equal(enc.buffers(1).features[0], want)
