@@ -38,6 +38,8 @@ class AttentionArgs(ctypes.Structure):
         ("v_dtype", ctypes.c_int32), ("out_dtype", ctypes.c_int32), ("qkv", ctypes.c_void_p),
         ("qkv_row_stride", ctypes.c_uint64), ("out", ctypes.c_void_p),
         ("out_row_stride", ctypes.c_uint64), ("out_head_base", ctypes.c_uint32),
+        ("kv_splits", ctypes.c_uint32), ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_uint64), ("trace", ctypes.c_void_p),
     ]
 
 
@@ -52,6 +54,7 @@ SIGNATURES = {
     "bl_version": (ctypes.c_char_p, []),
     "bl_status": (ctypes.c_int, [ctypes.POINTER(Status), ctypes.c_int]),
     "bl_attention": (ctypes.c_int, [ctypes.POINTER(AttentionArgs), ctypes.c_void_p]),
+    "bl_attention_workspace_bytes": (ctypes.c_uint64, [ctypes.POINTER(AttentionArgs)]),
 }
 
 

@@ -4,18 +4,28 @@
 // crates/beatlm-bench/src/reference.rs:437-494) as one kernel with an online
 // softmax, so the [tokens][heads][tokens] scores never reach memory.
 //
-// One CTA computes a 128-row query tile of one head of one sequence:
-//   warp 0      TMA producer: Q once, then K/V tiles of 128 keys into a
-//               4-stage ring (128-byte swizzle, zero fill past the last key).
-//   warp 1      MMA issuer (one thread): S_j = Q K_j^T into TMEM (M=128,
-//               N=128, K=64, f32), then O += P_{j-1} V_{j-1} with P read
-//               from TMEM (M=128, N=64, K=128, f16) so the next score tile
-//               is computed while the softmax works on this one.
-//   warps 2..5  softmax, one thread per query row (TMEM lane): reads its S
-//               row, updates the running max (rescaling O in TMEM only when
-//               the max grew by more than 2^8), writes P as f16 over the
-//               consumed S columns, and finally normalises O and stores it.
-// TMEM columns: S0 [0,128), S1 [128,256), O [256,320); P_j aliases S_{j%2}.
+// One CTA computes two 128-row query tiles of one head of one sequence over a
+// range of key tiles (all of them, or one split of them). 12 warps in three
+// warpgroups; the control warpgroup gives registers to the softmax ones
+// (setmaxnreg: 128 x 56 + 256 x 224 = 384 x 168, the launch allocation):
+//   warp 0      TMA producer: Q0 and Q1 once, then K/V tiles of 128 keys into
+//               a 4-stage ring (128-byte swizzle, zero fill past the last key).
+//   warp 1      MMA issuer (one thread): S_t = Q_t K^T into TMEM (M=128,
+//               N=128, K=64, f32) and O_t += P_t V with P read from TMEM
+//               (M=128, N=64, K=128, f16), issued so that the tensor core
+//               works on one tile while the other tile's softmax runs:
+//                 S0_0 S1_0 | PV0_0 S0_1 PV1_0 S1_1 | PV0_1 S0_2 PV1_1 ...
+//   warps 4..7  softmax of tile 0, warps 8..11 softmax of tile 1: one thread
+//               per query row (TMEM lane) holding its 128 scores in
+//               registers; the running max is updated lazily (O is rescaled
+//               in TMEM only when the max grew by more than 2^8); P is
+//               written as f16 over the consumed S columns. Of each 8 pairs
+//               of exponentials, 3 are evaluated by a polynomial on the FMA
+//               pipe and 5 by the MUFU ex2 unit, so neither pipe idles.
+// With more than one key split, each CTA writes its unnormalised O and its
+// (max, sum) per row to a workspace; the last CTA of a tile group (an atomic
+// counter, no waiting) combines them. TMEM: S0 [0,128) S1 [128,256)
+// O0 [256,320) O1 [320,384); P_t aliases S_t.
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 
@@ -24,46 +34,71 @@
 namespace bl {
 namespace attn {
 
-constexpr int BM = 128;      // query rows per CTA
-constexpr int BN = 128;      // keys per tile
-constexpr int HD = 64;       // head width
-constexpr int STAGES = 4;    // K/V ring depth
-constexpr int kThreads = 192;
-constexpr uint32_t kTileBytes = BM * HD * 2;  // 16 KiB per 128x64 16-bit tile
+constexpr int BM = 128;       // query rows per tile
+constexpr int QT = 2;         // query tiles per CTA
+constexpr int ROWS = BM * QT; // query rows per CTA
+constexpr int BN = 128;       // keys per tile
+constexpr int HD = 64;        // head width
+constexpr int STAGES = 4;     // K/V ring depth
+constexpr int kSoftmaxWarp0 = 4;
+constexpr int kThreads = 32 * (kSoftmaxWarp0 + 4 * QT);  // 384
+// Register split (setmaxnreg): the launch gives every thread kLaunchRegs.
+constexpr int kLaunchRegs = 168;
+constexpr int kControlRegs = 56;
+constexpr int kSoftmaxRegs = 224;
+static_assert(128 * kControlRegs + 32 * 4 * QT * kSoftmaxRegs <= kThreads * kLaunchRegs,
+              "register split exceeds the launch allocation");
+constexpr uint32_t kTileBytes = BM * HD * 2;  // 16 KiB per 128x64 tile
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO = 256;
-// Lazy rescaling: the running max used for exponents may trail the true
-// max by up to this (log2 units), so p <= 2^8, well inside f16.
+constexpr uint32_t kColS = 0, kColO = 256;  // S_t at kColS + 128 t, O_t at kColO + 64 t
+// Lazy rescaling: the max used for exponents may trail the true max by up to
+// this (log2 units), so p <= 2^8, well inside f16.
 constexpr float kRescaleThreshold = 8.0f;
 
 struct Params {
     int tokens;
     int head_begin;
+    int heads_rel;        // heads in this launch (gridDim.y)
     int row_begin, row_end;
     int q_col0, k_col0, v_col0;  // element column of head 0's Q/K/V in a row
     float scale_log2;            // scale * log2(e)
     int qk_fmt;                  // 0 = f16, 1 = bf16
-    int out_dtype;               // BL_F32 / BL_F16 / BL_BF16
     void* out;
     long long out_row_stride;    // elements
     long long out_batch_stride;  // elements
     int out_head_base;
+    int splits;       // key splits; gridDim.z = batch * splits
+    int kv_tiles;     // ceil(tokens / BN)
+    float* part_o;    // [unit][split][ROWS][HD]
+    float* part_ml;   // [unit][split][ROWS][2]
+    unsigned* counters;  // [unit]
+    unsigned long long* trace;  // optional per-CTA timeline
     Status* status;
 };
+
+__device__ __forceinline__ void trace_stamp(unsigned long long* trace, int slot) {
+    if (trace == nullptr) return;
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    const size_t b = blockIdx.x + gridDim.x * (blockIdx.y + static_cast<size_t>(gridDim.y) *
+                                                               blockIdx.z);
+    trace[4 * b + slot] = t;
+}
 
 struct SmemTail {
     uint64_t q_full;
     uint64_t kv_full[STAGES];
     uint64_t kv_empty[STAGES];
-    uint64_t s_full[2];
-    uint64_t p_full[2];
-    uint64_t o_done;
+    uint64_t s_full[QT];
+    uint64_t p_full[QT];
+    uint64_t o_done[QT];
     uint64_t drain;
     uint32_t tmem_base;
     int abort;
+    unsigned last;  // this CTA combines the splits
 };
 
-constexpr size_t kSmemBytes = 1024 /*align slack*/ + kTileBytes /*Q*/ +
+constexpr size_t kSmemBytes = 1024 /*align slack*/ + QT * kTileBytes /*Q*/ +
                               STAGES * 2 * kTileBytes /*K,V*/ + sizeof(SmemTail);
 
 __device__ __forceinline__ uint64_t desc_kmajor(uint32_t addr) {
@@ -76,40 +111,88 @@ __device__ __forceinline__ uint64_t desc_v(uint32_t addr) {
     return sdesc_sw128(addr, kTileBytes, 1024);
 }
 
-template <int kOutDtype>
-__device__ __forceinline__ void store_row(void* base, const float* o, float inv_l);
+// Packed two-lane f32 arithmetic (Blackwell fma/add .f32x2).
+__device__ __forceinline__ unsigned long long f2pack(float a, float b) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void f2unpack(unsigned long long r, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ unsigned long long ffma2(unsigned long long a, unsigned long long b,
+                                                    unsigned long long c) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ unsigned long long fadd2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
 
-template <>
-__device__ __forceinline__ void store_row<BL_F32>(void* base, const float* o, float inv_l) {
-    float4* dst = reinterpret_cast<float4*>(base);
-#pragma unroll
-    for (int c = 0; c < HD / 4; ++c)
-        dst[c] = make_float4(o[4 * c] * inv_l, o[4 * c + 1] * inv_l, o[4 * c + 2] * inv_l,
-                             o[4 * c + 3] * inv_l);
+// 2^x for a pair, x <= 2^22, on the FMA pipe. Range reduction: x = j + f
+// with j = round(x) (adding 1.5 * 2^23 leaves j in the low mantissa bits) and
+// f in [-0.5, 0.5]; 2^f by a degree-3 polynomial fitted here by the Remez
+// exchange algorithm for minimax relative error (7.5e-5 on [-0.5, 0.5], far
+// below the f16 rounding of P); 2^j by adding j to the exponent field. x is
+// clamped at -120 so the exponent never underflows (2^-120 is 0 in f16).
+__device__ __forceinline__ void exp2_poly2(unsigned long long x2, float& r0, float& r1) {
+    constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+    constexpr float c0 = 0.99992806f, c1 = 0.69326097f, c2 = 0.24261113f, c3 = 0.05517167f;
+    float x0, x1;
+    f2unpack(x2, x0, x1);
+    x0 = fmaxf(x0, -120.0f);
+    x1 = fmaxf(x1, -120.0f);
+    const unsigned long long xc = f2pack(x0, x1);
+    const unsigned long long t = fadd2(xc, f2pack(kShift, kShift));  // j in the low bits
+    const unsigned long long j = fadd2(t, f2pack(-kShift, -kShift));  // round(x)
+    const unsigned long long f = ffma2(j, f2pack(-1.0f, -1.0f), xc);  // x - j
+    unsigned long long p = ffma2(f2pack(c3, c3), f, f2pack(c2, c2));
+    p = ffma2(p, f, f2pack(c1, c1));
+    p = ffma2(p, f, f2pack(c0, c0));
+    float t0, t1, p0, p1;
+    f2unpack(t, t0, t1);
+    f2unpack(p, p0, p1);
+    r0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+    r1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
 }
-template <>
-__device__ __forceinline__ void store_row<BL_F16>(void* base, const float* o, float inv_l) {
+
+__device__ __forceinline__ void store_row(void* base, int dt, const float* o, float inv_l) {
+    if (dt == BL_F32) {
+        float4* dst = reinterpret_cast<float4*>(base);
+#pragma unroll
+        for (int c = 0; c < HD / 4; ++c)
+            dst[c] = make_float4(o[4 * c] * inv_l, o[4 * c + 1] * inv_l, o[4 * c + 2] * inv_l,
+                                 o[4 * c + 3] * inv_l);
+        return;
+    }
     uint4* dst = reinterpret_cast<uint4*>(base);
 #pragma unroll
     for (int c = 0; c < HD / 8; ++c) {
         const float* v = o + 8 * c;
-        dst[c] = make_uint4(pack_f16x2(v[0] * inv_l, v[1] * inv_l),
-                            pack_f16x2(v[2] * inv_l, v[3] * inv_l),
-                            pack_f16x2(v[4] * inv_l, v[5] * inv_l),
-                            pack_f16x2(v[6] * inv_l, v[7] * inv_l));
+        if (dt == BL_F16)
+            dst[c] = make_uint4(pack_f16x2(v[0] * inv_l, v[1] * inv_l),
+                                pack_f16x2(v[2] * inv_l, v[3] * inv_l),
+                                pack_f16x2(v[4] * inv_l, v[5] * inv_l),
+                                pack_f16x2(v[6] * inv_l, v[7] * inv_l));
+        else
+            dst[c] = make_uint4(pack_bf16x2(v[0] * inv_l, v[1] * inv_l),
+                                pack_bf16x2(v[2] * inv_l, v[3] * inv_l),
+                                pack_bf16x2(v[4] * inv_l, v[5] * inv_l),
+                                pack_bf16x2(v[6] * inv_l, v[7] * inv_l));
     }
 }
-template <>
-__device__ __forceinline__ void store_row<BL_BF16>(void* base, const float* o, float inv_l) {
-    uint4* dst = reinterpret_cast<uint4*>(base);
-#pragma unroll
-    for (int c = 0; c < HD / 8; ++c) {
-        const float* v = o + 8 * c;
-        dst[c] = make_uint4(pack_bf16x2(v[0] * inv_l, v[1] * inv_l),
-                            pack_bf16x2(v[2] * inv_l, v[3] * inv_l),
-                            pack_bf16x2(v[4] * inv_l, v[5] * inv_l),
-                            pack_bf16x2(v[6] * inv_l, v[7] * inv_l));
-    }
+
+// The 256 softmax threads (warps 4..11) only.
+__device__ __forceinline__ void softmax_bar() {
+    asm volatile("bar.sync 1, %0;" ::"n"(32 * 4 * QT) : "memory");
 }
 
 template <int kOutDtype>
@@ -120,38 +203,44 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint8_t* sQ = smem;
-    uint8_t* sK = smem + kTileBytes;                       // stage s at + s*kTileBytes
-    uint8_t* sV = smem + kTileBytes + STAGES * kTileBytes;  // stage s at + s*kTileBytes
-    SmemTail* tail = reinterpret_cast<SmemTail*>(smem + kTileBytes + 2 * STAGES * kTileBytes);
+    uint8_t* sQ = smem;                                          // tile t at + t*kTileBytes
+    uint8_t* sK = smem + QT * kTileBytes;                        // stage s at + s*kTileBytes
+    uint8_t* sV = smem + QT * kTileBytes + STAGES * kTileBytes;  // stage s at + s*kTileBytes
+    SmemTail* tail =
+        reinterpret_cast<SmemTail*>(smem + QT * kTileBytes + 2 * STAGES * kTileBytes);
     volatile int* abort = &tail->abort;
 
     const int warp = warp_id();
     const int lane = lane_id();
     const int head = p.head_begin + blockIdx.y;
-    const int batch = blockIdx.z;
-    const int q0 = p.row_begin + blockIdx.x * BM;
-    const int n_kv = (p.tokens + BN - 1) / BN;
-
-    const uint32_t b_q_full = smem_u32(&tail->q_full);
-    const uint32_t b_o_done = smem_u32(&tail->o_done);
-    const uint32_t b_drain = smem_u32(&tail->drain);
+    const int batch = blockIdx.z / p.splits;
+    const int split = blockIdx.z % p.splits;
+    const int q0 = p.row_begin + blockIdx.x * ROWS;
+    // this CTA's key tiles [t0, t1)
+    const int t0 = p.kv_tiles * split / p.splits;
+    const int t1 = p.kv_tiles * (split + 1) / p.splits;
+    const int n = t1 - t0;
 
     if (threadIdx.x == 0) {
-        mbar_init(b_q_full, 1);
+        trace_stamp(p.trace, 0);
+        mbar_init(smem_u32(&tail->q_full), 1);
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(smem_u32(&tail->kv_full[s]), 1);
             mbar_init(smem_u32(&tail->kv_empty[s]), 1);
         }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(smem_u32(&tail->s_full[b]), 1);
-            mbar_init(smem_u32(&tail->p_full[b]), BM);
+        for (int t = 0; t < QT; ++t) {
+            mbar_init(smem_u32(&tail->s_full[t]), 1);
+            mbar_init(smem_u32(&tail->p_full[t]), BM);
+            mbar_init(smem_u32(&tail->o_done[t]), 1);
         }
-        mbar_init(b_o_done, 1);
-        mbar_init(b_drain, 1);
+        mbar_init(smem_u32(&tail->drain), 1);
         tail->abort = 0;
+        tail->last = 0;
         fence_barrier_init();
         fence_proxy_async_smem();
+        tma_prefetch_desc(&tm_q);
+        tma_prefetch_desc(&tm_k);
+        tma_prefetch_desc(&tm_v);
     }
     if (warp == 1) {
         tmem_alloc(smem_u32(&tail->tmem_base), kTmemCols);
@@ -161,131 +250,157 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tail->tmem_base;
+    pdl_trigger();
+    pdl_wait();
+    if (threadIdx.x == 0) trace_stamp(p.trace, 1);
 
-    if (warp == 0) {
-        // ------------------------------------------------------ producer
-        if (lane == 0) {
-            tma_prefetch_desc(&tm_q);
-            tma_prefetch_desc(&tm_k);
-            tma_prefetch_desc(&tm_v);
-            mbar_arrive_expect_tx(b_q_full, kTileBytes);
-            tma_load_3d(smem_u32(sQ), &tm_q, p.q_col0 + head * HD, q0, batch, b_q_full);
+    if (warp < kSoftmaxWarp0) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kControlRegs));
+        if (warp == 0 && lane == 0) {
+            // -------------------------------------------------- producer
+            const uint32_t b_q = smem_u32(&tail->q_full);
+            mbar_arrive_expect_tx(b_q, QT * kTileBytes);
+            for (int t = 0; t < QT; ++t)
+                tma_load_3d(smem_u32(sQ + t * kTileBytes), &tm_q, p.q_col0 + head * HD,
+                            q0 + t * BM, batch, b_q);
             int issued[STAGES];
 #pragma unroll
             for (int s = 0; s < STAGES; ++s) issued[s] = 0;
-            bool ok = true;
-            for (int j = 0; j < n_kv && ok; ++j) {
-                const int s = j % STAGES;
-                const int r = j / STAGES;
-                if (r > 0)
-                    ok = mbar_wait(smem_u32(&tail->kv_empty[s]), (r - 1) & 1, abort, p.status,
-                                   ST_TIMEOUT_TMA, j);
-                if (!ok) break;
+            for (int i = 0; i < n; ++i) {
+                const int s = i % STAGES;
+                const int r = i / STAGES;
+                if (r > 0 && !mbar_wait(smem_u32(&tail->kv_empty[s]), (r - 1) & 1, abort,
+                                        p.status, ST_TIMEOUT_TMA, i))
+                    break;
                 const uint32_t bar = smem_u32(&tail->kv_full[s]);
                 mbar_arrive_expect_tx(bar, 2 * kTileBytes);
-                tma_load_3d(smem_u32(sK + s * kTileBytes), &tm_k, p.k_col0 + head * HD, j * BN,
-                            batch, bar);
-                tma_load_3d(smem_u32(sV + s * kTileBytes), &tm_v, p.v_col0 + head * HD, j * BN,
-                            batch, bar);
+                tma_load_3d(smem_u32(sK + s * kTileBytes), &tm_k, p.k_col0 + head * HD,
+                            (t0 + i) * BN, batch, bar);
+                tma_load_3d(smem_u32(sV + s * kTileBytes), &tm_v, p.v_col0 + head * HD,
+                            (t0 + i) * BN, batch, bar);
                 issued[s] += 1;
             }
             if (*abort) {
                 // Unwinding: let every copy this thread started land before
                 // the CTA's shared memory is released.
-                mbar_wait(b_q_full, 0, nullptr, p.status, ST_TIMEOUT_DRAIN, 0);
+                mbar_wait(b_q, 0, nullptr, p.status, ST_TIMEOUT_DRAIN, 0);
                 for (int s = 0; s < STAGES; ++s)
                     if (issued[s] > 0)
                         mbar_wait(smem_u32(&tail->kv_full[s]), (issued[s] - 1) & 1, nullptr,
                                   p.status, ST_TIMEOUT_DRAIN, s);
             }
-        }
-    } else if (warp == 1) {
-        // ------------------------------------------------------ MMA issuer
-        if (lane == 0) {
+        } else if (warp == 1 && lane == 0) {
+            // -------------------------------------------------- MMA issuer
             const uint32_t idesc_s = idesc_f16(BM, BN, p.qk_fmt, p.qk_fmt, 0, 0);
             const uint32_t idesc_o = idesc_f16(BM, HD, 0, 0, 0, 1);
-            const uint32_t q_addr = smem_u32(sQ);
-            bool ok = mbar_wait(b_q_full, 0, abort, p.status, ST_TIMEOUT_MMA, 0xFFFF);
+            bool ok = mbar_wait(smem_u32(&tail->q_full), 0, abort, p.status, ST_TIMEOUT_MMA,
+                                0xFFFF);
             tc_fence_after();
-            auto issue_pv = [&](int i) -> bool {
-                const int bb = i & 1;
-                if (!mbar_wait(smem_u32(&tail->p_full[bb]), (i >> 1) & 1, abort, p.status,
-                               ST_TIMEOUT_MMA, 0x10000 | i))
+            auto wait_kv = [&](int i) -> bool {
+                if (!mbar_wait(smem_u32(&tail->kv_full[i % STAGES]), (i / STAGES) & 1, abort,
+                               p.status, ST_TIMEOUT_MMA, i))
                     return false;
                 tc_fence_after();
-                const int s = i % STAGES;
-                const uint32_t v_addr = smem_u32(sV + s * kTileBytes);
-                const uint32_t p_col = tmem + (bb ? kColS1 : kColS0);
-#pragma unroll
-                for (int k = 0; k < BN / 16; ++k)
-                    mma_ts(tmem + kColO, p_col + k * 8, desc_v(v_addr + k * 16 * 128), idesc_o,
-                           (i > 0 || k > 0) ? 1u : 0u);
-                // Only stages the producer will refill are released, so no
-                // arrival lands after the CTA has finished.
-                if (i + STAGES < n_kv) mma_commit(smem_u32(&tail->kv_empty[s]));
-                mma_commit(b_o_done);
                 return true;
             };
-            for (int j = 0; j < n_kv && ok; ++j) {
-                const int s = j % STAGES;
-                ok = mbar_wait(smem_u32(&tail->kv_full[s]), (j / STAGES) & 1, abort, p.status,
-                               ST_TIMEOUT_MMA, j);
-                if (!ok) break;
-                tc_fence_after();
-                const int b = j & 1;
-                const uint32_t k_addr = smem_u32(sK + s * kTileBytes);
-                const uint32_t d = tmem + (b ? kColS1 : kColS0);
+            auto issue_s = [&](int t, int i) {
+                const uint32_t q_addr = smem_u32(sQ + t * kTileBytes);
+                const uint32_t k_addr = smem_u32(sK + (i % STAGES) * kTileBytes);
 #pragma unroll
                 for (int k = 0; k < HD / 16; ++k)
-                    mma_ss(d, desc_kmajor(q_addr + k * 32), desc_kmajor(k_addr + k * 32), idesc_s,
-                           k > 0 ? 1u : 0u);
-                mma_commit(smem_u32(&tail->s_full[b]));
-                if (j > 0) ok = issue_pv(j - 1);
+                    mma_ss(tmem + kColS + 128 * t, desc_kmajor(q_addr + k * 32),
+                           desc_kmajor(k_addr + k * 32), idesc_s, k > 0 ? 1u : 0u);
+                mma_commit(smem_u32(&tail->s_full[t]));
+            };
+            auto issue_pv = [&](int t, int i) -> bool {
+                if (!mbar_wait(smem_u32(&tail->p_full[t]), i & 1, abort, p.status,
+                               ST_TIMEOUT_MMA, 0x10000 | (t << 12) | i))
+                    return false;
+                tc_fence_after();
+                const uint32_t v_addr = smem_u32(sV + (i % STAGES) * kTileBytes);
+                const uint32_t p_col = tmem + kColS + 128 * t;
+#pragma unroll
+                for (int k = 0; k < BN / 16; ++k)
+                    mma_ts(tmem + kColO + 64 * t, p_col + k * 8, desc_v(v_addr + k * 16 * 128),
+                           idesc_o, (i > 0 || k > 0) ? 1u : 0u);
+                // The stage is released after its last reader (tile 1's PV),
+                // and only if the producer will refill it, so no arrival
+                // lands after the CTA has finished.
+                if (t == QT - 1 && i + STAGES < n)
+                    mma_commit(smem_u32(&tail->kv_empty[i % STAGES]));
+                mma_commit(smem_u32(&tail->o_done[t]));
+                return true;
+            };
+            if (ok) ok = wait_kv(0);
+            if (ok) {
+                for (int t = 0; t < QT; ++t) issue_s(t, 0);
             }
-            if (ok) ok = issue_pv(n_kv - 1);
+            for (int i = 0; i < n && ok; ++i) {
+                // tile 0: PV_i, then the next S (it overwrites P0_i: after PV)
+                ok = issue_pv(0, i);
+                if (ok && i + 1 < n) {
+                    ok = wait_kv(i + 1);
+                    if (ok) issue_s(0, i + 1);
+                }
+                if (ok) ok = issue_pv(1, i);
+                if (ok && i + 1 < n) issue_s(1, i + 1);
+            }
             if (!ok) {
                 // Unwinding: wait for the tensor core to finish what was
                 // issued before TMEM is released.
-                mma_commit(b_drain);
-                mbar_wait(b_drain, 0, nullptr, p.status, ST_TIMEOUT_DRAIN, 0xD);
+                mma_commit(smem_u32(&tail->drain));
+                mbar_wait(smem_u32(&tail->drain), 0, nullptr, p.status, ST_TIMEOUT_DRAIN, 0xD);
             }
         }
     } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
         // ------------------------------------------------------ softmax
-        const int sub = warp & 3;                 // TMEM sub-partition of this warp
-        const int row = sub * 32 + lane;          // query row within the tile
+        constexpr unsigned kFull = 0xFFFFFFFFu;
+        const int t = (warp - kSoftmaxWarp0) / 4;  // query tile of this warpgroup
+        const int sub = warp & 3;                  // TMEM sub-partition of this warp
+        const int row = sub * 32 + lane;           // query row within the tile
         const uint32_t t_lane = tmem + (static_cast<uint32_t>(sub * 32) << 16);
+        const uint32_t s_col = t_lane + kColS + 128 * t;
+        const uint32_t o_col = t_lane + kColO + 64 * t;
+        const uint32_t b_s = smem_u32(&tail->s_full[t]);
+        const uint32_t b_p = smem_u32(&tail->p_full[t]);
+        const uint32_t b_o = smem_u32(&tail->o_done[t]);
         const float c = p.scale_log2;
+        const unsigned long long c2 = f2pack(c, c);
         float m_used = -INFINITY;
         float l = 0.0f;
         bool ok = true;
-        constexpr unsigned kFull = 0xFFFFFFFFu;
-        for (int j = 0; j < n_kv; ++j) {
-            const int b = j & 1;
-            ok = mbar_wait(smem_u32(&tail->s_full[b]), (j >> 1) & 1, abort, p.status,
-                           ST_TIMEOUT_SOFTMAX, j);
+        for (int i = 0; i < n; ++i) {
+            ok = mbar_wait(b_s, i & 1, abort, p.status, ST_TIMEOUT_SOFTMAX, (t << 12) | i);
             ok = __all_sync(kFull, ok);
             if (!ok) break;
             tc_fence_after();
-            const uint32_t s_col = t_lane + (b ? kColS1 : kColS0);
             uint32_t s[BN];
             tmem_ld32(s_col + 0, *reinterpret_cast<uint32_t(*)[32]>(s + 0));
             tmem_ld32(s_col + 32, *reinterpret_cast<uint32_t(*)[32]>(s + 32));
             tmem_ld32(s_col + 64, *reinterpret_cast<uint32_t(*)[32]>(s + 64));
             tmem_ld32(s_col + 96, *reinterpret_cast<uint32_t(*)[32]>(s + 96));
             tmem_wait_ld();
-            const int valid = min(BN, p.tokens - j * BN);
-            float mx = -INFINITY;
+            const int valid = p.tokens - (t0 + i) * BN;  // keys of this tile that exist
+            if (valid < BN) {                            // only the sequence's last tile
 #pragma unroll
-            for (int i = 0; i < BN; ++i) {
-                float v = (i < valid) ? __uint_as_float(s[i]) : -INFINITY;
-                s[i] = __float_as_uint(v);
-                mx = fmaxf(mx, v);
+                for (int k = 0; k < BN; ++k)
+                    if (k >= valid) s[k] = __float_as_uint(-INFINITY);
             }
+            // row max: four independent chains of three-input max
+            float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+            for (int k = 0; k < BN; k += 8) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    mx[q] = fmax3(mx[q], __uint_as_float(s[k + 2 * q]),
+                                  __uint_as_float(s[k + 2 * q + 1]));
+            }
+            const float m_row = fmax3(fmaxf(mx[0], mx[1]), mx[2], mx[3]);
             // Lazy rescaling, decided per row; the O read-modify-write is a
             // warp-collective TMEM access, so a warp does it when any of its
             // rows needs it (the others multiply by 1, which is exact).
-            const float m_new = fmaxf(m_used, mx * c);
+            const float m_new = fmaxf(m_used, m_row * c);
             const bool need = m_new > m_used + kRescaleThreshold;
             float alpha = 1.0f;
             if (need) {
@@ -293,60 +408,135 @@ __global__ void __launch_bounds__(kThreads, 1)
                 l *= alpha;
                 m_used = m_new;
             }
-            if (j > 0 && __any_sync(kFull, need)) {
-                ok = mbar_wait(b_o_done, (j - 1) & 1, abort, p.status, ST_TIMEOUT_SOFTMAX,
-                               0x10000 | j);
+            if (i > 0 && __any_sync(kFull, need)) {
+                ok = mbar_wait(b_o, (i - 1) & 1, abort, p.status, ST_TIMEOUT_SOFTMAX,
+                               0x10000 | (t << 12) | i);
                 ok = __all_sync(kFull, ok);
                 if (!ok) break;
                 tc_fence_after();
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     uint32_t o[32];
-                    tmem_ld32(t_lane + kColO + 32 * h, o);
+                    tmem_ld32(o_col + 32 * h, o);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                    tmem_st32(t_lane + kColO + 32 * h, o);
+                    for (int k = 0; k < 32; ++k)
+                        o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
+                    tmem_st32(o_col + 32 * h, o);
                 }
                 tmem_wait_st();
             }
-            float sum = 0.0f;
-            uint32_t pk[BN / 2];
+            // exponents: pairs k with k % 8 in {0, 3, 5} on the FMA pipe, the
+            // rest on MUFU; four partial sums; P packed to f16 in place
+            // (pair k lands in s[k], whose own score was consumed at pair k/2)
+            const unsigned long long nm2 = f2pack(-m_used, -m_used);
+            unsigned long long acc[4];
 #pragma unroll
-            for (int i = 0; i < BN / 2; ++i) {
-                const float p0 = ex2(fmaf(__uint_as_float(s[2 * i]), c, -m_used));
-                const float p1 = ex2(fmaf(__uint_as_float(s[2 * i + 1]), c, -m_used));
-                sum += p0 + p1;
-                pk[i] = pack_f16x2(p0, p1);
+            for (int q = 0; q < 4; ++q) acc[q] = f2pack(0.0f, 0.0f);
+#pragma unroll
+            for (int k = 0; k < BN / 2; ++k) {
+                const unsigned long long x2 =
+                    ffma2(f2pack(__uint_as_float(s[2 * k]), __uint_as_float(s[2 * k + 1])), c2,
+                          nm2);
+                float p0, p1;
+                if ((k & 7) == 0 || (k & 7) == 3 || (k & 7) == 5) {
+                    exp2_poly2(x2, p0, p1);
+                } else {
+                    float x0, x1;
+                    f2unpack(x2, x0, x1);
+                    p0 = ex2(x0);
+                    p1 = ex2(x1);
+                }
+                acc[k & 3] = fadd2(acc[k & 3], f2pack(p0, p1));
+                s[k] = pack_f16x2(p0, p1);
             }
-            l += sum;
-            tmem_st32(s_col + 0, *reinterpret_cast<uint32_t(*)[32]>(pk + 0));
-            tmem_st32(s_col + 32, *reinterpret_cast<uint32_t(*)[32]>(pk + 32));
+            const unsigned long long a01 = fadd2(acc[0], acc[1]);
+            const unsigned long long a23 = fadd2(acc[2], acc[3]);
+            float sa, sb;
+            f2unpack(fadd2(a01, a23), sa, sb);
+            l += sa + sb;
+            tmem_st32(s_col + 0, *reinterpret_cast<uint32_t(*)[32]>(s + 0));
+            tmem_st32(s_col + 32, *reinterpret_cast<uint32_t(*)[32]>(s + 32));
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(smem_u32(&tail->p_full[b]));
+            mbar_arrive(b_p);
         }
-        if (ok) ok = mbar_wait(b_o_done, (n_kv - 1) & 1, abort, p.status, ST_TIMEOUT_SOFTMAX,
-                               0x20000);
+        if (ok) ok = mbar_wait(b_o, (n - 1) & 1, abort, p.status, ST_TIMEOUT_SOFTMAX,
+                               0x20000 | t);
+        if (threadIdx.x == 32 * kSoftmaxWarp0) trace_stamp(p.trace, 2);
         ok = __all_sync(kFull, ok);
+        float o[HD];
         if (ok) {
             tc_fence_after();
-            float o[HD];
-            tmem_ld32(t_lane + kColO, *reinterpret_cast<uint32_t(*)[32]>(o));
-            tmem_ld32(t_lane + kColO + 32, *reinterpret_cast<uint32_t(*)[32]>(o + 32));
+            tmem_ld32(o_col, *reinterpret_cast<uint32_t(*)[32]>(o));
+            tmem_ld32(o_col + 32, *reinterpret_cast<uint32_t(*)[32]>(o + 32));
             tmem_wait_ld();
-            const int grow = q0 + row;
-            if (grow < p.row_end && grow < p.tokens) {
-                const float inv_l = 1.0f / l;
-                const size_t esz = kOutDtype == BL_F32 ? 4 : 2;
-                uint8_t* dst = static_cast<uint8_t*>(p.out) +
-                               esz * (static_cast<size_t>(batch) * p.out_batch_stride +
-                                      static_cast<size_t>(grow) * p.out_row_stride +
-                                      static_cast<size_t>(head - p.out_head_base) * HD);
-                store_row<kOutDtype>(dst, o, inv_l);
+        }
+        const int crow = t * BM + row;  // row within the CTA's 256
+        const int grow = q0 + crow;
+        const bool store = grow < p.row_end && grow < p.tokens;
+        auto out_ptr = [&]() {
+            const size_t esz = kOutDtype == BL_F32 ? 4 : 2;
+            return static_cast<uint8_t*>(p.out) +
+                   esz * (static_cast<size_t>(batch) * p.out_batch_stride +
+                          static_cast<size_t>(grow) * p.out_row_stride +
+                          static_cast<size_t>(head - p.out_head_base) * HD);
+        };
+        bool do_store = ok && store;
+        float inv_l = 1.0f / l;
+        if (p.splits > 1) {
+            // ------------------------------------------ split-key combine
+            const size_t unit = (static_cast<size_t>(batch) * p.heads_rel + blockIdx.y) *
+                                    gridDim.x + blockIdx.x;
+            float* po = p.part_o + ((unit * p.splits + split) * ROWS + crow) * HD;
+            float* pml = p.part_ml + ((unit * p.splits + split) * ROWS + crow) * 2;
+            if (ok) {
+#pragma unroll
+                for (int k = 0; k < HD; k += 4)
+                    *reinterpret_cast<float4*>(po + k) =
+                        make_float4(o[k], o[k + 1], o[k + 2], o[k + 3]);
+                pml[0] = m_used;
+                pml[1] = l;
+            }
+            __threadfence();
+            softmax_bar();
+            if (threadIdx.x == 32 * kSoftmaxWarp0) {
+                const unsigned prev = atomicAdd(p.counters + unit, 1u);
+                tail->last = prev == static_cast<unsigned>(p.splits) - 1;
+            }
+            softmax_bar();
+            do_store = false;
+            if (tail->last) {
+                __threadfence();
+                if (store) {
+                    // O = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s
+                    const float* base_o = p.part_o + (unit * p.splits * ROWS + crow) * HD;
+                    const float* base_ml = p.part_ml + (unit * p.splits * ROWS + crow) * 2;
+                    float mxs = -INFINITY;
+                    for (int s = 0; s < p.splits; ++s) mxs = fmaxf(mxs, base_ml[s * ROWS * 2]);
+#pragma unroll
+                    for (int k = 0; k < HD; ++k) o[k] = 0.0f;
+                    float lsum = 0.0f;
+                    for (int s = 0; s < p.splits; ++s) {
+                        const float w = ex2(base_ml[s * ROWS * 2] - mxs);
+                        lsum += w * base_ml[s * ROWS * 2 + 1];
+                        const float* os = base_o + static_cast<size_t>(s) * ROWS * HD;
+#pragma unroll
+                        for (int k = 0; k < HD; k += 4) {
+                            const float4 v = *reinterpret_cast<const float4*>(os + k);
+                            o[k] += w * v.x;
+                            o[k + 1] += w * v.y;
+                            o[k + 2] += w * v.z;
+                            o[k + 3] += w * v.w;
+                        }
+                    }
+                    inv_l = 1.0f / lsum;
+                    do_store = true;
+                }
+                if (threadIdx.x == 32 * kSoftmaxWarp0) p.counters[unit] = 0u;  // self-cleaning
             }
         }
+        if (do_store) store_row(out_ptr(), kOutDtype, o, inv_l);
     }
 
     tc_fence_before();
@@ -356,9 +546,41 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
+    if (threadIdx.x == 0) trace_stamp(p.trace, 3);
 }
 
-int prepare(const bl_attention_args& a, Launch* out) {
+struct Plan {
+    int splits;
+    int q_ctas;
+    int kv_tiles;
+    size_t units;
+    size_t bytes;  // workspace
+};
+
+Plan plan(const bl_attention_args& a, int splits) {
+    Plan pl{};
+    pl.q_ctas = static_cast<int>((a.row_end - a.row_begin + ROWS - 1) / ROWS);
+    pl.kv_tiles = static_cast<int>((a.tokens + BN - 1) / BN);
+    pl.units = static_cast<size_t>(a.batch) * (a.head_end - a.head_begin) * pl.q_ctas;
+    pl.splits = splits < 1 ? 1 : (splits > pl.kv_tiles ? pl.kv_tiles : splits);
+    pl.bytes = pl.splits > 1 ? pl.units * (static_cast<size_t>(pl.splits) * ROWS * (HD + 2) *
+                                               sizeof(float) + sizeof(unsigned))
+                             : 0;
+    return pl;
+}
+
+// Key splits that fill the 148 SMs of a B200 in one wave when the tile grid
+// alone does not: at most one CTA per SM, at least two key tiles per split.
+int auto_splits(const bl_attention_args& a) {
+    const Plan p1 = plan(a, 1);
+    const size_t ctas = p1.units;
+    if (ctas * 2 > 148) return 1;
+    int s = static_cast<int>(148 / ctas);
+    const int max_s = p1.kv_tiles / 2 > 0 ? p1.kv_tiles / 2 : 1;
+    return s > max_s ? max_s : s;
+}
+
+int validate(const bl_attention_args& a) {
     if (a.head_dim != HD) return fail(BL_ERR_UNSUPPORTED, "attention: head_dim %u (only 64)", a.head_dim);
     if (a.batch == 0 || a.tokens == 0 || a.heads == 0)
         return fail(BL_ERR_INVALID, "attention: zero dimension");
@@ -368,6 +590,12 @@ int prepare(const bl_attention_args& a, Launch* out) {
     if (a.row_begin >= a.row_end || a.row_end > a.tokens)
         return fail(BL_ERR_INVALID, "attention: rows [%u, %u) outside [0, %u)", a.row_begin,
                     a.row_end, a.tokens);
+    return BL_OK;
+}
+
+int prepare(const bl_attention_args& a, void* workspace, uint64_t workspace_bytes, Launch* out) {
+    int rc = validate(a);
+    if (rc != BL_OK) return rc;
     if (a.qk_dtype != BL_F16 && a.qk_dtype != BL_BF16)
         return fail(BL_ERR_UNSUPPORTED, "attention: Q/K dtype %d (f16 or bf16)", a.qk_dtype);
     if (a.v_dtype != BL_F16)
@@ -387,16 +615,33 @@ int prepare(const bl_attention_args& a, Launch* out) {
         (reinterpret_cast<uintptr_t>(a.out) & 15u) != 0)
         return fail(BL_ERR_INVALID, "attention: output stride/alignment");
 
+    // Key splits: as asked; automatic (0) picks the most that fill the SMs and
+    // fit the given workspace (none: 1).
+    int want = static_cast<int>(a.kv_splits);
+    if (want == 0) {
+        want = workspace != nullptr ? auto_splits(a) : 1;
+        while (want > 1 && plan(a, want).bytes > workspace_bytes) --want;
+    }
+    const Plan pl = plan(a, want);
+    if (pl.splits > 1) {
+        if (workspace == nullptr || workspace_bytes < pl.bytes)
+            return fail(BL_ERR_CAPACITY, "attention: %d key splits need a %zu-byte workspace",
+                        pl.splits, pl.bytes);
+        if (reinterpret_cast<uintptr_t>(workspace) & 255u)
+            return fail(BL_ERR_INVALID, "attention: workspace must be 256-byte aligned");
+    }
+
     CUtensorMap tm;
     const uint64_t dims[3] = {row, a.tokens, a.batch};
     const uint64_t strides[2] = {row * 2, row * 2 * a.tokens};
     const uint32_t box[3] = {HD, BM, 1};
-    int rc = make_tmap_16bit_3d(&tm, a.qkv, dims, strides, box);
+    rc = make_tmap_16bit_3d(&tm, a.qkv, dims, strides, box);
     if (rc != BL_OK) return rc;
 
     Params p{};
     p.tokens = static_cast<int>(a.tokens);
     p.head_begin = static_cast<int>(a.head_begin);
+    p.heads_rel = static_cast<int>(a.head_end - a.head_begin);
     p.row_begin = static_cast<int>(a.row_begin);
     p.row_end = static_cast<int>(a.row_end);
     p.q_col0 = 0;
@@ -404,33 +649,60 @@ int prepare(const bl_attention_args& a, Launch* out) {
     p.v_col0 = static_cast<int>(2 * a.heads * HD);
     p.scale_log2 = a.scale * 1.4426950408889634f;
     p.qk_fmt = a.qk_dtype == BL_BF16 ? 1 : 0;
-    p.out_dtype = a.out_dtype;
     p.out = a.out;
     p.out_row_stride = static_cast<long long>(orow);
     p.out_batch_stride = static_cast<long long>(orow) * a.tokens;
     p.out_head_base = static_cast<int>(a.out_head_base);
+    p.splits = pl.splits;
+    p.kv_tiles = pl.kv_tiles;
+    if (pl.splits > 1) {
+        uint8_t* ws = static_cast<uint8_t*>(workspace);
+        const size_t po = pl.units * pl.splits * ROWS * HD * sizeof(float);
+        const size_t pm = pl.units * pl.splits * ROWS * 2 * sizeof(float);
+        p.part_o = reinterpret_cast<float*>(ws);
+        p.part_ml = reinterpret_cast<float*>(ws + po);
+        p.counters = reinterpret_cast<unsigned*>(ws + po + pm);
+    }
+    p.trace = reinterpret_cast<unsigned long long*>(a.trace);
     p.status = status_ptr();
 
-    dim3 grid((a.row_end - a.row_begin + BM - 1) / BM, a.head_end - a.head_begin, a.batch);
+    const dim3 grid(pl.q_ctas, a.head_end - a.head_begin, a.batch * pl.splits);
     if (grid.y > 65535 || grid.z > 65535) return fail(BL_ERR_INVALID, "attention: grid too large");
     auto kern = a.out_dtype == BL_F32   ? attention_fwd<BL_F32>
                 : a.out_dtype == BL_F16 ? attention_fwd<BL_F16>
                                         : attention_fwd<BL_BF16>;
     BL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(kSmemBytes)));
+    // setmaxnreg.inc draws on the block's launch allocation: the split above
+    // is sized for exactly kLaunchRegs per thread, so refuse any other build.
+    cudaFuncAttributes fa{};
+    BL_CUDA_TRY(cudaFuncGetAttributes(&fa, kern));
+    if (fa.numRegs != kLaunchRegs)
+        return fail(BL_ERR_UNSUPPORTED,
+                    "attention: kernel built with %d registers per thread, the register split "
+                    "needs exactly %d",
+                    fa.numRegs, kLaunchRegs);
     out->op = 1;
     out->run = [=](cudaStream_t s) {
-        kern<<<grid, kThreads, kSmemBytes, s>>>(tm, tm, tm, p);
-        return cudaGetLastError();
+        return launch_k(kern, grid, dim3(kThreads), kSmemBytes, s, tm, tm, tm, p);
     };
     return BL_OK;
 }
 
 }  // namespace attn
 
-int prepare_attention(const bl_attention_args& a, Launch* out) { return attn::prepare(a, out); }
+int prepare_attention(const bl_attention_args& a, Launch* out) {
+    return attn::prepare(a, a.workspace, a.workspace_bytes, out);
+}
 
 }  // namespace bl
+
+extern "C" uint64_t bl_attention_workspace_bytes(const bl_attention_args* args) {
+    if (args == nullptr || bl::attn::validate(*args) != BL_OK) return 0;
+    const int want = args->kv_splits == 0 ? bl::attn::auto_splits(*args)
+                                          : static_cast<int>(args->kv_splits);
+    return bl::attn::plan(*args, want).bytes;
+}
 
 extern "C" int bl_attention(const bl_attention_args* args, void* stream) {
     if (args == nullptr) return bl::fail(BL_ERR_INVALID, "attention: null args");

@@ -165,6 +165,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tail->abort = 0;
         fence_barrier_init();
         fence_proxy_async_smem();
+        // descriptors are launch parameters: fetch them while the previous
+        // kernel may still be running
+        tma_prefetch_desc(&tm_b);
+        if (!kLn) tma_prefetch_desc(&tm_a);
     }
     if (warp == 1) {
         tmem_alloc(smem_u32(&tail->tmem_base), L::kTmemCols);
@@ -174,6 +178,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tail->tmem_base;
+    pdl_trigger();
+    pdl_wait();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -235,25 +241,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         if (kLn) {
             // ---------------------------------------------- LayerNorm prologue
-            // Row statistics, one thread per row: a one-pass sum and sum of
-            // squares shifted by the row's first element (so a large mean does
-            // not cancel), the biased variance of reference.rs:247-270.
-            float mean = 0.0f, rstd = 0.0f;
-            const float* xr = p.x + static_cast<long long>(grow) * p.ldx;
-            if (grow < p.M) {
+            // Warp w normalises rows [32 w, 32 w + 32) of the tile, the lanes
+            // spread along the row so every load is one coalesced segment.
+            // Statistics: a one-pass sum and sum of squares of the deviations
+            // from the row's first element (so a large mean does not cancel),
+            // the biased variance of reference.rs:247-270; lane r keeps row r's.
+            const int dt = p.ab_fmt ? BL_BF16 : BL_F16;
+            const float inv_k = 1.0f / static_cast<float>(p.K);
+            float my_mean = 0.0f, my_rstd = 0.0f;
+            for (int r = 0; r < 32; ++r) {
+                const int gr = m0 + sub * 32 + r;
+                if (gr >= p.M) break;
+                const float* xr = p.x + static_cast<long long>(gr) * p.ldx;
                 const float x0 = xr[0];
                 float s1 = 0.0f, s2 = 0.0f;
-                for (int k = 0; k < p.K; k += 4) {
-                    const float4 v = *reinterpret_cast<const float4*>(xr + k);
-                    const float d0 = v.x - x0, d1 = v.y - x0, d2 = v.z - x0, d3 = v.w - x0;
-                    s1 += (d0 + d1) + (d2 + d3);
-                    s2 += (d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3);
+                for (int k = 2 * lane; k < p.K; k += 64) {
+                    const float2 v = *reinterpret_cast<const float2*>(xr + k);
+                    const float d0 = v.x - x0, d1 = v.y - x0;
+                    s1 += d0 + d1;
+                    s2 += d0 * d0 + d1 * d1;
                 }
-                const float inv_k = 1.0f / static_cast<float>(p.K);
-                const float dm = s1 * inv_k;
-                const float var = fmaxf(s2 * inv_k - dm * dm, 0.0f);
-                mean = x0 + dm;
-                rstd = rsqrtf(var + p.eps);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    s1 += __shfl_xor_sync(kFull, s1, o);
+                    s2 += __shfl_xor_sync(kFull, s2, o);
+                }
+                if (lane == r) {
+                    const float dm = s1 * inv_k;
+                    my_mean = x0 + dm;
+                    my_rstd = rsqrtf(fmaxf(s2 * inv_k - dm * dm, 0.0f) + p.eps);
+                }
             }
             for (int kb = 0; kb < nk; ++kb) {
                 const int s = kb % STAGES;
@@ -263,30 +280,27 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ok = __all_sync(kFull, ok);
                     if (!ok) break;
                 }
-                uint8_t* arow = sA(s) + row * 128;
-#pragma unroll
-                for (int ch = 0; ch < 8; ++ch) {
-                    const int k = kb * BK + ch * 8;
-                    uint4 w = make_uint4(0, 0, 0, 0);
-                    if (grow < p.M) {
-                        const float4 v0 = *reinterpret_cast<const float4*>(xr + k);
-                        const float4 v1 = *reinterpret_cast<const float4*>(xr + k + 4);
-                        const float4 g0 = __ldg(reinterpret_cast<const float4*>(p.gamma + k));
-                        const float4 g1 = __ldg(reinterpret_cast<const float4*>(p.gamma + k + 4));
-                        const float4 b0 = __ldg(reinterpret_cast<const float4*>(p.beta + k));
-                        const float4 b1 = __ldg(reinterpret_cast<const float4*>(p.beta + k + 4));
-                        const int dt = p.ab_fmt ? BL_BF16 : BL_F16;
-                        w.x = pack2((v0.x - mean) * rstd * g0.x + b0.x,
-                                    (v0.y - mean) * rstd * g0.y + b0.y, dt);
-                        w.y = pack2((v0.z - mean) * rstd * g0.z + b0.z,
-                                    (v0.w - mean) * rstd * g0.w + b0.w, dt);
-                        w.z = pack2((v1.x - mean) * rstd * g1.x + b1.x,
-                                    (v1.y - mean) * rstd * g1.y + b1.y, dt);
-                        w.w = pack2((v1.z - mean) * rstd * g1.z + b1.z,
-                                    (v1.w - mean) * rstd * g1.w + b1.w, dt);
+                const int k = kb * BK + 2 * lane;
+                const float2 g = __ldg(reinterpret_cast<const float2*>(p.gamma + k));
+                const float2 b = __ldg(reinterpret_cast<const float2*>(p.beta + k));
+                uint8_t* tile = sA(s);
+                // lane's 4 bytes: 16-byte chunk lane/4 of the row, XOR row%8
+                const int chunk = lane >> 2, off = (lane & 3) * 4;
+#pragma unroll 4
+                for (int r = 0; r < 32; ++r) {
+                    const int trow = sub * 32 + r;
+                    const int gr = m0 + trow;
+                    const float mean = __shfl_sync(kFull, my_mean, r);
+                    const float rstd = __shfl_sync(kFull, my_rstd, r);
+                    uint32_t w = 0;
+                    if (gr < p.M) {
+                        const float2 v = *reinterpret_cast<const float2*>(
+                            p.x + static_cast<long long>(gr) * p.ldx + k);
+                        w = pack2((v.x - mean) * rstd * g.x + b.x, (v.y - mean) * rstd * g.y + b.y,
+                                  dt);
                     }
-                    // 128-byte swizzle: 16-byte chunk index XOR (row % 8).
-                    *reinterpret_cast<uint4*>(arow + ((ch ^ (row & 7)) << 4)) = w;
+                    *reinterpret_cast<uint32_t*>(tile + trow * 128 + ((chunk ^ (trow & 7)) << 4) +
+                                                 off) = w;
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
@@ -396,8 +410,7 @@ int prepare_t(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, Lau
     const dim3 grid(p.m_tiles, p.N / BN);
     out->op = 2;
     out->run = [=](cudaStream_t s) {
-        kern<<<grid, kThreads, smem, s>>>(ta, tb, p);
-        return cudaGetLastError();
+        return launch_k(kern, grid, dim3(kThreads), smem, s, ta, tb, p);
     };
     return BL_OK;
 }

@@ -8,6 +8,7 @@
 #include <cstdarg>
 #include <cstdint>
 #include <functional>
+#include <utility>
 
 #include "../../include/beatlm_b200.h"
 #include "sm100.cuh"
@@ -49,6 +50,29 @@ int prepare_layernorm(const bl_layernorm_args& a, Launch* out);
 int prepare_layernorm_rows(const bl_layernorm_args& a, uint32_t row_begin, uint32_t row_end,
                            Launch* out);
 int prepare_patchify(const bl_patchify_args& a, Launch* out);
+
+// Whether launches carry the programmatic-stream-serialisation attribute
+// (on unless the environment sets BEATLM_B200_PDL=0).
+bool pdl_enabled();
+
+// Launches `kern` on `s` with programmatic dependent launch when enabled;
+// every kernel of this library executes pdl_wait() before touching global
+// memory, so the attribute is always safe.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                     Args&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 inline int enqueue(const Launch& l, cudaStream_t s) {
     cudaError_t e = l.run(s);

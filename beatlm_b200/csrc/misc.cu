@@ -23,6 +23,8 @@ __device__ __forceinline__ uint16_t to16(float v, int dt) {
 // defines the layer norm; f32 arithmetic.
 template <int kPerLane>
 __global__ void __launch_bounds__(256) layernorm_kernel(bl_layernorm_args a, int row_begin, int row_end) {
+    pdl_trigger();
+    pdl_wait();
     const int row = row_begin + static_cast<int>(blockIdx.x) * 8 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= row_end) return;
@@ -69,6 +71,8 @@ __global__ void __launch_bounds__(256) layernorm_kernel(bl_layernorm_args a, int
 // is (ky, kx, ci) = (t / (p*cin), (t / cin) % p, t % cin), the HWIO order of
 // the reference's patch weights, so row . weight[cout][t] is its patch_embed.
 __global__ void patchify_kernel(bl_patchify_args a, int grid_side, int taps) {
+    pdl_trigger();
+    pdl_wait();
     const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
     const int groups = static_cast<int>(a.k_pad / 8);
     const long long patches = static_cast<long long>(a.frames) * grid_side * grid_side;
@@ -102,6 +106,8 @@ __global__ void patchify_kernel(bl_patchify_args a, int grid_side, int taps) {
 // Class-token rows: x[f][0][c] = cls[c] + pos[0][c] (f64-free f32 add, as a
 // fused epilogue Add would do).
 __global__ void cls_rows_kernel(bl_patchify_args a, int tokens) {
+    pdl_trigger();
+    pdl_wait();
     const int f = blockIdx.x;
     for (int c = threadIdx.x; c < static_cast<int>(a.dim); c += blockDim.x)
         a.x[static_cast<long long>(f) * tokens * a.dim + c] = a.cls[c] + a.pos[c];
@@ -134,8 +140,7 @@ int prepare_layernorm_rows(const bl_layernorm_args& a, uint32_t row_begin, uint3
                                                       : misc::layernorm_kernel<32>;
     out->op = 3;
     out->run = [=](cudaStream_t s) {
-        kern<<<grid, 256, 0, s>>>(b, r0, r1);
-        return cudaGetLastError();
+        return launch_k(kern, grid, dim3(256), 0, s, b, r0, r1);
     };
     return BL_OK;
 }
@@ -162,9 +167,11 @@ int prepare_patchify(const bl_patchify_args& a, Launch* out) {
     const unsigned blocks = static_cast<unsigned>((work + 255) / 256);
     out->op = 4;
     out->run = [=](cudaStream_t s) {
-        misc::patchify_kernel<<<blocks, 256, 0, s>>>(a, g, static_cast<int>(taps));
-        if (a.x != nullptr) misc::cls_rows_kernel<<<a.frames, 128, 0, s>>>(a, g * g + 1);
-        return cudaGetLastError();
+        cudaError_t e = launch_k(misc::patchify_kernel, dim3(blocks), dim3(256), 0, s, a, g,
+                                 static_cast<int>(taps));
+        if (e == cudaSuccess && a.x != nullptr)
+            e = launch_k(misc::cls_rows_kernel, dim3(a.frames), dim3(128), 0, s, a, g * g + 1);
+        return e;
     };
     return BL_OK;
 }

@@ -1,5 +1,6 @@
 // Error reporting, the device status word and TMA tensor-map encoding.
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -41,6 +42,14 @@ int fail(int code, const char* fmt, ...) {
     vsnprintf(g_msg, sizeof g_msg, fmt, ap);
     va_end(ap);
     return code;
+}
+
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* v = getenv("BEATLM_B200_PDL");
+        return !(v != nullptr && v[0] == '0');
+    }();
+    return on;
 }
 
 Status* status_ptr() {

@@ -29,14 +29,9 @@ struct Status {
     uint32_t count;     // number of error events
 };
 
-// A wait gives up after this long (nanoseconds of %globaltimer).
-constexpr uint64_t kWaitLimitNs = 1000ull * 1000ull * 1000ull;  // 1 s
-
-__device__ __forceinline__ uint64_t global_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
+// A wait gives up after this many SM clock cycles: 1 s at the B200's
+// 1965 MHz maximum, under 2 s at any clock the part runs at under load.
+constexpr long long kWaitLimitCycles = 1965ll * 1000ll * 1000ll;
 
 __device__ __forceinline__ void record_status(Status* st, uint32_t code, uint32_t where) {
     if (st == nullptr) return;
@@ -88,17 +83,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 
 // Waits for the phase of parity `parity` to complete. Gives up when `abort`
 // (a shared flag; may be null) is raised by another role, or after
-// kWaitLimitNs, in which case it records `code` and raises `abort`. Returns
-// false when it gave up.
+// kWaitLimitCycles, in which case it records `code` and raises `abort`.
+// Returns false when it gave up. The clock is read only on the slow path.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
                                           Status* st, uint32_t code, uint32_t where) {
     if (mbar_try_wait(bar, parity)) return true;
-    uint64_t t0 = global_ns();
-    for (uint32_t spin = 0;; ++spin) {
+    const long long t0 = clock64();
+    for (uint32_t spin = 1;; ++spin) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((spin & 15u) == 15u) {
+        if ((spin & 255u) == 0u) {
             if (abort != nullptr && *abort) return false;
-            if (global_ns() - t0 > kWaitLimitNs) {
+            if (clock64() - t0 > kWaitLimitCycles) {
                 if (abort != nullptr) *abort = 1;
                 record_status(st, code, where);
                 return false;
@@ -271,6 +266,16 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
     return r;
 }
+
+// Programmatic dependent launch. Each kernel signals at its start that the
+// next kernel in the stream may be scheduled (its own setup then overlaps this
+// kernel), and waits for the previous kernel's completion and memory before
+// its first global access. Both are no-ops for a kernel launched without the
+// programmatic-serialisation attribute.
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 __device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }

@@ -192,41 +192,69 @@ class Buffers:
         self.x = torch.empty((rows, cfg.dim), dtype=torch.float32, device=device)
         self.qkv = torch.empty((rows, 3 * cfg.dim), dtype=torch.int16, device=device)
         self.o = torch.empty((rows, cfg.dim), dtype=td, device=device)
+        self.xn = torch.empty((rows, cfg.dim), dtype=td, device=device)
         self.h = torch.empty((rows, cfg.mlp), dtype=td, device=device)
         self.patches = torch.empty((frames * (t - 1), cfg.k_pad), dtype=td, device=device)
+        # split-key attention workspace, sized for the automatic split count
+        proto = ops.attention_args(self.qkv, tokens=t, heads=cfg.heads, head_dim=cfg.head_dim,
+                                   batch=frames, out=self.o)
+        self.attn_ws = ops.attention_workspace(ops.attention_workspace_bytes(proto), device)
         self.features = ([torch.empty((frames * (t - 1), cfg.dim), dtype=torch.float32,
                                       device=device) for _ in cfg.out_indices]
                          if features else [])
 
 
 def block_specs(blk: DeviceBlock, cfg: ViTConfig, buf: Buffers, layer: int = 0,
-                parts: int = 1) -> list:
-    """The five fused kernels of one pre-norm block (reference.rs:520-544),
-    in place on ``buf.x``:
-    x1 = x + ls1 * proj(attention(norm1(x))); x = x1 + ls2 * fc2(gelu(fc1(norm2(x1))))."""
+                parts: int = 1, fused_ln: bool = False) -> list:
+    """The fused kernels of one pre-norm block (reference.rs:520-544), in
+    place on ``buf.x``:
+    x1 = x + ls1 * proj(attention(norm1(x))); x = x1 + ls2 * fc2(gelu(fc1(norm2(x1)))).
+
+    ``fused_ln=False`` (default, 7 kernels): each LayerNorm is its own
+    bandwidth-bound kernel writing 16-bit rows that the next GEMM loads by
+    TMA. ``fused_ln=True`` (5 kernels): the LayerNorm is the QKV/fc1 GEMM's
+    prologue. At ViT-S shapes (K = 384) every N-tile CTA of the prologue form
+    must read the whole 128 x 384 f32 row block, which costs more than the
+    extra launch, so the split form is the default; both are tested."""
     from .runtime import Spec
     d = cfg.dim
     name = "block%d." % layer
+    attn = Spec(ops.attention_args(buf.qkv, tokens=buf.tokens, heads=cfg.heads,
+                                   head_dim=cfg.head_dim, batch=buf.frames, qk_dtype=blk.dtype,
+                                   out=buf.o, workspace=buf.attn_ws), name + "attention", parts)
+    proj = Spec(ops.gemm_args(blk.proj_w, a=buf.o, bias=blk.proj_b, chan_scale=blk.ls1,
+                              residual=buf.x, out=buf.x), name + "proj", parts)
+    fc2 = Spec(ops.gemm_args(blk.fc2_w, a=buf.h, bias=blk.fc2_b, chan_scale=blk.ls2,
+                             residual=buf.x, out=buf.x), name + "fc2", parts)
+    if fused_ln:
+        return [
+            Spec(ops.gemm_args(blk.qkv_w, ln=(buf.x, blk.norm1[0], blk.norm1[1], cfg.eps),
+                               bias=blk.qkv_b, out=buf.qkv, out_dtype=blk.dtype,
+                               out_split=(2 * d, "f16")), name + "qkv", parts),
+            attn, proj,
+            Spec(ops.gemm_args(blk.fc1_w, ln=(buf.x, blk.norm2[0], blk.norm2[1], cfg.eps),
+                               bias=blk.fc1_b, act="gelu_erf", out=buf.h), name + "fc1", parts),
+            fc2,
+        ]
     return [
-        Spec(ops.gemm_args(blk.qkv_w, ln=(buf.x, blk.norm1[0], blk.norm1[1], cfg.eps),
-                           bias=blk.qkv_b, out=buf.qkv, out_dtype=blk.dtype,
+        Spec(ops.layernorm_args(buf.x, blk.norm1[0], blk.norm1[1], cfg.eps, out=buf.xn),
+             name + "norm1", parts),
+        Spec(ops.gemm_args(blk.qkv_w, a=buf.xn, bias=blk.qkv_b, out=buf.qkv, out_dtype=blk.dtype,
                            out_split=(2 * d, "f16")), name + "qkv", parts),
-        Spec(ops.attention_args(buf.qkv, tokens=buf.tokens, heads=cfg.heads,
-                                head_dim=cfg.head_dim, batch=buf.frames, qk_dtype=blk.dtype,
-                                out=buf.o), name + "attention", parts),
-        Spec(ops.gemm_args(blk.proj_w, a=buf.o, bias=blk.proj_b, chan_scale=blk.ls1,
-                           residual=buf.x, out=buf.x), name + "proj", parts),
-        Spec(ops.gemm_args(blk.fc1_w, ln=(buf.x, blk.norm2[0], blk.norm2[1], cfg.eps),
-                           bias=blk.fc1_b, act="gelu_erf", out=buf.h), name + "fc1", parts),
-        Spec(ops.gemm_args(blk.fc2_w, a=buf.h, bias=blk.fc2_b, chan_scale=blk.ls2,
-                           residual=buf.x, out=buf.x), name + "fc2", parts),
+        attn, proj,
+        Spec(ops.layernorm_args(buf.x, blk.norm2[0], blk.norm2[1], cfg.eps, out=buf.xn),
+             name + "norm2", parts),
+        Spec(ops.gemm_args(blk.fc1_w, a=buf.xn, bias=blk.fc1_b, act="gelu_erf", out=buf.h),
+             name + "fc1", parts),
+        fc2,
     ]
 
 
-def run_block(blk: DeviceBlock, cfg: ViTConfig, buf: Buffers, stream=None, parts: int = 1):
+def run_block(blk: DeviceBlock, cfg: ViTConfig, buf: Buffers, stream=None, parts: int = 1,
+              fused_ln: bool = False):
     """One block, built and encoded at once (tests; the encoder prebuilds)."""
     from .runtime import Kernels
-    k = Kernels(block_specs(blk, cfg, buf, parts=parts))
+    k = Kernels(block_specs(blk, cfg, buf, parts=parts, fused_ln=fused_ln))
     k.encode_all(stream)
     return k
 
@@ -307,4 +335,4 @@ class Encoder:
     def launches_per_frame_batch(self, layers: int | None = None) -> int:
         n = self.cfg.layers if layers is None else layers
         taken = sum(1 for i in self.cfg.out_indices if i <= n)
-        return 3 + 5 * n + taken  # patchify (2 kernels) + patch GEMM, 5 per block, norms
+        return 3 + 7 * n + taken  # patchify (2 kernels) + patch GEMM, 7 per block, norms

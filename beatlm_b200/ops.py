@@ -50,7 +50,11 @@ def pack_qkv(qkv, qk_dtype: str = "f16", device="cuda"):
 
 def attention_args(qkv, *, tokens, heads, out, head_dim=64, batch=1, qk_dtype="f16",
                    out_dtype=None, scale=None, rows=None, head_range=None, out_head_base=0,
-                   qkv_row_stride=0, out_row_stride=None):
+                   qkv_row_stride=0, out_row_stride=None, workspace=None, kv_splits=0,
+                   trace=None):
+    """``workspace``: a zero-filled device buffer of at least
+    ``attention_workspace_bytes`` bytes enables key splits (``kv_splits`` 0 =
+    automatic); without one the kernel runs unsplit."""
     if scale is None:
         scale = 1.0 / math.sqrt(head_dim)
     r0, r1 = rows or (0, tokens)
@@ -62,13 +66,30 @@ def attention_args(qkv, *, tokens, heads, out, head_dim=64, batch=1, qk_dtype="f
                            qkv=qkv.data_ptr(), qkv_row_stride=qkv_row_stride,
                            out=out.data_ptr(),
                            out_row_stride=out.shape[-1] if out_row_stride is None
-                           else out_row_stride, out_head_base=out_head_base)
+                           else out_row_stride, out_head_base=out_head_base,
+                           kv_splits=kv_splits,
+                           workspace=None if workspace is None else workspace.data_ptr(),
+                           workspace_bytes=0 if workspace is None else workspace.numel(),
+                           trace=None if trace is None else trace.data_ptr())
+
+
+def attention_workspace_bytes(args) -> int:
+    """Bytes of workspace ``bl_attention`` wants for these arguments (with
+    ``kv_splits`` 0 it reports what the automatic choice would use)."""
+    return N.lib().bl_attention_workspace_bytes(ctypes.byref(args))
+
+
+def attention_workspace(nbytes: int, device="cuda"):
+    """A zero-filled, 256-byte-aligned device workspace (torch allocations are
+    256-byte aligned)."""
+    import torch
+    return torch.zeros(max(int(nbytes), 256), dtype=torch.uint8, device=device)
 
 
 def attention(qkv, *, tokens: int, heads: int, head_dim: int = 64, batch: int = 1,
               qk_dtype: str = "f16", out=None, out_dtype: str = "f32", scale: float | None = None,
               rows: tuple[int, int] | None = None, head_range: tuple[int, int] | None = None,
-              out_head_base: int = 0, stream=None):
+              out_head_base: int = 0, stream=None, workspace=None, kv_splits: int = 0):
     """The fused scores -> scale -> softmax -> values chain of one layer
     (reference kernel.rs:722-777) on packed ``[batch][tokens][3][heads][64]``
     16-bit ``qkv``; returns ``out`` ``[batch][tokens][heads * 64]``."""
@@ -83,7 +104,8 @@ def attention(qkv, *, tokens: int, heads: int, head_dim: int = 64, batch: int = 
         odt = None if out.dtype.is_floating_point else out_dtype
     a = attention_args(qkv, tokens=tokens, heads=heads, out=out, head_dim=head_dim, batch=batch,
                        qk_dtype=qk_dtype, out_dtype=odt, scale=scale, rows=rows,
-                       head_range=head_range, out_head_base=out_head_base)
+                       head_range=head_range, out_head_base=out_head_base,
+                       workspace=workspace, kv_splits=kv_splits)
     N.check(N.lib().bl_attention(ctypes.byref(a), _stream_ptr(stream)))
     return out
 

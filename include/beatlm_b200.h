@@ -85,6 +85,16 @@ typedef enum bl_dtype { BL_F32 = 0, BL_F16 = 1, BL_BF16 = 2 } bl_dtype;
  * (kernel.rs:2384) and a head slab for head-parallel runs. head_dim must be
  * 64. qkv and out must be 16-byte aligned and their row strides multiples of
  * 8 elements (16 bytes). Enqueues on `stream`; allocates nothing.
+ *
+ * Key splits: when the query tiles alone would leave SMs idle (ViT-S at one
+ * frame: 36 CTAs for 148 SMs), the keys are split across CTAs whose partial
+ * results are combined by the last CTA of each group. That needs a
+ * caller-owned device workspace of bl_attention_workspace_bytes() bytes,
+ * 256-byte aligned, zero-filled once before its first use (every call leaves
+ * its counters at zero again; calls that overlap on the GPU must not share
+ * one). kv_splits = 0 picks the split count when a workspace is given and
+ * uses 1 (no workspace) otherwise; 1 never splits; larger counts need the
+ * workspace (BL_ERR_CAPACITY otherwise).
  */
 typedef struct bl_attention_args {
     uint32_t batch;
@@ -102,9 +112,20 @@ typedef struct bl_attention_args {
     void* out;
     uint64_t out_row_stride; /* 0 = heads * head_dim */
     uint32_t out_head_base;
+    uint32_t kv_splits;      /* 0 = automatic (with a workspace), 1 = none */
+    void* workspace;
+    uint64_t workspace_bytes;
+    /* Optional per-CTA timeline (NULL = off): CTA b writes four %globaltimer
+     * stamps (ns) at trace[4b..4b+3]: entry, setup done, softmax done, exit.
+     * CTAs are numbered x-fastest over the grid (query groups, heads,
+     * batch x splits); the buffer holds 4 * CTAs uint64 values. */
+    uint64_t* trace;
 } bl_attention_args;
 
 int bl_attention(const bl_attention_args* args, void* stream);
+
+/* Workspace bytes bl_attention needs for these arguments (0: no split). */
+uint64_t bl_attention_workspace_bytes(const bl_attention_args* args);
 
 /* ------------------------------------------------------------------ linear */
 

@@ -55,6 +55,48 @@ def test_attention_matches_the_oracle(t, qk_dtype):
     assert rel <= REL_L2 and mx < 5e-3
 
 
+@pytest.mark.parametrize("t,splits", [(300, 2), (1370, 3), (1370, 0), (1370, 11), (129, 2),
+                                      (5477, 0)])
+def test_key_splits_match_the_oracle(t, splits):
+    """Keys split across CTAs, combined by the last CTA of each tile group
+    through a caller-owned workspace; repeated calls reuse it (its counters
+    return to zero)."""
+    import torch
+    import beatlm_b200 as bl
+    from beatlm_b200 import ops
+    h = 6
+    qkv = oracle.normal(300 + t, t * 3 * h * 64).reshape(1, t, 3, h, 64)
+    dev = bl.pack_qkv(qkv, "bf16")
+    out = torch.zeros((1, t, h * 64), dtype=torch.float32, device="cuda")
+    args = ops.attention_args(dev, tokens=t, heads=h, out=out, qk_dtype="bf16",
+                              kv_splits=splits)
+    nbytes = ops.attention_workspace_bytes(args)
+    ws = ops.attention_workspace(nbytes)
+    for _ in range(2):
+        out.zero_()
+        bl.attention(dev, tokens=t, heads=h, qk_dtype="bf16", out=out, workspace=ws,
+                     kv_splits=splits)
+    torch.cuda.synchronize()
+    assert bl.status(reset=True).code == 0
+    units = h * -(-t // 256)  # one counter per (head, 256-row query group), at the end
+    assert nbytes == 0 or not ws[nbytes - 4 * units:nbytes].any()  # counters back at zero
+    rows = (0, t) if t < 2000 else (1000, 1130)
+    want = oracle.attention(_rounded(qkv, "bf16")[0].reshape(t, -1), t, h, 64, rows=rows)
+    rel, mx = _errors(out.cpu().numpy()[0][rows[0]:rows[1]], want)
+    print("T=%d splits=%d (workspace %d B): rel-L2 %.3e" % (t, splits, nbytes, rel))
+    assert rel <= REL_L2
+
+
+def test_split_workspace_too_small_is_an_error():
+    import torch
+    import beatlm_b200 as bl
+    t, h = 1370, 6
+    dev = bl.pack_qkv(np.zeros((1, t, 3, h, 64), np.float32), "f16")
+    ws = torch.zeros(1024, dtype=torch.uint8, device="cuda")
+    with pytest.raises(bl.BackendError, match="workspace"):
+        bl.attention(dev, tokens=t, heads=h, workspace=ws, kv_splits=4)
+
+
 @pytest.mark.parametrize("out_dtype", ["f16", "bf16"])
 def test_16bit_outputs(out_dtype):
     t, h = 257, 2

@@ -28,8 +28,9 @@ def _rel(got, want):
         np.max(np.abs(got - want)))
 
 
+@pytest.mark.parametrize("fused_ln", [False, True])
 @pytest.mark.parametrize("dtype", ["f16", "bf16"])
-def test_one_block_matches_the_reference_block(dtype):
+def test_one_block_matches_the_reference_block(dtype, fused_ln):
     import torch
     import beatlm_b200 as bl
     from beatlm_b200.model import (Buffers, DeviceBlock, ViTConfig, block_weights_by_role,
@@ -40,7 +41,7 @@ def test_one_block_matches_the_reference_block(dtype):
     blk = DeviceBlock(w, D, MLP, dtype)
     buf = Buffers(cfg, 1, dtype, features=False)
     buf.x.copy_(torch.from_numpy(x.reshape(T, D)))
-    run_block(blk, cfg, buf)
+    run_block(blk, cfg, buf, fused_ln=fused_ln)
     torch.cuda.synchronize()
     st = bl.status(reset=True)
     assert st.code == 0, hex(st.code)

@@ -32,9 +32,9 @@ def test_split_block_equals_the_whole_block(parts):
     cfg, blk, buf, x0 = _block(frames=2)
     whole = Kernels(block_specs(blk, cfg, buf))
     split = Kernels(block_specs(blk, cfg, buf, parts=parts))
-    assert len(whole) == 5
-    assert len(split) > 5
-    assert split.label(0).startswith("block0.qkv [1/")
+    assert len(whole) == 7
+    assert len(split) > 7
+    assert split.label(0).startswith("block0.norm1 [1/")
     buf.x.copy_(x0)
     whole.encode_all()
     torch.cuda.synchronize()
@@ -89,7 +89,7 @@ def test_slice_timer_rules():
     got = t.collect_ready()
     assert [f.frame for f in got] == [0, 1, 2]           # submission order
     for f in got:
-        assert [kernel for kernel, _ in f.compute] == [0, 1, 2, 3, 4]
+        assert [kernel for kernel, _ in f.compute] == [0, 1, 2, 3, 4, 5, 6]
         assert all(us > 0 for _, us in f.compute)
         assert f.begin_us[0] == 0.0 and f.begin_us == sorted(f.begin_us)
     assert t.stats()["frames_collected"] == 3
