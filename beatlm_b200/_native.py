@@ -55,6 +55,7 @@ SIGNATURES = {
     "bl_status": (ctypes.c_int, [ctypes.POINTER(Status), ctypes.c_int]),
     "bl_attention": (ctypes.c_int, [ctypes.POINTER(AttentionArgs), ctypes.c_void_p]),
     "bl_attention_workspace_bytes": (ctypes.c_uint64, [ctypes.POINTER(AttentionArgs)]),
+    "bl_attention_noalloc": (ctypes.c_int, [ctypes.POINTER(AttentionArgs), ctypes.c_void_p]),
 }
 
 

@@ -29,6 +29,8 @@
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 
+#include <mutex>
+
 #include "host.h"
 
 namespace bl {
@@ -696,6 +698,73 @@ int prepare_attention(const bl_attention_args& a, Launch* out) {
 }
 
 }  // namespace bl
+
+// ---------------------------------------------------------------- no-alloc
+// bl_attention_noalloc: the same kernel with its split-key scratch in a
+// file-scope device array instead of a caller-owned workspace, for callers
+// that cannot allocate device memory (see the header).
+namespace {
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;  // 16 MiB
+// Every GPU that loads this library holds this array until the process exits.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {};
+
+// The array's device address on the current device. In host code the
+// array's name is only a host-side stand-in, so the address is looked up
+// once per device, with that device current, and cached.
+int noalloc_scratch(void** out) {
+    int dev = 0;
+    BL_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return bl::fail(BL_ERR_UNSUPPORTED, "no-alloc attention: device %d", dev);
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (g_noalloc_addr[dev] == nullptr) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || p == nullptr)
+            return bl::fail(BL_ERR_CUDA, "no-alloc attention: cudaGetSymbolAddress: %s",
+                            cudaGetErrorString(e));
+        g_noalloc_addr[dev] = p;
+    }
+    *out = g_noalloc_addr[dev];
+    return BL_OK;
+}
+}  // namespace
+
+extern "C" int bl_attention_noalloc(const bl_attention_args* args, void* stream) {
+    using namespace bl;
+    if (args == nullptr) return fail(BL_ERR_INVALID, "no-alloc attention: null args");
+    int rc = attn::validate(*args);
+    if (rc != BL_OK) return rc;
+    // the split count bl_attention would use with a workspace of this size
+    int want = static_cast<int>(args->kv_splits);
+    if (want == 0) {
+        want = attn::auto_splits(*args);
+        while (want > 1 && attn::plan(*args, want).bytes > kNoAllocScratchBytes) --want;
+    }
+    const attn::Plan pl = attn::plan(*args, want);
+    if (pl.bytes > kNoAllocScratchBytes)
+        return fail(BL_ERR_CAPACITY,
+                    "no-alloc attention: %d key splits need %zu bytes of scratch, more than "
+                    "the %zu-byte static scratch",
+                    pl.splits, pl.bytes, kNoAllocScratchBytes);
+    void* scratch = nullptr;
+    if ((rc = noalloc_scratch(&scratch)) != BL_OK) return rc;
+    Launch l;
+    rc = attn::prepare(*args, scratch, kNoAllocScratchBytes, &l);
+    if (rc != BL_OK) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (pl.splits > 1) {
+        // The array keeps the last call's contents: the split counters must
+        // start at zero, so clear them (no allocation involved).
+        const size_t po = pl.units * pl.splits * attn::ROWS * attn::HD * sizeof(float);
+        const size_t pm = pl.units * pl.splits * attn::ROWS * 2 * sizeof(float);
+        BL_CUDA_TRY(cudaMemsetAsync(static_cast<unsigned char*>(scratch) + po + pm, 0,
+                                    pl.units * sizeof(unsigned), s));
+    }
+    return enqueue(l, s);
+}
 
 extern "C" uint64_t bl_attention_workspace_bytes(const bl_attention_args* args) {
     if (args == nullptr || bl::attn::validate(*args) != BL_OK) return 0;

@@ -127,6 +127,27 @@ int bl_attention(const bl_attention_args* args, void* stream);
 /* Workspace bytes bl_attention needs for these arguments (0: no split). */
 uint64_t bl_attention_workspace_bytes(const bl_attention_args* args);
 
+/*
+ * bl_attention for callers that cannot allocate device memory. No counterpart
+ * in the reference: it exists for hosts whose device memory is fixed up front
+ * (a static memory plan realised once, nothing allocated in the frame loop),
+ * for host runtimes reaching this library through an FFI without a CUDA
+ * allocator of their own, and for code that must not allocate while it runs.
+ * Such a caller cannot provide the split-key workspace, so this entry point
+ * keeps that scratch in a 16 MiB array inside the library (every GPU that
+ * loads the library holds it until the process exits) and allocates nothing:
+ * no cudaMalloc, no cudaFree, no allocating library routine.
+ *
+ * args->workspace and args->workspace_bytes are ignored. kv_splits = 0 picks
+ * the split count that fits the 16 MiB; an explicit count whose scratch would
+ * exceed 16 MiB is rejected with BL_ERR_CAPACITY. The first call on each
+ * device looks up the array's device address (once, with that device
+ * current), so make that first call before any stream capture. Each call
+ * clears the split counters on `stream` before its launch. All calls share the
+ * one array: calls that overlap on the GPU race and must not be issued.
+ */
+int bl_attention_noalloc(const bl_attention_args* args, void* stream);
+
 /* ------------------------------------------------------------------ linear */
 
 enum { BL_ACT_NONE = 0, BL_ACT_RELU = 1, BL_ACT_GELU_TANH = 2, BL_ACT_GELU_ERF = 3 };
