@@ -29,6 +29,7 @@
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "host.h"
@@ -70,6 +71,7 @@ struct Params {
     long long out_batch_stride;  // elements
     int out_head_base;
     int splits;       // key splits; gridDim.z = batch * splits
+    int cluster;      // 1: the splits of a query group are one cluster, combined in DSMEM
     int kv_tiles;     // ceil(tokens / BN)
     float* part_o;    // [unit][split][ROWS][HD]
     float* part_ml;   // [unit][split][ROWS][2]
@@ -84,7 +86,7 @@ __device__ __forceinline__ void trace_stamp(unsigned long long* trace, int slot)
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     const size_t b = blockIdx.x + gridDim.x * (blockIdx.y + static_cast<size_t>(gridDim.y) *
                                                                blockIdx.z);
-    trace[4 * b + slot] = t;
+    trace[8 * b + slot] = t;
 }
 
 struct SmemTail {
@@ -102,6 +104,12 @@ struct SmemTail {
 
 constexpr size_t kSmemBytes = 1024 /*align slack*/ + QT * kTileBytes /*Q*/ +
                               STAGES * 2 * kTileBytes /*K,V*/ + sizeof(SmemTail);
+// Cluster combine: a row's partial (64 O values, then max and sum) in the
+// K/V ring, 68 floats apart so eight threads' 16-byte accesses hit distinct
+// banks.
+constexpr int kPartStride = HD + 4;
+static_assert(ROWS * kPartStride * 4 <= 2 * STAGES * kTileBytes, "partials exceed the ring");
+constexpr int kMaxClusterSplits = 8;  // portable cluster size
 
 __device__ __forceinline__ uint64_t desc_kmajor(uint32_t addr) {
     return sdesc_sw128(addr, 16, 1024);
@@ -354,6 +362,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_wait(smem_u32(&tail->drain), 0, nullptr, p.status, ST_TIMEOUT_DRAIN, 0xD);
             }
         }
+        if (p.cluster) {
+            // the two cluster barriers of the split combine (softmax side below)
+            __syncwarp();
+            cluster_sync();
+            cluster_sync();
+        }
     } else {
         asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
         // ------------------------------------------------------ softmax
@@ -466,6 +480,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok) ok = mbar_wait(b_o, (n - 1) & 1, abort, p.status, ST_TIMEOUT_SOFTMAX,
                                0x20000 | t);
         if (threadIdx.x == 32 * kSoftmaxWarp0) trace_stamp(p.trace, 2);
+        if (threadIdx.x == 32 * (kSoftmaxWarp0 + 4)) trace_stamp(p.trace, 3);
         ok = __all_sync(kFull, ok);
         float o[HD];
         if (ok) {
@@ -486,7 +501,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         };
         bool do_store = ok && store;
         float inv_l = 1.0f / l;
-        if (p.splits > 1) {
+        if (p.cluster) {
+            // ------------------------------ split-key partials, cluster form
+            // Both tiles' last PV must be complete before the K/V ring is
+            // reused for the partials: each warpgroup has seen its own; this
+            // barrier makes it both.
+            softmax_bar();
+            float* part = reinterpret_cast<float*>(sK);  // [ROWS][kPartStride], then m, l
+            float* pr = part + crow * kPartStride;
+#pragma unroll
+            for (int k = 0; k < HD; k += 4)
+                *reinterpret_cast<float4*>(pr + k) = make_float4(o[k], o[k + 1], o[k + 2], o[k + 3]);
+            *reinterpret_cast<float2*>(pr + HD) = make_float2(ok ? m_used : -INFINITY, l);
+            do_store = false;
+            if (threadIdx.x == 32 * kSoftmaxWarp0) trace_stamp(p.trace, 4);
+        } else if (p.splits > 1) {
             // ------------------------------------------ split-key combine
             const size_t unit = (static_cast<size_t>(batch) * p.heads_rel + blockIdx.y) *
                                     gridDim.x + blockIdx.x;
@@ -539,6 +568,77 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
         if (do_store) store_row(out_ptr(), kOutDtype, o, inv_l);
+        if (p.cluster) {
+            // ------------------------------------ cluster combine (DSMEM)
+            // CTA `rank` of the cluster (= its key split) combines rows
+            // [rank * R, rank * R + R) of the 256 from every CTA's partials:
+            // O = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s.
+            __syncwarp();
+            cluster_sync();  // every CTA's partials are in its shared memory
+            if (threadIdx.x == 32 * kSoftmaxWarp0) trace_stamp(p.trace, 5);
+            // Sixteen threads per row, one 16-byte chunk each, so a warp
+            // reads two whole 256-byte rows per remote load and writes two
+            // whole output rows.
+            const int rank = static_cast<int>(cluster_rank());
+            const int per = (ROWS + p.splits - 1) / p.splits;
+            const int i = threadIdx.x - 32 * kSoftmaxWarp0;
+            const int chunk = i & 15;
+            for (int base = 0; base < per; base += 16) {
+                const int r = base + (i >> 4);
+                const int mrow = rank * per + r;  // the row this thread helps combine
+                const int mgrow = q0 + mrow;
+                if (r >= per || mrow >= ROWS || mgrow >= p.row_end || mgrow >= p.tokens) continue;
+                const uint32_t local = smem_u32(sK) + mrow * kPartStride * 4;
+                float2 ml[kMaxClusterSplits];
+                float4 v[kMaxClusterSplits];
+#pragma unroll
+                for (int s = 0; s < kMaxClusterSplits; ++s) {
+                    if (s < p.splits) {
+                        const uint32_t rs = dsmem_addr(local, s);
+                        ml[s] = dsmem_ld2(rs + HD * 4);
+                        v[s] = dsmem_ld4(rs + chunk * 16);
+                    }
+                }
+                float mxs = -INFINITY;
+#pragma unroll
+                for (int s = 0; s < kMaxClusterSplits; ++s)
+                    if (s < p.splits) mxs = fmaxf(mxs, ml[s].x);
+                float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                float lsum = 0.0f;
+#pragma unroll
+                for (int s = 0; s < kMaxClusterSplits; ++s) {
+                    if (s < p.splits) {
+                        const float w = ex2(ml[s].x - mxs);
+                        lsum += w * ml[s].y;
+                        acc.x += w * v[s].x;
+                        acc.y += w * v[s].y;
+                        acc.z += w * v[s].z;
+                        acc.w += w * v[s].w;
+                    }
+                }
+                const float inv = 1.0f / lsum;
+                const size_t esz = kOutDtype == BL_F32 ? 4 : 2;
+                uint8_t* dst = static_cast<uint8_t*>(p.out) +
+                               esz * (static_cast<size_t>(batch) * p.out_batch_stride +
+                                      static_cast<size_t>(mgrow) * p.out_row_stride +
+                                      static_cast<size_t>(head - p.out_head_base) * HD +
+                                      chunk * 4);
+                if (kOutDtype == BL_F32) {
+                    *reinterpret_cast<float4*>(dst) =
+                        make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+                } else if (kOutDtype == BL_F16) {
+                    *reinterpret_cast<uint2*>(dst) = make_uint2(
+                        pack_f16x2(acc.x * inv, acc.y * inv), pack_f16x2(acc.z * inv, acc.w * inv));
+                } else {
+                    *reinterpret_cast<uint2*>(dst) =
+                        make_uint2(pack_bf16x2(acc.x * inv, acc.y * inv),
+                                   pack_bf16x2(acc.z * inv, acc.w * inv));
+                }
+            }
+            if (threadIdx.x == 32 * kSoftmaxWarp0) trace_stamp(p.trace, 6);
+            __syncwarp();
+            cluster_sync();  // no CTA leaves while its partials are being read
+        }
     }
 
     tc_fence_before();
@@ -548,7 +648,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
-    if (threadIdx.x == 0) trace_stamp(p.trace, 3);
+    if (threadIdx.x == 0) trace_stamp(p.trace, 7);
 }
 
 struct Plan {
@@ -617,16 +717,26 @@ int prepare(const bl_attention_args& a, void* workspace, uint64_t workspace_byte
         (reinterpret_cast<uintptr_t>(a.out) & 15u) != 0)
         return fail(BL_ERR_INVALID, "attention: output stride/alignment");
 
-    // Key splits: as asked; automatic (0) picks the most that fill the SMs and
-    // fit the given workspace (none: 1).
+    auto kern = a.out_dtype == BL_F32   ? attention_fwd<BL_F32>
+                : a.out_dtype == BL_F16 ? attention_fwd<BL_F16>
+                                        : attention_fwd<BL_BF16>;
+    BL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(kSmemBytes)));
+    BL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0));
+
+    // Key splits: as asked, or automatic (0). With a workspace the partials
+    // go through it (global combine); without one the splits of a query group
+    // form a thread-block cluster that combines in distributed shared memory.
     int want = static_cast<int>(a.kv_splits);
-    if (want == 0) {
-        want = workspace != nullptr ? auto_splits(a) : 1;
-        while (want > 1 && plan(a, want).bytes > workspace_bytes) --want;
-    }
+    if (want == 0) want = attention_auto_splits(a, workspace != nullptr ? workspace_bytes : 0);
     const Plan pl = plan(a, want);
-    if (pl.splits > 1) {
-        if (workspace == nullptr || workspace_bytes < pl.bytes)
+    const bool cluster = pl.splits > 1 && workspace == nullptr;
+    if (cluster && pl.splits > kMaxClusterSplits)
+        return fail(BL_ERR_CAPACITY,
+                    "attention: %d key splits exceed a cluster (%d); give a %zu-byte workspace",
+                    pl.splits, kMaxClusterSplits, pl.bytes);
+    if (pl.splits > 1 && !cluster) {
+        if (workspace_bytes < pl.bytes)
             return fail(BL_ERR_CAPACITY, "attention: %d key splits need a %zu-byte workspace",
                         pl.splits, pl.bytes);
         if (reinterpret_cast<uintptr_t>(workspace) & 255u)
@@ -656,8 +766,9 @@ int prepare(const bl_attention_args& a, void* workspace, uint64_t workspace_byte
     p.out_batch_stride = static_cast<long long>(orow) * a.tokens;
     p.out_head_base = static_cast<int>(a.out_head_base);
     p.splits = pl.splits;
+    p.cluster = cluster ? 1 : 0;
     p.kv_tiles = pl.kv_tiles;
-    if (pl.splits > 1) {
+    if (pl.splits > 1 && !cluster) {
         uint8_t* ws = static_cast<uint8_t*>(workspace);
         const size_t po = pl.units * pl.splits * ROWS * HD * sizeof(float);
         const size_t pm = pl.units * pl.splits * ROWS * 2 * sizeof(float);
@@ -670,11 +781,6 @@ int prepare(const bl_attention_args& a, void* workspace, uint64_t workspace_byte
 
     const dim3 grid(pl.q_ctas, a.head_end - a.head_begin, a.batch * pl.splits);
     if (grid.y > 65535 || grid.z > 65535) return fail(BL_ERR_INVALID, "attention: grid too large");
-    auto kern = a.out_dtype == BL_F32   ? attention_fwd<BL_F32>
-                : a.out_dtype == BL_F16 ? attention_fwd<BL_F16>
-                                        : attention_fwd<BL_BF16>;
-    BL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(kSmemBytes)));
     // setmaxnreg.inc draws on the block's launch allocation: the split above
     // is sized for exactly kLaunchRegs per thread, so refuse any other build.
     cudaFuncAttributes fa{};
@@ -685,13 +791,73 @@ int prepare(const bl_attention_args& a, void* workspace, uint64_t workspace_byte
                     "needs exactly %d",
                     fa.numRegs, kLaunchRegs);
     out->op = 1;
-    out->run = [=](cudaStream_t s) {
-        return launch_k(kern, grid, dim3(kThreads), kSmemBytes, s, tm, tm, tm, p);
-    };
+    if (cluster) {
+        const dim3 cdim(1, 1, pl.splits);
+        out->run = [=](cudaStream_t s) {
+            return launch_k_cluster(kern, grid, dim3(kThreads), cdim, kSmemBytes, s, tm, tm, tm,
+                                    p);
+        };
+    } else {
+        out->run = [=](cudaStream_t s) {
+            return launch_k(kern, grid, dim3(kThreads), kSmemBytes, s, tm, tm, tm, p);
+        };
+    }
     return BL_OK;
 }
 
+// How many clusters of `splits` CTAs (this kernel's shared memory, one CTA
+// per SM) the B200 runs at once; clusters must sit within one GPC, so this
+// is below 148 / splits. Queried once per split count.
+int max_active_clusters(int splits) {
+    static int cache[kMaxClusterSplits + 1] = {};
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
+    if (splits < 1 || splits > kMaxClusterSplits) return 0;
+    if (cache[splits] == 0) {
+        auto kern = attention_fwd<BL_F32>;
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kSmemBytes)) != cudaSuccess)
+            return 0;
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(1, 1, splits);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = kSmemBytes;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = splits;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+        }
+        cache[splits] = n > 0 ? n : -1;
+    }
+    return cache[splits] > 0 ? cache[splits] : 0;
+}
+
 }  // namespace attn
+
+int attention_auto_splits(const bl_attention_args& a, uint64_t workspace_bytes) {
+    using namespace attn;
+    const Plan p1 = plan(a, 1);
+    if (workspace_bytes > 0) {  // global combine: fill the SMs within the workspace
+        int want = auto_splits(a);
+        while (want > 1 && plan(a, want).bytes > workspace_bytes) --want;
+        return want;
+    }
+    // cluster combine: the most splits whose clusters all run in one wave
+    if (p1.units * 2 > 148) return 1;
+    const int max_s = std::min(kMaxClusterSplits, std::max(1, p1.kv_tiles / 2));
+    for (int s = max_s; s >= 2; --s) {
+        if (p1.units * s > 148) continue;
+        if (static_cast<int>(p1.units) <= max_active_clusters(s)) return s;
+    }
+    return 1;
+}
 
 int prepare_attention(const bl_attention_args& a, Launch* out) {
     return attn::prepare(a, a.workspace, a.workspace_bytes, out);

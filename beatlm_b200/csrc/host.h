@@ -74,6 +74,31 @@ cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
     return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
+// launch_k for a grid of thread-block clusters of `cluster` CTAs.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, dim3 cluster,
+                             size_t smem, cudaStream_t s, Args&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = cluster.x;
+    attr[1].val.clusterDim.y = cluster.y;
+    attr[1].val.clusterDim.z = cluster.z;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
+// Attention's automatic key-split count for these arguments given a
+// workspace of `workspace_bytes` (0 = none: the cluster combine).
+int attention_auto_splits(const bl_attention_args& a, uint64_t workspace_bytes);
+
 inline int enqueue(const Launch& l, cudaStream_t s) {
     cudaError_t e = l.run(s);
     if (e != cudaSuccess) return fail(BL_ERR_CUDA, "launch failed: %s", cudaGetErrorString(e));

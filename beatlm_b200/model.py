@@ -195,10 +195,6 @@ class Buffers:
         self.xn = torch.empty((rows, cfg.dim), dtype=td, device=device)
         self.h = torch.empty((rows, cfg.mlp), dtype=td, device=device)
         self.patches = torch.empty((frames * (t - 1), cfg.k_pad), dtype=td, device=device)
-        # split-key attention workspace, sized for the automatic split count
-        proto = ops.attention_args(self.qkv, tokens=t, heads=cfg.heads, head_dim=cfg.head_dim,
-                                   batch=frames, out=self.o)
-        self.attn_ws = ops.attention_workspace(ops.attention_workspace_bytes(proto), device)
         self.features = ([torch.empty((frames * (t - 1), cfg.dim), dtype=torch.float32,
                                       device=device) for _ in cfg.out_indices]
                          if features else [])
@@ -221,7 +217,7 @@ def block_specs(blk: DeviceBlock, cfg: ViTConfig, buf: Buffers, layer: int = 0,
     name = "block%d." % layer
     attn = Spec(ops.attention_args(buf.qkv, tokens=buf.tokens, heads=cfg.heads,
                                    head_dim=cfg.head_dim, batch=buf.frames, qk_dtype=blk.dtype,
-                                   out=buf.o, workspace=buf.attn_ws), name + "attention", parts)
+                                   out=buf.o), name + "attention", parts)
     proj = Spec(ops.gemm_args(blk.proj_w, a=buf.o, bias=blk.proj_b, chan_scale=blk.ls1,
                               residual=buf.x, out=buf.x), name + "proj", parts)
     fc2 = Spec(ops.gemm_args(blk.fc2_w, a=buf.h, bias=blk.fc2_b, chan_scale=blk.ls2,

@@ -115,10 +115,12 @@ typedef struct bl_attention_args {
     uint32_t kv_splits;      /* 0 = automatic (with a workspace), 1 = none */
     void* workspace;
     uint64_t workspace_bytes;
-    /* Optional per-CTA timeline (NULL = off): CTA b writes four %globaltimer
-     * stamps (ns) at trace[4b..4b+3]: entry, setup done, softmax done, exit.
-     * CTAs are numbered x-fastest over the grid (query groups, heads,
-     * batch x splits); the buffer holds 4 * CTAs uint64 values. */
+    /* Optional per-CTA timeline (NULL = off): CTA b writes %globaltimer
+     * stamps (ns) at trace[8b..8b+7]: entry, setup done, tile 0 softmax done,
+     * tile 1 softmax done, partials stored (cluster combine), cluster barrier
+     * passed, combine done, exit (slots a path does not reach stay as they
+     * were). CTAs are numbered x-fastest over the grid (query groups, heads,
+     * batch x splits); the buffer holds 8 * CTAs uint64 values. */
     uint64_t* trace;
 } bl_attention_args;
 

@@ -135,16 +135,43 @@ def test_row_parts_cover_the_output_and_equal_the_whole():
     t, h = 1370, 6
     qkv = oracle.normal(5, t * 3 * h * 64).reshape(1, t, 3, h, 64)
     dev = bl.pack_qkv(qkv, "f16")
-    whole = bl.attention(dev, tokens=t, heads=h)
-    for parts in (3, 7, 22, 200):
-        bounds = [round(i * t / min(parts, t)) for i in range(min(parts, t) + 1)]
-        out = torch.zeros_like(whole)
-        for r0, r1 in zip(bounds[:-1], bounds[1:]):
-            if r1 > r0:
-                bl.attention(dev, tokens=t, heads=h, out=out, rows=(r0, r1))
-        torch.cuda.synchronize()
-        assert torch.equal(out, whole), parts
+    for splits in (1, 3):  # unsplit, and keys split over a cluster of 3
+        whole = bl.attention(dev, tokens=t, heads=h, kv_splits=splits)
+        for parts in (3, 7, 22, 200):
+            bounds = [round(i * t / min(parts, t)) for i in range(min(parts, t) + 1)]
+            out = torch.zeros_like(whole)
+            for r0, r1 in zip(bounds[:-1], bounds[1:]):
+                if r1 > r0:
+                    bl.attention(dev, tokens=t, heads=h, out=out, rows=(r0, r1),
+                                 kv_splits=splits)
+            torch.cuda.synchronize()
+            assert torch.equal(out, whole), (splits, parts)
     assert bl.status(reset=True).code == 0
+
+
+@pytest.mark.parametrize("splits", [2, 3, 4, 8])
+def test_cluster_combine_equals_the_workspace_combine(splits):
+    """Without a workspace the key splits of a query group form a thread-block
+    cluster and combine in distributed shared memory; with one they combine
+    through it. Same partials, same formula: the results agree, and both meet
+    the oracle."""
+    import torch
+    import beatlm_b200 as bl
+    from beatlm_b200 import ops
+    t, h = 1370, 6
+    qkv = oracle.normal(600 + splits, t * 3 * h * 64).reshape(1, t, 3, h, 64)
+    dev = bl.pack_qkv(qkv, "bf16")
+    clus = bl.attention(dev, tokens=t, heads=h, qk_dtype="bf16", kv_splits=splits)
+    a = ops.attention_args(dev, tokens=t, heads=h, out=clus, qk_dtype="bf16", kv_splits=splits)
+    ws = ops.attention_workspace(ops.attention_workspace_bytes(a))
+    glob = bl.attention(dev, tokens=t, heads=h, qk_dtype="bf16", kv_splits=splits, workspace=ws)
+    torch.cuda.synchronize()
+    assert bl.status(reset=True).code == 0
+    rel, mx = _errors(clus.cpu().numpy(), glob.cpu().numpy())
+    assert rel < 1e-6, rel
+    want = oracle.attention(_rounded(qkv, "bf16")[0].reshape(t, -1), t, h, 64)
+    rel, mx = _errors(clus.cpu().numpy()[0], want)
+    assert rel <= REL_L2
 
 
 def test_hires_rows_sample():
