@@ -175,3 +175,47 @@ SIGNATURES.update({
     "bl_layernorm": (ctypes.c_int, [ctypes.POINTER(LayerNormArgs), ctypes.c_void_p]),
     "bl_patchify": (ctypes.c_int, [ctypes.POINTER(PatchifyArgs), ctypes.c_void_p]),
 })
+
+
+class TensorDesc(ctypes.Structure):
+    _fields_ = [("id", ctypes.c_uint32), ("elem_bytes", ctypes.c_uint32),
+                ("elements", ctypes.c_uint64), ("first_use", ctypes.c_uint32),
+                ("last_use", ctypes.c_uint32)]
+
+
+class DeviceProfile(ctypes.Structure):
+    _fields_ = [("max_binding_bytes", ctypes.c_uint64), ("max_buffer_bytes", ctypes.c_uint64),
+                ("offset_alignment", ctypes.c_uint32)]
+
+
+class PlanErrorInfo(ctypes.Structure):
+    _fields_ = [("kind", ctypes.c_int32), ("id", ctypes.c_uint32), ("a", ctypes.c_uint64),
+                ("b", ctypes.c_uint64)]
+
+
+class Placement(ctypes.Structure):
+    _fields_ = [("arena", ctypes.c_uint32), ("reserved", ctypes.c_uint32),
+                ("offset", ctypes.c_uint64), ("size", ctypes.c_uint64)]
+
+
+_u64 = ctypes.c_uint64
+SIGNATURES.update({
+    "bl_device_profile_webgpu_baseline": (ctypes.c_int, [ctypes.POINTER(DeviceProfile)]),
+    "bl_device_profile_cuda": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(DeviceProfile)]),
+    "bl_plan_create": (ctypes.c_int, [ctypes.POINTER(TensorDesc), _sz,
+                                      ctypes.POINTER(DeviceProfile), ctypes.POINTER(_vp),
+                                      ctypes.POINTER(PlanErrorInfo)]),
+    "bl_plan_destroy": (None, [_vp]),
+    "bl_plan_arenas": (_sz, [_vp, ctypes.POINTER(_u64), _sz]),
+    "bl_plan_placement": (ctypes.c_int, [_vp, ctypes.c_uint32, ctypes.POINTER(Placement)]),
+    "bl_plan_peak_live_bytes": (_u64, [_vp]),
+    "bl_plan_total_bytes": (_u64, [_vp]),
+    "bl_plan_valid_on": (ctypes.c_int, [_vp, ctypes.POINTER(DeviceProfile)]),
+    "bl_arenas_create": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.POINTER(_vp)]),
+    "bl_arenas_destroy": (None, [_vp]),
+    "bl_arenas_bytes": (_u64, [_vp]),
+    "bl_arenas_base": (ctypes.c_int, [_vp, ctypes.c_uint32, ctypes.POINTER(_vp)]),
+    "bl_arenas_binding": (ctypes.c_int, [_vp, ctypes.POINTER(Placement), ctypes.POINTER(_vp)]),
+    "bl_arenas_write": (ctypes.c_int, [_vp, ctypes.POINTER(Placement), _u64, _vp, _u64, _vp]),
+    "bl_arenas_read": (ctypes.c_int, [_vp, ctypes.POINTER(Placement), _u64, _vp, _u64, _vp]),
+})

@@ -1,5 +1,5 @@
 // Thin inline-PTX wrappers for the Blackwell (sm_100a) features the kernels
-// use: mbarriers with bounded waits, TMA tile loads (never multicast), and
+// use: mbarriers with bounded waits, TMA tile loads into the issuing CTA, and
 // the tcgen05 tensor-core / tensor-memory instructions. Written from the PTX
 // ISA; the descriptor bit layouts follow the public CUTLASS sources
 // (cute/arch/mma_sm100_desc.hpp).
@@ -108,7 +108,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
 }
 
 // 3-D tiled bulk tensor load into this CTA's shared memory, completing on
-// mbarrier `bar`. No multicast: every CTA fetches its own tiles.
+// mbarrier `bar`. Every CTA fetches its own tiles.
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int x, int y, int z,
                                             uint32_t bar) {
     asm volatile(

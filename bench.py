@@ -2,19 +2,26 @@
 """Benchmark of the ViT attention hot path on B200 (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload attention]
+                    [--workload encoder|attention|vitl|hires]
 
 Workloads (synthetic data, seeded):
+  encoder    config 3 (default): the DA-V2-Small ViT-S/14 encoder at 518 px,
+             one frame per step through a CUDA graph; frames/s.
   attention  config 1: one ViT-S self-attention op, batch 1, 6 heads x 64,
              1370 tokens, Q/K/V ~ N(0,1), scale 1/8; f16 Q/K/V, f32 output.
+  vitl       config 4: the ViT-L/14 encoder, one independent stream per GPU.
+  hires      config 5: T=5477 attention, 16 heads split over the GPUs, NCCL
+             all-gather of the head outputs; TFLOP/s of the whole op.
 
 A step is one pass of the hot path over one batch. `value` is whole-job
 throughput (all ranks) with the inputs resident in HBM; L2 is flushed (a
-256 MiB write) before every timed launch and the flush is outside the timed
+256 MiB write) before every timed step and the flush is outside the timed
 events. `e2e` is the same metric through the public call with host buffers:
-the H2D copy of the packed Q/K/V from pinned memory and the D2H copy of the
-output are inside its timed region. Multi-GPU: one process per GPU (torchrun),
-replicas only (config 1 does not shard), times are the max over ranks.
+the H2D copy of the step's inputs from pinned memory and the D2H copy of its
+result are inside its timed region. Multi-GPU: one process per GPU
+(torchrun); configs 1-4 run independent replicas or streams (weak scaling),
+config 5 splits one op by heads (strong scaling); times are the max over
+ranks.
 
 `--impl reference` times the reference's CPU path (the C restatement of its
 f64 interpreter, oracle/, all host threads) on the same workload, rank 0 only.
@@ -98,6 +105,10 @@ class AttentionWorkload:
     dtype = "f16 Q/K/V and P; f32 scores, softmax and accumulator"
     data = "synthetic Q/K/V ~ N(0,1), seeded"
     workload_name = "vit_s_attention_op (config 1)"
+    scaling = "weak"
+
+    def parallelism(self, world):
+        return "replicas x%d (no collective)" % world
 
     def roofline(self, stream, avg_ms):
         return {"achieved_tflops": self.flops / (avg_ms / 1e3) / 1e12,
@@ -158,27 +169,31 @@ class AttentionWorkload:
         return self.flops / 1e12  # TFLOP per step
 
     def cpu_baseline(self, threads: int, budget_s: float = 15.0):
-        """The reference's CPU path (oracle/, a C restatement of
-        reference.rs:437-494) on a bounded sample of query rows."""
         import torch
-        import oracle
-        t, h = self.t, self.h
-        qkv = self.host[0].view(torch.float16).float().numpy().reshape(t, -1)
-        rows = 64
-        t0 = time.perf_counter()
+        qkv = self.host[0].view(torch.float16).float().numpy().reshape(self.t, -1)
+        return oracle_attention_rate(qkv, self.t, self.h, threads, budget_s)
+
+
+def oracle_attention_rate(qkv, t, h, threads, budget_s):
+    """The reference's CPU path for one attention op (oracle/, a C restatement
+    of reference.rs:437-494, f64 accumulation) timed on a bounded sample of
+    query rows of every head, in TFLOP/s."""
+    import oracle
+    rows = 16
+    t0 = time.perf_counter()
+    oracle.attention(qkv, t, h, 64, rows=(0, rows), threads=threads)
+    dt = time.perf_counter() - t0
+    rows = int(min(t, max(rows, rows * budget_s / max(dt, 1e-6) / 4)))
+    t0 = time.perf_counter()
+    n = 0
+    while time.perf_counter() - t0 < budget_s / 2 or n == 0:
         oracle.attention(qkv, t, h, 64, rows=(0, rows), threads=threads)
-        dt = time.perf_counter() - t0
-        rows = int(min(t, max(rows, rows * budget_s / max(dt, 1e-6) / 4)))
-        t0 = time.perf_counter()
-        n = 0
-        while time.perf_counter() - t0 < budget_s / 2 or n == 0:
-            oracle.attention(qkv, t, h, 64, rows=(0, rows), threads=threads)
-            n += 1
-        dt = time.perf_counter() - t0
-        flops = 4.0 * rows * t * h * 64 * n
-        return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-                "sample": "%d of %d query rows x %d heads, %d repeats (f64 accumulation, "
-                          "oracle/oracle.c)" % (rows, t, h, n)}
+        n += 1
+    dt = time.perf_counter() - t0
+    flops = 4.0 * rows * t * h * 64 * n
+    return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": "%d of %d query rows x %d heads, %d repeats (f64 accumulation, "
+                      "oracle/oracle.c)" % (rows, t, h, n)}
 
 
 class EncoderWorkload:
@@ -205,27 +220,36 @@ class EncoderWorkload:
                        "(non-graph) encodes after the timed region",
                 "kernels": {k: round(v[1] / steps, 2) for k, v in sorted(prof.items())}}
 
+    large = False
+
     @classmethod
     def reference_step(cls, threads):
-        """One encoder block of the oracle per step (a twelfth of a frame; the
+        """One encoder block of the oracle per step (1/layers of a frame; the
         patch embedding, under 1 % of a frame's arithmetic, is left out)."""
         import numpy as np
         import oracle
         from beatlm_b200.model import ViTConfig, block_weights_normal
-        c = ViTConfig.small()
+        c = ViTConfig.large() if cls.large else ViTConfig.small()
         rng = np.random.default_rng(5)
         w = block_weights_normal(rng, c.dim, c.mlp)
         x = rng.standard_normal(c.tokens * c.dim, dtype=np.float32)
         fn = lambda: oracle.vit_block(x, w, c.tokens, c.heads, c.head_dim, c.mlp, c.eps,
                                       threads=threads)
-        return fn, 1.0 / c.layers, ("one ViT-S block (T=1370) per step = 1/12 frame, "
-                                    "f64 oracle, patch embedding excluded")
+        return fn, 1.0 / c.layers, ("one %s block (T=%d) per step = 1/%d frame, f64 oracle, "
+                                    "patch embedding excluded"
+                                    % ("ViT-L" if cls.large else "ViT-S", c.tokens, c.layers))
 
-    def __init__(self, rank: int, frames: int = 1, large: bool = False):
+    scaling = "weak"
+
+    def parallelism(self, world):
+        return ("%d independent streams, one per GPU, no collective" % world if world > 1
+                else "1 stream")
+
+    def __init__(self, rank: int, frames: int = 1):
         import numpy as np
         import torch
         from beatlm_b200.model import Encoder, ViTConfig, block_weights_normal
-        self.cfg = ViTConfig.large() if large else ViTConfig.small()
+        self.cfg = ViTConfig.large() if self.large else ViTConfig.small()
         cfg = self.cfg
         rng = np.random.default_rng(99 + rank)
         n = lambda *s: rng.standard_normal(int(np.prod(s)), dtype=np.float32) * 0.02
@@ -323,7 +347,114 @@ class EncoderWorkload:
                           "%d threads" % (t_block, c.layers, t_embed, threads)}
 
 
-WORKLOADS = {"attention": AttentionWorkload, "encoder": EncoderWorkload}
+class VitLWorkload(EncoderWorkload):
+    """Config 4: a ViT-L/14-shaped encoder (24 blocks, dim 1024, 16 heads,
+    MLP 4096, 1370 tokens), bf16, random N(0, 0.02) weights. Eight
+    independent input streams shard one per GPU with no collective: each rank
+    runs its own stream, one frame per step."""
+
+    name = "vitl"
+    large = True
+    workload_name = "vit_l14_encoder (config 4)"
+    data = "synthetic: ImageNet-normalised U[0,1] 518x518x3 image per stream, N(0,0.02) weights"
+
+
+class HiresWorkload:
+    """Config 5: the high-resolution ViT-L attention, T = 74*74 + 1 = 5477,
+    16 heads x 64, bf16 Q/K (V f16), Q/K/V ~ N(0,1), batch 1. With g ranks
+    each holds 16/g heads (made locally from the seed), computes their
+    output slab and an NCCL all-gather assembles [T][1024] on every rank. A
+    step is the whole op: the attention launch, the all-gather and the
+    permute to heads side by side."""
+
+    name = "hires"
+    unit = "TFLOP/s"
+    dtype = "bf16 Q/K, f16 V and P; f32 scores, softmax and accumulator; f16 output"
+    data = "synthetic Q/K/V ~ N(0,1), seeded, each rank makes its own heads"
+    workload_name = "hires_vit_l_attention_T5477 (config 5)"
+    scaling = "strong"
+    T, H = 5477, 16
+
+    def parallelism(self, world):
+        return ("heads/%d per GPU + NCCL all-gather of head outputs" % world if world > 1
+                else "1 GPU, all heads")
+
+    @classmethod
+    def _qkv(cls, h0, h1):
+        import numpy as np
+        rng = np.random.default_rng(4321)
+        full = rng.standard_normal((1, cls.T, 3, cls.H, 64), dtype=np.float32)
+        return np.ascontiguousarray(full[:, :, :, h0:h1])
+
+    @classmethod
+    def reference_step(cls, threads):
+        import oracle
+        t, h = cls.T, cls.H
+        qkv = oracle.round_f16(cls._qkv(0, h)[0].reshape(t, -1))
+        rows = 8
+        t0 = time.perf_counter()
+        oracle.attention(qkv, t, h, 64, rows=(0, rows), threads=threads)
+        per_row = (time.perf_counter() - t0) / rows
+        rows = int(max(8, min(t, 2.0 / max(per_row, 1e-9))))
+        fn = lambda: oracle.attention(qkv, t, h, 64, rows=(0, rows), threads=threads)
+        return fn, 4.0 * rows * t * h * 64 / 1e12, (
+            "%d of %d query rows x %d heads per step (oracle/oracle.c, f64)" % (rows, t, h))
+
+    def __init__(self, rank: int, world: int = 1):
+        import torch
+        import beatlm_b200 as bl
+        from beatlm_b200.parallel import HeadParallelAttention
+        self.world = world
+        self.op = HeadParallelAttention(self.T, self.H, rank, world, out_dtype="f16")
+        qkv = self._qkv(self.op.h0, self.op.h1)
+        self.dev = bl.pack_qkv(qkv, "bf16")
+        self.host = self.dev.cpu().pin_memory()
+        self.out_host = torch.empty(self.op.out.shape, dtype=self.op.out.dtype).pin_memory()
+        self.launches_per_step = 1
+
+    def config(self):
+        return {"workload": self.workload_name, "batch": 1, "tokens": self.T, "heads": self.H,
+                "head_dim": 64, "heads_per_gpu": self.op.local_heads,
+                "qkv_dtype": "bf16 Q/K, f16 V", "out_dtype": "f16",
+                "collective": "all_gather_into_tensor (NCCL) + permute" if self.world > 1
+                              else "none",
+                "l2": "flushed before every timed step (256 MiB write)"}
+
+    def step(self, stream):
+        self.op(self.dev, stream=stream)
+
+    def step_e2e(self, stream):
+        self.dev.copy_(self.host, non_blocking=True)
+        self.step(stream)
+        self.out_host.copy_(self.op.out, non_blocking=True)
+
+    def e2e_bytes(self):
+        return self.host.numel() * 2, self.out_host.numel() * 2
+
+    def units(self):
+        return self.op.flops() / self.world / 1e12  # this rank's share, TFLOP per step
+
+    def roofline(self, stream, avg_ms, reps: int = 10):
+        """This rank's attention launch alone, CUDA events on its stream."""
+        import torch
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+        ms = time_device(lambda s: self.op.compute(self.dev, stream=s), reps, 3, stream, flush)
+        avg = sum(ms) / len(ms)
+        return {"achieved_tflops": self.op.flops() / self.world / (avg / 1e3) / 1e12,
+                "kernel": "bl::attn::attention_fwd (%d heads of %d on this GPU)"
+                          % (self.op.local_heads, self.H),
+                "how": "CUDA events around %d attention-only launches after the timed region, "
+                       "L2 flushed between them" % reps,
+                "attention_ms": round(avg, 5)}
+
+    def cpu_baseline(self, threads: int, budget_s: float = 15.0):
+        import oracle
+        qkv = oracle.round_f16(self._qkv(0, self.H)[0].reshape(self.T, -1))
+        return oracle_attention_rate(qkv, self.T, self.H, threads, budget_s)
+
+
+WORKLOADS = {"attention": AttentionWorkload, "encoder": EncoderWorkload,
+             "vitl": VitLWorkload, "hires": HiresWorkload}
 
 
 # ------------------------------------------------------------------ timing
@@ -373,7 +504,8 @@ def main():
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
-    wl = WORKLOADS[args.workload](rank)
+    cls = WORKLOADS[args.workload]
+    wl = cls(rank, world=world) if cls is HiresWorkload else cls(rank)
     stream = torch.cuda.Stream()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
 
@@ -409,9 +541,9 @@ def main():
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": wl.unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(avg_ms, 5),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None,
             "dtype": wl.dtype, "data": wl.data,
-            "config": dict(wl.config(), parallelism="replicas x%d (no collective)" % world),
+            "config": dict(wl.config(), parallelism=wl.parallelism(world)),
             "e2e": {"value": round(e2e_value, 3), "unit": wl.unit,
                     "h2d_bytes_per_step": wl.e2e_bytes()[0],
                     "d2h_bytes_per_step": wl.e2e_bytes()[1]},
@@ -450,7 +582,7 @@ def run_reference(args, world, rank):
     value = units_per_step * args.steps / dt
     line = {"metric": METRIC, "impl": "reference", "value": value, "unit": wl.unit,
             "n_gpus": world, "steps": args.steps, "warmup": 1,
-            "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": wl.scaling,
             "vs_baseline": None, "dtype": "f64 accumulate, f32 storage",
             "data": "synthetic, seeded", "config": {"workload": wl.workload_name},
             "cpu_baseline": {"value": value, "unit": wl.unit, "cores": threads, "kind": "port",

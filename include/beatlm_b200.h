@@ -87,14 +87,16 @@ typedef enum bl_dtype { BL_F32 = 0, BL_F16 = 1, BL_BF16 = 2 } bl_dtype;
  * 8 elements (16 bytes). Enqueues on `stream`; allocates nothing.
  *
  * Key splits: when the query tiles alone would leave SMs idle (ViT-S at one
- * frame: 36 CTAs for 148 SMs), the keys are split across CTAs whose partial
- * results are combined by the last CTA of each group. That needs a
- * caller-owned device workspace of bl_attention_workspace_bytes() bytes,
- * 256-byte aligned, zero-filled once before its first use (every call leaves
- * its counters at zero again; calls that overlap on the GPU must not share
- * one). kv_splits = 0 picks the split count when a workspace is given and
- * uses 1 (no workspace) otherwise; 1 never splits; larger counts need the
- * workspace (BL_ERR_CAPACITY otherwise).
+ * frame: 36 CTAs for 148 SMs), the keys are split across CTAs and their
+ * partial results combined. kv_splits = 0 picks the split count, 1 never
+ * splits. Without a workspace the CTAs of one query group form a
+ * thread-block cluster (at most 8 splits) and combine in distributed shared
+ * memory. With a workspace the partials go through it and the last CTA of
+ * each group combines them: a caller-owned device buffer of
+ * bl_attention_workspace_bytes() bytes, 256-byte aligned, zero-filled once
+ * before its first use (every call leaves its counters at zero again; calls
+ * that overlap on the GPU must not share one); too small a workspace is
+ * BL_ERR_CAPACITY. Both combines give the same result.
  */
 typedef struct bl_attention_args {
     uint32_t batch;
@@ -112,7 +114,7 @@ typedef struct bl_attention_args {
     void* out;
     uint64_t out_row_stride; /* 0 = heads * head_dim */
     uint32_t out_head_base;
-    uint32_t kv_splits;      /* 0 = automatic (with a workspace), 1 = none */
+    uint32_t kv_splits;      /* 0 = automatic, 1 = none */
     void* workspace;
     uint64_t workspace_bytes;
     /* Optional per-CTA timeline (NULL = off): CTA b writes %globaltimer
@@ -380,6 +382,127 @@ typedef struct bl_timer_stats {
     uint64_t frames_failed;
 } bl_timer_stats;
 int bl_timer_get_stats(const bl_timer* t, bl_timer_stats* out);
+
+/* ------------------------------------------------------------ memory plan */
+
+/*
+ * The static memory plan (MemoryPlan, crates/beatlm-core/src/memory.rs:285-375)
+ * and its realisation as ONE device allocation (Arenas,
+ * crates/beatlm/src/gpu/arenas.rs:65-140, which makes one buffer per arena;
+ * here the arenas are consecutive 256-byte-aligned ranges of a single
+ * cudaMalloc). Planning is host-only work and needs no GPU.
+ *
+ * The plan keeps the reference's five rules: tensors whose use ranges
+ * intersect (inclusive at both ends) never share a byte of one arena;
+ * offsets are multiples of the profile's alignment and sizes are the byte
+ * size rounded up to 4; no arena exceeds the profile's arena cap, and a
+ * larger tensor is an error, never split; the same set of tensors gives the
+ * same plan whatever order they are listed in; malformed input is an error.
+ * Algorithm: greedy by rounded size, descending, ties by id; each tensor goes
+ * to the lowest aligned offset of the first arena where it fits beside the
+ * already placed tensors whose lifetimes intersect its own; a new arena
+ * opens when none fits.
+ */
+
+/* TensorDesc (memory.rs:158-170). elem_bytes is DType::size_bytes: 4 for
+ * f32, 2 for f16 and bf16 (any non-zero width is accepted). */
+typedef struct bl_tensor_desc {
+    uint32_t id;
+    uint32_t elem_bytes;
+    uint64_t elements;   /* at least 1 */
+    uint32_t first_use;  /* operation index in program order */
+    uint32_t last_use;   /* not before first_use */
+} bl_tensor_desc;
+
+/* The profile fields the planner reads (DeviceProfile, crates/beatlm-core/
+ * src/device.rs:97-125): the arena cap is min(max_binding_bytes,
+ * max_buffer_bytes). */
+typedef struct bl_device_profile {
+    uint64_t max_binding_bytes;
+    uint64_t max_buffer_bytes;
+    uint32_t offset_alignment;
+} bl_device_profile;
+
+/* DeviceProfile::webgpu_baseline (device.rs:97): 128 MiB binding, 256 MiB
+ * buffer, 256-byte alignment. */
+int bl_device_profile_webgpu_baseline(bl_device_profile* out);
+/* The profile of CUDA device `device`: 256-byte alignment and an arena cap
+ * of the device's total memory (a kernel addresses any byte of one
+ * allocation). Needs the device; allocates nothing. */
+int bl_device_profile_cuda(int device, bl_device_profile* out);
+
+/* PlanError (memory.rs:220-265). On failure bl_plan_create fills a
+ * bl_plan_error: `id` the tensor, and a/b = first_use/last_use for
+ * INVALID_LIFETIME or size/limit for TENSOR_TOO_LARGE. */
+enum {
+    BL_PLAN_DUPLICATE_TENSOR = 1,
+    BL_PLAN_INVALID_LIFETIME = 2,
+    BL_PLAN_EMPTY_TENSOR = 3,
+    BL_PLAN_SIZE_OVERFLOW = 4,
+    BL_PLAN_TENSOR_TOO_LARGE = 5,
+    BL_PLAN_INVALID_PROFILE = 6,
+    BL_PLAN_TOO_MANY_TENSORS = 7
+};
+typedef struct bl_plan_error {
+    int32_t kind; /* 0 = none, else BL_PLAN_* */
+    uint32_t id;
+    uint64_t a;
+    uint64_t b;
+} bl_plan_error;
+
+/* Placement (memory.rs:200-218). */
+typedef struct bl_placement {
+    uint32_t arena;
+    uint32_t reserved;
+    uint64_t offset;
+    uint64_t size;
+} bl_placement;
+
+typedef struct bl_plan bl_plan;
+
+/* MemoryPlan::new (memory.rs:285). Returns BL_OK, or BL_ERR_INVALID /
+ * BL_ERR_CAPACITY (TENSOR_TOO_LARGE) with *err filled when err != NULL. */
+int bl_plan_create(const bl_tensor_desc* tensors, size_t n, const bl_device_profile* profile,
+                   bl_plan** out, bl_plan_error* err);
+void bl_plan_destroy(bl_plan* p);
+/* MemoryPlan::arenas (memory.rs:379): arena sizes, each the end of the last
+ * byte used in it. Writes min(count, cap) sizes; returns the count. */
+size_t bl_plan_arenas(const bl_plan* p, uint64_t* sizes, size_t cap);
+/* MemoryPlan::placement (memory.rs:385): BL_OK, or BL_ERR_INVALID for a
+ * tensor the plan was not made with. */
+int bl_plan_placement(const bl_plan* p, uint32_t id, bl_placement* out);
+/* MemoryPlan::peak_live_bytes / total_bytes (memory.rs:403-414). */
+uint64_t bl_plan_peak_live_bytes(const bl_plan* p);
+uint64_t bl_plan_total_bytes(const bl_plan* p);
+/* MemoryPlan::valid_on (memory.rs:423): 1 when every arena fits the
+ * profile's cap and the plan's alignment is a multiple of the profile's. */
+int bl_plan_valid_on(const bl_plan* p, const bl_device_profile* profile);
+
+typedef struct bl_arenas bl_arenas;
+
+/* Arenas::new (arenas.rs:88): ONE cudaMalloc on `device` holding every
+ * arena of the plan, arena i at a 256-byte-aligned base. BL_ERR_INVALID when
+ * the plan is not valid on the device's profile (ArenaError::
+ * PlanNotValidOnDevice). The only allocation a plan needs: nothing in the
+ * steady state allocates. */
+int bl_arenas_create(const bl_plan* p, int device, bl_arenas** out);
+void bl_arenas_destroy(bl_arenas* a);
+/* Bytes of the single allocation. */
+uint64_t bl_arenas_bytes(const bl_arenas* a);
+/* Arenas::buffer (arenas.rs:117): the device address of arena `arena`. */
+int bl_arenas_base(const bl_arenas* a, uint32_t arena, void** out);
+/* Arenas::binding (arenas.rs:131): the device address of a placement,
+ * after the reference's checks (unknown arena, out of range or empty,
+ * misaligned offset), each BL_ERR_INVALID with its reason in the message. */
+int bl_arenas_binding(const bl_arenas* a, const bl_placement* p, void** out);
+/* Host writes of weights and inputs into a placement, and reads of results
+ * (the reference's queue.write_buffer and copy-out). `offset` is relative to
+ * the placement and offset + bytes must lie inside it. Enqueued on `stream`;
+ * pinned host memory makes them asynchronous. */
+int bl_arenas_write(const bl_arenas* a, const bl_placement* p, uint64_t offset,
+                    const void* src, uint64_t bytes, void* stream);
+int bl_arenas_read(const bl_arenas* a, const bl_placement* p, uint64_t offset, void* dst,
+                   uint64_t bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -117,3 +117,26 @@ def test_encoder_features_match_the_reference_chain(dtype):
             print("encoder %s frame %d feature %d: rel-L2 %.3e max-abs %.3e" % (
                 dtype, f, i, rel, mx))
             assert rel <= REL[dtype]
+
+
+def test_vit_l_block_matches_the_reference_block():
+    """Config-4 block shape: D=1024, 16 heads, MLP 4096, T=1370, bf16, weights
+    N(0, 0.02) with gamma 1 / beta 0 / LayerScale 1, input N(0, 1)."""
+    import torch
+    import beatlm_b200 as bl
+    from beatlm_b200.model import Buffers, DeviceBlock, ViTConfig, block_weights_normal, run_block
+    cfg = ViTConfig.large()
+    rng = np.random.default_rng(24)
+    w = block_weights_normal(rng, cfg.dim, cfg.mlp)
+    x = rng.standard_normal(cfg.tokens * cfg.dim, dtype=np.float32)
+    blk = DeviceBlock(w, cfg.dim, cfg.mlp, "bf16")
+    buf = Buffers(cfg, 1, "bf16", features=False)
+    buf.x.copy_(torch.from_numpy(x.reshape(cfg.tokens, cfg.dim)))
+    run_block(blk, cfg, buf)
+    torch.cuda.synchronize()
+    assert bl.status(reset=True).code == 0
+    want = oracle.vit_block(x, DeviceBlock.rounded(w, "bf16"), cfg.tokens, cfg.heads, 64,
+                            cfg.mlp, cfg.eps, qkv_round="qk_bf16")
+    rel, mx = _rel(buf.x.cpu().numpy(), want)
+    print("ViT-L block bf16: rel-L2 %.3e max-abs %.3e" % (rel, mx))
+    assert rel <= REL["bf16"]
