@@ -219,3 +219,4 @@ SIGNATURES.update({
     "bl_arenas_write": (ctypes.c_int, [_vp, ctypes.POINTER(Placement), _u64, _vp, _u64, _vp]),
     "bl_arenas_read": (ctypes.c_int, [_vp, ctypes.POINTER(Placement), _u64, _vp, _u64, _vp]),
 })
+SIGNATURES["bl_stream_hold"] = (ctypes.c_int, [_vp, ctypes.c_uint32])

@@ -128,3 +128,26 @@ extern "C" int bl_status(bl_status_t* out, int reset) {
     if (reset) BL_CUDA_TRY(cudaMemset(p, 0, sizeof s));
     return BL_OK;
 }
+
+namespace bl {
+// One warp that waits `ns` nanoseconds of %globaltimer time and exits. The
+// loop ends by construction (the wait is bounded by the argument, at most
+// one second, checked on the host).
+__global__ void hold_kernel(uint64_t ns) {
+    uint64_t t0, t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    do {
+        __nanosleep(2000);
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    } while (t - t0 < ns);
+}
+}  // namespace bl
+
+extern "C" int bl_stream_hold(void* stream, uint32_t microseconds) {
+    if (microseconds > 1000000)
+        return bl::fail(BL_ERR_INVALID, "stream hold: %u us (max 1 s)", microseconds);
+    bl::hold_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(1000ull * microseconds);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return bl::fail(BL_ERR_CUDA, "stream hold: %s", cudaGetErrorString(e));
+    return BL_OK;
+}

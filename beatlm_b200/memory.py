@@ -162,9 +162,6 @@ class _CudaView:
         self.device = device
 
 
-_TYPESTR = {F32: "<f4", F16: "<f2", "u8": "|u1", "i16": "<i2", "i32": "<i4"}
-
-
 class Arenas:
     """Arenas::new (arenas.rs:88) as ONE device allocation holding every arena
     of `plan`. Placements are bound by device address; nothing else is ever
@@ -195,18 +192,25 @@ class Arenas:
         N.check(N.lib().bl_arenas_binding(self._h, ctypes.byref(p._c()), ctypes.byref(out)))
         return int(out.value or 0)
 
-    def tensor(self, p: Placement, shape, dtype: str):
-        """A torch view of placement `p` (no copy). `dtype` is f32, f16, u8,
-        i16 or i32; bf16 data lives in an i16 view (torch reads bf16 from
-        __cuda_array_interface__ only through int16)."""
+    def tensor(self, p: Placement, shape, dtype):
+        """A torch view of placement `p` (no copy), valid while this object
+        lives. `dtype` is a torch dtype or one of f32, f16, u8, i16, i32
+        (bf16 goes through an int16 carrier: __cuda_array_interface__ has no
+        bf16 type)."""
         import math
         import torch
-        width = {F32: 4, F16: 2, "u8": 1, "i16": 2, "i32": 4}[dtype]
+        names = {F32: torch.float32, F16: torch.float16, "u8": torch.uint8, "i16": torch.int16,
+                 "i32": torch.int32}
+        dt = names.get(dtype, dtype)
+        carrier = {torch.float32: "<f4", torch.float16: "<f2", torch.bfloat16: "<i2",
+                   torch.uint8: "|u1", torch.int16: "<i2", torch.int32: "<i4"}[dt]
+        width = torch.empty((), dtype=dt).element_size()
         if math.prod(shape) * width > p.size:
             raise ValueError("a %s view of %s needs %d bytes, the placement has %d"
-                             % (dtype, tuple(shape), math.prod(shape) * width, p.size))
-        view = _CudaView(self.binding(p), shape, _TYPESTR[dtype], self.device)
-        return torch.as_tensor(view, device="cuda:%d" % self.device)
+                             % (dt, tuple(shape), math.prod(shape) * width, p.size))
+        view = _CudaView(self.binding(p), tuple(shape), carrier, self.device)
+        t = torch.as_tensor(view, device="cuda:%d" % self.device)
+        return t.view(dt) if dt == torch.bfloat16 else t
 
     def write(self, p: Placement, host, offset: int = 0, stream=None):
         """Host -> placement bytes (weights and inputs); `host` is a

@@ -181,23 +181,41 @@ class Buffers:
     prebuilt program reads, so a caller writes each frame's pixels there."""
 
     def __init__(self, cfg: ViTConfig, frames: int, dtype: str, tokens: int | None = None,
-                 device="cuda", features: bool = True):
+                 device="cuda", features: bool = True, alloc=None):
+        """``alloc(name, shape, torch_dtype)`` makes each buffer (default: a
+        torch allocation on `device`); the static plan passes views of its
+        arena instead."""
         import torch
+        if alloc is None:
+            alloc = lambda name, shape, dt: torch.empty(shape, dtype=dt, device=device)
         td = torch.bfloat16 if dtype == "bf16" else torch.float16
         t = cfg.tokens if tokens is None else tokens
         rows = frames * t
         self.frames, self.tokens, self.rows = frames, t, rows
-        self.image = torch.zeros((frames, cfg.side, cfg.side, cfg.cin), dtype=torch.float32,
-                                 device=device)
-        self.x = torch.empty((rows, cfg.dim), dtype=torch.float32, device=device)
-        self.qkv = torch.empty((rows, 3 * cfg.dim), dtype=torch.int16, device=device)
-        self.o = torch.empty((rows, cfg.dim), dtype=td, device=device)
-        self.xn = torch.empty((rows, cfg.dim), dtype=td, device=device)
-        self.h = torch.empty((rows, cfg.mlp), dtype=td, device=device)
-        self.patches = torch.empty((frames * (t - 1), cfg.k_pad), dtype=td, device=device)
-        self.features = ([torch.empty((frames * (t - 1), cfg.dim), dtype=torch.float32,
-                                      device=device) for _ in cfg.out_indices]
-                         if features else [])
+        self.image = alloc("image", (frames, cfg.side, cfg.side, cfg.cin), torch.float32)
+        self.image.zero_()
+        self.x = alloc("x", (rows, cfg.dim), torch.float32)
+        self.qkv = alloc("qkv", (rows, 3 * cfg.dim), torch.int16)
+        self.o = alloc("o", (rows, cfg.dim), td)
+        self.xn = alloc("xn", (rows, cfg.dim), td)
+        self.h = alloc("h", (rows, cfg.mlp), td)
+        self.patches = alloc("patches", (frames * (t - 1), cfg.k_pad), td)
+        self.features = ([alloc("features.%d" % i, (frames * (t - 1), cfg.dim), torch.float32)
+                          for i in cfg.out_indices] if features else [])
+
+    # Lifetimes for the static plan, in kernel-spec order of the encoder
+    # program (spec 0 patchify, spec 1 patch GEMM, blocks from spec 2). The
+    # image is refilled by the host every frame and the features are read
+    # after it, so both live for the whole program, as do the weights and
+    # the residual stream; the patch matrix dies at the patch GEMM and the
+    # block scratch is born at the first block, so those may share bytes.
+    @staticmethod
+    def lifetime(name: str, last: int) -> tuple[int, int]:
+        if name == "patches":
+            return 0, 1
+        if name in ("qkv", "o", "xn", "h"):
+            return 2, last
+        return 0, last
 
 
 def block_specs(blk: DeviceBlock, cfg: ViTConfig, buf: Buffers, layer: int = 0,
@@ -258,27 +276,114 @@ def run_block(blk: DeviceBlock, cfg: ViTConfig, buf: Buffers, stream=None, parts
 class Encoder:
     """The DA-V2 ViT encoder (depth_anything_v2.rs:435-545) on the device."""
 
-    def __init__(self, cfg: ViTConfig, weights: dict, dtype: str = "bf16", device="cuda"):
+    def __init__(self, cfg: ViTConfig, weights: dict, dtype: str = "bf16", device="cuda",
+                 planned_frames: int | None = None):
         """``weights``: ``blocks`` (list of per-block dicts in the reference
         layout), ``patch_w`` [patch][patch][cin][dim] (HWIO), ``patch_b`` [dim],
-        ``cls`` [dim], ``pos`` [tokens][dim], ``norm_g``/``norm_b`` [dim]."""
+        ``cls`` [dim], ``pos`` [tokens][dim], ``norm_g``/``norm_b`` [dim].
+
+        ``planned_frames``: place every weight and every activation buffer of
+        the ``planned_frames``-frame program in ONE device allocation laid out
+        by the static memory plan (memory.MemoryPlan, then memory.Arenas;
+        the reference's MemoryPlan::new and Arenas::new). The weights are
+        staged on the host and written into their placements; afterwards
+        nothing is allocated. Without it each buffer is its own torch
+        allocation."""
         import torch
         td = torch.bfloat16 if dtype == "bf16" else torch.float16
         self.cfg, self.dtype = cfg, dtype
-        self.blocks = [DeviceBlock(w, cfg.dim, cfg.mlp, dtype, device) for w in weights["blocks"]]
+        self.arena, self.plan = None, None
+        stage = "cpu" if planned_frames is not None else device
+        self.blocks = [DeviceBlock(w, cfg.dim, cfg.mlp, dtype, stage) for w in weights["blocks"]]
         pw = np.zeros((cfg.dim, cfg.k_pad), np.float32)
         pw[:, :cfg.taps] = np.asarray(weights["patch_w"], np.float32).reshape(cfg.taps, cfg.dim).T
-        f32 = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(device)
-        self.patch_w = torch.from_numpy(pw).to(td).to(device)
+        f32 = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(stage)
+        self.patch_w = torch.from_numpy(pw).to(td).to(stage)
         self.patch_b = f32(weights["patch_b"])
         self.cls = f32(weights["cls"])
         self.pos = f32(np.asarray(weights["pos"], np.float32).reshape(cfg.tokens, cfg.dim))
         self.norm = (f32(weights["norm_g"]), f32(weights["norm_b"]))
         self._buffers = {}
         self._programs = {}
+        if planned_frames is not None:
+            self._place_in_arena(planned_frames, torch.device(device))
+
+    def _weights(self):
+        """(owner, attribute, index or None) of every weight tensor."""
+        out = []
+        for owner in [self] + self.blocks:
+            for attr, v in sorted(vars(owner).items()):
+                if attr.startswith("_") or attr in ("blocks", "cfg"):
+                    continue
+                if hasattr(v, "data_ptr"):
+                    out.append((owner, attr, None))
+                elif isinstance(v, tuple) and v and all(hasattr(x, "data_ptr") for x in v):
+                    out += [(owner, attr, i) for i in range(len(v))]
+        return out
+
+    def memory_plan(self, frames: int, profile):
+        """The static plan of every weight and activation buffer of the
+        `frames`-frame program against `profile` (host-only). Tensor ids:
+        the weights first, in ``_weights()`` order, then the activation
+        buffers in the order Buffers makes them. Returns (plan, weights,
+        activations as (name, shape, torch dtype))."""
+        import torch
+        from .memory import F16, F32, MemoryPlan, TensorDesc
+        last = len(self.specs_layout(frames)) - 1
+        acts = []
+        Buffers(self.cfg, frames, self.dtype, device="meta",
+                alloc=lambda n, s, dt: acts.append((n, s, dt)) or torch.empty(s, dtype=dt,
+                                                                              device="meta"))
+        wts = self._weights()
+        descs = []
+        for k, (o, a, i) in enumerate(wts):
+            t = getattr(o, a) if i is None else getattr(o, a)[i]
+            descs.append(TensorDesc(k, F32 if t.element_size() == 4 else F16, t.numel(), 0, last))
+        for k, (name, shape, dt) in enumerate(acts, start=len(wts)):
+            first, end = Buffers.lifetime(name.split(".")[0], last)
+            descs.append(TensorDesc(k, F32 if torch.empty((), dtype=dt).element_size() == 4
+                                    else F16, int(np.prod(shape)), first, end))
+        return MemoryPlan(descs, profile), wts, acts
+
+    def _place_in_arena(self, frames: int, device):
+        import torch
+        from .memory import Arenas, DeviceProfile
+        cfg = self.cfg
+        self.plan, wts, acts = self.memory_plan(frames, DeviceProfile.cuda(device.index or 0))
+        self.arena = Arenas(self.plan, device.index or 0)
+        get = lambda o, a, i: getattr(o, a) if i is None else getattr(o, a)[i]
+        for k, (o, a, i) in enumerate(wts):
+            src = get(o, a, i)
+            view = self.arena.tensor(self.plan.placement(k), tuple(src.shape), src.dtype)
+            view.copy_(src)
+            if i is None:
+                setattr(o, a, view)
+            else:
+                tup = list(getattr(o, a))
+                tup[i] = view
+                setattr(o, a, tuple(tup))
+        views = {name: self.arena.tensor(self.plan.placement(k), shape, dt)
+                 for k, (name, shape, dt) in enumerate(acts, start=len(wts))}
+        self._buffers[frames] = Buffers(cfg, frames, self.dtype,
+                                        alloc=lambda n, s, dt: views[n])
+        torch.cuda.synchronize(device)
+
+    def specs_layout(self, frames: int) -> list:
+        """The spec labels of the encoder program, in order (no device work)."""
+        cfg = self.cfg
+        out = ["embed.patchify", "embed.patch"]
+        for i in range(cfg.layers):
+            out += ["block%d.%s" % (i, k) for k in
+                    ("norm1", "qkv", "attention", "proj", "norm2", "fc1", "fc2")]
+            if (i + 1) in cfg.out_indices:
+                out.append("features.%d" % (i + 1))
+        return out
 
     def buffers(self, frames: int) -> Buffers:
         if frames not in self._buffers:
+            if self.arena is not None:
+                raise ValueError("this encoder's memory is planned for %s frames"
+                                 % sorted(self._buffers))
             self._buffers[frames] = Buffers(self.cfg, frames, self.dtype)
         return self._buffers[frames]
 

@@ -18,6 +18,12 @@ _OP_OF = {N.AttentionArgs: OP_ATTENTION, N.GemmArgs: OP_GEMM,
           N.LayerNormArgs: OP_LAYERNORM, N.PatchifyArgs: OP_PATCHIFY}
 
 
+def hold(stream, microseconds: int):
+    """Holds `stream` for `microseconds` of device time (bl_stream_hold), so
+    that what is enqueued behind it starts back to back on the GPU."""
+    N.check(N.lib().bl_stream_hold(_stream_ptr(stream), microseconds))
+
+
 @dataclasses.dataclass
 class Spec:
     """One kernel of a program: its packed arguments, a label, its parts."""

@@ -383,6 +383,14 @@ typedef struct bl_timer_stats {
 } bl_timer_stats;
 int bl_timer_get_stats(const bl_timer* t, bl_timer_stats* out);
 
+/* Holds `stream` for `microseconds` of device time (at most 1 s) with one
+ * single-warp kernel, so that work the host enqueues behind it meanwhile
+ * starts back to back. Event pairs around each launch then time the kernels,
+ * not the host's launch rate. A measurement aid with no counterpart in the
+ * reference, whose timestamp queries are written inside the passes
+ * (timer.rs:208). */
+int bl_stream_hold(void* stream, uint32_t microseconds);
+
 /* ------------------------------------------------------------ memory plan */
 
 /*

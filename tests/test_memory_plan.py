@@ -263,3 +263,33 @@ def test_the_oracle_pins_the_reference_known_answers():
     assert orc.plan([(0, 4, 256, 0, 0), (1, 4, 257, 0, 0)], (1024, 256 << 20, 256)) == (
         "TensorTooLarge", 1, 1028, 1024)
     assert orc.plan([(0, 4, 100, 0, 2), (1, 4, 50, 1, 1), (2, 4, 25, 3, 3)], b)[2] == 600
+
+
+def test_the_encoder_plan_keeps_the_rules_and_reuses_the_patch_matrix():
+    """The ViT-S encoder's weights and activation buffers planned against a
+    B200-like profile (one arena up to the device's memory): one arena, and
+    the patch matrix, dead after the patch GEMM, shares bytes with the block
+    scratch born after it."""
+    import numpy as np
+    from beatlm_b200.model import Encoder, ViTConfig, block_weights_normal
+    cfg = ViTConfig.small(layers=2, out_indices=(1, 2))
+    rng = np.random.default_rng(3)
+    n = lambda *s: rng.standard_normal(int(np.prod(s)), dtype=np.float32) * 0.02
+    w = {"blocks": [block_weights_normal(rng, cfg.dim, cfg.mlp) for _ in range(cfg.layers)],
+         "patch_w": n(cfg.patch, cfg.patch, cfg.cin, cfg.dim), "patch_b": n(cfg.dim),
+         "cls": n(cfg.dim), "pos": n(cfg.tokens, cfg.dim),
+         "norm_g": np.ones(cfg.dim, np.float32), "norm_b": np.zeros(cfg.dim, np.float32)}
+    enc = Encoder(cfg, w, "bf16", device="cpu")
+    plan, wts, acts = enc.memory_plan(1, DeviceProfile(180 << 30, 180 << 30, 256))
+    assert len(plan.arenas()) == 1
+    # patch_w/b, cls, pos, final norm gamma/beta; 14 per block (two norms, four
+    # linear weights and biases, two LayerScales)
+    assert len(wts) == 6 + 14 * cfg.layers
+    names = [a[0] for a in acts]
+    assert "image" in names and "features.1" in names
+    ids = {name: k for k, name in enumerate(names, start=len(wts))}
+    patches = plan.placement(ids["patches"])
+    scratch = [plan.placement(ids[k]) for k in ("qkv", "o", "xn", "h")]
+    assert any(not (p.end() <= patches.offset or patches.end() <= p.offset) for p in scratch)
+    assert plan.total_bytes() < sum(p.size for _, p in plan.placements())
+    assert plan.peak_live_bytes() <= plan.total_bytes()
