@@ -70,10 +70,15 @@ struct Layout {
 struct Tail {
     uint64_t full[STAGES];
     uint64_t empty[STAGES];
-    uint64_t acc_full;
+    uint64_t acc_full[2];   // accumulator b holds a finished tile (the persistent
+    uint64_t acc_empty[2];  // kernel alternates two; the one-tile kernel uses [0])
     uint64_t drain;
     uint32_t tmem_base;
     int abort;
+    // the tile's bias and channel-scale columns, staged by the epilogue warps
+    // while the main loop runs
+    alignas(16) float bias[128];
+    alignas(16) float chan[128];
 };
 
 template <int BN>
@@ -136,6 +141,128 @@ __device__ __forceinline__ void load16(const void* base, int dt, float* v) {
     }
 }
 
+// Where one accumulator row (TMEM lane) of a tile goes: its output row
+// (row groups and offset applied) and its residual row.
+struct RowCtx {
+    bool live;
+    long long orow, res_row;
+};
+
+__device__ __forceinline__ RowCtx row_ctx(const Params& p, int grow) {
+    RowCtx rc;
+    rc.live = grow < p.M;
+    rc.orow = grow;
+    if (p.out_group_rows > 0)
+        rc.orow = grow + static_cast<long long>(grow / p.out_group_rows) * p.out_group_gap;
+    rc.orow += p.out_row_offset;
+    rc.res_row = p.res_period > 0 ? rc.orow % p.res_period : rc.orow;
+    return rc;
+}
+
+// The tile's bias and channel-scale columns into shared memory, by the four
+// epilogue warps (threads 64..191); the caller synchronises them after.
+template <int BN>
+__device__ __forceinline__ void stage_vectors(const Params& p, Tail* tail, int n0) {
+    const int t = static_cast<int>(threadIdx.x) - 64;
+    if (t >= 0 && t < BN) {
+        tail->bias[t] = p.bias != nullptr ? __ldg(p.bias + n0 + t) : 0.0f;
+        tail->chan[t] = p.chan_scale != nullptr ? __ldg(p.chan_scale + n0 + t) : 1.0f;
+    }
+}
+
+// The first 32 residual columns of this thread's row, into registers.
+__device__ __forceinline__ void prefetch_residual(const Params& p, const RowCtx& rc, int n0,
+                                                  float* rv0) {
+    if (p.residual == nullptr || !rc.live) return;
+    const size_t esz = p.res_dtype == BL_F32 ? 4 : 2;
+    const uint8_t* rb = static_cast<const uint8_t*>(p.residual) + esz * (rc.res_row * p.res_ld + n0);
+    load16(rb, p.res_dtype, rv0);
+    load16(rb + esz * 16, p.res_dtype, rv0 + 16);
+}
+
+// The epilogue chain of one accumulator row: TMEM columns 32 at a time, then
+// bias, activation, scale, channel scale, residual and the store.
+template <int BN>
+__device__ __forceinline__ void store_tile(const Params& p, const Tail* tail, uint32_t t_lane,
+                                           int n0, const RowCtx& rc, const float* rv0) {
+    const bool live = rc.live;
+    const long long orow = rc.orow, res_row = rc.res_row;
+    const size_t res_esz = p.res_dtype == BL_F32 ? 4 : 2;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(t_lane + c * 32, r);
+        tmem_wait_ld();
+        if (!live) continue;
+        const int col = n0 + c * 32;
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+        if (p.bias != nullptr) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+                const float4 b = *reinterpret_cast<const float4*>(tail->bias + c * 32 + i);
+                v[i] += b.x; v[i + 1] += b.y; v[i + 2] += b.z; v[i + 3] += b.w;
+            }
+        }
+        if (p.act == 1) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = fmaxf(v[i], 0.0f);
+        } else if (p.act == 2) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
+        } else if (p.act == 3) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+        }
+        if (p.scale != 1.0f) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] *= p.scale;
+        }
+        if (p.chan_scale != nullptr) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+                const float4 s = *reinterpret_cast<const float4*>(tail->chan + c * 32 + i);
+                v[i] *= s.x; v[i + 1] *= s.y; v[i + 2] *= s.z; v[i + 3] *= s.w;
+            }
+        }
+        if (p.residual != nullptr) {
+            if (c == 0) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] += rv0[i];
+            } else {
+                const uint8_t* rb = static_cast<const uint8_t*>(p.residual) +
+                                    res_esz * (res_row * p.res_ld + col);
+                float rv[16];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    load16(rb + res_esz * 16 * h, p.res_dtype, rv);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) v[16 * h + i] += rv[i];
+                }
+            }
+        }
+        const int dt = col >= p.split_col ? p.out_dtype_hi : p.out_dtype;
+        if (dt == BL_F32) {
+            float4* o = reinterpret_cast<float4*>(static_cast<float*>(p.out) +
+                                                  orow * p.out_ld + col);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                o[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        } else {
+            uint4* o = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) +
+                                                orow * p.out_ld + col);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                o[i] = make_uint4(pack2(v[8 * i], v[8 * i + 1], dt),
+                                  pack2(v[8 * i + 2], v[8 * i + 3], dt),
+                                  pack2(v[8 * i + 4], v[8 * i + 5], dt),
+                                  pack2(v[8 * i + 6], v[8 * i + 7], dt));
+        }
+    }
+
+}
+
 template <int BN, bool kLn>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
@@ -160,7 +287,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(smem_u32(&tail->full[s]), kLn ? 1 + 4 : 1);
             mbar_init(smem_u32(&tail->empty[s]), 1);
         }
-        mbar_init(smem_u32(&tail->acc_full), 1);
+        mbar_init(smem_u32(&tail->acc_full[0]), 1);
         mbar_init(smem_u32(&tail->drain), 1);
         tail->abort = 0;
         fence_barrier_init();
@@ -227,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (kb + STAGES < nk) mma_commit(smem_u32(&tail->empty[s]));
             }
             if (ok) {
-                mma_commit(smem_u32(&tail->acc_full));
+                mma_commit(smem_u32(&tail->acc_full[0]));
             } else {
                 mma_commit(smem_u32(&tail->drain));
                 mbar_wait(smem_u32(&tail->drain), 0, nullptr, p.status, ST_TIMEOUT_DRAIN, 0xD);
@@ -308,87 +435,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
         // -------------------------------------------------------- epilogue
-        if (ok) ok = mbar_wait(smem_u32(&tail->acc_full), 0, abort, p.status, ST_TIMEOUT_SOFTMAX,
+        // What the epilogue reads is fetched while the main loop still runs.
+        const RowCtx rc = row_ctx(p, grow);
+        stage_vectors<BN>(p, tail, n0);
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        float rv0[32];
+        prefetch_residual(p, rc, n0, rv0);
+        if (ok) ok = mbar_wait(smem_u32(&tail->acc_full[0]), 0, abort, p.status, ST_TIMEOUT_SOFTMAX,
                                0xE);
         ok = __all_sync(kFull, ok);
         if (ok) {
             tc_fence_after();
-            const uint32_t t_lane = tmem + (static_cast<uint32_t>(sub * 32) << 16);
-            const bool live = grow < p.M;
-            long long orow = grow;
-            if (p.out_group_rows > 0)
-                orow = grow + static_cast<long long>(grow / p.out_group_rows) * p.out_group_gap;
-            orow += p.out_row_offset;
-#pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld32(t_lane + c * 32, r);
-                tmem_wait_ld();
-                if (!live) continue;
-                const int col = n0 + c * 32;
-                float v[32];
-#pragma unroll
-                for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-                if (p.bias != nullptr) {
-#pragma unroll
-                    for (int i = 0; i < 32; i += 4) {
-                        const float4 b = __ldg(reinterpret_cast<const float4*>(p.bias + col + i));
-                        v[i] += b.x; v[i + 1] += b.y; v[i + 2] += b.z; v[i + 3] += b.w;
-                    }
-                }
-                if (p.act == 1) {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) v[i] = fmaxf(v[i], 0.0f);
-                } else if (p.act == 2) {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
-                } else if (p.act == 3) {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
-                }
-                if (p.scale != 1.0f) {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) v[i] *= p.scale;
-                }
-                if (p.chan_scale != nullptr) {
-#pragma unroll
-                    for (int i = 0; i < 32; i += 4) {
-                        const float4 s =
-                            __ldg(reinterpret_cast<const float4*>(p.chan_scale + col + i));
-                        v[i] *= s.x; v[i + 1] *= s.y; v[i + 2] *= s.z; v[i + 3] *= s.w;
-                    }
-                }
-                if (p.residual != nullptr) {
-                    const long long rrow = p.res_period > 0 ? orow % p.res_period : orow;
-                    const size_t esz = p.res_dtype == BL_F32 ? 4 : 2;
-                    const uint8_t* rb = static_cast<const uint8_t*>(p.residual) +
-                                        esz * (rrow * p.res_ld + col);
-                    float rv[16];
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        load16(rb + esz * 16 * h, p.res_dtype, rv);
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) v[16 * h + i] += rv[i];
-                    }
-                }
-                const int dt = col >= p.split_col ? p.out_dtype_hi : p.out_dtype;
-                if (dt == BL_F32) {
-                    float4* o = reinterpret_cast<float4*>(static_cast<float*>(p.out) +
-                                                          orow * p.out_ld + col);
-#pragma unroll
-                    for (int i = 0; i < 8; ++i)
-                        o[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-                } else {
-                    uint4* o = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) +
-                                                        orow * p.out_ld + col);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i)
-                        o[i] = make_uint4(pack2(v[8 * i], v[8 * i + 1], dt),
-                                          pack2(v[8 * i + 2], v[8 * i + 3], dt),
-                                          pack2(v[8 * i + 4], v[8 * i + 5], dt),
-                                          pack2(v[8 * i + 6], v[8 * i + 7], dt));
-                }
-            }
+            store_tile<BN>(p, tail, tmem + (static_cast<uint32_t>(sub * 32) << 16), n0, rc, rv0);
         }
     }
 
@@ -401,14 +459,215 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+__device__ __forceinline__ bool epilogue_all(bool ok) {
+    // AND of `ok` over the four epilogue warps; also their barrier
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, 1, 128, p;\n"
+        " selp.u32 %0, 1, 0, q;\n}"
+        : "=r"(r)
+        : "r"(ok ? 1u : 0u)
+        : "memory");
+    return r != 0;
+}
+
+// The persistent form, for A loaded by TMA: one CTA per SM walks tiles
+// t = blockIdx.x, blockIdx.x + gridDim.x, ... of this launch (tile t is row
+// tile t % m_tiles, column tile t / m_tiles). Two TMEM accumulators: the
+// epilogue warps drain tile j from one while the MMA thread fills tile j + 1
+// in the other, and the TMA ring runs on across tiles, so the epilogue and the
+// CTA's set-up leave the critical path once a CTA has more than one tile.
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_persistent(const __grid_constant__ CUtensorMap tm_a,
+                    const __grid_constant__ CUtensorMap tm_b, const Params p) {
+    using L = Layout<BN>;
+    constexpr uint32_t kCols = 2 * L::kTmemCols;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    Tail* tail = reinterpret_cast<Tail*>(smem + STAGES * L::kStage);
+    volatile int* abort = &tail->abort;
+    auto sA = [&](int s) { return smem + s * L::kStage; };
+    auto sB = [&](int s) { return smem + s * L::kStage + kTileA; };
+
+    const int warp = warp_id();
+    const int lane = lane_id();
+    const int nk = p.K / BK;
+    const int total = p.m_tiles * (p.N / BN);
+    const int mine = static_cast<int>(blockIdx.x) < total
+                         ? (total - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                               static_cast<int>(gridDim.x)
+                         : 0;
+    auto tile_m0 = [&](int j) {
+        const int t = static_cast<int>(blockIdx.x) + j * static_cast<int>(gridDim.x);
+        return (p.m_tile0 + t % p.m_tiles) * BM;
+    };
+    auto tile_n0 = [&](int j) {
+        const int t = static_cast<int>(blockIdx.x) + j * static_cast<int>(gridDim.x);
+        return (t / p.m_tiles) * BN;
+    };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(smem_u32(&tail->full[s]), 1);
+            mbar_init(smem_u32(&tail->empty[s]), 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(smem_u32(&tail->acc_full[b]), 1);
+            mbar_init(smem_u32(&tail->acc_empty[b]), 4);
+        }
+        mbar_init(smem_u32(&tail->drain), 1);
+        tail->abort = 0;
+        fence_barrier_init();
+        fence_proxy_async_smem();
+        tma_prefetch_desc(&tm_a);
+        tma_prefetch_desc(&tm_b);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(&tail->tmem_base), kCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tail->tmem_base;
+    pdl_trigger();
+    pdl_wait();
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int issued[STAGES];
+#pragma unroll
+            for (int s = 0; s < STAGES; ++s) issued[s] = 0;
+            int g = 0;
+            bool ok = true;
+            for (int j = 0; j < mine && ok; ++j) {
+                const int m0 = tile_m0(j), n0 = tile_n0(j);
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const int s = g % STAGES;
+                    if (g >= STAGES &&
+                        !mbar_wait(smem_u32(&tail->empty[s]), ((g / STAGES) - 1) & 1, abort,
+                                   p.status, ST_TIMEOUT_TMA, g)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t bar = smem_u32(&tail->full[s]);
+                    mbar_arrive_expect_tx(bar, kTileA + L::kTileB);
+                    tma_load_2d(smem_u32(sA(s)), &tm_a, kb * BK, m0, bar);
+                    tma_load_2d(smem_u32(sB(s)), &tm_b, kb * BK, n0, bar);
+                    issued[s] += 1;
+                }
+            }
+            if (*abort) {
+                for (int s = 0; s < STAGES; ++s)
+                    if (issued[s] > 0)
+                        mbar_wait(smem_u32(&tail->full[s]), (issued[s] - 1) & 1, nullptr,
+                                  p.status, ST_TIMEOUT_DRAIN, s);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc = idesc_f16(BM, BN, p.ab_fmt, p.ab_fmt, 0, 0);
+            const int total_g = mine * nk;
+            int g = 0;
+            bool ok = true;
+            for (int j = 0; j < mine && ok; ++j) {
+                const int b = j & 1, use = j >> 1;
+                if (use > 0 && !mbar_wait(smem_u32(&tail->acc_empty[b]), (use - 1) & 1, abort,
+                                          p.status, ST_TIMEOUT_MMA, 0x100 + j)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t acc = tmem + static_cast<uint32_t>(b) * L::kTmemCols;
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const int s = g % STAGES;
+                    ok = mbar_wait(smem_u32(&tail->full[s]), (g / STAGES) & 1, abort, p.status,
+                                   ST_TIMEOUT_MMA, g);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t a = smem_u32(sA(s)), bb = smem_u32(sB(s));
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k)
+                        mma_ss(acc, desc_k(a + 32 * k), desc_k(bb + 32 * k), idesc,
+                               (kb > 0 || k > 0) ? 1u : 0u);
+                    // release the stage only if the producer will refill it, so
+                    // no arrival lands after the CTA has finished
+                    if (g + STAGES < total_g) mma_commit(smem_u32(&tail->empty[s]));
+                }
+                if (ok) mma_commit(smem_u32(&tail->acc_full[b]));
+            }
+            if (!ok) {
+                mma_commit(smem_u32(&tail->drain));
+                mbar_wait(smem_u32(&tail->drain), 0, nullptr, p.status, ST_TIMEOUT_DRAIN, 0xD);
+            }
+        }
+    } else {
+        const int sub = warp & 3;
+        const int row = sub * 32 + lane;
+        for (int j = 0; j < mine; ++j) {
+            const int b = j & 1, use = j >> 1;
+            const int m0 = tile_m0(j), n0 = tile_n0(j);
+            const RowCtx rc = row_ctx(p, m0 + row);
+            epilogue_all(true);  // the previous tile's staged vectors are no longer read
+            stage_vectors<BN>(p, tail, n0);
+            epilogue_all(true);
+            float rv0[32];
+            prefetch_residual(p, rc, n0, rv0);
+            bool ok = mbar_wait(smem_u32(&tail->acc_full[b]), use & 1, abort, p.status,
+                                ST_TIMEOUT_SOFTMAX, 0x200 + j);
+            if (!epilogue_all(ok)) break;
+            tc_fence_after();
+            store_tile<BN>(p, tail,
+                           tmem + static_cast<uint32_t>(b) * L::kTmemCols +
+                               (static_cast<uint32_t>(sub * 32) << 16),
+                           n0, rc, rv0);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&tail->acc_empty[b]));
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, kCols);
+    }
+}
+
+int sm_count() {
+    static int n = 0;
+    if (n == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+            n = 148;
+    }
+    return n;
+}
+
 template <int BN, bool kLn>
 int prepare_t(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, Launch* out) {
-    auto kern = gemm_kernel<BN, kLn>;
     constexpr size_t smem = smem_bytes<BN>();
+    out->op = 2;
+    if (!kLn) {
+        auto kern = gemm_persistent<BN>;
+        BL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem)));
+        const int tiles = p.m_tiles * (p.N / BN);
+        const dim3 grid(std::min(tiles, sm_count()));
+        out->run = [=](cudaStream_t s) {
+            return launch_k(kern, grid, dim3(kThreads), smem, s, ta, tb, p);
+        };
+        return BL_OK;
+    }
+    auto kern = gemm_kernel<BN, kLn>;
     BL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(smem)));
     const dim3 grid(p.m_tiles, p.N / BN);
-    out->op = 2;
     out->run = [=](cudaStream_t s) {
         return launch_k(kern, grid, dim3(kThreads), smem, s, ta, tb, p);
     };

@@ -33,12 +33,15 @@ __global__ void __launch_bounds__(256) layernorm_kernel(bl_layernorm_args a, int
     in_row += a.in_row_offset;
     const float* x = a.x + in_row * static_cast<long long>(a.ldx);
     const int cols = static_cast<int>(a.cols);
-    float v[kPerLane];
+    // All loads (row, gamma, beta) before the first store: see layernorm_vec_kernel.
+    float v[kPerLane], g[kPerLane], b[kPerLane];
     float s = 0.0f;
 #pragma unroll
     for (int i = 0; i < kPerLane; ++i) {
         const int c = lane + 32 * i;
-        v[i] = c < cols ? x[c] : 0.0f;
+        v[i] = c < cols ? __ldg(x + c) : 0.0f;
+        g[i] = c < cols ? __ldg(a.gamma + c) : 0.0f;
+        b[i] = c < cols ? __ldg(a.beta + c) : 0.0f;
         s += v[i];
     }
 #pragma unroll
@@ -59,11 +62,82 @@ __global__ void __launch_bounds__(256) layernorm_kernel(bl_layernorm_args a, int
     for (int i = 0; i < kPerLane; ++i) {
         const int c = lane + 32 * i;
         if (c >= cols) break;
-        const float y = (v[i] - mean) * rstd * a.gamma[c] + a.beta[c];
+        const float y = (v[i] - mean) * rstd * g[i] + b[i];
         if (a.out_dtype == BL_F32)
             static_cast<float*>(a.out)[orow + c] = y;
         else
             static_cast<uint16_t*>(a.out)[orow + c] = to16(y, a.out_dtype);
+    }
+}
+
+// The same LayerNorm with 16-byte accesses: lane l holds columns
+// [4(l + 32i), 4(l + 32i) + 4) for i < kVec, so each warp load or store of
+// a row moves 512 contiguous bytes (f32 in) or 256 bytes (16-bit out). For
+// rows whose column count, strides and bases are multiples of 4 elements and
+// 16 / 8 bytes; four rows (warps) per 128-thread block.
+template <int kVec>
+__global__ void __launch_bounds__(128) layernorm_vec_kernel(bl_layernorm_args a, int row_begin,
+                                                            int row_end) {
+    pdl_trigger();
+    pdl_wait();
+    const int row = row_begin + static_cast<int>(blockIdx.x) * 4 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= row_end) return;
+    long long in_row = row;
+    if (a.in_group_rows > 0) in_row += static_cast<long long>(row / a.in_group_rows) * a.in_group_gap;
+    in_row += a.in_row_offset;
+    const float4* x = reinterpret_cast<const float4*>(a.x + in_row * static_cast<long long>(a.ldx));
+    const float4* g4 = reinterpret_cast<const float4*>(a.gamma);
+    const float4* b4 = reinterpret_cast<const float4*>(a.beta);
+    const int quads = static_cast<int>(a.cols) >> 2;
+    // Every load is issued before the first store: the output may alias
+    // gamma and beta as far as the compiler knows, so loads left between
+    // stores would each wait for the one before.
+    float4 v[kVec], g[kVec], b[kVec];
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < kVec; ++i) {
+        const int q = lane + 32 * i;
+        v[i] = q < quads ? __ldg(x + q) : zero;
+        g[i] = q < quads ? __ldg(g4 + q) : zero;
+        b[i] = q < quads ? __ldg(b4 + q) : zero;
+    }
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kVec; ++i) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
+    const float mean = s / static_cast<float>(a.cols);
+    float sq = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kVec; ++i) {
+        if (lane + 32 * i < quads) {
+            const float d0 = v[i].x - mean, d1 = v[i].y - mean, d2 = v[i].z - mean,
+                        d3 = v[i].w - mean;
+            sq += (d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xFFFFFFFFu, sq, o);
+    const float rstd = rsqrtf(sq / static_cast<float>(a.cols) + a.eps);
+    const long long orow = static_cast<long long>(row) * static_cast<long long>(a.ldo);
+#pragma unroll
+    for (int i = 0; i < kVec; ++i) {
+        const int q = lane + 32 * i;
+        if (q >= quads) break;
+        float4 y;
+        y.x = (v[i].x - mean) * rstd * g[i].x + b[i].x;
+        y.y = (v[i].y - mean) * rstd * g[i].y + b[i].y;
+        y.z = (v[i].z - mean) * rstd * g[i].z + b[i].z;
+        y.w = (v[i].w - mean) * rstd * g[i].w + b[i].w;
+        if (a.out_dtype == BL_F32) {
+            reinterpret_cast<float4*>(static_cast<float*>(a.out) + orow)[q] = y;
+        } else {
+            uint2 w;
+            w.x = to16(y.x, a.out_dtype) | (static_cast<uint32_t>(to16(y.y, a.out_dtype)) << 16);
+            w.y = to16(y.z, a.out_dtype) | (static_cast<uint32_t>(to16(y.w, a.out_dtype)) << 16);
+            reinterpret_cast<uint2*>(static_cast<uint16_t*>(a.out) + orow)[q] = w;
+        }
     }
 }
 
@@ -132,13 +206,29 @@ int prepare_layernorm_rows(const bl_layernorm_args& a, uint32_t row_begin, uint3
     if (b.ldo == 0) b.ldo = b.cols;
     if (row_begin >= row_end || row_end > a.rows)
         return fail(BL_ERR_INVALID, "layernorm: row part [%u, %u) outside [0, %u)", row_begin, row_end, a.rows);
-    const dim3 grid((row_end - row_begin + 7) / 8);
     const int r0 = static_cast<int>(row_begin), r1 = static_cast<int>(row_end);
+    auto aligned = [](const void* p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; };
+    const bool vec = b.cols % 4 == 0 && b.ldx % 4 == 0 && b.ldo % 4 == 0 && aligned(b.x, 16) &&
+                     aligned(b.gamma, 16) && aligned(b.beta, 16) &&
+                     aligned(b.out, b.out_dtype == BL_F32 ? 16 : 8);
+    out->op = 3;
+    if (vec) {
+        const int kvec = static_cast<int>((b.cols + 127) / 128);
+        void (*kern)(bl_layernorm_args, int, int) = kvec <= 1   ? misc::layernorm_vec_kernel<1>
+                                                  : kvec <= 2 ? misc::layernorm_vec_kernel<2>
+                                                  : kvec <= 3 ? misc::layernorm_vec_kernel<3>
+                                                  : kvec <= 4 ? misc::layernorm_vec_kernel<4>
+                                                  : kvec <= 6 ? misc::layernorm_vec_kernel<6>
+                                                              : misc::layernorm_vec_kernel<8>;
+        const dim3 grid((row_end - row_begin + 3) / 4);
+        out->run = [=](cudaStream_t s) { return launch_k(kern, grid, dim3(128), 0, s, b, r0, r1); };
+        return BL_OK;
+    }
+    const dim3 grid((row_end - row_begin + 7) / 8);
     void (*kern)(bl_layernorm_args, int, int) = a.cols <= 128   ? misc::layernorm_kernel<4>
                                       : a.cols <= 384 ? misc::layernorm_kernel<12>
                                       : a.cols <= 512 ? misc::layernorm_kernel<16>
                                                       : misc::layernorm_kernel<32>;
-    out->op = 3;
     out->run = [=](cudaStream_t s) {
         return launch_k(kern, grid, dim3(256), 0, s, b, r0, r1);
     };

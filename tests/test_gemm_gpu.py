@@ -53,8 +53,11 @@ def _check_status():
 @pytest.mark.parametrize("dtype", ["f16", "bf16"])
 @pytest.mark.parametrize("m,n,k,tile", [(1370, 1152, 384, 0), (1370, 384, 384, 32),
                                         (1370, 1536, 384, 128), (1370, 384, 1536, 32),
-                                        (200, 192, 128, 96), (1, 64, 64, 64), (129, 128, 640, 64)])
+                                        (200, 192, 128, 96), (1, 64, 64, 64), (129, 128, 640, 64),
+                                        (1370, 4096, 1024, 128), (2740, 1536, 384, 64)])
 def test_plain_gemm_with_bias(dtype, m, n, k, tile):
+    """Shapes from one tile to several tiles per CTA of the persistent grid
+    (1370 x 4096 at 128 columns: 352 tiles for 148 CTAs)."""
     import torch
     import beatlm_b200 as bl
     a = _rnd(oracle.normal(m + n, m * k), dtype)
@@ -70,12 +73,13 @@ def test_plain_gemm_with_bias(dtype, m, n, k, tile):
 
 
 @pytest.mark.parametrize("dtype", ["f16", "bf16"])
-def test_layerscale_residual_epilogue(dtype):
+@pytest.mark.parametrize("m,n,k", [(1370, 384, 384), (1370, 1024, 4096)])
+def test_layerscale_residual_epilogue(dtype, m, n, k):
     """x1 = x + ls * (A.W + b): ChannelScale then Add (reference.rs:379, 301),
-    in place on the f32 residual stream."""
+    in place on the f32 residual stream (ViT-S proj; ViT-L fc2, more than one
+    tile per CTA)."""
     import torch
     import beatlm_b200 as bl
-    m, n, k = 1370, 384, 384
     a = _rnd(oracle.normal(1, m * k), dtype)
     w = _rnd(oracle.uniform(2, k * n, -0.05, 0.05), dtype)
     b, ls = oracle.uniform(3, n, -0.1, 0.1), oracle.uniform(4, n, 0.1, 1.0)
