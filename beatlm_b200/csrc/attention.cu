@@ -53,7 +53,11 @@ static_assert(128 * kControlRegs + 32 * 4 * QT * kSoftmaxRegs <= kThreads * kLau
               "register split exceeds the launch allocation");
 constexpr uint32_t kTileBytes = BM * HD * 2;  // 16 KiB per 128x64 tile
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 0, kColO = 256;  // S_t at kColS + 128 t, O_t at kColO + 64 t
+// Three S buffers of 128 columns rotate over the (key tile, query tile) slots
+// j = 2 i + t (slot j uses buffer j % 3); O_t at kColO + 64 t.
+constexpr int kSBufs = 3;
+constexpr uint32_t kColS = 0, kColO = 128 * kSBufs;
+static_assert(kColO + 64 * QT <= kTmemCols, "TMEM columns");
 // Lazy rescaling: the max used for exponents may trail the true max by up to
 // this (log2 units), so p <= 2^8, well inside f16.
 constexpr float kRescaleThreshold = 8.0f;
@@ -93,9 +97,12 @@ struct SmemTail {
     uint64_t q_full;
     uint64_t kv_full[STAGES];
     uint64_t kv_empty[STAGES];
-    uint64_t s_full[QT];
-    uint64_t p_full[QT];
+    // S_t(i) ready / P_t(i) written: two barriers per tile, for even and odd
+    // key tiles, so neither side can run two phases ahead of the other
+    uint64_t s_full[QT][2];
+    uint64_t p_full[QT][2];
     uint64_t o_done[QT];
+    uint64_t o_final[QT];  // the last PV of tile t is complete
     uint64_t drain;
     uint32_t tmem_base;
     int abort;
@@ -108,8 +115,10 @@ constexpr size_t kSmemBytes = 1024 /*align slack*/ + QT * kTileBytes /*Q*/ +
 // K/V ring, 68 floats apart so eight threads' 16-byte accesses hit distinct
 // banks.
 constexpr int kPartStride = HD + 4;
-static_assert(ROWS * kPartStride * 4 <= 2 * STAGES * kTileBytes, "partials exceed the ring");
 constexpr int kMaxClusterSplits = 8;  // portable cluster size
+// splits * ceil(ROWS / splits) rows of partials per CTA
+static_assert((ROWS + kMaxClusterSplits) * kPartStride * 4 <= 2 * STAGES * kTileBytes,
+              "partials exceed the ring");
 
 __device__ __forceinline__ uint64_t desc_kmajor(uint32_t addr) {
     return sdesc_sw128(addr, 16, 1024);
@@ -239,9 +248,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(smem_u32(&tail->kv_empty[s]), 1);
         }
         for (int t = 0; t < QT; ++t) {
-            mbar_init(smem_u32(&tail->s_full[t]), 1);
-            mbar_init(smem_u32(&tail->p_full[t]), BM);
+            for (int e = 0; e < 2; ++e) {
+                mbar_init(smem_u32(&tail->s_full[t][e]), 1);
+                mbar_init(smem_u32(&tail->p_full[t][e]), BM);
+            }
             mbar_init(smem_u32(&tail->o_done[t]), 1);
+            mbar_init(smem_u32(&tail->o_final[t]), 1);
         }
         mbar_init(smem_u32(&tail->drain), 1);
         tail->abort = 0;
@@ -273,9 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int t = 0; t < QT; ++t)
                 tma_load_3d(smem_u32(sQ + t * kTileBytes), &tm_q, p.q_col0 + head * HD,
                             q0 + t * BM, batch, b_q);
-            int issued[STAGES];
-#pragma unroll
-            for (int s = 0; s < STAGES; ++s) issued[s] = 0;
+            int loaded = 0;  // key tiles whose loads were started
             for (int i = 0; i < n; ++i) {
                 const int s = i % STAGES;
                 const int r = i / STAGES;
@@ -288,16 +298,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                             (t0 + i) * BN, batch, bar);
                 tma_load_3d(smem_u32(sV + s * kTileBytes), &tm_v, p.v_col0 + head * HD,
                             (t0 + i) * BN, batch, bar);
-                issued[s] += 1;
+                ++loaded;
             }
             if (*abort) {
                 // Unwinding: let every copy this thread started land before
                 // the CTA's shared memory is released.
                 mbar_wait(b_q, 0, nullptr, p.status, ST_TIMEOUT_DRAIN, 0);
-                for (int s = 0; s < STAGES; ++s)
-                    if (issued[s] > 0)
-                        mbar_wait(smem_u32(&tail->kv_full[s]), (issued[s] - 1) & 1, nullptr,
-                                  p.status, ST_TIMEOUT_DRAIN, s);
+                for (int s = 0; s < STAGES && s < loaded; ++s) {
+                    const int uses = (loaded - s - 1) / STAGES + 1;
+                    mbar_wait(smem_u32(&tail->kv_full[s]), (uses - 1) & 1, nullptr, p.status,
+                              ST_TIMEOUT_DRAIN, s);
+                }
             }
         } else if (warp == 1 && lane == 0) {
             // -------------------------------------------------- MMA issuer
@@ -313,47 +324,63 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 return true;
             };
-            auto issue_s = [&](int t, int i) {
-                const uint32_t q_addr = smem_u32(sQ + t * kTileBytes);
-                const uint32_t k_addr = smem_u32(sK + (i % STAGES) * kTileBytes);
+            // Slot j = 2 i + t is (key tile i, query tile t); its S goes to
+            // buffer j % 3. The S of slot j + 3 reuses the buffer of slot j, so
+            // it is issued right after slot j's PV (the tensor core runs one
+            // thread's MMAs in order); the S of slots j + 1 and j + 2 are
+            // already issued by then, so a softmax warpgroup finds its next
+            // scores ready when it finishes its current ones.
+            // One thread issues every MMA, and an MMA costs its issuer tens of
+            // cycles, so the descriptors are built once: a tile or stage moves
+            // the 14-bit address field by kTileBytes / 16, a K step of 16
+            // elements by 32 bytes (K-major Q, K) or 16 rows (V).
+            const uint64_t dq = desc_kmajor(smem_u32(sQ));
+            const uint64_t dk = desc_kmajor(smem_u32(sK));
+            const uint64_t dv = desc_v(smem_u32(sV));
+            constexpr uint64_t kTileStep = kTileBytes >> 4;
+            auto issue_s = [&](int j) {
+                const int t = j & 1, i = j >> 1;
+                const uint64_t a = dq + t * kTileStep;
+                const uint64_t b = dk + (i % STAGES) * kTileStep;
+                const uint32_t dst = tmem + kColS + 128 * (j % kSBufs);
+                mma_ss(dst, a, b, idesc_s, 0u);
 #pragma unroll
-                for (int k = 0; k < HD / 16; ++k)
-                    mma_ss(tmem + kColS + 128 * t, desc_kmajor(q_addr + k * 32),
-                           desc_kmajor(k_addr + k * 32), idesc_s, k > 0 ? 1u : 0u);
-                mma_commit(smem_u32(&tail->s_full[t]));
+                for (int k = 1; k < HD / 16; ++k) mma_ss(dst, a + 2 * k, b + 2 * k, idesc_s, 1u);
+                mma_commit(smem_u32(&tail->s_full[t][i & 1]));
             };
-            auto issue_pv = [&](int t, int i) -> bool {
-                if (!mbar_wait(smem_u32(&tail->p_full[t]), i & 1, abort, p.status,
+            auto issue_pv = [&](int j) -> bool {
+                const int t = j & 1, i = j >> 1;
+                if (!mbar_wait(smem_u32(&tail->p_full[t][i & 1]), (i >> 1) & 1, abort, p.status,
                                ST_TIMEOUT_MMA, 0x10000 | (t << 12) | i))
                     return false;
                 tc_fence_after();
-                const uint32_t v_addr = smem_u32(sV + (i % STAGES) * kTileBytes);
-                const uint32_t p_col = tmem + kColS + 128 * t;
+                const uint64_t b = dv + (i % STAGES) * kTileStep;
+                const uint32_t p_col = tmem + kColS + 128 * (j % kSBufs);
+                const uint32_t o = tmem + kColO + 64 * t;
+                mma_ts(o, p_col, b, idesc_o, i > 0 ? 1u : 0u);
 #pragma unroll
-                for (int k = 0; k < BN / 16; ++k)
-                    mma_ts(tmem + kColO + 64 * t, p_col + k * 8, desc_v(v_addr + k * 16 * 128),
-                           idesc_o, (i > 0 || k > 0) ? 1u : 0u);
+                for (int k = 1; k < BN / 16; ++k) mma_ts(o, p_col + k * 8, b + 128 * k, idesc_o, 1u);
                 // The stage is released after its last reader (tile 1's PV),
                 // and only if the producer will refill it, so no arrival
                 // lands after the CTA has finished.
                 if (t == QT - 1 && i + STAGES < n)
                     mma_commit(smem_u32(&tail->kv_empty[i % STAGES]));
                 mma_commit(smem_u32(&tail->o_done[t]));
+                if (i == n - 1) mma_commit(smem_u32(&tail->o_final[t]));
                 return true;
             };
-            if (ok) ok = wait_kv(0);
-            if (ok) {
-                for (int t = 0; t < QT; ++t) issue_s(t, 0);
+            const int slots = QT * n;
+            for (int j = 0; j < kSBufs && j < slots && ok; ++j) {
+                if ((j & 1) == 0) ok = wait_kv(j >> 1);
+                if (ok) issue_s(j);
             }
-            for (int i = 0; i < n && ok; ++i) {
-                // tile 0: PV_i, then the next S (it overwrites P0_i: after PV)
-                ok = issue_pv(0, i);
-                if (ok && i + 1 < n) {
-                    ok = wait_kv(i + 1);
-                    if (ok) issue_s(0, i + 1);
+            for (int j = 0; j < slots && ok; ++j) {
+                ok = issue_pv(j);
+                const int next = j + kSBufs;
+                if (ok && next < slots) {
+                    if ((next & 1) == 0) ok = wait_kv(next >> 1);
+                    if (ok) issue_s(next);
                 }
-                if (ok) ok = issue_pv(1, i);
-                if (ok && i + 1 < n) issue_s(1, i + 1);
             }
             if (!ok) {
                 // Unwinding: wait for the tensor core to finish what was
@@ -376,10 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int sub = warp & 3;                  // TMEM sub-partition of this warp
         const int row = sub * 32 + lane;           // query row within the tile
         const uint32_t t_lane = tmem + (static_cast<uint32_t>(sub * 32) << 16);
-        const uint32_t s_col = t_lane + kColS + 128 * t;
         const uint32_t o_col = t_lane + kColO + 64 * t;
-        const uint32_t b_s = smem_u32(&tail->s_full[t]);
-        const uint32_t b_p = smem_u32(&tail->p_full[t]);
         const uint32_t b_o = smem_u32(&tail->o_done[t]);
         const float c = p.scale_log2;
         const unsigned long long c2 = f2pack(c, c);
@@ -387,7 +411,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         float l = 0.0f;
         bool ok = true;
         for (int i = 0; i < n; ++i) {
-            ok = mbar_wait(b_s, i & 1, abort, p.status, ST_TIMEOUT_SOFTMAX, (t << 12) | i);
+            const uint32_t s_col = t_lane + kColS + 128 * ((2 * i + t) % kSBufs);
+            const uint32_t b_p = smem_u32(&tail->p_full[t][i & 1]);
+            ok = mbar_wait(smem_u32(&tail->s_full[t][i & 1]), (i >> 1) & 1, abort, p.status,
+                           ST_TIMEOUT_SOFTMAX, (t << 12) | i);
             ok = __all_sync(kFull, ok);
             if (!ok) break;
             tc_fence_after();
@@ -425,6 +452,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 m_used = m_new;
             }
             if (i > 0 && __any_sync(kFull, need)) {
+                // O_t after PV_t(i-1). The S of this slot was issued after
+                // PV_t(i-2), so o_done is at most one phase behind here and
+                // the parity names the right phase.
                 ok = mbar_wait(b_o, (i - 1) & 1, abort, p.status, ST_TIMEOUT_SOFTMAX,
                                0x10000 | (t << 12) | i);
                 ok = __all_sync(kFull, ok);
@@ -477,8 +507,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_before();
             mbar_arrive(b_p);
         }
-        if (ok) ok = mbar_wait(b_o, (n - 1) & 1, abort, p.status, ST_TIMEOUT_SOFTMAX,
-                               0x20000 | t);
+        // The final O_t: o_done may be up to two phases from here (PV_t(n-2)
+        // can still be in flight), which one parity cannot tell apart, so the
+        // last PV has a barrier of its own.
+        if (ok) ok = mbar_wait(smem_u32(&tail->o_final[t]), 0, abort, p.status,
+                               ST_TIMEOUT_SOFTMAX, 0x20000 | t);
         if (threadIdx.x == 32 * kSoftmaxWarp0) trace_stamp(p.trace, 2);
         if (threadIdx.x == 32 * (kSoftmaxWarp0 + 4)) trace_stamp(p.trace, 3);
         ok = __all_sync(kFull, ok);
@@ -503,18 +536,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         float inv_l = 1.0f / l;
         if (p.cluster) {
             // ------------------------------ split-key partials, cluster form
-            // Both tiles' last PV must be complete before the K/V ring is
-            // reused for the partials: each warpgroup has seen its own; this
-            // barrier makes it both.
-            softmax_bar();
-            float* part = reinterpret_cast<float*>(sK);  // [ROWS][kPartStride], then m, l
-            float* pr = part + crow * kPartStride;
-#pragma unroll
-            for (int k = 0; k < HD; k += 4)
-                *reinterpret_cast<float4*>(pr + k) = make_float4(o[k], o[k + 1], o[k + 2], o[k + 3]);
-            *reinterpret_cast<float2*>(pr + HD) = make_float2(ok ? m_used : -INFINITY, l);
-            do_store = false;
+            // Row r of the 256 is combined by CTA r / per of the cluster. Each
+            // CTA pushes its unnormalised O and (max, sum) for a row into that
+            // CTA's K/V ring, at [own rank][r % per] (remote stores do not
+            // wait). First every CTA of the cluster must be done with its own
+            // ring: this barrier comes after each warpgroup's last PV.
+            __syncwarp();
+            cluster_sync();
             if (threadIdx.x == 32 * kSoftmaxWarp0) trace_stamp(p.trace, 4);
+            if (store) {
+                const int per = (ROWS + p.splits - 1) / p.splits;
+                const uint32_t me = cluster_rank();
+                const uint32_t local =
+                    smem_u32(sK) + static_cast<uint32_t>((me * per + crow % per) * kPartStride * 4);
+                const uint32_t dst = dsmem_addr(local, static_cast<uint32_t>(crow / per));
+#pragma unroll
+                for (int k = 0; k < HD; k += 4) dsmem_st4(dst + 4 * k, o[k], o[k + 1], o[k + 2], o[k + 3]);
+                dsmem_st2(dst + 4 * HD, ok ? m_used : -INFINITY, l);
+            }
+            do_store = false;
         } else if (p.splits > 1) {
             // ------------------------------------------ split-key combine
             const size_t unit = (static_cast<size_t>(batch) * p.heads_rel + blockIdx.y) *
@@ -570,33 +610,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (do_store) store_row(out_ptr(), kOutDtype, o, inv_l);
         if (p.cluster) {
             // ------------------------------------ cluster combine (DSMEM)
-            // CTA `rank` of the cluster (= its key split) combines rows
-            // [rank * R, rank * R + R) of the 256 from every CTA's partials:
+            // CTA `rank` of the cluster combines rows [rank * per, rank * per +
+            // per) of the 256 from the partials every CTA pushed into its ring:
             // O = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s.
             __syncwarp();
-            cluster_sync();  // every CTA's partials are in its shared memory
+            cluster_sync();  // every partial has landed; nothing reads remote memory after
             if (threadIdx.x == 32 * kSoftmaxWarp0) trace_stamp(p.trace, 5);
             // Sixteen threads per row, one 16-byte chunk each, so a warp
-            // reads two whole 256-byte rows per remote load and writes two
-            // whole output rows.
+            // reads two whole rows per load and writes two whole output rows.
             const int rank = static_cast<int>(cluster_rank());
             const int per = (ROWS + p.splits - 1) / p.splits;
             const int i = threadIdx.x - 32 * kSoftmaxWarp0;
             const int chunk = i & 15;
+            const float* part = reinterpret_cast<const float*>(sK);  // [split][per][kPartStride]
+#pragma unroll 2
             for (int base = 0; base < per; base += 16) {
                 const int r = base + (i >> 4);
                 const int mrow = rank * per + r;  // the row this thread helps combine
                 const int mgrow = q0 + mrow;
                 if (r >= per || mrow >= ROWS || mgrow >= p.row_end || mgrow >= p.tokens) continue;
-                const uint32_t local = smem_u32(sK) + mrow * kPartStride * 4;
                 float2 ml[kMaxClusterSplits];
                 float4 v[kMaxClusterSplits];
 #pragma unroll
                 for (int s = 0; s < kMaxClusterSplits; ++s) {
                     if (s < p.splits) {
-                        const uint32_t rs = dsmem_addr(local, s);
-                        ml[s] = dsmem_ld2(rs + HD * 4);
-                        v[s] = dsmem_ld4(rs + chunk * 16);
+                        const float* src = part + (s * per + r) * kPartStride;
+                        ml[s] = *reinterpret_cast<const float2*>(src + HD);
+                        v[s] = *reinterpret_cast<const float4*>(src + chunk * 4);
                     }
                 }
                 float mxs = -INFINITY;
@@ -636,8 +676,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             if (threadIdx.x == 32 * kSoftmaxWarp0) trace_stamp(p.trace, 6);
-            __syncwarp();
-            cluster_sync();  // no CTA leaves while its partials are being read
         }
     }
 

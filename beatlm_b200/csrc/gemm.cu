@@ -26,7 +26,8 @@ namespace gemm {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int STAGES = 4;
+constexpr int kMaxStages = 8;
+constexpr uint32_t kSmemLimit = 232448;  // 227 KiB of dynamic shared memory per CTA
 constexpr int kThreads = 192;
 constexpr uint32_t kTileA = BM * BK * 2;  // 16 KiB
 
@@ -64,12 +65,19 @@ template <int BN>
 struct Layout {
     static constexpr uint32_t kTileB = BN * BK * 2;
     static constexpr uint32_t kStage = kTileA + kTileB;
+    // As deep a TMA ring as shared memory holds (4 KiB kept for the barriers,
+    // the staged epilogue vectors and the alignment slack): a CTA's k-loop is
+    // bound by the bytes it has in flight, one SM's share of L2 latency.
+    static constexpr int kStages =
+        static_cast<int>((kSmemLimit - 4096) / kStage) < kMaxStages
+            ? static_cast<int>((kSmemLimit - 4096) / kStage)
+            : kMaxStages;
     static constexpr uint32_t kTmemCols = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
 };
 
 struct Tail {
-    uint64_t full[STAGES];
-    uint64_t empty[STAGES];
+    uint64_t full[kMaxStages];
+    uint64_t empty[kMaxStages];
     uint64_t acc_full[2];   // accumulator b holds a finished tile (the persistent
     uint64_t acc_empty[2];  // kernel alternates two; the one-tile kernel uses [0])
     uint64_t drain;
@@ -83,7 +91,7 @@ struct Tail {
 
 template <int BN>
 constexpr size_t smem_bytes() {
-    return 1024 + STAGES * Layout<BN>::kStage + sizeof(Tail);
+    return 1024 + Layout<BN>::kStages * Layout<BN>::kStage + sizeof(Tail);
 }
 
 __device__ __forceinline__ uint64_t desc_k(uint32_t addr) { return sdesc_sw128(addr, 16, 1024); }
@@ -268,6 +276,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                 const Params p) {
     using L = Layout<BN>;
+    constexpr int STAGES = L::kStages;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -312,9 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             tma_prefetch_desc(&tm_b);
             if (!kLn) tma_prefetch_desc(&tm_a);
-            int issued[STAGES];
-#pragma unroll
-            for (int s = 0; s < STAGES; ++s) issued[s] = 0;
+            int loaded = 0;  // k-blocks whose loads were started
             for (int kb = 0; kb < nk; ++kb) {
                 const int s = kb % STAGES;
                 if (kb >= STAGES &&
@@ -325,13 +332,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_arrive_expect_tx(bar, (kLn ? 0u : kTileA) + L::kTileB);
                 if (!kLn) tma_load_2d(smem_u32(sA(s)), &tm_a, kb * BK, m0, bar);
                 tma_load_2d(smem_u32(sB(s)), &tm_b, kb * BK, n0, bar);
-                issued[s] += 1;
+                ++loaded;
             }
             if (*abort) {
-                for (int s = 0; s < STAGES; ++s)
-                    if (issued[s] > 0)
-                        mbar_wait(smem_u32(&tail->full[s]), (issued[s] - 1) & 1, nullptr,
-                                  p.status, ST_TIMEOUT_DRAIN, s);
+                // let every started copy land before shared memory is released
+                for (int s = 0; s < STAGES && s < loaded; ++s) {
+                    const int uses = (loaded - s - 1) / STAGES + 1;
+                    mbar_wait(smem_u32(&tail->full[s]), (uses - 1) & 1, nullptr, p.status,
+                              ST_TIMEOUT_DRAIN, s);
+                }
             }
         }
     } else if (warp == 1) {
@@ -482,6 +491,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_persistent(const __grid_constant__ CUtensorMap tm_a,
                     const __grid_constant__ CUtensorMap tm_b, const Params p) {
     using L = Layout<BN>;
+    constexpr int STAGES = L::kStages;
     constexpr uint32_t kCols = 2 * L::kTmemCols;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -537,10 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            int issued[STAGES];
-#pragma unroll
-            for (int s = 0; s < STAGES; ++s) issued[s] = 0;
-            int g = 0;
+            int g = 0;  // k-blocks whose loads were started, over all tiles
             bool ok = true;
             for (int j = 0; j < mine && ok; ++j) {
                 const int m0 = tile_m0(j), n0 = tile_n0(j);
@@ -556,14 +563,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mbar_arrive_expect_tx(bar, kTileA + L::kTileB);
                     tma_load_2d(smem_u32(sA(s)), &tm_a, kb * BK, m0, bar);
                     tma_load_2d(smem_u32(sB(s)), &tm_b, kb * BK, n0, bar);
-                    issued[s] += 1;
                 }
             }
             if (*abort) {
-                for (int s = 0; s < STAGES; ++s)
-                    if (issued[s] > 0)
-                        mbar_wait(smem_u32(&tail->full[s]), (issued[s] - 1) & 1, nullptr,
-                                  p.status, ST_TIMEOUT_DRAIN, s);
+                // let every started copy land before shared memory is released
+                for (int s = 0; s < STAGES && s < g; ++s) {
+                    const int uses = (g - s - 1) / STAGES + 1;
+                    mbar_wait(smem_u32(&tail->full[s]), (uses - 1) & 1, nullptr, p.status,
+                              ST_TIMEOUT_DRAIN, s);
+                }
             }
         }
     } else if (warp == 1) {
@@ -676,9 +684,27 @@ int prepare_t(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, Lau
 
 int pick_bn(const bl_gemm_args& g) {
     if (g.tile_n) return static_cast<int>(g.tile_n);
-    // Fill the 148 SMs: the widest tile whose grid still covers them.
     const int mt = static_cast<int>((g.m + BM - 1) / BM);
     const int cands[4] = {128, 96, 64, 32};
+    if (g.ln_x == nullptr) {
+        // Persistent grid: the busiest CTA's tiles times a tile's cost. A
+        // k-block is bound by its operand bytes arriving (measured about 45
+        // bytes per SM clock from L2); the epilogue costs about 600 clocks
+        // per 32 columns. Ties go to the wider tile.
+        const long long nk = g.k / BK, sms = sm_count();
+        int best = 0;
+        long long best_cost = 0;
+        for (int bn : cands) {
+            if (g.n % bn != 0) continue;
+            const long long tiles = static_cast<long long>(mt) * (g.n / bn);
+            const long long per_cta = (tiles + sms - 1) / sms;
+            const long long tile = nk * (kTileA + bn * BK * 2) / 45 + 600LL * (bn / 32);
+            const long long cost = per_cta * tile;
+            if (best == 0 || cost < best_cost) best = bn, best_cost = cost;
+        }
+        return best;
+    }
+    // One tile per CTA: the widest tile whose grid still fills the SMs.
     for (int bn : cands)
         if (g.n % bn == 0 && mt * static_cast<int>(g.n / bn) >= 120) return bn;
     for (int i = 3; i >= 0; --i)

@@ -308,6 +308,16 @@ __device__ __forceinline__ float2 dsmem_ld2(uint32_t addr) {
     asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr));
     return v;
 }
+// Stores to a (possibly remote) distributed-shared-memory address; visible to
+// the target CTA after a release/acquire cluster barrier.
+__device__ __forceinline__ void dsmem_st4(uint32_t addr, float a, float b, float c, float d) {
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};"
+                 ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
+__device__ __forceinline__ void dsmem_st2(uint32_t addr, float a, float b) {
+    asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(a), "f"(b)
+                 : "memory");
+}
 
 __device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }

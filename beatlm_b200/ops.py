@@ -52,9 +52,11 @@ def attention_args(qkv, *, tokens, heads, out, head_dim=64, batch=1, qk_dtype="f
                    out_dtype=None, scale=None, rows=None, head_range=None, out_head_base=0,
                    qkv_row_stride=0, out_row_stride=None, workspace=None, kv_splits=0,
                    trace=None):
-    """``workspace``: a zero-filled device buffer of at least
-    ``attention_workspace_bytes`` bytes enables key splits (``kv_splits`` 0 =
-    automatic); without one the kernel runs unsplit."""
+    """``kv_splits`` 0 picks the key-split count. Without ``workspace`` the
+    splits of a query group combine in distributed shared memory (a cluster);
+    with one (a zero-filled device buffer of at least
+    ``attention_workspace_bytes`` bytes) they combine through it.
+    ``trace``: optional int64 device buffer for 8 timestamps per CTA."""
     if scale is None:
         scale = 1.0 / math.sqrt(head_dim)
     r0, r1 = rows or (0, tokens)

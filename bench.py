@@ -52,6 +52,20 @@ def peaks():
             "source": "fallback"}
 
 
+def profiled_traffic(name):
+    """DRAM bytes read + written per launch of the dominant kernel, from the
+    one ncu capture summarised in profiles/<name> (its
+    `traffic_bytes_per_launch:` line), or None without one."""
+    try:
+        with open(os.path.join(ROOT, "profiles", name)) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    return int(line.split(":", 1)[1])
+    except OSError:
+        pass
+    return None
+
+
 class Clocks:
     """nvidia-smi sampling of SM clocks and throttle reasons during timing."""
 
@@ -219,6 +233,8 @@ class EncoderWorkload:
                 "how": "cudaEvent slice timer (bl_timer) around every kernel of 5 direct "
                        "(non-graph) encodes after the timed region, each queued behind a "
                        "20 ms stream hold so the kernels run back to back",
+                "traffic": (None if self.large else
+                            profiled_traffic("attention_fwd_encoder_vit_s_T1370_H6.md")),
                 "kernels": {k: round(v[1] / steps, 2) for k, v in sorted(prof.items())}}
 
     large = False
@@ -451,6 +467,11 @@ class HiresWorkload:
                           % (self.op.local_heads, self.H),
                 "how": "CUDA events around %d attention-only launches after the timed region, "
                        "L2 flushed between them" % reps,
+                # one capture of the 16-head launch; a rank with fewer heads
+                # reads that share of the Q/K/V
+                "traffic": (lambda b: None if b is None else
+                            int(b * self.op.local_heads / self.H))(
+                    profiled_traffic("attention_fwd_hires_T5477_H16.md")),
                 "attention_ms": round(avg, 5)}
 
     def cpu_baseline(self, threads: int, budget_s: float = 15.0):
