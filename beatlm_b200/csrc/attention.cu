@@ -10,22 +10,24 @@
 // (setmaxnreg: 128 x 56 + 256 x 224 = 384 x 168, the launch allocation):
 //   warp 0      TMA producer: Q0 and Q1 once, then K/V tiles of 128 keys into
 //               a 4-stage ring (128-byte swizzle, zero fill past the last key).
-//   warp 1      MMA issuer (one thread): S_t = Q_t K^T into TMEM (M=128,
-//               N=128, K=64, f32) and O_t += P_t V with P read from TMEM
-//               (M=128, N=64, K=128, f16), issued so that the tensor core
-//               works on one tile while the other tile's softmax runs:
-//                 S0_0 S1_0 | PV0_0 S0_1 PV1_0 S1_1 | PV0_1 S0_2 PV1_1 ...
+//   warp 1      MMA issuer (one thread): S = Q_t K^T into TMEM (M=128,
+//               N=128, K=64, f32) and O_t += P V with P read from TMEM
+//               (M=128, N=64, K=128, f16). Three S buffers rotate over the
+//               slots j = 2 i + t (key tile i, query tile t), so the scores
+//               of the next two slots are computed before a softmax needs
+//               them: S_0 S_1 S_2 | PV_0 S_3 | PV_1 S_4 | PV_2 S_5 ...
 //   warps 4..7  softmax of tile 0, warps 8..11 softmax of tile 1: one thread
 //               per query row (TMEM lane) holding its 128 scores in
 //               registers; the running max is updated lazily (O is rescaled
 //               in TMEM only when the max grew by more than 2^8); P is
-//               written as f16 over the consumed S columns. Of each 8 pairs
-//               of exponentials, 3 are evaluated by a polynomial on the FMA
-//               pipe and 5 by the MUFU ex2 unit, so neither pipe idles.
-// With more than one key split, each CTA writes its unnormalised O and its
-// (max, sum) per row to a workspace; the last CTA of a tile group (an atomic
-// counter, no waiting) combines them. TMEM: S0 [0,128) S1 [128,256)
-// O0 [256,320) O1 [320,384); P_t aliases S_t.
+//               written as f16 over the consumed S columns; exponentials on
+//               the MUFU ex2 unit.
+// With more than one key split, the splits of a query group either form a
+// cluster and combine in distributed shared memory, or write their
+// unnormalised O and (max, sum) per row to a workspace where the last CTA
+// of the group (an atomic counter, no waiting) combines them.
+// TMEM: S buffers [0,128) [128,256) [256,384), O0 [384,448), O1 [448,512);
+// P aliases the S buffer it came from.
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 
@@ -154,33 +156,6 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
     float d;
     asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
     return d;
-}
-
-// 2^x for a pair, x <= 2^22, on the FMA pipe. Range reduction: x = j + f
-// with j = round(x) (adding 1.5 * 2^23 leaves j in the low mantissa bits) and
-// f in [-0.5, 0.5]; 2^f by a degree-3 polynomial fitted here by the Remez
-// exchange algorithm for minimax relative error (7.5e-5 on [-0.5, 0.5], far
-// below the f16 rounding of P); 2^j by adding j to the exponent field. x is
-// clamped at -120 so the exponent never underflows (2^-120 is 0 in f16).
-__device__ __forceinline__ void exp2_poly2(unsigned long long x2, float& r0, float& r1) {
-    constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
-    constexpr float c0 = 0.99992806f, c1 = 0.69326097f, c2 = 0.24261113f, c3 = 0.05517167f;
-    float x0, x1;
-    f2unpack(x2, x0, x1);
-    x0 = fmaxf(x0, -120.0f);
-    x1 = fmaxf(x1, -120.0f);
-    const unsigned long long xc = f2pack(x0, x1);
-    const unsigned long long t = fadd2(xc, f2pack(kShift, kShift));  // j in the low bits
-    const unsigned long long j = fadd2(t, f2pack(-kShift, -kShift));  // round(x)
-    const unsigned long long f = ffma2(j, f2pack(-1.0f, -1.0f), xc);  // x - j
-    unsigned long long p = ffma2(f2pack(c3, c3), f, f2pack(c2, c2));
-    p = ffma2(p, f, f2pack(c1, c1));
-    p = ffma2(p, f, f2pack(c0, c0));
-    float t0, t1, p0, p1;
-    f2unpack(t, t0, t1);
-    f2unpack(p, p0, p1);
-    r0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
-    r1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
 }
 
 __device__ __forceinline__ void store_row(void* base, int dt, const float* o, float inv_l) {
@@ -472,9 +447,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tmem_wait_st();
             }
-            // exponents: pairs k with k % 8 in {0, 3, 5} on the FMA pipe, the
-            // rest on MUFU; four partial sums; P packed to f16 in place
-            // (pair k lands in s[k], whose own score was consumed at pair k/2)
+            // exponents on the MUFU unit (measured: moving a share of them to
+            // a polynomial on the FMA pipe slows the MMA thread, which shares
+            // its issue slots with these warps, more than it unloads MUFU);
+            // four partial sums; P packed to f16 in place (pair k lands in
+            // s[k], whose own score was consumed at pair k/2)
             const unsigned long long nm2 = f2pack(-m_used, -m_used);
             unsigned long long acc[4];
 #pragma unroll
@@ -484,15 +461,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const unsigned long long x2 =
                     ffma2(f2pack(__uint_as_float(s[2 * k]), __uint_as_float(s[2 * k + 1])), c2,
                           nm2);
-                float p0, p1;
-                if ((k & 7) == 0 || (k & 7) == 3 || (k & 7) == 5) {
-                    exp2_poly2(x2, p0, p1);
-                } else {
-                    float x0, x1;
-                    f2unpack(x2, x0, x1);
-                    p0 = ex2(x0);
-                    p1 = ex2(x1);
-                }
+                float p0, p1, x0, x1;
+                f2unpack(x2, x0, x1);
+                p0 = ex2(x0);
+                p1 = ex2(x1);
                 acc[k & 3] = fadd2(acc[k & 3], f2pack(p0, p1));
                 s[k] = pack_f16x2(p0, p1);
             }

@@ -42,7 +42,11 @@ class DeviceProfile:
         return DeviceProfile(p.max_binding_bytes, p.max_buffer_bytes, p.offset_alignment)
 
     @staticmethod
-    def cuda(device: int = 0) -> "DeviceProfile":
+    def cuda(device: int | None = None) -> "DeviceProfile":
+        """The profile of CUDA device `device` (default: the current one)."""
+        if device is None:
+            import torch
+            device = torch.cuda.current_device()
         p = N.DeviceProfile()
         N.check(N.lib().bl_device_profile_cuda(device, ctypes.byref(p)))
         return DeviceProfile(p.max_binding_bytes, p.max_buffer_bytes, p.offset_alignment)
@@ -167,7 +171,11 @@ class Arenas:
     of `plan`. Placements are bound by device address; nothing else is ever
     allocated for the plan's tensors."""
 
-    def __init__(self, plan: MemoryPlan, device: int = 0):
+    def __init__(self, plan: MemoryPlan, device: int | None = None):
+        """`device`: the CUDA ordinal (default: the current device)."""
+        if device is None:
+            import torch
+            device = torch.cuda.current_device()
         handle = ctypes.c_void_p()
         N.check(N.lib().bl_arenas_create(plan.handle, device, ctypes.byref(handle)))
         self._h, self.device, self.plan = handle, device, plan

@@ -349,8 +349,11 @@ class Encoder:
         import torch
         from .memory import Arenas, DeviceProfile
         cfg = self.cfg
-        self.plan, wts, acts = self.memory_plan(frames, DeviceProfile.cuda(device.index or 0))
-        self.arena = Arenas(self.plan, device.index or 0)
+        # "cuda" without an index is the current device (one process per GPU
+        # sets it first), never device 0 by default
+        index = device.index if device.index is not None else torch.cuda.current_device()
+        self.plan, wts, acts = self.memory_plan(frames, DeviceProfile.cuda(index))
+        self.arena = Arenas(self.plan, index)
         get = lambda o, a, i: getattr(o, a) if i is None else getattr(o, a)[i]
         for k, (o, a, i) in enumerate(wts):
             src = get(o, a, i)

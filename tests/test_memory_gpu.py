@@ -87,3 +87,21 @@ def test_the_planned_encoder_matches_the_separately_allocated_one():
         assert torch.equal(got, want)
     with pytest.raises(ValueError, match="planned"):
         enc.buffers(2)
+
+
+def test_the_plan_lands_on_the_current_device():
+    """One process per GPU sets its device first; "cuda" then means that
+    device for the single allocation too (checked without launching work)."""
+    import torch
+    from beatlm_b200.memory import Arenas
+    from beatlm_b200.model import Encoder, ViTConfig
+    from test_block_gpu import _encoder_weights
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    with torch.cuda.device(1):
+        assert Arenas(_plan()).device == 1
+        cfg = ViTConfig.small(layers=1, out_indices=(1,))
+        enc = Encoder(cfg, _encoder_weights(cfg, 1), "bf16", planned_frames=1)
+        assert enc.arena.device == 1
+        assert enc.buffers(1).x.device == torch.device("cuda", 1)
+        assert enc.blocks[0].qkv_w.device == torch.device("cuda", 1)
