@@ -118,9 +118,9 @@ constexpr size_t kSmemBytes = 1024 /*align slack*/ + QT * kTileBytes /*Q*/ +
 // banks.
 constexpr int kPartStride = HD + 4;
 constexpr int kMaxClusterSplits = 8;  // portable cluster size
-// splits * ceil(ROWS / splits) rows of partials per CTA
-static_assert((ROWS + kMaxClusterSplits) * kPartStride * 4 <= 2 * STAGES * kTileBytes,
-              "partials exceed the ring");
+// A CTA receives splits * ceil(8 / splits) warps of 32 rows of partials, at
+// most 14 warps (7 splits); they live in the K/V ring.
+static_assert(14 * 32 * kPartStride * 4 <= 2 * STAGES * kTileBytes, "partials exceed the ring");
 
 __device__ __forceinline__ uint64_t desc_kmajor(uint32_t addr) {
     return sdesc_sw128(addr, 16, 1024);
@@ -508,20 +508,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         float inv_l = 1.0f / l;
         if (p.cluster) {
             // ------------------------------ split-key partials, cluster form
-            // Row r of the 256 is combined by CTA r / per of the cluster. Each
-            // CTA pushes its unnormalised O and (max, sum) for a row into that
-            // CTA's K/V ring, at [own rank][r % per] (remote stores do not
-            // wait). First every CTA of the cluster must be done with its own
-            // ring: this barrier comes after each warpgroup's last PV.
+            // Rows are owned by warp: the 32 rows of warp w (w = crow / 32) are
+            // combined in CTA w % splits of the cluster, by the very threads
+            // that hold those rows' O in registers. Every other CTA pushes its
+            // unnormalised O and (max, sum) for the row into the owner's K/V
+            // ring at [own rank][slot] (remote stores do not wait). First every
+            // CTA of the cluster must be done with its own ring: this barrier
+            // comes after each warpgroup's last PV.
             __syncwarp();
             cluster_sync();
             if (threadIdx.x == 32 * kSoftmaxWarp0) trace_stamp(p.trace, 4);
-            if (store) {
-                const int per = (ROWS + p.splits - 1) / p.splits;
-                const uint32_t me = cluster_rank();
+            const uint32_t me = cluster_rank();
+            const int owner = (crow >> 5) % p.splits;
+            const int slot = ((crow >> 5) / p.splits) * 32 + (crow & 31);
+            const int slots = ((ROWS / 32 + p.splits - 1) / p.splits) * 32;  // rows per owner
+            if (store && owner != static_cast<int>(me)) {
                 const uint32_t local =
-                    smem_u32(sK) + static_cast<uint32_t>((me * per + crow % per) * kPartStride * 4);
-                const uint32_t dst = dsmem_addr(local, static_cast<uint32_t>(crow / per));
+                    smem_u32(sK) + static_cast<uint32_t>((me * slots + slot) * kPartStride * 4);
+                const uint32_t dst = dsmem_addr(local, static_cast<uint32_t>(owner));
 #pragma unroll
                 for (int k = 0; k < HD; k += 4) dsmem_st4(dst + 4 * k, o[k], o[k + 1], o[k + 2], o[k + 3]);
                 dsmem_st2(dst + 4 * HD, ok ? m_used : -INFINITY, l);
@@ -582,70 +586,52 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (do_store) store_row(out_ptr(), kOutDtype, o, inv_l);
         if (p.cluster) {
             // ------------------------------------ cluster combine (DSMEM)
-            // CTA `rank` of the cluster combines rows [rank * per, rank * per +
-            // per) of the 256 from the partials every CTA pushed into its ring:
+            // The owner thread of a row combines its own partial (registers)
+            // with the ones pushed into its ring:
             // O = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s.
             __syncwarp();
             cluster_sync();  // every partial has landed; nothing reads remote memory after
             if (threadIdx.x == 32 * kSoftmaxWarp0) trace_stamp(p.trace, 5);
-            // Sixteen threads per row, one 16-byte chunk each, so a warp
-            // reads two whole rows per load and writes two whole output rows.
-            const int rank = static_cast<int>(cluster_rank());
-            const int per = (ROWS + p.splits - 1) / p.splits;
-            const int i = threadIdx.x - 32 * kSoftmaxWarp0;
-            const int chunk = i & 15;
-            const float* part = reinterpret_cast<const float*>(sK);  // [split][per][kPartStride]
-#pragma unroll 2
-            for (int base = 0; base < per; base += 16) {
-                const int r = base + (i >> 4);
-                const int mrow = rank * per + r;  // the row this thread helps combine
-                const int mgrow = q0 + mrow;
-                if (r >= per || mrow >= ROWS || mgrow >= p.row_end || mgrow >= p.tokens) continue;
-                float2 ml[kMaxClusterSplits];
-                float4 v[kMaxClusterSplits];
-#pragma unroll
-                for (int s = 0; s < kMaxClusterSplits; ++s) {
-                    if (s < p.splits) {
-                        const float* src = part + (s * per + r) * kPartStride;
-                        ml[s] = *reinterpret_cast<const float2*>(src + HD);
-                        v[s] = *reinterpret_cast<const float4*>(src + chunk * 4);
-                    }
-                }
-                float mxs = -INFINITY;
+            const uint32_t me = cluster_rank();
+            const int owner = (crow >> 5) % p.splits;
+            if (store && owner == static_cast<int>(me)) {
+                const int slot = ((crow >> 5) / p.splits) * 32 + (crow & 31);
+                const int slots = ((ROWS / 32 + p.splits - 1) / p.splits) * 32;
+                const float* part = reinterpret_cast<const float*>(sK);  // [rank][slots][kPartStride]
+                float mxs = ok ? m_used : -INFINITY;
 #pragma unroll
                 for (int s = 0; s < kMaxClusterSplits; ++s)
-                    if (s < p.splits) mxs = fmaxf(mxs, ml[s].x);
-                float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                float lsum = 0.0f;
+                    if (s < p.splits && s != static_cast<int>(me))
+                        mxs = fmaxf(mxs, part[(s * slots + slot) * kPartStride + HD]);
+                // splits in rank order whoever owns the row, so every row
+                // partition of the launch gives the same bits
+                float acc[HD];
 #pragma unroll
-                for (int s = 0; s < kMaxClusterSplits; ++s) {
-                    if (s < p.splits) {
-                        const float w = ex2(ml[s].x - mxs);
-                        lsum += w * ml[s].y;
-                        acc.x += w * v[s].x;
-                        acc.y += w * v[s].y;
-                        acc.z += w * v[s].z;
-                        acc.w += w * v[s].w;
+                for (int k = 0; k < HD; ++k) acc[k] = 0.0f;
+                float lsum = 0.0f;
+#pragma unroll 1
+                for (int s = 0; s < p.splits; ++s) {
+                    if (s == static_cast<int>(me)) {
+                        const float w = ok ? ex2(m_used - mxs) : 0.0f;
+                        lsum += w * l;
+#pragma unroll
+                        for (int k = 0; k < HD; ++k) acc[k] += w * o[k];
+                        continue;
+                    }
+                    const float* src = part + (s * slots + slot) * kPartStride;
+                    const float2 ml = *reinterpret_cast<const float2*>(src + HD);
+                    const float w = ex2(ml.x - mxs);
+                    lsum += w * ml.y;
+#pragma unroll
+                    for (int k = 0; k < HD; k += 4) {
+                        const float4 v = *reinterpret_cast<const float4*>(src + k);
+                        acc[k] += w * v.x;
+                        acc[k + 1] += w * v.y;
+                        acc[k + 2] += w * v.z;
+                        acc[k + 3] += w * v.w;
                     }
                 }
-                const float inv = 1.0f / lsum;
-                const size_t esz = kOutDtype == BL_F32 ? 4 : 2;
-                uint8_t* dst = static_cast<uint8_t*>(p.out) +
-                               esz * (static_cast<size_t>(batch) * p.out_batch_stride +
-                                      static_cast<size_t>(mgrow) * p.out_row_stride +
-                                      static_cast<size_t>(head - p.out_head_base) * HD +
-                                      chunk * 4);
-                if (kOutDtype == BL_F32) {
-                    *reinterpret_cast<float4*>(dst) =
-                        make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
-                } else if (kOutDtype == BL_F16) {
-                    *reinterpret_cast<uint2*>(dst) = make_uint2(
-                        pack_f16x2(acc.x * inv, acc.y * inv), pack_f16x2(acc.z * inv, acc.w * inv));
-                } else {
-                    *reinterpret_cast<uint2*>(dst) =
-                        make_uint2(pack_bf16x2(acc.x * inv, acc.y * inv),
-                                   pack_bf16x2(acc.z * inv, acc.w * inv));
-                }
+                store_row(out_ptr(), kOutDtype, acc, 1.0f / lsum);
             }
             if (threadIdx.x == 32 * kSoftmaxWarp0) trace_stamp(p.trace, 6);
         }
@@ -859,14 +845,23 @@ int attention_auto_splits(const bl_attention_args& a, uint64_t workspace_bytes) 
         while (want > 1 && plan(a, want).bytes > workspace_bytes) --want;
         return want;
     }
-    // cluster combine: the most splits whose clusters all run in one wave
-    if (p1.units * 2 > 148) return 1;
+    // Cluster combine: the split count with the least estimated time, waves
+    // of co-resident clusters times a wave's length. Measured on B200: a
+    // 128-key step of a CTA takes about 1.8 us, set-up about 0.5 us, the
+    // cluster combine about 3 us. Unsplit, one CTA per SM.
+    const long long units = static_cast<long long>(p1.units);
     const int max_s = std::min(kMaxClusterSplits, std::max(1, p1.kv_tiles / 2));
-    for (int s = max_s; s >= 2; --s) {
-        if (p1.units * s > 148) continue;
-        if (static_cast<int>(p1.units) <= max_active_clusters(s)) return s;
+    int best = 1;
+    double best_t = 0.0;
+    for (int s = 1; s <= max_s; ++s) {
+        const long long per_wave = s == 1 ? 148 : max_active_clusters(s);
+        if (per_wave <= 0) continue;
+        const long long waves = (units + per_wave - 1) / per_wave;
+        const int steps = (p1.kv_tiles + s - 1) / s;
+        const double t = static_cast<double>(waves) * (steps * 1.8 + 0.5 + (s > 1 ? 3.0 : 0.0));
+        if (s == 1 || t < best_t) best = s, best_t = t;
     }
-    return 1;
+    return best;
 }
 
 int prepare_attention(const bl_attention_args& a, Launch* out) {
