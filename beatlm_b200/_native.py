@@ -106,6 +106,8 @@ class GemmArgs(ctypes.Structure):
         ("split_col", ctypes.c_uint32), ("out_dtype_hi", ctypes.c_int32),
         ("out_row_offset", ctypes.c_uint32), ("out_group_rows", ctypes.c_uint32),
         ("out_group_gap", ctypes.c_uint32), ("tile_n", ctypes.c_uint32),
+        ("stats_out", ctypes.c_void_p), ("stats_parts", ctypes.c_uint32),
+        ("ln_stats", ctypes.c_void_p), ("ln_stats_parts", ctypes.c_uint32),
     ]
 
 

@@ -58,6 +58,10 @@ struct Params {
     int out_group_rows;  // out_row = m + (m / group_rows) * group_gap + offset
     int out_group_gap;
     int m_tile0, m_tiles;  // row tiles [m_tile0, m_tile0 + m_tiles) of this launch (a part)
+    float2* stats_out;     // [out row][stats_parts] (mean, M2) of the stored row slice
+    int stats_parts;
+    const float2* ln_stats;  // LN prologue: [row][ln_stats_parts] partials of x
+    int ln_stats_parts;
     Status* status;
 };
 
@@ -196,6 +200,7 @@ __device__ __forceinline__ void store_tile(const Params& p, const Tail* tail, ui
     const bool live = rc.live;
     const long long orow = rc.orow, res_row = rc.res_row;
     const size_t res_esz = p.res_dtype == BL_F32 ? 4 : 2;
+    float run_mean = 0.0f, run_m2 = 0.0f;  // row statistics of the stored slice
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
@@ -250,6 +255,20 @@ __device__ __forceinline__ void store_tile(const Params& p, const Tail* tail, ui
                 }
             }
         }
+        if (p.stats_out != nullptr) {
+            // this chunk's mean and M2, merged into the slice's (Chan et al.)
+            float cs = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) cs += v[i];
+            const float cm = cs * (1.0f / 32.0f);
+            float cm2 = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) cm2 += (v[i] - cm) * (v[i] - cm);
+            const float na = 32.0f * static_cast<float>(c), nab = na + 32.0f;
+            const float delta = cm - run_mean;
+            run_mean += delta * (32.0f / nab);
+            run_m2 += cm2 + delta * delta * (na * 32.0f / nab);
+        }
         const int dt = col >= p.split_col ? p.out_dtype_hi : p.out_dtype;
         if (dt == BL_F32) {
             float4* o = reinterpret_cast<float4*>(static_cast<float*>(p.out) +
@@ -268,7 +287,8 @@ __device__ __forceinline__ void store_tile(const Params& p, const Tail* tail, ui
                                   pack2(v[8 * i + 6], v[8 * i + 7], dt));
         }
     }
-
+    if (p.stats_out != nullptr && live)
+        p.stats_out[orow * p.stats_parts + n0 / BN] = make_float2(run_mean, run_m2);
 }
 
 template <int BN, bool kLn>
@@ -385,7 +405,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int dt = p.ab_fmt ? BL_BF16 : BL_F16;
             const float inv_k = 1.0f / static_cast<float>(p.K);
             float my_mean = 0.0f, my_rstd = 0.0f;
-            for (int r = 0; r < 32; ++r) {
+            if (p.ln_stats != nullptr) {
+                // the producing GEMM left (mean, M2) per row slice: combine
+                // them (equal counts), lane r for row r
+                const int gr = m0 + sub * 32 + lane;
+                if (gr < p.M) {
+                    const float2* st = p.ln_stats + static_cast<long long>(gr) * p.ln_stats_parts;
+                    const float nper = static_cast<float>(p.K / p.ln_stats_parts);
+                    float sm = 0.0f;
+                    for (int q = 0; q < p.ln_stats_parts; ++q) sm += st[q].x;
+                    const float mean = sm / static_cast<float>(p.ln_stats_parts);
+                    float m2 = 0.0f;
+                    for (int q = 0; q < p.ln_stats_parts; ++q) {
+                        const float2 v = st[q];
+                        m2 += v.y + (v.x - mean) * (v.x - mean) * nper;
+                    }
+                    my_mean = mean;
+                    my_rstd = rsqrtf(m2 * inv_k + p.eps);
+                }
+            }
+            for (int r = 0; r < 32 && p.ln_stats == nullptr; ++r) {
                 const int gr = m0 + sub * 32 + r;
                 if (gr >= p.M) break;
                 const float* xr = p.x + static_cast<long long>(gr) * p.ldx;
@@ -410,31 +449,38 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             for (int kb = 0; kb < nk; ++kb) {
                 const int s = kb % STAGES;
+                // this k-block's 32 rows are loaded before the stage is
+                // awaited, all at once, so one memory latency covers them
+                const int k = kb * BK + 2 * lane;
+                float2 xv[32];
+#pragma unroll
+                for (int r = 0; r < 32; ++r) {
+                    const int gr = m0 + sub * 32 + r;
+                    xv[r] = gr < p.M ? *reinterpret_cast<const float2*>(
+                                           p.x + static_cast<long long>(gr) * p.ldx + k)
+                                     : make_float2(0.0f, 0.0f);
+                }
+                const float2 g = __ldg(reinterpret_cast<const float2*>(p.gamma + k));
+                const float2 b = __ldg(reinterpret_cast<const float2*>(p.beta + k));
                 if (kb >= STAGES) {
                     ok = mbar_wait(smem_u32(&tail->empty[s]), ((kb / STAGES) - 1) & 1, abort,
                                    p.status, ST_TIMEOUT_SOFTMAX, kb);
                     ok = __all_sync(kFull, ok);
                     if (!ok) break;
                 }
-                const int k = kb * BK + 2 * lane;
-                const float2 g = __ldg(reinterpret_cast<const float2*>(p.gamma + k));
-                const float2 b = __ldg(reinterpret_cast<const float2*>(p.beta + k));
                 uint8_t* tile = sA(s);
                 // lane's 4 bytes: 16-byte chunk lane/4 of the row, XOR row%8
                 const int chunk = lane >> 2, off = (lane & 3) * 4;
-#pragma unroll 4
+#pragma unroll
                 for (int r = 0; r < 32; ++r) {
                     const int trow = sub * 32 + r;
                     const int gr = m0 + trow;
                     const float mean = __shfl_sync(kFull, my_mean, r);
                     const float rstd = __shfl_sync(kFull, my_rstd, r);
-                    uint32_t w = 0;
-                    if (gr < p.M) {
-                        const float2 v = *reinterpret_cast<const float2*>(
-                            p.x + static_cast<long long>(gr) * p.ldx + k);
-                        w = pack2((v.x - mean) * rstd * g.x + b.x, (v.y - mean) * rstd * g.y + b.y,
-                                  dt);
-                    }
+                    const uint32_t w =
+                        gr < p.M ? pack2((xv[r].x - mean) * rstd * g.x + b.x,
+                                         (xv[r].y - mean) * rstd * g.y + b.y, dt)
+                                 : 0u;
                     *reinterpret_cast<uint32_t*>(tile + trow * 128 + ((chunk ^ (trow & 7)) << 4) +
                                                  off) = w;
                 }
@@ -717,10 +763,30 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
     if (g.k % BK != 0) return fail(BL_ERR_UNSUPPORTED, "gemm: K=%u is not a multiple of 64", g.k);
     if (g.ab_dtype != BL_F16 && g.ab_dtype != BL_BF16)
         return fail(BL_ERR_UNSUPPORTED, "gemm: operand dtype %d (f16 or bf16)", g.ab_dtype);
-    const int bn = pick_bn(g);
+    int bn = pick_bn(g);
+    if (g.stats_out != nullptr) {
+        // one stats slice per column tile
+        if (g.stats_parts == 0 || g.n % g.stats_parts != 0)
+            return fail(BL_ERR_INVALID, "gemm: %u stats parts do not divide N=%u", g.stats_parts, g.n);
+        const uint32_t w = g.n / g.stats_parts;
+        if (g.tile_n && g.tile_n != w)
+            return fail(BL_ERR_INVALID, "gemm: tile width %u differs from the stats slice %u",
+                        g.tile_n, w);
+        if (g.out_dtype != BL_F32 || (g.split_col > 0 && g.split_col < g.n))
+            return fail(BL_ERR_INVALID, "gemm: row statistics need an f32 output of one type");
+        if (reinterpret_cast<uintptr_t>(g.stats_out) & 7)
+            return fail(BL_ERR_INVALID, "gemm: stats output must be 8-byte aligned");
+        bn = static_cast<int>(w);
+    }
     if (bn == 0 || g.n % bn != 0 || (bn != 32 && bn != 64 && bn != 96 && bn != 128))
         return fail(BL_ERR_UNSUPPORTED, "gemm: N=%u has no tile width (32/64/96/128)", g.n);
     const bool ln = g.ln_x != nullptr;
+    if (g.ln_stats != nullptr &&
+        (!ln || g.ln_stats_parts == 0 || g.k % g.ln_stats_parts != 0 ||
+         (reinterpret_cast<uintptr_t>(g.ln_stats) & 7)))
+        return fail(BL_ERR_INVALID,
+                    "gemm: LayerNorm statistics need the LayerNorm prologue, parts dividing K=%u "
+                    "and 8-byte alignment", g.k);
     if (!ln && g.a == nullptr) return fail(BL_ERR_INVALID, "gemm: no A operand");
     if (ln && (g.ln_gamma == nullptr || g.ln_beta == nullptr || !(g.ln_eps > 0.0f)))
         return fail(BL_ERR_INVALID, "gemm: LayerNorm prologue needs gamma, beta and eps > 0");
@@ -793,6 +859,10 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
     p.out_row_offset = static_cast<int>(g.out_row_offset);
     p.out_group_rows = static_cast<int>(g.out_group_rows);
     p.out_group_gap = static_cast<int>(g.out_group_gap);
+    p.stats_out = static_cast<float2*>(g.stats_out);
+    p.stats_parts = static_cast<int>(g.stats_parts);
+    p.ln_stats = static_cast<const float2*>(g.ln_stats);
+    p.ln_stats_parts = static_cast<int>(g.ln_stats_parts);
     p.m_tile0 = static_cast<int>(row_begin / BM);
     p.m_tiles = static_cast<int>((std::min(row_end, g.m) + BM - 1) / BM) - p.m_tile0;
     if (row_begin % BM != 0 || row_begin >= row_end || p.m_tiles <= 0)

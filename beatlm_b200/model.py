@@ -200,6 +200,10 @@ class Buffers:
         self.xn = alloc("xn", (rows, cfg.dim), td)
         self.h = alloc("h", (rows, cfg.mlp), td)
         self.patches = alloc("patches", (frames * (t - 1), cfg.k_pad), td)
+        # per-row partial LayerNorm statistics written by the GEMMs that write
+        # x: (mean, M2) for each 32-column slice
+        self.stats1 = alloc("stats1", (rows, cfg.dim // 32, 2), torch.float32)
+        self.stats2 = alloc("stats2", (rows, cfg.dim // 32, 2), torch.float32)
         self.features = ([alloc("features.%d" % i, (frames * (t - 1), cfg.dim), torch.float32)
                           for i in cfg.out_indices] if features else [])
 
@@ -213,7 +217,7 @@ class Buffers:
     def lifetime(name: str, last: int) -> tuple[int, int]:
         if name == "patches":
             return 0, 1
-        if name in ("qkv", "o", "xn", "h"):
+        if name in ("qkv", "o", "xn", "h", "stats1", "stats2"):
             return 2, last
         return 0, last
 
@@ -224,30 +228,46 @@ def block_specs(blk: DeviceBlock, cfg: ViTConfig, buf: Buffers, layer: int = 0,
     place on ``buf.x``:
     x1 = x + ls1 * proj(attention(norm1(x))); x = x1 + ls2 * fc2(gelu(fc1(norm2(x1)))).
 
-    ``fused_ln=False`` (default, 7 kernels): each LayerNorm is its own
-    bandwidth-bound kernel writing 16-bit rows that the next GEMM loads by
-    TMA. ``fused_ln=True`` (5 kernels): the LayerNorm is the QKV/fc1 GEMM's
-    prologue. At ViT-S shapes (K = 384) every N-tile CTA of the prologue form
-    must read the whole 128 x 384 f32 row block, which costs more than the
-    extra launch, so the split form is the default; both are tested."""
+    ``fused_ln=False`` (7 kernels): each LayerNorm is its own bandwidth-bound
+    kernel writing 16-bit rows that the next GEMM loads by TMA.
+    ``fused_ln=True`` (5 kernels; 7 for block 0): the GEMM that writes x also
+    writes each row's partial statistics (proj for norm2, the previous block's
+    fc2 for norm1: ``buf.stats2`` / ``buf.stats1``), and the QKV / fc1 GEMM
+    normalises its A operand from x in its prologue with them, so no
+    LayerNorm launch and no pass over the rows remain. Block 0's norm1 reads
+    the embedding's output, for which no statistics exist: it stays a
+    standalone LayerNorm."""
     from .runtime import Spec
     d = cfg.dim
     name = "block%d." % layer
     attn = Spec(ops.attention_args(buf.qkv, tokens=buf.tokens, heads=cfg.heads,
                                    head_dim=cfg.head_dim, batch=buf.frames, qk_dtype=blk.dtype,
                                    out=buf.o), name + "attention", parts)
+    stats = (lambda s: s) if fused_ln else (lambda s: None)
     proj = Spec(ops.gemm_args(blk.proj_w, a=buf.o, bias=blk.proj_b, chan_scale=blk.ls1,
-                              residual=buf.x, out=buf.x), name + "proj", parts)
+                              residual=buf.x, out=buf.x, stats_out=stats(buf.stats2)),
+                name + "proj", parts)
     fc2 = Spec(ops.gemm_args(blk.fc2_w, a=buf.h, bias=blk.fc2_b, chan_scale=blk.ls2,
-                             residual=buf.x, out=buf.x), name + "fc2", parts)
+                             residual=buf.x, out=buf.x, stats_out=stats(buf.stats1)),
+               name + "fc2", parts)
     if fused_ln:
-        return [
-            Spec(ops.gemm_args(blk.qkv_w, ln=(buf.x, blk.norm1[0], blk.norm1[1], cfg.eps),
-                               bias=blk.qkv_b, out=buf.qkv, out_dtype=blk.dtype,
-                               out_split=(2 * d, "f16")), name + "qkv", parts),
+        if layer == 0:
+            head = [
+                Spec(ops.layernorm_args(buf.x, blk.norm1[0], blk.norm1[1], cfg.eps, out=buf.xn),
+                     name + "norm1", parts),
+                Spec(ops.gemm_args(blk.qkv_w, a=buf.xn, bias=blk.qkv_b, out=buf.qkv,
+                                   out_dtype=blk.dtype, out_split=(2 * d, "f16")),
+                     name + "qkv", parts)]
+        else:
+            head = [Spec(ops.gemm_args(blk.qkv_w, ln=(buf.x, blk.norm1[0], blk.norm1[1], cfg.eps),
+                                       ln_stats=buf.stats1, bias=blk.qkv_b, out=buf.qkv,
+                                       out_dtype=blk.dtype, out_split=(2 * d, "f16")),
+                         name + "qkv", parts)]
+        return head + [
             attn, proj,
             Spec(ops.gemm_args(blk.fc1_w, ln=(buf.x, blk.norm2[0], blk.norm2[1], cfg.eps),
-                               bias=blk.fc1_b, act="gelu_erf", out=buf.h), name + "fc1", parts),
+                               ln_stats=buf.stats2, bias=blk.fc1_b, act="gelu_erf", out=buf.h),
+                 name + "fc1", parts),
             fc2,
         ]
     return [
@@ -277,7 +297,7 @@ class Encoder:
     """The DA-V2 ViT encoder (depth_anything_v2.rs:435-545) on the device."""
 
     def __init__(self, cfg: ViTConfig, weights: dict, dtype: str = "bf16", device="cuda",
-                 planned_frames: int | None = None):
+                 planned_frames: int | None = None, fused_ln: bool | None = None):
         """``weights``: ``blocks`` (list of per-block dicts in the reference
         layout), ``patch_w`` [patch][patch][cin][dim] (HWIO), ``patch_b`` [dim],
         ``cls`` [dim], ``pos`` [tokens][dim], ``norm_g``/``norm_b`` [dim].
@@ -288,10 +308,18 @@ class Encoder:
         the reference's MemoryPlan::new and Arenas::new). The weights are
         staged on the host and written into their placements; afterwards
         nothing is allocated. Without it each buffer is its own torch
-        allocation."""
+        allocation.
+
+        ``fused_ln``: the LayerNorms inside the blocks are fed by statistics
+        from the GEMM before them (``block_specs``). Off by default: measured
+        at ViT-S (one frame), the QKV and fc1 GEMMs that normalise their A
+        operand from the f32 rows through the load/store units take longer
+        than a standalone LayerNorm plus a GEMM that loads 16-bit rows by TMA
+        (1129 against 1345 frames/s)."""
         import torch
         td = torch.bfloat16 if dtype == "bf16" else torch.float16
         self.cfg, self.dtype = cfg, dtype
+        self.fused_ln = bool(fused_ln)
         self.arena, self.plan = None, None
         stage = "cpu" if planned_frames is not None else device
         self.blocks = [DeviceBlock(w, cfg.dim, cfg.mlp, dtype, stage) for w in weights["blocks"]]
@@ -376,8 +404,11 @@ class Encoder:
         cfg = self.cfg
         out = ["embed.patchify", "embed.patch"]
         for i in range(cfg.layers):
-            out += ["block%d.%s" % (i, k) for k in
-                    ("norm1", "qkv", "attention", "proj", "norm2", "fc1", "fc2")]
+            kinds = ("norm1", "qkv", "attention", "proj", "norm2", "fc1", "fc2")
+            if self.fused_ln:
+                kinds = (("norm1", "qkv") if i == 0 else ("qkv",)) + ("attention", "proj", "fc1",
+                                                                      "fc2")
+            out += ["block%d.%s" % (i, k) for k in kinds]
             if (i + 1) in cfg.out_indices:
                 out.append("features.%d" % (i + 1))
         return out
@@ -406,7 +437,7 @@ class Encoder:
         ]
         n = cfg.layers if layers is None else layers
         for i in range(n):
-            out += block_specs(self.blocks[i], cfg, buf, i, parts)
+            out += block_specs(self.blocks[i], cfg, buf, i, parts, fused_ln=self.fused_ln)
             if (i + 1) in cfg.out_indices:
                 f = buf.features[cfg.out_indices.index(i + 1)]
                 out.append(Spec(ops.layernorm_args(buf.x, self.norm[0], self.norm[1], cfg.eps,
@@ -439,4 +470,5 @@ class Encoder:
     def launches_per_frame_batch(self, layers: int | None = None) -> int:
         n = self.cfg.layers if layers is None else layers
         taken = sum(1 for i in self.cfg.out_indices if i <= n)
-        return 3 + 7 * n + taken  # patchify (2 kernels) + patch GEMM, 7 per block, norms
+        per_block = [7 if not self.fused_ln else (6 if i == 0 else 5) for i in range(n)]
+        return 3 + sum(per_block) + taken  # patchify (2 kernels) + patch GEMM, blocks, norms

@@ -116,7 +116,11 @@ def attention(qkv, *, tokens: int, heads: int, head_dim: int = 64, batch: int = 
 
 def gemm_args(w, *, a=None, ln=None, bias=None, act=None, scale=None, chan_scale=None,
               residual=None, res_period=0, out, out_dtype=None, out_split=None, m=None,
-              out_row_offset=0, out_group=(0, 0), tile_n=0):
+              out_row_offset=0, out_group=(0, 0), tile_n=0, stats_out=None, ln_stats=None):
+    """``stats_out``: a float32 ``[rows][parts][2]`` tensor the epilogue fills
+    with per-slice (mean, M2) of each stored row (``parts`` = n / tile width).
+    ``ln_stats``: such a tensor for ``ln``'s input, used instead of a pass
+    over its rows."""
     import torch
     n, k = w.shape
     ab = {torch.float16: "f16", torch.bfloat16: "bf16"}[w.dtype]
@@ -141,6 +145,10 @@ def gemm_args(w, *, a=None, ln=None, bias=None, act=None, scale=None, chan_scale
         g.ln_x, g.ln_ldx, g.ln_gamma, g.ln_beta, g.ln_eps = (x.data_ptr(), x.stride(0),
                                                              gamma.data_ptr(), beta.data_ptr(),
                                                              eps)
+    if stats_out is not None:
+        g.stats_out, g.stats_parts = stats_out.data_ptr(), stats_out.shape[1]
+    if ln_stats is not None:
+        g.ln_stats, g.ln_stats_parts = ln_stats.data_ptr(), ln_stats.shape[1]
     return g
 
 
@@ -152,7 +160,9 @@ def linear(w, *, stream=None, **kw):
     ``ln=(x, gamma, beta, eps)``, LayerNorm of the f32 rows ``x`` computed
     inside the kernel. ``out_dtype`` defaults to ``out``'s own type;
     ``out_split=(col, dtype)`` stores columns from ``col`` on as ``dtype``
-    (the f16 V part of packed Q|K|V rows)."""
+    (the f16 V part of packed Q|K|V rows). ``stats_out`` / ``ln_stats``:
+    per-row partial LayerNorm statistics written by this GEMM's epilogue /
+    consumed by its LayerNorm prologue (``gemm_args``)."""
     g = gemm_args(w, **kw)
     N.check(N.lib().bl_gemm(ctypes.byref(g), _stream_ptr(stream)))
     return kw["out"]

@@ -209,6 +209,18 @@ typedef struct bl_gemm_args {
     int32_t out_dtype_hi;
     uint32_t out_row_offset, out_group_rows, out_group_gap;
     uint32_t tile_n;
+    /* Row statistics for a LayerNorm that follows (optional; f32 outputs
+     * only). The epilogue also writes, for every output row and each of
+     * `stats_parts` equal column slices (n / stats_parts columns, which is then
+     * the kernel's tile width), the slice's mean and sum of squared deviations
+     * of the stored values: float2 [out row][part]. */
+    void* stats_out;
+    uint32_t stats_parts;
+    /* LayerNorm prologue only: take each row's mean and variance from such
+     * partial statistics of ln_x (ln_stats_parts equal slices of the k
+     * columns, combined by Chan's formula) instead of a pass over the row. */
+    const void* ln_stats;
+    uint32_t ln_stats_parts;
 } bl_gemm_args;
 
 int bl_gemm(const bl_gemm_args* args, void* stream);

@@ -93,10 +93,11 @@ def oracle_encoder(cfg, w, image, layers, dtype):
     return feats
 
 
-@pytest.mark.parametrize("dtype", ["bf16", "f16"])
-def test_encoder_features_match_the_reference_chain(dtype):
+@pytest.mark.parametrize("dtype,fused_ln", [("bf16", False), ("f16", False), ("bf16", True)])
+def test_encoder_features_match_the_reference_chain(dtype, fused_ln):
     """Config-3 shapes (518 px, ViT-S) with 3 blocks and a feature taken after
-    blocks 1 and 3, batch 2 frames."""
+    blocks 1 and 3, batch 2 frames; also with the LayerNorms fed by the
+    statistics of the GEMMs before them."""
     import torch
     import beatlm_b200 as bl
     from beatlm_b200.model import Encoder, ViTConfig
@@ -105,7 +106,7 @@ def test_encoder_features_match_the_reference_chain(dtype):
     w = _encoder_weights(cfg, layers)
     rng = np.random.default_rng(7)
     image = imagenet_image(rng, cfg.side, frames=2)
-    enc = Encoder(cfg, w, dtype)
+    enc = Encoder(cfg, w, dtype, fused_ln=fused_ln)
     feats = enc.forward(torch.from_numpy(image).cuda(), frames=2)
     torch.cuda.synchronize()
     assert bl.status(reset=True).code == 0

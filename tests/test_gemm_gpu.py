@@ -135,11 +135,22 @@ def test_gelu_erf_on_the_gpu_is_within_its_stated_error():
     assert worst <= 5e-7
 
 
+def _slice_stats(x, parts):
+    """(mean, M2) of each of `parts` equal column slices of each row, f64."""
+    m, d = x.shape
+    xs = x.astype(np.float64).reshape(m, parts, d // parts)
+    mean = xs.mean(axis=2)
+    return np.stack([mean, ((xs - mean[:, :, None]) ** 2).sum(axis=2)], axis=2)
+
+
 @pytest.mark.parametrize("dtype", ["f16", "bf16"])
 @pytest.mark.parametrize("d", [384, 1024])
-def test_layernorm_prologue(dtype, d):
+@pytest.mark.parametrize("given_stats", [False, True])
+def test_layernorm_prologue(dtype, d, given_stats):
     """QKV projection of LN(x): the LayerNorm (reference.rs:247-270) computed
-    inside the GEMM; Q|K stored in `dtype`, V in f16 (split store)."""
+    inside the GEMM, its row statistics either from a pass over the rows or
+    given as per-slice (mean, M2) partials; Q|K stored in `dtype`, V in f16
+    (split store)."""
     import torch
     import beatlm_b200 as bl
     m, n = 1370, 3 * d
@@ -148,9 +159,11 @@ def test_layernorm_prologue(dtype, d):
     w = _rnd(oracle.uniform(12, d * n, -1 / math.sqrt(d), 1 / math.sqrt(d)), dtype)
     b = oracle.uniform(13, n, -0.1, 0.1)
     out = torch.zeros((m, n), dtype=torch.int16, device="cuda")
+    stats = (torch.from_numpy(_slice_stats(x.reshape(m, d), d // 32).astype(np.float32)).cuda()
+             if given_stats else None)
     bl.ops.linear(_dev(w.reshape(d, n).T, dtype), ln=(_dev(x.reshape(m, d), "f32"),
                   _dev(g, "f32"), _dev(be, "f32"), 1e-6), bias=_dev(b, "f32"), out=out,
-                  out_dtype=dtype, out_split=(2 * d, "f16"))
+                  out_dtype=dtype, out_split=(2 * d, "f16"), ln_stats=stats)
     torch.cuda.synchronize()
     _check_status()
     o = out.cpu()
@@ -163,6 +176,55 @@ def test_layernorm_prologue(dtype, d):
     rel_v = _rel(v, oracle.round_f16(want[:, 2 * d:]))
     print("LN prologue %s D=%d: rel-L2 QK %.2e V %.2e" % (dtype, d, rel_qk, rel_v))
     assert rel_qk < 2e-4 and rel_v < 2e-4
+
+
+@pytest.mark.parametrize("m,n,k", [(1370, 384, 384), (1370, 384, 1536), (300, 1024, 256)])
+def test_row_statistics_of_the_stored_output(m, n, k):
+    """A residual GEMM (x1 = x + ls * (A.W + b), f32) also writes each row's
+    per-32-column (mean, M2) of the values it stored: checked against the
+    stored output itself, and the LayerNorm prologue fed by them gives the
+    same rows as a standalone LayerNorm of that output."""
+    import torch
+    import beatlm_b200 as bl
+    a = _rnd(oracle.normal(21, m * k), "bf16")
+    w = _rnd(oracle.uniform(22, k * n, -0.05, 0.05), "bf16")
+    x = torch.from_numpy(oracle.uniform(23, m * n, -2, 2).reshape(m, n)).cuda()
+    stats = torch.zeros((m, n // 32, 2), dtype=torch.float32, device="cuda")
+    bl.ops.linear(_dev(w.reshape(k, n).T, "bf16"), a=_dev(a.reshape(m, k), "bf16"),
+                  bias=_dev(oracle.uniform(24, n, -0.1, 0.1), "f32"),
+                  chan_scale=_dev(oracle.uniform(25, n, 0.1, 1.0), "f32"), residual=x, out=x,
+                  stats_out=stats)
+    torch.cuda.synchronize()
+    _check_status()
+    want = _slice_stats(x.cpu().numpy(), n // 32)
+    got = stats.cpu().numpy().astype(np.float64)
+    assert np.allclose(got[..., 0], want[..., 0], rtol=1e-5, atol=1e-6)
+    assert np.allclose(got[..., 1], want[..., 1], rtol=1e-4, atol=1e-5)
+    # the consumer: LN(x) . W2 with the given statistics vs LN by its own kernel
+    g, be = _dev(oracle.uniform(26, n, 0.8, 1.2), "f32"), _dev(oracle.uniform(27, n, -0.1, 0.1), "f32")
+    w2 = _dev(_rnd(oracle.uniform(28, n * 64, -0.1, 0.1), "bf16").reshape(n, 64).T, "bf16")
+    y1 = torch.zeros((m, 64), dtype=torch.float32, device="cuda")
+    y2 = torch.zeros_like(y1)
+    bl.ops.linear(w2, ln=(x, g, be, 1e-6), ln_stats=stats, out=y1)
+    xn = torch.zeros((m, n), dtype=torch.bfloat16, device="cuda")
+    bl.ops.layernorm(x, g, be, 1e-6, out=xn)
+    bl.ops.linear(w2, a=xn, out=y2)
+    torch.cuda.synchronize()
+    _check_status()
+    assert _rel(y1.cpu().numpy(), y2.cpu().numpy()) < 2e-3
+
+
+def test_statistics_arguments_are_checked():
+    import torch
+    import beatlm_b200 as bl
+    w = torch.zeros((384, 384), dtype=torch.bfloat16, device="cuda")
+    a = torch.zeros((128, 384), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(bl.BackendError, match="f32"):
+        bl.ops.linear(w, a=a, out=torch.zeros((128, 384), dtype=torch.bfloat16, device="cuda"),
+                      stats_out=torch.zeros((128, 12, 2), device="cuda"))
+    with pytest.raises(bl.BackendError, match="parts"):
+        bl.ops.linear(w, a=a, out=torch.zeros((128, 384), device="cuda"),
+                      stats_out=torch.zeros((128, 7, 2), device="cuda"))
 
 
 def test_patch_rows_land_after_the_class_token():
