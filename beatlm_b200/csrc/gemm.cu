@@ -105,16 +105,33 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, int dt) {
 }
 
 // GELU through erf, Abramowitz and Stegun 7.1.26 (the reference's
-// GELU_ERF_P / GELU_ERF_A, kernel.rs:355-372), in f32 as its kernels do.
-__device__ __forceinline__ float gelu_erf(float x) {
+// GELU_ERF_P / GELU_ERF_A, kernel.rs:355-372), in f32 as its kernels do:
+//   z = |x| / sqrt(2), t = 1 / (1 + p z),
+//   q = 0.5 t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) 2^(-z^2 log2 e),
+//   GELU(x) = x (1 - q) for x >= 0, x q otherwise.
+// Two values at once, the arithmetic in packed f32x2 instructions; the
+// reciprocal is the correctly rounded intrinsic (the value of 1 / (...)
+// without the general division's slow path).
+__device__ __forceinline__ void gelu_erf2(float& x0, float& x1) {
     const float p = 0.3275911f;
     const float a1 = 0.254829592f, a2 = -0.284496736f, a3 = 1.421413741f, a4 = -1.453152027f,
                 a5 = 1.061405429f;
-    const float z = fabsf(x) * 0.70710678118654752f;
-    const float t = 1.0f / (1.0f + p * z);
-    const float poly = t * (a1 + t * (a2 + t * (a3 + t * (a4 + t * a5))));
-    const float q = 0.5f * poly * ex2(-z * z * 1.4426950408889634f);
-    return x * (x >= 0.0f ? 1.0f - q : q);
+    const unsigned long long z =
+        fmul2(f2pack(fabsf(x0), fabsf(x1)), f2pack(0.70710678118654752f, 0.70710678118654752f));
+    float d0, d1;
+    f2unpack(ffma2(f2pack(p, p), z, f2pack(1.0f, 1.0f)), d0, d1);
+    const unsigned long long t = f2pack(__frcp_rn(d0), __frcp_rn(d1));
+    unsigned long long poly = ffma2(t, f2pack(a5, a5), f2pack(a4, a4));
+    poly = ffma2(t, poly, f2pack(a3, a3));
+    poly = ffma2(t, poly, f2pack(a2, a2));
+    poly = ffma2(t, poly, f2pack(a1, a1));
+    poly = fmul2(t, poly);
+    float e0, e1;
+    f2unpack(fmul2(fmul2(z, z), f2pack(-1.4426950408889634f, -1.4426950408889634f)), e0, e1);
+    float q0, q1;
+    f2unpack(fmul2(fmul2(f2pack(0.5f, 0.5f), poly), f2pack(ex2(e0), ex2(e1))), q0, q1);
+    x0 = x0 * (x0 >= 0.0f ? 1.0f - q0 : q0);
+    x1 = x1 * (x1 >= 0.0f ? 1.0f - q1 : q1);
 }
 
 __device__ __forceinline__ float gelu_tanh(float x) {
@@ -226,7 +243,7 @@ __device__ __forceinline__ void store_tile(const Params& p, const Tail* tail, ui
             for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
         } else if (p.act == 3) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+            for (int i = 0; i < 32; i += 2) gelu_erf2(v[i], v[i + 1]);
         }
         if (p.scale != 1.0f) {
 #pragma unroll
@@ -736,7 +753,9 @@ int pick_bn(const bl_gemm_args& g) {
         // Persistent grid: the busiest CTA's tiles times a tile's cost. A
         // k-block is bound by its operand bytes arriving (measured about 45
         // bytes per SM clock from L2); the epilogue costs about 600 clocks
-        // per 32 columns. Ties go to the wider tile.
+        // per 32 columns. Ties go to the wider tile. (Adding the L2's total
+        // delivery as a bound picked 64 columns for ViT-S fc2, measured 10 %
+        // slower than 32.)
         const long long nk = g.k / BK, sms = sm_count();
         int best = 0;
         long long best_cost = 0;
