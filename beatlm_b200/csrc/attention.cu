@@ -265,16 +265,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                               ST_TIMEOUT_DRAIN, s);
                 }
             }
-        } else if (warp == 1 && lane == 0) {
+        } else if (warp == 1) {
             // -------------------------------------------------- MMA issuer
+            // The whole warp runs the issuer's loop and one elected lane
+            // issues, so descriptors and loop state stay warp-uniform (the
+            // MMA's operands are uniform registers; single-lane code paid
+            // about 75 cycles per MMA instead of about 30). One lane waits on
+            // each barrier and the vote hands its outcome to the warp.
+            const bool elected = elect_one();
+            auto wait_all = [&](uint32_t bar, uint32_t parity, uint32_t where) -> bool {
+                bool r = true;
+                if (elected) r = mbar_wait(bar, parity, abort, p.status, ST_TIMEOUT_MMA, where);
+                return __all_sync(0xFFFFFFFFu, r);
+            };
             const uint32_t idesc_s = idesc_f16(BM, BN, p.qk_fmt, p.qk_fmt, 0, 0);
             const uint32_t idesc_o = idesc_f16(BM, HD, 0, 0, 0, 1);
-            bool ok = mbar_wait(smem_u32(&tail->q_full), 0, abort, p.status, ST_TIMEOUT_MMA,
-                                0xFFFF);
+            bool ok = wait_all(smem_u32(&tail->q_full), 0, 0xFFFF);
             tc_fence_after();
             auto wait_kv = [&](int i) -> bool {
-                if (!mbar_wait(smem_u32(&tail->kv_full[i % STAGES]), (i / STAGES) & 1, abort,
-                               p.status, ST_TIMEOUT_MMA, i))
+                if (!wait_all(smem_u32(&tail->kv_full[i % STAGES]), (i / STAGES) & 1, i))
                     return false;
                 tc_fence_after();
                 return true;
@@ -285,10 +294,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             // thread's MMAs in order); the S of slots j + 1 and j + 2 are
             // already issued by then, so a softmax warpgroup finds its next
             // scores ready when it finishes its current ones.
-            // One thread issues every MMA, and an MMA costs its issuer tens of
-            // cycles, so the descriptors are built once: a tile or stage moves
-            // the 14-bit address field by kTileBytes / 16, a K step of 16
-            // elements by 32 bytes (K-major Q, K) or 16 rows (V).
+            // Descriptors are built once: a tile or stage moves the 14-bit
+            // address field by kTileBytes / 16, a K step of 16 elements by 32
+            // bytes (K-major Q, K) or 16 rows (V).
             const uint64_t dq = desc_kmajor(smem_u32(sQ));
             const uint64_t dk = desc_kmajor(smem_u32(sK));
             const uint64_t dv = desc_v(smem_u32(sV));
@@ -298,30 +306,37 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint64_t a = dq + t * kTileStep;
                 const uint64_t b = dk + (i % STAGES) * kTileStep;
                 const uint32_t dst = tmem + kColS + 128 * (j % kSBufs);
-                mma_ss(dst, a, b, idesc_s, 0u);
+                if (elected) {
+                    mma_ss(dst, a, b, idesc_s, 0u);
 #pragma unroll
-                for (int k = 1; k < HD / 16; ++k) mma_ss(dst, a + 2 * k, b + 2 * k, idesc_s, 1u);
-                mma_commit(smem_u32(&tail->s_full[t][i & 1]));
+                    for (int k = 1; k < HD / 16; ++k) mma_ss(dst, a + 2 * k, b + 2 * k, idesc_s, 1u);
+                    mma_commit(smem_u32(&tail->s_full[t][i & 1]));
+                }
+                __syncwarp();
             };
             auto issue_pv = [&](int j) -> bool {
                 const int t = j & 1, i = j >> 1;
-                if (!mbar_wait(smem_u32(&tail->p_full[t][i & 1]), (i >> 1) & 1, abort, p.status,
-                               ST_TIMEOUT_MMA, 0x10000 | (t << 12) | i))
+                if (!wait_all(smem_u32(&tail->p_full[t][i & 1]), (i >> 1) & 1,
+                              0x10000 | (t << 12) | i))
                     return false;
                 tc_fence_after();
                 const uint64_t b = dv + (i % STAGES) * kTileStep;
                 const uint32_t p_col = tmem + kColS + 128 * (j % kSBufs);
                 const uint32_t o = tmem + kColO + 64 * t;
-                mma_ts(o, p_col, b, idesc_o, i > 0 ? 1u : 0u);
+                if (elected) {
+                    mma_ts(o, p_col, b, idesc_o, i > 0 ? 1u : 0u);
 #pragma unroll
-                for (int k = 1; k < BN / 16; ++k) mma_ts(o, p_col + k * 8, b + 128 * k, idesc_o, 1u);
-                // The stage is released after its last reader (tile 1's PV),
-                // and only if the producer will refill it, so no arrival
-                // lands after the CTA has finished.
-                if (t == QT - 1 && i + STAGES < n)
-                    mma_commit(smem_u32(&tail->kv_empty[i % STAGES]));
-                mma_commit(smem_u32(&tail->o_done[t]));
-                if (i == n - 1) mma_commit(smem_u32(&tail->o_final[t]));
+                    for (int k = 1; k < BN / 16; ++k)
+                        mma_ts(o, p_col + k * 8, b + 128 * k, idesc_o, 1u);
+                    // The stage is released after its last reader (tile 1's
+                    // PV), and only if the producer will refill it, so no
+                    // arrival lands after the CTA has finished.
+                    if (t == QT - 1 && i + STAGES < n)
+                        mma_commit(smem_u32(&tail->kv_empty[i % STAGES]));
+                    mma_commit(smem_u32(&tail->o_done[t]));
+                    if (i == n - 1) mma_commit(smem_u32(&tail->o_final[t]));
+                }
+                __syncwarp();
                 return true;
             };
             const int slots = QT * n;
@@ -340,8 +355,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok) {
                 // Unwinding: wait for the tensor core to finish what was
                 // issued before TMEM is released.
-                mma_commit(smem_u32(&tail->drain));
-                mbar_wait(smem_u32(&tail->drain), 0, nullptr, p.status, ST_TIMEOUT_DRAIN, 0xD);
+                if (elected) {
+                    mma_commit(smem_u32(&tail->drain));
+                    mbar_wait(smem_u32(&tail->drain), 0, nullptr, p.status, ST_TIMEOUT_DRAIN, 0xD);
+                }
+                __syncwarp();
             }
         }
         if (p.cluster) {

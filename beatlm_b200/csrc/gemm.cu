@@ -387,24 +387,34 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            const uint32_t idesc = idesc_f16(BM, BN, p.ab_fmt, p.ab_fmt, 0, 0);
-            bool ok = true;
-            for (int kb = 0; kb < nk; ++kb) {
-                const int s = kb % STAGES;
-                ok = mbar_wait(smem_u32(&tail->full[s]), (kb / STAGES) & 1, abort, p.status,
-                               ST_TIMEOUT_MMA, kb);
-                if (!ok) break;
-                tc_fence_after();
-                const uint32_t a = smem_u32(sA(s)), b = smem_u32(sB(s));
+        // The whole warp runs the issuer's loop and one elected lane issues,
+        // keeping descriptors warp-uniform; that lane alone waits on each
+        // barrier and the vote hands its outcome to the warp.
+        const bool elected = elect_one();
+        const uint32_t idesc = idesc_f16(BM, BN, p.ab_fmt, p.ab_fmt, 0, 0);
+        bool ok = true;
+        for (int kb = 0; kb < nk; ++kb) {
+            const int s = kb % STAGES;
+            bool r = true;
+            if (elected)
+                r = mbar_wait(smem_u32(&tail->full[s]), (kb / STAGES) & 1, abort, p.status,
+                              ST_TIMEOUT_MMA, kb);
+            ok = __all_sync(0xFFFFFFFFu, r);
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t a = smem_u32(sA(s)), b = smem_u32(sB(s));
+            if (elected) {
 #pragma unroll
                 for (int k = 0; k < BK / 16; ++k)
                     mma_ss(tmem, desc_k(a + 32 * k), desc_k(b + 32 * k), idesc,
                            (kb > 0 || k > 0) ? 1u : 0u);
-                // Release the stage only if the producers will refill it, so no
-                // arrival lands after the CTA has finished.
+                // Release the stage only if the producers will refill it, so
+                // no arrival lands after the CTA has finished.
                 if (kb + STAGES < nk) mma_commit(smem_u32(&tail->empty[s]));
             }
+            __syncwarp();
+        }
+        if (elected) {
             if (ok) {
                 mma_commit(smem_u32(&tail->acc_full[0]));
             } else {
@@ -412,6 +422,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_wait(smem_u32(&tail->drain), 0, nullptr, p.status, ST_TIMEOUT_DRAIN, 0xD);
             }
         }
+        __syncwarp();
     } else {
         constexpr unsigned kFull = 0xFFFFFFFFu;
         const int sub = warp & 3;
@@ -644,42 +655,51 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            const uint32_t idesc = idesc_f16(BM, BN, p.ab_fmt, p.ab_fmt, 0, 0);
-            const int total_g = mine * nk;
-            int g = 0;
-            bool ok = true;
-            for (int j = 0; j < mine && ok; ++j) {
-                const int b = j & 1, use = j >> 1;
-                if (use > 0 && !mbar_wait(smem_u32(&tail->acc_empty[b]), (use - 1) & 1, abort,
-                                          p.status, ST_TIMEOUT_MMA, 0x100 + j)) {
-                    ok = false;
-                    break;
-                }
+        // whole-warp issuer loop, one elected lane issues and waits (see
+        // gemm_kernel)
+        const bool elected = elect_one();
+        auto wait_all = [&](uint32_t bar, uint32_t parity, uint32_t where) -> bool {
+            bool r = true;
+            if (elected) r = mbar_wait(bar, parity, abort, p.status, ST_TIMEOUT_MMA, where);
+            return __all_sync(0xFFFFFFFFu, r);
+        };
+        const uint32_t idesc = idesc_f16(BM, BN, p.ab_fmt, p.ab_fmt, 0, 0);
+        const int total_g = mine * nk;
+        int g = 0;
+        bool ok = true;
+        for (int j = 0; j < mine && ok; ++j) {
+            const int b = j & 1, use = j >> 1;
+            if (use > 0 && !wait_all(smem_u32(&tail->acc_empty[b]), (use - 1) & 1, 0x100 + j)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t acc = tmem + static_cast<uint32_t>(b) * L::kTmemCols;
+            for (int kb = 0; kb < nk; ++kb, ++g) {
+                const int s = g % STAGES;
+                ok = wait_all(smem_u32(&tail->full[s]), (g / STAGES) & 1, g);
+                if (!ok) break;
                 tc_fence_after();
-                const uint32_t acc = tmem + static_cast<uint32_t>(b) * L::kTmemCols;
-                for (int kb = 0; kb < nk; ++kb, ++g) {
-                    const int s = g % STAGES;
-                    ok = mbar_wait(smem_u32(&tail->full[s]), (g / STAGES) & 1, abort, p.status,
-                                   ST_TIMEOUT_MMA, g);
-                    if (!ok) break;
-                    tc_fence_after();
-                    const uint32_t a = smem_u32(sA(s)), bb = smem_u32(sB(s));
+                const uint32_t a = smem_u32(sA(s)), bb = smem_u32(sB(s));
+                if (elected) {
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k)
                         mma_ss(acc, desc_k(a + 32 * k), desc_k(bb + 32 * k), idesc,
                                (kb > 0 || k > 0) ? 1u : 0u);
-                    // release the stage only if the producer will refill it, so
-                    // no arrival lands after the CTA has finished
+                    // release the stage only if the producer will refill it,
+                    // so no arrival lands after the CTA has finished
                     if (g + STAGES < total_g) mma_commit(smem_u32(&tail->empty[s]));
                 }
-                if (ok) mma_commit(smem_u32(&tail->acc_full[b]));
+                __syncwarp();
             }
-            if (!ok) {
-                mma_commit(smem_u32(&tail->drain));
-                mbar_wait(smem_u32(&tail->drain), 0, nullptr, p.status, ST_TIMEOUT_DRAIN, 0xD);
-            }
+            if (ok && elected) mma_commit(smem_u32(&tail->acc_full[b]));
+            __syncwarp();
         }
+        if (!ok && elected) {
+            mma_commit(smem_u32(&tail->drain));
+            mbar_wait(smem_u32(&tail->drain), 0, nullptr, p.status, ST_TIMEOUT_DRAIN, 0xD);
+        }
+        __syncwarp();
     } else {
         const int sub = warp & 3;
         const int row = sub * 32 + lane;

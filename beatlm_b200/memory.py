@@ -109,13 +109,13 @@ class MemoryPlan:
             if err.kind:
                 raise PlanError(err.kind, err.id, err.a, err.b, N.last_error())
             raise N.BackendError(rc, N.last_error())
-        self._h = handle
+        self._h, self._lib = handle, N.lib()  # the library outlives module teardown
         self._ids = [t.id for t in tensors]
 
     def __del__(self):
         h = getattr(self, "_h", None)
         if h:
-            N.lib().bl_plan_destroy(h)
+            self._lib.bl_plan_destroy(h)
             self._h = None
 
     @property
@@ -179,10 +179,11 @@ class Arenas:
         handle = ctypes.c_void_p()
         N.check(N.lib().bl_arenas_create(plan.handle, device, ctypes.byref(handle)))
         self._h, self.device, self.plan = handle, device, plan
+        self._lib = N.lib()  # the library outlives module teardown
 
     def close(self):
         if getattr(self, "_h", None):
-            N.lib().bl_arenas_destroy(self._h)
+            self._lib.bl_arenas_destroy(self._h)
             self._h = None
 
     __del__ = close
