@@ -113,10 +113,14 @@ struct SmemTail {
 
 constexpr size_t kSmemBytes = 1024 /*align slack*/ + QT * kTileBytes /*Q*/ +
                               STAGES * 2 * kTileBytes /*K,V*/ + sizeof(SmemTail);
-// Cluster combine: a row's partial (64 O values, then max and sum) in the
-// K/V ring, 68 floats apart so eight threads' 16-byte accesses hit distinct
-// banks.
-constexpr int kPartStride = HD + 4;
+// Cluster combine: a row's partial is 17 float4s (64 O values, then max and
+// sum), stored k-major in the K/V ring: float4 k of every row of a rank's
+// block is contiguous, so a warp's remote store of one float4 per row covers
+// 512 consecutive bytes (row-major rows made it 32 separate 16-byte pieces,
+// measured 3 us for the push at ViT-S), and the owner's reads are
+// conflict-free.
+constexpr int kPartVec = HD / 4 + 1;
+constexpr int kPartStride = 4 * kPartVec;  // floats per row
 constexpr int kMaxClusterSplits = 8;  // portable cluster size
 // A CTA receives splits * ceil(8 / splits) warps of 32 rows of partials, at
 // most 14 warps (7 splits); they live in the K/V ring.
@@ -521,12 +525,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int slot = ((crow >> 5) / p.splits) * 32 + (crow & 31);
             const int slots = ((ROWS / 32 + p.splits - 1) / p.splits) * 32;  // rows per owner
             if (store && owner != static_cast<int>(me)) {
+                // float4 v of this row at [me][v][slot]
                 const uint32_t local =
-                    smem_u32(sK) + static_cast<uint32_t>((me * slots + slot) * kPartStride * 4);
+                    smem_u32(sK) + static_cast<uint32_t>((me * kPartVec * slots + slot) * 16);
                 const uint32_t dst = dsmem_addr(local, static_cast<uint32_t>(owner));
+                const uint32_t vstep = static_cast<uint32_t>(slots * 16);
 #pragma unroll
-                for (int k = 0; k < HD; k += 4) dsmem_st4(dst + 4 * k, o[k], o[k + 1], o[k + 2], o[k + 3]);
-                dsmem_st2(dst + 4 * HD, ok ? m_used : -INFINITY, l);
+                for (int k = 0; k < HD; k += 4)
+                    dsmem_st4(dst + (k / 4) * vstep, o[k], o[k + 1], o[k + 2], o[k + 3]);
+                dsmem_st2(dst + (HD / 4) * vstep, ok ? m_used : -INFINITY, l);
             }
             do_store = false;
         } else if (p.splits > 1) {
@@ -595,12 +602,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (store && owner == static_cast<int>(me)) {
                 const int slot = ((crow >> 5) / p.splits) * 32 + (crow & 31);
                 const int slots = ((ROWS / 32 + p.splits - 1) / p.splits) * 32;
-                const float* part = reinterpret_cast<const float*>(sK);  // [rank][slots][kPartStride]
+                // [rank][float4 v][slot]
+                const float4* part = reinterpret_cast<const float4*>(sK);
+                auto vec = [&](int s, int v) -> const float4& {
+                    return part[(s * kPartVec + v) * slots + slot];
+                };
                 float mxs = ok ? m_used : -INFINITY;
 #pragma unroll
                 for (int s = 0; s < kMaxClusterSplits; ++s)
                     if (s < p.splits && s != static_cast<int>(me))
-                        mxs = fmaxf(mxs, part[(s * slots + slot) * kPartStride + HD]);
+                        mxs = fmaxf(mxs, vec(s, HD / 4).x);
                 // splits in rank order whoever owns the row, so every row
                 // partition of the launch gives the same bits
                 float acc[HD];
@@ -616,13 +627,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int k = 0; k < HD; ++k) acc[k] += w * o[k];
                         continue;
                     }
-                    const float* src = part + (s * slots + slot) * kPartStride;
-                    const float2 ml = *reinterpret_cast<const float2*>(src + HD);
+                    const float4 ml = vec(s, HD / 4);
                     const float w = ex2(ml.x - mxs);
                     lsum += w * ml.y;
 #pragma unroll
                     for (int k = 0; k < HD; k += 4) {
-                        const float4 v = *reinterpret_cast<const float4*>(src + k);
+                        const float4 v = vec(s, k / 4);
                         acc[k] += w * v.x;
                         acc[k + 1] += w * v.y;
                         acc[k + 2] += w * v.z;
