@@ -62,19 +62,31 @@ struct Params {
     int stats_parts;
     const float2* ln_stats;  // LN prologue: [row][ln_stats_parts] partials of x
     int ln_stats_parts;
+    int tma_store;  // persistent kernel: rows leave through the output tensor map
     Status* status;
 };
 
-template <int BN>
+// A stage holds KC k-blocks: KC A tiles, then KC B tiles, each a 128-byte
+// swizzled K-major tile. One TMA copy brings all KC tiles of an operand (a
+// 3-D view whose third dimension steps 64 columns): a thread's bulk copies
+// complete one after another, each in about 530 SM clocks whatever its size
+// up to 64 KiB (measured), so bytes per copy set a CTA's feed rate.
+// Output staging of the persistent kernel's epilogue: one 32 x 32 block of
+// up to 4-byte values per epilogue warp, stored to global memory by TMA.
+constexpr uint32_t kEpiBlock = 32 * 32 * 4;
+constexpr uint32_t kEpiBytes = 4 * kEpiBlock;
+
+template <int BN, int KC = 1, bool kEpi = false>
 struct Layout {
     static constexpr uint32_t kTileB = BN * BK * 2;
-    static constexpr uint32_t kStage = kTileA + kTileB;
+    static constexpr uint32_t kStage = KC * (kTileA + kTileB);
+    static constexpr uint32_t kReserve = 4096 + (kEpi ? kEpiBytes : 0);
     // As deep a TMA ring as shared memory holds (4 KiB kept for the barriers,
-    // the staged epilogue vectors and the alignment slack): a CTA's k-loop is
-    // bound by the bytes it has in flight, one SM's share of L2 latency.
+    // the staged epilogue vectors and the alignment slack, plus the output
+    // staging).
     static constexpr int kStages =
-        static_cast<int>((kSmemLimit - 4096) / kStage) < kMaxStages
-            ? static_cast<int>((kSmemLimit - 4096) / kStage)
+        static_cast<int>((kSmemLimit - kReserve) / kStage) < kMaxStages
+            ? static_cast<int>((kSmemLimit - kReserve) / kStage)
             : kMaxStages;
     static constexpr uint32_t kTmemCols = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
 };
@@ -93,9 +105,10 @@ struct Tail {
     alignas(16) float chan[128];
 };
 
-template <int BN>
+template <int BN, int KC = 1, bool kEpi = false>
 constexpr size_t smem_bytes() {
-    return 1024 + Layout<BN>::kStages * Layout<BN>::kStage + sizeof(Tail);
+    using L = Layout<BN, KC, kEpi>;
+    return 1024 + L::kStages * L::kStage + (kEpi ? kEpiBytes : 0) + sizeof(Tail);
 }
 
 __device__ __forceinline__ uint64_t desc_k(uint32_t addr) { return sdesc_sw128(addr, 16, 1024); }
@@ -217,19 +230,28 @@ __device__ __forceinline__ void prefetch_residual(const Params& p, const RowCtx&
 
 // The epilogue chain of one accumulator row: TMEM columns 32 at a time, then
 // bias, activation, scale, channel scale, residual and the store.
+// `tmo` (may be null): the output tensor map. Each warp then writes its
+// 32 x 32 block into `buf`, swizzled as the map's 128-byte (4-byte values) or
+// 64-byte (2-byte values) swizzle lays it out, so a quarter-warp's 16-byte
+// writes hit distinct banks, and one lane stores the block with first output
+// row `box_row`; rows past the output are clipped by the map. Without it each
+// thread stores its own row.
 template <int BN>
 __device__ __forceinline__ void store_tile(const Params& p, const Tail* tail, uint32_t t_lane,
-                                           int n0, const RowCtx& rc, const float* rv0) {
+                                           int n0, const RowCtx& rc, const float* rv0,
+                                           const CUtensorMap* tmo = nullptr,
+                                           uint8_t* buf = nullptr, int box_row = 0) {
     const bool live = rc.live;
     const long long orow = rc.orow, res_row = rc.res_row;
     const size_t res_esz = p.res_dtype == BL_F32 ? 4 : 2;
+    const int lane = lane_id();
     float run_mean = 0.0f, run_m2 = 0.0f;  // row statistics of the stored slice
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
         tmem_ld32(t_lane + c * 32, r);
         tmem_wait_ld();
-        if (!live) continue;
+        if (!live && tmo == nullptr) continue;
         const int col = n0 + c * 32;
         float v[32];
 #pragma unroll
@@ -262,7 +284,7 @@ __device__ __forceinline__ void store_tile(const Params& p, const Tail* tail, ui
                 v[i] *= s.x; v[i + 1] *= s.y; v[i + 2] *= s.z; v[i + 3] *= s.w;
             }
         }
-        if (p.residual != nullptr) {
+        if (p.residual != nullptr && live) {
             if (c == 0) {
 #pragma unroll
                 for (int i = 0; i < 32; ++i) v[i] += rv0[i];
@@ -293,7 +315,30 @@ __device__ __forceinline__ void store_tile(const Params& p, const Tail* tail, ui
             run_m2 += cm2 + delta * delta * (na * 32.0f / nab);
         }
         const int dt = col >= p.split_col ? p.out_dtype_hi : p.out_dtype;
-        if (dt == BL_F32) {
+        if (tmo != nullptr) {
+            if (lane == 0) bulk_wait_read();  // the previous block has left `buf`
+            __syncwarp();
+            if (dt == BL_F32) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    *reinterpret_cast<float4*>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+                        make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    *reinterpret_cast<uint4*>(buf + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) =
+                        make_uint4(pack2(v[8 * j], v[8 * j + 1], dt),
+                                   pack2(v[8 * j + 2], v[8 * j + 3], dt),
+                                   pack2(v[8 * j + 4], v[8 * j + 5], dt),
+                                   pack2(v[8 * j + 6], v[8 * j + 7], dt));
+            }
+            fence_proxy_async_smem();  // the writes above, seen by the bulk copy
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_2d(tmo, smem_u32(buf), col, box_row);
+                bulk_commit();
+            }
+        } else if (dt == BL_F32) {
             float4* o = reinterpret_cast<float4*>(static_cast<float*>(p.out) +
                                                   orow * p.out_ld + col);
 #pragma unroll
@@ -566,24 +611,27 @@ __device__ __forceinline__ bool epilogue_all(bool ok) {
 // epilogue warps drain tile j from one while the MMA thread fills tile j + 1
 // in the other, and the TMA ring runs on across tiles, so the epilogue and the
 // CTA's set-up leave the critical path once a CTA has more than one tile.
-template <int BN>
+template <int BN, int KC>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_persistent(const __grid_constant__ CUtensorMap tm_a,
-                    const __grid_constant__ CUtensorMap tm_b, const Params p) {
-    using L = Layout<BN>;
+                    const __grid_constant__ CUtensorMap tm_b,
+                    const __grid_constant__ CUtensorMap tm_o, const Params p) {
+    using L = Layout<BN, KC, true>;
     constexpr int STAGES = L::kStages;
+    static_assert(STAGES >= 2, "a stage ring needs two stages");
     constexpr uint32_t kCols = 2 * L::kTmemCols;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    Tail* tail = reinterpret_cast<Tail*>(smem + STAGES * L::kStage);
+    uint8_t* epi = smem + STAGES * L::kStage;  // output staging, kEpiBytes
+    Tail* tail = reinterpret_cast<Tail*>(epi + kEpiBytes);
     volatile int* abort = &tail->abort;
     auto sA = [&](int s) { return smem + s * L::kStage; };
-    auto sB = [&](int s) { return smem + s * L::kStage + kTileA; };
+    auto sB = [&](int s) { return smem + s * L::kStage + KC * kTileA; };
 
     const int warp = warp_id();
     const int lane = lane_id();
-    const int nk = p.K / BK;
+    const int nk = p.K / (BK * KC);  // stages per tile (the host makes KC divide K / 64)
     const int total = p.m_tiles * (p.N / BN);
     const int mine = static_cast<int>(blockIdx.x) < total
                          ? (total - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
@@ -613,6 +661,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_proxy_async_smem();
         tma_prefetch_desc(&tm_a);
         tma_prefetch_desc(&tm_b);
+        if (p.tma_store) tma_prefetch_desc(&tm_o);
     }
     if (warp == 1) {
         tmem_alloc(smem_u32(&tail->tmem_base), kCols);
@@ -626,34 +675,42 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_wait();
 
     if (warp == 0) {
-        if (lane == 0) {
-            int g = 0;  // k-blocks whose loads were started, over all tiles
-            bool ok = true;
-            for (int j = 0; j < mine && ok; ++j) {
-                const int m0 = tile_m0(j), n0 = tile_n0(j);
-                for (int kb = 0; kb < nk; ++kb, ++g) {
-                    const int s = g % STAGES;
-                    if (g >= STAGES &&
-                        !mbar_wait(smem_u32(&tail->empty[s]), ((g / STAGES) - 1) & 1, abort,
-                                   p.status, ST_TIMEOUT_TMA, g)) {
-                        ok = false;
-                        break;
-                    }
-                    const uint32_t bar = smem_u32(&tail->full[s]);
-                    mbar_arrive_expect_tx(bar, kTileA + L::kTileB);
-                    tma_load_2d(smem_u32(sA(s)), &tm_a, kb * BK, m0, bar);
-                    tma_load_2d(smem_u32(sB(s)), &tm_b, kb * BK, n0, bar);
+        // The whole warp runs the producer loop in step; lane 0 arms the
+        // stage and copies A, lane 1 copies B, so the two copies of a stage
+        // are in flight together (each thread's copies are serial). Lane 0
+        // alone waits for the stage to be free; the vote hands the outcome
+        // to the warp, so both lanes start the same stages.
+        int g = 0;  // stages whose loads were started, over all tiles
+        bool ok = true;
+        for (int j = 0; j < mine && ok; ++j) {
+            const int m0 = tile_m0(j), n0 = tile_n0(j);
+            for (int kb = 0; kb < nk; ++kb, ++g) {
+                const int s = g % STAGES;
+                bool r = true;
+                if (lane == 0 && g >= STAGES)
+                    r = mbar_wait(smem_u32(&tail->empty[s]), ((g / STAGES) - 1) & 1, abort,
+                                  p.status, ST_TIMEOUT_TMA, g);
+                ok = __all_sync(0xFFFFFFFFu, r);
+                if (!ok) break;
+                const uint32_t bar = smem_u32(&tail->full[s]);
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(bar, L::kStage);
+                    tma_load_3d(smem_u32(sA(s)), &tm_a, 0, m0, kb * KC, bar);
+                } else if (lane == 1) {
+                    tma_load_3d(smem_u32(sB(s)), &tm_b, 0, n0, kb * KC, bar);
                 }
-            }
-            if (*abort) {
-                // let every started copy land before shared memory is released
-                for (int s = 0; s < STAGES && s < g; ++s) {
-                    const int uses = (g - s - 1) / STAGES + 1;
-                    mbar_wait(smem_u32(&tail->full[s]), (uses - 1) & 1, nullptr, p.status,
-                              ST_TIMEOUT_DRAIN, s);
-                }
+                __syncwarp();
             }
         }
+        if (lane == 0 && *abort) {
+            // let every started copy land before shared memory is released
+            for (int s = 0; s < STAGES && s < g; ++s) {
+                const int uses = (g - s - 1) / STAGES + 1;
+                mbar_wait(smem_u32(&tail->full[s]), (uses - 1) & 1, nullptr, p.status,
+                          ST_TIMEOUT_DRAIN, s);
+            }
+        }
+        __syncwarp();
     } else if (warp == 1) {
         // whole-warp issuer loop, one elected lane issues and waits (see
         // gemm_kernel)
@@ -683,9 +740,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t a = smem_u32(sA(s)), bb = smem_u32(sB(s));
                 if (elected) {
 #pragma unroll
-                    for (int k = 0; k < BK / 16; ++k)
-                        mma_ss(acc, desc_k(a + 32 * k), desc_k(bb + 32 * k), idesc,
-                               (kb > 0 || k > 0) ? 1u : 0u);
+                    for (int c = 0; c < KC; ++c)
+#pragma unroll
+                        for (int k = 0; k < BK / 16; ++k)
+                            mma_ss(acc, desc_k(a + c * kTileA + 32 * k),
+                                   desc_k(bb + c * L::kTileB + 32 * k), idesc,
+                                   (kb > 0 || c > 0 || k > 0) ? 1u : 0u);
                     // release the stage only if the producer will refill it,
                     // so no arrival lands after the CTA has finished
                     if (g + STAGES < total_g) mma_commit(smem_u32(&tail->empty[s]));
@@ -719,11 +779,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             store_tile<BN>(p, tail,
                            tmem + static_cast<uint32_t>(b) * L::kTmemCols +
                                (static_cast<uint32_t>(sub * 32) << 16),
-                           n0, rc, rv0);
+                           n0, rc, rv0, p.tma_store ? &tm_o : nullptr, epi + sub * kEpiBlock,
+                           m0 + sub * 32 + p.out_row_offset);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&tail->acc_empty[b]));
         }
+        // stores complete before the staging is released and the kernel ends
+        if (p.tma_store && lane == 0) bulk_wait_all();
+        __syncwarp();
     }
 
     tc_fence_before();
@@ -746,21 +810,49 @@ int sm_count() {
     return n;
 }
 
+template <int BN, int KC>
+int prepare_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+                       const Params& p, Launch* out) {
+    constexpr size_t smem = smem_bytes<BN, KC, true>();
+    out->op = 2;
+    auto kern = gemm_persistent<BN, KC>;
+    BL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(smem)));
+    const int tiles = p.m_tiles * (p.N / BN);
+    const dim3 grid(std::min(tiles, sm_count()));
+    out->run = [=](cudaStream_t s) {
+        return launch_k(kern, grid, dim3(kThreads), smem, s, ta, tb, to, p);
+    };
+    return BL_OK;
+}
+
+template <int BN>
+int prepare_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+                       const Params& p, int kc, Launch* out) {
+    // only the depths whose ring holds two stages are built
+    if constexpr (Layout<BN, 4, true>::kStages >= 2)
+        if (kc == 4) return prepare_persistent<BN, 4>(ta, tb, to, p, out);
+    if constexpr (Layout<BN, 2, true>::kStages >= 2)
+        if (kc == 2) return prepare_persistent<BN, 2>(ta, tb, to, p, out);
+    if (kc != 1) return fail(BL_ERR_UNSUPPORTED, "gemm: no kernel for %d k-blocks per stage", kc);
+    return prepare_persistent<BN, 1>(ta, tb, to, p, out);
+}
+
+// k-blocks per stage of the persistent kernel: the most (4, 2, 1) that divide
+// K / 64 and still leave a ring of two stages beside the output staging.
+int pick_kc(int bn, uint32_t k) {
+    const uint32_t nk = k / BK;
+    for (int kc : {4, 2}) {
+        const uint32_t stage = kc * (kTileA + bn * BK * 2);
+        if (nk % kc == 0 && (kSmemLimit - 4096 - kEpiBytes) / stage >= 2) return kc;
+    }
+    return 1;
+}
+
 template <int BN, bool kLn>
 int prepare_t(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, Launch* out) {
     constexpr size_t smem = smem_bytes<BN>();
     out->op = 2;
-    if (!kLn) {
-        auto kern = gemm_persistent<BN>;
-        BL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem)));
-        const int tiles = p.m_tiles * (p.N / BN);
-        const dim3 grid(std::min(tiles, sm_count()));
-        out->run = [=](cudaStream_t s) {
-            return launch_k(kern, grid, dim3(kThreads), smem, s, ta, tb, p);
-        };
-        return BL_OK;
-    }
     auto kern = gemm_kernel<BN, kLn>;
     BL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(smem)));
@@ -866,14 +958,20 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
 
     CUtensorMap ta{}, tb{};
     int rc;
+    const int kc = ln ? 1 : pick_kc(bn, g.k);
+    const uint64_t ldb = g.ldb ? g.ldb : g.k;
     if (!ln) {
+        // Persistent kernel: 3-D views (64 columns, rows, 64-column block)
+        // so one copy brings kc consecutive k-blocks of 128 (A) or bn (B)
+        // rows.
         const uint64_t lda = g.lda ? g.lda : g.k;
-        const uint64_t dims[2] = {g.k, g.m};
-        const uint32_t box[2] = {BK, BM};
-        if ((rc = make_tmap_16bit_2d(&ta, g.a, dims, lda * 2, box)) != BL_OK) return rc;
-    }
-    {
-        const uint64_t ldb = g.ldb ? g.ldb : g.k;
+        const uint64_t da[3] = {BK, g.m, g.k / BK}, sa[2] = {lda * 2, BK * 2};
+        const uint32_t ba[3] = {BK, BM, static_cast<uint32_t>(kc)};
+        if ((rc = make_tmap_16bit_3d(&ta, g.a, da, sa, ba)) != BL_OK) return rc;
+        const uint64_t db[3] = {BK, g.n, g.k / BK}, sb[2] = {ldb * 2, BK * 2};
+        const uint32_t bb[3] = {BK, static_cast<uint32_t>(bn), static_cast<uint32_t>(kc)};
+        if ((rc = make_tmap_16bit_3d(&tb, g.b, db, sb, bb)) != BL_OK) return rc;
+    } else {
         const uint64_t dims[2] = {g.k, g.n};
         const uint32_t box[2] = {BK, static_cast<uint32_t>(bn)};
         if ((rc = make_tmap_16bit_2d(&tb, g.b, dims, ldb * 2, box)) != BL_OK) return rc;
@@ -921,11 +1019,23 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
             default: return prepare_t<128, true>(ta, tb, p, out);
         }
     }
+    // Output rows leave through a tensor map when they form one strided 2-D
+    // array of a single element size (no row groups).
+    CUtensorMap to{};
+    const int esz = static_cast<int>(dtype_size(dts[0]));
+    if (g.out_group_rows == 0 && dtype_size(dts[1]) == dtype_size(dts[0])) {
+        const uint64_t dims[2] = {g.n, static_cast<uint64_t>(g.m) + g.out_row_offset};
+        const uint32_t box[2] = {32, 32};
+        if ((rc = make_tmap_store_2d(&to, g.out, esz, dims, out_ld * esz, box,
+                                     esz == 4 ? 128 : 64)) != BL_OK)
+            return rc;
+        p.tma_store = 1;
+    }
     switch (bn) {
-        case 32: return prepare_t<32, false>(ta, tb, p, out);
-        case 64: return prepare_t<64, false>(ta, tb, p, out);
-        case 96: return prepare_t<96, false>(ta, tb, p, out);
-        default: return prepare_t<128, false>(ta, tb, p, out);
+        case 32: return prepare_persistent<32>(ta, tb, to, p, kc, out);
+        case 64: return prepare_persistent<64>(ta, tb, to, p, kc, out);
+        case 96: return prepare_persistent<96>(ta, tb, to, p, kc, out);
+        default: return prepare_persistent<128>(ta, tb, to, p, kc, out);
     }
 }
 

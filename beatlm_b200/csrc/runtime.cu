@@ -65,7 +65,9 @@ Status* status_ptr() {
 }
 
 static int encode(CUtensorMap* map, const void* base, cuuint32_t rank, const cuuint64_t* dims,
-                  const cuuint64_t* strides, const cuuint32_t* box) {
+                  const cuuint64_t* strides, const cuuint32_t* box,
+                  CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_UINT16,
+                  CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
     EncodeTiledFn fn = encode_fn();
     if (fn == nullptr) return fail(BL_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
     if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
@@ -75,9 +77,8 @@ static int encode(CUtensorMap* map, const void* base, cuuint32_t rank, const cuu
             return fail(BL_ERR_INVALID, "tensor stride %llu is not a multiple of 16 bytes",
                         (unsigned long long)strides[i]);
     cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, rank, const_cast<void*>(base), dims,
-                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+    CUresult r = fn(map, dtype, rank, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(BL_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     return BL_OK;
@@ -89,6 +90,16 @@ int make_tmap_16bit_3d(CUtensorMap* map, const void* base, const uint64_t dims[3
     cuuint64_t s[2] = {strides_bytes[0], strides_bytes[1]};
     cuuint32_t b[3] = {box[0], box[1], box[2]};
     return encode(map, base, 3, d, s, b);
+}
+
+int make_tmap_store_2d(CUtensorMap* map, void* base, int esz, const uint64_t dims[2],
+                       uint64_t row_stride_bytes, const uint32_t box[2], int swizzle_bytes) {
+    cuuint64_t d[2] = {dims[0], dims[1]};
+    cuuint64_t s[1] = {row_stride_bytes};
+    cuuint32_t b[2] = {box[0], box[1]};
+    return encode(map, base, 2, d, s, b,
+                  esz == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16,
+                  swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
 }
 
 int make_tmap_16bit_2d(CUtensorMap* map, const void* base, const uint64_t dims[2],

@@ -118,6 +118,28 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int 
         : "memory");
 }
 
+// 2-D tiled bulk tensor store from this CTA's shared memory (bulk-group
+// completion: commit, then wait before the source is rewritten or the kernel
+// ends).
+__device__ __forceinline__ void tma_store_2d(const void* tmap, uint32_t src, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+            reinterpret_cast<uint64_t>(tmap)),
+        "r"(src), "r"(x), "r"(y)
+        : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// the shared-memory sources of all committed stores have been read
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// all committed stores are complete
+__device__ __forceinline__ void bulk_wait_all() {
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int x, int y,
                                             uint32_t bar) {
     asm volatile(
