@@ -108,6 +108,10 @@ class GemmArgs(ctypes.Structure):
         ("out_group_gap", ctypes.c_uint32), ("tile_n", ctypes.c_uint32),
         ("stats_out", ctypes.c_void_p), ("stats_parts", ctypes.c_uint32),
         ("ln_stats", ctypes.c_void_p), ("ln_stats_parts", ctypes.c_uint32),
+        ("norm_out", ctypes.c_void_p), ("norm_out_dtype", ctypes.c_int32),
+        ("norm_out_ld", ctypes.c_uint64), ("norm_gamma", ctypes.c_void_p),
+        ("norm_beta", ctypes.c_void_p), ("norm_eps", ctypes.c_float),
+        ("norm_sync", ctypes.c_void_p), ("norm_sync_bytes", ctypes.c_uint64),
     ]
 
 
@@ -174,6 +178,7 @@ SIGNATURES.update({
                                               ctypes.POINTER(_sz), ctypes.POINTER(_sz)]),
     "bl_timer_get_stats": (ctypes.c_int, [_vp, ctypes.POINTER(TimerStats)]),
     "bl_gemm": (ctypes.c_int, [ctypes.POINTER(GemmArgs), ctypes.c_void_p]),
+    "bl_gemm_norm_sync_bytes": (ctypes.c_uint64, [ctypes.POINTER(GemmArgs)]),
     "bl_layernorm": (ctypes.c_int, [ctypes.POINTER(LayerNormArgs), ctypes.c_void_p]),
     "bl_patchify": (ctypes.c_int, [ctypes.POINTER(PatchifyArgs), ctypes.c_void_p]),
 })

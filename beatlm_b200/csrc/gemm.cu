@@ -63,6 +63,16 @@ struct Params {
     const float2* ln_stats;  // LN prologue: [row][ln_stats_parts] partials of x
     int ln_stats_parts;
     int tma_store;  // persistent kernel: rows leave through the output tensor map
+    // LayerNorm of the stored rows in the epilogue (32-column tiles, one tile
+    // per CTA): per-slice statistics meet in norm_stats, row tiles count their
+    // published slices in norm_ctr[2 * tile] and their readers in [2 * tile + 1]
+    void* norm_out;
+    int norm_dtype;
+    const float* norm_gamma;
+    const float* norm_beta;
+    float norm_eps;
+    unsigned* norm_ctr;
+    float2* norm_stats;
     Status* status;
 };
 
@@ -240,7 +250,8 @@ template <int BN>
 __device__ __forceinline__ void store_tile(const Params& p, const Tail* tail, uint32_t t_lane,
                                            int n0, const RowCtx& rc, const float* rv0,
                                            const CUtensorMap* tmo = nullptr,
-                                           uint8_t* buf = nullptr, int box_row = 0) {
+                                           uint8_t* buf = nullptr, int box_row = 0,
+                                           float* keep = nullptr) {
     const bool live = rc.live;
     const long long orow = rc.orow, res_row = rc.res_row;
     const size_t res_esz = p.res_dtype == BL_F32 ? 4 : 2;
@@ -313,6 +324,10 @@ __device__ __forceinline__ void store_tile(const Params& p, const Tail* tail, ui
             const float delta = cm - run_mean;
             run_mean += delta * (32.0f / nab);
             run_m2 += cm2 + delta * delta * (na * 32.0f / nab);
+        }
+        if (keep != nullptr && c == 0) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) keep[i] = v[i];
         }
         const int dt = col >= p.split_col ? p.out_dtype_hi : p.out_dtype;
         if (tmo != nullptr) {
@@ -605,6 +620,104 @@ __device__ __forceinline__ bool epilogue_all(bool ok) {
     return r != 0;
 }
 
+constexpr int kMaxNormParts = 16;  // epilogue LayerNorm rows of at most 512 columns
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// The epilogue LayerNorm of one 32-column tile (persistent kernel, every
+// tile of the launch resident at once): publish this slice's (mean, M2) of
+// each row, wait until the row tile's other column tiles have published
+// theirs (a bounded spin on a counter), merge them in column order (Chan et
+// al.; every tile of the row gets the same bits), normalise the slice's 32
+// values `v` and store them through `tmn`. The last tile of the row tile to
+// finish zeroes its counters for the next launch. Returns false when the
+// wait ran out.
+__device__ bool norm_tile(const Params& p, const CUtensorMap* tmn, const float* v, bool live,
+                          int m0, int n0, int row, uint8_t* buf, volatile int* abort) {
+    const int parts = p.N / 32;
+    const int grow = m0 + row;
+    const int lane = lane_id();
+    unsigned* ctr = p.norm_ctr + 2 * (m0 / BM);
+    if (live) {
+        float sum = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sum += v[i];
+        const float mean = sum * (1.0f / 32.0f);
+        float m2 = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) m2 += (v[i] - mean) * (v[i] - mean);
+        p.norm_stats[static_cast<size_t>(grow) * parts + n0 / 32] = make_float2(mean, m2);
+    }
+    epilogue_all(true);  // the tile's rows are written
+    bool ok = true;
+    if (row == 0) {
+        __threadfence();  // ... and published (cumulative over the barrier)
+        atomicAdd(ctr, 1u);
+        const long long t0 = clock64();
+        while (ld_acquire_gpu(ctr) < static_cast<unsigned>(parts)) {
+            if (*abort || clock64() - t0 > kWaitLimitCycles) {
+                if (!*abort) record_status(p.status, ST_TIMEOUT_SOFTMAX, 0x300 + m0 / BM);
+                *abort = 1;
+                ok = false;
+                break;
+            }
+            __nanosleep(32);
+        }
+    }
+    if (!epilogue_all(ok)) return false;
+    float mu = 0.0f, m2 = 0.0f;
+    if (live) {
+        // every partial's load is issued before the merge (one L2 round trip)
+        const float2* st = p.norm_stats + static_cast<size_t>(grow) * parts;
+        float2 part[kMaxNormParts];
+#pragma unroll
+        for (int q = 0; q < kMaxNormParts; ++q)
+            if (q < parts) part[q] = __ldcg(st + q);
+#pragma unroll
+        for (int q = 0; q < kMaxNormParts; ++q) {
+            if (q < parts) {
+                const float na = 32.0f * static_cast<float>(q), nab = na + 32.0f;
+                const float delta = part[q].x - mu;
+                mu += delta * (32.0f / nab);
+                m2 += part[q].y + delta * delta * (na * 32.0f / nab);
+            }
+        }
+    }
+    const float rstd = rsqrtf(m2 / static_cast<float>(p.N) + p.norm_eps);
+    uint32_t y[16];
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+        const float4 g = __ldg(reinterpret_cast<const float4*>(p.norm_gamma + n0 + i));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(p.norm_beta + n0 + i));
+        y[i / 2] = pack2((v[i] - mu) * rstd * g.x + b.x, (v[i + 1] - mu) * rstd * g.y + b.y,
+                         p.norm_dtype);
+        y[i / 2 + 1] = pack2((v[i + 2] - mu) * rstd * g.z + b.z,
+                             (v[i + 3] - mu) * rstd * g.w + b.w, p.norm_dtype);
+    }
+    if (lane == 0) bulk_wait_read();  // the output block has left `buf`
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        *reinterpret_cast<uint4*>(buf + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) =
+            make_uint4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+        tma_store_2d(tmn, smem_u32(buf), n0, m0 + (row & ~31));
+        bulk_commit();
+    }
+    epilogue_all(true);  // every reader of this tile is past the statistics
+    if (row == 0 && atomicAdd(ctr + 1, 1u) == static_cast<unsigned>(parts) - 1) {
+        ctr[0] = 0u;
+        ctr[1] = 0u;
+    }
+    return true;
+}
+
 // The persistent form, for A loaded by TMA: one CTA per SM walks tiles
 // t = blockIdx.x, blockIdx.x + gridDim.x, ... of this launch (tile t is row
 // tile t % m_tiles, column tile t / m_tiles). Two TMEM accumulators: the
@@ -615,7 +728,8 @@ template <int BN, int KC>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_persistent(const __grid_constant__ CUtensorMap tm_a,
                     const __grid_constant__ CUtensorMap tm_b,
-                    const __grid_constant__ CUtensorMap tm_o, const Params p) {
+                    const __grid_constant__ CUtensorMap tm_o,
+                    const __grid_constant__ CUtensorMap tm_n, const Params p) {
     using L = Layout<BN, KC, true>;
     constexpr int STAGES = L::kStages;
     static_assert(STAGES >= 2, "a stage ring needs two stages");
@@ -776,14 +890,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 ST_TIMEOUT_SOFTMAX, 0x200 + j);
             if (!epilogue_all(ok)) break;
             tc_fence_after();
+            float keep[32];
             store_tile<BN>(p, tail,
                            tmem + static_cast<uint32_t>(b) * L::kTmemCols +
                                (static_cast<uint32_t>(sub * 32) << 16),
                            n0, rc, rv0, p.tma_store ? &tm_o : nullptr, epi + sub * kEpiBlock,
-                           m0 + sub * 32 + p.out_row_offset);
+                           m0 + sub * 32 + p.out_row_offset,
+                           p.norm_out != nullptr ? keep : nullptr);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&tail->acc_empty[b]));
+            if (p.norm_out != nullptr &&
+                !norm_tile(p, &tm_n, keep, rc.live, m0, n0, row, epi + sub * kEpiBlock, abort))
+                break;
         }
         // stores complete before the staging is released and the kernel ends
         if (p.tma_store && lane == 0) bulk_wait_all();
@@ -812,7 +931,7 @@ int sm_count() {
 
 template <int BN, int KC>
 int prepare_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
-                       const Params& p, Launch* out) {
+                       const CUtensorMap& tn, const Params& p, Launch* out) {
     constexpr size_t smem = smem_bytes<BN, KC, true>();
     out->op = 2;
     auto kern = gemm_persistent<BN, KC>;
@@ -821,21 +940,21 @@ int prepare_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
     const int tiles = p.m_tiles * (p.N / BN);
     const dim3 grid(std::min(tiles, sm_count()));
     out->run = [=](cudaStream_t s) {
-        return launch_k(kern, grid, dim3(kThreads), smem, s, ta, tb, to, p);
+        return launch_k(kern, grid, dim3(kThreads), smem, s, ta, tb, to, tn, p);
     };
     return BL_OK;
 }
 
 template <int BN>
 int prepare_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
-                       const Params& p, int kc, Launch* out) {
+                       const CUtensorMap& tn, const Params& p, int kc, Launch* out) {
     // only the depths whose ring holds two stages are built
     if constexpr (Layout<BN, 4, true>::kStages >= 2)
-        if (kc == 4) return prepare_persistent<BN, 4>(ta, tb, to, p, out);
+        if (kc == 4) return prepare_persistent<BN, 4>(ta, tb, to, tn, p, out);
     if constexpr (Layout<BN, 2, true>::kStages >= 2)
-        if (kc == 2) return prepare_persistent<BN, 2>(ta, tb, to, p, out);
+        if (kc == 2) return prepare_persistent<BN, 2>(ta, tb, to, tn, p, out);
     if (kc != 1) return fail(BL_ERR_UNSUPPORTED, "gemm: no kernel for %d k-blocks per stage", kc);
-    return prepare_persistent<BN, 1>(ta, tb, to, p, out);
+    return prepare_persistent<BN, 1>(ta, tb, to, tn, p, out);
 }
 
 // k-blocks per stage of the persistent kernel: the most (4, 2, 1) that divide
@@ -861,6 +980,12 @@ int prepare_t(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, Lau
         return launch_k(kern, grid, dim3(kThreads), smem, s, ta, tb, p);
     };
     return BL_OK;
+}
+
+// norm_sync: the counters (two per row tile), then float2 [m][n / 32]
+uint64_t norm_ctr_bytes(uint32_t m) { return ((8ull * ((m + BM - 1) / BM)) + 15) & ~15ull; }
+uint64_t norm_sync_bytes(uint32_t m, uint32_t n) {
+    return norm_ctr_bytes(m) + 8ull * m * (n / 32);
 }
 
 int pick_bn(const bl_gemm_args& g) {
@@ -915,9 +1040,46 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
             return fail(BL_ERR_INVALID, "gemm: stats output must be 8-byte aligned");
         bn = static_cast<int>(w);
     }
+    const bool norm = g.norm_out != nullptr;
+    if (norm) {
+        if (g.tile_n && g.tile_n != 32)
+            return fail(BL_ERR_UNSUPPORTED, "gemm: the epilogue LayerNorm needs 32-column tiles");
+        bn = 32;
+    }
     if (bn == 0 || g.n % bn != 0 || (bn != 32 && bn != 64 && bn != 96 && bn != 128))
         return fail(BL_ERR_UNSUPPORTED, "gemm: N=%u has no tile width (32/64/96/128)", g.n);
     const bool ln = g.ln_x != nullptr;
+    if (norm) {
+        const uint64_t tiles = ((static_cast<uint64_t>(g.m) + BM - 1) / BM) * (g.n / 32);
+        if (ln || g.out_dtype != BL_F32 || (g.split_col > 0 && g.split_col < g.n) ||
+            g.out_group_rows != 0 || g.stats_out != nullptr)
+            return fail(BL_ERR_UNSUPPORTED,
+                        "gemm: the epilogue LayerNorm needs an f32 output of one type, no row "
+                        "groups, no LayerNorm prologue and no statistics output");
+        if (g.n > 32 * kMaxNormParts)
+            return fail(BL_ERR_UNSUPPORTED, "gemm: the epilogue LayerNorm takes rows of at most %d "
+                        "columns", 32 * kMaxNormParts);
+        if (tiles > static_cast<uint64_t>(sm_count()))
+            return fail(BL_ERR_UNSUPPORTED,
+                        "gemm: the epilogue LayerNorm needs every tile resident (%llu tiles, %d "
+                        "SMs)", (unsigned long long)tiles, sm_count());
+        if (row_begin != 0 || row_end < g.m)
+            return fail(BL_ERR_UNSUPPORTED, "gemm: the epilogue LayerNorm covers whole launches");
+        if (g.norm_out_dtype != BL_F16 && g.norm_out_dtype != BL_BF16)
+            return fail(BL_ERR_INVALID, "gemm: LayerNorm output dtype %d (f16 or bf16)",
+                        g.norm_out_dtype);
+        const uint64_t nld = g.norm_out_ld ? g.norm_out_ld : g.n;
+        if ((reinterpret_cast<uintptr_t>(g.norm_out) & 15) || (nld * 2) % 16 ||
+            g.norm_gamma == nullptr || g.norm_beta == nullptr ||
+            (reinterpret_cast<uintptr_t>(g.norm_gamma) & 15) ||
+            (reinterpret_cast<uintptr_t>(g.norm_beta) & 15))
+            return fail(BL_ERR_INVALID,
+                        "gemm: LayerNorm output rows and gamma / beta must be 16-byte aligned");
+        if (g.norm_sync == nullptr || (reinterpret_cast<uintptr_t>(g.norm_sync) & 15) ||
+            g.norm_sync_bytes < norm_sync_bytes(g.m, g.n))
+            return fail(BL_ERR_INVALID, "gemm: norm_sync must be 16-byte aligned and hold %llu bytes",
+                        (unsigned long long)norm_sync_bytes(g.m, g.n));
+    }
     if (g.ln_stats != nullptr &&
         (!ln || g.ln_stats_parts == 0 || g.k % g.ln_stats_parts != 0 ||
          (reinterpret_cast<uintptr_t>(g.ln_stats) & 7)))
@@ -1019,6 +1181,22 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
             default: return prepare_t<128, true>(ta, tb, p, out);
         }
     }
+    CUtensorMap tn{};
+    if (norm) {
+        const uint64_t nld = g.norm_out_ld ? g.norm_out_ld : g.n;
+        const uint64_t dims[2] = {g.n, g.m};
+        const uint32_t box[2] = {32, 32};
+        if ((rc = make_tmap_store_2d(&tn, g.norm_out, 2, dims, nld * 2, box, 64)) != BL_OK)
+            return rc;
+        p.norm_out = g.norm_out;
+        p.norm_dtype = g.norm_out_dtype;
+        p.norm_gamma = g.norm_gamma;
+        p.norm_beta = g.norm_beta;
+        p.norm_eps = g.norm_eps;
+        p.norm_ctr = static_cast<unsigned*>(g.norm_sync);
+        p.norm_stats = reinterpret_cast<float2*>(static_cast<uint8_t*>(g.norm_sync) +
+                                                 norm_ctr_bytes(g.m));
+    }
     // Output rows leave through a tensor map when they form one strided 2-D
     // array of a single element size (no row groups).
     CUtensorMap to{};
@@ -1032,10 +1210,10 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
         p.tma_store = 1;
     }
     switch (bn) {
-        case 32: return prepare_persistent<32>(ta, tb, to, p, kc, out);
-        case 64: return prepare_persistent<64>(ta, tb, to, p, kc, out);
-        case 96: return prepare_persistent<96>(ta, tb, to, p, kc, out);
-        default: return prepare_persistent<128>(ta, tb, to, p, kc, out);
+        case 32: return prepare_persistent<32>(ta, tb, to, tn, p, kc, out);
+        case 64: return prepare_persistent<64>(ta, tb, to, tn, p, kc, out);
+        case 96: return prepare_persistent<96>(ta, tb, to, tn, p, kc, out);
+        default: return prepare_persistent<128>(ta, tb, to, tn, p, kc, out);
     }
 }
 
@@ -1047,6 +1225,10 @@ int prepare_gemm_rows(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_en
 }
 
 }  // namespace bl
+
+extern "C" size_t bl_gemm_norm_sync_bytes(const bl_gemm_args* args) {
+    return args == nullptr ? 0 : static_cast<size_t>(bl::gemm::norm_sync_bytes(args->m, args->n));
+}
 
 extern "C" int bl_gemm(const bl_gemm_args* args, void* stream) {
     if (args == nullptr) return bl::fail(BL_ERR_INVALID, "gemm: null args");

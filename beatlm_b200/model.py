@@ -204,6 +204,11 @@ class Buffers:
         # x: (mean, M2) for each 32-column slice
         self.stats1 = alloc("stats1", (rows, cfg.dim // 32, 2), torch.float32)
         self.stats2 = alloc("stats2", (rows, cfg.dim // 32, 2), torch.float32)
+        # exchange buffer of the epilogue LayerNorm (counters, then per-slice
+        # statistics); zero-filled once, every launch leaves it so
+        sync_bytes = (8 * ((rows + 127) // 128) + 15) // 16 * 16 + 8 * rows * (cfg.dim // 32)
+        self.norm_sync = alloc("norm_sync", (sync_bytes,), torch.uint8)
+        self.norm_sync.zero_()
         self.features = ([alloc("features.%d" % i, (frames * (t - 1), cfg.dim), torch.float32)
                           for i in cfg.out_indices] if features else [])
 
@@ -222,8 +227,16 @@ class Buffers:
         return 0, last
 
 
+def norm_epilogue_fits(rows: int, dim: int) -> bool:
+    """Whether a GEMM writing `rows` x `dim` can carry the epilogue LayerNorm:
+    every 32-column tile must be resident at once, one per SM."""
+    import torch
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    return dim <= 512 and -(-rows // 128) * (dim // 32) <= sms
+
+
 def block_specs(blk: DeviceBlock, cfg: ViTConfig, buf: Buffers, layer: int = 0,
-                parts: int = 1, fused_ln: bool = False) -> list:
+                parts: int = 1, fused_ln=False, next_norm=None) -> list:
     """The fused kernels of one pre-norm block (reference.rs:520-544), in
     place on ``buf.x``:
     x1 = x + ls1 * proj(attention(norm1(x))); x = x1 + ls2 * fc2(gelu(fc1(norm2(x1)))).
@@ -236,13 +249,40 @@ def block_specs(blk: DeviceBlock, cfg: ViTConfig, buf: Buffers, layer: int = 0,
     normalises its A operand from x in its prologue with them, so no
     LayerNorm launch and no pass over the rows remain. Block 0's norm1 reads
     the embedding's output, for which no statistics exist: it stays a
-    standalone LayerNorm."""
+    standalone LayerNorm.
+    ``fused_ln="epilogue"`` (5 kernels; 6 for block 0): proj writes x and
+    norm2(x) (``buf.xn``), fc2 writes x and ``next_norm`` (the next block's
+    norm1 weights; none for the last block) of it, each LayerNorm computed in
+    the GEMM's epilogue from statistics its column tiles exchange; QKV and
+    fc1 load ``buf.xn`` by TMA. Where the GEMM has more 32-column tiles than
+    the device has SMs (``norm_epilogue_fits``) the block is built as with
+    ``fused_ln=False``."""
     from .runtime import Spec
     d = cfg.dim
     name = "block%d." % layer
     attn = Spec(ops.attention_args(buf.qkv, tokens=buf.tokens, heads=cfg.heads,
                                    head_dim=cfg.head_dim, batch=buf.frames, qk_dtype=blk.dtype,
                                    out=buf.o), name + "attention", parts)
+    if fused_ln == "epilogue" and not norm_epilogue_fits(buf.rows, d):
+        fused_ln = False
+    if fused_ln == "epilogue":
+        ep = lambda w: None if w is None else (w[0], w[1], cfg.eps, buf.xn)
+        head = ([Spec(ops.layernorm_args(buf.x, blk.norm1[0], blk.norm1[1], cfg.eps, out=buf.xn),
+                      name + "norm1", parts)] if layer == 0 else [])
+        return head + [
+            Spec(ops.gemm_args(blk.qkv_w, a=buf.xn, bias=blk.qkv_b, out=buf.qkv,
+                               out_dtype=blk.dtype, out_split=(2 * d, "f16")), name + "qkv", parts),
+            attn,
+            Spec(ops.gemm_args(blk.proj_w, a=buf.o, bias=blk.proj_b, chan_scale=blk.ls1,
+                               residual=buf.x, out=buf.x, norm=ep(blk.norm2),
+                               norm_sync=buf.norm_sync), name + "proj", parts),
+            Spec(ops.gemm_args(blk.fc1_w, a=buf.xn, bias=blk.fc1_b, act="gelu_erf", out=buf.h),
+                 name + "fc1", parts),
+            Spec(ops.gemm_args(blk.fc2_w, a=buf.h, bias=blk.fc2_b, chan_scale=blk.ls2,
+                               residual=buf.x, out=buf.x, norm=ep(next_norm),
+                               norm_sync=buf.norm_sync if next_norm is not None else None),
+                 name + "fc2", parts),
+        ]
     stats = (lambda s: s) if fused_ln else (lambda s: None)
     proj = Spec(ops.gemm_args(blk.proj_w, a=buf.o, bias=blk.proj_b, chan_scale=blk.ls1,
                               residual=buf.x, out=buf.x, stats_out=stats(buf.stats2)),
@@ -315,11 +355,16 @@ class Encoder:
         at ViT-S (one frame), the QKV and fc1 GEMMs that normalise their A
         operand from the f32 rows through the load/store units take longer
         than a standalone LayerNorm plus a GEMM that loads 16-bit rows by TMA
-        (1129 against 1345 frames/s)."""
+        (1129 against 1345 frames/s). ``fused_ln="epilogue"``: the GEMMs that
+        write x also write the next LayerNorm's output (``block_specs``);
+        needs every 32-column tile of those GEMMs resident at once (ViT-S
+        at one frame: 132 tiles). Also measured slower at ViT-S, one frame:
+        668 against 640 us, the column tiles' exchange of statistics through
+        L2 costing more than the LayerNorm launch it replaces."""
         import torch
         td = torch.bfloat16 if dtype == "bf16" else torch.float16
         self.cfg, self.dtype = cfg, dtype
-        self.fused_ln = bool(fused_ln)
+        self.fused_ln = fused_ln if fused_ln == "epilogue" else bool(fused_ln)
         self.arena, self.plan = None, None
         stage = "cpu" if planned_frames is not None else device
         self.blocks = [DeviceBlock(w, cfg.dim, cfg.mlp, dtype, stage) for w in weights["blocks"]]
@@ -405,13 +450,20 @@ class Encoder:
         out = ["embed.patchify", "embed.patch"]
         for i in range(cfg.layers):
             kinds = ("norm1", "qkv", "attention", "proj", "norm2", "fc1", "fc2")
-            if self.fused_ln:
+            if self._fused(frames):
                 kinds = (("norm1", "qkv") if i == 0 else ("qkv",)) + ("attention", "proj", "fc1",
                                                                       "fc2")
             out += ["block%d.%s" % (i, k) for k in kinds]
             if (i + 1) in cfg.out_indices:
                 out.append("features.%d" % (i + 1))
         return out
+
+    def _fused(self, frames: int):
+        """The LayerNorm mode the blocks are built with for `frames` frames."""
+        if self.fused_ln == "epilogue" and not norm_epilogue_fits(frames * self.cfg.tokens,
+                                                                  self.cfg.dim):
+            return False
+        return self.fused_ln
 
     def buffers(self, frames: int) -> Buffers:
         if frames not in self._buffers:
@@ -437,7 +489,9 @@ class Encoder:
         ]
         n = cfg.layers if layers is None else layers
         for i in range(n):
-            out += block_specs(self.blocks[i], cfg, buf, i, parts, fused_ln=self.fused_ln)
+            nxt = self.blocks[i + 1].norm1 if i + 1 < n else None
+            out += block_specs(self.blocks[i], cfg, buf, i, parts, fused_ln=self.fused_ln,
+                               next_norm=nxt)
             if (i + 1) in cfg.out_indices:
                 f = buf.features[cfg.out_indices.index(i + 1)]
                 out.append(Spec(ops.layernorm_args(buf.x, self.norm[0], self.norm[1], cfg.eps,
@@ -467,8 +521,9 @@ class Encoder:
         self.program(frames, layers).encode_all(stream)
         return self.features(frames, layers)
 
-    def launches_per_frame_batch(self, layers: int | None = None) -> int:
+    def launches_per_frame_batch(self, layers: int | None = None, frames: int = 1) -> int:
         n = self.cfg.layers if layers is None else layers
         taken = sum(1 for i in self.cfg.out_indices if i <= n)
-        per_block = [7 if not self.fused_ln else (6 if i == 0 else 5) for i in range(n)]
+        fused = self._fused(frames)
+        per_block = [7 if not fused else (6 if i == 0 else 5) for i in range(n)]
         return 3 + sum(per_block) + taken  # patchify (2 kernels) + patch GEMM, blocks, norms

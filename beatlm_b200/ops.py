@@ -116,11 +116,14 @@ def attention(qkv, *, tokens: int, heads: int, head_dim: int = 64, batch: int = 
 
 def gemm_args(w, *, a=None, ln=None, bias=None, act=None, scale=None, chan_scale=None,
               residual=None, res_period=0, out, out_dtype=None, out_split=None, m=None,
-              out_row_offset=0, out_group=(0, 0), tile_n=0, stats_out=None, ln_stats=None):
+              out_row_offset=0, out_group=(0, 0), tile_n=0, stats_out=None, ln_stats=None,
+              norm=None, norm_sync=None):
     """``stats_out``: a float32 ``[rows][parts][2]`` tensor the epilogue fills
     with per-slice (mean, M2) of each stored row (``parts`` = n / tile width).
     ``ln_stats``: such a tensor for ``ln``'s input, used instead of a pass
-    over its rows."""
+    over its rows. ``norm=(gamma, beta, eps, out)``: the epilogue also writes
+    LayerNorm of every stored f32 row to the 16-bit ``out``; ``norm_sync`` is
+    its zero-filled exchange buffer (``gemm_norm_sync_bytes``)."""
     import torch
     n, k = w.shape
     ab = {torch.float16: "f16", torch.bfloat16: "bf16"}[w.dtype]
@@ -149,7 +152,18 @@ def gemm_args(w, *, a=None, ln=None, bias=None, act=None, scale=None, chan_scale
         g.stats_out, g.stats_parts = stats_out.data_ptr(), stats_out.shape[1]
     if ln_stats is not None:
         g.ln_stats, g.ln_stats_parts = ln_stats.data_ptr(), ln_stats.shape[1]
+    if norm is not None:
+        gamma, beta, eps, nout = norm
+        g.norm_out, g.norm_out_dtype, g.norm_out_ld = nout.data_ptr(), _dt(nout), nout.stride(0)
+        g.norm_gamma, g.norm_beta, g.norm_eps = gamma.data_ptr(), beta.data_ptr(), eps
+        g.norm_sync, g.norm_sync_bytes = norm_sync.data_ptr(), norm_sync.numel()
     return g
+
+
+def gemm_norm_sync_bytes(m: int, n: int) -> int:
+    """Bytes of the exchange buffer of an epilogue LayerNorm over m rows of
+    n columns (``bl_gemm_norm_sync_bytes``)."""
+    return int(N.lib().bl_gemm_norm_sync_bytes(ctypes.byref(N.GemmArgs(m=m, n=n))))
 
 
 def linear(w, *, stream=None, **kw):

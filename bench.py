@@ -290,7 +290,7 @@ class EncoderWorkload:
         fl = cfg.flops_per_frame()
         self.flops = fl["total"] * frames
         self.attn_flops = 4.0 * cfg.tokens * cfg.tokens * cfg.dim * frames  # per layer launch
-        self.launches_per_step = self.enc.launches_per_frame_batch()
+        self.launches_per_step = self.enc.launches_per_frame_batch(frames=frames)
 
     def config(self):
         c = self.cfg

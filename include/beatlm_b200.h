@@ -221,9 +221,33 @@ typedef struct bl_gemm_args {
      * columns, combined by Chan's formula) instead of a pass over the row. */
     const void* ln_stats;
     uint32_t ln_stats_parts;
+    /* LayerNorm of the stored rows in the epilogue (optional; no counterpart
+     * in the reference, which runs its LayerNorm op, kernel.rs:644-659, as a
+     * pass of its own): with norm_out set, every output row is also
+     * normalised over its n stored f32 values (biased variance, then
+     * norm_gamma / norm_beta, eps norm_eps) and written to norm_out (f16 or
+     * bf16, row stride norm_out_ld elements; row r of the product lands in
+     * row r). The 32-column tiles of a 128-row tile exchange partial
+     * (mean, M2) statistics through norm_sync: a zero-filled device buffer of
+     * at least bl_gemm_norm_sync_bytes() bytes, 16-byte aligned, that each
+     * launch leaves zero-filled again (one launch at a time per buffer).
+     * Requires an f32 output of one type without row groups, n <= 512,
+     * 32-column tiles (tile_n 0 or 32), and no more tiles than the device has
+     * SMs; otherwise BL_ERR_UNSUPPORTED. */
+    void* norm_out;
+    int32_t norm_out_dtype;
+    uint64_t norm_out_ld;
+    const float* norm_gamma;
+    const float* norm_beta;
+    float norm_eps;
+    void* norm_sync;
+    uint64_t norm_sync_bytes;
 } bl_gemm_args;
 
 int bl_gemm(const bl_gemm_args* args, void* stream);
+
+/* Bytes of norm_sync that bl_gemm needs for these arguments (m and n). */
+size_t bl_gemm_norm_sync_bytes(const bl_gemm_args* args);
 
 /*
  * Standalone LayerNorm over rows of `cols` f32 values (reference.rs:247-270;

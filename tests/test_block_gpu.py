@@ -28,7 +28,7 @@ def _rel(got, want):
         np.max(np.abs(got - want)))
 
 
-@pytest.mark.parametrize("fused_ln", [False, True])
+@pytest.mark.parametrize("fused_ln", [False, True, "epilogue"])
 @pytest.mark.parametrize("dtype", ["f16", "bf16"])
 def test_one_block_matches_the_reference_block(dtype, fused_ln):
     import torch
@@ -93,7 +93,8 @@ def oracle_encoder(cfg, w, image, layers, dtype):
     return feats
 
 
-@pytest.mark.parametrize("dtype,fused_ln", [("bf16", False), ("f16", False), ("bf16", True)])
+@pytest.mark.parametrize("dtype,fused_ln", [("bf16", False), ("f16", False), ("bf16", True),
+                                            ("bf16", "epilogue")])
 def test_encoder_features_match_the_reference_chain(dtype, fused_ln):
     """Config-3 shapes (518 px, ViT-S) with 3 blocks and a feature taken after
     blocks 1 and 3, batch 2 frames; also with the LayerNorms fed by the
@@ -118,6 +119,34 @@ def test_encoder_features_match_the_reference_chain(dtype, fused_ln):
             print("encoder %s frame %d feature %d: rel-L2 %.3e max-abs %.3e" % (
                 dtype, f, i, rel, mx))
             assert rel <= REL[dtype]
+
+
+def test_encoder_with_layernorms_in_the_gemm_epilogues_matches_the_reference():
+    """One frame (132 column tiles of 32 per GEMM, all resident): proj and
+    fc2 write the next LayerNorm's rows from their epilogues. Features after
+    blocks 1 and 3 against the oracle chain, and the program has 5 kernels per
+    block after the first."""
+    import torch
+    import beatlm_b200 as bl
+    from beatlm_b200.model import Encoder, ViTConfig
+    layers = 3
+    cfg = ViTConfig.small(layers=layers, out_indices=(1, 3))
+    w = _encoder_weights(cfg, layers, seed=3)
+    image = imagenet_image(np.random.default_rng(8), cfg.side, frames=1)
+    enc = Encoder(cfg, w, "bf16", fused_ln="epilogue")
+    feats = enc.forward(torch.from_numpy(image).cuda(), frames=1)
+    torch.cuda.synchronize()
+    assert bl.status(reset=True).code == 0
+    assert enc.launches_per_frame_batch(frames=1) == 3 + 6 + 5 + 5 + 2
+    want = oracle_encoder(cfg, w, image[0], layers, "bf16")
+    for i, ft in enumerate(feats):
+        rel, mx = _rel(ft.cpu().numpy().ravel(), want[i])
+        print("encoder (epilogue LayerNorm) feature %d: rel-L2 %.3e max-abs %.3e" % (i, rel, mx))
+        assert rel <= REL["bf16"]
+    # the exchange buffer is left zero-filled for the next launch
+    buf = enc.buffers(1)
+    ctr = buf.norm_sync[:16 * ((8 * ((buf.rows + 127) // 128) + 15) // 16)]
+    assert int(ctr.count_nonzero()) == 0
 
 
 def test_vit_l_block_matches_the_reference_block():

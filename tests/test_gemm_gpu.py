@@ -214,6 +214,58 @@ def test_row_statistics_of_the_stored_output(m, n, k):
     assert _rel(y1.cpu().numpy(), y2.cpu().numpy()) < 2e-3
 
 
+@pytest.mark.parametrize("m", [1370, 300])
+def test_layernorm_in_the_epilogue_matches_a_standalone_layernorm(m):
+    """x1 = x + ls * (A.W + b) (f32, stored) and LayerNorm(x1) written by the
+    same GEMM's epilogue: the normalised rows equal a standalone LayerNorm of
+    the stored x1 to within a 16-bit rounding, and the exchange buffer is
+    zero-filled again afterwards (a second launch gives the same rows)."""
+    import torch
+    import beatlm_b200 as bl
+    n, k = 384, 1536
+    a = _rnd(oracle.normal(31, m * k), "bf16")
+    w = _rnd(oracle.uniform(32, k * n, -0.05, 0.05), "bf16")
+    x0 = oracle.uniform(33, m * n, -2, 2).reshape(m, n)
+    g = _dev(oracle.uniform(36, n, 0.8, 1.2), "f32")
+    be = _dev(oracle.uniform(37, n, -0.1, 0.1), "f32")
+    sync = torch.zeros(bl.ops.gemm_norm_sync_bytes(m, n), dtype=torch.uint8, device="cuda")
+    outs = []
+    for rep in range(2):
+        x = torch.from_numpy(x0.copy()).cuda()
+        xn = torch.zeros((m, n), dtype=torch.bfloat16, device="cuda")
+        bl.ops.linear(_dev(w.reshape(k, n).T, "bf16"), a=_dev(a.reshape(m, k), "bf16"),
+                      bias=_dev(oracle.uniform(34, n, -0.1, 0.1), "f32"),
+                      chan_scale=_dev(oracle.uniform(35, n, 0.1, 1.0), "f32"), residual=x, out=x,
+                      norm=(g, be, 1e-6, xn), norm_sync=sync)
+        torch.cuda.synchronize()
+        _check_status()
+        nctr = (8 * ((m + 127) // 128) + 15) // 16 * 16  # the counters, first in the buffer
+        assert int(sync[:nctr].count_nonzero()) == 0
+        want = torch.zeros_like(xn)
+        bl.ops.layernorm(x, g, be, 1e-6, out=want)
+        torch.cuda.synchronize()
+        got, ref = xn.float().cpu().numpy(), want.float().cpu().numpy()
+        assert np.all(np.abs(got - ref) <= 2 ** -7 * np.abs(ref) + 2e-3), np.max(np.abs(got - ref))
+        outs.append(got)
+    assert np.array_equal(outs[0], outs[1])
+
+
+def test_layernorm_in_the_epilogue_is_refused_where_tiles_do_not_fit():
+    import torch
+    import beatlm_b200 as bl
+    m, n = 128 * 40, 384  # 480 column tiles of 32
+    w = torch.zeros((n, 64), dtype=torch.bfloat16, device="cuda")
+    a = torch.zeros((m, 64), dtype=torch.bfloat16, device="cuda")
+    x = torch.zeros((m, n), dtype=torch.float32, device="cuda")
+    xn = torch.zeros((m, n), dtype=torch.bfloat16, device="cuda")
+    g = torch.ones(n, device="cuda")
+    sync = torch.zeros(bl.ops.gemm_norm_sync_bytes(m, n), dtype=torch.uint8, device="cuda")
+    with pytest.raises(bl.BackendError, match="resident"):
+        bl.ops.linear(w, a=a, out=x, norm=(g, g, 1e-6, xn), norm_sync=sync)
+    with pytest.raises(bl.BackendError, match="norm_sync"):
+        bl.ops.linear(w, a=a[:128], out=x[:128], norm=(g, g, 1e-6, xn[:128]), norm_sync=sync[:64])
+
+
 def test_statistics_arguments_are_checked():
     import torch
     import beatlm_b200 as bl
