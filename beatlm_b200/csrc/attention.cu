@@ -237,29 +237,40 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp < kSoftmaxWarp0) {
         asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kControlRegs));
-        if (warp == 0 && lane == 0) {
+        if (warp == 0) {
             // -------------------------------------------------- producer
+            // The warp runs the loop in step: lane 0 copies the CTA's Q rows
+            // (one box) and each stage's K, arming the stage; lane 1 copies
+            // each stage's V, so K and V are in flight together (a thread's
+            // bulk copies complete one after another). Lane 0 alone waits
+            // for a free stage and the vote hands the outcome to the warp.
             const uint32_t b_q = smem_u32(&tail->q_full);
-            mbar_arrive_expect_tx(b_q, QT * kTileBytes);
-            for (int t = 0; t < QT; ++t)
-                tma_load_3d(smem_u32(sQ + t * kTileBytes), &tm_q, p.q_col0 + head * HD,
-                            q0 + t * BM, batch, b_q);
+            if (lane == 0) {
+                mbar_arrive_expect_tx(b_q, QT * kTileBytes);
+                tma_load_3d(smem_u32(sQ), &tm_q, p.q_col0 + head * HD, q0, batch, b_q);
+            }
             int loaded = 0;  // key tiles whose loads were started
             for (int i = 0; i < n; ++i) {
                 const int s = i % STAGES;
                 const int r = i / STAGES;
-                if (r > 0 && !mbar_wait(smem_u32(&tail->kv_empty[s]), (r - 1) & 1, abort,
-                                        p.status, ST_TIMEOUT_TMA, i))
-                    break;
+                bool w = true;
+                if (lane == 0 && r > 0)
+                    w = mbar_wait(smem_u32(&tail->kv_empty[s]), (r - 1) & 1, abort, p.status,
+                                  ST_TIMEOUT_TMA, i);
+                if (!__all_sync(0xFFFFFFFFu, w)) break;
                 const uint32_t bar = smem_u32(&tail->kv_full[s]);
-                mbar_arrive_expect_tx(bar, 2 * kTileBytes);
-                tma_load_3d(smem_u32(sK + s * kTileBytes), &tm_k, p.k_col0 + head * HD,
-                            (t0 + i) * BN, batch, bar);
-                tma_load_3d(smem_u32(sV + s * kTileBytes), &tm_v, p.v_col0 + head * HD,
-                            (t0 + i) * BN, batch, bar);
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(bar, 2 * kTileBytes);
+                    tma_load_3d(smem_u32(sK + s * kTileBytes), &tm_k, p.k_col0 + head * HD,
+                                (t0 + i) * BN, batch, bar);
+                } else if (lane == 1) {
+                    tma_load_3d(smem_u32(sV + s * kTileBytes), &tm_v, p.v_col0 + head * HD,
+                                (t0 + i) * BN, batch, bar);
+                }
+                __syncwarp();
                 ++loaded;
             }
-            if (*abort) {
+            if (lane == 0 && *abort) {
                 // Unwinding: let every copy this thread started land before
                 // the CTA's shared memory is released.
                 mbar_wait(b_q, 0, nullptr, p.status, ST_TIMEOUT_DRAIN, 0);
@@ -269,6 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                               ST_TIMEOUT_DRAIN, s);
                 }
             }
+            __syncwarp();
         } else if (warp == 1) {
             // -------------------------------------------------- MMA issuer
             // The whole warp runs the issuer's loop and one elected lane
@@ -747,11 +759,14 @@ int prepare(const bl_attention_args& a, void* workspace, uint64_t workspace_byte
             return fail(BL_ERR_INVALID, "attention: workspace must be 256-byte aligned");
     }
 
-    CUtensorMap tm;
+    CUtensorMap tm, tm_q;  // K / V tiles; the CTA's QT query tiles as one box
     const uint64_t dims[3] = {row, a.tokens, a.batch};
     const uint64_t strides[2] = {row * 2, row * 2 * a.tokens};
     const uint32_t box[3] = {HD, BM, 1};
     rc = make_tmap_16bit_3d(&tm, a.qkv, dims, strides, box);
+    if (rc != BL_OK) return rc;
+    const uint32_t qbox[3] = {HD, static_cast<uint32_t>(QT * BM), 1};
+    rc = make_tmap_16bit_3d(&tm_q, a.qkv, dims, strides, qbox);
     if (rc != BL_OK) return rc;
 
     Params p{};
@@ -798,12 +813,12 @@ int prepare(const bl_attention_args& a, void* workspace, uint64_t workspace_byte
     if (cluster) {
         const dim3 cdim(1, 1, pl.splits);
         out->run = [=](cudaStream_t s) {
-            return launch_k_cluster(kern, grid, dim3(kThreads), cdim, kSmemBytes, s, tm, tm, tm,
+            return launch_k_cluster(kern, grid, dim3(kThreads), cdim, kSmemBytes, s, tm_q, tm, tm,
                                     p);
         };
     } else {
         out->run = [=](cudaStream_t s) {
-            return launch_k(kern, grid, dim3(kThreads), kSmemBytes, s, tm, tm, tm, p);
+            return launch_k(kern, grid, dim3(kThreads), kSmemBytes, s, tm_q, tm, tm, p);
         };
     }
     return BL_OK;
