@@ -63,6 +63,7 @@ struct Params {
     const float2* ln_stats;  // LN prologue: [row][ln_stats_parts] partials of x
     int ln_stats_parts;
     int tma_store;  // persistent kernel: rows leave through the output tensor map
+    int weights_static;  // B and the epilogue vectors may be read before the PDL wait
     // LayerNorm of the stored rows in the epilogue (32-column tiles, one tile
     // per CTA): per-slice statistics meet in norm_stats, row tiles count their
     // published slices in norm_ctr[2 * tile] and their readers in [2 * tile + 1]
@@ -331,17 +332,25 @@ __device__ __forceinline__ void store_tile(const Params& p, const Tail* tail, ui
         }
         const int dt = col >= p.split_col ? p.out_dtype_hi : p.out_dtype;
         if (tmo != nullptr) {
-            if (lane == 0) bulk_wait_read();  // the previous block has left `buf`
+            // 4-byte blocks fill `buf`; 2-byte blocks alternate between its
+            // halves, so a block is written while the previous one is still
+            // being read out (a tile's first block waits for every earlier one)
+            const bool wide = dt == BL_F32;
+            uint8_t* blk = wide ? buf : buf + (c & 1) * (kEpiBlock / 2);
+            if (lane == 0) {
+                if (wide || c == 0) bulk_wait_read();
+                else bulk_wait_read1();
+            }
             __syncwarp();
-            if (dt == BL_F32) {
+            if (wide) {
 #pragma unroll
                 for (int j = 0; j < 8; ++j)
-                    *reinterpret_cast<float4*>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+                    *reinterpret_cast<float4*>(blk + lane * 128 + ((j ^ (lane & 7)) << 4)) =
                         make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
             } else {
 #pragma unroll
                 for (int j = 0; j < 4; ++j)
-                    *reinterpret_cast<uint4*>(buf + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) =
+                    *reinterpret_cast<uint4*>(blk + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) =
                         make_uint4(pack2(v[8 * j], v[8 * j + 1], dt),
                                    pack2(v[8 * j + 2], v[8 * j + 3], dt),
                                    pack2(v[8 * j + 4], v[8 * j + 5], dt),
@@ -350,7 +359,7 @@ __device__ __forceinline__ void store_tile(const Params& p, const Tail* tail, ui
             fence_proxy_async_smem();  // the writes above, seen by the bulk copy
             __syncwarp();
             if (lane == 0) {
-                tma_store_2d(tmo, smem_u32(buf), col, box_row);
+                tma_store_2d(tmo, smem_u32(blk), col, box_row);
                 bulk_commit();
             }
         } else if (dt == BL_F32) {
@@ -785,8 +794,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tail->tmem_base;
+    // Programmatic dependent launch: with weights_static, B and the epilogue
+    // vectors do not depend on the previous kernel, so the first stages' B
+    // copies and the vector staging start before the wait; A, the residual
+    // and every store come after it (each role waits before its first
+    // dependent access; the MMA warp touches no global memory).
     pdl_trigger();
-    pdl_wait();
 
     if (warp == 0) {
         // The whole warp runs the producer loop in step; lane 0 arms the
@@ -794,6 +807,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         // are in flight together (each thread's copies are serial). Lane 0
         // alone waits for the stage to be free; the vote hands the outcome
         // to the warp, so both lanes start the same stages.
+        const int first = !p.weights_static ? 0 : STAGES < mine * nk ? STAGES : mine * nk;
+        for (int g = 0; g < first; ++g) {  // stages whose B is fetched up front
+            const uint32_t bar = smem_u32(&tail->full[g]);
+            if (lane == 0) mbar_arrive_expect_tx(bar, L::kStage);
+            if (lane == 1)
+                tma_load_3d(smem_u32(sB(g)), &tm_b, 0, tile_n0(g / nk), (g % nk) * KC, bar);
+        }
+        pdl_wait();
         int g = 0;  // stages whose loads were started, over all tiles
         bool ok = true;
         for (int j = 0; j < mine && ok; ++j) {
@@ -808,9 +829,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!ok) break;
                 const uint32_t bar = smem_u32(&tail->full[s]);
                 if (lane == 0) {
-                    mbar_arrive_expect_tx(bar, L::kStage);
+                    if (g >= first) mbar_arrive_expect_tx(bar, L::kStage);
                     tma_load_3d(smem_u32(sA(s)), &tm_a, 0, m0, kb * KC, bar);
-                } else if (lane == 1) {
+                } else if (lane == 1 && g >= first) {
                     tma_load_3d(smem_u32(sB(s)), &tm_b, 0, n0, kb * KC, bar);
                 }
                 __syncwarp();
@@ -882,8 +903,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int m0 = tile_m0(j), n0 = tile_n0(j);
             const RowCtx rc = row_ctx(p, m0 + row);
             epilogue_all(true);  // the previous tile's staged vectors are no longer read
+            if (!p.weights_static) pdl_wait();
             stage_vectors<BN>(p, tail, n0);
             epilogue_all(true);
+            pdl_wait();  // the residual and the outputs belong to the previous kernels
             float rv0[32];
             prefetch_residual(p, rc, n0, rv0);
             bool ok = mbar_wait(smem_u32(&tail->acc_full[b]), use & 1, abort, p.status,
@@ -1168,6 +1191,7 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
     p.stats_parts = static_cast<int>(g.stats_parts);
     p.ln_stats = static_cast<const float2*>(g.ln_stats);
     p.ln_stats_parts = static_cast<int>(g.ln_stats_parts);
+    p.weights_static = g.weights_static ? 1 : 0;
     p.m_tile0 = static_cast<int>(row_begin / BM);
     p.m_tiles = static_cast<int>((std::min(row_end, g.m) + BM - 1) / BM) - p.m_tile0;
     if (row_begin % BM != 0 || row_begin >= row_end || p.m_tiles <= 0)

@@ -227,6 +227,12 @@ class Buffers:
         return 0, last
 
 
+def _weights_gemm(w, **kw):
+    """``ops.gemm_args`` for a GEMM whose B, bias and scale are model weights
+    (never written by the kernel before it: fetched before that one ends)."""
+    return ops.gemm_args(w, weights_static=True, **kw)
+
+
 def norm_epilogue_fits(rows: int, dim: int) -> bool:
     """Whether a GEMM writing `rows` x `dim` can carry the epilogue LayerNorm:
     every 32-column tile must be resident at once, one per SM."""
@@ -270,24 +276,24 @@ def block_specs(blk: DeviceBlock, cfg: ViTConfig, buf: Buffers, layer: int = 0,
         head = ([Spec(ops.layernorm_args(buf.x, blk.norm1[0], blk.norm1[1], cfg.eps, out=buf.xn),
                       name + "norm1", parts)] if layer == 0 else [])
         return head + [
-            Spec(ops.gemm_args(blk.qkv_w, a=buf.xn, bias=blk.qkv_b, out=buf.qkv,
+            Spec(_weights_gemm(blk.qkv_w, a=buf.xn, bias=blk.qkv_b, out=buf.qkv,
                                out_dtype=blk.dtype, out_split=(2 * d, "f16")), name + "qkv", parts),
             attn,
-            Spec(ops.gemm_args(blk.proj_w, a=buf.o, bias=blk.proj_b, chan_scale=blk.ls1,
+            Spec(_weights_gemm(blk.proj_w, a=buf.o, bias=blk.proj_b, chan_scale=blk.ls1,
                                residual=buf.x, out=buf.x, norm=ep(blk.norm2),
                                norm_sync=buf.norm_sync), name + "proj", parts),
-            Spec(ops.gemm_args(blk.fc1_w, a=buf.xn, bias=blk.fc1_b, act="gelu_erf", out=buf.h),
+            Spec(_weights_gemm(blk.fc1_w, a=buf.xn, bias=blk.fc1_b, act="gelu_erf", out=buf.h),
                  name + "fc1", parts),
-            Spec(ops.gemm_args(blk.fc2_w, a=buf.h, bias=blk.fc2_b, chan_scale=blk.ls2,
+            Spec(_weights_gemm(blk.fc2_w, a=buf.h, bias=blk.fc2_b, chan_scale=blk.ls2,
                                residual=buf.x, out=buf.x, norm=ep(next_norm),
                                norm_sync=buf.norm_sync if next_norm is not None else None),
                  name + "fc2", parts),
         ]
     stats = (lambda s: s) if fused_ln else (lambda s: None)
-    proj = Spec(ops.gemm_args(blk.proj_w, a=buf.o, bias=blk.proj_b, chan_scale=blk.ls1,
+    proj = Spec(_weights_gemm(blk.proj_w, a=buf.o, bias=blk.proj_b, chan_scale=blk.ls1,
                               residual=buf.x, out=buf.x, stats_out=stats(buf.stats2)),
                 name + "proj", parts)
-    fc2 = Spec(ops.gemm_args(blk.fc2_w, a=buf.h, bias=blk.fc2_b, chan_scale=blk.ls2,
+    fc2 = Spec(_weights_gemm(blk.fc2_w, a=buf.h, bias=blk.fc2_b, chan_scale=blk.ls2,
                              residual=buf.x, out=buf.x, stats_out=stats(buf.stats1)),
                name + "fc2", parts)
     if fused_ln:
@@ -295,17 +301,17 @@ def block_specs(blk: DeviceBlock, cfg: ViTConfig, buf: Buffers, layer: int = 0,
             head = [
                 Spec(ops.layernorm_args(buf.x, blk.norm1[0], blk.norm1[1], cfg.eps, out=buf.xn),
                      name + "norm1", parts),
-                Spec(ops.gemm_args(blk.qkv_w, a=buf.xn, bias=blk.qkv_b, out=buf.qkv,
+                Spec(_weights_gemm(blk.qkv_w, a=buf.xn, bias=blk.qkv_b, out=buf.qkv,
                                    out_dtype=blk.dtype, out_split=(2 * d, "f16")),
                      name + "qkv", parts)]
         else:
-            head = [Spec(ops.gemm_args(blk.qkv_w, ln=(buf.x, blk.norm1[0], blk.norm1[1], cfg.eps),
+            head = [Spec(_weights_gemm(blk.qkv_w, ln=(buf.x, blk.norm1[0], blk.norm1[1], cfg.eps),
                                        ln_stats=buf.stats1, bias=blk.qkv_b, out=buf.qkv,
                                        out_dtype=blk.dtype, out_split=(2 * d, "f16")),
                          name + "qkv", parts)]
         return head + [
             attn, proj,
-            Spec(ops.gemm_args(blk.fc1_w, ln=(buf.x, blk.norm2[0], blk.norm2[1], cfg.eps),
+            Spec(_weights_gemm(blk.fc1_w, ln=(buf.x, blk.norm2[0], blk.norm2[1], cfg.eps),
                                ln_stats=buf.stats2, bias=blk.fc1_b, act="gelu_erf", out=buf.h),
                  name + "fc1", parts),
             fc2,
@@ -313,12 +319,12 @@ def block_specs(blk: DeviceBlock, cfg: ViTConfig, buf: Buffers, layer: int = 0,
     return [
         Spec(ops.layernorm_args(buf.x, blk.norm1[0], blk.norm1[1], cfg.eps, out=buf.xn),
              name + "norm1", parts),
-        Spec(ops.gemm_args(blk.qkv_w, a=buf.xn, bias=blk.qkv_b, out=buf.qkv, out_dtype=blk.dtype,
+        Spec(_weights_gemm(blk.qkv_w, a=buf.xn, bias=blk.qkv_b, out=buf.qkv, out_dtype=blk.dtype,
                            out_split=(2 * d, "f16")), name + "qkv", parts),
         attn, proj,
         Spec(ops.layernorm_args(buf.x, blk.norm2[0], blk.norm2[1], cfg.eps, out=buf.xn),
              name + "norm2", parts),
-        Spec(ops.gemm_args(blk.fc1_w, a=buf.xn, bias=blk.fc1_b, act="gelu_erf", out=buf.h),
+        Spec(_weights_gemm(blk.fc1_w, a=buf.xn, bias=blk.fc1_b, act="gelu_erf", out=buf.h),
              name + "fc1", parts),
         fc2,
     ]
@@ -483,7 +489,7 @@ class Encoder:
                                    cin=cfg.cin, k_pad=cfg.k_pad, a_out=buf.patches,
                                    a_dtype=self.dtype, cls=self.cls, pos=self.pos, x=buf.x),
                  "embed.patchify"),
-            Spec(ops.gemm_args(self.patch_w, a=buf.patches, bias=self.patch_b, residual=self.pos,
+            Spec(_weights_gemm(self.patch_w, a=buf.patches, bias=self.patch_b, residual=self.pos,
                                res_period=t, out=buf.x, out_row_offset=1, out_group=(t - 1, 1)),
                  "embed.patch", parts),
         ]

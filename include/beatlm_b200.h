@@ -242,6 +242,11 @@ typedef struct bl_gemm_args {
     float norm_eps;
     void* norm_sync;
     uint64_t norm_sync_bytes;
+    /* Nonzero: b, bias and chan_scale are not written by the kernel launched
+     * just before this one on the stream, so they may be fetched before that
+     * kernel has finished (programmatic dependent launch; a, residual and the
+     * outputs always wait for it). Model weights qualify. */
+    uint32_t weights_static;
 } bl_gemm_args;
 
 int bl_gemm(const bl_gemm_args* args, void* stream);
