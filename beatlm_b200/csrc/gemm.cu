@@ -108,6 +108,7 @@ struct Tail {
     uint64_t acc_full[2];   // accumulator b holds a finished tile (the persistent
     uint64_t acc_empty[2];  // kernel alternates two; the one-tile kernel uses [0])
     uint64_t drain;
+    uint64_t conv[kMaxStages];  // gemm_ln_staged: a stage's A tile is normalised
     uint32_t tmem_base;
     int abort;
     // the tile's bias and channel-scale columns, staged by the epilogue warps
@@ -941,6 +942,261 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// The LayerNorm prologue with its rows brought by TMA (one tile per CTA):
+// A = LayerNorm(x) for f32 rows x whose per-row statistics the GEMM that
+// wrote x left as (mean, M2) per column slice. A stage holds a k-block of x
+// (128 rows x 64 f32, unswizzled, by TMA), the 16-bit A tile the epilogue
+// warps normalise from it into the MMA's swizzled layout, and the B tile.
+// The epilogue warps are free while the main loop runs, as each CTA has
+// one tile; they then run the epilogue. Barriers per stage: full (x and B
+// landed), conv (A written), empty (the MMAs are done with the stage).
+constexpr uint32_t kTileX = BM * BK * 4;  // 32 KiB
+
+template <int BN>
+struct LnLayout {
+    static constexpr uint32_t kTileB = BN * BK * 2;
+    static constexpr uint32_t kStage = kTileX + kTileA + kTileB;
+    static constexpr int kStages =
+        static_cast<int>((kSmemLimit - 4096 - kEpiBytes) / kStage) < kMaxStages
+            ? static_cast<int>((kSmemLimit - 4096 - kEpiBytes) / kStage)
+            : kMaxStages;
+};
+
+template <int BN>
+constexpr size_t ln_smem_bytes() {
+    return 1024 + LnLayout<BN>::kStages * LnLayout<BN>::kStage + kEpiBytes + sizeof(Tail);
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_ln_staged(const __grid_constant__ CUtensorMap tm_x,
+                   const __grid_constant__ CUtensorMap tm_b,
+                   const __grid_constant__ CUtensorMap tm_o, const Params p) {
+    using L = LnLayout<BN>;
+    constexpr int STAGES = L::kStages;
+    static_assert(STAGES >= 2, "a stage ring needs two stages");
+    constexpr uint32_t kCols = Layout<BN>::kTmemCols;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint8_t* epi = smem + STAGES * L::kStage;
+    Tail* tail = reinterpret_cast<Tail*>(epi + kEpiBytes);
+    volatile int* abort = &tail->abort;
+    auto sX = [&](int s) { return smem + s * L::kStage; };
+    auto sA = [&](int s) { return smem + s * L::kStage + kTileX; };
+    auto sB = [&](int s) { return smem + s * L::kStage + kTileX + kTileA; };
+
+    const int warp = warp_id();
+    const int lane = lane_id();
+    const int nk = p.K / BK;
+    const int t = static_cast<int>(blockIdx.x);  // the grid has one CTA per tile
+    const int m0 = (p.m_tile0 + t % p.m_tiles) * BM;
+    const int n0 = (t / p.m_tiles) * BN;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(smem_u32(&tail->full[s]), 1);
+            mbar_init(smem_u32(&tail->conv[s]), 4);
+            mbar_init(smem_u32(&tail->empty[s]), 1);
+        }
+        mbar_init(smem_u32(&tail->acc_full[0]), 1);
+        mbar_init(smem_u32(&tail->drain), 1);
+        tail->abort = 0;
+        fence_barrier_init();
+        fence_proxy_async_smem();
+        tma_prefetch_desc(&tm_x);
+        tma_prefetch_desc(&tm_b);
+        if (p.tma_store) tma_prefetch_desc(&tm_o);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(&tail->tmem_base), kCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tail->tmem_base;
+    pdl_trigger();
+
+    if (warp == 0) {
+        // lane 0 arms each stage and copies x, lane 1 copies B (with
+        // weights_static the first stages' B before the dependency wait)
+        const int first = !p.weights_static ? 0 : (STAGES < nk ? STAGES : nk);
+        for (int g = 0; g < first; ++g) {
+            const uint32_t bar = smem_u32(&tail->full[g]);
+            if (lane == 0) mbar_arrive_expect_tx(bar, kTileX + L::kTileB);
+            if (lane == 1) tma_load_3d(smem_u32(sB(g)), &tm_b, 0, n0, g, bar);
+        }
+        pdl_wait();
+        int g = 0;
+        for (; g < nk; ++g) {
+            const int s = g % STAGES;
+            bool r = true;
+            if (lane == 0 && g >= STAGES)
+                r = mbar_wait(smem_u32(&tail->empty[s]), ((g / STAGES) - 1) & 1, abort, p.status,
+                              ST_TIMEOUT_TMA, g);
+            if (!__all_sync(0xFFFFFFFFu, r)) break;
+            const uint32_t bar = smem_u32(&tail->full[s]);
+            if (lane == 0) {
+                if (g >= first) mbar_arrive_expect_tx(bar, kTileX + L::kTileB);
+                tma_load_2d(smem_u32(sX(s)), &tm_x, g * BK, m0, bar);
+            } else if (lane == 1 && g >= first) {
+                tma_load_3d(smem_u32(sB(s)), &tm_b, 0, n0, g, bar);
+            }
+            __syncwarp();
+        }
+        if (lane == 0 && *abort) {
+            for (int s = 0; s < STAGES && s < g; ++s) {
+                const int uses = (g - s - 1) / STAGES + 1;
+                mbar_wait(smem_u32(&tail->full[s]), (uses - 1) & 1, nullptr, p.status,
+                          ST_TIMEOUT_DRAIN, s);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        const bool elected = elect_one();
+        const uint32_t idesc = idesc_f16(BM, BN, p.ab_fmt, p.ab_fmt, 0, 0);
+        bool ok = true;
+        for (int kb = 0; kb < nk; ++kb) {
+            const int s = kb % STAGES;
+            bool r = true;
+            if (elected)
+                r = mbar_wait(smem_u32(&tail->conv[s]), (kb / STAGES) & 1, abort, p.status,
+                              ST_TIMEOUT_MMA, kb);
+            ok = __all_sync(0xFFFFFFFFu, r);
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t a = smem_u32(sA(s)), b = smem_u32(sB(s));
+            if (elected) {
+#pragma unroll
+                for (int k = 0; k < BK / 16; ++k)
+                    mma_ss(tmem, desc_k(a + 32 * k), desc_k(b + 32 * k), idesc,
+                           (kb > 0 || k > 0) ? 1u : 0u);
+                if (kb + STAGES < nk) mma_commit(smem_u32(&tail->empty[s]));
+            }
+            __syncwarp();
+        }
+        if (elected) {
+            if (ok) {
+                mma_commit(smem_u32(&tail->acc_full[0]));
+            } else {
+                mma_commit(smem_u32(&tail->drain));
+                mbar_wait(smem_u32(&tail->drain), 0, nullptr, p.status, ST_TIMEOUT_DRAIN, 0xD);
+            }
+        }
+        __syncwarp();
+    } else {
+        constexpr unsigned kFull = 0xFFFFFFFFu;
+        const int sub = warp & 3;
+        const int row = sub * 32 + lane;
+        const int dt = p.ab_fmt ? BL_BF16 : BL_F16;
+        pdl_wait();  // x's statistics come from the previous kernel
+        // lane r: mean and 1/std of the warp's row r, from the slices'
+        // (mean, M2) (equal counts: the mean of means, then the M2s plus
+        // each slice's squared offset times its count)
+        float my_mean = 0.0f, my_rstd = 0.0f;
+        {
+            const int gr = m0 + row;
+            if (gr < p.M) {
+                const float2* st = p.ln_stats + static_cast<long long>(gr) * p.ln_stats_parts;
+                const float nper = static_cast<float>(p.K / p.ln_stats_parts);
+                float2 part[kMaxNormParts];
+#pragma unroll
+                for (int q = 0; q < kMaxNormParts; ++q)
+                    if (q < p.ln_stats_parts) part[q] = st[q];
+                float sm = 0.0f;
+#pragma unroll
+                for (int q = 0; q < kMaxNormParts; ++q)
+                    if (q < p.ln_stats_parts) sm += part[q].x;
+                const float mean = sm / static_cast<float>(p.ln_stats_parts);
+                float m2 = 0.0f;
+#pragma unroll
+                for (int q = 0; q < kMaxNormParts; ++q)
+                    if (q < p.ln_stats_parts)
+                        m2 += part[q].y + (part[q].x - mean) * (part[q].x - mean) * nper;
+                my_mean = mean;
+                my_rstd = rsqrtf(m2 / static_cast<float>(p.K) + p.eps);
+            }
+        }
+        // Every lane needs all 32 rows' (1/std, -mean/std): gathered once
+        // into registers (rows past M get 0 and 0: their A rows hold beta,
+        // and their output rows are never stored).
+        float ra[32], rc2[32];
+#pragma unroll
+        for (int r2 = 0; r2 < 32; ++r2) {
+            const float rs = __shfl_sync(kFull, my_rstd, r2);
+            ra[r2] = rs;
+            rc2[r2] = -__shfl_sync(kFull, my_mean, r2) * rs;
+        }
+        bool ok = true;
+        const int chunk = lane >> 2, off = (lane & 3) * 4;
+        for (int kb = 0; kb < nk; ++kb) {
+            const int s = kb % STAGES;
+            const int k = kb * BK + 2 * lane;
+            const float2 g = __ldg(reinterpret_cast<const float2*>(p.gamma + k));
+            const float2 b = __ldg(reinterpret_cast<const float2*>(p.beta + k));
+            const unsigned long long g2 = f2pack(g.x, g.y), b2 = f2pack(b.x, b.y);
+            bool r = true;
+            if (lane == 0)
+                r = mbar_wait(smem_u32(&tail->full[s]), (kb / STAGES) & 1, abort, p.status,
+                              ST_TIMEOUT_SOFTMAX, 0x400 + kb);
+            ok = __all_sync(kFull, r);
+            if (!ok) break;
+            const uint8_t* xs = sX(s) + sub * 32 * (BK * 4) + lane * 8;
+            uint8_t* tile = sA(s) + sub * 32 * 128 + off;
+            // y = (x * rstd - mean * rstd) * gamma + beta, two packed FMAs a
+            // pair. Sixteen rows are read before any is written: the stores
+            // may alias the loads as far as the compiler knows, so mixing them
+            // would serialise every row's latency.
+#pragma unroll
+            for (int h = 0; h < 32; h += 16) {
+                float2 xv[16];
+#pragma unroll
+                for (int r2 = 0; r2 < 16; ++r2)
+                    xv[r2] = *reinterpret_cast<const float2*>(xs + (h + r2) * (BK * 4));
+#pragma unroll
+                for (int r2 = 0; r2 < 16; ++r2) {
+                    const int rr = h + r2;
+                    const unsigned long long t2 = ffma2(f2pack(xv[r2].x, xv[r2].y),
+                                                        f2pack(ra[rr], ra[rr]),
+                                                        f2pack(rc2[rr], rc2[rr]));
+                    float y0, y1;
+                    f2unpack(ffma2(t2, g2, b2), y0, y1);
+                    *reinterpret_cast<uint32_t*>(tile + rr * 128 + ((chunk ^ (rr & 7)) << 4)) =
+                        pack2(y0, y1, dt);
+                }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&tail->conv[s]));
+        }
+        // ------------------------------------------------------ epilogue
+        const RowCtx rc = row_ctx(p, m0 + row);
+        stage_vectors<BN>(p, tail, n0);
+        epilogue_all(true);
+        float rv0[32];
+        prefetch_residual(p, rc, n0, rv0);
+        if (ok) ok = mbar_wait(smem_u32(&tail->acc_full[0]), 0, abort, p.status,
+                               ST_TIMEOUT_SOFTMAX, 0xE);
+        if (epilogue_all(ok)) {
+            tc_fence_after();
+            store_tile<BN>(p, tail, tmem + (static_cast<uint32_t>(sub * 32) << 16), n0, rc, rv0,
+                           p.tma_store ? &tm_o : nullptr, epi + sub * kEpiBlock,
+                           m0 + sub * 32 + p.out_row_offset);
+        }
+        if (p.tma_store && lane == 0) bulk_wait_all();
+        __syncwarp();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, kCols);
+    }
+}
+
 int sm_count() {
     static int n = 0;
     if (n == 0) {
@@ -989,6 +1245,21 @@ int pick_kc(int bn, uint32_t k) {
         if (nk % kc == 0 && (kSmemLimit - 4096 - kEpiBytes) / stage >= 2) return kc;
     }
     return 1;
+}
+
+template <int BN>
+int prepare_ln_staged(const CUtensorMap& tx, const CUtensorMap& tb, const CUtensorMap& to,
+                      const Params& p, Launch* out) {
+    constexpr size_t smem = ln_smem_bytes<BN>();
+    out->op = 2;
+    auto kern = gemm_ln_staged<BN>;
+    BL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(smem)));
+    const dim3 grid(p.m_tiles * (p.N / BN));
+    out->run = [=](cudaStream_t s) {
+        return launch_k(kern, grid, dim3(kThreads), smem, s, tx, tb, to, p);
+    };
+    return BL_OK;
 }
 
 template <int BN, bool kLn>
@@ -1143,9 +1414,25 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
 
     CUtensorMap ta{}, tb{};
     int rc;
+    // A LayerNorm prologue whose statistics were left by the GEMM that wrote
+    // x runs with its rows brought by TMA when every tile fits one CTA per SM
+    // (gemm_ln_staged); otherwise, or without statistics, the epilogue warps
+    // load the rows (gemm_kernel).
+    const uint64_t ldx = g.ln_ldx ? g.ln_ldx : g.k;
+    const uint64_t row_tiles = (std::min(row_end, g.m) + BM - 1) / BM - row_begin / BM;
+    const bool staged = ln && g.ln_stats != nullptr && g.ln_stats_parts <= kMaxNormParts &&
+                        row_tiles * (g.n / bn) <= static_cast<uint64_t>(sm_count()) &&
+                        (ldx * 4) % 16 == 0 && (reinterpret_cast<uintptr_t>(g.ln_x) & 15) == 0;
     const int kc = ln ? 1 : pick_kc(bn, g.k);
     const uint64_t ldb = g.ldb ? g.ldb : g.k;
-    if (!ln) {
+    if (staged) {
+        const uint64_t dx[2] = {g.k, g.m};
+        const uint32_t bx[2] = {BK, BM};
+        if ((rc = make_tmap_2d(&ta, g.ln_x, 4, dx, ldx * 4, bx, 0)) != BL_OK) return rc;
+        const uint64_t db[3] = {BK, g.n, g.k / BK}, sb[2] = {ldb * 2, BK * 2};
+        const uint32_t bb[3] = {BK, static_cast<uint32_t>(bn), 1};
+        if ((rc = make_tmap_16bit_3d(&tb, g.b, db, sb, bb)) != BL_OK) return rc;
+    } else if (!ln) {
         // Persistent kernel: 3-D views (64 columns, rows, 64-column block)
         // so one copy brings kc consecutive k-blocks of 128 (A) or bn (B)
         // rows.
@@ -1197,7 +1484,7 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
     if (row_begin % BM != 0 || row_begin >= row_end || p.m_tiles <= 0)
         return fail(BL_ERR_INVALID, "gemm: row part [%u, %u) is not whole 128-row tiles", row_begin, row_end);
     p.status = status_ptr();
-    if (ln) {
+    if (ln && !staged) {
         switch (bn) {
             case 32: return prepare_t<32, true>(ta, tb, p, out);
             case 64: return prepare_t<64, true>(ta, tb, p, out);
@@ -1210,7 +1497,7 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
         const uint64_t nld = g.norm_out_ld ? g.norm_out_ld : g.n;
         const uint64_t dims[2] = {g.n, g.m};
         const uint32_t box[2] = {32, 32};
-        if ((rc = make_tmap_store_2d(&tn, g.norm_out, 2, dims, nld * 2, box, 64)) != BL_OK)
+        if ((rc = make_tmap_2d(&tn, g.norm_out, 2, dims, nld * 2, box, 64)) != BL_OK)
             return rc;
         p.norm_out = g.norm_out;
         p.norm_dtype = g.norm_out_dtype;
@@ -1228,10 +1515,18 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
     if (g.out_group_rows == 0 && dtype_size(dts[1]) == dtype_size(dts[0])) {
         const uint64_t dims[2] = {g.n, static_cast<uint64_t>(g.m) + g.out_row_offset};
         const uint32_t box[2] = {32, 32};
-        if ((rc = make_tmap_store_2d(&to, g.out, esz, dims, out_ld * esz, box,
+        if ((rc = make_tmap_2d(&to, g.out, esz, dims, out_ld * esz, box,
                                      esz == 4 ? 128 : 64)) != BL_OK)
             return rc;
         p.tma_store = 1;
+    }
+    if (staged) {
+        switch (bn) {
+            case 32: return prepare_ln_staged<32>(ta, tb, to, p, out);
+            case 64: return prepare_ln_staged<64>(ta, tb, to, p, out);
+            case 96: return prepare_ln_staged<96>(ta, tb, to, p, out);
+            default: return prepare_ln_staged<128>(ta, tb, to, p, out);
+        }
     }
     switch (bn) {
         case 32: return prepare_persistent<32>(ta, tb, to, tn, p, kc, out);

@@ -27,12 +27,13 @@ Status* status_ptr();
 int make_tmap_16bit_3d(CUtensorMap* map, const void* base, const uint64_t dims[3],
                        const uint64_t strides_bytes[2], const uint32_t box[3]);
 
-// A 2-D map for stores: elements of `esz` bytes (2 or 4), swizzle of
-// `swizzle_bytes` (64 or 128) matching the box's inner extent.
-int make_tmap_store_2d(CUtensorMap* map, void* base, int esz, const uint64_t dims[2],
-                       uint64_t row_stride_bytes, const uint32_t box[2], int swizzle_bytes);
+// A 2-D map of elements of `esz` bytes (2 or 4) with a swizzle of
+// `swizzle_bytes` (0 = none, 64 or 128) matching the box's inner extent; zero
+// fill out of bounds.
+int make_tmap_2d(CUtensorMap* map, const void* base, int esz, const uint64_t dims[2],
+                 uint64_t row_stride_bytes, const uint32_t box[2], int swizzle_bytes);
 
-// Same, 2-D.
+// The map of make_tmap_16bit_3d in two dimensions.
 int make_tmap_16bit_2d(CUtensorMap* map, const void* base, const uint64_t dims[2],
                        uint64_t row_stride_bytes, const uint32_t box[2]);
 

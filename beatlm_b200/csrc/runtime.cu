@@ -92,14 +92,16 @@ int make_tmap_16bit_3d(CUtensorMap* map, const void* base, const uint64_t dims[3
     return encode(map, base, 3, d, s, b);
 }
 
-int make_tmap_store_2d(CUtensorMap* map, void* base, int esz, const uint64_t dims[2],
-                       uint64_t row_stride_bytes, const uint32_t box[2], int swizzle_bytes) {
+int make_tmap_2d(CUtensorMap* map, const void* base, int esz, const uint64_t dims[2],
+                 uint64_t row_stride_bytes, const uint32_t box[2], int swizzle_bytes) {
     cuuint64_t d[2] = {dims[0], dims[1]};
     cuuint64_t s[1] = {row_stride_bytes};
     cuuint32_t b[2] = {box[0], box[1]};
     return encode(map, base, 2, d, s, b,
                   esz == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16,
-                  swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+                  swizzle_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                  : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                        : CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
 int make_tmap_16bit_2d(CUtensorMap* map, const void* base, const uint64_t dims[2],

@@ -359,9 +359,9 @@ class Encoder:
         ``fused_ln``: the LayerNorms inside the blocks are fed by statistics
         from the GEMM before them (``block_specs``). Off by default: measured
         at ViT-S (one frame), the QKV and fc1 GEMMs that normalise their A
-        operand from the f32 rows through the load/store units take longer
-        than a standalone LayerNorm plus a GEMM that loads 16-bit rows by TMA
-        (1129 against 1345 frames/s). ``fused_ln="epilogue"``: the GEMMs that
+        operand from the f32 rows (brought by TMA, normalised by the epilogue
+        warps) take longer than a standalone LayerNorm plus a GEMM that loads
+        16-bit rows by TMA (676 against 633 us per frame). ``fused_ln="epilogue"``: the GEMMs that
         write x also write the next LayerNorm's output (``block_specs``);
         needs every 32-column tile of those GEMMs resident at once (ViT-S
         at one frame: 132 tiles). Also measured slower at ViT-S, one frame:
