@@ -248,7 +248,7 @@ __device__ __forceinline__ void prefetch_residual(const Params& p, const RowCtx&
 // writes hit distinct banks, and one lane stores the block with first output
 // row `box_row`; rows past the output are clipped by the map. Without it each
 // thread stores its own row.
-template <int BN>
+template <int BN, int ACT = -1>
 __device__ __forceinline__ void store_tile(const Params& p, const Tail* tail, uint32_t t_lane,
                                            int n0, const RowCtx& rc, const float* rv0,
                                            const CUtensorMap* tmo = nullptr,
@@ -276,13 +276,16 @@ __device__ __forceinline__ void store_tile(const Params& p, const Tail* tail, ui
                 v[i] += b.x; v[i + 1] += b.y; v[i + 2] += b.z; v[i + 3] += b.w;
             }
         }
-        if (p.act == 1) {
+        // ACT >= 0: the activation is fixed at compile time (0 covers none and
+        // ReLU), so the kernel carries only its own epilogue code
+        const int act = ACT < 0 ? p.act : ACT == 0 ? (p.act == 1 ? 1 : 0) : ACT;
+        if (act == 1) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = fmaxf(v[i], 0.0f);
-        } else if (p.act == 2) {
+        } else if (act == 2) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
-        } else if (p.act == 3) {
+        } else if (act == 3) {
 #pragma unroll
             for (int i = 0; i < 32; i += 2) gelu_erf2(v[i], v[i + 1]);
         }
@@ -734,7 +737,7 @@ __device__ bool norm_tile(const Params& p, const CUtensorMap* tmn, const float* 
 // epilogue warps drain tile j from one while the MMA thread fills tile j + 1
 // in the other, and the TMA ring runs on across tiles, so the epilogue and the
 // CTA's set-up leave the critical path once a CTA has more than one tile.
-template <int BN, int KC>
+template <int BN, int KC, int ACT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_persistent(const __grid_constant__ CUtensorMap tm_a,
                     const __grid_constant__ CUtensorMap tm_b,
@@ -915,7 +918,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!epilogue_all(ok)) break;
             tc_fence_after();
             float keep[32];
-            store_tile<BN>(p, tail,
+            store_tile<BN, ACT>(p, tail,
                            tmem + static_cast<uint32_t>(b) * L::kTmemCols +
                                (static_cast<uint32_t>(sub * 32) << 16),
                            n0, rc, rv0, p.tma_store ? &tm_o : nullptr, epi + sub * kEpiBlock,
@@ -1208,12 +1211,12 @@ int sm_count() {
     return n;
 }
 
-template <int BN, int KC>
+template <int BN, int KC, int ACT>
 int prepare_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
                        const CUtensorMap& tn, const Params& p, Launch* out) {
     constexpr size_t smem = smem_bytes<BN, KC, true>();
     out->op = 2;
-    auto kern = gemm_persistent<BN, KC>;
+    auto kern = gemm_persistent<BN, KC, ACT>;
     BL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(smem)));
     const int tiles = p.m_tiles * (p.N / BN);
@@ -1224,16 +1227,25 @@ int prepare_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
     return BL_OK;
 }
 
-template <int BN>
+template <int BN, int ACT>
 int prepare_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
                        const CUtensorMap& tn, const Params& p, int kc, Launch* out) {
     // only the depths whose ring holds two stages are built
     if constexpr (Layout<BN, 4, true>::kStages >= 2)
-        if (kc == 4) return prepare_persistent<BN, 4>(ta, tb, to, tn, p, out);
+        if (kc == 4) return prepare_persistent<BN, 4, ACT>(ta, tb, to, tn, p, out);
     if constexpr (Layout<BN, 2, true>::kStages >= 2)
-        if (kc == 2) return prepare_persistent<BN, 2>(ta, tb, to, tn, p, out);
+        if (kc == 2) return prepare_persistent<BN, 2, ACT>(ta, tb, to, tn, p, out);
     if (kc != 1) return fail(BL_ERR_UNSUPPORTED, "gemm: no kernel for %d k-blocks per stage", kc);
-    return prepare_persistent<BN, 1>(ta, tb, to, tn, p, out);
+    return prepare_persistent<BN, 1, ACT>(ta, tb, to, tn, p, out);
+}
+
+// the activation as a compile-time epilogue variant: 0 (none or ReLU), 2, 3
+template <int BN>
+int prepare_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+                       const CUtensorMap& tn, const Params& p, int kc, Launch* out) {
+    if (p.act == 3) return prepare_persistent<BN, 3>(ta, tb, to, tn, p, kc, out);
+    if (p.act == 2) return prepare_persistent<BN, 2>(ta, tb, to, tn, p, kc, out);
+    return prepare_persistent<BN, 0>(ta, tb, to, tn, p, kc, out);
 }
 
 // k-blocks per stage of the persistent kernel: the most (4, 2, 1) that divide
