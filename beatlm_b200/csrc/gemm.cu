@@ -248,7 +248,12 @@ __device__ __forceinline__ void prefetch_residual(const Params& p, const RowCtx&
 // writes hit distinct banks, and one lane stores the block with first output
 // row `box_row`; rows past the output are clipped by the map. Without it each
 // thread stores its own row.
-template <int BN, int ACT = -1>
+// EPI: the epilogue fixed at compile time, so a kernel carries only its own
+// code (measured: the generic chain's size stalled instruction fetch). -1
+// generic (everything decided at run time); 0 plain (bias only, 16-bit out);
+// 1 bias + GELU-erf, 16-bit out; 2 bias, LayerScale and f32 residual. The
+// host picks a fixed form only where the arguments match it exactly.
+template <int BN, int EPI = -1>
 __device__ __forceinline__ void store_tile(const Params& p, const Tail* tail, uint32_t t_lane,
                                            int n0, const RowCtx& rc, const float* rv0,
                                            const CUtensorMap* tmo = nullptr,
@@ -276,9 +281,7 @@ __device__ __forceinline__ void store_tile(const Params& p, const Tail* tail, ui
                 v[i] += b.x; v[i + 1] += b.y; v[i + 2] += b.z; v[i + 3] += b.w;
             }
         }
-        // ACT >= 0: the activation is fixed at compile time (0 covers none and
-        // ReLU), so the kernel carries only its own epilogue code
-        const int act = ACT < 0 ? p.act : ACT == 0 ? (p.act == 1 ? 1 : 0) : ACT;
+        const int act = EPI < 0 ? p.act : EPI == 1 ? 3 : 0;
         if (act == 1) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = fmaxf(v[i], 0.0f);
@@ -289,18 +292,18 @@ __device__ __forceinline__ void store_tile(const Params& p, const Tail* tail, ui
 #pragma unroll
             for (int i = 0; i < 32; i += 2) gelu_erf2(v[i], v[i + 1]);
         }
-        if (p.scale != 1.0f) {
+        if (EPI < 0 && p.scale != 1.0f) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] *= p.scale;
         }
-        if (p.chan_scale != nullptr) {
+        if (EPI < 0 ? p.chan_scale != nullptr : EPI == 2) {
 #pragma unroll
             for (int i = 0; i < 32; i += 4) {
                 const float4 s = *reinterpret_cast<const float4*>(tail->chan + c * 32 + i);
                 v[i] *= s.x; v[i + 1] *= s.y; v[i + 2] *= s.z; v[i + 3] *= s.w;
             }
         }
-        if (p.residual != nullptr && live) {
+        if ((EPI < 0 ? p.residual != nullptr : EPI == 2) && live) {
             if (c == 0) {
 #pragma unroll
                 for (int i = 0; i < 32; ++i) v[i] += rv0[i];
@@ -316,7 +319,7 @@ __device__ __forceinline__ void store_tile(const Params& p, const Tail* tail, ui
                 }
             }
         }
-        if (p.stats_out != nullptr) {
+        if (EPI < 0 && p.stats_out != nullptr) {
             // this chunk's mean and M2, merged into the slice's (Chan et al.)
             float cs = 0.0f;
 #pragma unroll
@@ -334,8 +337,8 @@ __device__ __forceinline__ void store_tile(const Params& p, const Tail* tail, ui
 #pragma unroll
             for (int i = 0; i < 32; ++i) keep[i] = v[i];
         }
-        const int dt = col >= p.split_col ? p.out_dtype_hi : p.out_dtype;
-        if (tmo != nullptr) {
+        const int dt = EPI == 2 ? BL_F32 : col >= p.split_col ? p.out_dtype_hi : p.out_dtype;
+        if (EPI >= 0 || tmo != nullptr) {
             // 4-byte blocks fill `buf`; 2-byte blocks alternate between its
             // halves, so a block is written while the previous one is still
             // being read out (a tile's first block waits for every earlier one)
@@ -383,7 +386,7 @@ __device__ __forceinline__ void store_tile(const Params& p, const Tail* tail, ui
                                   pack2(v[8 * i + 6], v[8 * i + 7], dt));
         }
     }
-    if (p.stats_out != nullptr && live)
+    if (EPI < 0 && p.stats_out != nullptr && live)
         p.stats_out[orow * p.stats_parts + n0 / BN] = make_float2(run_mean, run_m2);
 }
 
@@ -737,7 +740,7 @@ __device__ bool norm_tile(const Params& p, const CUtensorMap* tmn, const float* 
 // epilogue warps drain tile j from one while the MMA thread fills tile j + 1
 // in the other, and the TMA ring runs on across tiles, so the epilogue and the
 // CTA's set-up leave the critical path once a CTA has more than one tile.
-template <int BN, int KC, int ACT>
+template <int BN, int KC, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_persistent(const __grid_constant__ CUtensorMap tm_a,
                     const __grid_constant__ CUtensorMap tm_b,
@@ -918,7 +921,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!epilogue_all(ok)) break;
             tc_fence_after();
             float keep[32];
-            store_tile<BN, ACT>(p, tail,
+            store_tile<BN, EPI>(p, tail,
                            tmem + static_cast<uint32_t>(b) * L::kTmemCols +
                                (static_cast<uint32_t>(sub * 32) << 16),
                            n0, rc, rv0, p.tma_store ? &tm_o : nullptr, epi + sub * kEpiBlock,
@@ -1211,12 +1214,12 @@ int sm_count() {
     return n;
 }
 
-template <int BN, int KC, int ACT>
+template <int BN, int KC, int EPI>
 int prepare_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
                        const CUtensorMap& tn, const Params& p, Launch* out) {
     constexpr size_t smem = smem_bytes<BN, KC, true>();
     out->op = 2;
-    auto kern = gemm_persistent<BN, KC, ACT>;
+    auto kern = gemm_persistent<BN, KC, EPI>;
     BL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(smem)));
     const int tiles = p.m_tiles * (p.N / BN);
@@ -1227,25 +1230,40 @@ int prepare_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
     return BL_OK;
 }
 
-template <int BN, int ACT>
+template <int BN, int EPI>
 int prepare_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
                        const CUtensorMap& tn, const Params& p, int kc, Launch* out) {
     // only the depths whose ring holds two stages are built
     if constexpr (Layout<BN, 4, true>::kStages >= 2)
-        if (kc == 4) return prepare_persistent<BN, 4, ACT>(ta, tb, to, tn, p, out);
+        if (kc == 4) return prepare_persistent<BN, 4, EPI>(ta, tb, to, tn, p, out);
     if constexpr (Layout<BN, 2, true>::kStages >= 2)
-        if (kc == 2) return prepare_persistent<BN, 2, ACT>(ta, tb, to, tn, p, out);
+        if (kc == 2) return prepare_persistent<BN, 2, EPI>(ta, tb, to, tn, p, out);
     if (kc != 1) return fail(BL_ERR_UNSUPPORTED, "gemm: no kernel for %d k-blocks per stage", kc);
-    return prepare_persistent<BN, 1, ACT>(ta, tb, to, tn, p, out);
+    return prepare_persistent<BN, 1, EPI>(ta, tb, to, tn, p, out);
 }
 
-// the activation as a compile-time epilogue variant: 0 (none or ReLU), 2, 3
+// The epilogue form (store_tile's EPI) these arguments match exactly, or -1.
+int epilogue_form(const Params& p) {
+    if (!p.tma_store || p.scale != 1.0f || p.stats_out != nullptr || p.norm_out != nullptr)
+        return -1;
+    const bool wide = p.out_dtype == BL_F32, one_type = p.out_dtype_hi == p.out_dtype;
+    const bool plain_tail = p.chan_scale == nullptr && p.residual == nullptr && !wide;
+    if (plain_tail && p.act == 0) return 0;
+    if (plain_tail && p.act == 3) return 1;
+    if (p.act == 0 && p.chan_scale != nullptr && p.residual != nullptr && wide && one_type)
+        return 2;
+    return -1;
+}
+
 template <int BN>
 int prepare_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
                        const CUtensorMap& tn, const Params& p, int kc, Launch* out) {
-    if (p.act == 3) return prepare_persistent<BN, 3>(ta, tb, to, tn, p, kc, out);
-    if (p.act == 2) return prepare_persistent<BN, 2>(ta, tb, to, tn, p, kc, out);
-    return prepare_persistent<BN, 0>(ta, tb, to, tn, p, kc, out);
+    switch (epilogue_form(p)) {
+        case 0: return prepare_persistent<BN, 0>(ta, tb, to, tn, p, kc, out);
+        case 1: return prepare_persistent<BN, 1>(ta, tb, to, tn, p, kc, out);
+        case 2: return prepare_persistent<BN, 2>(ta, tb, to, tn, p, kc, out);
+        default: return prepare_persistent<BN, -1>(ta, tb, to, tn, p, kc, out);
+    }
 }
 
 // k-blocks per stage of the persistent kernel: the most (4, 2, 1) that divide
