@@ -79,8 +79,8 @@ struct Params {
     int splits;       // key splits; gridDim.z = batch * splits
     int cluster;      // 1: the splits of a query group are one cluster, combined in DSMEM
     int kv_tiles;     // ceil(tokens / BN)
-    float* part_o;    // [unit][split][ROWS][HD]
-    float* part_ml;   // [unit][split][ROWS][2]
+    uint4* part_o;    // [unit][split][ROWS][HD / 8]: f16 O / l of each row
+    float2* part_ml;  // [unit][split][ROWS]: (max, sum)
     unsigned* counters;  // [unit]
     unsigned long long* trace;  // optional per-CTA timeline
     Status* status;
@@ -106,25 +106,32 @@ struct SmemTail {
     uint64_t o_done[QT];
     uint64_t o_final[QT];  // the last PV of tile t is complete
     uint64_t drain;
+    uint64_t parts_full;  // cluster combine: the partials this CTA combines have landed
     uint32_t tmem_base;
     int abort;
     unsigned last;  // this CTA combines the splits
 };
 
-constexpr size_t kSmemBytes = 1024 /*align slack*/ + QT * kTileBytes /*Q*/ +
-                              STAGES * 2 * kTileBytes /*K,V*/ + sizeof(SmemTail);
-// Cluster combine: a row's partial is 17 float4s (64 O values, then max and
-// sum), stored k-major in the K/V ring: float4 k of every row of a rank's
-// block is contiguous, so a warp's remote store of one float4 per row covers
-// 512 consecutive bytes (row-major rows made it 32 separate 16-byte pieces,
-// measured 3 us for the push at ViT-S), and the owner's reads are
-// conflict-free.
-constexpr int kPartVec = HD / 4 + 1;
-constexpr int kPartStride = 4 * kPartVec;  // floats per row
 constexpr int kMaxClusterSplits = 8;  // portable cluster size
-// A CTA receives splits * ceil(8 / splits) warps of 32 rows of partials, at
-// most 14 warps (7 splits); they live in the K/V ring.
-static_assert(14 * 32 * kPartStride * 4 <= 2 * STAGES * kTileBytes, "partials exceed the ring");
+// Cluster combine: a pushed partial is 9 vectors of 16 bytes (the row's O / l
+// as 64 f16, then (max, sum)), stored k-major: vector v of every row a source
+// pushes is contiguous, so a warp's remote store covers 512 consecutive bytes
+// and the owner's reads are conflict-free. The area holds the splits - 1
+// sources of up to ceil(8 / splits) warps of rows: most at 7 splits.
+constexpr int kPartVecs = HD / 8 + 1;
+constexpr size_t part_area(int splits) {
+    return static_cast<size_t>(splits - 1) * kPartVecs * ((ROWS / 32 + splits - 1) / splits) *
+           32 * 16;
+}
+constexpr size_t max_part_area(int s = 2) {
+    return s > kMaxClusterSplits ? 0
+                                 : (part_area(s) > max_part_area(s + 1) ? part_area(s)
+                                                                        : max_part_area(s + 1));
+}
+constexpr size_t kPartArea = max_part_area();
+constexpr size_t kSmemBytes = 1024 /*align slack*/ + QT * kTileBytes /*Q*/ +
+                              STAGES * 2 * kTileBytes /*K,V*/ + kPartArea + sizeof(SmemTail);
+static_assert(kSmemBytes <= 232448, "shared memory");
 
 __device__ __forceinline__ uint64_t desc_kmajor(uint32_t addr) {
     return sdesc_sw128(addr, 16, 1024);
@@ -184,8 +191,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* sQ = smem;                                          // tile t at + t*kTileBytes
     uint8_t* sK = smem + QT * kTileBytes;                        // stage s at + s*kTileBytes
     uint8_t* sV = smem + QT * kTileBytes + STAGES * kTileBytes;  // stage s at + s*kTileBytes
-    SmemTail* tail =
-        reinterpret_cast<SmemTail*>(smem + QT * kTileBytes + 2 * STAGES * kTileBytes);
+    uint8_t* sP = smem + QT * kTileBytes + 2 * STAGES * kTileBytes;  // cluster partials
+    SmemTail* tail = reinterpret_cast<SmemTail*>(sP + kPartArea);
     volatile int* abort = &tail->abort;
 
     const int warp = warp_id();
@@ -215,6 +222,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(smem_u32(&tail->o_final[t]), 1);
         }
         mbar_init(smem_u32(&tail->drain), 1);
+        if (p.cluster) {
+            // one arrival per pushing warp: the warps w = rank (mod splits) of
+            // each other CTA of the cluster
+            const int me = static_cast<int>(cluster_rank());
+            const int nw = (ROWS / 32 - me + p.splits - 1) / p.splits;
+            mbar_init(smem_u32(&tail->parts_full), static_cast<uint32_t>(nw * (p.splits - 1)));
+        }
         tail->abort = 0;
         tail->last = 0;
         fence_barrier_init();
@@ -231,6 +245,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tail->tmem_base;
+    // the cluster barrier's arrive now (every CTA's barriers are initialised),
+    // its wait just before the first remote access
+    if (p.cluster) cluster_arrive();
     pdl_trigger();
     pdl_wait();
     if (threadIdx.x == 0) trace_stamp(p.trace, 1);
@@ -379,10 +396,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
         if (p.cluster) {
-            // the two cluster barriers of the split combine (softmax side below)
+            // the wait of the cluster barrier arrived on at set-up
             __syncwarp();
-            cluster_sync();
-            cluster_sync();
+            cluster_wait();
         }
     } else {
         asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
@@ -520,141 +536,135 @@ __global__ void __launch_bounds__(kThreads, 1)
         };
         bool do_store = ok && store;
         float inv_l = 1.0f / l;
-        if (p.cluster) {
-            // ------------------------------ split-key partials, cluster form
-            // Rows are owned by warp: the 32 rows of warp w (w = crow / 32) are
-            // combined in CTA w % splits of the cluster, by the very threads
-            // that hold those rows' O in registers. Every other CTA pushes its
-            // unnormalised O and (max, sum) for the row into the owner's K/V
-            // ring at [own rank][slot] (remote stores do not wait). First every
-            // CTA of the cluster must be done with its own ring: this barrier
-            // comes after each warpgroup's last PV.
-            __syncwarp();
-            cluster_sync();
-            if (threadIdx.x == 32 * kSoftmaxWarp0) trace_stamp(p.trace, 4);
-            const uint32_t me = cluster_rank();
-            const int owner = (crow >> 5) % p.splits;
-            const int slot = ((crow >> 5) / p.splits) * 32 + (crow & 31);
-            const int slots = ((ROWS / 32 + p.splits - 1) / p.splits) * 32;  // rows per owner
-            if (store && owner != static_cast<int>(me)) {
-                // float4 v of this row at [me][v][slot]
-                const uint32_t local =
-                    smem_u32(sK) + static_cast<uint32_t>((me * kPartVec * slots + slot) * 16);
-                const uint32_t dst = dsmem_addr(local, static_cast<uint32_t>(owner));
-                const uint32_t vstep = static_cast<uint32_t>(slots * 16);
+        if (p.splits > 1) {
+            // ---------------------------------------------- split-key combine
+            // Every split's partial for a row is O / l rounded to f16 (a
+            // convex combination of f16 V rows, so within f16 range) and
+            // (max, sum); the combiner forms
+            //   O = sum_s W_s (O_s / l_s) / sum_s W_s,  W_s = 2^(m_s - M) l_s
+            // over the splits in rank order, whichever form and whichever
+            // CTA combines, so both forms and every row partition give the
+            // same bits.
+            const float il = ok && l > 0.0f ? 1.0f / l : 0.0f;
+            const float mine_m = ok ? m_used : -INFINITY, mine_l = ok ? l : 0.0f;
+            uint4 on[HD / 8];
 #pragma unroll
-                for (int k = 0; k < HD; k += 4)
-                    dsmem_st4(dst + (k / 4) * vstep, o[k], o[k + 1], o[k + 2], o[k + 3]);
-                dsmem_st2(dst + (HD / 4) * vstep, ok ? m_used : -INFINITY, l);
-            }
-            do_store = false;
-        } else if (p.splits > 1) {
-            // ------------------------------------------ split-key combine
-            const size_t unit = (static_cast<size_t>(batch) * p.heads_rel + blockIdx.y) *
-                                    gridDim.x + blockIdx.x;
-            float* po = p.part_o + ((unit * p.splits + split) * ROWS + crow) * HD;
-            float* pml = p.part_ml + ((unit * p.splits + split) * ROWS + crow) * 2;
-            if (ok) {
-#pragma unroll
-                for (int k = 0; k < HD; k += 4)
-                    *reinterpret_cast<float4*>(po + k) =
-                        make_float4(o[k], o[k + 1], o[k + 2], o[k + 3]);
-                pml[0] = m_used;
-                pml[1] = l;
-            }
-            __threadfence();
-            softmax_bar();
-            if (threadIdx.x == 32 * kSoftmaxWarp0) {
-                const unsigned prev = atomicAdd(p.counters + unit, 1u);
-                tail->last = prev == static_cast<unsigned>(p.splits) - 1;
-            }
-            softmax_bar();
-            do_store = false;
-            if (tail->last) {
-                __threadfence();
-                if (store) {
-                    // O = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s
-                    const float* base_o = p.part_o + (unit * p.splits * ROWS + crow) * HD;
-                    const float* base_ml = p.part_ml + (unit * p.splits * ROWS + crow) * 2;
-                    float mxs = -INFINITY;
-                    for (int s = 0; s < p.splits; ++s) mxs = fmaxf(mxs, base_ml[s * ROWS * 2]);
-#pragma unroll
-                    for (int k = 0; k < HD; ++k) o[k] = 0.0f;
-                    float lsum = 0.0f;
-                    for (int s = 0; s < p.splits; ++s) {
-                        const float w = ex2(base_ml[s * ROWS * 2] - mxs);
-                        lsum += w * base_ml[s * ROWS * 2 + 1];
-                        const float* os = base_o + static_cast<size_t>(s) * ROWS * HD;
-#pragma unroll
-                        for (int k = 0; k < HD; k += 4) {
-                            const float4 v = *reinterpret_cast<const float4*>(os + k);
-                            o[k] += w * v.x;
-                            o[k + 1] += w * v.y;
-                            o[k + 2] += w * v.z;
-                            o[k + 3] += w * v.w;
-                        }
-                    }
-                    inv_l = 1.0f / lsum;
-                    do_store = true;
-                }
-                if (threadIdx.x == 32 * kSoftmaxWarp0) p.counters[unit] = 0u;  // self-cleaning
-            }
-        }
-        if (do_store) store_row(out_ptr(), kOutDtype, o, inv_l);
-        if (p.cluster) {
-            // ------------------------------------ cluster combine (DSMEM)
-            // The owner thread of a row combines its own partial (registers)
-            // with the ones pushed into its ring:
-            // O = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s.
-            __syncwarp();
-            cluster_sync();  // every partial has landed; nothing reads remote memory after
-            if (threadIdx.x == 32 * kSoftmaxWarp0) trace_stamp(p.trace, 5);
-            const uint32_t me = cluster_rank();
-            const int owner = (crow >> 5) % p.splits;
-            if (store && owner == static_cast<int>(me)) {
-                const int slot = ((crow >> 5) / p.splits) * 32 + (crow & 31);
-                const int slots = ((ROWS / 32 + p.splits - 1) / p.splits) * 32;
-                // [rank][float4 v][slot]
-                const float4* part = reinterpret_cast<const float4*>(sK);
-                auto vec = [&](int s, int v) -> const float4& {
-                    return part[(s * kPartVec + v) * slots + slot];
-                };
-                float mxs = ok ? m_used : -INFINITY;
-#pragma unroll
-                for (int s = 0; s < kMaxClusterSplits; ++s)
-                    if (s < p.splits && s != static_cast<int>(me))
-                        mxs = fmaxf(mxs, vec(s, HD / 4).x);
-                // splits in rank order whoever owns the row, so every row
-                // partition of the launch gives the same bits
+            for (int k = 0; k < HD / 8; ++k)
+                on[k] = make_uint4(pack_f16x2(o[8 * k] * il, o[8 * k + 1] * il),
+                                   pack_f16x2(o[8 * k + 2] * il, o[8 * k + 3] * il),
+                                   pack_f16x2(o[8 * k + 4] * il, o[8 * k + 5] * il),
+                                   pack_f16x2(o[8 * k + 6] * il, o[8 * k + 7] * il));
+            auto combine = [&](auto&& part_on, auto&& part_ml) {
+                float mxs = -INFINITY;
+                for (int sp = 0; sp < p.splits; ++sp) mxs = fmaxf(mxs, part_ml(sp).x);
                 float acc[HD];
 #pragma unroll
                 for (int k = 0; k < HD; ++k) acc[k] = 0.0f;
-                float lsum = 0.0f;
+                float wsum = 0.0f;
 #pragma unroll 1
-                for (int s = 0; s < p.splits; ++s) {
-                    if (s == static_cast<int>(me)) {
-                        const float w = ok ? ex2(m_used - mxs) : 0.0f;
-                        lsum += w * l;
+                for (int sp = 0; sp < p.splits; ++sp) {
+                    const float2 ml = part_ml(sp);
+                    const float w = ml.y > 0.0f ? ex2(ml.x - mxs) * ml.y : 0.0f;
+                    wsum += w;
 #pragma unroll
-                        for (int k = 0; k < HD; ++k) acc[k] += w * o[k];
-                        continue;
-                    }
-                    const float4 ml = vec(s, HD / 4);
-                    const float w = ex2(ml.x - mxs);
-                    lsum += w * ml.y;
+                    for (int k = 0; k < HD / 8; ++k) {
+                        const uint4 q = part_on(sp, k);
+                        const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-                    for (int k = 0; k < HD; k += 4) {
-                        const float4 v = vec(s, k / 4);
-                        acc[k] += w * v.x;
-                        acc[k + 1] += w * v.y;
-                        acc[k + 2] += w * v.z;
-                        acc[k + 3] += w * v.w;
+                        for (int e = 0; e < 4; ++e) {
+                            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&wd[e]));
+                            acc[8 * k + 2 * e] += w * f.x;
+                            acc[8 * k + 2 * e + 1] += w * f.y;
+                        }
                     }
                 }
-                store_row(out_ptr(), kOutDtype, acc, 1.0f / lsum);
+                store_row(out_ptr(), kOutDtype, acc, 1.0f / wsum);
+            };
+            do_store = false;
+            if (p.cluster) {
+                // ------------------------------ cluster form (distributed
+                // shared memory). Rows are owned by warp: the 32 rows of warp
+                // w (w = crow / 32) are combined in CTA w % splits of the
+                // cluster by the threads that hold them. Every other CTA
+                // pushes its partials for those rows into the owner's
+                // partial area at [source][vector][slot] (source = rank with
+                // the owner's own left out; vector 0..7 the f16 O / l, 8 the
+                // (max, sum)), then arrives on the owner's barrier; the
+                // owner waits for its arrivals only, not for the cluster.
+                __syncwarp();
+                cluster_wait();  // every barrier of the cluster is initialised
+                if (threadIdx.x == 32 * kSoftmaxWarp0) trace_stamp(p.trace, 4);
+                const int me = static_cast<int>(cluster_rank());
+                const int owner = (crow >> 5) % p.splits;
+                const int slot = ((crow >> 5) / p.splits) * 32 + (crow & 31);
+                const int slots = ((ROWS / 32 + p.splits - 1) / p.splits) * 32;
+                const uint32_t vstep = static_cast<uint32_t>(slots * 16);
+                if (owner != me) {
+                    const int src = me < owner ? me : me - 1;
+                    const uint32_t dst = dsmem_addr(
+                        smem_u32(sP) + static_cast<uint32_t>((src * kPartVecs * slots + slot) * 16),
+                        static_cast<uint32_t>(owner));
+                    if (store) {
+#pragma unroll
+                        for (int k = 0; k < HD / 8; ++k) dsmem_st4u(dst + k * vstep, on[k]);
+                        dsmem_st2(dst + (HD / 8) * vstep, mine_m, mine_l);
+                    }
+                    fence_cluster();
+                    __syncwarp();
+                    if (lane == 0)
+                        mbar_arrive_remote(dsmem_addr(smem_u32(&tail->parts_full),
+                                                      static_cast<uint32_t>(owner)));
+                } else {
+                    const bool got = mbar_wait_cluster(smem_u32(&tail->parts_full), 0, abort,
+                                                       p.status, ST_TIMEOUT_SOFTMAX, 0x30000 | t);
+                    if (threadIdx.x == 32 * kSoftmaxWarp0) trace_stamp(p.trace, 5);
+                    if (got && store) {
+                        const uint4* part = reinterpret_cast<const uint4*>(sP);
+                        auto at = [&](int sp, int v) -> const uint4& {
+                            const int src = sp < me ? sp : sp - 1;
+                            return part[(src * kPartVecs + v) * slots + slot];
+                        };
+                        combine(
+                            [&](int sp, int k) { return sp == me ? on[k] : at(sp, k); },
+                            [&](int sp) {
+                                if (sp == me) return make_float2(mine_m, mine_l);
+                                const uint4 q = at(sp, HD / 8);
+                                return make_float2(__uint_as_float(q.x), __uint_as_float(q.y));
+                            });
+                    }
+                }
+                if (threadIdx.x == 32 * kSoftmaxWarp0) trace_stamp(p.trace, 6);
+            } else {
+                // ------------------------------ workspace form: partials in
+                // the caller's buffer, the last CTA of the group combines (an
+                // atomic counter; nothing waits)
+                const size_t unit = (static_cast<size_t>(batch) * p.heads_rel + blockIdx.y) *
+                                        gridDim.x + blockIdx.x;
+                uint4* po = p.part_o + ((unit * p.splits + split) * ROWS + crow) * (HD / 8);
+                float2* pml = p.part_ml + (unit * p.splits + split) * ROWS + crow;
+#pragma unroll
+                for (int k = 0; k < HD / 8; ++k) po[k] = on[k];
+                *pml = make_float2(mine_m, mine_l);
+                __threadfence();
+                softmax_bar();
+                if (threadIdx.x == 32 * kSoftmaxWarp0) {
+                    const unsigned prev = atomicAdd(p.counters + unit, 1u);
+                    tail->last = prev == static_cast<unsigned>(p.splits) - 1;
+                }
+                softmax_bar();
+                if (tail->last) {
+                    __threadfence();
+                    if (store) {
+                        const uint4* bo = p.part_o + (unit * p.splits * ROWS + crow) * (HD / 8);
+                        const float2* bml = p.part_ml + unit * p.splits * ROWS + crow;
+                        combine([&](int sp, int k) { return __ldcg(bo + static_cast<size_t>(sp) * ROWS * (HD / 8) + k); },
+                                [&](int sp) { return __ldcg(bml + static_cast<size_t>(sp) * ROWS); });
+                    }
+                    if (threadIdx.x == 32 * kSoftmaxWarp0) p.counters[unit] = 0u;  // self-cleaning
+                }
             }
-            if (threadIdx.x == 32 * kSoftmaxWarp0) trace_stamp(p.trace, 6);
         }
+        if (do_store) store_row(out_ptr(), kOutDtype, o, inv_l);
     }
 
     tc_fence_before();
@@ -681,10 +691,18 @@ Plan plan(const bl_attention_args& a, int splits) {
     pl.kv_tiles = static_cast<int>((a.tokens + BN - 1) / BN);
     pl.units = static_cast<size_t>(a.batch) * (a.head_end - a.head_begin) * pl.q_ctas;
     pl.splits = splits < 1 ? 1 : (splits > pl.kv_tiles ? pl.kv_tiles : splits);
-    pl.bytes = pl.splits > 1 ? pl.units * (static_cast<size_t>(pl.splits) * ROWS * (HD + 2) *
-                                               sizeof(float) + sizeof(unsigned))
+    // per unit: splits x ROWS rows of f16 O / l (HD x 2 bytes) and (max, sum)
+    pl.bytes = pl.splits > 1 ? pl.units * (static_cast<size_t>(pl.splits) * ROWS *
+                                               (HD * 2 + 2 * sizeof(float)) +
+                                           sizeof(unsigned))
                              : 0;
     return pl;
+}
+
+// The workspace: f16 O / l, then (max, sum), then one counter per unit.
+size_t part_o_bytes(const Plan& pl) { return pl.units * pl.splits * ROWS * HD * 2; }
+size_t counters_offset(const Plan& pl) {
+    return part_o_bytes(pl) + pl.units * pl.splits * ROWS * 2 * sizeof(float);
 }
 
 // Key splits that fill the 148 SMs of a B200 in one wave when the tile grid
@@ -789,11 +807,9 @@ int prepare(const bl_attention_args& a, void* workspace, uint64_t workspace_byte
     p.kv_tiles = pl.kv_tiles;
     if (pl.splits > 1 && !cluster) {
         uint8_t* ws = static_cast<uint8_t*>(workspace);
-        const size_t po = pl.units * pl.splits * ROWS * HD * sizeof(float);
-        const size_t pm = pl.units * pl.splits * ROWS * 2 * sizeof(float);
-        p.part_o = reinterpret_cast<float*>(ws);
-        p.part_ml = reinterpret_cast<float*>(ws + po);
-        p.counters = reinterpret_cast<unsigned*>(ws + po + pm);
+        p.part_o = reinterpret_cast<uint4*>(ws);
+        p.part_ml = reinterpret_cast<float2*>(ws + part_o_bytes(pl));
+        p.counters = reinterpret_cast<unsigned*>(ws + counters_offset(pl));
     }
     p.trace = reinterpret_cast<unsigned long long*>(a.trace);
     p.status = status_ptr();
@@ -952,10 +968,8 @@ extern "C" int bl_attention_noalloc(const bl_attention_args* args, void* stream)
     if (pl.splits > 1) {
         // The array keeps the last call's contents: the split counters must
         // start at zero, so clear them (no allocation involved).
-        const size_t po = pl.units * pl.splits * attn::ROWS * attn::HD * sizeof(float);
-        const size_t pm = pl.units * pl.splits * attn::ROWS * 2 * sizeof(float);
-        BL_CUDA_TRY(cudaMemsetAsync(static_cast<unsigned char*>(scratch) + po + pm, 0,
-                                    pl.units * sizeof(unsigned), s));
+        BL_CUDA_TRY(cudaMemsetAsync(static_cast<unsigned char*>(scratch) + attn::counters_offset(pl),
+                                    0, pl.units * sizeof(unsigned), s));
     }
     return enqueue(l, s);
 }

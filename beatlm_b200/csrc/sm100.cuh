@@ -310,6 +310,56 @@ __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
                  "barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// The two halves of cluster_sync, for an arrive early and a wait late. The
+// arrive is relaxed: it follows fence_barrier_init, whose release covers
+// the barrier set-up the other CTAs rely on (a releasing arrive here was
+// measured to delay the CTA's start by ~0.5 us).
+__device__ __forceinline__ void cluster_arrive() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Arrive on an mbarrier of another CTA of the cluster (`cluster_addr` from
+// dsmem_addr), ordering this thread's earlier writes before the arrival.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
+                     cluster_addr)
+                 : "memory");
+}
+__device__ __forceinline__ void fence_cluster() {
+    asm volatile("fence.acq_rel.cluster;" ::: "memory");
+}
+// mbar_wait for a barrier that other CTAs of the cluster arrive on: the
+// phase is observed with cluster-scope acquire.
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
+                                                  volatile int* abort, Status* st,
+                                                  uint32_t code, uint32_t where) {
+    auto probe = [&]() {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(bar), "r"(parity)
+            : "memory");
+        return ok != 0;
+    };
+    if (probe()) return true;
+    const long long t0 = clock64();
+    for (uint32_t spin = 1;; ++spin) {
+        if (probe()) return true;
+        if ((spin & 255u) == 0u) {
+            if (abort != nullptr && *abort) return false;
+            if (clock64() - t0 > kWaitLimitCycles) {
+                if (abort != nullptr) *abort = 1;
+                record_status(st, code, where);
+                return false;
+            }
+        }
+    }
+}
 __device__ __forceinline__ uint32_t cluster_rank() {
     uint32_t r;
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -365,6 +415,11 @@ __device__ __forceinline__ unsigned long long fmul2(unsigned long long a, unsign
 __device__ __forceinline__ void dsmem_st4(uint32_t addr, float a, float b, float c, float d) {
     asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};"
                  ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
+__device__ __forceinline__ void dsmem_st4u(uint32_t addr, uint4 v) {
+    asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x),
+                 "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
 }
 __device__ __forceinline__ void dsmem_st2(uint32_t addr, float a, float b) {
     asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(a), "f"(b)
