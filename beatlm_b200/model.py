@@ -527,6 +527,40 @@ class Encoder:
         self.program(frames, layers).encode_all(stream)
         return self.features(frames, layers)
 
+    def capture_host(self, frames: int, host_image, host_features: list, stream=None):
+        """One CUDA graph of a whole host-to-host pass over `frames` frames:
+        the pinned ``host_image`` (f32 NHWC) copied in, the encoder program,
+        and each feature map copied out to its pinned ``host_features[j]`` on
+        a second stream as soon as its LayerNorm has run, so the copies of
+        the early features overlap the later blocks. Returns the
+        ``torch.cuda.CUDAGraph``; ``replay()`` on a stream runs one pass."""
+        import torch
+        prog = self.program(frames)
+        buf = self.buffers(frames)
+        cuts = [i + 1 for i in range(len(prog)) if prog.label(i).startswith("features.")]
+        feats = self.features(frames)
+        if len(host_features) != len(feats):
+            raise ValueError("%d host feature buffers for %d feature maps"
+                             % (len(host_features), len(feats)))
+        side = torch.cuda.Stream()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            s = torch.cuda.current_stream()
+            buf.image.copy_(host_image, non_blocking=True)
+            begin = 0
+            for j, end in enumerate(cuts):
+                prog.encode_all(s, begin=begin, end=end)
+                ready = torch.cuda.Event()
+                ready.record(s)
+                side.wait_event(ready)
+                with torch.cuda.stream(side):
+                    host_features[j].copy_(feats[j], non_blocking=True)
+                begin = end
+            if begin < len(prog):
+                prog.encode_all(s, begin=begin)
+            s.wait_stream(side)
+        return g
+
     def launches_per_frame_batch(self, layers: int | None = None, frames: int = 1) -> int:
         n = self.cfg.layers if layers is None else layers
         taken = sum(1 for i in self.cfg.out_indices if i <= n)

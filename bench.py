@@ -313,10 +313,12 @@ class EncoderWorkload:
         self.graph.launch(stream)
 
     def step_e2e(self, stream):
-        self.buf.image.copy_(self.host, non_blocking=True)
-        self.step(stream)
-        for h, f in zip(self.feats_host, self.enc.features(self.frames)):
-            h.copy_(f, non_blocking=True)
+        # Encoder.capture_host: image in, the encoder, each feature out on a
+        # second stream once its LayerNorm has run (one graph per step)
+        if getattr(self, "host_graph", None) is None:
+            self.host_graph = self.enc.capture_host(self.frames, self.host, self.feats_host,
+                                                    stream)
+        self.host_graph.replay()
 
     def e2e_bytes(self):
         return (self.host.numel() * 4, sum(h.numel() * 4 for h in self.feats_host))

@@ -148,3 +148,31 @@ def test_encoder_program_graph_equals_direct():
     g.launch(s)
     s.synchronize()
     assert torch.equal(enc.buffers(1).features[0], want)
+
+
+def test_host_to_host_graph_equals_the_device_features():
+    """Encoder.capture_host: the image copied in, the program, each feature
+    copied out on a second stream right after its LayerNorm, in one graph;
+    two replays with different images each give that image's features."""
+    import torch
+    from beatlm_b200.model import Encoder, ViTConfig
+    from test_block_gpu import _encoder_weights, imagenet_image
+    cfg = ViTConfig.small(layers=3, out_indices=(1, 3))
+    enc = Encoder(cfg, _encoder_weights(cfg, 3), "bf16")
+    images = [imagenet_image(np.random.default_rng(40 + i), cfg.side) for i in range(2)]
+    wants = []
+    for im in images:
+        feats = enc.forward(torch.from_numpy(im).cuda(), frames=1)
+        torch.cuda.synchronize()
+        wants.append([f.cpu().clone() for f in feats])
+    host_image = torch.empty((1, cfg.side, cfg.side, cfg.cin), dtype=torch.float32).pin_memory()
+    host_feats = [torch.empty(f.shape, dtype=f.dtype).pin_memory() for f in enc.features(1)]
+    s = torch.cuda.Stream()
+    g = enc.capture_host(1, host_image, host_feats, s)
+    for im, want in zip(images, wants):
+        host_image.copy_(torch.from_numpy(im).reshape(host_image.shape))
+        with torch.cuda.stream(s):
+            g.replay()
+        s.synchronize()
+        for h, w in zip(host_feats, want):
+            assert torch.equal(h, w)
