@@ -185,6 +185,40 @@ SIGNATURES.update({
 })
 
 
+class Estimator(ctypes.Structure):
+    _fields_ = [("kind", ctypes.c_int32), ("window", ctypes.c_uint32),
+                ("frame_window", ctypes.c_uint32), ("reserved", ctypes.c_uint32),
+                ("alpha", ctypes.c_double), ("sigmas", ctypes.c_double),
+                ("cap", ctypes.c_double), ("quantile", ctypes.c_double)]
+
+
+_u64 = ctypes.c_uint64
+SIGNATURES.update({
+    "bl_estimator_default": (None, [ctypes.POINTER(Estimator)]),
+    "bl_cost_create": (ctypes.c_int, [_u64, ctypes.POINTER(Estimator), ctypes.POINTER(_vp),
+                                      ctypes.POINTER(_i32)]),
+    "bl_cost_clone": (ctypes.c_int, [_vp, ctypes.POINTER(_vp)]),
+    "bl_cost_destroy": (None, [_vp]),
+    "bl_cost_estimator": (ctypes.c_int, [_vp, ctypes.POINTER(Estimator)]),
+    "bl_cost_record": (None, [_vp, _u32, _u64]),
+    "bl_cost_record_calibration": (None, [_vp, _u32, _u64]),
+    "bl_cost_frame_estimate": (ctypes.c_int, [_vp, _u32, ctypes.POINTER(_u64)]),
+    "bl_cost_record_frame": (None, [_vp, _u64, _u64]),
+    "bl_cost_frame_scale": (_i32, [_vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_u64),
+                                   ctypes.POINTER(_u64)]),
+    "bl_cost_frames_recorded": (_u64, [_vp]),
+    "bl_cost_planning_estimate": (_u64, [_vp, _u32]),
+    "bl_cost_estimate": (_u64, [_vp, _u32]),
+    "bl_cost_samples": (_u32, [_vp, _u32]),
+    "bl_micros_nearest": (_u64, [ctypes.c_double]),
+    "bl_kernel_spec_max_parts": (_u32, [ctypes.POINTER(KernelSpec)]),
+    "bl_program_parts_within": (ctypes.c_int, [ctypes.POINTER(KernelSpec), _sz,
+                                               ctypes.POINTER(_u64), _sz, _u64,
+                                               ctypes.POINTER(_u32)]),
+    "bl_cost_record_passes": (_sz, [_vp, ctypes.POINTER(SliceTime), _sz, ctypes.c_int]),
+})
+
+
 class TensorDesc(ctypes.Structure):
     _fields_ = [("id", ctypes.c_uint32), ("elem_bytes", ctypes.c_uint32),
                 ("elements", ctypes.c_uint64), ("first_use", ctypes.c_uint32),

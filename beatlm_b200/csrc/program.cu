@@ -35,6 +35,25 @@ extern "C" uint32_t bl_parts_within(uint64_t duration_us, uint64_t bound_us, uin
     return static_cast<uint32_t>(want < cap ? want : cap);
 }
 
+// Program::parts_within (kernel.rs:2350-2366): bl_parts_within for every
+// kernel with its own duration and max_parts.
+extern "C" int bl_program_parts_within(const bl_kernel_spec* specs, size_t n,
+                                       const uint64_t* durations_us, size_t n_durations,
+                                       uint64_t bound_us, uint32_t* parts_out) {
+    if (n_durations != n)
+        return bl::fail(BL_ERR_INVALID, "parts_within: %zu durations for %zu kernels (PartCounts)",
+                        n_durations, n);
+    if (bound_us == 0)
+        return bl::fail(BL_ERR_INVALID, "parts_within: no dispatch fits a bound of zero (ZeroBound)");
+    if (n > 0 && (specs == nullptr || durations_us == nullptr || parts_out == nullptr))
+        return bl::fail(BL_ERR_INVALID, "parts_within: null argument");
+    for (size_t i = 0; i < n; ++i) {
+        const uint32_t mp = bl_kernel_spec_max_parts(&specs[i]);
+        parts_out[i] = bl_parts_within(durations_us[i], bound_us, mp > 0 ? mp : 1);
+    }
+    return BL_OK;
+}
+
 // ------------------------------------------------------------------ timer
 
 namespace bl {
@@ -248,23 +267,34 @@ struct bl_graph {
 
 namespace {
 
+// The split dimension of a spec and its grain (the split_extent and
+// split_grain of the reference's MainOp, kernel.rs:1975): query rows in
+// 128-row tiles for attention, output rows in 128-row tiles for a matrix
+// multiply, rows for a LayerNorm; a patch embedding runs whole. False for an
+// unknown op.
+bool split_dims(const bl_kernel_spec& s, uint32_t* extent, uint32_t* grain) {
+    *extent = 1, *grain = 1;
+    switch (s.op) {
+        case BL_OP_ATTENTION: {
+            const auto& a = *static_cast<const bl_attention_args*>(s.args);
+            *extent = a.row_end > a.row_begin ? a.row_end - a.row_begin : 0;
+            *grain = 128;
+            return true;
+        }
+        case BL_OP_GEMM: *extent = static_cast<const bl_gemm_args*>(s.args)->m; *grain = 128; return true;
+        case BL_OP_LAYERNORM: *extent = static_cast<const bl_layernorm_args*>(s.args)->rows; return true;
+        case BL_OP_PATCHIFY: return true;
+        default: return false;
+    }
+}
+
 int add_spec(bl_kernels* k, const bl_kernel_spec& s, size_t index) {
     using namespace bl;
     if (s.args == nullptr) return fail(BL_ERR_INVALID, "kernel %zu: null args", index);
     const std::string base = s.label ? s.label : ("kernel " + std::to_string(index));
     uint32_t extent = 1, grain = 1;
-    switch (s.op) {
-        case BL_OP_ATTENTION: {
-            const auto& a = *static_cast<const bl_attention_args*>(s.args);
-            extent = a.row_end > a.row_begin ? a.row_end - a.row_begin : 0;
-            grain = 128;
-            break;
-        }
-        case BL_OP_GEMM: extent = static_cast<const bl_gemm_args*>(s.args)->m; grain = 128; break;
-        case BL_OP_LAYERNORM: extent = static_cast<const bl_layernorm_args*>(s.args)->rows; break;
-        case BL_OP_PATCHIFY: break;
-        default: return fail(BL_ERR_INVALID, "kernel %zu: unknown op %d", index, s.op);
-    }
+    if (!split_dims(s, &extent, &grain))
+        return fail(BL_ERR_INVALID, "kernel %zu: unknown op %d", index, s.op);
     std::vector<uint32_t> edges(static_cast<size_t>(s.parts > 1 ? s.parts : 1) + 1);
     const uint32_t count = s.op == BL_OP_PATCHIFY ? 1 : bl_split_edges(extent, grain, s.parts, edges.data());
     if (s.op == BL_OP_PATCHIFY) { edges[0] = 0; edges[1] = 1; }
@@ -410,4 +440,13 @@ extern "C" void bl_graph_destroy(bl_graph* g) {
     if (g->exec) cudaGraphExecDestroy(g->exec);
     if (g->graph) cudaGraphDestroy(g->graph);
     delete g;
+}
+
+// KernelSpec::max_parts (kernel.rs:1975): the split extent in grains.
+extern "C" uint32_t bl_kernel_spec_max_parts(const bl_kernel_spec* s) {
+    if (s == nullptr || s->args == nullptr) return 0;
+    uint32_t extent = 1, grain = 1;
+    if (!split_dims(*s, &extent, &grain)) return 0;
+    if (s->op == BL_OP_PATCHIFY) return 1;
+    return static_cast<uint32_t>((static_cast<uint64_t>(extent) + grain - 1) / grain);
 }

@@ -48,16 +48,47 @@ def parts_within(duration_us: int, bound_us: int, max_parts: int) -> int:
     return N.lib().bl_parts_within(duration_us, bound_us, max_parts)
 
 
+def _spec_array(specs: list[Spec]):
+    arr = (N.KernelSpec * max(1, len(specs)))()
+    labels = [s.label.encode() for s in specs]
+    for i, s in enumerate(specs):
+        arr[i] = N.KernelSpec(op=s.op, args=ctypes.cast(ctypes.pointer(s.args), ctypes.c_void_p),
+                              label=labels[i], parts=s.parts)
+    return arr, labels
+
+
+def max_parts(spec: Spec) -> int:
+    """KernelSpec::max_parts (kernel.rs:1975), from the library."""
+    arr, _ = _spec_array([spec])
+    return N.lib().bl_kernel_spec_max_parts(arr)
+
+
+def program_parts_within(specs: list[Spec], durations_us: list[int], bound_us: int) -> list[int]:
+    """Program::parts_within (kernel.rs:2350-2366): the part count of every
+    kernel for its measured duration; raises for a bound of zero or a
+    duration list of the wrong length."""
+    arr, _ = _spec_array(specs)
+    d = (ctypes.c_uint64 * max(1, len(durations_us)))(*durations_us)
+    out = (ctypes.c_uint32 * max(1, len(specs)))()
+    N.check(N.lib().bl_program_parts_within(arr, len(specs), d, len(durations_us), bound_us, out))
+    return list(out[:len(specs)])
+
+
+def split(specs: list[Spec], parts: list[int]) -> list[Spec]:
+    """Program::split (kernel.rs:2368-2407) as specs: kernel i in parts[i]
+    parts (the library clamps the count to 1..=max_parts)."""
+    if len(parts) != len(specs):
+        raise ValueError("split: %d part counts for %d kernels" % (len(parts), len(specs)))
+    if any(s.parts != 1 for s in specs):
+        raise ValueError("split: the program is already split")
+    return [dataclasses.replace(s, parts=max(1, int(p))) for s, p in zip(specs, parts)]
+
+
 class Kernels:
     """Prebuilt launches of a program; ``len`` counts parts."""
 
     def __init__(self, specs: list[Spec]):
-        arr = (N.KernelSpec * len(specs))()
-        self._labels = [s.label.encode() for s in specs]
-        for i, s in enumerate(specs):
-            arr[i] = N.KernelSpec(op=s.op, args=ctypes.cast(ctypes.pointer(s.args),
-                                                            ctypes.c_void_p),
-                                  label=self._labels[i], parts=s.parts)
+        arr, self._labels = _spec_array(specs)
         h = ctypes.c_void_p()
         N.check(N.lib().bl_kernels_create(arr, len(specs), ctypes.byref(h)))
         self._h = h

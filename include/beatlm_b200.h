@@ -345,6 +345,18 @@ void bl_kernels_destroy(bl_kernels* k);
 size_t bl_kernels_len(const bl_kernels* k);
 /* The spec's label with " [i/n]" appended for a part; NULL out of range. */
 const char* bl_kernels_label(const bl_kernels* k, size_t kernel);
+/* KernelSpec::max_parts (crates/beatlm-core/src/kernel.rs:1975): how many
+ * parts a spec's split dimension allows (attention query rows and matrix
+ * multiply output rows in 128-row tiles, LayerNorm rows one by one, a patch
+ * embedding 1); 0 for a NULL or unknown spec. */
+uint32_t bl_kernel_spec_max_parts(const bl_kernel_spec* spec);
+/* Program::parts_within (kernel.rs:2350-2366): parts_out[i] =
+ * bl_parts_within(durations_us[i], bound_us, max_parts of spec i). Fails with
+ * BL_ERR_INVALID when n_durations != n (PartCounts) or bound_us == 0
+ * (ZeroBound). The split itself is bl_kernels_create with these counts as
+ * the specs' `parts`. */
+int bl_program_parts_within(const bl_kernel_spec* specs, size_t n, const uint64_t* durations_us,
+                            size_t n_durations, uint64_t bound_us, uint32_t* parts_out);
 
 typedef struct bl_timer bl_timer;
 
@@ -431,6 +443,85 @@ int bl_timer_get_stats(const bl_timer* t, bl_timer_stats* out);
  * reference, whose timestamp queries are written inside the passes
  * (timer.rs:208). */
 int bl_stream_hold(void* stream, uint32_t microseconds);
+
+/* ------------------------------------------------------------- cost model */
+
+/*
+ * Measured slice durations as the estimates the frame scheduler plans with:
+ * the reference's CostModel (crates/beatlm-core/src/cost.rs:726-966), fed
+ * from this library's cudaEvent slice timer (bl_cost_record_passes) instead
+ * of wgpu timestamp queries. A slice is a kernel index of the program
+ * (SliceId, cost.rs:273). Every duration is in whole microseconds. Nothing
+ * here touches the GPU.
+ */
+enum {
+    BL_EST_MEAN_PLUS_SIGMAS = 0,  /* Estimator::MeanPlusSigmas {alpha, sigmas} */
+    BL_EST_WINDOWED_QUANTILE = 1, /* Estimator::WindowedQuantile {window, quantile} */
+    BL_EST_CAPPED_DEVIATION = 2,  /* Estimator::CappedDeviation {alpha, sigmas, cap} */
+    BL_EST_FRAME_SCALED = 3       /* Estimator::FrameScaled {window, frame_window,
+                                     frame_quantile = quantile} */
+};
+/* CostError (cost.rs:298-325): which parameter bl_cost_create rejected. */
+enum {
+    BL_COST_INVALID_ALPHA = 1,
+    BL_COST_INVALID_SIGMAS = 2,
+    BL_COST_INVALID_WINDOW = 3,
+    BL_COST_INVALID_QUANTILE = 4,
+    BL_COST_INVALID_FRAME_WINDOW = 5,
+    BL_COST_INVALID_CAP = 6,
+    BL_COST_UNKNOWN_ESTIMATOR = 7 /* a `kind` outside the four above (no reference case) */
+};
+/* FrameScale (cost.rs:398-414). */
+enum { BL_FRAME_SCALE_NONE = 0, BL_FRAME_SCALE_WARMING_UP = 1, BL_FRAME_SCALE_MEASURED = 2 };
+enum { BL_COST_MAX_WINDOW = 4096 /* MAX_WINDOW, cost.rs:294 */ };
+
+typedef struct bl_estimator {
+    int32_t kind;          /* BL_EST_* */
+    uint32_t window;       /* measurements kept per slice (quantile, frame-scaled) */
+    uint32_t frame_window; /* frames whose ratio is kept (frame-scaled) */
+    uint32_t reserved;
+    double alpha;          /* weight of a new measurement (mean + sigmas, capped) */
+    double sigmas;         /* standard deviations added to the mean */
+    double cap;            /* most padding, as a multiple of the mean (capped) */
+    double quantile;       /* the window's rank to read; frame-scaled: the frame quantile */
+} bl_estimator;
+
+typedef struct bl_cost bl_cost;
+
+/* Estimator::default (cost.rs:416-425): the 0.9 quantile of the last 32. */
+void bl_estimator_default(bl_estimator* out);
+/* CostModel::new (cost.rs:748): BL_OK, or BL_ERR_INVALID with *cost_error =
+ * the BL_COST_* of the first parameter out of range. */
+int bl_cost_create(uint64_t prior_us, const bl_estimator* est, bl_cost** out, int32_t* cost_error);
+int bl_cost_clone(const bl_cost* c, bl_cost** out);
+void bl_cost_destroy(bl_cost* c);
+/* CostModel::estimator (cost.rs:771). */
+int bl_cost_estimator(const bl_cost* c, bl_estimator* out);
+/* CostModel::record / record_calibration (cost.rs:779-795). */
+void bl_cost_record(bl_cost* c, uint32_t slice, uint64_t measured_us);
+void bl_cost_record_calibration(bl_cost* c, uint32_t slice, uint64_t measured_us);
+/* CostModel::frame_estimate (cost.rs:851): 1 and *out set when the slice
+ * counts in a frame's ratio, 0 when it is left out (None). */
+int bl_cost_frame_estimate(const bl_cost* c, uint32_t slice, uint64_t* out);
+/* CostModel::record_frame (cost.rs:871). */
+void bl_cost_record_frame(bl_cost* c, uint64_t predicted_us, uint64_t measured_us);
+/* CostModel::frame_scale (cost.rs:898): BL_FRAME_SCALE_*; *scale is set
+ * when MEASURED, *recorded and *needed when WARMING_UP (any may be NULL). */
+int32_t bl_cost_frame_scale(const bl_cost* c, double* scale, uint64_t* recorded, uint64_t* needed);
+/* CostModel::frames_recorded / planning_estimate / estimate / samples
+ * (cost.rs:910-975). */
+uint64_t bl_cost_frames_recorded(const bl_cost* c);
+uint64_t bl_cost_planning_estimate(const bl_cost* c, uint32_t slice);
+uint64_t bl_cost_estimate(const bl_cost* c, uint32_t slice);
+uint32_t bl_cost_samples(const bl_cost* c, uint32_t slice);
+/* A timer duration in whole microseconds, rounded to nearest, saturating
+ * (ticks_to_micros, crates/beatlm/src/gpu/timer.rs:781-800). */
+uint64_t bl_micros_nearest(double micros);
+/* Folds the passes bl_timer_collect_ready wrote: each pass's duration,
+ * rounded by bl_micros_nearest, under its kernel index, as the loop's
+ * measurements (calibration = 0, CostModel::record) or calibration's
+ * (record_calibration; calibrate.rs:165-174). Returns the passes folded. */
+size_t bl_cost_record_passes(bl_cost* c, const bl_slice_time* passes, size_t n, int calibration);
 
 /* ------------------------------------------------------------ memory plan */
 

@@ -176,3 +176,63 @@ def test_host_to_host_graph_equals_the_device_features():
         s.synchronize()
         for h, w in zip(host_feats, want):
             assert torch.equal(h, w)
+
+
+def test_the_loop_feeds_timer_measurements_into_the_cost_model():
+    """North star (c): the scheduler's slice costs come from cudaEvent timings.
+    Each collected frame folds every pass under its kernel index; a frame
+    planned once its slices were warm records its measured-over-planned
+    ratio (cost.rs:863-870)."""
+    import torch
+    import beatlm_b200 as bl
+    from beatlm_b200.cost import CostModel, FrameScaled, Measured, WARM_SAMPLES
+    from beatlm_b200.model import block_specs
+    from beatlm_b200.runtime import Kernels, SliceTimer
+    cfg, blk, buf, x0 = _block()
+    k = Kernels(block_specs(blk, cfg, buf))
+    t = SliceTimer(max_slices=len(k))
+    m = CostModel(1000, FrameScaled(8, 2, 0.9))
+    buf.x.copy_(x0)
+    planned, done = {}, 0
+    for f in range(12):
+        planned[f] = m.plan_frame(range(len(k)))
+        h = t.begin_frame(f)
+        k.encode_all(timer=t, frame=h)
+        t.submitted(h)
+        torch.cuda.synchronize()
+        for timing in t.collect_ready():
+            assert [kern for kern, _ in timing.compute] == list(range(len(k)))
+            m.record_timing(timing, planned=planned.pop(timing.frame))
+            done += 1
+    assert done == 12
+    for s in range(len(k)):
+        assert m.samples(s) == 12 and 1 <= m.estimate(s) < 1000
+    # frames WARM_SAMPLES.. had a plan: their ratios fill the 2-frame window
+    assert isinstance(m.frame_scale(), Measured)
+    assert m.frames_recorded() == 12 - WARM_SAMPLES
+    assert bl.status(reset=True).code == 0
+
+
+def test_calibration_splits_by_measured_durations_and_seeds_the_cost_model():
+    """calibrate.rs:105-186 on the ViT-S block: pass 1 times whole kernels,
+    Program::parts_within splits each for its median, pass 2 times every
+    part into the cost model as calibration's measurements."""
+    import beatlm_b200 as bl
+    from beatlm_b200.calibration import calibrate
+    from beatlm_b200.cost import WindowedQuantile
+    from beatlm_b200.model import block_specs
+    from beatlm_b200.runtime import Kernels, program_parts_within
+    cfg, blk, buf, x0 = _block()
+    specs = block_specs(blk, cfg, buf)
+    buf.x.copy_(x0)
+    frames, bound = 8, 4
+    cal = calibrate(specs, bound, frames=frames, period_us=2000,
+                    estimator=WindowedQuantile(32, 0.9))
+    assert len(cal.durations) == len(specs) and all(d >= 1 for d in cal.durations)
+    assert cal.parts == program_parts_within(specs, cal.durations, bound)
+    assert max(cal.parts) > 1  # the attention alone takes well over 4 us
+    split = Kernels(cal.specs)
+    assert len(split) == sum(cal.parts)
+    for part in range(len(split)):
+        assert cal.cost.samples(part) == frames // 2 and cal.cost.estimate(part) >= 1
+    assert bl.status(reset=True).code == 0
