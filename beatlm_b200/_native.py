@@ -192,6 +192,19 @@ class Estimator(ctypes.Structure):
                 ("cap", ctypes.c_double), ("quantile", ctypes.c_double)]
 
 
+class PassCostArgs(ctypes.Structure):
+    _fields_ = [("variant", ctypes.c_int32), ("passes", ctypes.c_uint32),
+                ("every", ctypes.c_uint32), ("groups", ctypes.c_uint32),
+                ("sink", ctypes.c_void_p), ("kernels", ctypes.c_void_p),
+                ("stream", ctypes.c_void_p)]
+
+
+class PassCostFrame(ctypes.Structure):
+    _fields_ = [("span_us", ctypes.c_double), ("passes_us", ctypes.c_double),
+                ("encode_us", ctypes.c_double), ("pairs", ctypes.c_uint32),
+                ("reserved", ctypes.c_uint32)]
+
+
 _u64 = ctypes.c_uint64
 SIGNATURES.update({
     "bl_estimator_default": (None, [ctypes.POINTER(Estimator)]),
@@ -212,6 +225,8 @@ SIGNATURES.update({
     "bl_cost_samples": (_u32, [_vp, _u32]),
     "bl_micros_nearest": (_u64, [ctypes.c_double]),
     "bl_kernel_spec_max_parts": (_u32, [ctypes.POINTER(KernelSpec)]),
+    "bl_pass_cost_frame_run": (ctypes.c_int, [ctypes.POINTER(PassCostArgs),
+                                              ctypes.POINTER(PassCostFrame)]),
     "bl_program_parts_within": (ctypes.c_int, [ctypes.POINTER(KernelSpec), _sz,
                                                ctypes.POINTER(_u64), _sz, _u64,
                                                ctypes.POINTER(_u32)]),

@@ -1,6 +1,7 @@
 // The program of a model on the device: prepared launches (the reference's
 // Kernels), the row split of Program::split, CUDA-graph replay, and the
 // cudaEvent slice timer with the reference SliceTimer's semantics.
+#include <chrono>
 #include <cstdio>
 #include <cstring>
 #include <deque>
@@ -449,4 +450,140 @@ extern "C" uint32_t bl_kernel_spec_max_parts(const bl_kernel_spec* s) {
     if (!split_dims(*s, &extent, &grain)) return 0;
     if (s->op == BL_OP_PATCHIFY) return 1;
     return static_cast<uint32_t>((static_cast<uint64_t>(extent) + grain - 1) / grain);
+}
+
+// ------------------------------------------------------------------ pass cost
+// What a launch costs apart from the work it does, with and without its
+// event pair: the reference's pass-cost workload
+// (crates/beatlm-host/src/pass_cost.rs:1-110) with a CUDA launch as the pass,
+// a cudaEvent pair as its timestamp writes and a CUDA graph as "one pass".
+
+namespace {
+
+// One block of one thread per group adds one to its word, so every launch
+// reads what the one before it wrote (the reference's SHADER, pass_cost.rs:128).
+__global__ void pass_cost_kernel(uint32_t* sink) { sink[blockIdx.x] += 1u; }
+
+// The same under programmatic dependent launch: the next launch may start
+// at once, and each waits for the one before it to finish before its
+// read-modify-write.
+__global__ void pass_cost_kernel_pdl(uint32_t* sink) {
+    asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    sink[blockIdx.x] += 1u;
+}
+
+struct EventSet {
+    std::vector<cudaEvent_t> ev;
+    ~EventSet() {
+        for (cudaEvent_t e : ev) cudaEventDestroy(e);
+    }
+};
+
+}  // namespace
+
+extern "C" int bl_pass_cost_frame_run(const bl_pass_cost_args* a, bl_pass_cost_frame* out) {
+    using namespace bl;
+    if (a == nullptr || out == nullptr) return fail(BL_ERR_INVALID, "pass cost: null argument");
+    const uint32_t P = a->passes;
+    if (P < 1) return fail(BL_ERR_INVALID, "pass cost: at least one pass");
+    if (a->variant < BL_PASS_PER_PASS || a->variant > BL_PASS_ONE_PASS_PDL)
+        return fail(BL_ERR_INVALID, "pass cost: variant %d", a->variant);
+    if (a->variant == BL_PASS_EVERY && a->every < 1)
+        return fail(BL_ERR_INVALID, "pass cost: every:k needs k >= 1");
+    if (a->kernels != nullptr) {
+        if (P > a->kernels->launches.size())
+            return fail(BL_ERR_INVALID, "pass cost: %u passes of a %zu-kernel program", P,
+                        a->kernels->launches.size());
+    } else if (a->sink == nullptr || a->groups < 1 || a->groups > 65535) {
+        return fail(BL_ERR_INVALID, "pass cost: the trivial kernel needs a sink and 1..65535 groups");
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(a->stream);
+    const bool graph_form = a->variant == BL_PASS_ONE_PASS || a->variant == BL_PASS_ONE_PASS_PDL;
+    auto launch = [&](uint32_t i, cudaStream_t st) -> int {
+        if (a->kernels != nullptr) return enqueue(a->kernels->launches[i], st);
+        if (a->variant == BL_PASS_ONE_PASS_PDL) {
+            cudaLaunchConfig_t cfg{};
+            cfg.gridDim = dim3(a->groups);
+            cfg.blockDim = dim3(1);
+            cfg.stream = st;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[0].val.programmaticStreamSerializationAllowed = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            const cudaError_t e = cudaLaunchKernelEx(&cfg, pass_cost_kernel_pdl, a->sink);
+            return e == cudaSuccess ? BL_OK : fail(BL_ERR_CUDA, "pass cost: %s", cudaGetErrorString(e));
+        }
+        pass_cost_kernel<<<a->groups, 1, 0, st>>>(a->sink);
+        const cudaError_t e = cudaGetLastError();
+        return e == cudaSuccess ? BL_OK : fail(BL_ERR_CUDA, "pass cost: %s", cudaGetErrorString(e));
+    };
+    // which passes carry a pair: every one (A), the first's begin and the
+    // last's end (B), every k-th and the last (D); C has one pair around the graph
+    auto timed = [&](uint32_t i) {
+        return a->variant == BL_PASS_PER_PASS ||
+               (a->variant == BL_PASS_EVERY && (i % a->every == 0 || i == P - 1));
+    };
+    EventSet ev;
+    ev.ev.resize(2 * static_cast<size_t>(P));
+    for (cudaEvent_t& e : ev.ev) BL_CUDA_TRY(cudaEventCreate(&e));
+    cudaEvent_t* b = ev.ev.data();
+    cudaEvent_t* en = ev.ev.data() + P;
+
+    const auto t0 = std::chrono::steady_clock::now();
+    uint32_t pairs = 0;
+    int rc = BL_OK;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    cudaStream_t cap = nullptr;
+    if (graph_form) {
+        BL_CUDA_TRY(cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking));
+        cudaError_t e = cudaStreamBeginCapture(cap, cudaStreamCaptureModeRelaxed);
+        for (uint32_t i = 0; i < P && rc == BL_OK && e == cudaSuccess; ++i) rc = launch(i, cap);
+        const cudaError_t e2 = cudaStreamEndCapture(cap, &graph);
+        if (e == cudaSuccess) e = e2;
+        if (rc == BL_OK && e == cudaSuccess) e = cudaGraphInstantiate(&exec, graph, 0);
+        if (rc == BL_OK && e == cudaSuccess) e = cudaEventRecord(b[0], s);
+        if (rc == BL_OK && e == cudaSuccess) e = cudaGraphLaunch(exec, s);
+        if (rc == BL_OK && e == cudaSuccess) e = cudaEventRecord(en[0], s);
+        if (rc == BL_OK && e != cudaSuccess) rc = fail(BL_ERR_CUDA, "pass cost graph: %s", cudaGetErrorString(e));
+        pairs = 1;
+    } else {
+        for (uint32_t i = 0; i < P && rc == BL_OK; ++i) {
+            const bool pair = timed(i);
+            if (pair || (a->variant == BL_PASS_ENDS && i == 0)) BL_CUDA_TRY(cudaEventRecord(b[i], s));
+            rc = launch(i, s);
+            if (rc == BL_OK && (pair || (a->variant == BL_PASS_ENDS && i == P - 1)))
+                BL_CUDA_TRY(cudaEventRecord(en[i], s));
+            pairs += pair ? 1 : 0;
+        }
+        if (a->variant == BL_PASS_ENDS) pairs = 1;
+    }
+    const auto t1 = std::chrono::steady_clock::now();
+    const cudaError_t es = cudaStreamSynchronize(s);
+    if (exec) cudaGraphExecDestroy(exec);
+    if (graph) cudaGraphDestroy(graph);
+    if (cap) cudaStreamDestroy(cap);
+    if (rc != BL_OK) return rc;
+    if (es != cudaSuccess) return fail(BL_ERR_CUDA, "pass cost: %s", cudaGetErrorString(es));
+
+    float ms = 0.0f;
+    const uint32_t last = graph_form ? 0 : P - 1;
+    BL_CUDA_TRY(cudaEventElapsedTime(&ms, b[0], en[last]));
+    out->span_us = 1000.0 * ms;
+    double sum = 0.0;
+    if (a->variant == BL_PASS_PER_PASS || a->variant == BL_PASS_EVERY) {
+        for (uint32_t i = 0; i < P; ++i) {
+            if (!timed(i)) continue;
+            BL_CUDA_TRY(cudaEventElapsedTime(&ms, b[i], en[i]));
+            sum += 1000.0 * ms;
+        }
+    } else {
+        sum = out->span_us;
+    }
+    out->passes_us = sum;
+    out->pairs = pairs;
+    out->encode_us = std::chrono::duration<double, std::micro>(t1 - t0).count();
+    return BL_OK;
 }

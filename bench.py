@@ -300,14 +300,20 @@ class EncoderWorkload:
                 "heads": c.heads, "mlp": c.mlp, "layers": c.layers, "image": c.side,
                 "weights": "random N(0,0.02), LN gamma=1 beta=0, LayerScale=1",
                 "dtype": "bf16 weights/activations, f16 V and P, f32 residual",
-                "launch": "one CUDA graph per frame (%d kernels)" % self.launches_per_step,
+                "launch": ("one CUDA graph per frame (%d kernels)" if self.launch == "graph" else
+                           "%d direct launches per frame") % self.launches_per_step,
                 "memory": "static plan: %d tensors in one device allocation of %d bytes "
                           "(peak live %d)" % (len(self.enc.plan.placements()),
                                               self.enc.arena.bytes(),
                                               self.enc.plan.peak_live_bytes()),
                 "l2": "flushed before every timed step (256 MiB write)"}
 
+    launch = "graph"  # or "direct": every kernel launched from the host each step
+
     def step(self, stream):
+        if self.launch == "direct":
+            self.prog.encode_all(stream)
+            return
         if self.graph is None:
             self.graph = self.prog.capture(stream)
         self.graph.launch(stream)
@@ -516,6 +522,9 @@ def main():
     ap.add_argument("--workload", default="encoder", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true",
                     help="skip the cpu_baseline leg (profiling runs)")
+    ap.add_argument("--launch", default="graph", choices=["graph", "direct"],
+                    help="encoder workloads: replay one CUDA graph per step (default) or "
+                         "launch every kernel from the host")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -535,6 +544,8 @@ def main():
                                 device_id=torch.device("cuda", local))
     cls = WORKLOADS[args.workload]
     wl = cls(rank, world=world) if cls is HiresWorkload else cls(rank)
+    if isinstance(wl, EncoderWorkload):
+        wl.launch = args.launch
     stream = torch.cuda.Stream()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
 

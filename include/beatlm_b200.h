@@ -444,6 +444,46 @@ int bl_timer_get_stats(const bl_timer* t, bl_timer_stats* out);
  * (timer.rs:208). */
 int bl_stream_hold(void* stream, uint32_t microseconds);
 
+/* ------------------------------------------------------------- pass cost */
+
+/*
+ * One frame of the reference's pass-cost workload
+ * (crates/beatlm-host/src/pass_cost.rs:1-110): what a pass costs apart from
+ * its work, with and without its timestamps. Here a pass is one CUDA launch,
+ * its timestamp writes a cudaEvent pair, and "one pass" holding every
+ * dispatch is one CUDA graph of the P launches (pass_cost.rs:148 Variant).
+ * The dispatches are the trivial kernel (`groups` blocks of one thread, each
+ * adding one to its word of `sink`, which must hold `groups` device words)
+ * or, with `kernels`, the first `passes` kernels of that program. Blocks
+ * until the frame is done (one frame in flight, pass_cost.rs:29-39).
+ */
+enum {
+    BL_PASS_PER_PASS = 0, /* A: a pair on every launch */
+    BL_PASS_ENDS = 1,     /* B: the first launch's begin and the last's end */
+    BL_PASS_ONE_PASS = 2, /* C: one graph of all launches, one pair around it */
+    BL_PASS_EVERY = 3,    /* D: a pair on every k-th launch, the first included, and the last */
+    BL_PASS_ONE_PASS_PDL = 4 /* C with programmatic dependent launch between the graph's
+                                trivial launches (no reference counterpart: the boundary
+                                cost B200 kernels pay when each overlaps its predecessor) */
+};
+typedef struct bl_pass_cost_args {
+    int32_t variant;           /* BL_PASS_* */
+    uint32_t passes;           /* P >= 1 */
+    uint32_t every;            /* k of BL_PASS_EVERY */
+    uint32_t groups;           /* trivial kernel: 1..65535 blocks */
+    uint32_t* sink;            /* trivial kernel: device words, at least `groups` */
+    const bl_kernels* kernels; /* non-NULL: time this program's first `passes` kernels */
+    void* stream;              /* a cudaStream_t */
+} bl_pass_cost_args;
+typedef struct bl_pass_cost_frame {
+    double span_us;   /* first launch's begin to last launch's end (device) */
+    double passes_us; /* sum of the timed launches' own durations (B and C: the span) */
+    double encode_us; /* host time to enqueue the frame (C: capture, instantiate, launch) */
+    uint32_t pairs;   /* event pairs the frame carried */
+    uint32_t reserved;
+} bl_pass_cost_frame;
+int bl_pass_cost_frame_run(const bl_pass_cost_args* args, bl_pass_cost_frame* out);
+
 /* ------------------------------------------------------------- cost model */
 
 /*

@@ -474,3 +474,36 @@ def test_program_parts_within_splits_each_kernel_for_its_duration():  # kernel.r
     assert [s.parts for s in parts] == [1, 1, 3, 1]
     with pytest.raises(ValueError, match="already split"):
         split(parts, [1, 1, 1, 1])
+
+
+# ------------------------------------------------------------ pass cost
+
+def test_pass_cost_variants_parse_and_time_their_passes():  # pass_cost.rs:148-222
+    from beatlm_b200.pass_cost import Variant
+    for text in ["per-pass", "ends", "one-pass", "every:8", "one-pass-pdl"]:
+        assert Variant.parse(text).name == text
+    for bad in ["every:0", "every:x", "all"]:
+        with pytest.raises(ValueError):
+            Variant.parse(bad)
+    e = Variant.parse("every:3")
+    assert [e.times_pass(i, 8) for i in range(8)] == [True, False, False, True, False, False,
+                                                      True, True]
+    assert all(Variant("per-pass").times_pass(i, 4) for i in range(4))
+    assert not any(Variant("ends").times_pass(i, 4) or Variant("one-pass").times_pass(i, 4)
+                   for i in range(4))
+
+
+def test_pass_cost_derives_from_nearest_rank_medians():  # pass_cost.rs:80-105
+    from beatlm_b200.pass_cost import Frame, derive, nearest_rank
+    assert nearest_rank([1, 2, 3, 4], 50) == 2 and nearest_rank([5], 90) == 5
+    assert nearest_rank([], 50) is None
+    f = lambda span, passes=None, enc=1.0: Frame(span, span if passes is None else passes, enc, 1)
+    frames = {("per-pass", 1): [f(10), f(11), f(12)], ("per-pass", 9): [f(50, 40, 9.0)],
+              ("ends", 9): [f(42)], ("one-pass", 1): [f(9)], ("one-pass", 9): [f(25)]}
+    d = derive(frames)
+    assert d["span_us"]["[per-pass,1]"] == 11
+    a = d["derived"]["[per-pass,9]"]
+    assert a["per_pass_us"] == (50 - 11) / 8 and a["over_one_pass_us"] == (50 - 25) / 8
+    assert a["over_ends_us"] == 1.0 and a["between_us"] == 10 and a["encode_per_pass_us"] == 1.0
+    assert d["derived"]["[one-pass,9]"]["per_dispatch_us"] == 2.0
+    assert "per_pass_us" not in derive(frames, trivial=False)["derived"]["[per-pass,9]"]

@@ -236,3 +236,35 @@ def test_calibration_splits_by_measured_durations_and_seeds_the_cost_model():
     for part in range(len(split)):
         assert cal.cost.samples(part) == frames // 2 and cal.cost.estimate(part) >= 1
     assert bl.status(reset=True).code == 0
+
+
+@pytest.mark.parametrize("kernels", ["trivial", "block"])
+def test_pass_cost_frames_time_every_variant(kernels):
+    """pass_cost.rs's workload with CUDA launches as passes: every cell is
+    timed, spans grow with the pass count, and only A and D carry pairs per
+    launch."""
+    import beatlm_b200 as bl
+    from beatlm_b200.model import block_specs
+    from beatlm_b200.pass_cost import DEFAULT_VARIANTS, derive, run
+    from beatlm_b200.runtime import Kernels
+    program = None
+    if kernels == "block":
+        cfg, blk, buf, x0 = _block()
+        buf.x.copy_(x0)
+        program = Kernels(block_specs(blk, cfg, buf))
+    passes = (1, 7) if program is not None else (1, 8)
+    res = run(passes, DEFAULT_VARIANTS, frames_per_cell=4, period_us=0, kernels=program)
+    for (name, p), frames in res.items():
+        assert len(frames) == 4
+        for f in frames:
+            assert f.span_us > 0 and f.encode_us > 0
+            want = {"per-pass": p, "ends": 1, "one-pass": 1, "one-pass-pdl": 1,
+                    "every:8": len([i for i in range(p) if i % 8 == 0 or i == p - 1])}[name]
+            assert f.pairs == want, (name, p)
+            if name == "per-pass":
+                assert f.passes_us <= f.span_us + 1.0
+    d = derive(res, trivial=program is None)
+    big = passes[-1]
+    assert d["span_us"]["[per-pass,%d]" % big] > d["span_us"]["[per-pass,1]"]
+    assert "over_one_pass_us" in d["derived"]["[per-pass,%d]" % big]
+    assert bl.status(reset=True).code == 0
