@@ -170,3 +170,43 @@ def test_vit_l_block_matches_the_reference_block():
     rel, mx = _rel(buf.x.cpu().numpy(), want)
     print("ViT-L block bf16: rel-L2 %.3e max-abs %.3e" % (rel, mx))
     assert rel <= REL["bf16"]
+
+
+@pytest.mark.parametrize("side", [518, 266])
+def test_encoder_from_a_checkpoint_file_matches_the_reference(side, tmp_path):
+    """A safetensors file in the checkpoint's names and layouts (random
+    values) through beatlm_b200.load into the encoder: linear weights
+    transposed, Q|K|V side by side, the patch projection to HWIO and, at 266
+    px, the stored 37 x 37 position grid resampled to 19 x 19. Features
+    against the oracle chain fed the converted weights."""
+    import torch
+    import beatlm_b200 as bl
+    from beatlm_b200 import load
+    from beatlm_b200.model import Encoder, ViTConfig
+    layers = 2
+    cfg = ViTConfig.small(layers=layers, out_indices=(2,), side=side)
+    rng = np.random.default_rng(11)
+    ck = {}
+    for name, shape, role in load.inventory(cfg):
+        r = role[1] if isinstance(role, tuple) else role
+        if r in ("norm1_g", "norm2_g", "norm_g"):
+            ck[name] = (1.0 + 0.1 * rng.standard_normal(shape)).astype(np.float32)
+        elif r in ("ls1", "ls2"):
+            ck[name] = rng.uniform(0.1, 1.0, shape).astype(np.float32)
+        else:
+            ck[name] = (0.02 * rng.standard_normal(shape)).astype(np.float32)
+    path = tmp_path / "model.safetensors"
+    path.write_bytes(load.write(ck, metadata={"format": "pt"}))
+    w = load.encoder_weights(str(path), cfg)
+    image = imagenet_image(np.random.default_rng(12), cfg.side, frames=1)
+    enc = Encoder(cfg, w, "bf16")
+    feats = enc.forward(torch.from_numpy(image).cuda(), frames=1)
+    torch.cuda.synchronize()
+    assert bl.status(reset=True).code == 0
+    flat = {k: (np.asarray(v).ravel() if k != "blocks" else
+                [{bk: np.asarray(bv).ravel() for bk, bv in b.items()} for b in v])
+            for k, v in w.items()}
+    want = oracle_encoder(cfg, flat, image[0], layers, "bf16")
+    rel, mx = _rel(feats[0].cpu().numpy().ravel(), want[0])
+    print("encoder from a checkpoint at %d px: rel-L2 %.3e max-abs %.3e" % (side, rel, mx))
+    assert rel <= REL["bf16"]
