@@ -192,6 +192,41 @@ class Estimator(ctypes.Structure):
                 ("cap", ctypes.c_double), ("quantile", ctypes.c_double)]
 
 
+class SyncPolicy(ctypes.Structure):
+    _fields_ = [("kind", ctypes.c_int32), ("frames", ctypes.c_uint32),
+                ("margin_us", ctypes.c_uint64), ("grid_origin_us", ctypes.c_uint64),
+                ("grid_beat_us", ctypes.c_uint64)]
+
+
+class FrameInfo(ctypes.Structure):
+    _fields_ = [("index", ctypes.c_uint64), ("start_us", ctypes.c_uint64),
+                ("period_us", ctypes.c_uint64)]
+
+
+class SliceRun(ctypes.Structure):
+    _fields_ = [("job", ctypes.c_uint64), ("slice", ctypes.c_uint32),
+                ("reserved", ctypes.c_uint32), ("position", ctypes.c_uint64)]
+
+
+class Delivery(ctypes.Structure):
+    _fields_ = [("job", ctypes.c_uint64), ("input", ctypes.c_uint64)]
+
+
+class Due(ctypes.Structure):
+    _fields_ = [("kind", ctypes.c_int32), ("reserved", ctypes.c_uint32), ("at", ctypes.c_uint64)]
+
+
+class Missed(ctypes.Structure):
+    _fields_ = [("job", ctypes.c_uint64), ("input", ctypes.c_uint64), ("due", Due),
+                ("policy", ctypes.c_int32), ("reserved", ctypes.c_uint32)]
+
+
+class FramePlanInfo(ctypes.Structure):
+    _fields_ = [("runs", ctypes.c_size_t), ("delivered", ctypes.c_size_t),
+                ("missed", ctypes.c_size_t), ("spent_estimate_us", ctypes.c_uint64),
+                ("budget_us", ctypes.c_uint64)]
+
+
 class PassCostArgs(ctypes.Structure):
     _fields_ = [("variant", ctypes.c_int32), ("passes", ctypes.c_uint32),
                 ("every", ctypes.c_uint32), ("groups", ctypes.c_uint32),
@@ -225,6 +260,23 @@ SIGNATURES.update({
     "bl_cost_samples": (_u32, [_vp, _u32]),
     "bl_micros_nearest": (_u64, [ctypes.c_double]),
     "bl_kernel_spec_max_parts": (_u32, [ctypes.POINTER(KernelSpec)]),
+    "bl_budget_for_frame": (_u64, [_u64, _u64, _u64]),
+    "bl_beat_map_next": (ctypes.c_int, [ctypes.POINTER(_u64), _sz, _u64, ctypes.POINTER(_u64)]),
+    "bl_scheduler_create": (ctypes.c_int, [ctypes.POINTER(SyncPolicy), _i32, _u64,
+                                           ctypes.POINTER(_vp)]),
+    "bl_scheduler_destroy": (None, [_vp]),
+    "bl_scheduler_set_expected_budget": (None, [_vp, _u64]),
+    "bl_scheduler_expected_budget": (_u64, [_vp]),
+    "bl_scheduler_replace_beat_grid": (ctypes.c_int, [_vp, _u64, _u64, _u64]),
+    "bl_scheduler_submit": (ctypes.c_int, [_vp, ctypes.POINTER(FrameInfo), ctypes.POINTER(_u32),
+                                           _sz, _vp, ctypes.POINTER(_u64)]),
+    "bl_scheduler_plan_frame": (ctypes.c_int, [_vp, ctypes.POINTER(FrameInfo), _u64, _vp,
+                                               ctypes.POINTER(FramePlanInfo)]),
+    "bl_scheduler_plan_runs": (_sz, [_vp, ctypes.POINTER(SliceRun), _sz]),
+    "bl_scheduler_plan_delivered": (_sz, [_vp, ctypes.POINTER(Delivery), _sz]),
+    "bl_scheduler_plan_missed": (_sz, [_vp, ctypes.POINTER(Missed), _sz]),
+    "bl_scheduler_pending": (_sz, [_vp]),
+    "bl_scheduler_due": (ctypes.c_int, [_vp, _u64, ctypes.POINTER(Due)]),
     "bl_pass_cost_frame_run": (ctypes.c_int, [ctypes.POINTER(PassCostArgs),
                                               ctypes.POINTER(PassCostFrame)]),
     "bl_program_parts_within": (ctypes.c_int, [ctypes.POINTER(KernelSpec), _sz,

@@ -563,6 +563,95 @@ uint64_t bl_micros_nearest(double micros);
  * (record_calibration; calibrate.rs:165-174). Returns the passes folded. */
 size_t bl_cost_record_passes(bl_cost* c, const bl_slice_time* passes, size_t n, int calibration);
 
+/* -------------------------------------------------------------- scheduler */
+
+/*
+ * The frame-slice scheduler (crates/beatlm-core/src/schedule.rs:160-790, with
+ * sync.rs, budget.rs and the beat grids of time.rs): each submitted input
+ * becomes a job with a deadline fixed by the sync policy; each frame the
+ * budget is spent on pending jobs in submission order (jobs never
+ * interleave), reading every slice at bl_cost_planning_estimate, so the
+ * plan follows the cudaEvent-measured costs. Times are whole microseconds
+ * on the host's clock. Host code only.
+ */
+enum { BL_SYNC_FIXED_LATENCY = 0, BL_SYNC_SAME_FRAME = 1, BL_SYNC_ON_BEAT = 2 };
+enum { BL_MISS_HOLD_PREVIOUS = 0, BL_MISS_DROP = 1 };
+enum { BL_DUE_FRAME = 0, BL_DUE_BEAT = 1 };
+
+/* SyncPolicy (sync.rs): FixedLatency {frames}, SameFrame, or OnBeat {margin,
+ * grid}: beats every grid_beat_us from grid_origin_us. */
+typedef struct bl_sync_policy {
+    int32_t kind;            /* BL_SYNC_* */
+    uint32_t frames;         /* FixedLatency */
+    uint64_t margin_us;      /* OnBeat */
+    uint64_t grid_origin_us; /* OnBeat */
+    uint64_t grid_beat_us;   /* OnBeat; 0 is ZeroBeat */
+} bl_sync_policy;
+
+/* FrameInfo (time.rs): a frame's index, start and period. */
+typedef struct bl_frame_info {
+    uint64_t index;
+    uint64_t start_us;
+    uint64_t period_us;
+} bl_frame_info;
+
+typedef struct bl_slice_run { /* SliceRun: submit before the frame's render pass */
+    uint64_t job;
+    uint32_t slice;
+    uint32_t reserved;
+    uint64_t position;        /* the slice's index within its job */
+} bl_slice_run;
+typedef struct bl_delivery { uint64_t job; uint64_t input; } bl_delivery;
+typedef struct bl_due { int32_t kind; uint32_t reserved; uint64_t at; } bl_due; /* frame or beat */
+typedef struct bl_missed {   /* Missed: the input with no result, and when it was due */
+    uint64_t job;
+    uint64_t input;
+    bl_due due;
+    int32_t policy;           /* BL_MISS_* */
+    uint32_t reserved;
+} bl_missed;
+typedef struct bl_frame_plan_info {
+    size_t runs, delivered, missed; /* counts of the plan's three lists */
+    uint64_t spent_estimate_us;     /* summed planning estimates of the runs, <= budget */
+    uint64_t budget_us;
+} bl_frame_plan_info;
+
+typedef struct bl_scheduler bl_scheduler;
+
+/* Budget::for_frame (budget.rs): period - render - margin, saturating at 0. */
+uint64_t bl_budget_for_frame(uint64_t period_us, uint64_t render_us, uint64_t margin_us);
+/* BeatMap::next_beat_at_or_after (time.rs): `grids` holds n (from, origin,
+ * beat) triples, the first in effect from 0 and each later one put in effect
+ * from its `from` (BeatMap::replace_from); BL_ERR_INVALID for a zero beat. */
+int bl_beat_map_next(const uint64_t* grids, size_t n, uint64_t t_us, uint64_t* out);
+/* Scheduler::new (schedule.rs:525). */
+int bl_scheduler_create(const bl_sync_policy* policy, int32_t miss, uint64_t expected_budget_us,
+                        bl_scheduler** out);
+void bl_scheduler_destroy(bl_scheduler* s);
+/* Scheduler::set_expected_budget / expected_budget (schedule.rs:553-566). */
+void bl_scheduler_set_expected_budget(bl_scheduler* s, uint64_t expected_us);
+uint64_t bl_scheduler_expected_budget(const bl_scheduler* s);
+/* Scheduler::replace_beat_grid (schedule.rs:574): BL_ERR_INVALID when the
+ * policy is not OnBeat (NotOnBeat) or the beat is zero. */
+int bl_scheduler_replace_beat_grid(bl_scheduler* s, uint64_t from_us, uint64_t origin_us,
+                                   uint64_t beat_us);
+/* Scheduler::submit (schedule.rs:618): *job = the new job's id; an empty
+ * job is BL_ERR_INVALID (EmptyJob). */
+int bl_scheduler_submit(bl_scheduler* s, const bl_frame_info* input, const uint32_t* slices,
+                        size_t n, const bl_cost* cost, uint64_t* job);
+/* Scheduler::plan_frame (schedule.rs:706): plans `frame` against
+ * `budget_us`; the plan's lists are read with the three calls below (each
+ * returns the list's length and copies up to `cap` entries). */
+int bl_scheduler_plan_frame(bl_scheduler* s, const bl_frame_info* frame, uint64_t budget_us,
+                            const bl_cost* cost, bl_frame_plan_info* info);
+size_t bl_scheduler_plan_runs(const bl_scheduler* s, bl_slice_run* out, size_t cap);
+size_t bl_scheduler_plan_delivered(const bl_scheduler* s, bl_delivery* out, size_t cap);
+size_t bl_scheduler_plan_missed(const bl_scheduler* s, bl_missed* out, size_t cap);
+/* Scheduler::pending / due (schedule.rs:773-790): due returns 1 and fills
+ * *out while the job is pending, 0 otherwise. */
+size_t bl_scheduler_pending(const bl_scheduler* s);
+int bl_scheduler_due(const bl_scheduler* s, uint64_t job, bl_due* out);
+
 /* ------------------------------------------------------------ memory plan */
 
 /*

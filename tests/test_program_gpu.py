@@ -268,3 +268,42 @@ def test_pass_cost_frames_time_every_variant(kernels):
     assert d["span_us"]["[per-pass,%d]" % big] > d["span_us"]["[per-pass,1]"]
     assert "over_one_pass_us" in d["derived"]["[per-pass,%d]" % big]
     assert bl.status(reset=True).code == 0
+
+
+def test_the_frame_loop_schedules_timed_slices_and_learns_their_costs():
+    """North star (c) end to end: the scheduler plans each frame of the split
+    ViT-S block with the cost model, the planned slices run under the
+    cudaEvent slice timer, and their measured durations come back into the
+    model. With a budget every job fits, every job is delivered on its frame
+    (latency 2), and the residual stream equals the block run once per job."""
+    import torch
+    import beatlm_b200 as bl
+    from beatlm_b200.cost import CostModel
+    from beatlm_b200.model import block_specs
+    from beatlm_b200.runtime import Kernels, SliceTimer
+    from beatlm_b200.schedule import FixedLatency, FrameInfo, FrameLoop, Scheduler
+    cfg, blk, buf, x0 = _block()
+    k = Kernels(block_specs(blk, cfg, buf, parts=3))
+    n = len(k)
+    loop = FrameLoop(k, Scheduler(FixedLatency(2), "hold_previous", 5000), CostModel(50),
+                     SliceTimer(max_slices=n))
+    buf.x.copy_(x0)
+    jobs, delivered = 0, []
+    for i in range(12):
+        submit = i % 2 == 0 and i < 10
+        jobs += submit
+        p = loop.tick(FrameInfo(i, i * 16667, 16667), 5000, submit)
+        torch.cuda.synchronize()
+        assert p.spent_estimate <= p.budget and not p.missed, i
+        delivered += [(i, d.job) for d in p.delivered]
+    loop.collect()
+    assert delivered == [(2 * j + 2, j) for j in range(jobs)]
+    for s in range(n):
+        assert loop.cost.samples(s) >= jobs - 1 and loop.cost.estimate(s) != 50
+    got = buf.x.clone()
+    buf.x.copy_(x0)
+    for _ in range(jobs):
+        k.encode_all()
+    torch.cuda.synchronize()
+    assert torch.equal(got, buf.x)
+    assert bl.status(reset=True).code == 0
