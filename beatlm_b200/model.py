@@ -181,10 +181,15 @@ class Buffers:
     prebuilt program reads, so a caller writes each frame's pixels there."""
 
     def __init__(self, cfg: ViTConfig, frames: int, dtype: str, tokens: int | None = None,
-                 device="cuda", features: bool = True, alloc=None):
+                 device="cuda", features: bool = True, alloc=None, slots: int = 1):
         """``alloc(name, shape, torch_dtype)`` makes each buffer (default: a
         torch allocation on `device`); the static plan passes views of its
-        arena instead."""
+        arena instead. ``slots``: one input image and one set of feature maps
+        per job in flight (the reference's Net slots,
+        crates/beatlm-host/src/slots.rs:1-30): slot 0 is ``image`` /
+        ``features``, slot s > 0 its own pair (``images[s]``,
+        ``slot_features[s]``), live for the whole program; everything else is
+        shared, since jobs run as one sequence."""
         import torch
         if alloc is None:
             alloc = lambda name, shape, dt: torch.empty(shape, dtype=dt, device=device)
@@ -211,6 +216,14 @@ class Buffers:
         self.norm_sync.zero_()
         self.features = ([alloc("features.%d" % i, (frames * (t - 1), cfg.dim), torch.float32)
                           for i in cfg.out_indices] if features else [])
+        self.images, self.slot_features = [self.image], [self.features]
+        for slot in range(1, slots):
+            img = alloc("image.s%d" % slot, (frames, cfg.side, cfg.side, cfg.cin), torch.float32)
+            img.zero_()
+            self.images.append(img)
+            self.slot_features.append(
+                [alloc("features.%d.s%d" % (i, slot), (frames * (t - 1), cfg.dim), torch.float32)
+                 for i in cfg.out_indices] if features else [])
 
     # Lifetimes for the static plan, in kernel-spec order of the encoder
     # program (spec 0 patchify, spec 1 patch GEMM, blocks from spec 2). The
@@ -343,7 +356,8 @@ class Encoder:
     """The DA-V2 ViT encoder (depth_anything_v2.rs:435-545) on the device."""
 
     def __init__(self, cfg: ViTConfig, weights: dict, dtype: str = "bf16", device="cuda",
-                 planned_frames: int | None = None, fused_ln: bool | None = None):
+                 planned_frames: int | None = None, fused_ln: bool | None = None,
+                 slots: int = 1):
         """``weights``: ``blocks`` (list of per-block dicts in the reference
         layout), ``patch_w`` [patch][patch][cin][dim] (HWIO), ``patch_b`` [dim],
         ``cls`` [dim], ``pos`` [tokens][dim], ``norm_g``/``norm_b`` [dim].
@@ -366,10 +380,15 @@ class Encoder:
         needs every 32-column tile of those GEMMs resident at once (ViT-S
         at one frame: 132 tiles). Also measured slower at ViT-S, one frame:
         668 against 640 us, the column tiles' exchange of statistics through
-        L2 costing more than the LayerNorm launch it replaces."""
+        L2 costing more than the LayerNorm launch it replaces.
+
+        ``slots``: input/output slots for that many jobs in flight
+        (``Buffers``); ``program(frames, slot=s)`` reads slot s's image and
+        writes its feature maps."""
         import torch
         td = torch.bfloat16 if dtype == "bf16" else torch.float16
         self.cfg, self.dtype = cfg, dtype
+        self.slots = max(1, int(slots))
         self.fused_ln = fused_ln if fused_ln == "epilogue" else bool(fused_ln)
         self.arena, self.plan = None, None
         stage = "cpu" if planned_frames is not None else device
@@ -410,7 +429,7 @@ class Encoder:
         from .memory import F16, F32, MemoryPlan, TensorDesc
         last = len(self.specs_layout(frames)) - 1
         acts = []
-        Buffers(self.cfg, frames, self.dtype, device="meta",
+        Buffers(self.cfg, frames, self.dtype, device="meta", slots=self.slots,
                 alloc=lambda n, s, dt: acts.append((n, s, dt)) or torch.empty(s, dtype=dt,
                                                                               device="meta"))
         wts = self._weights()
@@ -446,7 +465,7 @@ class Encoder:
                 setattr(o, a, tuple(tup))
         views = {name: self.arena.tensor(self.plan.placement(k), shape, dt)
                  for k, (name, shape, dt) in enumerate(acts, start=len(wts))}
-        self._buffers[frames] = Buffers(cfg, frames, self.dtype,
+        self._buffers[frames] = Buffers(cfg, frames, self.dtype, slots=self.slots,
                                         alloc=lambda n, s, dt: views[n])
         torch.cuda.synchronize(device)
 
@@ -476,16 +495,20 @@ class Encoder:
             if self.arena is not None:
                 raise ValueError("this encoder's memory is planned for %s frames"
                                  % sorted(self._buffers))
-            self._buffers[frames] = Buffers(self.cfg, frames, self.dtype)
+            self._buffers[frames] = Buffers(self.cfg, frames, self.dtype, slots=self.slots)
         return self._buffers[frames]
 
-    def specs(self, frames: int, layers: int | None = None, parts: int = 1) -> list:
-        """The encoder as kernel specs over the buffers of `frames` frames."""
+    def specs(self, frames: int, layers: int | None = None, parts: int = 1,
+              slot: int = 0) -> list:
+        """The encoder as kernel specs over the buffers of `frames` frames,
+        reading slot `slot`'s image and writing its feature maps."""
         from .runtime import Spec
         cfg, buf = self.cfg, self.buffers(frames)
+        if not 0 <= slot < self.slots:
+            raise ValueError("slot %d of %d" % (slot, self.slots))
         t = cfg.tokens
         out = [
-            Spec(ops.patchify_args(buf.image, frames=frames, side=cfg.side, patch=cfg.patch,
+            Spec(ops.patchify_args(buf.images[slot], frames=frames, side=cfg.side, patch=cfg.patch,
                                    cin=cfg.cin, k_pad=cfg.k_pad, a_out=buf.patches,
                                    a_dtype=self.dtype, cls=self.cls, pos=self.pos, x=buf.x),
                  "embed.patchify"),
@@ -499,23 +522,24 @@ class Encoder:
             out += block_specs(self.blocks[i], cfg, buf, i, parts, fused_ln=self.fused_ln,
                                next_norm=nxt)
             if (i + 1) in cfg.out_indices:
-                f = buf.features[cfg.out_indices.index(i + 1)]
+                f = buf.slot_features[slot][cfg.out_indices.index(i + 1)]
                 out.append(Spec(ops.layernorm_args(buf.x, self.norm[0], self.norm[1], cfg.eps,
                                                    out=f, in_row_offset=1, in_group=(t - 1, 1)),
                                 "features.%d" % (i + 1), parts))
         return out
 
-    def program(self, frames: int = 1, layers: int | None = None, parts: int = 1):
+    def program(self, frames: int = 1, layers: int | None = None, parts: int = 1,
+                slot: int = 0):
         from .runtime import Kernels
-        key = (frames, layers, parts)
+        key = (frames, layers, parts, slot)
         if key not in self._programs:
-            self._programs[key] = Kernels(self.specs(frames, layers, parts))
+            self._programs[key] = Kernels(self.specs(frames, layers, parts, slot))
         return self._programs[key]
 
-    def features(self, frames: int, layers: int | None = None) -> list:
+    def features(self, frames: int, layers: int | None = None, slot: int = 0) -> list:
         n = self.cfg.layers if layers is None else layers
         buf = self.buffers(frames)
-        return [buf.features[j] for j, i in enumerate(self.cfg.out_indices) if i <= n]
+        return [buf.slot_features[slot][j] for j, i in enumerate(self.cfg.out_indices) if i <= n]
 
     def forward(self, image, frames: int = 1, stream=None, layers: int | None = None):
         """``image``: device f32 NHWC [frames][side][side][cin], copied into the

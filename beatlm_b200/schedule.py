@@ -222,25 +222,42 @@ class Scheduler:
 class FrameLoop:
     """The host's side of a frame over a program (the reference host's
     `tick`, crates/beatlm/src/lib.rs:69-120): submit this frame's input as a
-    job of every kernel of ``kernels``, plan the frame, encode the planned
+    job of every kernel of the program, plan the frame, encode the planned
     slices on ``stream`` with the slice timer, and fold every frame whose
     events have completed into the cost model (with its planned estimates,
     so a frame-scaled model records the frame's ratio). Nothing blocks: the
-    timings of a frame arrive in a later tick."""
+    timings of a frame arrive in a later tick.
+
+    ``kernels`` is one program, or one per input/output slot (the same
+    kernels over each slot's input and output, ``model.Encoder.program(slot=
+    s)``): job j runs on slot j % slots, as the reference's Net does
+    (crates/beatlm-host/src/slots.rs:1-30), so up to ``slots`` jobs in
+    flight keep their own input and output."""
 
     def __init__(self, kernels, scheduler: Scheduler, cost, timer):
-        self.kernels, self.scheduler, self.cost, self.timer = kernels, scheduler, cost, timer
+        self.programs = list(kernels) if isinstance(kernels, (list, tuple)) else [kernels]
+        self.scheduler, self.cost, self.timer = scheduler, cost, timer
         self._planned = {}
 
-    def tick(self, frame: FrameInfo, budget: int, submit: bool, stream=None) -> FramePlan:
+    def slot_of(self, job: int) -> int:
+        return job % len(self.programs)
+
+    def tick(self, frame: FrameInfo, budget: int, submit: bool, stream=None,
+             write_input=None) -> FramePlan:
+        """``write_input(slot)``, when given, fills the new job's input slot
+        before the frame's slices are encoded."""
         if submit:
-            self.scheduler.submit(frame, list(range(len(self.kernels))), self.cost)
+            job = self.scheduler.submit(frame, list(range(len(self.programs[0]))), self.cost)
+            if write_input is not None:
+                write_input(self.slot_of(job))
         plan = self.scheduler.plan_frame(frame, budget, self.cost)
         handle = self.timer.begin_frame(frame.index) if plan.runs else -1
         if handle >= 0:
             self._planned[frame.index] = self.cost.plan_frame({r.slice for r in plan.runs})
         for r in plan.runs:
-            self.kernels.encode(r.slice, stream, self.timer if handle >= 0 else None, handle)
+            self.programs[self.slot_of(r.job)].encode(r.slice, stream,
+                                                      self.timer if handle >= 0 else None,
+                                                      handle)
         if handle >= 0:
             self.timer.submitted(handle)
         self.collect()

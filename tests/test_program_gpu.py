@@ -307,3 +307,70 @@ def test_the_frame_loop_schedules_timed_slices_and_learns_their_costs():
     torch.cuda.synchronize()
     assert torch.equal(got, buf.x)
     assert bl.status(reset=True).code == 0
+
+
+def test_jobs_in_flight_keep_their_own_input_and_output_slots():
+    """The reference's Net slots (crates/beatlm-host/src/slots.rs:1-30) on
+    the encoder: three slots for latency 2, each job a different image, a
+    budget of three quarters of a job per frame, so a job spreads over two
+    frames and the next one's input is written while it still runs. Every delivered job's features equal a direct
+    forward pass of its own image."""
+    import torch
+    import beatlm_b200 as bl
+    from beatlm_b200.cost import CostModel
+    from beatlm_b200.model import Encoder, ViTConfig, block_weights_normal
+    from beatlm_b200.runtime import SliceTimer
+    from beatlm_b200.schedule import FixedLatency, FrameInfo, FrameLoop, Scheduler, max_in_flight
+    cfg = ViTConfig.small(layers=2, out_indices=(2,))
+    rng = np.random.default_rng(21)
+    n = lambda *s: rng.standard_normal(int(np.prod(s)), dtype=np.float32) * 0.02
+    w = {"blocks": [block_weights_normal(rng, cfg.dim, cfg.mlp) for _ in range(2)],
+         "patch_w": n(cfg.patch, cfg.patch, cfg.cin, cfg.dim), "patch_b": n(cfg.dim),
+         "cls": n(cfg.dim), "pos": n(cfg.tokens, cfg.dim),
+         "norm_g": np.ones(cfg.dim, np.float32), "norm_b": np.zeros(cfg.dim, np.float32)}
+    policy = FixedLatency(2)
+    slots = max_in_flight(policy)
+    enc = Encoder(cfg, w, "bf16", planned_frames=1, slots=slots)
+    images = [torch.from_numpy(rng.random((1, cfg.side, cfg.side, cfg.cin), dtype=np.float32))
+              .cuda() for _ in range(6)]
+    want = []
+    for img in images:  # direct passes, slot 0
+        want.append(enc.forward(img, frames=1)[0].clone())
+    torch.cuda.synchronize()
+    buf = enc.buffers(1)
+    programs = [enc.program(1, slot=s) for s in range(slots)]
+    # measured costs first, so the budget below splits a job over two frames
+    cost = CostModel(1)
+    loop = FrameLoop(programs, Scheduler(policy, "hold_previous", 0), cost,
+                     SliceTimer(max_slices=2 * len(programs[0])))
+    per_job = None
+    got, submitted = {}, [0]
+
+    def write(slot):
+        buf.images[slot].copy_(images[submitted[0]])
+
+    for i in range(20):
+        submit = i % 2 == 0 and submitted[0] < len(images) and i >= 2
+        if i < 2:  # two warm-up jobs to measure every slice
+            loop.scheduler.set_expected_budget(10 ** 6)
+            loop.tick(FrameInfo(i, i * 16667, 16667), 10 ** 6, True, write_input=write)
+            torch.cuda.synchronize()
+            loop.collect()
+            continue
+        if per_job is None:
+            per_job = sum(cost.planning_estimate(s) for s in range(len(programs[0])))
+            loop.scheduler.set_expected_budget(per_job * 3 // 4 + 1)
+        p = loop.tick(FrameInfo(i, i * 16667, 16667), per_job * 3 // 4 + 1, submit,
+                      write_input=write if submit else None)
+        if submit:
+            submitted[0] += 1
+        torch.cuda.synchronize()
+        assert not p.missed, (i, p.missed)
+        for d in p.delivered:
+            if d.job >= 2:
+                slot = loop.slot_of(d.job)
+                got[d.job - 2] = buf.slot_features[slot][0].clone()
+    assert sorted(got) == list(range(len(images)))
+    for j, f in got.items():
+        assert torch.equal(f, want[j]), j
+    assert bl.status(reset=True).code == 0
