@@ -227,6 +227,13 @@ class FramePlanInfo(ctypes.Structure):
                 ("budget_us", ctypes.c_uint64)]
 
 
+class Im2colArgs(ctypes.Structure):
+    _fields_ = [("input", ctypes.c_void_p), ("h", ctypes.c_uint32), ("w", ctypes.c_uint32),
+                ("cin", ctypes.c_uint32), ("ksize", ctypes.c_uint32), ("stride", ctypes.c_uint32),
+                ("relu", ctypes.c_uint32), ("out", ctypes.c_void_p), ("out_dtype", ctypes.c_int32),
+                ("k_pad", ctypes.c_uint32)]
+
+
 class PassCostArgs(ctypes.Structure):
     _fields_ = [("variant", ctypes.c_int32), ("passes", ctypes.c_uint32),
                 ("every", ctypes.c_uint32), ("groups", ctypes.c_uint32),
@@ -260,6 +267,9 @@ SIGNATURES.update({
     "bl_cost_samples": (_u32, [_vp, _u32]),
     "bl_micros_nearest": (_u64, [ctypes.c_double]),
     "bl_kernel_spec_max_parts": (_u32, [ctypes.POINTER(KernelSpec)]),
+    "bl_im2col": (ctypes.c_int, [ctypes.POINTER(Im2colArgs), _vp]),
+    "bl_blocks_to_map": (ctypes.c_int, [_vp, _vp, _vp, _u32, _u32, _u32, _u32, _vp]),
+    "bl_resize_bilinear": (ctypes.c_int, [_vp, _vp, _u32, _u32, _u32, _u32, _u32, _vp]),
     "bl_budget_for_frame": (_u64, [_u64, _u64, _u64]),
     "bl_beat_map_next": (ctypes.c_int, [ctypes.POINTER(_u64), _sz, _u64, ctypes.POINTER(_u64)]),
     "bl_scheduler_create": (ctypes.c_int, [ctypes.POINTER(SyncPolicy), _i32, _u64,

@@ -1,0 +1,228 @@
+// The DPT decoder's data-movement kernels; its convolutions run on the
+// tcgen05 GEMM (csrc/gemm.cu). A 3x3 (or 1x1) convolution is an im2col
+// gather of NHWC f32 pixels into 16-bit rows of K = taps x cin (zero padding
+// at the image border, an optional ReLU on the way in: the residual units'
+// pre-activation, the reference's ReLU prologue, crates/beatlm-core/src/
+// kernel.rs:265-319) followed by one GEMM with the HWIO weights as [cout][K].
+// A transposed convolution of kernel = stride = f is one GEMM per pixel into
+// [pixels][f*f*cout] and a scatter of each pixel's f x f block. The bilinear
+// resampling (corners aligned) is its own kernel. All HBM-bound byte moves:
+// coalesced 16-byte stores, grid-stride loops over a multiple of the SMs.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "host.h"
+
+namespace bl {
+namespace gemm {
+int sm_count();  // csrc/gemm.cu
+}
+namespace dec {
+
+template <typename T>
+__device__ __forceinline__ uint16_t to16(float v);
+template <>
+__device__ __forceinline__ uint16_t to16<__half>(float v) {
+    return __half_as_ushort(__float2half_rn(v));
+}
+template <>
+__device__ __forceinline__ uint16_t to16<__nv_bfloat16>(float v) {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+}
+
+// One thread writes 8 consecutive columns (16 bytes) of one output row:
+// column k = (ky * ks + kx) * cin + ci, zero past ks * ks * cin.
+template <typename T>
+__global__ void im2col_kernel(const float* __restrict__ in, uint4* __restrict__ out, int h,
+                              int w, int cin, int ks, int stride, int relu, int oh, int ow,
+                              int k_pad) {
+    const int vecs = k_pad / 8;
+    const long long total = static_cast<long long>(oh) * ow * vecs;
+    const int taps = ks * cin * ks;
+    const int pad = ks / 2;
+    for (long long v = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; v < total;
+         v += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long pix = v / vecs;
+        const int k0 = static_cast<int>(v % vecs) * 8;
+        const int y = static_cast<int>(pix / ow), x = static_cast<int>(pix % ow);
+        uint16_t r[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int k = k0 + j;
+            float val = 0.0f;
+            if (k < taps) {
+                const int tap = k / cin, ci = k - tap * cin;
+                const int iy = y * stride + tap / ks - pad, ix = x * stride + tap % ks - pad;
+                if (iy >= 0 && iy < h && ix >= 0 && ix < w) {
+                    val = __ldg(in + (static_cast<long long>(iy) * w + ix) * cin + ci);
+                    if (relu) val = fmaxf(val, 0.0f);
+                }
+            }
+            r[j] = to16<T>(val);
+        }
+        out[v] = make_uint4(r[0] | (uint32_t(r[1]) << 16), r[2] | (uint32_t(r[3]) << 16),
+                            r[4] | (uint32_t(r[5]) << 16), r[6] | (uint32_t(r[7]) << 16));
+    }
+}
+
+// out[(y f + ky) * (w f) + x f + kx][co] = blocks[y * w + x][(ky f + kx) cout + co] + bias[co]
+__global__ void blocks_to_map_kernel(const float* __restrict__ blocks, const float* __restrict__ bias,
+                                     float* __restrict__ out, int h, int w, int f, int cout) {
+    const long long total = static_cast<long long>(h) * f * w * f * cout;
+    const int ow = w * f;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int co = static_cast<int>(i % cout);
+        const long long opix = i / cout;
+        const int oy = static_cast<int>(opix / ow), ox = static_cast<int>(opix % ow);
+        const int y = oy / f, ky = oy % f, x = ox / f, kx = ox % f;
+        float v = __ldg(blocks + (static_cast<long long>(y) * w + x) * (f * f * cout) +
+                        (ky * f + kx) * cout + co);
+        if (bias) v += __ldg(bias + co);
+        out[i] = v;
+    }
+}
+
+// Corners aligned: output row oy reads position oy (ih-1)/(oh-1) (0 for one
+// row) between its floor and the next row, clamped; columns likewise.
+__device__ __forceinline__ void axis(int o, int in, int outn, int* i0, int* i1, float* l) {
+    const float pos = outn > 1 ? static_cast<float>(o) * static_cast<float>(in - 1) /
+                                     static_cast<float>(outn - 1)
+                               : 0.0f;
+    int a = static_cast<int>(floorf(pos));
+    a = a > in - 1 ? in - 1 : a;
+    *i0 = a;
+    *i1 = a + 1 < in ? a + 1 : in - 1;
+    *l = pos - static_cast<float>(a);
+}
+
+__global__ void resize_bilinear_kernel(const float* __restrict__ in, float* __restrict__ out, int ih,
+                                       int iw, int oh, int ow, int c) {
+    const long long total = static_cast<long long>(oh) * ow * c;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int ch = static_cast<int>(i % c);
+        const long long p = i / c;
+        const int oy = static_cast<int>(p / ow), ox = static_cast<int>(p % ow);
+        int y0, y1, x0, x1;
+        float ly, lx;
+        axis(oy, ih, oh, &y0, &y1, &ly);
+        axis(ox, iw, ow, &x0, &x1, &lx);
+        const float a00 = __ldg(in + (static_cast<long long>(y0) * iw + x0) * c + ch);
+        const float a01 = __ldg(in + (static_cast<long long>(y0) * iw + x1) * c + ch);
+        const float a10 = __ldg(in + (static_cast<long long>(y1) * iw + x0) * c + ch);
+        const float a11 = __ldg(in + (static_cast<long long>(y1) * iw + x1) * c + ch);
+        const float top = (1.0f - lx) * a00 + lx * a01;
+        const float bottom = (1.0f - lx) * a10 + lx * a11;
+        out[i] = (1.0f - ly) * top + ly * bottom;
+    }
+}
+
+// cin a multiple of 8 (every DPT width): a thread's 8 columns are 8
+// consecutive channels of one tap, read as two 16-byte loads; one division
+// per thread instead of one per column.
+template <typename T>
+__global__ void im2col_vec8_kernel(const float* __restrict__ in, uint4* __restrict__ out, int h,
+                                   int w, int cin, int ks, int stride, int relu, int oh, int ow,
+                                   int k_pad) {
+    const int vecs = k_pad / 8;
+    const long long total = static_cast<long long>(oh) * ow * vecs;
+    const int taps = ks * ks * cin;
+    const int pad = ks / 2;
+    for (long long v = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; v < total;
+         v += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long pix = v / vecs;
+        const int k0 = static_cast<int>(v - pix * vecs) * 8;
+        const int y = static_cast<int>(pix / ow), x = static_cast<int>(pix - static_cast<long long>(y) * ow);
+        float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
+        if (k0 < taps) {
+            const int tap = k0 / cin, ci = k0 - tap * cin;
+            const int ky = tap / ks, kx = tap - ky * ks;
+            const int iy = y * stride + ky - pad, ix = x * stride + kx - pad;
+            if (iy >= 0 && iy < h && ix >= 0 && ix < w) {
+                const float4* src = reinterpret_cast<const float4*>(
+                    in + (static_cast<long long>(iy) * w + ix) * cin + ci);
+                lo = __ldg(src);
+                hi = __ldg(src + 1);
+                if (relu) {
+                    lo = make_float4(fmaxf(lo.x, 0.f), fmaxf(lo.y, 0.f), fmaxf(lo.z, 0.f), fmaxf(lo.w, 0.f));
+                    hi = make_float4(fmaxf(hi.x, 0.f), fmaxf(hi.y, 0.f), fmaxf(hi.z, 0.f), fmaxf(hi.w, 0.f));
+                }
+            }
+        }
+        out[v] = make_uint4(to16<T>(lo.x) | (uint32_t(to16<T>(lo.y)) << 16),
+                            to16<T>(lo.z) | (uint32_t(to16<T>(lo.w)) << 16),
+                            to16<T>(hi.x) | (uint32_t(to16<T>(hi.y)) << 16),
+                            to16<T>(hi.z) | (uint32_t(to16<T>(hi.w)) << 16));
+    }
+}
+
+// blocks of 256 threads, up to 8 per SM, never more than the work needs
+unsigned grid_for(long long work) {
+    const long long blocks = (work + 255) / 256;
+    const long long cap = 8ll * gemm::sm_count();
+    return static_cast<unsigned>(blocks < cap ? (blocks > 0 ? blocks : 1) : cap);
+}
+
+}  // namespace dec
+}  // namespace bl
+
+extern "C" {
+
+int bl_im2col(const bl_im2col_args* a, void* stream) {
+    using namespace bl;
+    if (a == nullptr || a->input == nullptr || a->out == nullptr)
+        return fail(BL_ERR_INVALID, "im2col: null argument");
+    if (a->ksize != 1 && a->ksize != 3) return fail(BL_ERR_UNSUPPORTED, "im2col: kernel %u (1 or 3)", a->ksize);
+    if (a->stride < 1 || a->h == 0 || a->w == 0 || a->cin == 0)
+        return fail(BL_ERR_INVALID, "im2col: zero dimension or stride");
+    const uint64_t taps = 1ull * a->ksize * a->ksize * a->cin;
+    if (a->k_pad % 64 != 0 || a->k_pad < taps)
+        return fail(BL_ERR_INVALID, "im2col: k_pad %u must be a multiple of 64 and at least %llu",
+                    a->k_pad, (unsigned long long)taps);
+    if (a->out_dtype != BL_F16 && a->out_dtype != BL_BF16)
+        return fail(BL_ERR_UNSUPPORTED, "im2col: out dtype %d (f16 or bf16)", a->out_dtype);
+    if (reinterpret_cast<uintptr_t>(a->out) & 15u) return fail(BL_ERR_INVALID, "im2col: out must be 16-byte aligned");
+    const int pad = static_cast<int>(a->ksize / 2);
+    const int oh = static_cast<int>((a->h + 2 * pad - a->ksize) / a->stride + 1);
+    const int ow = static_cast<int>((a->w + 2 * pad - a->ksize) / a->stride + 1);
+    const long long work = 1ll * oh * ow * (a->k_pad / 8);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const bool vec = a->cin % 8 == 0 && (reinterpret_cast<uintptr_t>(a->input) & 15u) == 0;
+    auto kern = vec ? (a->out_dtype == BL_F16 ? dec::im2col_vec8_kernel<__half>
+                                              : dec::im2col_vec8_kernel<__nv_bfloat16>)
+                    : (a->out_dtype == BL_F16 ? dec::im2col_kernel<__half>
+                                              : dec::im2col_kernel<__nv_bfloat16>);
+    kern<<<dec::grid_for(work), 256, 0, s>>>(a->input, static_cast<uint4*>(a->out), a->h, a->w,
+                                            a->cin, a->ksize, a->stride, a->relu ? 1 : 0, oh, ow,
+                                            a->k_pad);
+    BL_CUDA_TRY(cudaGetLastError());
+    return BL_OK;
+}
+
+int bl_blocks_to_map(const float* blocks, const float* bias, float* out, uint32_t h, uint32_t w,
+                     uint32_t f, uint32_t cout, void* stream) {
+    using namespace bl;
+    if (blocks == nullptr || out == nullptr) return fail(BL_ERR_INVALID, "blocks_to_map: null argument");
+    if (h == 0 || w == 0 || f == 0 || cout == 0) return fail(BL_ERR_INVALID, "blocks_to_map: zero dimension");
+    const long long work = 1ll * h * f * w * f * cout;
+    dec::blocks_to_map_kernel<<<dec::grid_for(work), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        blocks, bias, out, h, w, f, cout);
+    BL_CUDA_TRY(cudaGetLastError());
+    return BL_OK;
+}
+
+int bl_resize_bilinear(const float* in, float* out, uint32_t ih, uint32_t iw, uint32_t oh,
+                       uint32_t ow, uint32_t c, void* stream) {
+    using namespace bl;
+    if (in == nullptr || out == nullptr) return fail(BL_ERR_INVALID, "resize: null argument");
+    if (ih == 0 || iw == 0 || oh == 0 || ow == 0 || c == 0)
+        return fail(BL_ERR_INVALID, "resize: zero dimension");
+    const long long work = 1ll * oh * ow * c;
+    dec::resize_bilinear_kernel<<<dec::grid_for(work), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        in, out, ih, iw, oh, ow, c);
+    BL_CUDA_TRY(cudaGetLastError());
+    return BL_OK;
+}
+
+}  // extern "C"

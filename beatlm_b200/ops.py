@@ -215,3 +215,98 @@ def patchify(image, *, stream=None, **kw):
     a = patchify_args(image, **kw)
     N.check(N.lib().bl_patchify(ctypes.byref(a), _stream_ptr(stream)))
     return kw["a_out"]
+
+
+# ------------------------------------------------------------------ DPT decoder
+# The reference's Conv2d3x3 / Conv2d1x1 / ConvTranspose2d / ResizeBilinear main
+# ops (crates/beatlm-core/src/kernel.rs:265-319, wgsl.rs:387-514; CPU
+# definitions crates/beatlm-bench/src/reference.rs:25-175) on NHWC f32 maps:
+# a convolution is bl_im2col into 16-bit rows then the tcgen05 GEMM.
+
+def _round_up(v: int, m: int) -> int:
+    return (v + m - 1) // m * m
+
+
+def conv_weights(hwio, ksize: int, cin: int, cout: int, dtype: str = "f16", device="cuda"):
+    """HWIO weights [ks][ks][cin][cout] as the GEMM's [n_pad][k_pad] 16-bit
+    matrix (row co holds column (ky ks + kx) cin + ci), zero-padded to a
+    multiple of 32 rows and 64 columns."""
+    import torch
+    k = ksize * ksize * cin
+    w = np.asarray(hwio, np.float32).reshape(k, cout).T
+    m = np.zeros((_round_up(cout, 32), _round_up(k, 64)), np.float32)
+    m[:cout, :k] = w
+    td = torch.float16 if dtype == "f16" else torch.bfloat16
+    return torch.from_numpy(m).to(td).to(device)
+
+
+def im2col(x, h: int, w: int, cin: int, ksize: int = 3, stride: int = 1, relu: bool = False,
+           k_pad: int | None = None, dtype: str = "f16", stream=None):
+    """``bl_im2col``: the [oh * ow][k_pad] 16-bit rows of an NHWC f32 map."""
+    import torch
+    pad = ksize // 2
+    oh, ow = (h + 2 * pad - ksize) // stride + 1, (w + 2 * pad - ksize) // stride + 1
+    k_pad = k_pad or _round_up(ksize * ksize * cin, 64)
+    td = torch.float16 if dtype == "f16" else torch.bfloat16
+    out = torch.empty((oh * ow, k_pad), dtype=td, device=x.device)
+    a = N.Im2colArgs(input=x.data_ptr(), h=h, w=w, cin=cin, ksize=ksize, stride=stride,
+                     relu=1 if relu else 0, out=out.data_ptr(), out_dtype=_TD[dtype], k_pad=k_pad)
+    N.check(N.lib().bl_im2col(ctypes.byref(a), _stream_ptr(stream)))
+    return out, oh, ow
+
+
+def conv2d(x, weights, bias, h: int, w: int, cin: int, cout: int, *, ksize: int = 3,
+           stride: int = 1, relu_input: bool = False, act=None, residual=None, stream=None):
+    """A 3x3 (zero padding 1) or 1x1 convolution of the NHWC f32 map ``x``:
+    ``weights`` from ``conv_weights``, ``bias`` f32 [cout] or None, ``act``
+    "relu" on the result, ``residual`` an f32 [oh * ow][cout] map added last
+    (cout a multiple of 32). Returns f32 [oh * ow][cout]."""
+    import torch
+    dt = "f16" if weights.dtype == torch.float16 else "bf16"
+    cols, oh, ow = im2col(x, h, w, cin, ksize, stride, relu_input, weights.shape[1], dt, stream)
+    n_pad = weights.shape[0]
+    if residual is not None:
+        if n_pad != cout:
+            raise ValueError("conv2d: a residual needs cout a multiple of 32")
+        residual = residual.reshape(oh * ow, cout)
+    bias_pad = None
+    if bias is not None:
+        bias_pad = torch.zeros(n_pad, dtype=torch.float32, device=x.device)
+        bias_pad[:cout] = bias
+    out = torch.empty((oh * ow, n_pad), dtype=torch.float32, device=x.device)
+    g = gemm_args(weights, a=cols, bias=bias_pad, act=act, residual=residual, out=out)
+    N.check(N.lib().bl_gemm(ctypes.byref(g), _stream_ptr(stream)))
+    return out if n_pad == cout else out[:, :cout].contiguous()
+
+
+def conv_transpose(x, hwio, bias, h: int, w: int, cin: int, cout: int, f: int,
+                   dtype: str = "f16", stream=None):
+    """Transposed convolution of kernel = stride = f, no padding: one GEMM of
+    each pixel by the [(ky f + kx) cout + co][ci] weights, then the f x f
+    blocks scattered into the [h f][w f][cout] map with the bias."""
+    import torch
+    n = f * f * cout
+    if n % 32 != 0:
+        raise ValueError("conv_transpose: f * f * cout must be a multiple of 32")
+    cols, _, _ = im2col(x, h, w, cin, 1, 1, False, None, dtype, stream)
+    wt = np.asarray(hwio, np.float32).reshape(f * f, cin, cout).transpose(0, 2, 1).reshape(n, cin)
+    m = np.zeros((n, cols.shape[1]), np.float32)
+    m[:, :cin] = wt
+    td = torch.float16 if dtype == "f16" else torch.bfloat16
+    wdev = torch.from_numpy(m).to(td).to(x.device)
+    blocks = torch.empty((h * w, n), dtype=torch.float32, device=x.device)
+    g = gemm_args(wdev, a=cols, out=blocks)
+    N.check(N.lib().bl_gemm(ctypes.byref(g), _stream_ptr(stream)))
+    out = torch.empty((h * f * w * f, cout), dtype=torch.float32, device=x.device)
+    N.check(N.lib().bl_blocks_to_map(blocks.data_ptr(), None if bias is None else bias.data_ptr(),
+                                     out.data_ptr(), h, w, f, cout, _stream_ptr(stream)))
+    return out
+
+
+def resize_bilinear(x, ih: int, iw: int, oh: int, ow: int, c: int, stream=None):
+    """``bl_resize_bilinear``: corners aligned, f32 NHWC."""
+    import torch
+    out = torch.empty((oh * ow, c), dtype=torch.float32, device=x.device)
+    N.check(N.lib().bl_resize_bilinear(x.data_ptr(), out.data_ptr(), ih, iw, oh, ow, c,
+                                       _stream_ptr(stream)))
+    return out

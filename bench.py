@@ -188,6 +188,109 @@ class AttentionWorkload:
         return oracle_attention_rate(qkv, self.t, self.h, threads, budget_s)
 
 
+class DecoderWorkload:
+    """A DPT-S fusion residual unit at the first fusion stage's 148 x 148 x 64
+    map: x + conv2(relu(conv1(relu(x)))) (crates/beatlm-bench/src/
+    reference.rs:190-201), two bl_im2col gathers and two tcgen05 GEMMs (the
+    second adds x in its epilogue)."""
+
+    name = "decoder"
+    unit = "TFLOP/s"
+    dtype = "f16 operands, f32 accumulation and maps"
+    data = "synthetic map ~ N(0,1), weights N(0, 1/sqrt(9c)), seeded"
+    workload_name = "dpt_s_residual_unit_148 (decoder, section 8 next row 1)"
+    scaling = "weak"
+    side, c = 148, 64
+
+    def parallelism(self, world):
+        return "replicas x%d (no collective)" % world
+
+    def roofline(self, stream, avg_ms):
+        return {"achieved_tflops": self.flops / (avg_ms / 1e3) / 1e12,
+                "kernel": "bl::gemm::gemm_persistent (2 launches) + im2col (2 launches)",
+                "how": "CUDA events around every timed step; the im2col gathers are inside the "
+                       "time, so the figure is the two GEMMs' floor"}
+
+    @classmethod
+    def reference_step(cls, threads):
+        import numpy as np
+        import oracle
+        side, c = 37, cls.c
+        rng = np.random.default_rng(99)
+        x = rng.standard_normal(side * side * c).astype(np.float32)
+        w = (rng.standard_normal(9 * c * c) / 24).astype(np.float32)
+        b = np.zeros(c, np.float32)
+        fn = lambda: oracle.residual_unit(x, w, b, w, b, side, side, c)
+        return fn, 2 * 2.0 * side * side * c * 9 * c / 1e12, (
+            "one residual unit on a 37 x 37 x 64 map (oracle/oracle.c, f64)")
+
+    def __init__(self, rank: int):
+        import ctypes
+        import numpy as np
+        import torch
+        from beatlm_b200 import _native as N
+        from beatlm_b200 import ops
+        self.N, self.ctypes = N, ctypes
+        side, c = self.side, self.c
+        px = side * side
+        rng = np.random.default_rng(77 + rank)
+        self.x = torch.from_numpy(rng.standard_normal((px, c)).astype(np.float32)).cuda()
+        ws = [(rng.standard_normal(9 * c * c) / 24).astype(np.float32) for _ in range(2)]
+        self.w = [ops.conv_weights(w, 3, c, c) for w in ws]
+        self.b = [torch.from_numpy((rng.standard_normal(c) * 0.1).astype(np.float32)).cuda()
+                  for _ in range(2)]
+        k_pad = self.w[0].shape[1]
+        self.cols = torch.empty((px, k_pad), dtype=torch.float16, device="cuda")
+        self.mid = torch.empty((px, c), dtype=torch.float32, device="cuda")
+        self.out = torch.empty((px, c), dtype=torch.float32, device="cuda")
+        self.host = self.x.cpu().pin_memory()
+        self.out_host = torch.empty((px, c), dtype=torch.float32).pin_memory()
+        mk = lambda src: N.Im2colArgs(input=src.data_ptr(), h=side, w=side, cin=c, ksize=3,
+                                      stride=1, relu=1, out=self.cols.data_ptr(),
+                                      out_dtype=N.BL_F16, k_pad=k_pad)
+        self.i2c = [mk(self.x), mk(self.mid)]
+        self.g = [ops.gemm_args(self.w[0], a=self.cols, bias=self.b[0], out=self.mid),
+                  ops.gemm_args(self.w[1], a=self.cols, bias=self.b[1], residual=self.x,
+                                out=self.out)]
+        self.flops = 2 * 2.0 * px * c * 9 * c
+        self.launches_per_step = 4
+
+    def config(self):
+        return {"workload": self.workload_name, "map": [self.side, self.side, self.c],
+                "convolutions": "2 x 3x3, padding 1, ReLU before each, residual add",
+                "k": 9 * self.c, "l2": "flushed before every timed step (256 MiB write)"}
+
+    def step(self, stream):
+        from beatlm_b200.ops import _stream_ptr
+        s = _stream_ptr(stream)
+        L = self.N.lib()
+        for i in range(2):
+            self.N.check(L.bl_im2col(self.ctypes.byref(self.i2c[i]), s))
+            self.N.check(L.bl_gemm(self.ctypes.byref(self.g[i]), s))
+
+    def step_e2e(self, stream):
+        self.x.copy_(self.host, non_blocking=True)
+        self.step(stream)
+        self.out_host.copy_(self.out, non_blocking=True)
+
+    def e2e_bytes(self):
+        return self.host.numel() * 4, self.out_host.numel() * 4
+
+    def units(self):
+        return self.flops / 1e12
+
+    def cpu_baseline(self, threads: int, budget_s: float = 15.0):
+        fn, tflop, sample = self.reference_step(threads)
+        t0 = time.perf_counter()
+        n = 0
+        while time.perf_counter() - t0 < budget_s or n == 0:
+            fn()
+            n += 1
+        dt = time.perf_counter() - t0
+        return {"value": tflop * n / dt, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                "sample": "%s, %d repeats" % (sample, n)}
+
+
 def oracle_attention_rate(qkv, t, h, threads, budget_s):
     """The reference's CPU path for one attention op (oracle/, a C restatement
     of reference.rs:437-494, f64 accumulation) timed on a bounded sample of
@@ -489,7 +592,7 @@ class HiresWorkload:
 
 
 WORKLOADS = {"attention": AttentionWorkload, "encoder": EncoderWorkload,
-             "vitl": VitLWorkload, "hires": HiresWorkload}
+             "vitl": VitLWorkload, "hires": HiresWorkload, "decoder": DecoderWorkload}
 
 
 # ------------------------------------------------------------------ timing

@@ -444,6 +444,39 @@ int bl_timer_get_stats(const bl_timer* t, bl_timer_stats* out);
  * (timer.rs:208). */
 int bl_stream_hold(void* stream, uint32_t microseconds);
 
+/* ------------------------------------------------------------ DPT decoder */
+
+/*
+ * The DPT decoder's kernels besides its GEMMs (the reference's Conv2d3x3,
+ * Conv2d1x1, ConvTranspose2d and ResizeBilinear main ops with the ReLU
+ * prologue, crates/beatlm-core/src/kernel.rs:265-319 and WGSL
+ * wgsl.rs:387-514; CPU definitions crates/beatlm-bench/src/reference.rs:25-175).
+ * Maps are NHWC f32. A convolution is bl_im2col then bl_gemm with the HWIO
+ * weights as a [cout][k_pad] 16-bit matrix; a transposed convolution of
+ * kernel = stride = f is bl_gemm into [pixels][f*f*cout] then
+ * bl_blocks_to_map. Each call enqueues on `stream`.
+ */
+typedef struct bl_im2col_args {
+    const float* input;  /* [h][w][cin] f32 */
+    uint32_t h, w, cin;
+    uint32_t ksize;      /* 1 or 3 (3: zero padding 1) */
+    uint32_t stride;     /* output pixel (y, x) centred on input (y stride, x stride) */
+    uint32_t relu;       /* non-zero: max(x, 0) applied to every input value */
+    void* out;           /* [oh * ow][k_pad] 16-bit, 16-byte aligned */
+    int32_t out_dtype;   /* BL_F16 or BL_BF16 */
+    uint32_t k_pad;      /* multiple of 64, >= ksize * ksize * cin; columns past it are 0 */
+} bl_im2col_args;
+int bl_im2col(const bl_im2col_args* args, void* stream);
+/* out[(y f + ky)][(x f + kx)][co] = blocks[y * w + x][(ky f + kx) cout + co] + bias[co]
+ * (bias may be NULL): the f x f block each input pixel of a transposed
+ * convolution writes (reference.rs:103-140). */
+int bl_blocks_to_map(const float* blocks, const float* bias, float* out, uint32_t h, uint32_t w,
+                     uint32_t f, uint32_t cout, void* stream);
+/* Bilinear resampling with corners aligned, [ih][iw][c] -> [oh][ow][c]
+ * (reference.rs:142-175), in f32. */
+int bl_resize_bilinear(const float* in, float* out, uint32_t ih, uint32_t iw, uint32_t oh,
+                       uint32_t ow, uint32_t c, void* stream);
+
 /* ------------------------------------------------------------- pass cost */
 
 /*

@@ -77,6 +77,10 @@ def lib():
             L.orc_attention_rows.argtypes = [F32P, sz, sz, sz, f, sz, sz, sz, sz, i, F32P]
             L.orc_vit_block.argtypes = [F32P, ctypes.POINTER(BlockWeights), sz, sz, sz, sz, f, i,
                                         ctypes.c_void_p, ctypes.c_void_p, F32P]
+            L.orc_conv3x3.argtypes = [F32P, F32P, F32P, sz, sz, sz, sz, sz, i, F32P]
+            L.orc_conv1x1.argtypes = [F32P, F32P, F32P, sz, sz, sz, i, F32P]
+            L.orc_conv_transpose.argtypes = [F32P, F32P, F32P, sz, sz, sz, sz, sz, i, F32P]
+            L.orc_resize_bilinear.argtypes = [F32P, sz, sz, sz, sz, sz, F32P]
             L.orc_round_f16.argtypes = [F32P, sz, ctypes.c_void_p]
             L.orc_round_bf16.argtypes = [F32P, sz, ctypes.c_void_p]
             L.orc_round_qkv_bf16.argtypes = [F32P, sz, ctypes.c_void_p]
@@ -262,3 +266,53 @@ def round_bf16(x):
     x = np.array(x, dtype=np.float32, copy=True)
     lib().orc_round_bf16(_p(x), x.size, None)
     return x
+
+
+# ------------------------------------------------------------- DPT decoder
+# crates/beatlm-bench/src/reference.rs:25-230: NHWC maps, HWIO weights.
+
+def conv3x3(x, w, bias, h, wd, cin, cout, stride=1, threads=None):
+    x, w = _f32(x), _f32(w)
+    bias = None if bias is None else _f32(bias)
+    oh, ow = (h - 1) // stride + 1, (wd - 1) // stride + 1
+    out = np.empty(oh * ow * cout, np.float32)
+    lib().orc_conv3x3(_p(x), _p(w), _p(bias), h, wd, cin, cout, stride,
+                      threads or default_threads(), _p(out))
+    return out
+
+
+def conv1x1(x, w, bias, pixels, cin, cout, threads=None):
+    x, w = _f32(x), _f32(w)
+    bias = None if bias is None else _f32(bias)
+    out = np.empty(pixels * cout, np.float32)
+    lib().orc_conv1x1(_p(x), _p(w), _p(bias), pixels, cin, cout, threads or default_threads(),
+                      _p(out))
+    return out
+
+
+def conv_transpose(x, w, bias, h, wd, cin, cout, f, threads=None):
+    x, w = _f32(x), _f32(w)
+    bias = None if bias is None else _f32(bias)
+    out = np.empty(h * f * wd * f * cout, np.float32)
+    lib().orc_conv_transpose(_p(x), _p(w), _p(bias), h, wd, cin, cout, f,
+                             threads or default_threads(), _p(out))
+    return out
+
+
+def resize_bilinear(x, ih, iw, oh, ow, c):
+    x = _f32(x)
+    out = np.empty(oh * ow * c, np.float32)
+    lib().orc_resize_bilinear(_p(x), ih, iw, oh, ow, c, _p(out))
+    return out
+
+
+def relu(x):
+    """reference.rs relu: max(x, 0) elementwise."""
+    return np.maximum(_f32(x), np.float32(0))
+
+
+def residual_unit(x, w1, b1, w2, b2, h, wd, c):
+    """reference.rs:190-201: x + conv2(relu(conv1(relu(x))))."""
+    first = conv3x3(relu(x), w1, b1, h, wd, c, c)
+    second = conv3x3(relu(first), w2, b2, h, wd, c, c)
+    return add(second, x)

@@ -370,3 +370,108 @@ void orc_round_qkv_bf16(float* values, size_t count, void* ctx) {
 void orc_round_qkv_f16(float* values, size_t count, void* ctx) {
     round_qkv(values, count, *(const size_t*)ctx, 0);
 }
+
+/* ------------------------------------------------------------- DPT decoder */
+
+/* crates/beatlm-bench/src/reference.rs:31-77 (conv3x3, conv3x3_strided):
+ * zero padding 1, output (y, x) centred on input (y s, x s), oh = (h-1)/s+1;
+ * per output value the bias, then taps ky, kx, then ci in increasing order,
+ * accumulated in f64 and rounded once. HWIO weights [3][3][cin][cout]. */
+void orc_conv3x3(const float* input, const float* w, const float* bias, size_t h, size_t wd,
+                 size_t cin, size_t cout, size_t stride, int threads, float* out) {
+    const size_t oh = (h - 1) / stride + 1, ow = (wd - 1) / stride + 1;
+#pragma omp parallel for num_threads(threads) schedule(static)
+    for (long long yy = 0; yy < (long long)oh; ++yy) {
+        const size_t y = (size_t)yy;
+        for (size_t x = 0; x < ow; ++x)
+            for (size_t co = 0; co < cout; ++co) {
+                double acc = bias ? (double)bias[co] : 0.0;
+                for (size_t ky = 0; ky < 3; ++ky)
+                    for (size_t kx = 0; kx < 3; ++kx) {
+                        const long long iy = (long long)(y * stride + ky) - 1;
+                        const long long ix = (long long)(x * stride + kx) - 1;
+                        if (iy < 0 || ix < 0 || iy >= (long long)h || ix >= (long long)wd) continue;
+                        const float* a = input + ((size_t)iy * wd + (size_t)ix) * cin;
+                        const float* b = w + (ky * 3 + kx) * cin * cout + co;
+                        for (size_t ci = 0; ci < cin; ++ci) acc += (double)a[ci] * (double)b[ci * cout];
+                    }
+                out[(y * ow + x) * cout + co] = (float)acc;
+            }
+    }
+}
+
+/* reference.rs:79-101 (conv1x1): [pixels][cin] x [cin][cout] + bias, f64. */
+void orc_conv1x1(const float* input, const float* w, const float* bias, size_t pixels,
+                 size_t cin, size_t cout, int threads, float* out) {
+#pragma omp parallel for num_threads(threads) schedule(static)
+    for (long long pp = 0; pp < (long long)pixels; ++pp) {
+        const size_t p = (size_t)pp;
+        for (size_t co = 0; co < cout; ++co) {
+            double acc = bias ? (double)bias[co] : 0.0;
+            for (size_t ci = 0; ci < cin; ++ci)
+                acc += (double)input[p * cin + ci] * (double)w[ci * cout + co];
+            out[p * cout + co] = (float)acc;
+        }
+    }
+}
+
+/* reference.rs:103-140 (conv_transpose): kernel = stride = f, no padding;
+ * input pixel (y, x) adds its channels times tap (ky, kx) of the HWIO weights
+ * [f][f][cin][cout] into output pixel (y f + ky, x f + kx), in f64; the bias
+ * is added last and the sum rounded once. */
+void orc_conv_transpose(const float* input, const float* w, const float* bias, size_t h,
+                        size_t wd, size_t cin, size_t cout, size_t f, int threads, float* out) {
+    const size_t ow = wd * f;
+#pragma omp parallel for num_threads(threads) schedule(static)
+    for (long long yy = 0; yy < (long long)h; ++yy) {
+        const size_t y = (size_t)yy;
+        double* acc = (double*)malloc(sizeof(double) * cout);
+        for (size_t x = 0; x < wd; ++x)
+            for (size_t ky = 0; ky < f; ++ky)
+                for (size_t kx = 0; kx < f; ++kx) {
+                    for (size_t co = 0; co < cout; ++co) acc[co] = 0.0;
+                    const float* px = input + (y * wd + x) * cin;
+                    for (size_t ci = 0; ci < cin; ++ci) {
+                        const float* taps = w + ((ky * f + kx) * cin + ci) * cout;
+                        for (size_t co = 0; co < cout; ++co) acc[co] += (double)px[ci] * (double)taps[co];
+                    }
+                    float* o = out + ((y * f + ky) * ow + x * f + kx) * cout;
+                    for (size_t co = 0; co < cout; ++co)
+                        o[co] = (float)(acc[co] + (bias ? (double)bias[co] : 0.0));
+                }
+        free(acc);
+    }
+}
+
+/* reference.rs:142-175 (resize_bilinear): corners aligned, f64; output row
+ * oy reads position oy (ih-1)/(oh-1) (0 for one output row), between its
+ * floor and the next row, clamped to the last; columns likewise. */
+static void bilinear_axis(size_t o, size_t in, size_t outn, size_t* i0, size_t* i1, double* l) {
+    const double pos = outn > 1 ? (double)o * (double)(in - 1) / (double)(outn - 1) : 0.0;
+    size_t a = (size_t)floor(pos);
+    if (a > in - 1) a = in - 1;
+    *i0 = a;
+    *i1 = a + 1 < in ? a + 1 : in - 1;
+    *l = pos - (double)a;
+}
+
+void orc_resize_bilinear(const float* input, size_t ih, size_t iw, size_t oh, size_t ow,
+                         size_t c, float* out) {
+    for (size_t oy = 0; oy < oh; ++oy) {
+        size_t y0, y1;
+        double ly;
+        bilinear_axis(oy, ih, oh, &y0, &y1, &ly);
+        for (size_t ox = 0; ox < ow; ++ox) {
+            size_t x0, x1;
+            double lx;
+            bilinear_axis(ox, iw, ow, &x0, &x1, &lx);
+            for (size_t ch = 0; ch < c; ++ch) {
+                const double a00 = input[(y0 * iw + x0) * c + ch], a01 = input[(y0 * iw + x1) * c + ch];
+                const double a10 = input[(y1 * iw + x0) * c + ch], a11 = input[(y1 * iw + x1) * c + ch];
+                const double top = (1.0 - lx) * a00 + lx * a01;
+                const double bottom = (1.0 - lx) * a10 + lx * a11;
+                out[(oy * ow + ox) * c + ch] = (float)((1.0 - ly) * top + ly * bottom);
+            }
+        }
+    }
+}

@@ -111,6 +111,17 @@ void orc_round_bf16(float* values, size_t count, void* ctx);
 void orc_round_qkv_bf16(float* values, size_t count, void* ctx);
 void orc_round_qkv_f16(float* values, size_t count, void* ctx);
 
+/* DPT decoder operations (crates/beatlm-bench/src/reference.rs:25-175), NHWC
+ * f32 maps, HWIO weights, f64 accumulation rounded once; bias may be NULL. */
+void orc_conv3x3(const float* input, const float* w, const float* bias, size_t h, size_t wd,
+                 size_t cin, size_t cout, size_t stride, int threads, float* out);
+void orc_conv1x1(const float* input, const float* w, const float* bias, size_t pixels,
+                 size_t cin, size_t cout, int threads, float* out);
+void orc_conv_transpose(const float* input, const float* w, const float* bias, size_t h,
+                        size_t wd, size_t cin, size_t cout, size_t f, int threads, float* out);
+void orc_resize_bilinear(const float* input, size_t ih, size_t iw, size_t oh, size_t ow,
+                         size_t c, float* out);
+
 #ifdef __cplusplus
 }
 #endif

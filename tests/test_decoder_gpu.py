@@ -1,0 +1,116 @@
+"""The DPT decoder's convolutions and resampling on the GPU (bl_im2col +
+the tcgen05 GEMM, bl_blocks_to_map, bl_resize_bilinear) against the oracle
+restatement of the reference's CPU definitions
+(crates/beatlm-bench/src/reference.rs:25-230), at DPT-S shapes on the 37 x 37
+patch grid. f16 operands, f32 accumulation: relative L2 <= 1e-3 against the
+f32 oracle, and <= 1e-5 against the oracle fed the same f16-rounded
+operands."""
+import numpy as np
+import pytest
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+REL = 1e-3
+REL_ROUNDED = 1e-5
+
+
+def _rel(got, want):
+    got, want = np.asarray(got, np.float64).ravel(), np.asarray(want, np.float64).ravel()
+    return float(np.linalg.norm(got - want) / max(np.linalg.norm(want), 1e-30))
+
+
+def _data(seed, n, scale=1.0):
+    return (np.random.default_rng(seed).standard_normal(n) * scale).astype(np.float32)
+
+
+@pytest.mark.parametrize("h,w,cin,cout,stride,relu", [
+    (37, 37, 64, 64, 1, True),     # a fusion residual unit's convolution
+    (37, 37, 384, 64, 1, False),   # the neck's 3x3 to the fusion width
+    (37, 37, 48, 48, 2, False),    # K = 432 padded to 448, cout 48 padded to 64
+    (19, 19, 192, 384, 2, False),  # the deepest stage's strided convolution
+    (20, 23, 3, 32, 1, True),      # cin not a multiple of 8: the per-column gather
+])
+def test_conv3x3_matches_the_reference(h, w, cin, cout, stride, relu):
+    import torch
+    import beatlm_b200 as bl
+    from beatlm_b200 import ops
+    x = _data(1, h * w * cin)
+    wt = _data(2, 9 * cin * cout, 1.0 / np.sqrt(9 * cin))
+    b = _data(3, cout, 0.1)
+    dev = torch.from_numpy(x).cuda()
+    got = ops.conv2d(dev, ops.conv_weights(wt, 3, cin, cout), torch.from_numpy(b).cuda(), h, w,
+                     cin, cout, stride=stride, relu_input=relu).cpu().numpy()
+    assert bl.status(reset=True).code == 0
+    xin = oracle.relu(x) if relu else x
+    want = oracle.conv3x3(xin, wt, b, h, w, cin, cout, stride)
+    assert got.size == want.size
+    rel = _rel(got, want)
+    rounded = oracle.conv3x3(oracle.round_f16(xin), oracle.round_f16(wt), b, h, w, cin, cout,
+                             stride)
+    rel_r = _rel(got, rounded)
+    print("conv3x3 %dx%dx%d->%d s%d: rel-L2 %.2e (f32 oracle), %.2e (rounded operands)"
+          % (h, w, cin, cout, stride, rel, rel_r))
+    assert rel <= REL and rel_r <= REL_ROUNDED
+
+
+@pytest.mark.parametrize("pixels,cin,cout,act", [(1369, 384, 96, None), (1369, 64, 64, "relu"),
+                                                 (5476, 64, 32, "relu")])
+def test_conv1x1_matches_the_reference(pixels, cin, cout, act):
+    import torch
+    from beatlm_b200 import ops
+    x, wt, b = _data(4, pixels * cin), _data(5, cin * cout, 1 / np.sqrt(cin)), _data(6, cout, 0.1)
+    got = ops.conv2d(torch.from_numpy(x).cuda(), ops.conv_weights(wt, 1, cin, cout),
+                     torch.from_numpy(b).cuda(), pixels, 1, cin, cout, ksize=1,
+                     act=act).cpu().numpy()
+    want = oracle.conv1x1(x, wt, b, pixels, cin, cout)
+    if act == "relu":
+        want = oracle.relu(want)
+    assert _rel(got, want) <= REL
+
+
+def test_a_residual_unit_matches_the_reference():
+    """x + conv2(relu(conv1(relu(x)))) (reference.rs:190-201) with the ReLU
+    applied on the way into each im2col and the residual added by the second
+    GEMM's epilogue."""
+    import torch
+    from beatlm_b200 import ops
+    h = w = 37
+    c = 64
+    x = _data(7, h * w * c)
+    w1, w2 = _data(8, 9 * c * c, 1 / 24), _data(9, 9 * c * c, 1 / 24)
+    b1, b2 = _data(10, c, 0.1), _data(11, c, 0.1)
+    dev = torch.from_numpy(x).cuda()
+    first = ops.conv2d(dev, ops.conv_weights(w1, 3, c, c), torch.from_numpy(b1).cuda(), h, w,
+                       c, c, relu_input=True)
+    got = ops.conv2d(first, ops.conv_weights(w2, 3, c, c), torch.from_numpy(b2).cuda(), h, w,
+                     c, c, relu_input=True, residual=dev).cpu().numpy()
+    want = oracle.residual_unit(x, w1, b1, w2, b2, h, w, c)
+    rel = _rel(got, want)
+    print("residual unit: rel-L2 %.2e" % rel)
+    assert rel <= REL
+
+
+@pytest.mark.parametrize("h,w,cin,cout,f", [(37, 37, 48, 48, 4), (37, 37, 96, 96, 2),
+                                            (3, 5, 64, 8, 2)])
+def test_conv_transpose_matches_the_reference(h, w, cin, cout, f):
+    import torch
+    from beatlm_b200 import ops
+    x, wt, b = _data(12, h * w * cin), _data(13, f * f * cin * cout, 1 / np.sqrt(cin)), \
+        _data(14, cout, 0.1)
+    got = ops.conv_transpose(torch.from_numpy(x).cuda(), wt, torch.from_numpy(b).cuda(), h, w,
+                             cin, cout, f).cpu().numpy()
+    want = oracle.conv_transpose(x, wt, b, h, w, cin, cout, f)
+    assert got.size == want.size and _rel(got, want) <= REL
+
+
+@pytest.mark.parametrize("ih,iw,oh,ow,c", [(37, 37, 74, 74, 64), (19, 19, 37, 37, 64),
+                                           (2, 2, 3, 3, 1), (1, 4, 1, 7, 1), (2, 1, 1, 1, 1)])
+def test_resize_bilinear_matches_the_reference(ih, iw, oh, ow, c):
+    import torch
+    from beatlm_b200 import ops
+    x = _data(15, ih * iw * c)
+    got = ops.resize_bilinear(torch.from_numpy(x).cuda(), ih, iw, oh, ow, c).cpu().numpy()
+    want = oracle.resize_bilinear(x, ih, iw, oh, ow, c)
+    assert np.abs(got.ravel() - want).max() <= 1e-5 * max(1.0, np.abs(want).max())
