@@ -121,19 +121,21 @@ __global__ void resize_bilinear_kernel(const float* __restrict__ in, float* __re
 // cin a multiple of 8 (every DPT width): a thread's 8 columns are 8
 // consecutive channels of one tap, read as two 16-byte loads; one division
 // per thread instead of one per column.
+// Index arithmetic in 32 bits (the host launches it only when every index
+// fits): 64-bit divisions cost several times more than the copy itself.
 template <typename T>
 __global__ void im2col_vec8_kernel(const float* __restrict__ in, uint4* __restrict__ out, int h,
                                    int w, int cin, int ks, int stride, int relu, int oh, int ow,
                                    int k_pad) {
-    const int vecs = k_pad / 8;
-    const long long total = static_cast<long long>(oh) * ow * vecs;
+    const unsigned vecs = static_cast<unsigned>(k_pad) / 8u;
+    const unsigned total = static_cast<unsigned>(oh) * static_cast<unsigned>(ow) * vecs;
     const int taps = ks * ks * cin;
     const int pad = ks / 2;
-    for (long long v = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; v < total;
-         v += static_cast<long long>(gridDim.x) * blockDim.x) {
-        const long long pix = v / vecs;
+    for (unsigned v = blockIdx.x * blockDim.x + threadIdx.x; v < total; v += gridDim.x * blockDim.x) {
+        const unsigned pix = v / vecs;
         const int k0 = static_cast<int>(v - pix * vecs) * 8;
-        const int y = static_cast<int>(pix / ow), x = static_cast<int>(pix - static_cast<long long>(y) * ow);
+        const int y = static_cast<int>(pix / static_cast<unsigned>(ow));
+        const int x = static_cast<int>(pix - static_cast<unsigned>(y) * static_cast<unsigned>(ow));
         float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
         if (k0 < taps) {
             const int tap = k0 / cin, ci = k0 - tap * cin;
@@ -188,7 +190,10 @@ int bl_im2col(const bl_im2col_args* a, void* stream) {
     const int ow = static_cast<int>((a->w + 2 * pad - a->ksize) / a->stride + 1);
     const long long work = 1ll * oh * ow * (a->k_pad / 8);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const bool vec = a->cin % 8 == 0 && (reinterpret_cast<uintptr_t>(a->input) & 15u) == 0;
+    // the vector path indexes in 32 bits: outputs and inputs below 2^31 elements
+    const bool vec = a->cin % 8 == 0 && (reinterpret_cast<uintptr_t>(a->input) & 15u) == 0 &&
+                     work < (1ll << 31) - 2ll * 256 * 8 * 148 &&
+                     1ll * a->h * a->w * a->cin < (1ll << 31);
     auto kern = vec ? (a->out_dtype == BL_F16 ? dec::im2col_vec8_kernel<__half>
                                               : dec::im2col_vec8_kernel<__nv_bfloat16>)
                     : (a->out_dtype == BL_F16 ? dec::im2col_kernel<__half>
