@@ -591,3 +591,123 @@ class Encoder:
         fused = self._fused(frames)
         per_block = [7 if not fused else (6 if i == 0 else 5) for i in range(n)]
         return 3 + sum(per_block) + taken  # patchify (2 kernels) + patch GEMM, blocks, norms
+
+
+# ------------------------------------------------------------------ DPT head
+
+@dataclasses.dataclass
+class DecoderConfig:
+    """The DPT head of Depth-Anything-V2-Small (load/depth_anything_v2.rs
+    Config::small): per-stage widths and resampling ("up", f) / ("keep",) /
+    ("down", f), the fusion width and the head width."""
+    neck: tuple = (48, 96, 192, 384)
+    reassemble: tuple = (("up", 4), ("up", 2), ("keep",), ("down", 2))
+    fusion: int = 64
+    head: int = 32
+
+
+def decoder_weights_random(cfg: ViTConfig, dcfg: DecoderConfig, seed: int = 0) -> dict:
+    """Random DPT-head weights by role, HWIO convolutions: N(0, 1/sqrt(fan_in))
+    weights and N(0, 0.02) biases."""
+    rng = np.random.default_rng(seed)
+    w = lambda *s: (rng.standard_normal(s) / math.sqrt(np.prod(s[:-1]))).astype(np.float32)
+    b = lambda n: (rng.standard_normal(n) * 0.02).astype(np.float32)
+    F = dcfg.fusion
+    out = {"stages": [], "fusion": [], "head": {}}
+    for c, rs in zip(dcfg.neck, dcfg.reassemble):
+        st = {"proj_w": w(1, 1, cfg.dim, c), "proj_b": b(c), "neck_w": w(3, 3, c, F)}
+        if rs[0] == "up":
+            st["resize_w"], st["resize_b"] = w(rs[1], rs[1], c, c), b(c)
+        elif rs[0] == "down":
+            st["resize_w"], st["resize_b"] = w(3, 3, c, c), b(c)
+        out["stages"].append(st)
+    for _ in dcfg.neck:
+        unit = lambda: {"w1": w(3, 3, F, F), "b1": b(F), "w2": w(3, 3, F, F), "b2": b(F)}
+        out["fusion"].append({"unit1": unit(), "unit2": unit(), "proj_w": w(1, 1, F, F),
+                              "proj_b": b(F)})
+    out["head"] = {"w1": w(3, 3, F, F // 2), "b1": b(F // 2), "w2": w(3, 3, F // 2, dcfg.head),
+                   "b2": b(dcfg.head), "w3": w(1, 1, dcfg.head, 1), "b3": b(1)}
+    return out
+
+
+class Decoder:
+    """The DPT head on NHWC f32 maps (model/depth_anything_v2.rs:680-982): per
+    stage a 1x1 reassembly convolution and its resampling, a 3x3 convolution
+    without bias to the fusion width; fusion layers deepest first (residual
+    units x + conv2(relu(conv1(relu(x)))), bilinear resampling with corners
+    aligned to the next stage's size, or twice its own after the last, and a
+    1x1 projection); the head (3x3 to F/2, resampling to the input's side, 3x3
+    to the head width with ReLU, 1x1 to one channel with ReLU). Convolutions
+    run as im2col + tcgen05 GEMM (``ops.conv2d``)."""
+
+    def __init__(self, cfg: ViTConfig, dcfg: DecoderConfig, weights: dict, device="cuda"):
+        import torch
+        self.cfg, self.dcfg = cfg, dcfg
+        dev = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(device)
+        F = dcfg.fusion
+        self.stages = []
+        for c, rs, w in zip(dcfg.neck, dcfg.reassemble, weights["stages"]):
+            st = {"proj": (ops.conv_weights(w["proj_w"], 1, cfg.dim, c), dev(w["proj_b"])),
+                  "neck": ops.conv_weights(w["neck_w"], 3, c, F), "resample": rs, "c": c}
+            if rs[0] == "down":
+                st["resize"] = (ops.conv_weights(w["resize_w"], 3, c, c), dev(w["resize_b"]))
+            elif rs[0] == "up":
+                st["resize"] = (np.asarray(w["resize_w"], np.float32), dev(w["resize_b"]))
+            self.stages.append(st)
+        unit = lambda u: (ops.conv_weights(u["w1"], 3, F, F), dev(u["b1"]),
+                          ops.conv_weights(u["w2"], 3, F, F), dev(u["b2"]))
+        self.fusion = [{"unit1": unit(f["unit1"]), "unit2": unit(f["unit2"]),
+                        "proj": (ops.conv_weights(f["proj_w"], 1, F, F), dev(f["proj_b"]))}
+                       for f in weights["fusion"]]
+        h = weights["head"]
+        self.head = {"c1": (ops.conv_weights(h["w1"], 3, F, F // 2), dev(h["b1"])),
+                     "c2": (ops.conv_weights(h["w2"], 3, F // 2, dcfg.head), dev(h["b2"])),
+                     "c3": (ops.conv_weights(h["w3"], 1, dcfg.head, 1), dev(h["b3"]))}
+
+    def _unit(self, x, u, side, residual=None):
+        F = self.dcfg.fusion
+        first = ops.conv2d(x, u[0], u[1], side, side, F, F, relu_input=True)
+        return ops.conv2d(first, u[2], u[3], side, side, F, F, relu_input=True,
+                          residual=x if residual is None else residual)
+
+    def forward(self, features: list, stream=None):
+        """``features``: the encoder's feature maps, [grid^2][dim] f32 each,
+        shallowest first. Returns the relative depth, [side][side] f32 (side =
+        grid * patch)."""
+        cfg, F = self.cfg, self.dcfg.fusion
+        g = cfg.grid
+        maps = []
+        for feat, st in zip(features, self.stages):
+            c = st["c"]
+            x = ops.conv2d(feat, st["proj"][0], st["proj"][1], g, g, cfg.dim, c, ksize=1)
+            side = g
+            kind = st["resample"]
+            if kind[0] == "up":
+                x = ops.conv_transpose(x, st["resize"][0], st["resize"][1], g, g, c, c, kind[1])
+                side = g * kind[1]
+            elif kind[0] == "down":
+                x = ops.conv2d(x, st["resize"][0], st["resize"][1], g, g, c, c, stride=kind[1])
+                side = (g - 1) // kind[1] + 1
+            maps.append((ops.conv2d(x, st["neck"], None, side, side, c, F), side))
+        fused, side = None, None
+        for layer, (stage, s) in enumerate(reversed(maps)):
+            nxt = len(maps) - 2 - layer
+            out_side = maps[nxt][1] if nxt >= 0 else 2 * s
+            f = self.fusion[layer]
+            if fused is None:
+                x = stage
+            else:  # unit1(stage) + previous: the previous map joins the unit's residual
+                x = self._unit(stage, f["unit1"], s, residual=stage + fused)
+            x = self._unit(x, f["unit2"], s)
+            x = ops.resize_bilinear(x, s, s, out_side, out_side, F, stream)
+            fused = ops.conv2d(x, f["proj"][0], f["proj"][1], out_side, out_side, F, F, ksize=1)
+            side = out_side
+        out_side = g * cfg.patch
+        h = self.head
+        x = ops.conv2d(fused, h["c1"][0], h["c1"][1], side, side, F, F // 2)
+        x = ops.resize_bilinear(x, side, side, out_side, out_side, F // 2, stream)
+        x = ops.conv2d(x, h["c2"][0], h["c2"][1], out_side, out_side, F // 2, self.dcfg.head,
+                       act="relu")
+        x = ops.conv2d(x, h["c3"][0], h["c3"][1], out_side, out_side, self.dcfg.head, 1,
+                       ksize=1, act="relu")
+        return x.reshape(out_side, out_side)

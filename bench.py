@@ -188,6 +188,88 @@ class AttentionWorkload:
         return oracle_attention_rate(qkv, self.t, self.h, threads, budget_s)
 
 
+class DepthWorkload:
+    """The whole Depth-Anything-V2-Small model at 518 px, one frame per step:
+    the encoder (one CUDA graph, as the encoder workload runs it) and the DPT
+    head (model.Decoder: im2col + tcgen05 GEMM convolutions, transposed
+    convolutions, bilinear resampling), random weights; frames/s."""
+
+    name = "depth"
+    unit = "frames/s"
+    dtype = "bf16 encoder; f16 decoder operands; f32 accumulation, residual and maps"
+    data = "synthetic 518x518x3 image U[0,1] ImageNet-normalised, random weights, seeded"
+    workload_name = "da_v2_small_depth_518 (encoder + DPT head)"
+    scaling = "weak"
+
+    def parallelism(self, world):
+        return "replicas x%d (no collective)" % world
+
+    @classmethod
+    def reference_step(cls, threads):
+        return EncoderWorkload.reference_step(threads)
+
+    def __init__(self, rank: int):
+        import torch
+        from beatlm_b200.model import Decoder, DecoderConfig, decoder_weights_random
+        self.enc_wl = EncoderWorkload(rank)
+        cfg = self.enc_wl.cfg
+        self.dec = Decoder(cfg, DecoderConfig(), decoder_weights_random(cfg, DecoderConfig(),
+                                                                        seed=rank))
+        self.feats = self.enc_wl.enc.features(1)
+        side = cfg.grid * cfg.patch
+        self.depth_host = torch.empty((side, side), dtype=torch.float32).pin_memory()
+        # ours in the head: 2 per convolution (im2col, GEMM), 3 per transposed
+        # convolution, 1 per resampling: 24 reassembly, 40 fusion, 7 head
+        self.launches_per_step = self.enc_wl.launches_per_step + 71
+        self.flops = self.enc_wl.flops
+
+    def config(self):
+        c = dict(self.enc_wl.config())
+        c.update({"workload": self.workload_name,
+                  "decoder": "DPT-S head: neck 48/96/192/384, fusion 64, head 32, depth 518x518",
+                  "launch": "encoder: one CUDA graph; decoder: direct launches"})
+        return c
+
+    def step(self, stream):
+        self.enc_wl.step(stream)
+        self.depth = self.dec.forward(self.feats, stream)
+
+    def step_e2e(self, stream):
+        self.enc_wl.buf.image.copy_(self.enc_wl.host, non_blocking=True)
+        self.step(stream)
+        self.depth_host.copy_(self.depth, non_blocking=True)
+
+    def e2e_bytes(self):
+        return self.enc_wl.host.numel() * 4, self.depth_host.numel() * 4
+
+    def units(self):
+        return 1
+
+    def roofline(self, stream, avg_ms):
+        return self.enc_wl.roofline(stream, avg_ms)
+
+    def cpu_baseline(self, threads: int, budget_s: float = 15.0):
+        """The encoder's CPU rate (its own bounded sample) and one run of the
+        DPT head through the oracle at 518 px, combined per frame."""
+        import numpy as np
+        import oracle
+        from beatlm_b200.model import DecoderConfig, decoder_weights_random
+        enc = self.enc_wl.cpu_baseline(threads, budget_s)
+        cfg, d = self.enc_wl.cfg, DecoderConfig()
+        w = decoder_weights_random(cfg, d, seed=1)
+        rng = np.random.default_rng(3)
+        feats = [rng.standard_normal(cfg.grid * cfg.grid * cfg.dim).astype(np.float32)
+                 for _ in range(4)]
+        t0 = time.perf_counter()
+        oracle.dpt_head(cfg.grid, cfg.patch, cfg.dim, d.neck, d.reassemble, d.fusion, d.head,
+                        w, feats, threads=threads)
+        t_dec = time.perf_counter() - t0
+        frame_s = 1.0 / enc["value"] + t_dec
+        return {"value": 1.0 / frame_s, "unit": "frames/s", "cores": threads, "kind": "port",
+                "sample": "%s; plus one DPT head at 518 px through oracle/oracle.c (%.1f s)"
+                          % (enc["sample"], t_dec)}
+
+
 class DecoderWorkload:
     """A DPT-S fusion residual unit at the first fusion stage's 148 x 148 x 64
     map: x + conv2(relu(conv1(relu(x)))) (crates/beatlm-bench/src/
@@ -592,7 +674,8 @@ class HiresWorkload:
 
 
 WORKLOADS = {"attention": AttentionWorkload, "encoder": EncoderWorkload,
-             "vitl": VitLWorkload, "hires": HiresWorkload, "decoder": DecoderWorkload}
+             "vitl": VitLWorkload, "hires": HiresWorkload, "decoder": DecoderWorkload,
+             "depth": DepthWorkload}
 
 
 # ------------------------------------------------------------------ timing

@@ -316,3 +316,44 @@ def residual_unit(x, w1, b1, w2, b2, h, wd, c):
     first = conv3x3(relu(x), w1, b1, h, wd, c, c)
     second = conv3x3(relu(first), w2, b2, h, wd, c, c)
     return add(second, x)
+
+
+def dpt_head(grid, patch, dim, neck, reassemble, fusion, head, w, feats, threads=None):
+    """The DPT head of model/depth_anything_v2.rs:680-982 through the oracle's
+    operations (f64 per op): reassembly (1x1, then ConvTranspose up / 3x3
+    stride down / nothing), 3x3 to the fusion width without bias, fusion layers
+    deepest first, the head. `w` holds HWIO weights by role (as
+    beatlm_b200.model.decoder_weights_random makes them); returns the depth
+    map [grid*patch]^2."""
+    g, F = grid, fusion
+
+    def unit(x, u, s):
+        first = conv3x3(relu(x), u["w1"], u["b1"], s, s, F, F, threads=threads)
+        return add(conv3x3(relu(first), u["w2"], u["b2"], s, s, F, F, threads=threads), x)
+
+    maps = []
+    for feat, c, rs, st in zip(feats, neck, reassemble, w["stages"]):
+        x = conv1x1(feat, st["proj_w"], st["proj_b"], g * g, dim, c, threads=threads)
+        side = g
+        if rs[0] == "up":
+            x = conv_transpose(x, st["resize_w"], st["resize_b"], g, g, c, c, rs[1], threads=threads)
+            side = g * rs[1]
+        elif rs[0] == "down":
+            x = conv3x3(x, st["resize_w"], st["resize_b"], g, g, c, c, rs[1], threads=threads)
+            side = (g - 1) // rs[1] + 1
+        maps.append((conv3x3(x, st["neck_w"], None, side, side, c, F, threads=threads), side))
+    fused, side = None, None
+    for layer, (stage, s) in enumerate(reversed(maps)):
+        nxt = len(maps) - 2 - layer
+        out = maps[nxt][1] if nxt >= 0 else 2 * s
+        f = w["fusion"][layer]
+        x = stage if fused is None else add(unit(stage, f["unit1"], s), fused)
+        x = unit(x, f["unit2"], s)
+        x = resize_bilinear(x, s, s, out, out, F)
+        fused = conv1x1(x, f["proj_w"], f["proj_b"], out * out, F, F, threads=threads)
+        side = out
+    h, o = w["head"], g * patch
+    x = conv3x3(fused, h["w1"], h["b1"], side, side, F, F // 2, threads=threads)
+    x = resize_bilinear(x, side, side, o, o, F // 2)
+    x = relu(conv3x3(x, h["w2"], h["b2"], o, o, F // 2, head, threads=threads))
+    return relu(conv1x1(x, h["w3"], h["b3"], o * o, head, 1, threads=threads))

@@ -114,3 +114,30 @@ def test_resize_bilinear_matches_the_reference(ih, iw, oh, ow, c):
     got = ops.resize_bilinear(torch.from_numpy(x).cuda(), ih, iw, oh, ow, c).cpu().numpy()
     want = oracle.resize_bilinear(x, ih, iw, oh, ow, c)
     assert np.abs(got.ravel() - want).max() <= 1e-5 * max(1.0, np.abs(want).max())
+
+
+def _oracle_decoder(cfg, dcfg, w, feats):
+    return oracle.dpt_head(cfg.grid, cfg.patch, cfg.dim, dcfg.neck, dcfg.reassemble,
+                           dcfg.fusion, dcfg.head, w, feats)
+
+
+def test_the_dpt_head_matches_the_reference_chain():
+    """The whole DPT head of Depth-Anything-V2-Small at 266 px (grid 19:
+    stages 76, 38, 19 and 10 a side, fusion to 152, depth at 266 x 266) from
+    random features, against the oracle chain of the reference's decoder. Some
+    20 convolutions in f16 operands each add their rounding: relative L2
+    <= 3e-3 for the depth map."""
+    import torch
+    import beatlm_b200 as bl
+    from beatlm_b200.model import Decoder, DecoderConfig, ViTConfig, decoder_weights_random
+    cfg, dcfg = ViTConfig.small(side=266), DecoderConfig()
+    w = decoder_weights_random(cfg, dcfg, seed=5)
+    feats = [_data(40 + i, cfg.grid * cfg.grid * cfg.dim) for i in range(4)]
+    dec = Decoder(cfg, dcfg, w)
+    depth = dec.forward([torch.from_numpy(f).cuda() for f in feats]).cpu().numpy()
+    assert bl.status(reset=True).code == 0
+    want = _oracle_decoder(cfg, dcfg, w, feats)
+    assert depth.shape == (266, 266)
+    rel = _rel(depth, want)
+    print("DPT head at 266 px: rel-L2 %.2e, max-abs %.2e" % (rel, np.abs(depth.ravel() - want).max()))
+    assert rel <= 3e-3
