@@ -652,7 +652,8 @@ class Decoder:
             if rs[0] == "down":
                 st["resize"] = (ops.conv_weights(w["resize_w"], 3, c, c), dev(w["resize_b"]))
             elif rs[0] == "up":
-                st["resize"] = (np.asarray(w["resize_w"], np.float32), dev(w["resize_b"]))
+                st["resize"] = (ops.conv_transpose_weights(w["resize_w"], c, c, rs[1],
+                                                           device=device), dev(w["resize_b"]))
             self.stages.append(st)
         unit = lambda u: (ops.conv_weights(u["w1"], 3, F, F), dev(u["b1"]),
                           ops.conv_weights(u["w2"], 3, F, F), dev(u["b2"]))
@@ -711,3 +712,17 @@ class Decoder:
         x = ops.conv2d(x, h["c3"][0], h["c3"][1], out_side, out_side, self.dcfg.head, 1,
                        ksize=1, act="relu")
         return x.reshape(out_side, out_side)
+
+    def capture(self, features: list, stream):
+        """The head as one CUDA graph on the non-default ``stream``: every
+        launch's host-side preparation (tensor maps, arguments) and every
+        temporary is made once, at capture; ``replay()`` reruns the kernels
+        on whatever ``features`` then hold. Returns (graph, depth tensor)."""
+        import torch
+        with torch.cuda.stream(stream):
+            self.forward(features)  # first use: allocator pools, kernel attributes
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            depth = self.forward(features)
+        return g, depth

@@ -279,21 +279,35 @@ def conv2d(x, weights, bias, h: int, w: int, cin: int, cout: int, *, ksize: int 
     return out if n_pad == cout else out[:, :cout].contiguous()
 
 
+def conv_transpose_weights(hwio, cin: int, cout: int, f: int, dtype: str = "f16",
+                           device="cuda"):
+    """HWIO weights [f][f][cin][cout] of a transposed convolution as the GEMM's
+    [(ky f + kx) cout + co][k_pad] 16-bit matrix (k_pad = cin rounded up to 64)."""
+    import torch
+    n = f * f * cout
+    wt = np.asarray(hwio, np.float32).reshape(f * f, cin, cout).transpose(0, 2, 1).reshape(n, cin)
+    m = np.zeros((n, _round_up(cin, 64)), np.float32)
+    m[:, :cin] = wt
+    td = torch.float16 if dtype == "f16" else torch.bfloat16
+    return torch.from_numpy(m).to(td).to(device)
+
+
 def conv_transpose(x, hwio, bias, h: int, w: int, cin: int, cout: int, f: int,
                    dtype: str = "f16", stream=None):
     """Transposed convolution of kernel = stride = f, no padding: one GEMM of
     each pixel by the [(ky f + kx) cout + co][ci] weights, then the f x f
-    blocks scattered into the [h f][w f][cout] map with the bias."""
+    blocks scattered into the [h f][w f][cout] map with the bias. ``hwio`` is
+    the HWIO array, or its device matrix from ``conv_transpose_weights``
+    (which a CUDA graph capture needs: nothing then crosses from the host)."""
     import torch
     n = f * f * cout
     if n % 32 != 0:
         raise ValueError("conv_transpose: f * f * cout must be a multiple of 32")
     cols, _, _ = im2col(x, h, w, cin, 1, 1, False, None, dtype, stream)
-    wt = np.asarray(hwio, np.float32).reshape(f * f, cin, cout).transpose(0, 2, 1).reshape(n, cin)
-    m = np.zeros((n, cols.shape[1]), np.float32)
-    m[:, :cin] = wt
-    td = torch.float16 if dtype == "f16" else torch.bfloat16
-    wdev = torch.from_numpy(m).to(td).to(x.device)
+    if isinstance(hwio, torch.Tensor) and hwio.dim() == 2:
+        wdev = hwio
+    else:
+        wdev = conv_transpose_weights(hwio, cin, cout, f, dtype, x.device)
     blocks = torch.empty((h * w, n), dtype=torch.float32, device=x.device)
     g = gemm_args(wdev, a=cols, out=blocks)
     N.check(N.lib().bl_gemm(ctypes.byref(g), _stream_ptr(stream)))

@@ -227,12 +227,14 @@ class DepthWorkload:
         c = dict(self.enc_wl.config())
         c.update({"workload": self.workload_name,
                   "decoder": "DPT-S head: neck 48/96/192/384, fusion 64, head 32, depth 518x518",
-                  "launch": "encoder: one CUDA graph; decoder: direct launches"})
+                  "launch": "encoder: one CUDA graph; decoder: one CUDA graph"})
         return c
 
     def step(self, stream):
         self.enc_wl.step(stream)
-        self.depth = self.dec.forward(self.feats, stream)
+        if getattr(self, "dec_graph", None) is None:  # captured once, at the first warm-up
+            self.dec_graph, self.depth = self.dec.capture(self.feats, stream)
+        self.dec_graph.replay()
 
     def step_e2e(self, stream):
         self.enc_wl.buf.image.copy_(self.enc_wl.host, non_blocking=True)

@@ -141,3 +141,27 @@ def test_the_dpt_head_matches_the_reference_chain():
     rel = _rel(depth, want)
     print("DPT head at 266 px: rel-L2 %.2e, max-abs %.2e" % (rel, np.abs(depth.ravel() - want).max()))
     assert rel <= 3e-3
+
+
+def test_the_captured_head_replays_the_direct_pass():
+    """Decoder.capture: the same kernels on the same features as forward(),
+    so the replayed depth equals the direct one bit for bit, and a replay
+    after the features change follows them."""
+    import torch
+    from beatlm_b200.model import Decoder, DecoderConfig, ViTConfig, decoder_weights_random
+    cfg, dcfg = ViTConfig.small(side=266), DecoderConfig()
+    dec = Decoder(cfg, dcfg, decoder_weights_random(cfg, dcfg, seed=6))
+    feats = [torch.from_numpy(_data(60 + i, cfg.grid * cfg.grid * cfg.dim)).cuda()
+             for i in range(4)]
+    want = dec.forward(feats).clone()
+    s = torch.cuda.Stream()
+    g, depth = dec.capture(feats, s)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(depth, want)
+    for i, f in enumerate(feats):
+        f.copy_(torch.from_numpy(_data(70 + i, f.numel())))
+    want2 = dec.forward(feats).clone()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(depth, want2) and not torch.equal(want, want2)
