@@ -269,8 +269,8 @@ def conv2d(x, weights, bias, h: int, w: int, cin: int, cout: int, *, ksize: int 
         if n_pad != cout:
             raise ValueError("conv2d: a residual needs cout a multiple of 32")
         residual = residual.reshape(oh * ow, cout)
-    bias_pad = None
-    if bias is not None:
+    bias_pad = bias
+    if bias is not None and bias.numel() != n_pad:  # cout padded: zero bias past it
         bias_pad = torch.zeros(n_pad, dtype=torch.float32, device=x.device)
         bias_pad[:cout] = bias
     out = torch.empty((oh * ow, n_pad), dtype=torch.float32, device=x.device)
