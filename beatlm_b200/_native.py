@@ -339,3 +339,20 @@ SIGNATURES.update({
     "bl_arenas_read": (ctypes.c_int, [_vp, ctypes.POINTER(Placement), _u64, _vp, _u64, _vp]),
 })
 SIGNATURES["bl_stream_hold"] = (ctypes.c_int, [_vp, ctypes.c_uint32])
+SIGNATURES["bl_set_wait_limit"] = (ctypes.c_int, [ctypes.c_uint64])
+SIGNATURES["bl_wait_limit"] = (ctypes.c_uint64, [])
+SIGNATURES.update({
+    "bl_peers_buffer_bytes": (ctypes.c_uint64, [ctypes.c_uint64]),
+    "bl_peers_create": (ctypes.c_int, [ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint64,
+                                       ctypes.POINTER(ctypes.c_void_p)]),
+    "bl_peers_handle": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    "bl_peers_open": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t]),
+    "bl_peers_attach": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p]),
+    "bl_peers_slot": (ctypes.c_void_p, [ctypes.c_void_p, ctypes.c_uint32]),
+    "bl_peers_next_epoch": (ctypes.c_uint32, [ctypes.c_void_p]),
+    "bl_peers_destroy": (None, [ctypes.c_void_p]),
+    "bl_attention_peers": (ctypes.c_int, [ctypes.POINTER(AttentionArgs), ctypes.c_void_p,
+                                          ctypes.c_uint32, ctypes.POINTER(ctypes.c_uint32),
+                                          ctypes.c_void_p]),
+})
+PEER_HANDLE_BYTES = 64

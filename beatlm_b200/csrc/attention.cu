@@ -64,6 +64,23 @@ static_assert(kColO + 64 * QT <= kTmemCols, "TMEM columns");
 // this (log2 units), so p <= 2^8, well inside f16.
 constexpr float kRescaleThreshold = 8.0f;
 
+// Head-parallel exchange (bl_attention_peers): every output row of this
+// rank's heads is stored into each rank's output buffer (peer memory over
+// NVLink, the local buffer for this rank), and the launch ends with an
+// arrival barrier: the last CTA of the grid raises this rank's flag in every
+// rank's buffer and waits, bounded, until every rank's flag for this launch
+// has arrived in its own.
+constexpr int kMaxPeers = 8;
+struct PeerParams {
+    int n;                         // ranks the rows go to; 0 = store to `out` only
+    int rank;                      // this rank
+    unsigned epoch;                // this launch's flag value (increases by one per launch)
+    unsigned* done;                // this rank's count of finished CTAs (left at zero)
+    const unsigned* flags;         // this rank's arrival flags, one word per rank
+    uint8_t* dst[kMaxPeers];       // rank r's output base for this launch (column-shifted)
+    unsigned* flag_at[kMaxPeers];  // rank r's flag word of this rank
+};
+
 struct Params {
     int tokens;
     int head_begin;
@@ -175,16 +192,65 @@ __device__ __forceinline__ void store_row(void* base, int dt, const float* o, fl
     }
 }
 
+// One output row of 64 values scaled by inv_l, as eight 16-byte vectors of
+// the 16-bit output type.
+template <int kOutDtype>
+__device__ __forceinline__ void pack_row16(const float* o, float inv_l, uint4 (&pk)[HD / 8]) {
+#pragma unroll
+    for (int c = 0; c < HD / 8; ++c) {
+        const float* v = o + 8 * c;
+        if (kOutDtype == BL_F16)
+            pk[c] = make_uint4(pack_f16x2(v[0] * inv_l, v[1] * inv_l),
+                               pack_f16x2(v[2] * inv_l, v[3] * inv_l),
+                               pack_f16x2(v[4] * inv_l, v[5] * inv_l),
+                               pack_f16x2(v[6] * inv_l, v[7] * inv_l));
+        else
+            pk[c] = make_uint4(pack_bf16x2(v[0] * inv_l, v[1] * inv_l),
+                               pack_bf16x2(v[2] * inv_l, v[3] * inv_l),
+                               pack_bf16x2(v[4] * inv_l, v[5] * inv_l),
+                               pack_bf16x2(v[6] * inv_l, v[7] * inv_l));
+    }
+}
+
+// The end of a head-parallel launch, thread 0 of each CTA, after every
+// storing thread of the CTA fenced its row stores at system scope: count the
+// CTA as finished; the last CTA of the grid raises this rank's flag in every
+// rank's buffer and waits until every rank's flag for this launch has
+// arrived here (a bounded wait: on expiry it records ST_TIMEOUT_PEER with the
+// missing rank and returns). Ranks run on different GPUs, so waiting here for
+// the others cannot deadlock a GPU; a rank that never launches only costs
+// the wait limit.
+__device__ void peer_arrive(const Params& p, const PeerParams& q) {
+    const unsigned total = gridDim.x * gridDim.y * gridDim.z;
+    __threadfence_system();
+    if (atom_add_acq_rel_gpu(q.done, 1u) != total - 1) return;
+    *q.done = 0u;  // nothing else of this launch touches it; the next starts from zero
+    __threadfence_system();
+    for (int r = 0; r < q.n; ++r) st_release_sys(q.flag_at[r], q.epoch);
+    const long long t0 = clock64();
+    const long long limit = wait_limit(p.status);
+    for (int r = 0; r < q.n; ++r) {
+        while (static_cast<int>(ld_acquire_sys(q.flags + r) - q.epoch) < 0) {
+            if (clock64() - t0 > limit) {
+                record_status(p.status, ST_TIMEOUT_PEER, static_cast<uint32_t>(r));
+                return;
+            }
+            __nanosleep(128);
+        }
+    }
+}
+
 // The 256 softmax threads (warps 4..11) only.
 __device__ __forceinline__ void softmax_bar() {
     asm volatile("bar.sync 1, %0;" ::"n"(32 * 4 * QT) : "memory");
 }
 
-template <int kOutDtype>
+template <int kOutDtype, bool kPeers = false>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_fwd(const __grid_constant__ CUtensorMap tm_q,
                   const __grid_constant__ CUtensorMap tm_k,
-                  const __grid_constant__ CUtensorMap tm_v, const Params p) {
+                  const __grid_constant__ CUtensorMap tm_v, const Params p,
+                  const __grid_constant__ PeerParams peers) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -527,12 +593,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int crow = t * BM + row;  // row within the CTA's 256
         const int grow = q0 + crow;
         const bool store = grow < p.row_end && grow < p.tokens;
-        auto out_ptr = [&]() {
+        auto row_offset = [&]() {
             const size_t esz = kOutDtype == BL_F32 ? 4 : 2;
-            return static_cast<uint8_t*>(p.out) +
-                   esz * (static_cast<size_t>(batch) * p.out_batch_stride +
+            return esz * (static_cast<size_t>(batch) * p.out_batch_stride +
                           static_cast<size_t>(grow) * p.out_row_stride +
                           static_cast<size_t>(head - p.out_head_base) * HD);
+        };
+        // The finished row: into `out`, or (head-parallel exchange) into
+        // every rank's output, starting with the next rank so the CTAs of a
+        // rank spread their first stores over the peers.
+        auto store_out = [&](const float* v, float inv) {
+            if constexpr (kPeers && kOutDtype != BL_F32) {
+                {
+                    uint4 pk[HD / 8];
+                    pack_row16<kOutDtype>(v, inv, pk);
+                    const size_t off = row_offset();
+                    for (int d = 0; d < peers.n; ++d) {
+                        int r = peers.rank + 1 + d;
+                        r = r >= peers.n ? r - peers.n : r;
+                        uint4* dst = reinterpret_cast<uint4*>(peers.dst[r] + off);
+#pragma unroll
+                        for (int c = 0; c < HD / 8; ++c) dst[c] = pk[c];
+                    }
+                    return;
+                }
+            }
+            store_row(static_cast<uint8_t*>(p.out) + row_offset(), kOutDtype, v, inv);
         };
         bool do_store = ok && store;
         float inv_l = 1.0f / l;
@@ -578,7 +664,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
                 }
-                store_row(out_ptr(), kOutDtype, acc, 1.0f / wsum);
+                store_out(acc, 1.0f / wsum);
             };
             do_store = false;
             if (p.cluster) {
@@ -664,7 +750,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         }
-        if (do_store) store_row(out_ptr(), kOutDtype, o, inv_l);
+        if (do_store) store_out(o, inv_l);
+        // head-parallel exchange: this thread's row stores (to peers too)
+        // are visible system-wide before the CTA counts itself finished
+        if (kPeers) __threadfence_system();
     }
 
     tc_fence_before();
@@ -674,6 +763,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
+    if (kPeers && threadIdx.x == 0) peer_arrive(p, peers);
     if (threadIdx.x == 0) trace_stamp(p.trace, 7);
 }
 
@@ -729,7 +819,8 @@ int validate(const bl_attention_args& a) {
     return BL_OK;
 }
 
-int prepare(const bl_attention_args& a, void* workspace, uint64_t workspace_bytes, Launch* out) {
+int prepare(const bl_attention_args& a, void* workspace, uint64_t workspace_bytes, Launch* out,
+            const PeerParams* peers = nullptr) {
     int rc = validate(a);
     if (rc != BL_OK) return rc;
     if (a.qk_dtype != BL_F16 && a.qk_dtype != BL_BF16)
@@ -740,7 +831,8 @@ int prepare(const bl_attention_args& a, void* workspace, uint64_t workspace_byte
         return fail(BL_ERR_UNSUPPORTED, "attention: out dtype %d", a.out_dtype);
     if (!(a.scale > 0.0f) || !isfinite(a.scale))
         return fail(BL_ERR_INVALID, "attention: scale must be finite and positive");
-    if (a.qkv == nullptr || a.out == nullptr) return fail(BL_ERR_INVALID, "attention: null pointer");
+    if (a.qkv == nullptr || (a.out == nullptr && peers == nullptr))
+        return fail(BL_ERR_INVALID, "attention: null pointer");
     const uint64_t row = a.qkv_row_stride ? a.qkv_row_stride : 3ull * a.heads * HD;
     const uint64_t orow = a.out_row_stride ? a.out_row_stride : 1ull * a.heads * HD;
     if (row < 3ull * a.heads * HD || row % 8 != 0)
@@ -750,8 +842,20 @@ int prepare(const bl_attention_args& a, void* workspace, uint64_t workspace_byte
         (orow * dtype_size(a.out_dtype)) % 16 != 0 ||
         (reinterpret_cast<uintptr_t>(a.out) & 15u) != 0)
         return fail(BL_ERR_INVALID, "attention: output stride/alignment");
+    if (peers != nullptr) {
+        if (a.out_dtype == BL_F32)
+            return fail(BL_ERR_UNSUPPORTED, "attention: the peer exchange stores 16-bit rows");
+        if (peers->n < 1 || peers->n > kMaxPeers || peers->rank < 0 || peers->rank >= peers->n)
+            return fail(BL_ERR_INVALID, "attention: rank %d of %d peers", peers->rank, peers->n);
+        for (int r = 0; r < peers->n; ++r)
+            if (peers->dst[r] == nullptr || (reinterpret_cast<uintptr_t>(peers->dst[r]) & 15u) ||
+                peers->flag_at[r] == nullptr)
+                return fail(BL_ERR_INVALID, "attention: peer %d has no aligned output", r);
+    }
 
-    auto kern = a.out_dtype == BL_F32   ? attention_fwd<BL_F32>
+    auto kern = peers != nullptr       ? (a.out_dtype == BL_F16 ? attention_fwd<BL_F16, true>
+                                                                : attention_fwd<BL_BF16, true>)
+                : a.out_dtype == BL_F32 ? attention_fwd<BL_F32>
                 : a.out_dtype == BL_F16 ? attention_fwd<BL_F16>
                                         : attention_fwd<BL_BF16>;
     BL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -813,6 +917,7 @@ int prepare(const bl_attention_args& a, void* workspace, uint64_t workspace_byte
     }
     p.trace = reinterpret_cast<unsigned long long*>(a.trace);
     p.status = status_ptr();
+    const PeerParams pq = peers != nullptr ? *peers : PeerParams{};
 
     const dim3 grid(pl.q_ctas, a.head_end - a.head_begin, a.batch * pl.splits);
     if (grid.y > 65535 || grid.z > 65535) return fail(BL_ERR_INVALID, "attention: grid too large");
@@ -830,11 +935,11 @@ int prepare(const bl_attention_args& a, void* workspace, uint64_t workspace_byte
         const dim3 cdim(1, 1, pl.splits);
         out->run = [=](cudaStream_t s) {
             return launch_k_cluster(kern, grid, dim3(kThreads), cdim, kSmemBytes, s, tm_q, tm, tm,
-                                    p);
+                                    p, pq);
         };
     } else {
         out->run = [=](cudaStream_t s) {
-            return launch_k(kern, grid, dim3(kThreads), kSmemBytes, s, tm_q, tm, tm, p);
+            return launch_k(kern, grid, dim3(kThreads), kSmemBytes, s, tm_q, tm, tm, p, pq);
         };
     }
     return BL_OK;
@@ -919,25 +1024,69 @@ constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;  // 16 MiB
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 std::mutex g_noalloc_mu;
-void* g_noalloc_addr[64] = {};
+struct NoAllocSetup {
+    unsigned long long ctx_id = 0;  // the device context the address belongs to
+    void* addr = nullptr;
+};
+NoAllocSetup g_noalloc[64];
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+// The unique id of the calling thread's current CUDA context (cuCtxGetId):
+// a device reset destroys the primary context and the next one gets a new
+// id, so an address looked up in the old one is never reused.
+int current_context_id(unsigned long long* id) {
+    static CtxGetCurrentFn get_current = nullptr;
+    static CtxGetIdFn get_id = nullptr;
+    if (get_current == nullptr || get_id == nullptr) {
+        void* f1 = nullptr;
+        void* f2 = nullptr;
+        cudaDriverEntryPointQueryResult q1, q2;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f1, cudaEnableDefault, &q1) != cudaSuccess ||
+            q1 != cudaDriverEntryPointSuccess ||
+            cudaGetDriverEntryPoint("cuCtxGetId", &f2, cudaEnableDefault, &q2) != cudaSuccess ||
+            q2 != cudaDriverEntryPointSuccess)
+            return bl::fail(BL_ERR_CUDA, "no-alloc attention: cuCtxGetCurrent/cuCtxGetId unavailable");
+        get_current = reinterpret_cast<CtxGetCurrentFn>(f1);
+        get_id = reinterpret_cast<CtxGetIdFn>(f2);
+    }
+    CUcontext ctx = nullptr;
+    if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr || get_id(ctx, id) != CUDA_SUCCESS)
+        return bl::fail(BL_ERR_CUDA, "no-alloc attention: no current CUDA context");
+    return BL_OK;
+}
 
 // The array's device address on the current device. In host code the
 // array's name is only a host-side stand-in, so the address is looked up
-// once per device, with that device current, and cached.
+// with cudaGetSymbolAddress at set-up: once per device (with that device
+// current), and again only if the device's context was replaced (a device
+// reset), so a call never launches on an address from a destroyed context.
 int noalloc_scratch(void** out) {
     int dev = 0;
     BL_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return bl::fail(BL_ERR_UNSUPPORTED, "no-alloc attention: device %d", dev);
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
-    if (g_noalloc_addr[dev] == nullptr) {
-        void* p = nullptr;
-        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (e != cudaSuccess || p == nullptr)
-            return bl::fail(BL_ERR_CUDA, "no-alloc attention: cudaGetSymbolAddress: %s",
-                            cudaGetErrorString(e));
-        g_noalloc_addr[dev] = p;
+    NoAllocSetup& su = g_noalloc[dev];
+    unsigned long long ctx = 0;
+    if (su.addr != nullptr) {
+        int rc = current_context_id(&ctx);
+        if (rc != BL_OK) return rc;
+        if (ctx == su.ctx_id) {
+            *out = su.addr;
+            return BL_OK;
+        }
     }
-    *out = g_noalloc_addr[dev];
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);  // loads the module if needed
+    if (e != cudaSuccess || p == nullptr)
+        return bl::fail(BL_ERR_CUDA, "no-alloc attention: cudaGetSymbolAddress: %s",
+                        cudaGetErrorString(e));
+    int rc = current_context_id(&ctx);
+    if (rc != BL_OK) return rc;
+    su.addr = p;
+    su.ctx_id = ctx;
+    *out = p;
     return BL_OK;
 }
 }  // namespace
@@ -972,6 +1121,58 @@ extern "C" int bl_attention_noalloc(const bl_attention_args* args, void* stream)
                                     0, pl.units * sizeof(unsigned), s));
     }
     return enqueue(l, s);
+}
+
+extern "C" int bl_attention_peers(const bl_attention_args* args, bl_peers* peers,
+                                  uint32_t out_col, uint32_t* slot_out, void* stream) {
+    using namespace bl;
+    if (args == nullptr || peers == nullptr) return fail(BL_ERR_INVALID, "peer attention: null argument");
+    int dev = 0;
+    BL_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev != peers->device)
+        return fail(BL_ERR_INVALID, "peer attention: peers of device %d used on device %d",
+                    peers->device, dev);
+    for (uint32_t r = 0; r < peers->world; ++r)
+        if (peers->base[r] == nullptr)
+            return fail(BL_ERR_INVALID, "peer attention: rank %u's buffer is not mapped", r);
+    bl_attention_args a = *args;
+    const uint64_t orow = a.out_row_stride ? a.out_row_stride : 1ull * a.heads * attn::HD;
+    const uint64_t esz = dtype_size(a.out_dtype);
+    if (a.out_dtype == BL_F32)
+        return fail(BL_ERR_UNSUPPORTED, "peer attention: the exchange stores 16-bit rows");
+    if ((out_col * esz) % 16 != 0 ||
+        out_col + 1ull * (a.head_end - a.out_head_base) * attn::HD > orow)
+        return fail(BL_ERR_INVALID, "peer attention: column %u of %llu-element rows", out_col,
+                    (unsigned long long)orow);
+    if (1ull * a.batch * a.tokens * orow * esz > peers->slot_bytes)
+        return fail(BL_ERR_CAPACITY, "peer attention: the output needs %llu bytes, a slot holds %llu",
+                    (unsigned long long)(1ull * a.batch * a.tokens * orow * esz),
+                    (unsigned long long)peers->slot_bytes);
+    const uint32_t epoch = peers->epoch + 1;
+    const uint32_t slot = epoch & 1u;
+    attn::PeerParams pp{};
+    pp.n = static_cast<int>(peers->world);
+    pp.rank = static_cast<int>(peers->rank);
+    pp.epoch = epoch;
+    pp.done = reinterpret_cast<unsigned*>(peers->local + bl_peers::kDoneOffset);
+    pp.flags = reinterpret_cast<const unsigned*>(peers->local);
+    const uint64_t off = bl_peers::kHeader + slot * peers->slot_stride + out_col * esz;
+    for (uint32_t r = 0; r < peers->world; ++r) {
+        pp.dst[r] = peers->base[r] + off;
+        pp.flag_at[r] = reinterpret_cast<unsigned*>(peers->base[r]) + peers->rank;
+    }
+    a.out = pp.dst[peers->rank];
+    a.out_row_stride = orow;
+    a.workspace = nullptr;  // key splits combine in a cluster
+    a.workspace_bytes = 0;
+    Launch l;
+    int rc = attn::prepare(a, nullptr, 0, &l, &pp);
+    if (rc != BL_OK) return rc;
+    rc = enqueue(l, static_cast<cudaStream_t>(stream));
+    if (rc != BL_OK) return rc;
+    peers->epoch = epoch;
+    if (slot_out != nullptr) *slot_out = slot;
+    return BL_OK;
 }
 
 extern "C" uint64_t bl_attention_workspace_bytes(const bl_attention_args* args) {

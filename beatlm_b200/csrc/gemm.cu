@@ -674,8 +674,9 @@ __device__ bool norm_tile(const Params& p, const CUtensorMap* tmn, const float* 
         __threadfence();  // ... and published (cumulative over the barrier)
         atomicAdd(ctr, 1u);
         const long long t0 = clock64();
+        const long long limit = wait_limit(p.status);
         while (ld_acquire_gpu(ctr) < static_cast<unsigned>(parts)) {
-            if (*abort || clock64() - t0 > kWaitLimitCycles) {
+            if (*abort || clock64() - t0 > limit) {
                 if (!*abort) record_status(p.status, ST_TIMEOUT_SOFTMAX, 0x300 + m0 / BM);
                 *abort = 1;
                 ok = false;

@@ -131,15 +131,39 @@ extern "C" int bl_status(bl_status_t* out, int reset) {
     if (p == nullptr) return bl::fail(BL_ERR_CUDA, "no device status word on this device");
     BL_CUDA_TRY(cudaDeviceSynchronize());
     bl::Status s{};
-    BL_CUDA_TRY(cudaMemcpy(&s, p, sizeof s, cudaMemcpyDeviceToHost));
+    BL_CUDA_TRY(cudaMemcpy(&s, p, bl::kStatusReportBytes, cudaMemcpyDeviceToHost));
     if (out != nullptr) {
         out->code = s.code;
         out->block = s.block;
         out->where = s.where;
         out->count = s.count;
     }
-    if (reset) BL_CUDA_TRY(cudaMemset(p, 0, sizeof s));
+    // the error fields only: the wait limit stays as the host set it
+    if (reset) BL_CUDA_TRY(cudaMemset(p, 0, bl::kStatusReportBytes));
     return BL_OK;
+}
+
+extern "C" int bl_set_wait_limit(uint64_t cycles) {
+    bl::Status* p = bl::status_ptr();
+    if (p == nullptr) return bl::fail(BL_ERR_CUDA, "no device status word on this device");
+    if (cycles > 60ull * 1965ull * 1000ull * 1000ull)
+        return bl::fail(BL_ERR_INVALID, "wait limit %llu cycles (at most about 60 s)",
+                        (unsigned long long)cycles);
+    unsigned long long v = cycles;
+    // ordered after earlier work on the legacy stream and before later launches
+    BL_CUDA_TRY(cudaMemcpy(&p->limit_cycles, &v, sizeof v, cudaMemcpyHostToDevice));
+    return BL_OK;
+}
+
+extern "C" uint64_t bl_wait_limit(void) {
+    bl::Status* p = bl::status_ptr();
+    unsigned long long v = 0;
+    if (p == nullptr || cudaMemcpy(&v, &p->limit_cycles, sizeof v, cudaMemcpyDeviceToHost) !=
+                            cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return v;
 }
 
 namespace bl {

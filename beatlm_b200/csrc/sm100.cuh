@@ -20,6 +20,7 @@ enum : uint32_t {
     ST_TIMEOUT_SOFTMAX = 0x30,  // softmax waited for scores / output
     ST_TIMEOUT_DRAIN = 0x40,    // unwinding waited for copies in flight
     ST_BAD_ARGS = 0x50,
+    ST_TIMEOUT_PEER = 0x60,     // a peer rank's arrival flag never came
 };
 
 struct Status {
@@ -27,11 +28,26 @@ struct Status {
     uint32_t block;     // linear block index that recorded it
     uint32_t where;     // role / loop position
     uint32_t count;     // number of error events
+    // The wait limit in SM clock cycles, set from the host (bl_set_wait_limit;
+    // 0 = kWaitLimitCycles). Not cleared by a status reset.
+    unsigned long long limit_cycles;
+    unsigned long long reserved;
 };
+constexpr size_t kStatusReportBytes = 4 * sizeof(uint32_t);  // what bl_status reads and clears
 
-// A wait gives up after this many SM clock cycles: 1 s at the B200's
-// 1965 MHz maximum, under 2 s at any clock the part runs at under load.
+// A wait gives up after this many SM clock cycles unless the host set another
+// limit: 1 s at the B200's 1965 MHz maximum, under 2 s at any clock the part
+// runs at under load.
 constexpr long long kWaitLimitCycles = 1965ll * 1000ll * 1000ll;
+
+// The limit a wait that has started spinning applies (read once, on the slow
+// path).
+__device__ __forceinline__ long long wait_limit(const Status* st) {
+    if (st == nullptr) return kWaitLimitCycles;
+    const unsigned long long l = *reinterpret_cast<const volatile unsigned long long*>(
+        &st->limit_cycles);
+    return l != 0 ? static_cast<long long>(l) : kWaitLimitCycles;
+}
 
 __device__ __forceinline__ void record_status(Status* st, uint32_t code, uint32_t where) {
     if (st == nullptr) return;
@@ -41,6 +57,24 @@ __device__ __forceinline__ void record_status(Status* st, uint32_t code, uint32_
         st->where = where;
     }
     atomicAdd(&st->count, 1u);
+}
+
+// System-scope release store and acquire load of a 32-bit flag (a word in
+// this GPU's memory or a peer GPU's, mapped into this address space).
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+// atomicAdd with acquire-release semantics at GPU scope.
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v)
+                 : "memory");
+    return old;
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -83,7 +117,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 
 // Waits for the phase of parity `parity` to complete. Gives up when `abort`
 // (a shared flag; may be null) is raised by another role, or after
-// kWaitLimitCycles, in which case it records `code` and raises `abort`.
+// the wait limit (wait_limit), in which case it records `code` and raises
+// `abort`.
 // Returns false when it gave up. The clock is read only on the slow path.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
                                           Status* st, uint32_t code, uint32_t where) {
@@ -93,7 +128,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
         if (mbar_try_wait(bar, parity)) return true;
         if ((spin & 255u) == 0u) {
             if (abort != nullptr && *abort) return false;
-            if (clock64() - t0 > kWaitLimitCycles) {
+            if (clock64() - t0 > wait_limit(st)) {
                 if (abort != nullptr) *abort = 1;
                 record_status(st, code, where);
                 return false;
@@ -352,7 +387,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
         if (probe()) return true;
         if ((spin & 255u) == 0u) {
             if (abort != nullptr && *abort) return false;
-            if (clock64() - t0 > kWaitLimitCycles) {
+            if (clock64() - t0 > wait_limit(st)) {
                 if (abort != nullptr) *abort = 1;
                 record_status(st, code, where);
                 return false;

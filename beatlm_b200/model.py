@@ -240,6 +240,15 @@ class Buffers:
         return 0, last
 
 
+def _on_stream(stream):
+    """A context that makes ``stream`` current (no-op for None), so torch
+    copies and temporaries and every library call given no stream of its own
+    run on one stream."""
+    import contextlib
+    import torch
+    return torch.cuda.stream(stream) if stream is not None else contextlib.nullcontext()
+
+
 def _weights_gemm(w, **kw):
     """``ops.gemm_args`` for a GEMM whose B, bias and scale are model weights
     (never written by the kernel before it: fetched before that one ends)."""
@@ -547,8 +556,11 @@ class Encoder:
         [frames * grid^2][dim] each) of the layers in ``out_indices`` (those
         within ``layers``)."""
         buf = self.buffers(frames)
-        buf.image.copy_(image)
-        self.program(frames, layers).encode_all(stream)
+        # the copy and the kernels run on one stream: `stream` when given
+        # (made current for the copy), else the current stream
+        with _on_stream(stream):
+            buf.image.copy_(image)
+            self.program(frames, layers).encode_all(None)
         return self.features(frames, layers)
 
     def capture_host(self, frames: int, host_image, host_features: list, stream=None):
@@ -674,7 +686,14 @@ class Decoder:
     def forward(self, features: list, stream=None):
         """``features``: the encoder's feature maps, [grid^2][dim] f32 each,
         shallowest first. Returns the relative depth, [side][side] f32 (side =
-        grid * patch)."""
+        grid * patch). Every kernel and temporary of the head runs on
+        ``stream`` when given (it is made current for the whole pass), else
+        on the current stream."""
+        with _on_stream(stream):
+            return self._forward(features)
+
+    def _forward(self, features: list):
+        stream = None  # the current stream, for every op
         cfg, F = self.cfg, self.dcfg.fusion
         g = cfg.grid
         maps = []

@@ -270,9 +270,14 @@ def conv2d(x, weights, bias, h: int, w: int, cin: int, cout: int, *, ksize: int 
             raise ValueError("conv2d: a residual needs cout a multiple of 32")
         residual = residual.reshape(oh * ow, cout)
     bias_pad = bias
-    if bias is not None and bias.numel() != n_pad:  # cout padded: zero bias past it
+    # The kernel reads the bias as n_pad f32 values of device memory: the
+    # caller's tensor is used in place only when it is exactly that; anything
+    # else (another dtype, a stride, host memory, cout padded) is copied into
+    # a zero-padded f32 device vector.
+    if bias is not None and not (bias.dtype == torch.float32 and bias.is_contiguous()
+                                 and bias.device == x.device and bias.numel() == n_pad):
         bias_pad = torch.zeros(n_pad, dtype=torch.float32, device=x.device)
-        bias_pad[:cout] = bias
+        bias_pad[:cout] = bias.reshape(-1)[:cout].to(device=x.device, dtype=torch.float32)
     out = torch.empty((oh * ow, n_pad), dtype=torch.float32, device=x.device)
     g = gemm_args(weights, a=cols, bias=bias_pad, act=act, residual=residual, out=out)
     N.check(N.lib().bl_gemm(ctypes.byref(g), _stream_ptr(stream)))

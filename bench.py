@@ -2,36 +2,47 @@
 """Benchmark of the ViT attention hot path on B200 (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload encoder|attention|vitl|hires]
+                    [--workload encoder|attention|block|vitl|hires|decoder|depth]
+                    [--no-extra] [--no-cpu-baseline]
 
 Workloads (synthetic data, seeded):
   encoder    config 3 (default): the DA-V2-Small ViT-S/14 encoder at 518 px,
              one frame per step through a CUDA graph; frames/s.
   attention  config 1: one ViT-S self-attention op, batch 1, 6 heads x 64,
              1370 tokens, Q/K/V ~ N(0,1), scale 1/8; f16 Q/K/V, f32 output.
+  block      config 2: one pre-LN ViT-S block (dim 384, 6 heads, MLP 1536,
+             1370 tokens) in f16, one CUDA graph per step; TFLOP/s.
   vitl       config 4: the ViT-L/14 encoder, one independent stream per GPU.
-  hires      config 5: T=5477 attention, 16 heads split over the GPUs, NCCL
-             all-gather of the head outputs; TFLOP/s of the whole op.
+  hires      config 5: T=5477 attention, 16 heads split over the GPUs; each
+             rank's attention kernel stores its heads' rows straight into
+             every rank's [T][1024] output over NVLink (peer stores, no
+             separate collective); TFLOP/s of the whole op.
 
-A step is one pass of the hot path over one batch. `value` is whole-job
-throughput (all ranks) with the inputs resident in HBM; L2 is flushed (a
-256 MiB write) before every timed step and the flush is outside the timed
-events. `e2e` is the same metric through the public call with host buffers:
-the H2D copy of the step's inputs from pinned memory and the D2H copy of its
-result are inside its timed region. Multi-GPU: one process per GPU
-(torchrun); configs 1-4 run independent replicas or streams (weak scaling),
-config 5 splits one op by heads (strong scaling); times are the max over
-ranks.
+With the default workload the line also carries, under "configs", the other
+configs measured in the same run (configs 1, 2, 4 and 5 on one GPU; 4 and 5
+on several), each with its own roofline, parity against the oracle and, on
+one GPU, CPU baseline. A step is one pass of the hot path over one batch.
+`value` is whole-job throughput (all ranks) with the inputs resident in HBM;
+L2 is flushed (a 256 MiB write) before every timed step and the flush is
+outside the timed events. `e2e` is the same metric through the public call
+with host buffers: the H2D copy of the step's inputs from pinned memory and
+the D2H copy of its result are inside its timed region. Multi-GPU: one
+process per GPU (torchrun); configs 1-4 run independent replicas or streams
+(weak scaling), config 5 splits one op by heads (strong scaling); times are
+the max over ranks.
 
 `--impl reference` times the reference's CPU path (the C restatement of its
-f64 interpreter, oracle/, all host threads) on the same workload, rank 0 only.
+f64 interpreter, oracle/, all host threads) on the same workload, rank 0 only:
+for the encoder every step is one whole frame, evaluated op by op as the
+reference's `run` evaluates the encoder graph. The `cpu_baseline` leg of our
+own line times the same function on the same inputs (median of 3 frames).
 """
 from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
+import statistics
 import subprocess
 import sys
 import time
@@ -40,6 +51,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "ViT attention TFLOP/s (% of B200 bf16 peak); DA-V2-S 518² encoder frames/s"
+IMAGENET_MEAN = (0.485, 0.456, 0.406)
+IMAGENET_STD = (0.229, 0.224, 0.225)
 
 
 def peaks():
@@ -109,6 +122,26 @@ class Clocks:
                         "reasons": reasons, "samples": len(rows)}
 
 
+def _rel(got, want):
+    import numpy as np
+    got = np.asarray(got, np.float64).ravel()
+    want = np.asarray(want, np.float64).ravel()
+    return (float(np.linalg.norm(got - want) / max(np.linalg.norm(want), 1e-30)),
+            float(np.max(np.abs(got - want))))
+
+
+def _median_time(fn, repeats):
+    """Median wall time of `repeats` calls of fn (after none: the oracle's
+    thread pool and pages are warmed by the first repeat's own start), and
+    the last call's result."""
+    times, out = [], None
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        out = fn()
+        times.append(time.perf_counter() - t0)
+    return statistics.median(times), times, out
+
+
 # ------------------------------------------------------------------ workloads
 
 class AttentionWorkload:
@@ -120,6 +153,7 @@ class AttentionWorkload:
     data = "synthetic Q/K/V ~ N(0,1), seeded"
     workload_name = "vit_s_attention_op (config 1)"
     scaling = "weak"
+    T, H = 1370, 6
 
     def parallelism(self, world):
         return "replicas x%d (no collective)" % world
@@ -130,12 +164,16 @@ class AttentionWorkload:
                 "how": "CUDA events around every timed launch (a step is one launch)"}
 
     @classmethod
-    def reference_step(cls, threads):
+    def host_qkv(cls, seed=1234):
         import numpy as np
+        rng = np.random.default_rng(seed)
+        return rng.standard_normal((1, cls.T, 3, cls.H, 64), dtype=np.float32)
+
+    @classmethod
+    def reference_step(cls, threads):
         import oracle
-        t, h = 1370, 6
-        rng = np.random.default_rng(1234)
-        qkv = oracle.round_f16(rng.standard_normal((t, 3 * h * 64), dtype=np.float32))
+        t, h = cls.T, cls.H
+        qkv = oracle.round_f16(cls.host_qkv()[0].reshape(t, -1))
         rows = 32
         t0 = time.perf_counter()
         oracle.attention(qkv, t, h, 64, rows=(0, rows), threads=threads)
@@ -145,31 +183,26 @@ class AttentionWorkload:
         return fn, 4.0 * rows * t * h * 64 / 1e12, (
             "%d of %d query rows x %d heads per step (oracle/oracle.c, f64)" % (rows, t, h))
 
-    def __init__(self, rank: int, batch: int = 1):
-        import numpy as np
+    def __init__(self, rank: int, world: int = 1):
         import torch
         import beatlm_b200 as bl
         self.bl = bl
-        self.t, self.h, self.batch = 1370, 6, batch
-        rng = np.random.default_rng(1234 + rank)
-        qkv = rng.standard_normal((batch, self.t, 3, self.h, 64), dtype=np.float32)
-        self.dev = bl.pack_qkv(qkv, "f16")
+        self.t, self.h = self.T, self.H
+        self.qkv = self.host_qkv()
+        self.dev = bl.pack_qkv(self.qkv, "f16")
         self.host = self.dev.cpu().pin_memory()
-        self.out = torch.empty((batch, self.t, self.h * 64), dtype=torch.float32, device="cuda")
+        self.out = torch.empty((1, self.t, self.h * 64), dtype=torch.float32, device="cuda")
         self.out_host = torch.empty(self.out.shape, dtype=torch.float32).pin_memory()
-        self.flops = 4.0 * self.t * self.t * self.h * 64 * batch
-        self.unit_bytes = self.dev.numel() * 2 + self.out.numel() * 4
+        self.flops = 4.0 * self.t * self.t * self.h * 64
         self.launches_per_step = 1
 
     def config(self):
-        return {"workload": "vit_s_attention_op (config 1)", "batch": self.batch,
-                "tokens": self.t, "heads": self.h, "head_dim": 64,
-                "qkv_dtype": "f16", "out_dtype": "f32",
+        return {"workload": self.workload_name, "batch": 1, "tokens": self.t, "heads": self.h,
+                "head_dim": 64, "qkv_dtype": "f16", "out_dtype": "f32",
                 "l2": "flushed before every timed launch (256 MiB write)"}
 
     def step(self, stream):
-        self.bl.attention(self.dev, tokens=self.t, heads=self.h, batch=self.batch,
-                          out=self.out, stream=stream)
+        self.bl.attention(self.dev, tokens=self.t, heads=self.h, out=self.out, stream=stream)
 
     def step_e2e(self, stream):
         self.dev.copy_(self.host, non_blocking=True)
@@ -182,10 +215,573 @@ class AttentionWorkload:
     def units(self):
         return self.flops / 1e12  # TFLOP per step
 
-    def cpu_baseline(self, threads: int, budget_s: float = 15.0):
-        import torch
-        qkv = self.host[0].view(torch.float16).float().numpy().reshape(self.t, -1)
+    def parity(self):
+        """A sample of 64 query rows (all heads) against the oracle fed the
+        same f16 values."""
+        import oracle
+        rows = (0, 32), (self.t - 32, self.t)
+        ref_in = oracle.round_f16(self.qkv[0].reshape(self.t, -1))
+        got = self.out_host[0].numpy()
+        out = []
+        for r0, r1 in rows:
+            want = oracle.attention(ref_in, self.t, self.h, 64, rows=(r0, r1))
+            out.append((got[r0:r1].ravel(), want))
+        import numpy as np
+        rel, mx = _rel(np.concatenate([g for g, _ in out]), np.concatenate([w for _, w in out]))
+        return {"rel_l2": rel, "max_abs": mx, "bound": 1e-3,
+                "sample": "query rows 0-31 and 1338-1369, all 6 heads, vs oracle.attention"}
+
+    def cpu_baseline(self, threads: int, budget_s: float = 8.0):
+        import oracle
+        qkv = oracle.round_f16(self.qkv[0].reshape(self.t, -1))
         return oracle_attention_rate(qkv, self.t, self.h, threads, budget_s)
+
+
+def oracle_attention_rate(qkv, t, h, threads, budget_s):
+    """The reference's CPU path for one attention op (oracle/, a C restatement
+    of reference.rs:437-494, f64 accumulation) timed on a bounded sample of
+    query rows of every head, in TFLOP/s: the median of three repeats."""
+    import oracle
+    rows = 16
+    t0 = time.perf_counter()
+    oracle.attention(qkv, t, h, 64, rows=(0, rows), threads=threads)
+    dt = time.perf_counter() - t0
+    rows = int(min(t, max(rows, rows * budget_s / max(dt, 1e-6) / 4)))
+    med, _, _ = _median_time(lambda: oracle.attention(qkv, t, h, 64, rows=(0, rows),
+                                                      threads=threads), 3)
+    flops = 4.0 * rows * t * h * 64
+    return {"value": flops / med / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": "%d of %d query rows x %d heads, median of 3 repeats (f64 accumulation, "
+                      "oracle/oracle.c)" % (rows, t, h)}
+
+
+def encoder_host_inputs(cfg, seed=99):
+    """The encoder's random weights (N(0, 0.02) linear weights, biases 0,
+    LayerNorm gamma 1 / beta 0, LayerScale 1) and one ImageNet-normalised
+    U[0,1] frame, from one seed: the same values for the GPU run, its CPU
+    baseline and the reference arm."""
+    import numpy as np
+    from beatlm_b200.model import block_weights_normal
+    rng = np.random.default_rng(seed)
+    n = lambda *s: rng.standard_normal(int(np.prod(s)), dtype=np.float32) * 0.02
+    w = {"blocks": [block_weights_normal(rng, cfg.dim, cfg.mlp) for _ in range(cfg.layers)],
+         "patch_w": n(cfg.patch, cfg.patch, cfg.cin, cfg.dim), "patch_b": n(cfg.dim),
+         "cls": n(cfg.dim), "pos": n(cfg.tokens, cfg.dim),
+         "norm_g": np.ones(cfg.dim, np.float32), "norm_b": np.zeros(cfg.dim, np.float32)}
+    mean = np.array(IMAGENET_MEAN, np.float32)
+    std = np.array(IMAGENET_STD, np.float32)
+    img = ((rng.random((1, cfg.side, cfg.side, cfg.cin), dtype=np.float32) - mean)
+           / std).astype(np.float32)
+    return w, img
+
+
+def oracle_frame_fn(cfg, w, img, threads, dtype="bf16"):
+    """One whole encoder frame through the oracle (oracle.encoder_frame: the
+    reference's interpreter over the encoder graph), fed the weights and
+    pixels rounded as the device holds them."""
+    import oracle
+    from beatlm_b200.model import DeviceBlock
+    rnd = oracle.round_bf16 if dtype == "bf16" else oracle.round_f16
+    wr = dict(w, patch_w=rnd(w["patch_w"]),
+              blocks=[DeviceBlock.rounded(b, dtype) for b in w["blocks"]])
+    image = rnd(img[0])
+    return lambda: oracle.encoder_frame(image, wr, cfg.grid, cfg.patch, cfg.cin, cfg.dim,
+                                        cfg.heads, cfg.mlp, cfg.eps, cfg.out_indices,
+                                        qkv_round="qk_" + dtype, threads=threads)
+
+
+class EncoderWorkload:
+    """Config 3: the Depth-Anything-V2-Small ViT-S/14 encoder at 518 px, 12
+    blocks, bf16, random N(0, 0.02) weights (LayerNorm gamma 1 / beta 0,
+    LayerScale 1), one frame per forward (batch 1), input U[0,1] normalised by
+    the ImageNet mean/std. A step is one frame through a captured CUDA graph of
+    the whole encoder (patch embedding, 12 blocks, the four feature
+    LayerNorms)."""
+
+    name = "encoder"
+    unit = "frames/s"
+    dtype = "bf16 (weights, activations, Q/K); f16 V and P; f32 accumulate and residual"
+    data = "synthetic: ImageNet-normalised U[0,1] 518x518x3 image, N(0,0.02) weights, seeded"
+    workload_name = "da_v2_small_encoder_518 (config 3)"
+    large = False
+    scaling = "weak"
+    launch = "graph"  # or "direct": every kernel launched from the host each step
+
+    @classmethod
+    def vit_config(cls):
+        from beatlm_b200.model import ViTConfig
+        return ViTConfig.large() if cls.large else ViTConfig.small()
+
+    def roofline(self, stream, avg_ms):
+        prof = self.slice_profile(stream)
+        n, tot, avg_us = prof["attention"]
+        steps = n / self.cfg.layers
+        return {"achieved_tflops": self.attn_flops / (avg_us / 1e6) / 1e12,
+                "kernel": "bl::attn::attention_fwd (%d launches per frame)" % self.cfg.layers,
+                "how": "cudaEvent slice timer (bl_timer) around every kernel of 5 direct "
+                       "(non-graph) encodes after the timed region, each queued behind a "
+                       "20 ms stream hold so the kernels run back to back",
+                "traffic": (None if self.large else
+                            profiled_traffic("attention_fwd_encoder_vit_s_T1370_H6.md")),
+                "frame_tflops": self.flops / (avg_ms / 1e3) / 1e12,
+                "kernels": {k: round(v[1] / steps, 2) for k, v in sorted(prof.items())}}
+
+    @classmethod
+    def reference_step(cls, threads):
+        """ViT-S: one whole frame of the oracle per step (patch embedding, 12
+        blocks, the feature LayerNorms), the same function as the cpu_baseline
+        leg. ViT-L: one block per step (1/24 of a frame; a frame of the f64
+        oracle takes about half a minute), scaled to a frame."""
+        cfg = cls.vit_config()
+        if cls.large:
+            return VitLWorkload.block_step(cfg, threads)
+        w, img = encoder_host_inputs(cfg)
+        return oracle_frame_fn(cfg, w, img, threads), 1.0, (
+            "one whole ViT-S frame per step (patch embedding, 12 blocks, 4 feature "
+            "LayerNorms) through oracle.encoder_frame (reference.rs run), f64 accumulation")
+
+    def parallelism(self, world):
+        return ("%d independent streams, one per GPU, no collective" % world if world > 1
+                else "1 stream")
+
+    def __init__(self, rank: int, world: int = 1, frames: int = 1):
+        import torch
+        from beatlm_b200.model import Encoder
+        self.cfg = cfg = self.vit_config()
+        self.w, img = encoder_host_inputs(cfg, seed=99 + rank)
+        self.frames = frames
+        self.enc = Encoder(cfg, self.w, "bf16", planned_frames=frames)
+        self.img = img
+        self.host = torch.from_numpy(img).pin_memory()
+        self.buf = self.enc.buffers(frames)
+        self.buf.image.copy_(self.host)
+        self.prog = self.enc.program(frames)
+        self.graph = None
+        self.feats_host = [torch.empty(f.shape, dtype=f.dtype).pin_memory()
+                           for f in self.enc.features(frames)]
+        fl = cfg.flops_per_frame()
+        self.flops = fl["total"] * frames
+        self.attn_flops = 4.0 * cfg.tokens * cfg.tokens * cfg.dim * frames  # per layer launch
+        self.launches_per_step = self.enc.launches_per_frame_batch(frames=frames)
+
+    def config(self):
+        c = self.cfg
+        return {"workload": self.workload_name,
+                "frames_per_step": self.frames, "tokens": c.tokens, "dim": c.dim,
+                "heads": c.heads, "mlp": c.mlp, "layers": c.layers, "image": c.side,
+                "weights": "random N(0,0.02), LN gamma=1 beta=0, LayerScale=1",
+                "dtype": "bf16 weights/activations, f16 V and P, f32 residual",
+                "launch": ("one CUDA graph per frame (%d kernels)" if self.launch == "graph" else
+                           "%d direct launches per frame") % self.launches_per_step,
+                "memory": "static plan: %d tensors in one device allocation of %d bytes "
+                          "(peak live %d)" % (len(self.enc.plan.placements()),
+                                              self.enc.arena.bytes(),
+                                              self.enc.plan.peak_live_bytes()),
+                "l2": "flushed before every timed step (256 MiB write)"}
+
+    def step(self, stream):
+        if self.launch == "direct":
+            self.prog.encode_all(stream)
+            return
+        if self.graph is None:
+            self.graph = self.prog.capture(stream)
+        self.graph.launch(stream)
+
+    def step_e2e(self, stream):
+        # Encoder.capture_host: image in, the encoder, each feature out on a
+        # second stream once its LayerNorm has run (one graph per step)
+        if getattr(self, "host_graph", None) is None:
+            self.host_graph = self.enc.capture_host(self.frames, self.host, self.feats_host,
+                                                    stream)
+        self.host_graph.replay()
+
+    def e2e_bytes(self):
+        return (self.host.numel() * 4, sum(h.numel() * 4 for h in self.feats_host))
+
+    def units(self):
+        return self.frames  # frames per step
+
+    def slice_profile(self, stream, frames: int = 5):
+        """Per-kernel durations from the cudaEvent slice timer over `frames`
+        direct (non-graph) encodes: {kind: (launches, total_us, avg_us)}."""
+        import torch
+        from beatlm_b200.runtime import SliceTimer, hold
+        t = SliceTimer(max_slices=len(self.prog))
+        kinds = {}
+        for f in range(frames):
+            h = t.begin_frame(f)
+            hold(stream, 20000)  # the frame's launches queue up behind it
+            self.prog.encode_all(stream, timer=t, frame=h)
+            t.submitted(h)
+            torch.cuda.synchronize()
+            for ft in t.collect_ready():
+                for k, us in ft.compute:
+                    kind = self.prog.label(k).split(".")[-1].split(" ")[0]
+                    n, tot = kinds.get(kind, (0, 0.0))
+                    kinds[kind] = (n + 1, tot + us)
+        t.close()
+        return {k: (n, tot, tot / n) for k, (n, tot) in kinds.items()}
+
+    def cpu_baseline(self, threads: int):
+        """The whole frame through the oracle on every host core, three
+        frames, median: the same function `--impl reference` runs per step.
+        Its feature maps are kept for the parity check."""
+        fn = oracle_frame_fn(self.cfg, self.w, self.img, threads)
+        med, times, self._oracle_feats = _median_time(fn, 3)
+        return {"value": 1.0 / med, "unit": "frames/s", "cores": threads, "kind": "port",
+                "sample": "3 whole frames (patch embedding, %d blocks, %d feature LayerNorms) "
+                          "through oracle.encoder_frame (reference.rs run, f64 accumulation), "
+                          "median of %s s" % (self.cfg.layers, len(self.cfg.out_indices),
+                                              [round(x, 2) for x in times])}
+
+    def parity(self):
+        """The feature maps of the last e2e step (host copies) against the
+        oracle frame of the cpu_baseline leg, same inputs."""
+        want = getattr(self, "_oracle_feats", None)
+        if want is None:
+            return None
+        rels = [_rel(g.numpy(), w) for g, w in zip(self.feats_host, want)]
+        return {"rel_l2": max(r for r, _ in rels), "max_abs": max(m for _, m in rels),
+                "per_feature_rel_l2": [r for r, _ in rels], "bound": 4e-3,
+                "sample": "all 4 feature maps of the frame vs oracle.encoder_frame (bf16 block "
+                          "bound, as in tests/test_block_gpu.py)"}
+
+
+class VitLWorkload(EncoderWorkload):
+    """Config 4: a ViT-L/14-shaped encoder (24 blocks, dim 1024, 16 heads,
+    MLP 4096, 1370 tokens), bf16, random N(0, 0.02) weights. Eight
+    independent input streams shard one per GPU with no collective: each rank
+    runs its own stream, one frame per step."""
+
+    name = "vitl"
+    large = True
+    workload_name = "vit_l14_encoder (config 4)"
+    data = "synthetic: ImageNet-normalised U[0,1] 518x518x3 image per stream, N(0,0.02) weights"
+
+    @staticmethod
+    def block_step(cfg, threads):
+        import numpy as np
+        import oracle
+        from beatlm_b200.model import block_weights_normal
+        rng = np.random.default_rng(5)
+        w = block_weights_normal(rng, cfg.dim, cfg.mlp)
+        x = rng.standard_normal(cfg.tokens * cfg.dim, dtype=np.float32)
+        fn = lambda: oracle.vit_block(x, w, cfg.tokens, cfg.heads, cfg.head_dim, cfg.mlp,
+                                      cfg.eps, threads=threads)
+        return fn, 1.0 / cfg.layers, ("one ViT-L block (T=%d) per step = 1/%d frame, f64 "
+                                      "oracle" % (cfg.tokens, cfg.layers))
+
+    def cpu_baseline(self, threads: int):
+        """One ViT-L block through the oracle on every host core (median of 3)
+        times 24, plus the patch embedding: a whole ViT-L frame of the f64
+        oracle takes about half a minute, so the frame is scaled from its
+        blocks (stated in `sample`)."""
+        import numpy as np
+        import oracle
+        c = self.cfg
+        fn, _, _ = self.block_step(c, threads)
+        med, times, _ = _median_time(fn, 3)
+        pw = np.random.default_rng(6).standard_normal(c.taps * c.dim, dtype=np.float32) * 0.02
+        t_embed, _, _ = _median_time(lambda: oracle.patch_embed(
+            self.img[0], pw, None, c.grid, c.grid, c.patch, c.cin, c.dim, threads=threads), 1)
+        frame_s = c.layers * med + t_embed
+        return {"value": 1.0 / frame_s, "unit": "frames/s", "cores": threads, "kind": "port",
+                "sample": "1 ViT-L block (median of %s s) x %d + patch embedding (%.2f s), f64 "
+                          "oracle, %d threads" % ([round(x, 2) for x in times], c.layers,
+                                                  t_embed, threads)}
+
+    def parity(self):
+        return {"sample": "not in the bench line (a 24-block oracle frame takes about half a "
+                          "minute): tests/test_block_gpu.py::"
+                          "test_vit_l_encoder_matches_the_reference_chain checks it"}
+
+
+class BlockWorkload:
+    """Config 2: one pre-LN ViT-S transformer block (dim 384, 6 heads x 64,
+    MLP 1536 with GELU, 1370 tokens, batch 1) in f16, weights N(0, 0.02), LN
+    gamma 1 / beta 0, LayerScale 1 (BASELINE gives no value), input
+    activations N(0, 1). A step is the block's kernels (LayerNorm, QKV GEMM,
+    attention, out-projection with LayerScale and residual, LayerNorm, fc1 +
+    GELU-erf, fc2 with LayerScale and residual) replayed as one CUDA graph,
+    in place on the f32 residual stream; TFLOP/s of the block's 7.731 GFLOP."""
+
+    name = "block"
+    unit = "TFLOP/s"
+    dtype = "f16 weights and activations, f16 V and P; f32 accumulate and residual"
+    data = "synthetic x ~ N(0,1), N(0,0.02) weights, seeded"
+    workload_name = "vit_s_block_fp16 (config 2)"
+    scaling = "weak"
+
+    def parallelism(self, world):
+        return "replicas x%d (no collective)" % world
+
+    @staticmethod
+    def host_inputs(seed=2):
+        import numpy as np
+        from beatlm_b200.model import ViTConfig, block_weights_normal
+        cfg = ViTConfig.small()
+        rng = np.random.default_rng(seed)
+        w = block_weights_normal(rng, cfg.dim, cfg.mlp)
+        x = rng.standard_normal(cfg.tokens * cfg.dim, dtype=np.float32)
+        return cfg, w, x
+
+    @classmethod
+    def reference_step(cls, threads):
+        import oracle
+        cfg, w, x = cls.host_inputs()
+        fn = lambda: oracle.vit_block(x, w, cfg.tokens, cfg.heads, cfg.head_dim, cfg.mlp,
+                                      cfg.eps, threads=threads)
+        return fn, cfg.flops_per_frame()["linear"] / cfg.layers / 1e12 + \
+            4.0 * cfg.tokens ** 2 * cfg.dim / 1e12, "one ViT-S block per step (oracle, f64)"
+
+    def __init__(self, rank: int, world: int = 1):
+        import torch
+        from beatlm_b200.model import Buffers, DeviceBlock, block_specs
+        from beatlm_b200.runtime import Kernels
+        self.cfg, self.w, self.x = self.host_inputs()
+        cfg = self.cfg
+        self.blk = DeviceBlock(self.w, cfg.dim, cfg.mlp, "f16")
+        self.buf = Buffers(cfg, 1, "f16", features=False)
+        self.host = torch.from_numpy(self.x.reshape(cfg.tokens, cfg.dim)).pin_memory()
+        self.out_host = torch.empty((cfg.tokens, cfg.dim), dtype=torch.float32).pin_memory()
+        self.buf.x.copy_(self.host)
+        self.prog = Kernels(block_specs(self.blk, cfg, self.buf))
+        self.graph = None
+        t, d, m = cfg.tokens, cfg.dim, cfg.mlp
+        self.linear_flops = 2.0 * t * d * (3 * d + d + 2 * m)
+        self.attn_flops = 4.0 * t * t * d
+        self.flops = self.linear_flops + self.attn_flops
+        self.launches_per_step = len(self.prog)
+
+    def config(self):
+        c = self.cfg
+        return {"workload": self.workload_name, "tokens": c.tokens, "dim": c.dim,
+                "heads": c.heads, "mlp": c.mlp, "dtype": "f16",
+                "weights": "random N(0,0.02), LN gamma=1 beta=0, LayerScale=1",
+                "launch": "one CUDA graph per step (%d kernels)" % self.launches_per_step,
+                "gflop_per_step": round(self.flops / 1e9, 3),
+                "l2": "flushed before every timed step (256 MiB write)"}
+
+    def step(self, stream):
+        if self.graph is None:
+            self.graph = self.prog.capture(stream)
+        self.graph.launch(stream)
+
+    def step_e2e(self, stream):
+        self.buf.x.copy_(self.host, non_blocking=True)
+        self.step(stream)
+        self.out_host.copy_(self.buf.x, non_blocking=True)
+
+    def e2e_bytes(self):
+        return self.host.numel() * 4, self.out_host.numel() * 4
+
+    def units(self):
+        return self.flops / 1e12
+
+    def roofline(self, stream, avg_ms):
+        import torch
+        from beatlm_b200.runtime import SliceTimer, hold
+        t = SliceTimer(max_slices=len(self.prog))
+        kinds = {}
+        for f in range(5):
+            self.buf.x.copy_(self.host)
+            h = t.begin_frame(f)
+            hold(stream, 20000)
+            self.prog.encode_all(stream, timer=t, frame=h)
+            t.submitted(h)
+            torch.cuda.synchronize()
+            for ft in t.collect_ready():
+                for k, us in ft.compute:
+                    kind = self.prog.label(k).split(".")[-1]
+                    kinds.setdefault(kind, []).append(us)
+        t.close()
+        att = statistics.mean(kinds["attention"])
+        return {"achieved_tflops": self.attn_flops / (att / 1e6) / 1e12,
+                "kernel": "bl::attn::attention_fwd (the block's attention)",
+                "how": "cudaEvent slice timer around each kernel of 5 direct encodes, queued "
+                       "behind a stream hold",
+                "block_tflops": self.flops / (avg_ms / 1e3) / 1e12,
+                "gemm_tflops": self.linear_flops / (sum(statistics.mean(kinds[k]) for k in
+                                                        ("qkv", "proj", "fc1", "fc2")) / 1e6)
+                / 1e12,
+                "kernels_us": {k: round(statistics.mean(v), 2) for k, v in sorted(kinds.items())}}
+
+    def parity(self):
+        """One block from the seeded input against oracle.vit_block fed the
+        weights as the device holds them and Q/K/V as stored (f16)."""
+        import oracle
+        import torch
+        from beatlm_b200.model import DeviceBlock
+        cfg = self.cfg
+        self.buf.x.copy_(self.host)
+        self.prog.encode_all(None)
+        torch.cuda.synchronize()
+        want = oracle.vit_block(self.x, DeviceBlock.rounded(self.w, "f16"), cfg.tokens, cfg.heads,
+                                64, cfg.mlp, cfg.eps, qkv_round="qk_f16")
+        rel, mx = _rel(self.buf.x.cpu().numpy(), want)
+        return {"rel_l2": rel, "max_abs": mx, "bound": 1e-3,
+                "sample": "the whole block output vs oracle.vit_block"}
+
+    def cpu_baseline(self, threads: int):
+        import oracle
+        cfg = self.cfg
+        fn = lambda: oracle.vit_block(self.x, self.w, cfg.tokens, cfg.heads, 64, cfg.mlp,
+                                      cfg.eps, threads=threads)
+        med, times, _ = _median_time(fn, 3)
+        return {"value": self.flops / med / 1e12, "unit": "TFLOP/s", "cores": threads,
+                "kind": "port", "sample": "the whole block through oracle.vit_block "
+                                          "(reference.rs:520-544), median of %s s"
+                                          % [round(x, 2) for x in times]}
+
+
+class HiresWorkload:
+    """Config 5: the high-resolution ViT-L attention, T = 74*74 + 1 = 5477,
+    16 heads x 64, bf16 Q/K (V f16), Q/K/V ~ N(0,1), batch 1. With g ranks
+    each holds 16/g heads (made locally from the seed) and its attention
+    kernel stores each finished row of its heads into every rank's
+    [T][1024] output (peer stores over NVLink), then waits on the device for
+    the other ranks' arrival flags: the op is one launch per rank and the
+    head outputs cross NVLink while the kernel still computes."""
+
+    name = "hires"
+    unit = "TFLOP/s"
+    dtype = "bf16 Q/K, f16 V and P; f32 scores, softmax and accumulator; f16 output"
+    data = "synthetic Q/K/V ~ N(0,1), seeded, each rank makes its own heads"
+    workload_name = "hires_vit_l_attention_T5477 (config 5)"
+    scaling = "strong"
+    T, H = 5477, 16
+
+    def parallelism(self, world):
+        return ("heads/%d per GPU, outputs stored into every GPU by the attention kernel "
+                "(peer memory over NVLink)" % world if world > 1 else "1 GPU, all heads")
+
+    @classmethod
+    def _qkv(cls, h0, h1):
+        import numpy as np
+        rng = np.random.default_rng(4321)
+        full = rng.standard_normal((1, cls.T, 3, cls.H, 64), dtype=np.float32)
+        return np.ascontiguousarray(full[:, :, :, h0:h1])
+
+    @classmethod
+    def reference_step(cls, threads):
+        import oracle
+        t, h = cls.T, cls.H
+        qkv = cls._ref_input()
+        rows = 8
+        t0 = time.perf_counter()
+        oracle.attention(qkv, t, h, 64, rows=(0, rows), threads=threads)
+        per_row = (time.perf_counter() - t0) / rows
+        rows = int(max(8, min(t, 2.0 / max(per_row, 1e-9))))
+        fn = lambda: oracle.attention(qkv, t, h, 64, rows=(0, rows), threads=threads)
+        return fn, 4.0 * rows * t * h * 64 / 1e12, (
+            "%d of %d query rows x %d heads per step (oracle/oracle.c, f64)" % (rows, t, h))
+
+    @classmethod
+    def _ref_input(cls):
+        """All heads' Q/K/V rounded as the device holds them (bf16 Q/K, f16 V)."""
+        import oracle
+        q = cls._qkv(0, cls.H)[0]
+        q[:, :2] = oracle.round_bf16(q[:, :2])
+        q[:, 2:] = oracle.round_f16(q[:, 2:])
+        return q.reshape(cls.T, -1)
+
+    def __init__(self, rank: int, world: int = 1):
+        import torch
+        import beatlm_b200 as bl
+        from beatlm_b200.parallel import HeadParallelAttention
+        self.world, self.rank = world, rank
+        self.op = HeadParallelAttention(self.T, self.H, rank, world, out_dtype="f16")
+        qkv = self._qkv(self.op.h0, self.op.h1)
+        self.dev = bl.pack_qkv(qkv, "bf16")
+        self.host = self.dev.cpu().pin_memory()
+        self.out_host = torch.empty(self.op.out.shape, dtype=self.op.out.dtype).pin_memory()
+        self.launches_per_step = 1
+
+    def config(self):
+        return {"workload": self.workload_name, "batch": 1, "tokens": self.T, "heads": self.H,
+                "head_dim": 64, "heads_per_gpu": self.op.local_heads,
+                "qkv_dtype": "bf16 Q/K, f16 V", "out_dtype": "f16",
+                "exchange": self.op.exchange_name(),
+                "l2": "flushed before every timed step (256 MiB write)"}
+
+    def step(self, stream):
+        self.op(self.dev, stream=stream)
+
+    def step_e2e(self, stream):
+        self.dev.copy_(self.host, non_blocking=True)
+        self.step(stream)
+        self.out_host.copy_(self.op.out, non_blocking=True)
+
+    def e2e_bytes(self):
+        return self.host.numel() * 2, self.out_host.numel() * 2
+
+    def units(self):
+        return self.op.flops() / self.world / 1e12  # this rank's share, TFLOP per step
+
+    def roofline(self, stream, avg_ms, reps: int = 10):
+        """This rank's attention alone (local heads, local output, no
+        exchange), CUDA events on its stream; the exchange's share is the
+        step time minus this."""
+        import torch
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+        ms = time_device(lambda s: self.op.compute_local(self.dev, stream=s), reps, 3, stream,
+                         flush)
+        avg = sum(ms) / len(ms)
+        return {"achieved_tflops": self.op.flops() / self.world / (avg / 1e3) / 1e12,
+                "kernel": "bl::attn::attention_fwd (%d heads of %d on this GPU)"
+                          % (self.op.local_heads, self.H),
+                "how": "CUDA events around %d attention-only launches (no exchange) after the "
+                       "timed region, L2 flushed between them" % reps,
+                # one capture of the 16-head launch; a rank with fewer heads
+                # reads that share of the Q/K/V
+                "traffic": (lambda b: None if b is None else
+                            int(b * self.op.local_heads / self.H))(
+                    profiled_traffic("attention_fwd_hires_T5477_H16.md")),
+                "attention_ms": round(avg, 5),
+                "step_minus_attention_ms": round(avg_ms - avg, 5),
+                **self.nccl_baseline(stream)}
+
+    def nccl_baseline(self, stream, reps: int = 10):
+        """The same op with the plain collective form of the exchange (one
+        attention launch into this rank's slab, then an NCCL all-gather),
+        timed the same way: the baseline the fused exchange replaces. Every
+        rank runs it (it holds a collective)."""
+        if self.world == 1:
+            return {}
+        import torch
+        import torch.distributed as dist
+        from beatlm_b200.parallel import HeadParallelAttention
+        op = HeadParallelAttention(self.T, self.H, self.rank, self.world, out_dtype="f16",
+                                   exchange="nccl")
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+        ms = time_device(lambda s: op(self.dev, stream=s), reps, 3, stream, flush)
+        t = torch.tensor([sum(ms) / len(ms)], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        avg = float(t[0])
+        return {"nccl_allgather_form": {
+            "tflops": round(op.flops() / (avg / 1e3) / 1e12, 2), "ms_per_step": round(avg, 5),
+            "how": "attention into this rank's slab + NCCL all_gather_into_tensor, max over "
+                   "ranks of %d event-timed steps" % reps}}
+
+    def parity(self):
+        """64 query rows of the assembled [T][1024] output (all 16 heads, so
+        every rank's slab) on this rank, from the last e2e step's host copy,
+        against the oracle fed the same 16-bit Q/K/V."""
+        import numpy as np
+        import oracle
+        qkv = self._ref_input()
+        got = self.out_host.float().numpy().reshape(self.T, self.H * 64)
+        pairs = []
+        for r0 in (0, self.T // 2, self.T - 16, 1000):
+            want = oracle.attention(qkv, self.T, self.H, 64, rows=(r0, r0 + 16))
+            pairs.append((got[r0:r0 + 16].ravel(), want))
+        rel, mx = _rel(np.concatenate([g for g, _ in pairs]), np.concatenate([w for _, w in pairs]))
+        return {"rel_l2": rel, "max_abs": mx, "bound": 1e-3,
+                "sample": "64 query rows (0-15, 1000-1015, 2738-2753, 5461-5476) x all 16 heads "
+                          "of the assembled output on rank 0, vs oracle.attention"}
+
+    def cpu_baseline(self, threads: int, budget_s: float = 8.0):
+        return oracle_attention_rate(self._ref_input(), self.T, self.H, threads, budget_s)
 
 
 class DepthWorkload:
@@ -208,7 +804,7 @@ class DepthWorkload:
     def reference_step(cls, threads):
         return EncoderWorkload.reference_step(threads)
 
-    def __init__(self, rank: int):
+    def __init__(self, rank: int, world: int = 1):
         import torch
         from beatlm_b200.model import Decoder, DecoderConfig, decoder_weights_random
         self.enc_wl = EncoderWorkload(rank)
@@ -250,13 +846,16 @@ class DepthWorkload:
     def roofline(self, stream, avg_ms):
         return self.enc_wl.roofline(stream, avg_ms)
 
-    def cpu_baseline(self, threads: int, budget_s: float = 15.0):
-        """The encoder's CPU rate (its own bounded sample) and one run of the
-        DPT head through the oracle at 518 px, combined per frame."""
+    def parity(self):
+        return None
+
+    def cpu_baseline(self, threads: int):
+        """The encoder's CPU frame and one run of the DPT head through the
+        oracle at 518 px, combined per frame."""
         import numpy as np
         import oracle
         from beatlm_b200.model import DecoderConfig, decoder_weights_random
-        enc = self.enc_wl.cpu_baseline(threads, budget_s)
+        enc = self.enc_wl.cpu_baseline(threads)
         cfg, d = self.enc_wl.cfg, DecoderConfig()
         w = decoder_weights_random(cfg, d, seed=1)
         rng = np.random.default_rng(3)
@@ -308,7 +907,7 @@ class DecoderWorkload:
         return fn, 2 * 2.0 * side * side * c * 9 * c / 1e12, (
             "one residual unit on a 37 x 37 x 64 map (oracle/oracle.c, f64)")
 
-    def __init__(self, rank: int):
+    def __init__(self, rank: int, world: int = 1):
         import ctypes
         import numpy as np
         import torch
@@ -363,321 +962,22 @@ class DecoderWorkload:
     def units(self):
         return self.flops / 1e12
 
-    def cpu_baseline(self, threads: int, budget_s: float = 15.0):
+    def parity(self):
+        return None
+
+    def cpu_baseline(self, threads: int):
         fn, tflop, sample = self.reference_step(threads)
-        t0 = time.perf_counter()
-        n = 0
-        while time.perf_counter() - t0 < budget_s or n == 0:
-            fn()
-            n += 1
-        dt = time.perf_counter() - t0
-        return {"value": tflop * n / dt, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-                "sample": "%s, %d repeats" % (sample, n)}
+        med, _, _ = _median_time(fn, 3)
+        return {"value": tflop / med, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                "sample": "%s, median of 3" % sample}
 
 
-def oracle_attention_rate(qkv, t, h, threads, budget_s):
-    """The reference's CPU path for one attention op (oracle/, a C restatement
-    of reference.rs:437-494, f64 accumulation) timed on a bounded sample of
-    query rows of every head, in TFLOP/s."""
-    import oracle
-    rows = 16
-    t0 = time.perf_counter()
-    oracle.attention(qkv, t, h, 64, rows=(0, rows), threads=threads)
-    dt = time.perf_counter() - t0
-    rows = int(min(t, max(rows, rows * budget_s / max(dt, 1e-6) / 4)))
-    t0 = time.perf_counter()
-    n = 0
-    while time.perf_counter() - t0 < budget_s / 2 or n == 0:
-        oracle.attention(qkv, t, h, 64, rows=(0, rows), threads=threads)
-        n += 1
-    dt = time.perf_counter() - t0
-    flops = 4.0 * rows * t * h * 64 * n
-    return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-            "sample": "%d of %d query rows x %d heads, %d repeats (f64 accumulation, "
-                      "oracle/oracle.c)" % (rows, t, h, n)}
-
-
-class EncoderWorkload:
-    """Config 3: the Depth-Anything-V2-Small ViT-S/14 encoder at 518 px, 12
-    blocks, bf16, random N(0, 0.02) weights (LayerNorm gamma 1 / beta 0,
-    LayerScale 1), one frame per forward (batch 1), input U[0,1] normalised by
-    the ImageNet mean/std. A step is one frame through a captured CUDA graph of
-    the whole encoder (patch embedding, 12 blocks of 5 fused kernels, the four
-    feature LayerNorms)."""
-
-    name = "encoder"
-    unit = "frames/s"
-    dtype = "bf16 (weights, activations, Q/K); f16 V and P; f32 accumulate and residual"
-    data = "synthetic: ImageNet-normalised U[0,1] 518x518x3 image, N(0,0.02) weights, seeded"
-    workload_name = "da_v2_small_encoder_518 (config 3)"
-
-    def roofline(self, stream, avg_ms):
-        prof = self.slice_profile(stream)
-        n, tot, avg_us = prof["attention"]
-        steps = n / self.cfg.layers
-        return {"achieved_tflops": self.attn_flops / (avg_us / 1e6) / 1e12,
-                "kernel": "bl::attn::attention_fwd (%d launches per frame)" % self.cfg.layers,
-                "how": "cudaEvent slice timer (bl_timer) around every kernel of 5 direct "
-                       "(non-graph) encodes after the timed region, each queued behind a "
-                       "20 ms stream hold so the kernels run back to back",
-                "traffic": (None if self.large else
-                            profiled_traffic("attention_fwd_encoder_vit_s_T1370_H6.md")),
-                "kernels": {k: round(v[1] / steps, 2) for k, v in sorted(prof.items())}}
-
-    large = False
-
-    @classmethod
-    def reference_step(cls, threads):
-        """One encoder block of the oracle per step (1/layers of a frame; the
-        patch embedding, under 1 % of a frame's arithmetic, is left out)."""
-        import numpy as np
-        import oracle
-        from beatlm_b200.model import ViTConfig, block_weights_normal
-        c = ViTConfig.large() if cls.large else ViTConfig.small()
-        rng = np.random.default_rng(5)
-        w = block_weights_normal(rng, c.dim, c.mlp)
-        x = rng.standard_normal(c.tokens * c.dim, dtype=np.float32)
-        fn = lambda: oracle.vit_block(x, w, c.tokens, c.heads, c.head_dim, c.mlp, c.eps,
-                                      threads=threads)
-        return fn, 1.0 / c.layers, ("one %s block (T=%d) per step = 1/%d frame, f64 oracle, "
-                                    "patch embedding excluded"
-                                    % ("ViT-L" if cls.large else "ViT-S", c.tokens, c.layers))
-
-    scaling = "weak"
-
-    def parallelism(self, world):
-        return ("%d independent streams, one per GPU, no collective" % world if world > 1
-                else "1 stream")
-
-    def __init__(self, rank: int, frames: int = 1):
-        import numpy as np
-        import torch
-        from beatlm_b200.model import Encoder, ViTConfig, block_weights_normal
-        self.cfg = ViTConfig.large() if self.large else ViTConfig.small()
-        cfg = self.cfg
-        rng = np.random.default_rng(99 + rank)
-        n = lambda *s: rng.standard_normal(int(np.prod(s)), dtype=np.float32) * 0.02
-        w = {"blocks": [block_weights_normal(rng, cfg.dim, cfg.mlp) for _ in range(cfg.layers)],
-             "patch_w": n(cfg.patch, cfg.patch, cfg.cin, cfg.dim), "patch_b": n(cfg.dim),
-             "cls": n(cfg.dim), "pos": n(cfg.tokens, cfg.dim),
-             "norm_g": np.ones(cfg.dim, np.float32), "norm_b": np.zeros(cfg.dim, np.float32)}
-        self.frames = frames
-        self.enc = Encoder(cfg, w, "bf16", planned_frames=frames)
-        mean = np.array([0.485, 0.456, 0.406], np.float32)
-        std = np.array([0.229, 0.224, 0.225], np.float32)
-        img = ((rng.random((frames, cfg.side, cfg.side, cfg.cin), dtype=np.float32) - mean)
-               / std).astype(np.float32)
-        self.host = torch.from_numpy(img).pin_memory()
-        self.buf = self.enc.buffers(frames)
-        self.buf.image.copy_(self.host)
-        self.prog = self.enc.program(frames)
-        self.graph = None
-        self.feats_host = [torch.empty(f.shape, dtype=f.dtype).pin_memory()
-                           for f in self.enc.features(frames)]
-        fl = cfg.flops_per_frame()
-        self.flops = fl["total"] * frames
-        self.attn_flops = 4.0 * cfg.tokens * cfg.tokens * cfg.dim * frames  # per layer launch
-        self.launches_per_step = self.enc.launches_per_frame_batch(frames=frames)
-
-    def config(self):
-        c = self.cfg
-        return {"workload": ("vit_l14_encoder (config 4)" if c.dim == 1024 else
-                             "da_v2_small_encoder_518 (config 3)"),
-                "frames_per_step": self.frames, "tokens": c.tokens, "dim": c.dim,
-                "heads": c.heads, "mlp": c.mlp, "layers": c.layers, "image": c.side,
-                "weights": "random N(0,0.02), LN gamma=1 beta=0, LayerScale=1",
-                "dtype": "bf16 weights/activations, f16 V and P, f32 residual",
-                "launch": ("one CUDA graph per frame (%d kernels)" if self.launch == "graph" else
-                           "%d direct launches per frame") % self.launches_per_step,
-                "memory": "static plan: %d tensors in one device allocation of %d bytes "
-                          "(peak live %d)" % (len(self.enc.plan.placements()),
-                                              self.enc.arena.bytes(),
-                                              self.enc.plan.peak_live_bytes()),
-                "l2": "flushed before every timed step (256 MiB write)"}
-
-    launch = "graph"  # or "direct": every kernel launched from the host each step
-
-    def step(self, stream):
-        if self.launch == "direct":
-            self.prog.encode_all(stream)
-            return
-        if self.graph is None:
-            self.graph = self.prog.capture(stream)
-        self.graph.launch(stream)
-
-    def step_e2e(self, stream):
-        # Encoder.capture_host: image in, the encoder, each feature out on a
-        # second stream once its LayerNorm has run (one graph per step)
-        if getattr(self, "host_graph", None) is None:
-            self.host_graph = self.enc.capture_host(self.frames, self.host, self.feats_host,
-                                                    stream)
-        self.host_graph.replay()
-
-    def e2e_bytes(self):
-        return (self.host.numel() * 4, sum(h.numel() * 4 for h in self.feats_host))
-
-    def units(self):
-        return self.frames  # frames per step
-
-    def slice_profile(self, stream, frames: int = 5):
-        """Per-kernel durations from the cudaEvent slice timer over `frames`
-        direct (non-graph) encodes: {kind: (launches, total_us, avg_us)}."""
-        import torch
-        from beatlm_b200.runtime import SliceTimer, hold
-        t = SliceTimer(max_slices=len(self.prog))
-        kinds = {}
-        for f in range(frames):
-            h = t.begin_frame(f)
-            hold(stream, 20000)  # the frame's launches queue up behind it
-            self.prog.encode_all(stream, timer=t, frame=h)
-            t.submitted(h)
-            torch.cuda.synchronize()
-            for ft in t.collect_ready():
-                for k, us in ft.compute:
-                    kind = self.prog.label(k).split(".")[-1].split(" ")[0]
-                    n, tot = kinds.get(kind, (0, 0.0))
-                    kinds[kind] = (n + 1, tot + us)
-        t.close()
-        return {k: (n, tot, tot / n) for k, (n, tot) in kinds.items()}
-
-    def cpu_baseline(self, threads: int, budget_s: float = 15.0):
-        """One encoder block through the oracle (reference.rs:520-544) on all
-        host cores, scaled to a frame: 12 blocks plus the patch embedding."""
-        import oracle
-        from beatlm_b200.model import block_weights_normal
-        import numpy as np
-        c = self.cfg
-        rng = np.random.default_rng(5)
-        w = block_weights_normal(rng, c.dim, c.mlp)
-        x = rng.standard_normal(c.tokens * c.dim, dtype=np.float32)
-        t0 = time.perf_counter()
-        oracle.vit_block(x, w, c.tokens, c.heads, c.head_dim, c.mlp, c.eps, threads=threads)
-        t_block = time.perf_counter() - t0
-        img = self.host[0].numpy().ravel()
-        pw = rng.standard_normal(c.taps * c.dim, dtype=np.float32) * 0.02
-        t0 = time.perf_counter()
-        oracle.patch_embed(img, pw, None, c.grid, c.grid, c.patch, c.cin, c.dim, threads=threads)
-        t_embed = time.perf_counter() - t0
-        frame_s = c.layers * t_block + t_embed
-        return {"value": 1.0 / frame_s, "unit": "frames/s", "cores": threads, "kind": "port",
-                "sample": "1 block (%.2f s) x %d + patch embedding (%.2f s), f64 oracle, "
-                          "%d threads" % (t_block, c.layers, t_embed, threads)}
-
-
-class VitLWorkload(EncoderWorkload):
-    """Config 4: a ViT-L/14-shaped encoder (24 blocks, dim 1024, 16 heads,
-    MLP 4096, 1370 tokens), bf16, random N(0, 0.02) weights. Eight
-    independent input streams shard one per GPU with no collective: each rank
-    runs its own stream, one frame per step."""
-
-    name = "vitl"
-    large = True
-    workload_name = "vit_l14_encoder (config 4)"
-    data = "synthetic: ImageNet-normalised U[0,1] 518x518x3 image per stream, N(0,0.02) weights"
-
-
-class HiresWorkload:
-    """Config 5: the high-resolution ViT-L attention, T = 74*74 + 1 = 5477,
-    16 heads x 64, bf16 Q/K (V f16), Q/K/V ~ N(0,1), batch 1. With g ranks
-    each holds 16/g heads (made locally from the seed), computes their
-    output slab and an NCCL all-gather assembles [T][1024] on every rank. A
-    step is the whole op: the attention launch, the all-gather and the
-    permute to heads side by side."""
-
-    name = "hires"
-    unit = "TFLOP/s"
-    dtype = "bf16 Q/K, f16 V and P; f32 scores, softmax and accumulator; f16 output"
-    data = "synthetic Q/K/V ~ N(0,1), seeded, each rank makes its own heads"
-    workload_name = "hires_vit_l_attention_T5477 (config 5)"
-    scaling = "strong"
-    T, H = 5477, 16
-
-    def parallelism(self, world):
-        return ("heads/%d per GPU + NCCL all-gather of head outputs" % world if world > 1
-                else "1 GPU, all heads")
-
-    @classmethod
-    def _qkv(cls, h0, h1):
-        import numpy as np
-        rng = np.random.default_rng(4321)
-        full = rng.standard_normal((1, cls.T, 3, cls.H, 64), dtype=np.float32)
-        return np.ascontiguousarray(full[:, :, :, h0:h1])
-
-    @classmethod
-    def reference_step(cls, threads):
-        import oracle
-        t, h = cls.T, cls.H
-        qkv = oracle.round_f16(cls._qkv(0, h)[0].reshape(t, -1))
-        rows = 8
-        t0 = time.perf_counter()
-        oracle.attention(qkv, t, h, 64, rows=(0, rows), threads=threads)
-        per_row = (time.perf_counter() - t0) / rows
-        rows = int(max(8, min(t, 2.0 / max(per_row, 1e-9))))
-        fn = lambda: oracle.attention(qkv, t, h, 64, rows=(0, rows), threads=threads)
-        return fn, 4.0 * rows * t * h * 64 / 1e12, (
-            "%d of %d query rows x %d heads per step (oracle/oracle.c, f64)" % (rows, t, h))
-
-    def __init__(self, rank: int, world: int = 1):
-        import torch
-        import beatlm_b200 as bl
-        from beatlm_b200.parallel import HeadParallelAttention
-        self.world = world
-        self.op = HeadParallelAttention(self.T, self.H, rank, world, out_dtype="f16")
-        qkv = self._qkv(self.op.h0, self.op.h1)
-        self.dev = bl.pack_qkv(qkv, "bf16")
-        self.host = self.dev.cpu().pin_memory()
-        self.out_host = torch.empty(self.op.out.shape, dtype=self.op.out.dtype).pin_memory()
-        self.launches_per_step = 1
-
-    def config(self):
-        return {"workload": self.workload_name, "batch": 1, "tokens": self.T, "heads": self.H,
-                "head_dim": 64, "heads_per_gpu": self.op.local_heads,
-                "qkv_dtype": "bf16 Q/K, f16 V", "out_dtype": "f16",
-                "collective": "all_gather_into_tensor (NCCL) + permute" if self.world > 1
-                              else "none",
-                "l2": "flushed before every timed step (256 MiB write)"}
-
-    def step(self, stream):
-        self.op(self.dev, stream=stream)
-
-    def step_e2e(self, stream):
-        self.dev.copy_(self.host, non_blocking=True)
-        self.step(stream)
-        self.out_host.copy_(self.op.out, non_blocking=True)
-
-    def e2e_bytes(self):
-        return self.host.numel() * 2, self.out_host.numel() * 2
-
-    def units(self):
-        return self.op.flops() / self.world / 1e12  # this rank's share, TFLOP per step
-
-    def roofline(self, stream, avg_ms, reps: int = 10):
-        """This rank's attention launch alone, CUDA events on its stream."""
-        import torch
-        flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
-        ms = time_device(lambda s: self.op.compute(self.dev, stream=s), reps, 3, stream, flush)
-        avg = sum(ms) / len(ms)
-        return {"achieved_tflops": self.op.flops() / self.world / (avg / 1e3) / 1e12,
-                "kernel": "bl::attn::attention_fwd (%d heads of %d on this GPU)"
-                          % (self.op.local_heads, self.H),
-                "how": "CUDA events around %d attention-only launches after the timed region, "
-                       "L2 flushed between them" % reps,
-                # one capture of the 16-head launch; a rank with fewer heads
-                # reads that share of the Q/K/V
-                "traffic": (lambda b: None if b is None else
-                            int(b * self.op.local_heads / self.H))(
-                    profiled_traffic("attention_fwd_hires_T5477_H16.md")),
-                "attention_ms": round(avg, 5)}
-
-    def cpu_baseline(self, threads: int, budget_s: float = 15.0):
-        import oracle
-        qkv = oracle.round_f16(self._qkv(0, self.H)[0].reshape(self.T, -1))
-        return oracle_attention_rate(qkv, self.T, self.H, threads, budget_s)
-
-
-WORKLOADS = {"attention": AttentionWorkload, "encoder": EncoderWorkload,
+WORKLOADS = {"attention": AttentionWorkload, "block": BlockWorkload, "encoder": EncoderWorkload,
              "vitl": VitLWorkload, "hires": HiresWorkload, "decoder": DecoderWorkload,
              "depth": DepthWorkload}
+# the other configs carried in the default line, by GPU count
+EXTRAS_ONE = ("attention", "block", "vitl", "hires")
+EXTRAS_MANY = ("vitl", "hires")
 
 
 # ------------------------------------------------------------------ timing
@@ -701,6 +1001,70 @@ def time_device(fn, steps, warmup, stream, flush):
     return [s.elapsed_time(e) for s, e in zip(starts, ends)]
 
 
+def measure(wl, steps, warmup, stream, flush, world, rank, local, cpu_threads):
+    """Times one workload (device-resident and end to end), then its roofline,
+    parity and (one GPU, rank 0) CPU baseline. Every rank runs the same
+    collective steps in the same order. Returns the line's fields."""
+    import torch
+    import torch.distributed as dist
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    barrier()
+    with Clocks(local) as clk:
+        times = time_device(wl.step, steps, warmup, stream, flush)
+    barrier()
+    total_ms = sum(times)
+    barrier()
+    e2e_times = time_device(wl.step_e2e, steps, warmup, stream, flush)
+    barrier()
+    e2e_ms = sum(e2e_times)
+    if world > 1:
+        t = torch.tensor([total_ms, e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms, e2e_ms = float(t[0]), float(t[1])
+    value = wl.units() * steps * world / (total_ms / 1e3)
+    e2e_value = wl.units() * steps * world / (e2e_ms / 1e3)
+    extra = wl.roofline(stream, total_ms / steps)
+    barrier()
+    if rank != 0:
+        return None
+    pk = peaks()
+    achieved = extra.pop("achieved_tflops")
+    kernels = extra.pop("kernels", None)
+    kernel, how, traffic = extra.pop("kernel"), extra.pop("how"), extra.pop("traffic", None)
+    out = {
+        "metric": METRIC, "value": round(value, 3), "unit": wl.unit, "n_gpus": world,
+        "steps": steps, "warmup": warmup, "ms_per_step": round(total_ms / steps, 5),
+        "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None,
+        "dtype": wl.dtype, "data": wl.data,
+        "config": dict(wl.config(), parallelism=wl.parallelism(world)),
+        "e2e": {"value": round(e2e_value, 3), "unit": wl.unit,
+                "h2d_bytes_per_step": wl.e2e_bytes()[0],
+                "d2h_bytes_per_step": wl.e2e_bytes()[1]},
+        "gpu_launches": wl.launches_per_step * steps,
+        "roofline": dict({"bound": "tensor", "achieved": round(achieved, 2),
+                          "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                          "frac": round(achieved / pk["bf16_tflops"], 4),
+                          "peak_source": pk["source"] + " burst bf16 (MEASURED_PEAKS.json)",
+                          "traffic": traffic, "kernel": kernel, "how": how},
+                         **{k: (round(v, 3) if isinstance(v, float) else v)
+                            for k, v in extra.items()}),
+        "clocks": clk.summary,
+    }
+    if kernels:
+        out["kernels_us_per_step"] = kernels
+    if world == 1 and cpu_threads:
+        out["cpu_baseline"] = wl.cpu_baseline(threads=cpu_threads)
+    par = wl.parity()
+    if par is not None:
+        out["parity"] = par
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -709,7 +1073,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="encoder", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true",
-                    help="skip the cpu_baseline leg (profiling runs)")
+                    help="skip the cpu_baseline legs (profiling runs)")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="measure the chosen workload only (no other configs in the line)")
     ap.add_argument("--launch", default="graph", choices=["graph", "direct"],
                     help="encoder workloads: replay one CUDA graph per step (default) or "
                          "launch every kernel from the host")
@@ -730,89 +1096,62 @@ def main():
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
-    cls = WORKLOADS[args.workload]
-    wl = cls(rank, world=world) if cls is HiresWorkload else cls(rank)
-    if isinstance(wl, EncoderWorkload):
-        wl.launch = args.launch
     stream = torch.cuda.Stream()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    threads = 0 if args.no_cpu_baseline else (os.cpu_count() or 1)
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
+    wl = WORKLOADS[args.workload](rank, world=world)
+    if isinstance(wl, EncoderWorkload):
+        wl.launch = args.launch
+    line = measure(wl, args.steps, args.warmup, stream, flush, world, rank, local, threads)
+    del wl
+    torch.cuda.empty_cache()
 
-    # device-resident timing
-    barrier()
-    with Clocks(local) as clk:
-        times = time_device(wl.step, args.steps, args.warmup, stream, flush)
-    barrier()
-    total_ms = sum(times)
-    # e2e through the public call with host buffers
-    barrier()
-    e2e_times = time_device(wl.step_e2e, args.steps, args.warmup, stream, flush)
-    barrier()
-    e2e_ms = sum(e2e_times)
-    if world > 1:
-        t = torch.tensor([total_ms, e2e_ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms, e2e_ms = float(t[0]), float(t[1])
-    value = wl.units() * args.steps * world / (total_ms / 1e3)
-    e2e_value = wl.units() * args.steps * world / (e2e_ms / 1e3)
-    extra = wl.roofline(stream, total_ms / args.steps)
-    barrier()
-
+    if args.workload == "encoder" and not args.no_extra:
+        extra_steps = max(3, min(args.steps, 10))
+        configs = {}
+        for name in (EXTRAS_MANY if world > 1 else EXTRAS_ONE):
+            sub = WORKLOADS[name](rank, world=world)
+            r = measure(sub, extra_steps, 3, stream, flush, world, rank, local, threads)
+            if rank == 0:
+                r.pop("metric", None)
+                configs[name] = r
+            sub = None
+            torch.cuda.synchronize()
+            torch.cuda.empty_cache()
+        if rank == 0:
+            line["configs"] = configs
+            line["gpu_launches"] += sum(c["gpu_launches"] for c in configs.values())
     if rank == 0:
-        pk = peaks()
-        avg_ms = total_ms / args.steps
-        achieved, kernels = extra["achieved_tflops"], extra.get("kernels")
-        line = {
-            "metric": METRIC, "value": round(value, 3), "unit": wl.unit, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(avg_ms, 5),
-            "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None,
-            "dtype": wl.dtype, "data": wl.data,
-            "config": dict(wl.config(), parallelism=wl.parallelism(world)),
-            "e2e": {"value": round(e2e_value, 3), "unit": wl.unit,
-                    "h2d_bytes_per_step": wl.e2e_bytes()[0],
-                    "d2h_bytes_per_step": wl.e2e_bytes()[1]},
-            "gpu_launches": wl.launches_per_step * args.steps,
-            "roofline": {"bound": "tensor", "achieved": round(achieved, 2),
-                         "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
-                         "frac": round(achieved / pk["bf16_tflops"], 4),
-                         "peak_source": pk["source"] + " burst bf16 (MEASURED_PEAKS.json)",
-                         "traffic": extra.get("traffic"), "kernel": extra["kernel"],
-                         "how": extra["how"]},
-            "clocks": clk.summary,
-        }
-        if kernels:
-            line["kernels_us_per_step"] = kernels
-        if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = wl.cpu_baseline(threads=os.cpu_count() or 1)
         print(json.dumps(line), flush=True)
     if world > 1:
+        dist.barrier()
         dist.destroy_process_group()
 
 
 def run_reference(args, world, rank):
     """The reference's CPU implementation of the path: the oracle port (the
     Rust reference has no toolchain here), all host threads, rank 0 only; each
-    step is a bounded sample of the workload (WORKLOADS[...].reference_step)."""
+    step is the workload's reference_step (the encoder: one whole frame), run
+    `warmup` times untimed and `steps` times timed."""
     if rank != 0:
         return
     wl = WORKLOADS[args.workload]
     threads = os.cpu_count() or 1
     step, units_per_step, sample = wl.reference_step(threads)
-    step()
+    for _ in range(args.warmup):
+        step()
     t0 = time.perf_counter()
     for _ in range(args.steps):
         step()
     dt = time.perf_counter() - t0
     value = units_per_step * args.steps / dt
     line = {"metric": METRIC, "impl": "reference", "value": value, "unit": wl.unit,
-            "n_gpus": world, "steps": args.steps, "warmup": 1,
-            "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": wl.scaling,
-            "vs_baseline": None, "dtype": "f64 accumulate, f32 storage",
-            "data": "synthetic, seeded", "config": {"workload": wl.workload_name},
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
+            "scaling": wl.scaling, "vs_baseline": None, "dtype": "f64 accumulate, f32 storage",
+            "data": "synthetic, seeded (the same inputs as the GPU arm's cpu_baseline leg)",
+            "config": {"workload": wl.workload_name},
             "cpu_baseline": {"value": value, "unit": wl.unit, "cores": threads, "kind": "port",
                              "sample": sample},
             "e2e": {"value": value, "unit": wl.unit, "h2d_bytes_per_step": 0,

@@ -54,6 +54,16 @@ typedef struct bl_status_t {
  * reset != 0, clears it. */
 int bl_status(bl_status_t* out, int reset);
 
+/* How long a kernel's wait may spin before it gives up, records a timeout
+ * code and unwinds: `cycles` SM clock cycles on the current device (0 = the
+ * default of 1965e6, about 1 s; at most 60 s worth). It applies to launches
+ * made after the call; bl_status resets leave it alone. No counterpart in
+ * the reference, whose queue has no device-side waits: it lets a host (or a
+ * test) bound a stalled exchange, such as a peer that never signals, tightly. */
+int bl_set_wait_limit(uint64_t cycles);
+/* The current device's wait limit as set (0 = the default). */
+uint64_t bl_wait_limit(void);
+
 /* ------------------------------------------------------------------ types */
 
 typedef enum bl_dtype { BL_F32 = 0, BL_F16 = 1, BL_BF16 = 2 } bl_dtype;
@@ -146,11 +156,74 @@ uint64_t bl_attention_workspace_bytes(const bl_attention_args* args);
  * the split count that fits the 16 MiB; an explicit count whose scratch would
  * exceed 16 MiB is rejected with BL_ERR_CAPACITY. The first call on each
  * device looks up the array's device address (once, with that device
- * current), so make that first call before any stream capture. Each call
+ * current), so make that first call before any stream capture. After a
+ * device reset (cudaDeviceReset) the device has a new context and the next
+ * call looks the address up again, so that call too belongs outside a
+ * capture. Each call
  * clears the split counters on `stream` before its launch. All calls share the
  * one array: calls that overlap on the GPU race and must not be issued.
  */
 int bl_attention_noalloc(const bl_attention_args* args, void* stream);
+
+/* ------------------------------------------------- head-parallel exchange */
+
+/*
+ * The long-sequence attention split by heads over the GPUs of one node, with
+ * the exchange of head outputs fused into the attention kernel. The
+ * reference runs on one device (queue order is its only synchronisation,
+ * crates/beatlm-core/src/lib.rs:30-41); this takes the place of its
+ * AttentionScores -> Softmax -> AttentionValues chain for the heads of one
+ * rank plus the all-gather that assembles the [tokens][heads * 64] output
+ * (kernel.rs:157-161) on every rank.
+ *
+ * Each rank owns a peer buffer: a 256-byte header of arrival flags (rank r's
+ * flag is the 32-bit word at byte 4 r; bytes 64-67 count finished CTAs and
+ * are left at zero by every launch) and two output slots of slot_bytes each
+ * (slot s at byte 256 + s * slot_bytes rounded up to 256), in one device
+ * allocation made at create (the only allocation). The ranks exchange
+ * 64-byte CUDA IPC handles of their
+ * buffers by any host channel (bl_peers_handle on each, then bl_peers_open
+ * with all of them in rank order), or a host that maps a rank's buffer
+ * itself (another device of the same process with peer access, or a test)
+ * hands it over with bl_peers_attach: the buffer must then be
+ * bl_peers_buffer_bytes(slot_bytes) bytes, 256-byte aligned and zero-filled
+ * once. Every rank needs every rank's buffer before its first launch.
+ */
+enum { BL_PEER_HANDLE_BYTES = 64, BL_MAX_PEERS = 8 };
+typedef struct bl_peers bl_peers;
+uint64_t bl_peers_buffer_bytes(uint64_t slot_bytes);
+int bl_peers_create(uint32_t rank, uint32_t world, uint64_t slot_bytes, bl_peers** out);
+int bl_peers_handle(const bl_peers* p, void* handle /* BL_PEER_HANDLE_BYTES */);
+int bl_peers_open(bl_peers* p, const void* handles /* world x BL_PEER_HANDLE_BYTES */, size_t n);
+int bl_peers_attach(bl_peers* p, uint32_t rank, void* buffer);
+/* This rank's output slot 0 or 1 (device memory, slot_bytes long). */
+void* bl_peers_slot(const bl_peers* p, uint32_t slot);
+/* The flag value the next bl_attention_peers launch raises (launches count
+ * from 1; a launch uses slot epoch % 2). */
+uint32_t bl_peers_next_epoch(const bl_peers* p);
+/* Unmaps the other ranks' buffers and frees this one's. Every rank's
+ * launches must have completed first (synchronise, then a host barrier). */
+void bl_peers_destroy(bl_peers* p);
+
+/*
+ * bl_attention of this rank's heads whose output rows the kernel stores
+ * into EVERY rank's current output slot (16-bit rows, out_row_stride
+ * elements apart; this rank's head h at column out_col + (h - out_head_base) *
+ * 64), as soon as each row is final, so the exchange crosses NVLink while the
+ * kernel still computes. args->out and args->workspace are ignored; key
+ * splits combine in a thread-block cluster. The launch ends with an arrival
+ * barrier on the device: the last CTA raises this rank's flag in every
+ * rank's header and waits until every rank's flag for this launch has
+ * arrived in its own, so when the launch completes the whole output is in
+ * this rank's slot (*slot_out). The wait is bounded (bl_set_wait_limit); a
+ * rank that never launches makes the others record status 0x60 (peer
+ * timeout) and return with their output incomplete. Every rank must make
+ * the same sequence of calls. A slot is written again two launches later:
+ * read a launch's output on the launching stream before the launch after
+ * next. Enqueues on `stream`; allocates nothing.
+ */
+int bl_attention_peers(const bl_attention_args* args, bl_peers* peers, uint32_t out_col,
+                       uint32_t* slot_out, void* stream);
 
 /* ------------------------------------------------------------------ linear */
 

@@ -256,6 +256,35 @@ def vit_block(x, weights: dict, t, h, d, mlp, eps=1e-6, qkv_round=None, threads=
     return out
 
 
+def encoder_frame(image, w, grid, patch, cin, dim, heads, mlp, eps, out_indices, layers=None,
+                  qkv_round=None, threads=None):
+    """One frame of the DA-V2 ViT encoder graph
+    (crates/beatlm/src/model/depth_anything_v2.rs:435-545) evaluated op by op
+    in program order, as the reference's interpreter ``run``
+    (crates/beatlm-bench/src/reference.rs:552-625) evaluates it: PatchEmbed,
+    PrependToken (class token), Add (position embedding), the blocks
+    (``vit_block``, reference.rs:520-544) and, after each block in
+    ``out_indices``, the final LayerNorm and TokensToMap.
+
+    ``image`` NHWC f32 [grid*patch][grid*patch][cin]; ``w``: ``patch_w``
+    (HWIO), ``patch_b``, ``cls``, ``pos`` [tokens][dim], ``norm_g``/``norm_b``
+    and ``blocks`` (per-block dicts of ``WEIGHT_NAMES``). Returns the feature
+    maps, [grid*grid][dim] f32 each, in ``out_indices`` order."""
+    layers = len(w["blocks"]) if layers is None else layers
+    t = grid * grid + 1
+    x = patch_embed(image, w["patch_w"], w["patch_b"], grid, grid, patch, cin, dim,
+                    threads=threads)
+    x = add(prepend_token(w["cls"], x), w["pos"])
+    feats = []
+    for i in range(layers):
+        x = vit_block(x, w["blocks"][i], t, heads, dim // heads, mlp, eps, qkv_round=qkv_round,
+                      threads=threads)
+        if (i + 1) in out_indices:
+            feats.append(tokens_to_map(layernorm(x, w["norm_g"], w["norm_b"], eps,
+                                                 threads=threads), dim))
+    return feats
+
+
 def round_f16(x):
     x = np.array(x, dtype=np.float32, copy=True)
     lib().orc_round_f16(_p(x), x.size, None)

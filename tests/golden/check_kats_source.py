@@ -39,4 +39,6 @@ def main(root):
 
 
 if __name__ == "__main__":
-    sys.exit(main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference"))
+    if len(sys.argv) != 2:
+        sys.exit("usage: python check_kats_source.py /path/to/beatlm (the reference's root)")
+    sys.exit(main(sys.argv[1]))

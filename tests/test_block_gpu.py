@@ -75,22 +75,16 @@ def imagenet_image(rng, side, frames=1):
 
 
 def oracle_encoder(cfg, w, image, layers, dtype):
-    """The reference's encoder chain (depth_anything_v2.rs:435-545) through the
-    oracle, with the weights rounded as the device holds them."""
+    """The reference's encoder chain (depth_anything_v2.rs:435-545, evaluated
+    as reference.rs:552-625 does) through the oracle, with the image, the
+    patch weights and the block weights rounded as the device holds them."""
     from beatlm_b200.model import DeviceBlock
-    g = cfg.grid
     rnd = oracle.round_bf16 if dtype == "bf16" else oracle.round_f16
-    patches = oracle.patch_embed(rnd(image), rnd(w["patch_w"]), w["patch_b"], g, g, cfg.patch,
-                                 cfg.cin, cfg.dim)
-    x = oracle.add(oracle.prepend_token(w["cls"], patches), w["pos"])
-    feats = []
-    for i in range(layers):
-        x = oracle.vit_block(x, DeviceBlock.rounded(w["blocks"][i], dtype), cfg.tokens,
-                             cfg.heads, cfg.head_dim, cfg.mlp, cfg.eps, qkv_round="qk_" + dtype)
-        if (i + 1) in cfg.out_indices:
-            n = oracle.layernorm(x, w["norm_g"], w["norm_b"], cfg.eps)
-            feats.append(oracle.tokens_to_map(n, cfg.dim))
-    return feats
+    wr = dict(w, patch_w=rnd(w["patch_w"]),
+              blocks=[DeviceBlock.rounded(w["blocks"][i], dtype) for i in range(layers)])
+    return oracle.encoder_frame(rnd(image), wr, cfg.grid, cfg.patch, cfg.cin, cfg.dim, cfg.heads,
+                                cfg.mlp, cfg.eps, cfg.out_indices, layers=layers,
+                                qkv_round="qk_" + dtype)
 
 
 @pytest.mark.parametrize("dtype,fused_ln", [("bf16", False), ("f16", False), ("bf16", True),
@@ -210,3 +204,49 @@ def test_encoder_from_a_checkpoint_file_matches_the_reference(side, tmp_path):
     rel, mx = _rel(feats[0].cpu().numpy().ravel(), want[0])
     print("encoder from a checkpoint at %d px: rel-L2 %.3e max-abs %.3e" % (side, rel, mx))
     assert rel <= REL["bf16"]
+
+
+def test_vit_l_encoder_matches_the_reference_chain():
+    """Config 4 as benched: the whole 24-block ViT-L/14 encoder at 518 px
+    (T=1370, D=1024, 16 heads, MLP 4096), bf16, weights N(0, 0.02) with LN
+    gamma 1 / beta 0 / LayerScale 1, one frame through the planned program
+    (every tensor in one allocation), against the oracle chain on every host
+    core. The four feature maps (after blocks 6, 12, 18 and 24) within the
+    bf16 block bound."""
+    import torch
+    import beatlm_b200 as bl
+    from beatlm_b200.model import Encoder, ViTConfig
+    cfg = ViTConfig.large()
+    w = _encoder_weights(cfg, cfg.layers, seed=44)
+    image = imagenet_image(np.random.default_rng(45), cfg.side, frames=1)
+    enc = Encoder(cfg, w, "bf16", planned_frames=1)
+    feats = enc.forward(torch.from_numpy(image).cuda(), frames=1)
+    torch.cuda.synchronize()
+    assert bl.status(reset=True).code == 0
+    got = [f.cpu().numpy().ravel() for f in feats]
+    want = oracle_encoder(cfg, w, image[0], cfg.layers, "bf16")
+    assert len(got) == len(want) == 4
+    for i, (g, r) in enumerate(zip(got, want)):
+        rel, mx = _rel(g, r)
+        print("ViT-L encoder feature after block %d: rel-L2 %.3e max-abs %.3e"
+              % (cfg.out_indices[i], rel, mx))
+        assert rel <= REL["bf16"]
+
+
+def test_encoder_forward_on_a_side_stream_equals_the_current_stream():
+    """Encoder.forward(stream=s) with s not the current stream: the image
+    copy and every kernel run on s, so the result equals a pass on the
+    current stream bit for bit."""
+    import torch
+    from beatlm_b200.model import Encoder, ViTConfig
+    cfg = ViTConfig.small(layers=2, out_indices=(2,))
+    w = _encoder_weights(cfg, 2, seed=9)
+    enc = Encoder(cfg, w, "bf16")
+    img = torch.from_numpy(imagenet_image(np.random.default_rng(10), cfg.side)).cuda()
+    want = enc.forward(img, frames=1)[0].clone()
+    side = torch.cuda.Stream()
+    enc.buffers(1).x.fill_(float("nan"))
+    torch.cuda.synchronize()
+    got = enc.forward(img, frames=1, stream=side)[0]
+    side.synchronize()
+    assert torch.equal(got, want)

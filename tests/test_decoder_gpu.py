@@ -165,3 +165,21 @@ def test_the_captured_head_replays_the_direct_pass():
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(depth, want2) and not torch.equal(want, want2)
+
+
+def test_the_head_on_a_side_stream_equals_the_current_stream():
+    """Decoder.forward(stream=s) with s not the current stream: every
+    convolution, resampling, temporary and add of the head runs on s, so the
+    depth equals the pass on the current stream bit for bit."""
+    import torch
+    from beatlm_b200.model import Decoder, DecoderConfig, ViTConfig, decoder_weights_random
+    cfg, dcfg = ViTConfig.small(side=266), DecoderConfig()
+    dec = Decoder(cfg, dcfg, decoder_weights_random(cfg, dcfg, seed=8))
+    feats = [torch.from_numpy(_data(80 + i, cfg.grid * cfg.grid * cfg.dim)).cuda()
+             for i in range(4)]
+    want = dec.forward(feats).clone()
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    got = dec.forward(feats, stream=side)
+    side.synchronize()
+    assert torch.equal(got, want)

@@ -1,13 +1,14 @@
 """Host logic of the multi-GPU paths, on CPU: the head partition of config 5
-and the frame sharding of configs 3-4, and the head all-gather run by two
-gloo ranks (world size 2, 127.0.0.1)."""
+and the frame sharding of configs 3-4; with two gloo ranks (world size 2,
+127.0.0.1) the exchange of peer-buffer handles and the NCCL-form head
+all-gather."""
 import os
 import socket
 
 import numpy as np
 import pytest
 
-from beatlm_b200.parallel import gather_heads, head_slab, shard_frames
+from beatlm_b200.parallel import exchange_handles, gather_heads, head_slab, shard_frames
 
 
 @pytest.mark.parametrize("world", [1, 2, 4, 8, 16])
@@ -54,9 +55,10 @@ def _gather_rank(rank, world, port, t, heads, q):
         h0, h1 = head_slab(rank, world, heads)
         stacked = torch.full((world, t, (h1 - h0) * 64), -1.0)
         stacked[rank].copy_(full[:, h0:h1].reshape(t, -1))  # this rank's heads only
-        out = torch.empty((t, heads * 64))
-        gather_heads(stacked, rank, world, out)
-        q.put((rank, bool(torch.equal(out, full.reshape(t, -1)))))
+        view = gather_heads(stacked, rank, world)  # [t][world][w], no copy
+        ok = view.data_ptr() == stacked.data_ptr() and torch.equal(view.reshape(t, -1),
+                                                                    full.reshape(t, -1))
+        q.put((rank, bool(ok)))
     finally:
         dist.destroy_process_group()
 
@@ -80,4 +82,38 @@ def test_head_all_gather_assembles_heads_side_by_side_gloo():
 def test_gather_heads_checks_shapes():
     import torch
     with pytest.raises(ValueError):
-        gather_heads(torch.zeros(2, 4, 64), 0, 2, torch.zeros(4, 64))
+        gather_heads(torch.zeros(3, 4, 64), 0, 2)
+
+
+def _handles_rank(rank, world, port, q):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        mine = bytes((rank * 64 + i) % 251 for i in range(64))  # a 64-byte IPC handle's size
+        q.put((rank, exchange_handles(mine, world)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_peer_handles_are_exchanged_in_rank_order_gloo(world):
+    """Every rank ends with every rank's handle, rank order, as
+    bl_peers_open wants them."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_handles_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    want = b"".join(bytes((r * 64 + i) % 251 for i in range(64)) for r in range(world))
+    assert all(got[r] == want for r in range(world))
+
+
+def test_a_single_rank_exchanges_nothing():
+    assert exchange_handles(b"x" * 64, 1) == b"x" * 64

@@ -1,8 +1,15 @@
 """Config 5 split by heads (T=5477, 16 heads): every rank's slab computed
-through the C ABI, assembled heads side by side, against the whole op and
-the oracle. With one GPU the ranks run one after another on it (no
-collective); with two or more GPUs two NCCL processes run the real
-all-gather."""
+through the C ABI and assembled heads side by side, against the whole op and
+the oracle.
+
+With one GPU no two launches ever wait on each other: the ranks' slabs run
+one after another with no exchange, and the fused exchange
+(bl_attention_peers) runs as rank 0 of two with rank 1's buffer attached
+from local memory and rank 1's arrival written by the host, so the single
+launch's wait is satisfied (or, in the expiry case, left unsatisfied until
+its bounded wait gives up). With two or more GPUs two NCCL processes run the
+real exchange, both the fused form and the NCCL all-gather form."""
+import ctypes
 import os
 import socket
 
@@ -41,11 +48,12 @@ def test_head_slabs_assemble_to_the_whole_op(world):
     qkv = _qkv()
     whole = bl.attention(bl.pack_qkv(qkv, "bf16"), tokens=T, heads=H, qk_dtype="bf16",
                          out_dtype="f16")[0]
-    ops = [HeadParallelAttention(T, H, r, world, out_dtype="f16") for r in range(world)]
+    ops = [HeadParallelAttention(T, H, r, world, out_dtype="f16", exchange="nccl")
+           for r in range(world)]
     stacked = torch.empty_like(ops[0].stacked)
     for r, op in enumerate(ops):
         local = np.ascontiguousarray(qkv[:, :, :, op.h0:op.h1])
-        stacked[r].copy_(op.compute(bl.pack_qkv(local, "bf16")))
+        stacked[r].copy_(op.compute_local(bl.pack_qkv(local, "bf16")))
     torch.cuda.synchronize()
     assert bl.status(reset=True).code == 0
     out = stacked.permute(1, 0, 2).reshape(T, H * 64)
@@ -54,6 +62,106 @@ def test_head_slabs_assemble_to_the_whole_op(world):
     rel = _rel(out[ROWS[0]:ROWS[1]].float().cpu(), want)
     print("world %d: rel-L2 vs oracle %.3e" % (world, rel))
     assert rel <= 1e-3
+
+
+def test_fused_exchange_stores_into_every_rank_and_bounds_its_wait():
+    """bl_attention_peers as rank 0 of 2 (heads 0-7), rank 1's buffer a local
+    zeroed buffer attached in its place.
+
+    1. Rank 1's arrival for launch 1 is written by the host first: the launch
+       completes; its rows land in both buffers' slot 1 (this rank's columns
+       0-511 of [T][1024]), equal to the whole op's heads 0-7 and within 1e-3
+       of the oracle; its flag reached rank 1's header; the CTA counter is
+       back at zero.
+    2. Launch 2 with no arrival from rank 1 and a 1 ms wait limit: the kernel
+       returns by itself, the status word says peer timeout (0x60) for rank 1,
+       and the context stays usable.
+    3. Launch 3 with rank 1's arrival written: complete and correct again."""
+    import torch
+    import beatlm_b200 as bl
+    from beatlm_b200 import _native as N
+    from beatlm_b200 import ops
+    from beatlm_b200.parallel import PeerBuffers, device_view
+    L = N.lib()
+    qkv = _qkv(seed=21)
+    whole = bl.attention(bl.pack_qkv(qkv, "bf16"), tokens=T, heads=H, qk_dtype="bf16",
+                         out_dtype="f16")[0]
+    local = bl.pack_qkv(np.ascontiguousarray(qkv[:, :, :, :8]), "bf16")
+    slot_bytes = T * H * 64 * 2
+    peers = PeerBuffers(0, 2, slot_bytes)
+    other = torch.zeros(PeerBuffers.buffer_bytes(slot_bytes), dtype=torch.uint8, device="cuda")
+    peers.attach(1, other)
+    mine = L.bl_peers_slot(peers._h, 0) - 256  # this rank's header
+    stride = (slot_bytes + 255) // 256 * 256
+    flags = device_view(mine, (64,), torch.float16).view(torch.int32)  # 256-byte header
+    dummy = torch.empty((T, H * 64), dtype=torch.float16, device="cuda")
+    a = ops.attention_args(local, tokens=T, heads=8, out=dummy, qk_dtype="bf16",
+                           out_dtype="f16", out_row_stride=H * 64)
+    slot = ctypes.c_uint32()
+    try:
+        for launch in (1, 2, 3):
+            assert peers.next_epoch() == launch
+            arrives = launch != 2
+            if arrives:
+                flags[1] = launch  # rank 1 "arrived" for this launch
+            else:
+                N.check(L.bl_set_wait_limit(2_000_000))  # ~1 ms of SM clock
+            torch.cuda.synchronize()
+            N.check(L.bl_attention_peers(ctypes.byref(a), peers._h, 0, ctypes.byref(slot), None))
+            torch.cuda.synchronize()
+            N.check(L.bl_set_wait_limit(0))
+            st = bl.status(reset=True)
+            assert slot.value == launch % 2
+            if not arrives:
+                assert st.code == 0x60 and st.where == 1, (hex(st.code), st.where)
+                continue
+            assert st.code == 0, hex(st.code)
+            out = peers.slot(slot.value, (T, H * 64), torch.float16)
+            theirs = device_view(other.data_ptr() + 256 + slot.value * stride, (T, H * 64),
+                                 torch.float16)
+            assert torch.equal(out[:, :512], theirs[:, :512])
+            rel = _rel(out[:, :512].float().cpu(), whole[:, :512].float().cpu())
+            assert rel < 1e-6, rel
+            want = oracle.attention(_rounded(qkv)[0].reshape(T, -1), T, H, 64, rows=ROWS)
+            want = want.reshape(ROWS[1] - ROWS[0], H * 64)[:, :512]
+            rel_o = _rel(out[ROWS[0]:ROWS[1], :512].float().cpu(), want)
+            print("fused exchange launch %d: rel-L2 vs whole %.2e, vs oracle %.2e"
+                  % (launch, rel, rel_o))
+            assert rel_o <= 1e-3
+            theirs_flags = device_view(other.data_ptr(), (64,), torch.float16).view(torch.int32)
+            assert int(theirs_flags[0]) == launch  # this rank's arrival reached rank 1
+            assert int(flags[0]) == launch and int(flags[16]) == 0  # counter left at zero
+    finally:
+        L.bl_set_wait_limit(0)
+        torch.cuda.synchronize()
+        peers.close()
+
+
+def test_peer_attention_rejects_what_it_cannot_do():
+    import torch
+    import beatlm_b200 as bl
+    from beatlm_b200 import _native as N
+    from beatlm_b200 import ops
+    from beatlm_b200.parallel import PeerBuffers
+    L = N.lib()
+    peers = PeerBuffers(0, 2, 1370 * 384 * 2)
+    qkv = torch.zeros((1370, 3 * 6 * 64), dtype=torch.int16, device="cuda")
+    out = torch.zeros((1370, 384), dtype=torch.float16, device="cuda")
+    a = ops.attention_args(qkv, tokens=1370, heads=6, out=out, out_dtype="f16")
+    try:
+        with pytest.raises(bl.BackendError, match="not mapped"):
+            N.check(L.bl_attention_peers(ctypes.byref(a), peers._h, 0, None, None))
+        peers.attach(1, torch.zeros(PeerBuffers.buffer_bytes(1370 * 384 * 2), dtype=torch.uint8,
+                                    device="cuda"))
+        a.out_dtype = N.BL_F32
+        with pytest.raises(bl.BackendError, match="16-bit"):
+            N.check(L.bl_attention_peers(ctypes.byref(a), peers._h, 0, None, None))
+        a.out_dtype = N.BL_F16
+        with pytest.raises(bl.BackendError, match="column"):
+            N.check(L.bl_attention_peers(ctypes.byref(a), peers._h, 64, None, None))
+        assert peers.next_epoch() == 1  # nothing was launched
+    finally:
+        peers.close()
 
 
 def _free_port():
@@ -75,24 +183,29 @@ def _nccl_rank(rank, world, port, q):
                             device_id=torch.device("cuda", rank))
     try:
         qkv = _qkv()
-        op = HeadParallelAttention(T, H, rank, world, out_dtype="f16")
-        local = np.ascontiguousarray(qkv[:, :, :, op.h0:op.h1])
-        for _ in range(2):  # twice: the slots are overwritten, not accumulated
-            out = op(bl.pack_qkv(local, "bf16"))
-        torch.cuda.synchronize()
-        st = bl.status(reset=True).code
-        res = out.cpu().float().numpy()
+        res = {}
+        for exchange in ("peers", "nccl"):
+            op = HeadParallelAttention(T, H, rank, world, out_dtype="f16", exchange=exchange)
+            local = bl.pack_qkv(np.ascontiguousarray(qkv[:, :, :, op.h0:op.h1]), "bf16")
+            for _ in range(3):  # both slots, then the first again: overwritten, not accumulated
+                out = op(local)
+            torch.cuda.synchronize()
+            res[exchange] = (bl.status(reset=True).code,
+                             out.reshape(T, H * 64).cpu().float().numpy())
+            dist.barrier()
+            op.close()
         if rank == 0:
             whole = bl.attention(bl.pack_qkv(qkv, "bf16"), tokens=T, heads=H, qk_dtype="bf16",
                                  out_dtype="f16")[0].float().cpu().numpy()
-            q.put((rank, st, _rel(res, whole), res[ROWS[0]:ROWS[1]]))
+            q.put((rank, {k: (st, _rel(o, whole), o[ROWS[0]:ROWS[1]])
+                          for k, (st, o) in res.items()}))
         else:
-            q.put((rank, st, None, None))
+            q.put((rank, {k: (st, None, None) for k, (st, o) in res.items()}))
     finally:
         dist.destroy_process_group()
 
 
-def test_head_parallel_all_gather_over_nccl():
+def test_head_parallel_exchange_over_nvlink():
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < 2:
@@ -105,12 +218,15 @@ def test_head_parallel_all_gather_over_nccl():
         p.start()
     res = {}
     for _ in range(world):
-        r, st, rel, rows = q.get(timeout=300)
-        res[r] = (st, rel, rows)
+        r, d = q.get(timeout=300)
+        res[r] = d
     for p in procs:
         p.join(60)
         assert p.exitcode == 0
-    assert res[0][0] == 0 and res[1][0] == 0
-    assert res[0][1] < 1e-3
     want = oracle.attention(_rounded(_qkv())[0].reshape(T, -1), T, H, 64, rows=ROWS)
-    assert _rel(res[0][2], want) <= 1e-3
+    for exchange in ("peers", "nccl"):
+        assert res[0][exchange][0] == 0 and res[1][exchange][0] == 0, exchange
+        assert res[0][exchange][1] < 1e-3, exchange
+        rel = _rel(res[0][exchange][2], want)
+        print("%s exchange over 2 GPUs: rel-L2 vs oracle %.3e" % (exchange, rel))
+        assert rel <= 1e-3
