@@ -66,16 +66,17 @@ constexpr float kRescaleThreshold = 8.0f;
 
 // Head-parallel exchange (bl_attention_peers): every output row of this
 // rank's heads is stored into each rank's output buffer (peer memory over
-// NVLink, the local buffer for this rank), and the launch ends with an
-// arrival barrier: the last CTA of the grid raises this rank's flag in every
-// rank's buffer and waits, bounded, until every rank's flag for this launch
-// has arrived in its own.
+// NVLink, the local buffer for this rank) as soon as it is final, and the
+// CTAs exit without fences. A one-warp kernel launched right behind
+// (peer_arrive_kernel) starts when the attention grid has completed, so all
+// of its stores are performed, raises this rank's flag in every rank's
+// buffer and waits, bounded, until every rank's flag for this launch has
+// arrived in its own.
 constexpr int kMaxPeers = 8;
 struct PeerParams {
     int n;                         // ranks the rows go to; 0 = store to `out` only
     int rank;                      // this rank
     unsigned epoch;                // this launch's flag value (increases by one per launch)
-    unsigned* done;                // this rank's count of finished CTAs (left at zero)
     const unsigned* flags;         // this rank's arrival flags, one word per rank
     uint8_t* dst[kMaxPeers];       // rank r's output base for this launch (column-shifted)
     unsigned* flag_at[kMaxPeers];  // rank r's flag word of this rank
@@ -212,30 +213,29 @@ __device__ __forceinline__ void pack_row16(const float* o, float inv_l, uint4 (&
     }
 }
 
-// The end of a head-parallel launch, thread 0 of each CTA, after every
-// storing thread of the CTA fenced its row stores at system scope: count the
-// CTA as finished; the last CTA of the grid raises this rank's flag in every
-// rank's buffer and waits until every rank's flag for this launch has
-// arrived here (a bounded wait: on expiry it records ST_TIMEOUT_PEER with the
-// missing rank and returns). Ranks run on different GPUs, so waiting here for
-// the others cannot deadlock a GPU; a rank that never launches only costs
-// the wait limit.
-__device__ void peer_arrive(const Params& p, const PeerParams& q) {
-    const unsigned total = gridDim.x * gridDim.y * gridDim.z;
-    __threadfence_system();
-    if (atom_add_acq_rel_gpu(q.done, 1u) != total - 1) return;
-    *q.done = 0u;  // nothing else of this launch touches it; the next starts from zero
-    __threadfence_system();
-    for (int r = 0; r < q.n; ++r) st_release_sys(q.flag_at[r], q.epoch);
-    const long long t0 = clock64();
-    const long long limit = wait_limit(p.status);
-    for (int r = 0; r < q.n; ++r) {
+// The arrival barrier of a head-parallel launch: one warp, launched behind
+// the attention grid with programmatic dependent launch; griddepcontrol.wait
+// returns once that grid has completed and its memory operations (the row
+// stores into every rank's buffer) are performed. Lane r raises this rank's
+// flag in rank r's header (a system-scope release) and then waits for rank
+// r's flag for this launch in this rank's header (a system-scope acquire),
+// giving up after the wait limit with ST_TIMEOUT_PEER and the missing rank.
+// Ranks run on different GPUs, so waiting here for the others cannot
+// deadlock a GPU; a rank that never launches only costs the wait limit.
+__global__ void __launch_bounds__(32, 1) peer_arrive_kernel(const __grid_constant__ PeerParams q,
+                                                            Status* status) {
+    pdl_wait();
+    const int r = static_cast<int>(threadIdx.x);
+    if (r < q.n) {
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
+        st_release_sys(q.flag_at[r], q.epoch);
+        const long long t0 = clock64();
         while (static_cast<int>(ld_acquire_sys(q.flags + r) - q.epoch) < 0) {
-            if (clock64() - t0 > limit) {
-                record_status(p.status, ST_TIMEOUT_PEER, static_cast<uint32_t>(r));
-                return;
+            if (clock64() - t0 > wait_limit(status)) {
+                record_status(status, ST_TIMEOUT_PEER, static_cast<uint32_t>(r));
+                break;
             }
-            __nanosleep(128);
+            __nanosleep(64);
         }
     }
 }
@@ -599,26 +599,47 @@ __global__ void __launch_bounds__(kThreads, 1)
                           static_cast<size_t>(grow) * p.out_row_stride +
                           static_cast<size_t>(head - p.out_head_base) * HD);
         };
-        // The finished row: into `out`, or (head-parallel exchange) into
-        // every rank's output, starting with the next rank so the CTAs of a
-        // rank spread their first stores over the peers.
-        auto store_out = [&](const float* v, float inv) {
+        // The finished row into `out` (per thread; `valid` rows only). The
+        // head-parallel exchange instead stores into every rank's output,
+        // warp by warp: the warp's 32 rows (one per lane) are staged in its
+        // quarter of this tile's Q buffer (free once the tile's last scores
+        // are consumed) and each store instruction then writes four whole
+        // 128-byte rows, so the writes to peers leave as full lines; the
+        // ranks are visited starting with the next one so a rank's CTAs
+        // spread their first stores over the peers. In that form every lane
+        // of the warp must call it.
+        auto store_out = [&](const float* v, float inv, bool valid) {
             if constexpr (kPeers && kOutDtype != BL_F32) {
-                {
-                    uint4 pk[HD / 8];
-                    pack_row16<kOutDtype>(v, inv, pk);
-                    const size_t off = row_offset();
-                    for (int d = 0; d < peers.n; ++d) {
-                        int r = peers.rank + 1 + d;
-                        r = r >= peers.n ? r - peers.n : r;
-                        uint4* dst = reinterpret_cast<uint4*>(peers.dst[r] + off);
+                uint4 pk[HD / 8];
+                pack_row16<kOutDtype>(v, inv, pk);
+                uint8_t* stage = sQ + t * kTileBytes + sub * (32 * HD * 2);
 #pragma unroll
-                        for (int c = 0; c < HD / 8; ++c) dst[c] = pk[c];
+                for (int c = 0; c < HD / 8; ++c)
+                    *reinterpret_cast<uint4*>(stage + lane * (HD * 2) + ((c ^ (lane & 7)) << 4)) =
+                        pk[c];
+                __syncwarp();
+                const unsigned long long off = row_offset();
+                const int chunk = lane & 7;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int src = 4 * i + (lane >> 3);  // the lane whose row this is
+                    const unsigned long long roff = __shfl_sync(0xFFFFFFFFu, off, src);
+                    const bool rvalid = __shfl_sync(0xFFFFFFFFu, valid ? 1 : 0, src) != 0;
+                    const uint4 val = *reinterpret_cast<const uint4*>(
+                        stage + src * (HD * 2) + ((chunk ^ (src & 7)) << 4));
+                    if (rvalid) {
+                        for (int d = 0; d < peers.n; ++d) {
+                            int r = peers.rank + 1 + d;
+                            r = r >= peers.n ? r - peers.n : r;
+                            *reinterpret_cast<uint4*>(peers.dst[r] + roff + (chunk << 4)) = val;
+                        }
                     }
-                    return;
                 }
+                __syncwarp();
+            } else {
+                if (valid)
+                    store_row(static_cast<uint8_t*>(p.out) + row_offset(), kOutDtype, v, inv);
             }
-            store_row(static_cast<uint8_t*>(p.out) + row_offset(), kOutDtype, v, inv);
         };
         bool do_store = ok && store;
         float inv_l = 1.0f / l;
@@ -640,7 +661,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                    pack_f16x2(o[8 * k + 2] * il, o[8 * k + 3] * il),
                                    pack_f16x2(o[8 * k + 4] * il, o[8 * k + 5] * il),
                                    pack_f16x2(o[8 * k + 6] * il, o[8 * k + 7] * il));
-            auto combine = [&](auto&& part_on, auto&& part_ml) {
+            auto combine = [&](auto&& part_on, auto&& part_ml, bool valid) {
                 float mxs = -INFINITY;
                 for (int sp = 0; sp < p.splits; ++sp) mxs = fmaxf(mxs, part_ml(sp).x);
                 float acc[HD];
@@ -664,7 +685,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
                 }
-                store_out(acc, 1.0f / wsum);
+                store_out(acc, 1.0f / wsum, valid);
             };
             do_store = false;
             if (p.cluster) {
@@ -704,7 +725,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const bool got = mbar_wait_cluster(smem_u32(&tail->parts_full), 0, abort,
                                                        p.status, ST_TIMEOUT_SOFTMAX, 0x30000 | t);
                     if (threadIdx.x == 32 * kSoftmaxWarp0) trace_stamp(p.trace, 5);
-                    if (got && store) {
+                    // the exchange's stores are warp-collective: the whole
+                    // warp combines, rows past the end are not stored
+                    if (kPeers ? __all_sync(0xFFFFFFFFu, got) : (got && store)) {
                         const uint4* part = reinterpret_cast<const uint4*>(sP);
                         auto at = [&](int sp, int v) -> const uint4& {
                             const int src = sp < me ? sp : sp - 1;
@@ -716,7 +739,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 if (sp == me) return make_float2(mine_m, mine_l);
                                 const uint4 q = at(sp, HD / 8);
                                 return make_float2(__uint_as_float(q.x), __uint_as_float(q.y));
-                            });
+                            },
+                            store);
                     }
                 }
                 if (threadIdx.x == 32 * kSoftmaxWarp0) trace_stamp(p.trace, 6);
@@ -740,20 +764,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                 softmax_bar();
                 if (tail->last) {
                     __threadfence();
-                    if (store) {
+                    if (kPeers || store) {
                         const uint4* bo = p.part_o + (unit * p.splits * ROWS + crow) * (HD / 8);
                         const float2* bml = p.part_ml + unit * p.splits * ROWS + crow;
                         combine([&](int sp, int k) { return __ldcg(bo + static_cast<size_t>(sp) * ROWS * (HD / 8) + k); },
-                                [&](int sp) { return __ldcg(bml + static_cast<size_t>(sp) * ROWS); });
+                                [&](int sp) { return __ldcg(bml + static_cast<size_t>(sp) * ROWS); },
+                                store);
                     }
                     if (threadIdx.x == 32 * kSoftmaxWarp0) p.counters[unit] = 0u;  // self-cleaning
                 }
             }
         }
-        if (do_store) store_out(o, inv_l);
-        // head-parallel exchange: this thread's row stores (to peers too)
-        // are visible system-wide before the CTA counts itself finished
-        if (kPeers) __threadfence_system();
+        if (kPeers) {
+            if (p.splits == 1) store_out(o, inv_l, do_store);  // warp-collective
+        } else if (do_store) {
+            store_out(o, inv_l, true);
+        }
+        // head-parallel exchange: trace slot 6 is the first softmax warp
+        // past its row stores
+        if (kPeers && threadIdx.x == 32 * kSoftmaxWarp0) trace_stamp(p.trace, 6);
     }
 
     tc_fence_before();
@@ -763,7 +792,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
-    if (kPeers && threadIdx.x == 0) peer_arrive(p, peers);
     if (threadIdx.x == 0) trace_stamp(p.trace, 7);
 }
 
@@ -1154,7 +1182,6 @@ extern "C" int bl_attention_peers(const bl_attention_args* args, bl_peers* peers
     pp.n = static_cast<int>(peers->world);
     pp.rank = static_cast<int>(peers->rank);
     pp.epoch = epoch;
-    pp.done = reinterpret_cast<unsigned*>(peers->local + bl_peers::kDoneOffset);
     pp.flags = reinterpret_cast<const unsigned*>(peers->local);
     const uint64_t off = bl_peers::kHeader + slot * peers->slot_stride + out_col * esz;
     for (uint32_t r = 0; r < peers->world; ++r) {
@@ -1168,9 +1195,16 @@ extern "C" int bl_attention_peers(const bl_attention_args* args, bl_peers* peers
     Launch l;
     int rc = attn::prepare(a, nullptr, 0, &l, &pp);
     if (rc != BL_OK) return rc;
-    rc = enqueue(l, static_cast<cudaStream_t>(stream));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    rc = enqueue(l, st);
     if (rc != BL_OK) return rc;
+    // the arrival barrier; from here on the launch counts (the attention
+    // grid is queued and the peers expect this rank's flag)
     peers->epoch = epoch;
+    const cudaError_t e = launch_k(attn::peer_arrive_kernel, dim3(1), dim3(32), 0, st, pp,
+                                   status_ptr());
+    if (e != cudaSuccess)
+        return fail(BL_ERR_CUDA, "peer attention: arrival barrier: %s", cudaGetErrorString(e));
     if (slot_out != nullptr) *slot_out = slot;
     return BL_OK;
 }

@@ -114,13 +114,12 @@ inline int enqueue(const Launch& l, cudaStream_t s) {
 }  // namespace bl
 
 // The peer buffers of a head-parallel exchange (bl_peers_*): this rank's
-// buffer, a 256-byte header (arrival flags, one 32-bit word per rank, at 0;
-// the count of finished CTAs at 64) and two output slots, plus every other
-// rank's buffer mapped into this process.
+// buffer, a 256-byte header (arrival flags, one 32-bit word per rank, at 0)
+// and two output slots, plus every other rank's buffer mapped into this
+// process.
 struct bl_peers {
     static constexpr int kMax = 8;
     static constexpr uint64_t kHeader = 256;
-    static constexpr uint64_t kDoneOffset = 64;
     int device = -1;
     uint32_t rank = 0, world = 0;
     uint64_t slot_bytes = 0;   // as asked

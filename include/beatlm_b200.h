@@ -130,8 +130,8 @@ typedef struct bl_attention_args {
     /* Optional per-CTA timeline (NULL = off): CTA b writes %globaltimer
      * stamps (ns) at trace[8b..8b+7]: entry, setup done, tile 0 softmax done,
      * tile 1 softmax done, partials stored (cluster combine), cluster barrier
-     * passed, combine done, exit (slots a path does not reach stay as they
-     * were). CTAs are numbered x-fastest over the grid (query groups, heads,
+     * passed, combine done (bl_attention_peers: rows stored), exit (slots a
+     * path does not reach stay as they were). CTAs are numbered x-fastest over the grid (query groups, heads,
      * batch x splits); the buffer holds 8 * CTAs uint64 values. */
     uint64_t* trace;
 } bl_attention_args;
@@ -177,8 +177,7 @@ int bl_attention_noalloc(const bl_attention_args* args, void* stream);
  * (kernel.rs:157-161) on every rank.
  *
  * Each rank owns a peer buffer: a 256-byte header of arrival flags (rank r's
- * flag is the 32-bit word at byte 4 r; bytes 64-67 count finished CTAs and
- * are left at zero by every launch) and two output slots of slot_bytes each
+ * flag is the 32-bit word at byte 4 r) and two output slots of slot_bytes each
  * (slot s at byte 256 + s * slot_bytes rounded up to 256), in one device
  * allocation made at create (the only allocation). The ranks exchange
  * 64-byte CUDA IPC handles of their
@@ -211,10 +210,11 @@ void bl_peers_destroy(bl_peers* p);
  * elements apart; this rank's head h at column out_col + (h - out_head_base) *
  * 64), as soon as each row is final, so the exchange crosses NVLink while the
  * kernel still computes. args->out and args->workspace are ignored; key
- * splits combine in a thread-block cluster. The launch ends with an arrival
- * barrier on the device: the last CTA raises this rank's flag in every
- * rank's header and waits until every rank's flag for this launch has
- * arrived in its own, so when the launch completes the whole output is in
+ * splits combine in a thread-block cluster. The attention grid is followed
+ * on `stream` by an arrival barrier, a one-warp kernel that starts once the
+ * grid has completed (so its row stores are performed), raises this rank's
+ * flag in every rank's header and waits until every rank's flag for this
+ * launch has arrived in its own: when it completes, the whole output is in
  * this rank's slot (*slot_out). The wait is bounded (bl_set_wait_limit); a
  * rank that never launches makes the others record status 0x60 (peer
  * timeout) and return with their output incomplete. Every rank must make

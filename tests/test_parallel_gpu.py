@@ -70,9 +70,9 @@ def test_fused_exchange_stores_into_every_rank_and_bounds_its_wait():
 
     1. Rank 1's arrival for launch 1 is written by the host first: the launch
        completes; its rows land in both buffers' slot 1 (this rank's columns
-       0-511 of [T][1024]), equal to the whole op's heads 0-7 and within 1e-3
-       of the oracle; its flag reached rank 1's header; the CTA counter is
-       back at zero.
+       0-511 of [T][1024]), bit-equal to bl_attention of the same 8 heads and
+       within 1e-3 of the oracle; its flag reached rank 1's header and its
+       own.
     2. Launch 2 with no arrival from rank 1 and a 1 ms wait limit: the kernel
        returns by itself, the status word says peer timeout (0x60) for rank 1,
        and the context stays usable.
@@ -87,6 +87,9 @@ def test_fused_exchange_stores_into_every_rank_and_bounds_its_wait():
     whole = bl.attention(bl.pack_qkv(qkv, "bf16"), tokens=T, heads=H, qk_dtype="bf16",
                          out_dtype="f16")[0]
     local = bl.pack_qkv(np.ascontiguousarray(qkv[:, :, :, :8]), "bf16")
+    # the same 8 heads through bl_attention: the same grid and key splits, so
+    # the rows the exchange stores must be these bits
+    same = bl.attention(local, tokens=T, heads=8, qk_dtype="bf16", out_dtype="f16")[0]
     slot_bytes = T * H * 64 * 2
     peers = PeerBuffers(0, 2, slot_bytes)
     other = torch.zeros(PeerBuffers.buffer_bytes(slot_bytes), dtype=torch.uint8, device="cuda")
@@ -120,8 +123,9 @@ def test_fused_exchange_stores_into_every_rank_and_bounds_its_wait():
             theirs = device_view(other.data_ptr() + 256 + slot.value * stride, (T, H * 64),
                                  torch.float16)
             assert torch.equal(out[:, :512], theirs[:, :512])
+            assert torch.equal(out[:, :512], same)
             rel = _rel(out[:, :512].float().cpu(), whole[:, :512].float().cpu())
-            assert rel < 1e-6, rel
+            assert rel < 1e-3, rel  # the 16-head launch splits its keys differently
             want = oracle.attention(_rounded(qkv)[0].reshape(T, -1), T, H, 64, rows=ROWS)
             want = want.reshape(ROWS[1] - ROWS[0], H * 64)[:, :512]
             rel_o = _rel(out[ROWS[0]:ROWS[1], :512].float().cpu(), want)
@@ -130,7 +134,7 @@ def test_fused_exchange_stores_into_every_rank_and_bounds_its_wait():
             assert rel_o <= 1e-3
             theirs_flags = device_view(other.data_ptr(), (64,), torch.float16).view(torch.int32)
             assert int(theirs_flags[0]) == launch  # this rank's arrival reached rank 1
-            assert int(flags[0]) == launch and int(flags[16]) == 0  # counter left at zero
+            assert int(flags[0]) == launch  # and its own
     finally:
         L.bl_set_wait_limit(0)
         torch.cuda.synchronize()
