@@ -356,3 +356,24 @@ SIGNATURES.update({
                                           ctypes.c_void_p]),
 })
 PEER_HANDLE_BYTES = 64
+
+
+class AllGatherArgs(ctypes.Structure):
+    _fields_ = [("comm", ctypes.c_void_p), ("send", ctypes.c_void_p), ("recv", ctypes.c_void_p),
+                ("bytes", ctypes.c_uint64)]
+
+
+COMM_ID_BYTES = 128
+BL_ERR_COMM, BL_ERR_TIMEOUT = 6, 7
+SIGNATURES.update({
+    "bl_comm_available": (ctypes.c_int, []),
+    "bl_comm_unique_id": (ctypes.c_int, [ctypes.c_void_p]),
+    "bl_comm_init": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32,
+                                    ctypes.c_uint32, ctypes.POINTER(ctypes.c_void_p)]),
+    "bl_comm_all_gather": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                          ctypes.c_uint64, ctypes.c_void_p]),
+    "bl_comm_check": (ctypes.c_int, [ctypes.c_void_p]),
+    "bl_comm_abort": (ctypes.c_int, [ctypes.c_void_p]),
+    "bl_comm_aborted": (ctypes.c_int, [ctypes.c_void_p]),
+    "bl_comm_destroy": (ctypes.c_int, [ctypes.c_void_p]),
+})

@@ -44,6 +44,9 @@ inline size_t dtype_size(int dt) { return dt == BL_F32 ? 4 : 2; }
 // Kernels::new, which builds, and Kernels::encode, which records).
 struct Launch {
     std::function<cudaError_t(cudaStream_t)> run;
+    // set instead of `run` by launches that report a library status (a
+    // collective); enqueue() prefers it
+    std::function<int(cudaStream_t)> run_status;
     int op = 0;  // bl_op kind
 };
 
@@ -106,6 +109,7 @@ cudaError_t launch_k_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, dim3
 int attention_auto_splits(const bl_attention_args& a, uint64_t workspace_bytes);
 
 inline int enqueue(const Launch& l, cudaStream_t s) {
+    if (l.run_status) return l.run_status(s);
     cudaError_t e = l.run(s);
     if (e != cudaSuccess) return fail(BL_ERR_CUDA, "launch failed: %s", cudaGetErrorString(e));
     return BL_OK;

@@ -284,7 +284,8 @@ bool split_dims(const bl_kernel_spec& s, uint32_t* extent, uint32_t* grain) {
         }
         case BL_OP_GEMM: *extent = static_cast<const bl_gemm_args*>(s.args)->m; *grain = 128; return true;
         case BL_OP_LAYERNORM: *extent = static_cast<const bl_layernorm_args*>(s.args)->rows; return true;
-        case BL_OP_PATCHIFY: return true;
+        case BL_OP_PATCHIFY:
+        case BL_OP_ALLGATHER: return true;
         default: return false;
     }
 }
@@ -297,8 +298,9 @@ int add_spec(bl_kernels* k, const bl_kernel_spec& s, size_t index) {
     if (!split_dims(s, &extent, &grain))
         return fail(BL_ERR_INVALID, "kernel %zu: unknown op %d", index, s.op);
     std::vector<uint32_t> edges(static_cast<size_t>(s.parts > 1 ? s.parts : 1) + 1);
-    const uint32_t count = s.op == BL_OP_PATCHIFY ? 1 : bl_split_edges(extent, grain, s.parts, edges.data());
-    if (s.op == BL_OP_PATCHIFY) { edges[0] = 0; edges[1] = 1; }
+    const bool whole = s.op == BL_OP_PATCHIFY || s.op == BL_OP_ALLGATHER;
+    const uint32_t count = whole ? 1 : bl_split_edges(extent, grain, s.parts, edges.data());
+    if (whole) { edges[0] = 0; edges[1] = 1; }
     for (uint32_t i = 0; i < count; ++i) {
         Launch l;
         int rc = BL_OK;
@@ -324,6 +326,17 @@ int add_spec(bl_kernels* k, const bl_kernel_spec& s, size_t index) {
                 rc = prepare_layernorm_rows(*static_cast<const bl_layernorm_args*>(s.args),
                                             edges[i], edges[i + 1], &l);
                 break;
+            case BL_OP_ALLGATHER: {
+                const bl_allgather_args g = *static_cast<const bl_allgather_args*>(s.args);
+                if (g.comm == nullptr || g.send == nullptr || g.recv == nullptr)
+                    return fail(BL_ERR_INVALID, "kernel %zu: all-gather needs a communicator "
+                                                "and buffers", index);
+                l.op = BL_OP_ALLGATHER;
+                l.run_status = [g](cudaStream_t st) {
+                    return bl_comm_all_gather(g.comm, g.send, g.recv, g.bytes, st);
+                };
+                break;
+            }
             default:
                 rc = prepare_patchify(*static_cast<const bl_patchify_args*>(s.args), &l);
         }
@@ -448,7 +461,7 @@ extern "C" uint32_t bl_kernel_spec_max_parts(const bl_kernel_spec* s) {
     if (s == nullptr || s->args == nullptr) return 0;
     uint32_t extent = 1, grain = 1;
     if (!split_dims(*s, &extent, &grain)) return 0;
-    if (s->op == BL_OP_PATCHIFY) return 1;
+    if (s->op == BL_OP_PATCHIFY || s->op == BL_OP_ALLGATHER) return 1;
     return static_cast<uint32_t>((static_cast<uint64_t>(extent) + grain - 1) / grain);
 }
 

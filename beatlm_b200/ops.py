@@ -18,6 +18,10 @@ ACT = {None: 0, "none": 0, "relu": 1, "gelu_tanh": 2, "gelu_erf": 3}
 
 
 def _stream_ptr(stream):
+    """A cudaStream_t for the C ABI: a torch stream, a raw handle (int), or
+    None for torch's current stream."""
+    if isinstance(stream, int):
+        return ctypes.c_void_p(stream)
     import torch
     s = stream if stream is not None else torch.cuda.current_stream()
     return ctypes.c_void_p(s.cuda_stream)

@@ -13,9 +13,10 @@ import dataclasses
 from . import _native as N
 from .ops import _stream_ptr
 
-OP_ATTENTION, OP_GEMM, OP_LAYERNORM, OP_PATCHIFY = 1, 2, 3, 4
+OP_ATTENTION, OP_GEMM, OP_LAYERNORM, OP_PATCHIFY, OP_ALLGATHER = 1, 2, 3, 4, 5
 _OP_OF = {N.AttentionArgs: OP_ATTENTION, N.GemmArgs: OP_GEMM,
-          N.LayerNormArgs: OP_LAYERNORM, N.PatchifyArgs: OP_PATCHIFY}
+          N.LayerNormArgs: OP_LAYERNORM, N.PatchifyArgs: OP_PATCHIFY,
+          N.AllGatherArgs: OP_ALLGATHER}
 
 
 def hold(stream, microseconds: int):

@@ -31,7 +31,9 @@ enum {
     BL_ERR_UNSUPPORTED = 2, /* a shape or type this build does not implement */
     BL_ERR_CUDA = 3,        /* a CUDA runtime or driver call failed */
     BL_ERR_DEVICE = 4,      /* a kernel recorded an error in the device status word */
-    BL_ERR_CAPACITY = 5     /* a plan or buffer does not fit (reference: PlanError, memory.rs:220) */
+    BL_ERR_CAPACITY = 5,    /* a plan or buffer does not fit (reference: PlanError, memory.rs:220) */
+    BL_ERR_COMM = 6,        /* a communicator call failed (the communicator is then aborted) */
+    BL_ERR_TIMEOUT = 7      /* a communicator call did not complete within its timeout (aborted) */
 };
 
 /* Copies the calling thread's last error message (NUL-terminated, truncated
@@ -225,6 +227,45 @@ void bl_peers_destroy(bl_peers* p);
 int bl_attention_peers(const bl_attention_args* args, bl_peers* peers, uint32_t out_col,
                        uint32_t* slot_out, void* stream);
 
+/* ------------------------------------------------------------ communicator */
+
+/*
+ * NCCL for the multi-GPU configs, created non-blocking and never waited on
+ * without a bound. The reference runs on one device (no collectives); this
+ * is the collective form of the long-sequence attention's exchange (an
+ * all-gather of head slabs) and a host's way to run collectives without
+ * another runtime. NCCL is loaded at run time (libnccl.so.2, or the library
+ * the environment variable BEATLM_B200_NCCL names); where it cannot be
+ * loaded bl_comm_available() is 0 and the calls return BL_ERR_UNSUPPORTED.
+ *
+ * Every call that waits (init, a collective's enqueue, check, destroy) polls
+ * ncclCommGetAsyncError for at most the communicator's timeout; when the
+ * timeout runs out (a rank that never joins, a peer that stopped) or NCCL
+ * reports an error, the communicator is aborted (ncclCommAbort) and the call
+ * returns BL_ERR_TIMEOUT or BL_ERR_COMM. An aborted communicator refuses
+ * further work; destroy it. Collectives are enqueued on `stream` and complete
+ * there; every rank must issue the same collectives in the same order.
+ */
+enum { BL_COMM_ID_BYTES = 128 };
+typedef struct bl_comm bl_comm;
+int bl_comm_available(void);
+/* A new unique id (ncclGetUniqueId), made by one rank and shared with the
+ * others by any host channel. */
+int bl_comm_unique_id(void* id /* BL_COMM_ID_BYTES */);
+/* Joins rank `rank` of `world` (ncclCommInitRankConfig, blocking = 0) on the
+ * current device, waiting at most timeout_ms for the others. */
+int bl_comm_init(const void* id, uint32_t world, uint32_t rank, uint32_t timeout_ms,
+                 bl_comm** out);
+/* recv[r * bytes .. (r + 1) * bytes) = rank r's send (ncclAllGather). */
+int bl_comm_all_gather(bl_comm* c, const void* send, void* recv, uint64_t bytes, void* stream);
+/* Waits (bounded) until the communicator has no operation whose enqueue is
+ * still in progress and reports its asynchronous error state. */
+int bl_comm_check(bl_comm* c);
+int bl_comm_abort(bl_comm* c);
+int bl_comm_aborted(const bl_comm* c);
+/* Finalizes (bounded) and destroys; an aborted communicator is only freed. */
+int bl_comm_destroy(bl_comm* c);
+
 /* ------------------------------------------------------------------ linear */
 
 enum { BL_ACT_NONE = 0, BL_ACT_RELU = 1, BL_ACT_GELU_TANH = 2, BL_ACT_GELU_ERF = 3 };
@@ -390,13 +431,24 @@ uint32_t bl_parts_within(uint64_t duration_us, uint64_t bound_us, uint32_t max_p
 
 /* ------------------------------------------------------------------ kernels */
 
-enum { BL_OP_ATTENTION = 1, BL_OP_GEMM = 2, BL_OP_LAYERNORM = 3, BL_OP_PATCHIFY = 4 };
+enum { BL_OP_ATTENTION = 1, BL_OP_GEMM = 2, BL_OP_LAYERNORM = 3, BL_OP_PATCHIFY = 4,
+       BL_OP_ALLGATHER = 5 };
+
+/* The arguments of a BL_OP_ALLGATHER kernel spec: bl_comm_all_gather encoded
+ * like a kernel (recorded into a program, replayed in its CUDA graph). */
+typedef struct bl_allgather_args {
+    bl_comm* comm;
+    const void* send;
+    void* recv;
+    uint64_t bytes;
+} bl_allgather_args;
 
 /* One kernel of a program: an op and its arguments (the matching bl_*_args,
  * read during bl_kernels_create only), a label, and the number of row parts
  * it runs as (0 or 1 = whole). Split dimensions and grains: attention query
  * rows in 128-row tiles (every frame of the batch), GEMM output rows in
- * 128-row tiles, LayerNorm rows one by one; patchify is never split. */
+ * 128-row tiles, LayerNorm rows one by one; patchify and all-gather are
+ * never split. */
 typedef struct bl_kernel_spec {
     int32_t op;
     const void* args;

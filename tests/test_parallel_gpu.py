@@ -8,7 +8,8 @@ one after another with no exchange, and the fused exchange
 from local memory and rank 1's arrival written by the host, so the single
 launch's wait is satisfied (or, in the expiry case, left unsatisfied until
 its bounded wait gives up). With two or more GPUs two NCCL processes run the
-real exchange, both the fused form and the NCCL all-gather form."""
+real exchange, both the fused form and the NCCL all-gather form, and the C
+ABI's non-blocking communicator (bl_comm) over real NCCL."""
 import ctypes
 import os
 import socket
@@ -198,10 +199,33 @@ def _nccl_rank(rank, world, port, q):
                              out.reshape(T, H * 64).cpu().float().numpy())
             dist.barrier()
             op.close()
+        # the C ABI's own non-blocking communicator over real NCCL: an
+        # all-gather of device bytes, once directly and once as a kernel spec
+        from beatlm_b200 import comm as C
+        from beatlm_b200.parallel import exchange_handles
+        from beatlm_b200.runtime import Kernels, Spec
+        uid = exchange_handles(C.unique_id() if rank == 0 else bytes(128), world)[:128]
+        c = C.Comm(uid, world, rank, timeout_ms=30000)
+        send = torch.full((4096,), rank + 1, dtype=torch.uint8, device="cuda")
+        recv = torch.zeros(world * 4096, dtype=torch.uint8, device="cuda")
+        stream = torch.cuda.current_stream().cuda_stream
+        c.all_gather(send.data_ptr(), recv.data_ptr(), 4096, stream=stream)
+        torch.cuda.synchronize()
+        comm_ok = all(bool((recv[r * 4096:(r + 1) * 4096] == r + 1).all()) for r in range(world))
+        recv.zero_()
+        k = Kernels([Spec(c.args(send.data_ptr(), recv.data_ptr(), 4096), "exchange")])
+        k.encode(0, stream=stream)
+        torch.cuda.synchronize()
+        comm_ok = comm_ok and all(bool((recv[r * 4096:(r + 1) * 4096] == r + 1).all())
+                                  for r in range(world))
+        k.close()
+        c.close()
+        res["comm"] = (0 if comm_ok else 1, None)
         if rank == 0:
             whole = bl.attention(bl.pack_qkv(qkv, "bf16"), tokens=T, heads=H, qk_dtype="bf16",
                                  out_dtype="f16")[0].float().cpu().numpy()
-            q.put((rank, {k: (st, _rel(o, whole), o[ROWS[0]:ROWS[1]])
+            q.put((rank, {k: (st, None if o is None else _rel(o, whole),
+                              None if o is None else o[ROWS[0]:ROWS[1]])
                           for k, (st, o) in res.items()}))
         else:
             q.put((rank, {k: (st, None, None) for k, (st, o) in res.items()}))
@@ -227,6 +251,7 @@ def test_head_parallel_exchange_over_nvlink():
     for p in procs:
         p.join(60)
         assert p.exitcode == 0
+    assert res[0]["comm"][0] == 0 and res[1]["comm"][0] == 0  # bl_comm all-gathers
     want = oracle.attention(_rounded(_qkv())[0].reshape(T, -1), T, H, 64, rows=ROWS)
     for exchange in ("peers", "nccl"):
         assert res[0][exchange][0] == 0 and res[1][exchange][0] == 0, exchange
