@@ -140,6 +140,14 @@ class KernelSpec(ctypes.Structure):
                 ("parts", ctypes.c_uint32)]
 
 
+class Substitution(ctypes.Structure):
+    _fields_ = [("from_", ctypes.c_void_p), ("to", ctypes.c_void_p), ("bytes", ctypes.c_uint64)]
+
+
+class BindingSet(ctypes.Structure):
+    _fields_ = [("subs", ctypes.POINTER(Substitution)), ("n", ctypes.c_size_t)]
+
+
 class SliceTime(ctypes.Structure):
     _fields_ = [("frame", ctypes.c_uint64), ("slice", ctypes.c_uint32),
                 ("kernel", ctypes.c_uint32), ("begin_us", ctypes.c_double),
@@ -156,13 +164,15 @@ SIGNATURES.update({
     "bl_split_edges": (_u32, [_u32, _u32, _u32, ctypes.POINTER(_u32)]),
     "bl_parts_within": (_u32, [ctypes.c_uint64, ctypes.c_uint64, _u32]),
     "bl_kernels_create": (ctypes.c_int, [ctypes.POINTER(KernelSpec), _sz,
-                                         ctypes.POINTER(_vp)]),
+                                         ctypes.POINTER(BindingSet), _sz, ctypes.POINTER(_vp)]),
     "bl_kernels_destroy": (None, [_vp]),
     "bl_kernels_len": (_sz, [_vp]),
+    "bl_kernels_sets": (_sz, [_vp]),
+    "bl_kernels_launches": (_sz, [_vp]),
     "bl_kernels_label": (ctypes.c_char_p, [_vp, _sz]),
-    "bl_kernels_encode": (ctypes.c_int, [_vp, _sz, _vp, _vp, _i32]),
-    "bl_kernels_encode_range": (ctypes.c_int, [_vp, _sz, _sz, _vp, _vp, _i32]),
-    "bl_kernels_capture": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(_vp)]),
+    "bl_kernels_encode": (ctypes.c_int, [_vp, _sz, _sz, _vp, _vp, _i32]),
+    "bl_kernels_encode_range": (ctypes.c_int, [_vp, _sz, _sz, _sz, _vp, _vp, _i32]),
+    "bl_kernels_capture": (ctypes.c_int, [_vp, _sz, _vp, ctypes.POINTER(_vp)]),
     "bl_graph_launch": (ctypes.c_int, [_vp, _vp]),
     "bl_graph_destroy": (None, [_vp]),
     "bl_timer_create": (ctypes.c_int, [_u32, ctypes.POINTER(_vp)]),

@@ -256,9 +256,18 @@ extern "C" int bl_timer_get_stats(const bl_timer* t, bl_timer_stats* out) {
 
 // ------------------------------------------------------------------ kernels
 
+// The launches of a program: kernel i (a part) under binding set j is
+// launches[launch_of[i][j]]; a kernel that touches none of a set's
+// substituted tensors shares set 0's launch (the reference shares its bind
+// group between such sets, crates/beatlm/src/codegen/kernels.rs:1-10).
 struct bl_kernels {
     std::vector<bl::Launch> launches;
+    std::vector<std::vector<uint32_t>> launch_of;
     std::vector<std::string> labels;
+    size_t sets = 1;
+    const bl::Launch& at(size_t kernel, size_t set) const {
+        return launches[launch_of[kernel][set]];
+    }
 };
 
 struct bl_graph {
@@ -290,7 +299,96 @@ bool split_dims(const bl_kernel_spec& s, uint32_t* extent, uint32_t* grain) {
     }
 }
 
-int add_spec(bl_kernels* k, const bl_kernel_spec& s, size_t index) {
+// A binding set's substitutions applied to one pointer argument: a pointer
+// into [from, from + bytes) moves to the same offset from `to`. Counts the
+// pointers moved.
+struct Rebind {
+    const bl_binding_set* set = nullptr;
+    int moved = 0;
+    template <typename P>
+    void operator()(P*& p) {
+        if (set == nullptr || p == nullptr) return;
+        const uintptr_t v = reinterpret_cast<uintptr_t>(p);
+        for (size_t i = 0; i < set->n; ++i) {
+            const bl_substitution& u = set->subs[i];
+            const uintptr_t f = reinterpret_cast<uintptr_t>(u.from);
+            if (v >= f && v - f < u.bytes) {
+                p = reinterpret_cast<P*>(reinterpret_cast<uintptr_t>(u.to) + (v - f));
+                ++moved;
+                return;
+            }
+        }
+    }
+};
+
+void rebind(bl_attention_args& a, Rebind& r) { r(a.qkv), r(a.out), r(a.workspace), r(a.trace); }
+void rebind(bl_gemm_args& g, Rebind& r) {
+    r(g.a), r(g.b), r(g.ln_x), r(g.ln_gamma), r(g.ln_beta), r(g.bias), r(g.chan_scale);
+    r(g.residual), r(g.out), r(g.stats_out), r(g.ln_stats), r(g.norm_out), r(g.norm_gamma);
+    r(g.norm_beta), r(g.norm_sync);
+}
+void rebind(bl_layernorm_args& a, Rebind& r) { r(a.x), r(a.gamma), r(a.beta), r(a.out); }
+void rebind(bl_patchify_args& a, Rebind& r) { r(a.image), r(a.a), r(a.cls), r(a.pos), r(a.x); }
+void rebind(bl_allgather_args& a, Rebind& r) { r(a.send), r(a.recv); }
+
+// Part [edges[i], edges[i + 1]) of spec `s` with binding set `set` (NULL =
+// as given); *moved = how many pointer arguments the set redirected.
+int prepare_part(const bl_kernel_spec& s, const std::vector<uint32_t>& edges, uint32_t i,
+                 const bl_binding_set* set, int* moved, bl::Launch* l, size_t index) {
+    using namespace bl;
+    Rebind r;
+    r.set = set;
+    switch (s.op) {
+        case BL_OP_ATTENTION: {
+            bl_attention_args a = *static_cast<const bl_attention_args*>(s.args);
+            rebind(a, r);
+            // Every part uses the whole kernel's key-split count, so each
+            // row is computed exactly as the whole kernel computes it.
+            if (a.kv_splits == 0)
+                a.kv_splits = static_cast<uint32_t>(attention_auto_splits(
+                    a, a.workspace != nullptr ? a.workspace_bytes : 0));
+            const uint32_t r0 = a.row_begin;
+            a.row_begin = r0 + edges[i];
+            a.row_end = r0 + edges[i + 1];
+            *moved = r.moved;
+            return prepare_attention(a, l);
+        }
+        case BL_OP_GEMM: {
+            bl_gemm_args g = *static_cast<const bl_gemm_args*>(s.args);
+            rebind(g, r);
+            *moved = r.moved;
+            return prepare_gemm_rows(g, edges[i], edges[i + 1], l);
+        }
+        case BL_OP_LAYERNORM: {
+            bl_layernorm_args a = *static_cast<const bl_layernorm_args*>(s.args);
+            rebind(a, r);
+            *moved = r.moved;
+            return prepare_layernorm_rows(a, edges[i], edges[i + 1], l);
+        }
+        case BL_OP_ALLGATHER: {
+            bl_allgather_args g = *static_cast<const bl_allgather_args*>(s.args);
+            rebind(g, r);
+            *moved = r.moved;
+            if (g.comm == nullptr || g.send == nullptr || g.recv == nullptr)
+                return fail(BL_ERR_INVALID, "kernel %zu: all-gather needs a communicator "
+                                            "and buffers", index);
+            l->op = BL_OP_ALLGATHER;
+            l->run_status = [g](cudaStream_t st) {
+                return bl_comm_all_gather(g.comm, g.send, g.recv, g.bytes, st);
+            };
+            return BL_OK;
+        }
+        default: {
+            bl_patchify_args a = *static_cast<const bl_patchify_args*>(s.args);
+            rebind(a, r);
+            *moved = r.moved;
+            return prepare_patchify(a, l);
+        }
+    }
+}
+
+int add_spec(bl_kernels* k, const bl_kernel_spec& s, size_t index, const bl_binding_set* sets,
+             size_t nsets) {
     using namespace bl;
     if (s.args == nullptr) return fail(BL_ERR_INVALID, "kernel %zu: null args", index);
     const std::string base = s.label ? s.label : ("kernel " + std::to_string(index));
@@ -302,46 +400,20 @@ int add_spec(bl_kernels* k, const bl_kernel_spec& s, size_t index) {
     const uint32_t count = whole ? 1 : bl_split_edges(extent, grain, s.parts, edges.data());
     if (whole) { edges[0] = 0; edges[1] = 1; }
     for (uint32_t i = 0; i < count; ++i) {
-        Launch l;
-        int rc = BL_OK;
-        switch (s.op) {
-            case BL_OP_ATTENTION: {
-                bl_attention_args a = *static_cast<const bl_attention_args*>(s.args);
-                // Every part uses the whole kernel's key-split count, so each
-                // row is computed exactly as the whole kernel computes it.
-                if (a.kv_splits == 0)
-                    a.kv_splits = static_cast<uint32_t>(attention_auto_splits(
-                        a, a.workspace != nullptr ? a.workspace_bytes : 0));
-                const uint32_t r0 = a.row_begin;
-                a.row_begin = r0 + edges[i];
-                a.row_end = r0 + edges[i + 1];
-                rc = prepare_attention(a, &l);
-                break;
+        std::vector<uint32_t> of(nsets == 0 ? 1 : nsets);
+        for (size_t j = 0; j < of.size(); ++j) {
+            Launch l;
+            int moved = 0;
+            int rc = prepare_part(s, edges, i, nsets == 0 ? nullptr : &sets[j], &moved, &l, index);
+            if (rc != BL_OK) return rc;
+            if (j > 0 && moved == 0) {
+                of[j] = of[0];  // untouched by this set: set 0's launch
+                continue;
             }
-            case BL_OP_GEMM:
-                rc = prepare_gemm_rows(*static_cast<const bl_gemm_args*>(s.args), edges[i],
-                                       edges[i + 1], &l);
-                break;
-            case BL_OP_LAYERNORM:
-                rc = prepare_layernorm_rows(*static_cast<const bl_layernorm_args*>(s.args),
-                                            edges[i], edges[i + 1], &l);
-                break;
-            case BL_OP_ALLGATHER: {
-                const bl_allgather_args g = *static_cast<const bl_allgather_args*>(s.args);
-                if (g.comm == nullptr || g.send == nullptr || g.recv == nullptr)
-                    return fail(BL_ERR_INVALID, "kernel %zu: all-gather needs a communicator "
-                                                "and buffers", index);
-                l.op = BL_OP_ALLGATHER;
-                l.run_status = [g](cudaStream_t st) {
-                    return bl_comm_all_gather(g.comm, g.send, g.recv, g.bytes, st);
-                };
-                break;
-            }
-            default:
-                rc = prepare_patchify(*static_cast<const bl_patchify_args*>(s.args), &l);
+            of[j] = static_cast<uint32_t>(k->launches.size());
+            k->launches.push_back(std::move(l));
         }
-        if (rc != BL_OK) return rc;
-        k->launches.push_back(std::move(l));
+        k->launch_of.push_back(std::move(of));
         k->labels.push_back(count == 1 ? base
                                        : base + " [" + std::to_string(i + 1) + "/" +
                                              std::to_string(count) + "]");
@@ -349,10 +421,13 @@ int add_spec(bl_kernels* k, const bl_kernel_spec& s, size_t index) {
     return BL_OK;
 }
 
-int encode_one(const bl_kernels* k, size_t kernel, cudaStream_t s, bl_timer* t, int32_t h) {
+int encode_one(const bl_kernels* k, size_t kernel, size_t set, cudaStream_t s, bl_timer* t,
+               int32_t h) {
     using namespace bl;
-    if (kernel >= k->launches.size())
-        return fail(BL_ERR_INVALID, "encode: kernel %zu of %zu", kernel, k->launches.size());
+    if (kernel >= k->launch_of.size())
+        return fail(BL_ERR_INVALID, "encode: kernel %zu of %zu", kernel, k->launch_of.size());
+    if (set >= k->sets)
+        return fail(BL_ERR_INVALID, "encode: binding set %zu of %zu", set, k->sets);
     TimerSlot* slot = nullptr;
     if (t != nullptr && h >= 0) {
         if (!valid_handle(t, h) || t->slots[h].state != SlotState::Recording)
@@ -363,7 +438,7 @@ int encode_one(const bl_kernels* k, size_t kernel, cudaStream_t s, bl_timer* t, 
                         t->max_slices);
         BL_CUDA_TRY(cudaEventRecord(slot->begin[slot->used], s));
     }
-    int rc = enqueue(k->launches[kernel], s);
+    int rc = enqueue(k->at(kernel, set), s);
     if (rc != BL_OK) return rc;
     if (slot != nullptr) {
         BL_CUDA_TRY(cudaEventRecord(slot->end[slot->used], s));
@@ -375,12 +450,32 @@ int encode_one(const bl_kernels* k, size_t kernel, cudaStream_t s, bl_timer* t, 
 
 }  // namespace
 
-extern "C" int bl_kernels_create(const bl_kernel_spec* specs, size_t n, bl_kernels** out) {
-    if (out == nullptr || (specs == nullptr && n > 0))
-        return bl::fail(BL_ERR_INVALID, "kernels: null argument");
+extern "C" int bl_kernels_create(const bl_kernel_spec* specs, size_t n, const bl_binding_set* sets,
+                                 size_t nsets, bl_kernels** out) {
+    using namespace bl;
+    if (out == nullptr || (specs == nullptr && n > 0) || (sets == nullptr && nsets > 0))
+        return fail(BL_ERR_INVALID, "kernels: null argument");
+    for (size_t j = 0; j < nsets; ++j) {
+        if (sets[j].subs == nullptr && sets[j].n > 0)
+            return fail(BL_ERR_INVALID, "kernels: binding set %zu: null substitutions", j);
+        for (size_t i = 0; i < sets[j].n; ++i) {
+            const bl_substitution& u = sets[j].subs[i];
+            if (u.from == nullptr || u.to == nullptr || u.bytes == 0)
+                return fail(BL_ERR_INVALID, "kernels: binding set %zu, substitution %zu: empty", j, i);
+            const uintptr_t f = reinterpret_cast<uintptr_t>(u.from);
+            for (size_t i2 = 0; i2 < i; ++i2) {
+                const bl_substitution& w = sets[j].subs[i2];
+                const uintptr_t g = reinterpret_cast<uintptr_t>(w.from);
+                if (f < g + w.bytes && g < f + u.bytes)
+                    return fail(BL_ERR_INVALID, "kernels: binding set %zu: substitutions %zu and "
+                                                "%zu replace overlapping tensors", j, i2, i);
+            }
+        }
+    }
     bl_kernels* k = new bl_kernels();
+    k->sets = nsets == 0 ? 1 : nsets;
     for (size_t i = 0; i < n; ++i) {
-        int rc = add_spec(k, specs[i], i);
+        int rc = add_spec(k, specs[i], i, sets, nsets);
         if (rc != BL_OK) {
             delete k;
             return rc;
@@ -392,38 +487,43 @@ extern "C" int bl_kernels_create(const bl_kernel_spec* specs, size_t n, bl_kerne
 
 extern "C" void bl_kernels_destroy(bl_kernels* k) { delete k; }
 
-extern "C" size_t bl_kernels_len(const bl_kernels* k) { return k ? k->launches.size() : 0; }
+extern "C" size_t bl_kernels_len(const bl_kernels* k) { return k ? k->launch_of.size() : 0; }
+
+extern "C" size_t bl_kernels_sets(const bl_kernels* k) { return k ? k->sets : 0; }
+
+extern "C" size_t bl_kernels_launches(const bl_kernels* k) { return k ? k->launches.size() : 0; }
 
 extern "C" const char* bl_kernels_label(const bl_kernels* k, size_t kernel) {
     if (k == nullptr || kernel >= k->labels.size()) return nullptr;
     return k->labels[kernel].c_str();
 }
 
-extern "C" int bl_kernels_encode(const bl_kernels* k, size_t kernel, void* stream, bl_timer* t,
-                                 int32_t frame) {
+extern "C" int bl_kernels_encode(const bl_kernels* k, size_t kernel, size_t set, void* stream,
+                                 bl_timer* t, int32_t frame) {
     if (k == nullptr) return bl::fail(BL_ERR_INVALID, "encode: null kernels");
-    return encode_one(k, kernel, static_cast<cudaStream_t>(stream), t, frame);
+    return encode_one(k, kernel, set, static_cast<cudaStream_t>(stream), t, frame);
 }
 
-extern "C" int bl_kernels_encode_range(const bl_kernels* k, size_t begin, size_t end, void* stream,
-                                       bl_timer* t, int32_t frame) {
-    if (k == nullptr || begin > end || end > k->launches.size())
+extern "C" int bl_kernels_encode_range(const bl_kernels* k, size_t begin, size_t end, size_t set,
+                                       void* stream, bl_timer* t, int32_t frame) {
+    if (k == nullptr || begin > end || end > k->launch_of.size())
         return bl::fail(BL_ERR_INVALID, "encode: range [%zu, %zu)", begin, end);
     for (size_t i = begin; i < end; ++i) {
-        int rc = encode_one(k, i, static_cast<cudaStream_t>(stream), t, frame);
+        int rc = encode_one(k, i, set, static_cast<cudaStream_t>(stream), t, frame);
         if (rc != BL_OK) return rc;
     }
     return BL_OK;
 }
 
-extern "C" int bl_kernels_capture(const bl_kernels* k, void* stream, bl_graph** out) {
+extern "C" int bl_kernels_capture(const bl_kernels* k, size_t set, void* stream, bl_graph** out) {
     using namespace bl;
     if (k == nullptr || out == nullptr) return fail(BL_ERR_INVALID, "capture: null argument");
+    if (set >= k->sets) return fail(BL_ERR_INVALID, "capture: binding set %zu of %zu", set, k->sets);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (s == nullptr) return fail(BL_ERR_INVALID, "capture: needs a non-default stream");
     BL_CUDA_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeRelaxed));
     int rc = BL_OK;
-    for (size_t i = 0; i < k->launches.size() && rc == BL_OK; ++i) rc = enqueue(k->launches[i], s);
+    for (size_t i = 0; i < k->launch_of.size() && rc == BL_OK; ++i) rc = enqueue(k->at(i, set), s);
     cudaGraph_t g = nullptr;
     cudaError_t e = cudaStreamEndCapture(s, &g);
     if (rc != BL_OK) {
@@ -505,16 +605,16 @@ extern "C" int bl_pass_cost_frame_run(const bl_pass_cost_args* a, bl_pass_cost_f
     if (a->variant == BL_PASS_EVERY && a->every < 1)
         return fail(BL_ERR_INVALID, "pass cost: every:k needs k >= 1");
     if (a->kernels != nullptr) {
-        if (P > a->kernels->launches.size())
+        if (P > a->kernels->launch_of.size())
             return fail(BL_ERR_INVALID, "pass cost: %u passes of a %zu-kernel program", P,
-                        a->kernels->launches.size());
+                        a->kernels->launch_of.size());
     } else if (a->sink == nullptr || a->groups < 1 || a->groups > 65535) {
         return fail(BL_ERR_INVALID, "pass cost: the trivial kernel needs a sink and 1..65535 groups");
     }
     cudaStream_t s = static_cast<cudaStream_t>(a->stream);
     const bool graph_form = a->variant == BL_PASS_ONE_PASS || a->variant == BL_PASS_ONE_PASS_PDL;
     auto launch = [&](uint32_t i, cudaStream_t st) -> int {
-        if (a->kernels != nullptr) return enqueue(a->kernels->launches[i], st);
+        if (a->kernels != nullptr) return enqueue(a->kernels->at(i, 0), st);
         if (a->variant == BL_PASS_ONE_PASS_PDL) {
             cudaLaunchConfig_t cfg{};
             cfg.gridDim = dim3(a->groups);

@@ -392,8 +392,8 @@ class Encoder:
         L2 costing more than the LayerNorm launch it replaces.
 
         ``slots``: input/output slots for that many jobs in flight
-        (``Buffers``); ``program(frames, slot=s)`` reads slot s's image and
-        writes its feature maps."""
+        (``Buffers``); ``program(frames)`` carries one binding set per slot,
+        and set s reads slot s's image and writes its feature maps."""
         import torch
         td = torch.bfloat16 if dtype == "bf16" else torch.float16
         self.cfg, self.dtype = cfg, dtype
@@ -537,12 +537,24 @@ class Encoder:
                                 "features.%d" % (i + 1), parts))
         return out
 
-    def program(self, frames: int = 1, layers: int | None = None, parts: int = 1,
-                slot: int = 0):
+    def program(self, frames: int = 1, layers: int | None = None, parts: int = 1):
+        """The encoder's kernels over the buffers of `frames` frames, with one
+        binding set per input/output slot (the reference's Net slots bound
+        through Kernels::new's sets, crates/beatlm-host/src/slots.rs:45-60):
+        set s substitutes slot s's image and feature maps for slot 0's, so
+        ``encode(k, set=s)`` runs kernel k for the job in slot s; only the
+        kernels that touch those tensors get launches of their own."""
         from .runtime import Kernels
-        key = (frames, layers, parts, slot)
+        key = (frames, layers, parts)
         if key not in self._programs:
-            self._programs[key] = Kernels(self.specs(frames, layers, parts, slot))
+            buf = self.buffers(frames)
+            n = self.cfg.layers if layers is None else layers
+            taken = [j for j, i in enumerate(self.cfg.out_indices) if i <= n]
+            sets = [[]] + [[(buf.images[0], buf.images[s])] +
+                           [(buf.slot_features[0][j], buf.slot_features[s][j]) for j in taken]
+                           for s in range(1, self.slots)]
+            self._programs[key] = Kernels(self.specs(frames, layers, parts),
+                                          sets=sets if self.slots > 1 else None)
         return self._programs[key]
 
     def features(self, frames: int, layers: int | None = None, slot: int = 0) -> list:

@@ -85,36 +85,70 @@ def split(specs: list[Spec], parts: list[int]) -> list[Spec]:
     return [dataclasses.replace(s, parts=max(1, int(p))) for s, p in zip(specs, parts)]
 
 
-class Kernels:
-    """Prebuilt launches of a program; ``len`` counts parts."""
+def _substitution(pair) -> "N.Substitution":
+    """(original, stand_in) tensors of one size, or (from_ptr, to_ptr, bytes)."""
+    if len(pair) == 3:
+        return N.Substitution(pair[0], pair[1], pair[2])
+    a, b = pair
+    nbytes = a.numel() * a.element_size()
+    if b.numel() * b.element_size() != nbytes:
+        raise ValueError("a stand-in of %d bytes for a tensor of %d bytes"
+                         % (b.numel() * b.element_size(), nbytes))
+    return N.Substitution(a.data_ptr(), b.data_ptr(), nbytes)
 
-    def __init__(self, specs: list[Spec]):
+
+class Kernels:
+    """Prebuilt launches of a program; ``len`` counts parts.
+
+    ``sets``: binding sets (Kernels::new, kernels.rs:63-184), each a list of
+    substitutions ``(original, stand_in)`` (tensors of one byte size) or
+    ``(from_ptr, to_ptr, bytes)``; none means one set binding every spec as
+    given. ``encode(..., set=j)`` runs kernel k over set j's tensors."""
+
+    def __init__(self, specs: list[Spec], sets: list | None = None):
         arr, self._labels = _spec_array(specs)
+        sets = sets or []
+        self._subs = [(N.Substitution * max(1, len(s)))(*[_substitution(p) for p in s])
+                      for s in sets]
+        bs = (N.BindingSet * max(1, len(sets)))()
+        for j, s in enumerate(sets):
+            bs[j] = N.BindingSet(self._subs[j], len(s))
         h = ctypes.c_void_p()
-        N.check(N.lib().bl_kernels_create(arr, len(specs), ctypes.byref(h)))
+        N.check(N.lib().bl_kernels_create(arr, len(specs), bs if sets else None, len(sets),
+                                          ctypes.byref(h)))
         self._h = h
         self._graphs = []
 
     def __len__(self) -> int:
         return N.lib().bl_kernels_len(self._h)
 
+    @property
+    def sets(self) -> int:
+        return N.lib().bl_kernels_sets(self._h)
+
+    @property
+    def launches(self) -> int:
+        """Distinct launches built (parts x sets, less those sets share)."""
+        return N.lib().bl_kernels_launches(self._h)
+
     def label(self, k: int) -> str:
         s = N.lib().bl_kernels_label(self._h, k)
         return s.decode() if s is not None else None
 
-    def encode(self, k: int, stream=None, timer: "SliceTimer | None" = None, frame: int = -1):
-        N.check(N.lib().bl_kernels_encode(self._h, k, _stream_ptr(stream),
+    def encode(self, k: int, stream=None, timer: "SliceTimer | None" = None, frame: int = -1,
+               set: int = 0):
+        N.check(N.lib().bl_kernels_encode(self._h, k, set, _stream_ptr(stream),
                                           timer._h if timer else None, frame))
 
     def encode_all(self, stream=None, timer: "SliceTimer | None" = None, frame: int = -1,
-                   begin: int = 0, end: int | None = None):
+                   begin: int = 0, end: int | None = None, set: int = 0):
         end = len(self) if end is None else end
-        N.check(N.lib().bl_kernels_encode_range(self._h, begin, end, _stream_ptr(stream),
+        N.check(N.lib().bl_kernels_encode_range(self._h, begin, end, set, _stream_ptr(stream),
                                                 timer._h if timer else None, frame))
 
-    def capture(self, stream) -> "Graph":
+    def capture(self, stream, set: int = 0) -> "Graph":
         g = ctypes.c_void_p()
-        N.check(N.lib().bl_kernels_capture(self._h, _stream_ptr(stream), ctypes.byref(g)))
+        N.check(N.lib().bl_kernels_capture(self._h, set, _stream_ptr(stream), ctypes.byref(g)))
         graph = Graph(g)
         self._graphs.append(graph)
         return graph

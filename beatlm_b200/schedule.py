@@ -228,26 +228,26 @@ class FrameLoop:
     so a frame-scaled model records the frame's ratio). Nothing blocks: the
     timings of a frame arrive in a later tick.
 
-    ``kernels`` is one program, or one per input/output slot (the same
-    kernels over each slot's input and output, ``model.Encoder.program(slot=
-    s)``): job j runs on slot j % slots, as the reference's Net does
-    (crates/beatlm-host/src/slots.rs:1-30), so up to ``slots`` jobs in
-    flight keep their own input and output."""
+    ``kernels`` is one program (``runtime.Kernels``) with one binding set per
+    input/output slot (``model.Encoder.program``): job j runs with set
+    j % sets, as the reference's Net binds its slots
+    (crates/beatlm-host/src/slots.rs:1-60), so up to ``sets`` jobs in flight
+    keep their own input and output."""
 
     def __init__(self, kernels, scheduler: Scheduler, cost, timer):
-        self.programs = list(kernels) if isinstance(kernels, (list, tuple)) else [kernels]
+        self.kernels = kernels
         self.scheduler, self.cost, self.timer = scheduler, cost, timer
         self._planned = {}
 
     def slot_of(self, job: int) -> int:
-        return job % len(self.programs)
+        return job % self.kernels.sets
 
     def tick(self, frame: FrameInfo, budget: int, submit: bool, stream=None,
              write_input=None) -> FramePlan:
         """``write_input(slot)``, when given, fills the new job's input slot
         before the frame's slices are encoded."""
         if submit:
-            job = self.scheduler.submit(frame, list(range(len(self.programs[0]))), self.cost)
+            job = self.scheduler.submit(frame, list(range(len(self.kernels))), self.cost)
             if write_input is not None:
                 write_input(self.slot_of(job))
         plan = self.scheduler.plan_frame(frame, budget, self.cost)
@@ -255,9 +255,8 @@ class FrameLoop:
         if handle >= 0:
             self._planned[frame.index] = self.cost.plan_frame({r.slice for r in plan.runs})
         for r in plan.runs:
-            self.programs[self.slot_of(r.job)].encode(r.slice, stream,
-                                                      self.timer if handle >= 0 else None,
-                                                      handle)
+            self.kernels.encode(r.slice, stream, self.timer if handle >= 0 else None, handle,
+                                set=self.slot_of(r.job))
         if handle >= 0:
             self.timer.submitted(handle)
         self.collect()

@@ -459,15 +459,41 @@ typedef struct bl_kernel_spec {
 typedef struct bl_kernels bl_kernels;
 
 /*
+ * A binding set: tensors of the specs replaced by stand-ins of the same size
+ * (the reference's Substitution = (TensorId, TensorId),
+ * crates/beatlm/src/codegen/kernels.rs:21-26, for a host that keeps one copy
+ * of an input or output per job in flight). Tensors are device ranges here:
+ * every pointer argument of a spec that points into [from, from + bytes) is
+ * moved to the same offset from `to`. The ranges of one set must not overlap.
+ */
+typedef struct bl_substitution {
+    const void* from;
+    void* to;
+    uint64_t bytes;
+} bl_substitution;
+typedef struct bl_binding_set {
+    const bl_substitution* subs;
+    size_t n;
+} bl_binding_set;
+
+/*
  * Builds every launch of a program once: validates each spec, splits it into
  * its parts, encodes the TMA tensor maps and packs the kernel parameters
- * (Kernels::new, crates/beatlm/src/codegen/kernels.rs:63-184). Afterwards
- * encoding does no host work beyond the launch. Kernel i of the result is a
- * part; bl_kernels_len counts parts.
+ * (Kernels::new, crates/beatlm/src/codegen/kernels.rs:63-184), for every
+ * binding set: nsets = 0 means one set that binds every spec as given.
+ * A kernel that touches none of a set's substituted tensors shares one
+ * launch between the sets (the reference shares its bind group).
+ * Afterwards encoding does no host work beyond the launch. Kernel i of the
+ * result is a part; bl_kernels_len counts parts.
  */
-int bl_kernels_create(const bl_kernel_spec* specs, size_t n, bl_kernels** out);
+int bl_kernels_create(const bl_kernel_spec* specs, size_t n, const bl_binding_set* sets,
+                      size_t nsets, bl_kernels** out);
 void bl_kernels_destroy(bl_kernels* k);
 size_t bl_kernels_len(const bl_kernels* k);
+/* Kernels::sets (kernels.rs:200): how many binding sets (at least 1). */
+size_t bl_kernels_sets(const bl_kernels* k);
+/* How many distinct launches were built (parts x sets, less the shared). */
+size_t bl_kernels_launches(const bl_kernels* k);
 /* The spec's label with " [i/n]" appended for a part; NULL out of range. */
 const char* bl_kernels_label(const bl_kernels* k, size_t kernel);
 /* KernelSpec::max_parts (crates/beatlm-core/src/kernel.rs:1975): how many
@@ -486,23 +512,24 @@ int bl_program_parts_within(const bl_kernel_spec* specs, size_t n, const uint64_
 typedef struct bl_timer bl_timer;
 
 /*
- * Enqueues kernel `kernel` on `stream` (Kernels::encode, kernels.rs:217-233).
- * When `timer` is non-NULL and `frame` >= 0 (a handle from
- * bl_timer_begin_frame), the launch is bracketed by the frame's next pair of
- * cudaEvents, the compute-pass timestamp writes of the reference
- * (FrameTimestamps::compute_pass, gpu/timer.rs:507).
+ * Enqueues kernel `kernel` with binding set `set` on `stream`
+ * (Kernels::encode, kernels.rs:217-233; an index past those built is
+ * BL_ERR_INVALID and enqueues nothing). When `timer` is non-NULL and `frame`
+ * >= 0 (a handle from bl_timer_begin_frame), the launch is bracketed by the
+ * frame's next pair of cudaEvents, the compute-pass timestamp writes of the
+ * reference (FrameTimestamps::compute_pass, gpu/timer.rs:507).
  */
-int bl_kernels_encode(const bl_kernels* k, size_t kernel, void* stream, bl_timer* timer,
-                      int32_t frame);
+int bl_kernels_encode(const bl_kernels* k, size_t kernel, size_t set, void* stream,
+                      bl_timer* timer, int32_t frame);
 /* Kernels [begin, end) in order, each timed as bl_kernels_encode does. */
-int bl_kernels_encode_range(const bl_kernels* k, size_t begin, size_t end, void* stream,
-                            bl_timer* timer, int32_t frame);
+int bl_kernels_encode_range(const bl_kernels* k, size_t begin, size_t end, size_t set,
+                            void* stream, bl_timer* timer, int32_t frame);
 
 /* The whole program captured once into a CUDA graph (relaxed capture on
  * `stream`), replayed with one launch: the launch-bound ViT-S encoder's way
  * of paying the per-kernel launch cost once per frame instead of per kernel. */
 typedef struct bl_graph bl_graph;
-int bl_kernels_capture(const bl_kernels* k, void* stream, bl_graph** out);
+int bl_kernels_capture(const bl_kernels* k, size_t set, void* stream, bl_graph** out);
 int bl_graph_launch(const bl_graph* g, void* stream);
 void bl_graph_destroy(bl_graph* g);
 

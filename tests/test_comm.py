@@ -47,11 +47,19 @@ def _rank(rank, world, uid, workdir, lib, script, q):
         recv = (ctypes.c_uint8 * (16 * world))()
         try:
             if script.get("as_spec"):
+                # binding set 1 sends from `other` and receives into `recv2`
                 from beatlm_b200.runtime import Kernels, Spec
+                other = (ctypes.c_uint8 * 16)(*[(rank * 16 + i + 7) % 256 for i in range(16)])
+                recv2 = (ctypes.c_uint8 * (16 * world))()
                 k = Kernels([Spec(c.args(ctypes.addressof(send), ctypes.addressof(recv), 16),
-                                  "exchange")])
+                                  "exchange")],
+                            sets=[[], [(ctypes.addressof(send), ctypes.addressof(other), 16),
+                                       (ctypes.addressof(recv), ctypes.addressof(recv2),
+                                        16 * world)]])
                 out["len"] = len(k)
                 k.encode(0, stream=0)
+                k.encode(0, stream=0, set=1)
+                out["recv2"] = bytes(recv2)
             else:
                 c.all_gather(ctypes.addressof(send), ctypes.addressof(recv), 16)
             out["recv"] = bytes(recv)
@@ -112,9 +120,12 @@ def test_ranks_that_join_gather_each_others_bytes(fake_nccl, tmp_path, world):
 
 
 def test_the_all_gather_encodes_as_a_kernel_spec(fake_nccl, tmp_path):
+    """Set 0 as built; set 1 (a binding set) swaps both buffers."""
     res, _ = _run(2, fake_nccl, tmp_path, {"as_spec": True})
+    want2 = bytes((r * 16 + i + 7) % 256 for r in range(2) for i in range(16))
     for r in range(2):
         assert res[r]["len"] == 1 and res[r].get("recv") == _want(2), res[r]
+        assert res[r]["recv2"] == want2
 
 
 def test_a_rank_that_never_joins_times_out_and_aborts(fake_nccl, tmp_path):

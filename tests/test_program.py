@@ -51,3 +51,34 @@ def test_the_part_count_is_the_duration_over_the_bound_rounded_up_and_clamped():
                                    (2 ** 64 - 1, 1, 1000), (2 ** 64 - 1, 1000, 1000)]:
         assert parts_within(duration, bound, 1000) == parts, (duration, bound)
     assert parts_within(1, 0, 1000) == 0  # ZeroBound
+
+
+def test_binding_sets_rebind_only_the_kernels_that_touch_their_tensors():
+    """Kernels::new's binding sets (crates/beatlm/src/codegen/kernels.rs:63-184)
+    on all-gather specs, which need no device to build: a set that
+    substitutes a tensor a kernel reads or writes gives that kernel a launch
+    of its own; a kernel that touches none shares set 0's launch. Nothing is
+    encoded (the communicator handle is never used at build time)."""
+    import ctypes
+    from beatlm_b200 import _native as N
+    from beatlm_b200.runtime import Kernels, Spec
+    bufs = [(ctypes.c_uint8 * 64)() for _ in range(6)]
+    a = [ctypes.addressof(b) for b in bufs]
+    comm = 0x1000  # a handle: only stored at build time
+    specs = [Spec(N.AllGatherArgs(comm=comm, send=a[0], recv=a[1], bytes=16), "first"),
+             Spec(N.AllGatherArgs(comm=comm, send=a[2] + 8, recv=a[3], bytes=16), "second")]
+    k = Kernels(specs)
+    assert (len(k), k.sets, k.launches) == (2, 1, 2)
+    # set 1 replaces buffer 1 (only the first kernel's), set 2 buffer 2
+    # (the second kernel reads 8 bytes into it)
+    k = Kernels(specs, sets=[[], [(a[1], a[4], 64)], [(a[2], a[5], 64)]])
+    assert (len(k), k.sets, k.launches) == (2, 3, 4)
+    with pytest.raises(N.BackendError, match="binding set 3 of 3"):
+        k.encode(0, stream=0, set=3)
+    with pytest.raises(N.BackendError, match="overlapping"):
+        Kernels(specs, sets=[[(a[1], a[4], 64), (a[1] + 32, a[5], 16)]])
+    with pytest.raises(N.BackendError, match="empty"):
+        Kernels(specs, sets=[[(a[1], a[4], 0)]])
+    with pytest.raises(ValueError, match="stand-in"):
+        import torch
+        Kernels(specs, sets=[[(torch.zeros(4), torch.zeros(8))]])

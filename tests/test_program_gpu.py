@@ -310,8 +310,9 @@ def test_the_frame_loop_schedules_timed_slices_and_learns_their_costs():
 
 
 def test_jobs_in_flight_keep_their_own_input_and_output_slots():
-    """The reference's Net slots (crates/beatlm-host/src/slots.rs:1-30) on
-    the encoder: three slots for latency 2, each job a different image, a
+    """The reference's Net slots (crates/beatlm-host/src/slots.rs:1-60) on
+    the encoder, bound as binding sets of one program: three slots for
+    latency 2, each job a different image, a
     budget of three quarters of a job per frame, so a job spreads over two
     frames and the next one's input is written while it still runs. Every delivered job's features equal a direct
     forward pass of its own image."""
@@ -338,10 +339,15 @@ def test_jobs_in_flight_keep_their_own_input_and_output_slots():
         want.append(enc.forward(img, frames=1)[0].clone())
     torch.cuda.synchronize()
     buf = enc.buffers(1)
-    programs = [enc.program(1, slot=s) for s in range(slots)]
+    program = enc.program(1)
+    assert program.sets == slots
+    # only the kernels that read the image or write a feature map get a
+    # launch per slot: patchify and the feature LayerNorm here
+    assert program.launches == len(program) + (slots - 1) * 2
+    programs = [program]
     # measured costs first, so the budget below splits a job over two frames
     cost = CostModel(1)
-    loop = FrameLoop(programs, Scheduler(policy, "hold_previous", 0), cost,
+    loop = FrameLoop(program, Scheduler(policy, "hold_previous", 0), cost,
                      SliceTimer(max_slices=2 * len(programs[0])))
     per_job = None
     got, submitted = {}, [0]
