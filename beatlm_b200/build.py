@@ -73,9 +73,30 @@ def build(force: bool = False, verbose: bool = False) -> str:
     return LIB
 
 
+C_HOST = os.path.join(HERE, "c_host")
+
+
+def build_c_host(force: bool = False) -> str:
+    """The C-ABI-only host program ``c_host/vit_block.c`` (gcc, linked
+    against the library, found beside it at run time), as
+    ``_build/vit_block``; builds the library first."""
+    lib = build(force)
+    src = os.path.join(C_HOST, "vit_block.c")
+    exe = os.path.join(BUILD, "vit_block")
+    if force or _stale(exe, [src, lib, os.path.join(INCLUDE, "beatlm_b200.h")]):
+        cmd = ["gcc", "-O2", "-std=c11", "-Wall", "-I", INCLUDE, src, "-o", exe + ".tmp",
+               "-L", HERE, "-lbeatlm_b200", "-Wl,-rpath,$ORIGIN/..", "-lm"]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError("gcc failed for %s:\n%s%s" % (src, r.stdout, r.stderr))
+        os.replace(exe + ".tmp", exe)
+    return exe
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true")
     a = ap.parse_args()
     print(build(a.force, a.verbose))
+    print(build_c_host(a.force))
