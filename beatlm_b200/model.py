@@ -225,19 +225,19 @@ class Buffers:
                 [alloc("features.%d.s%d" % (i, slot), (frames * (t - 1), cfg.dim), torch.float32)
                  for i in cfg.out_indices] if features else [])
 
-    # Lifetimes for the static plan, in kernel-spec order of the encoder
-    # program (spec 0 patchify, spec 1 patch GEMM, blocks from spec 2). The
-    # image is refilled by the host every frame and the features are read
-    # after it, so both live for the whole program, as do the weights and
-    # the residual stream; the patch matrix dies at the patch GEMM and the
-    # block scratch is born at the first block, so those may share bytes.
     @staticmethod
-    def lifetime(name: str, last: int) -> tuple[int, int]:
-        if name == "patches":
-            return 0, 1
-        if name in ("qkv", "o", "xn", "h", "stats1", "stats2"):
-            return 2, last
-        return 0, last
+    def lifetime(name: str, used: list) -> tuple[int, int]:
+        """A buffer's lifetime in launch order, from the launches that bind
+        it (``used``: the buffer names of each launch; the reference's rule
+        that lifetimes come from the kernels, kernel.rs:67-79). Images and
+        feature maps are the program's inputs and outputs, written and read
+        by the host between passes, so they live for the whole program, as
+        does a buffer no launch binds."""
+        last = len(used) - 1
+        if name.startswith("image") or name.startswith("features"):
+            return 0, last
+        hits = [i for i, names in enumerate(used) if name in names]
+        return (hits[0], hits[-1]) if hits else (0, last)
 
 
 def _on_stream(stream):
@@ -255,101 +255,265 @@ def _weights_gemm(w, **kw):
     return ops.gemm_args(w, weights_static=True, **kw)
 
 
-def norm_epilogue_fits(rows: int, dim: int) -> bool:
+def norm_epilogue_fits(rows: int, dim: int, sms: int | None = None) -> bool:
     """Whether a GEMM writing `rows` x `dim` can carry the epilogue LayerNorm:
-    every 32-column tile must be resident at once, one per SM."""
-    import torch
-    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    every 32-column tile must be resident at once, one per SM (`sms`: the
+    device's count, queried when not given)."""
+    if sms is None:
+        import torch
+        sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
     return dim <= 512 and -(-rows // 128) * (dim // 32) <= sms
 
 
+# ------------------------------------------------------------------ graphs
+# The reference's graph builders (crates/beatlm/src/model/depth_anything_v2.rs:
+# block / layer_of 252-427, encoder 435-545) over graph.py's operations; the
+# program the device runs is what graph.Graph.lower makes of them.
+
+BLOCK_ACTS = ("n1", "qkv", "scores", "scaled", "probs", "values", "proj", "ls1x", "x1",
+              "n2", "hidden", "act", "out", "ls2x")
+
+
+def add_block(g, cfg: ViTConfig, x: int, base: int, name: str, out: int,
+              out_role: str = "activation") -> dict:
+    """One pre-norm block (reference.rs:520-544) on residual stream `x`,
+    writing `out`; weights at ids base + i in BLOCK_NAMES order, activations
+    at base + 20 + i in BLOCK_ACTS order. Returns the ids by name."""
+    from . import graph as G
+    t, d, m, h, hd = cfg.tokens, cfg.dim, cfg.mlp, cfg.heads, cfg.head_dim
+    sizes = {"norm1_g": d, "norm1_b": d, "qkv_w": d * 3 * d, "qkv_b": 3 * d, "proj_w": d * d,
+             "proj_b": d, "ls1": d, "norm2_g": d, "norm2_b": d, "fc1_w": d * m, "fc1_b": m,
+             "fc2_w": m * d, "fc2_b": d, "ls2": d}
+    ids = {k: g.tensor(base + i, G.WEIGHT, sizes[k]) for i, k in enumerate(BLOCK_NAMES)}
+    act_sizes = {"n1": t * d, "qkv": t * 3 * d, "scores": t * h * t, "scaled": t * h * t,
+                 "probs": t * h * t, "values": t * d, "proj": t * d, "ls1x": t * d, "x1": t * d,
+                 "n2": t * d, "hidden": t * m, "act": t * m, "out": t * d, "ls2x": t * d}
+    for i, k in enumerate(BLOCK_ACTS):
+        ids[k] = g.tensor(base + 20 + i, G.ACTIVATION, act_sizes[k])
+    g.tensor(out, out_role, t * d)
+    ids["x"], ids["y"] = x, out
+    ln = lambda inp, gm, bt: G.LayerNorm(inp, gm, bt, t, d, cfg.eps)
+    g.op(ln(x, ids["norm1_g"], ids["norm1_b"]), ids["n1"], name + "norm1")
+    g.op(G.MatMul(ids["n1"], ids["qkv_w"], ids["qkv_b"], t, d, 3 * d), ids["qkv"], name + "qkv")
+    g.op(G.AttentionScores(ids["qkv"], t, h, hd), ids["scores"], name + "attention")
+    g.op(G.Scale(ids["scores"], 1.0 / math.sqrt(hd), t * h * t), ids["scaled"], name + "scale")
+    g.op(G.Softmax(ids["scaled"], t * h, t), ids["probs"], name + "softmax")
+    g.op(G.AttentionValues(ids["probs"], ids["qkv"], t, h, hd), ids["values"], name + "values")
+    g.op(G.MatMul(ids["values"], ids["proj_w"], ids["proj_b"], t, d, d), ids["proj"],
+         name + "proj")
+    g.op(G.ChannelScale(ids["proj"], ids["ls1"], t, d), ids["ls1x"], name + "ls1")
+    g.op(G.Add(ids["ls1x"], x, t * d), ids["x1"], name + "residual1")
+    g.op(ln(ids["x1"], ids["norm2_g"], ids["norm2_b"]), ids["n2"], name + "norm2")
+    g.op(G.MatMul(ids["n2"], ids["fc1_w"], ids["fc1_b"], t, d, m), ids["hidden"], name + "fc1")
+    g.op(G.GeluErf(ids["hidden"], t * m), ids["act"], name + "gelu")
+    g.op(G.MatMul(ids["act"], ids["fc2_w"], ids["fc2_b"], t, m, d), ids["out"], name + "fc2")
+    g.op(G.ChannelScale(ids["out"], ids["ls2"], t, d), ids["ls2x"], name + "ls2")
+    g.op(G.Add(ids["x1"], ids["ls2x"], t * d), out, name + "residual2")
+    return ids
+
+
+def block_graph(cfg: ViTConfig):
+    """One block as a graph of its own: input x (id 0), output y (id 1)."""
+    from . import graph as G
+    g = G.Graph()
+    g.tensor(0, G.INPUT, cfg.tokens * cfg.dim)
+    ids = add_block(g, cfg, 0, 100, "block0.", 1, G.OUTPUT)
+    return g, [ids]
+
+
+def encoder_graph(cfg: ViTConfig, layers: int | None = None):
+    """The encoder (depth_anything_v2.rs:435-545): PatchEmbed, the class
+    token, the position Add, the blocks, and after each block of
+    out_indices the final LayerNorm and TokensToMap (a graph output). Ids:
+    image 1, patch weights 2/3, class token 4, positions 5, final norm 6/7,
+    embedding activations 10-12, block i at 1000 (i + 1), features 90000 + j
+    (normalised rows) and 91000 + j (maps). Returns (graph, block ids,
+    feature map ids)."""
+    from . import graph as G
+    t, d, n = cfg.tokens, cfg.dim, cfg.layers if layers is None else layers
+    g = G.Graph()
+    g.tensor(1, G.INPUT, cfg.side * cfg.side * cfg.cin)
+    for i, sz in ((2, cfg.taps * d), (3, d), (4, d), (5, t * d), (6, d), (7, d)):
+        g.tensor(i, G.WEIGHT, sz)
+    for i, sz in ((10, (t - 1) * d), (11, t * d), (12, t * d)):
+        g.tensor(i, G.ACTIVATION, sz)
+    g.op(G.PatchEmbed(1, 2, 3, cfg.grid, cfg.grid, cfg.patch, cfg.cin, d), 10, "embed")
+    g.op(G.PrependToken(4, 10, t - 1, d), 11, "embed.cls")
+    g.op(G.Add(11, 5, t * d), 12, "embed.pos")
+    x, blocks, maps = 12, [], []
+    for i in range(n):
+        base = 1000 * (i + 1)
+        ids = add_block(g, cfg, x, base, "block%d." % i, base + 99)
+        blocks.append(ids)
+        x = ids["y"]
+        if (i + 1) in cfg.out_indices:
+            j = cfg.out_indices.index(i + 1)
+            g.tensor(90000 + j, G.ACTIVATION, t * d)
+            g.tensor(91000 + j, G.OUTPUT, (t - 1) * d)
+            g.op(G.LayerNorm(x, 6, 7, t, d, cfg.eps), 90000 + j, "features.%d" % (i + 1))
+            g.op(G.TokensToMap(90000 + j, t, d), 91000 + j, "features.%d.map" % (i + 1))
+            maps.append(91000 + j)
+    return g, blocks, maps
+
+
+def lowering_forms(fused_ln, rows: int, dim: int, sms: int | None = None) -> tuple:
+    """The fused forms graph.Graph.lower applies for a LayerNorm placement:
+    False (standalone LayerNorms, the fastest measured at ViT-S), True
+    (LayerNorm prologues fed by the previous GEMM's row statistics) or
+    "epilogue" (LayerNorms as a second output of the GEMM before them, where
+    every column tile fits on the device at once; otherwise as False)."""
+    from .graph import B200_FORMS
+    if fused_ln == "epilogue":
+        return B200_FORMS + (("ln_epilogue",) if norm_epilogue_fits(rows, dim, sms) else ())
+    return B200_FORMS + (("ln_prologue",) if fused_ln else ())
+
+
+class _Binder:
+    """Launches for a lowered program: each kernel's tensors bound to device
+    buffers (``bind``: tensor id -> (buffer name, tensor)), its main
+    operation, prologue and epilogue turned into the C ABI's arguments. A
+    PatchEmbed kernel becomes two launches (the patch matrix with the class
+    rows, then its GEMM). Records which buffers each launch binds, from which
+    the memory plan's lifetimes follow (rule 1: lifetimes come from the
+    kernels)."""
+
+    def __init__(self, program, bind: dict, cfg: ViTConfig, dtype: str, frames: int,
+                 extra: dict, parts: int = 1):
+        self.program, self.bind, self.cfg = program, bind, cfg
+        self.dtype, self.frames, self.parts, self.extra = dtype, frames, parts, extra
+        # tensors a LayerNorm prologue reads: their writer adds row statistics
+        self.stats_read = {k.main.a for k in program.kernels
+                           if k.prologue and k.prologue[0].kind == "layernorm"}
+
+    def t(self, tid):
+        return None if tid is None else self.bind[tid][1]
+
+    def names(self, *tids):
+        return {self.bind[t][0] for t in tids if t is not None and t in self.bind}
+
+    def specs(self) -> tuple[list, list]:
+        """(specs, buffer names each spec binds)."""
+        from . import graph as G
+        from .runtime import Spec
+        out, used = [], []
+        cfg, frames = self.cfg, self.frames
+        t = cfg.tokens
+        for k in self.program.kernels:
+            main, label = k.main, k.label
+            steps = {e.kind: e for e in k.epilogue}
+            if isinstance(main, G.PatchEmbed):
+                cls, pos = steps["prepend_token"].tensor, steps["add"].tensor
+                image, x, patches = self.t(main.input), self.t(k.output), self.extra["patches"]
+                out.append(Spec(ops.patchify_args(image, frames=frames, side=cfg.side,
+                                                  patch=cfg.patch, cin=cfg.cin, k_pad=cfg.k_pad,
+                                                  a_out=patches, a_dtype=self.dtype,
+                                                  cls=self.t(cls), pos=self.t(pos), x=x),
+                                "embed.patchify"))
+                used.append(self.names(main.input, cls, pos, k.output) | {"patches"})
+                out.append(Spec(_weights_gemm(self.t(main.weights), a=patches,
+                                              bias=self.t(main.bias), residual=self.t(pos),
+                                              res_period=t, out=x, out_row_offset=1,
+                                              out_group=(t - 1, 1)), "embed.patch", self.parts))
+                used.append(self.names(main.weights, main.bias, pos, k.output) | {"patches"})
+            elif isinstance(main, G.LayerNorm):
+                kw = dict(in_row_offset=1, in_group=(t - 1, 1)) if "tokens_to_map" in steps else {}
+                out.append(Spec(ops.layernorm_args(self.t(main.input), self.t(main.gamma),
+                                                   self.t(main.beta), main.eps,
+                                                   out=self.t(k.output), **kw),
+                                label, self.parts))
+                used.append(self.names(main.input, main.gamma, main.beta, k.output))
+            elif isinstance(main, G.Attention):
+                out.append(Spec(ops.attention_args(self.t(main.qkv), tokens=t, heads=cfg.heads,
+                                                   head_dim=cfg.head_dim, batch=frames,
+                                                   qk_dtype=self.dtype, out=self.t(k.output)),
+                                label, self.parts))
+                used.append(self.names(main.qkv, k.output))
+            elif isinstance(main, G.MatMul):
+                kw = {}
+                names = self.names(main.b, main.bias, k.output)
+                if k.prologue:
+                    p = k.prologue[0]
+                    kw["ln"] = (self.t(main.a), self.t(p.tensor), self.t(p.beta), p.value)
+                    kw["ln_stats"] = self.extra["stats"][main.a]
+                    names |= self.names(main.a, p.tensor, p.beta)
+                    names |= {self.extra["stats_name"][main.a]}
+                else:
+                    kw["a"] = self.t(main.a)
+                    names |= self.names(main.a)
+                if "gelu_erf" in steps:
+                    kw["act"] = "gelu_erf"
+                if "channel_scale" in steps:
+                    kw["chan_scale"] = self.t(steps["channel_scale"].tensor)
+                    names |= self.names(steps["channel_scale"].tensor)
+                if "add" in steps:
+                    kw["residual"] = self.t(steps["add"].tensor)
+                    names |= self.names(steps["add"].tensor)
+                if "layernorm" in steps:
+                    e = steps["layernorm"]
+                    kw["norm"] = (self.t(e.tensor), self.t(e.beta), e.value, self.t(e.out))
+                    kw["norm_sync"] = self.extra["norm_sync"]
+                    names |= self.names(e.tensor, e.beta, e.out) | {"norm_sync"}
+                if k.output in self.stats_read:
+                    kw["stats_out"] = self.extra["stats"][k.output]
+                    names |= {self.extra["stats_name"][k.output]}
+                if self.bind[k.output][0] == "qkv":  # packed Q|K|V: V in f16
+                    kw["out_dtype"], kw["out_split"] = self.dtype, (2 * cfg.dim, "f16")
+                out.append(Spec(_weights_gemm(self.t(main.b), bias=self.t(main.bias),
+                                              out=self.t(k.output), **kw), label, self.parts))
+                used.append(names)
+            else:
+                raise ValueError("no launch for kernel %s" % k.name())
+        return out, used
+
+
+def _block_binding(ids: dict, blk: "DeviceBlock", buf: "Buffers") -> dict:
+    """A block's tensors on the buffers: the residual stream (x, x1, y) in
+    place in buf.x (each epilogue reads a residual element and writes the
+    same element), both LayerNorms' rows in buf.xn, and the weights."""
+    w = {"norm1_g": blk.norm1[0], "norm1_b": blk.norm1[1], "qkv_w": blk.qkv_w,
+         "qkv_b": blk.qkv_b, "proj_w": blk.proj_w, "proj_b": blk.proj_b, "ls1": blk.ls1,
+         "norm2_g": blk.norm2[0], "norm2_b": blk.norm2[1], "fc1_w": blk.fc1_w,
+         "fc1_b": blk.fc1_b, "fc2_w": blk.fc2_w, "fc2_b": blk.fc2_b, "ls2": blk.ls2}
+    bind = {ids[k]: ("weight", v) for k, v in w.items()}
+    for k, name in (("x", "x"), ("x1", "x"), ("y", "x"), ("n1", "xn"), ("n2", "xn"),
+                    ("qkv", "qkv"), ("values", "o"), ("act", "h")):
+        bind[ids[k]] = (name, getattr(buf, name))
+    return bind
+
+
+def _stats(blocks: list, buf: "Buffers") -> tuple[dict, dict]:
+    """Row-statistics buffers of the residual stream's tensors: stats2 for
+    each block's x1, stats1 for the stream between blocks."""
+    stats, names = {}, {}
+    for ids in blocks:
+        for k, sb in (("x", "stats1"), ("y", "stats1"), ("x1", "stats2")):
+            stats[ids[k]], names[ids[k]] = getattr(buf, sb), sb
+    return stats, names
+
+
 def block_specs(blk: DeviceBlock, cfg: ViTConfig, buf: Buffers, layer: int = 0,
-                parts: int = 1, fused_ln=False, next_norm=None) -> list:
-    """The fused kernels of one pre-norm block (reference.rs:520-544), in
-    place on ``buf.x``:
+                parts: int = 1, fused_ln=False, sms: int | None = None) -> list:
+    """The kernels of one pre-norm block (reference.rs:520-544) in place on
+    ``buf.x``, as graph.Graph.lower makes them of the block's graph:
     x1 = x + ls1 * proj(attention(norm1(x))); x = x1 + ls2 * fc2(gelu(fc1(norm2(x1)))).
 
-    ``fused_ln=False`` (7 kernels): each LayerNorm is its own bandwidth-bound
-    kernel writing 16-bit rows that the next GEMM loads by TMA.
-    ``fused_ln=True`` (5 kernels; 7 for block 0): the GEMM that writes x also
-    writes each row's partial statistics (proj for norm2, the previous block's
-    fc2 for norm1: ``buf.stats2`` / ``buf.stats1``), and the QKV / fc1 GEMM
-    normalises its A operand from x in its prologue with them, so no
-    LayerNorm launch and no pass over the rows remain. Block 0's norm1 reads
-    the embedding's output, for which no statistics exist: it stays a
-    standalone LayerNorm.
-    ``fused_ln="epilogue"`` (5 kernels; 6 for block 0): proj writes x and
-    norm2(x) (``buf.xn``), fc2 writes x and ``next_norm`` (the next block's
-    norm1 weights; none for the last block) of it, each LayerNorm computed in
-    the GEMM's epilogue from statistics its column tiles exchange; QKV and
-    fc1 load ``buf.xn`` by TMA. Where the GEMM has more 32-column tiles than
-    the device has SMs (``norm_epilogue_fits``) the block is built as with
-    ``fused_ln=False``."""
-    from .runtime import Spec
-    d = cfg.dim
-    name = "block%d." % layer
-    attn = Spec(ops.attention_args(buf.qkv, tokens=buf.tokens, heads=cfg.heads,
-                                   head_dim=cfg.head_dim, batch=buf.frames, qk_dtype=blk.dtype,
-                                   out=buf.o), name + "attention", parts)
-    if fused_ln == "epilogue" and not norm_epilogue_fits(buf.rows, d):
-        fused_ln = False
-    if fused_ln == "epilogue":
-        ep = lambda w: None if w is None else (w[0], w[1], cfg.eps, buf.xn)
-        head = ([Spec(ops.layernorm_args(buf.x, blk.norm1[0], blk.norm1[1], cfg.eps, out=buf.xn),
-                      name + "norm1", parts)] if layer == 0 else [])
-        return head + [
-            Spec(_weights_gemm(blk.qkv_w, a=buf.xn, bias=blk.qkv_b, out=buf.qkv,
-                               out_dtype=blk.dtype, out_split=(2 * d, "f16")), name + "qkv", parts),
-            attn,
-            Spec(_weights_gemm(blk.proj_w, a=buf.o, bias=blk.proj_b, chan_scale=blk.ls1,
-                               residual=buf.x, out=buf.x, norm=ep(blk.norm2),
-                               norm_sync=buf.norm_sync), name + "proj", parts),
-            Spec(_weights_gemm(blk.fc1_w, a=buf.xn, bias=blk.fc1_b, act="gelu_erf", out=buf.h),
-                 name + "fc1", parts),
-            Spec(_weights_gemm(blk.fc2_w, a=buf.h, bias=blk.fc2_b, chan_scale=blk.ls2,
-                               residual=buf.x, out=buf.x, norm=ep(next_norm),
-                               norm_sync=buf.norm_sync if next_norm is not None else None),
-                 name + "fc2", parts),
-        ]
-    stats = (lambda s: s) if fused_ln else (lambda s: None)
-    proj = Spec(_weights_gemm(blk.proj_w, a=buf.o, bias=blk.proj_b, chan_scale=blk.ls1,
-                              residual=buf.x, out=buf.x, stats_out=stats(buf.stats2)),
-                name + "proj", parts)
-    fc2 = Spec(_weights_gemm(blk.fc2_w, a=buf.h, bias=blk.fc2_b, chan_scale=blk.ls2,
-                             residual=buf.x, out=buf.x, stats_out=stats(buf.stats1)),
-               name + "fc2", parts)
-    if fused_ln:
-        if layer == 0:
-            head = [
-                Spec(ops.layernorm_args(buf.x, blk.norm1[0], blk.norm1[1], cfg.eps, out=buf.xn),
-                     name + "norm1", parts),
-                Spec(_weights_gemm(blk.qkv_w, a=buf.xn, bias=blk.qkv_b, out=buf.qkv,
-                                   out_dtype=blk.dtype, out_split=(2 * d, "f16")),
-                     name + "qkv", parts)]
-        else:
-            head = [Spec(_weights_gemm(blk.qkv_w, ln=(buf.x, blk.norm1[0], blk.norm1[1], cfg.eps),
-                                       ln_stats=buf.stats1, bias=blk.qkv_b, out=buf.qkv,
-                                       out_dtype=blk.dtype, out_split=(2 * d, "f16")),
-                         name + "qkv", parts)]
-        return head + [
-            attn, proj,
-            Spec(_weights_gemm(blk.fc1_w, ln=(buf.x, blk.norm2[0], blk.norm2[1], cfg.eps),
-                               ln_stats=buf.stats2, bias=blk.fc1_b, act="gelu_erf", out=buf.h),
-                 name + "fc1", parts),
-            fc2,
-        ]
-    return [
-        Spec(ops.layernorm_args(buf.x, blk.norm1[0], blk.norm1[1], cfg.eps, out=buf.xn),
-             name + "norm1", parts),
-        Spec(_weights_gemm(blk.qkv_w, a=buf.xn, bias=blk.qkv_b, out=buf.qkv, out_dtype=blk.dtype,
-                           out_split=(2 * d, "f16")), name + "qkv", parts),
-        attn, proj,
-        Spec(ops.layernorm_args(buf.x, blk.norm2[0], blk.norm2[1], cfg.eps, out=buf.xn),
-             name + "norm2", parts),
-        Spec(_weights_gemm(blk.fc1_w, a=buf.xn, bias=blk.fc1_b, act="gelu_erf", out=buf.h),
-             name + "fc1", parts),
-        fc2,
-    ]
+    ``fused_ln`` (``lowering_forms``): False gives 7 kernels (each LayerNorm
+    a kernel of its own writing 16-bit rows the next GEMM loads by TMA);
+    True and "epilogue" fold norm2 into the GEMM after it (a prologue fed by
+    the out-projection's row statistics) or before it (a second output of
+    the out-projection): 6 kernels. The block's input is the graph's input,
+    written by no kernel, so norm1 stays a kernel of its own either way."""
+    from .graph import Fusion
+    g, blocks = block_graph(cfg)
+    forms = lowering_forms(fused_ln, buf.rows, cfg.dim, sms)
+    prog = g.lower(Fusion.ON, forms)
+    for k in prog.kernels:
+        k.label = k.label.replace("block0.", "block%d." % layer)
+    stats, stats_name = _stats(blocks, buf)
+    extra = {"stats": stats, "stats_name": stats_name, "norm_sync": buf.norm_sync}
+    specs, _ = _Binder(prog, _block_binding(blocks[0], blk, buf), cfg, blk.dtype, buf.frames,
+                       extra, parts).specs()
+    return specs
 
 
 def run_block(blk: DeviceBlock, cfg: ViTConfig, buf: Buffers, stream=None, parts: int = 1,
@@ -366,7 +530,7 @@ class Encoder:
 
     def __init__(self, cfg: ViTConfig, weights: dict, dtype: str = "bf16", device="cuda",
                  planned_frames: int | None = None, fused_ln: bool | None = None,
-                 slots: int = 1):
+                 slots: int = 1, sms: int | None = None):
         """``weights``: ``blocks`` (list of per-block dicts in the reference
         layout), ``patch_w`` [patch][patch][cin][dim] (HWIO), ``patch_b`` [dim],
         ``cls`` [dim], ``pos`` [tokens][dim], ``norm_g``/``norm_b`` [dim].
@@ -393,10 +557,14 @@ class Encoder:
 
         ``slots``: input/output slots for that many jobs in flight
         (``Buffers``); ``program(frames)`` carries one binding set per slot,
-        and set s reads slot s's image and writes its feature maps."""
+        and set s reads slot s's image and writes its feature maps.
+
+        ``sms``: the device's SM count for the fusion decisions that depend
+        on it (queried from the current device when not given)."""
         import torch
         td = torch.bfloat16 if dtype == "bf16" else torch.float16
         self.cfg, self.dtype = cfg, dtype
+        self._sms, self._device = sms, device
         self.slots = max(1, int(slots))
         self.fused_ln = fused_ln if fused_ln == "epilogue" else bool(fused_ln)
         self.arena, self.plan = None, None
@@ -436,18 +604,19 @@ class Encoder:
         activations as (name, shape, torch dtype))."""
         import torch
         from .memory import F16, F32, MemoryPlan, TensorDesc
-        last = len(self.specs_layout(frames)) - 1
         acts = []
-        Buffers(self.cfg, frames, self.dtype, device="meta", slots=self.slots,
-                alloc=lambda n, s, dt: acts.append((n, s, dt)) or torch.empty(s, dtype=dt,
-                                                                              device="meta"))
+        meta = Buffers(self.cfg, frames, self.dtype, device="meta", slots=self.slots,
+                       alloc=lambda n, s, dt: acts.append((n, s, dt)) or torch.empty(
+                           s, dtype=dt, device="meta"))
+        _, used = self._launches(frames, None, 1, 0, meta)
+        last = len(used) - 1
         wts = self._weights()
         descs = []
         for k, (o, a, i) in enumerate(wts):
             t = getattr(o, a) if i is None else getattr(o, a)[i]
             descs.append(TensorDesc(k, F32 if t.element_size() == 4 else F16, t.numel(), 0, last))
         for k, (name, shape, dt) in enumerate(acts, start=len(wts)):
-            first, end = Buffers.lifetime(name.split(".")[0], last)
+            first, end = Buffers.lifetime(name, used)
             descs.append(TensorDesc(k, F32 if torch.empty((), dtype=dt).element_size() == 4
                                     else F16, int(np.prod(shape)), first, end))
         return MemoryPlan(descs, profile), wts, acts
@@ -478,64 +647,59 @@ class Encoder:
                                         alloc=lambda n, s, dt: views[n])
         torch.cuda.synchronize(device)
 
+    def lowered(self, frames: int, layers: int | None = None):
+        """The encoder graph (``encoder_graph``) lowered with this encoder's
+        LayerNorm placement for `frames` frames: (program, block ids, feature
+        map ids). No device work."""
+        from .graph import Fusion
+        g, blocks, maps = encoder_graph(self.cfg, layers)
+        forms = lowering_forms(self.fused_ln, frames * self.cfg.tokens, self.cfg.dim, self._sms)
+        return g.lower(Fusion.ON, forms), blocks, maps
+
     def specs_layout(self, frames: int) -> list:
-        """The spec labels of the encoder program, in order (no device work)."""
-        cfg = self.cfg
-        out = ["embed.patchify", "embed.patch"]
-        for i in range(cfg.layers):
-            kinds = ("norm1", "qkv", "attention", "proj", "norm2", "fc1", "fc2")
-            if self._fused(frames):
-                kinds = (("norm1", "qkv") if i == 0 else ("qkv",)) + ("attention", "proj", "fc1",
-                                                                      "fc2")
-            out += ["block%d.%s" % (i, k) for k in kinds]
-            if (i + 1) in cfg.out_indices:
-                out.append("features.%d" % (i + 1))
+        """The spec labels of the encoder program, in order (no device work):
+        a PatchEmbed kernel is two launches, every other kernel one."""
+        from .graph import PatchEmbed
+        prog, _, _ = self.lowered(frames)
+        out = []
+        for k in prog.kernels:
+            out += (["embed.patchify", "embed.patch"] if isinstance(k.main, PatchEmbed)
+                    else [k.label])
         return out
 
-    def _fused(self, frames: int):
-        """The LayerNorm mode the blocks are built with for `frames` frames."""
-        if self.fused_ln == "epilogue" and not norm_epilogue_fits(frames * self.cfg.tokens,
-                                                                  self.cfg.dim):
-            return False
-        return self.fused_ln
+    def _launches(self, frames: int, layers, parts: int, slot: int, buf: Buffers):
+        """(specs, buffer names each spec binds) of the lowered encoder over
+        `buf`, reading slot `slot`'s image and writing its feature maps."""
+        prog, blocks, maps = self.lowered(frames, layers)
+        if not 0 <= slot < self.slots:
+            raise ValueError("slot %d of %d" % (slot, self.slots))
+        bind = {1: ("image", buf.images[slot]), 2: ("weight", self.patch_w),
+                3: ("weight", self.patch_b), 4: ("weight", self.cls), 5: ("weight", self.pos),
+                6: ("weight", self.norm[0]), 7: ("weight", self.norm[1]), 12: ("x", buf.x)}
+        for i, ids in enumerate(blocks):
+            bind.update(_block_binding(ids, self.blocks[i], buf))
+        for j, m in enumerate(maps):
+            bind[m] = ("features.%d" % self.cfg.out_indices[j], buf.slot_features[slot][j])
+        stats, stats_name = _stats(blocks, buf)
+        extra = {"patches": buf.patches, "stats": stats, "stats_name": stats_name,
+                 "norm_sync": buf.norm_sync}
+        return _Binder(prog, bind, self.cfg, self.dtype, frames, extra, parts).specs()
 
     def buffers(self, frames: int) -> Buffers:
         if frames not in self._buffers:
             if self.arena is not None:
                 raise ValueError("this encoder's memory is planned for %s frames"
                                  % sorted(self._buffers))
-            self._buffers[frames] = Buffers(self.cfg, frames, self.dtype, slots=self.slots)
+            self._buffers[frames] = Buffers(self.cfg, frames, self.dtype, slots=self.slots,
+                                            device=self._device)
         return self._buffers[frames]
 
     def specs(self, frames: int, layers: int | None = None, parts: int = 1,
               slot: int = 0) -> list:
         """The encoder as kernel specs over the buffers of `frames` frames,
-        reading slot `slot`'s image and writing its feature maps."""
-        from .runtime import Spec
-        cfg, buf = self.cfg, self.buffers(frames)
-        if not 0 <= slot < self.slots:
-            raise ValueError("slot %d of %d" % (slot, self.slots))
-        t = cfg.tokens
-        out = [
-            Spec(ops.patchify_args(buf.images[slot], frames=frames, side=cfg.side, patch=cfg.patch,
-                                   cin=cfg.cin, k_pad=cfg.k_pad, a_out=buf.patches,
-                                   a_dtype=self.dtype, cls=self.cls, pos=self.pos, x=buf.x),
-                 "embed.patchify"),
-            Spec(_weights_gemm(self.patch_w, a=buf.patches, bias=self.patch_b, residual=self.pos,
-                               res_period=t, out=buf.x, out_row_offset=1, out_group=(t - 1, 1)),
-                 "embed.patch", parts),
-        ]
-        n = cfg.layers if layers is None else layers
-        for i in range(n):
-            nxt = self.blocks[i + 1].norm1 if i + 1 < n else None
-            out += block_specs(self.blocks[i], cfg, buf, i, parts, fused_ln=self.fused_ln,
-                               next_norm=nxt)
-            if (i + 1) in cfg.out_indices:
-                f = buf.slot_features[slot][cfg.out_indices.index(i + 1)]
-                out.append(Spec(ops.layernorm_args(buf.x, self.norm[0], self.norm[1], cfg.eps,
-                                                   out=f, in_row_offset=1, in_group=(t - 1, 1)),
-                                "features.%d" % (i + 1), parts))
-        return out
+        reading slot `slot`'s image and writing its feature maps: the
+        launches of the lowered encoder graph (``lowered``)."""
+        return self._launches(frames, layers, parts, slot, self.buffers(frames))[0]
 
     def program(self, frames: int = 1, layers: int | None = None, parts: int = 1):
         """The encoder's kernels over the buffers of `frames` frames, with one
@@ -610,11 +774,11 @@ class Encoder:
         return g
 
     def launches_per_frame_batch(self, layers: int | None = None, frames: int = 1) -> int:
-        n = self.cfg.layers if layers is None else layers
-        taken = sum(1 for i in self.cfg.out_indices if i <= n)
-        fused = self._fused(frames)
-        per_block = [7 if not fused else (6 if i == 0 else 5) for i in range(n)]
-        return 3 + sum(per_block) + taken  # patchify (2 kernels) + patch GEMM, blocks, norms
+        """Kernels launched per pass: the program's specs, with the patch
+        matrix and its class rows counted as two."""
+        from .graph import PatchEmbed
+        prog, _, _ = self.lowered(frames, layers)
+        return sum(3 if isinstance(k.main, PatchEmbed) else 1 for k in prog.kernels)
 
 
 # ------------------------------------------------------------------ DPT head
