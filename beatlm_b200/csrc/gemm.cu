@@ -29,6 +29,7 @@ constexpr int BK = 64;
 constexpr int kMaxStages = 8;
 constexpr uint32_t kSmemLimit = 232448;  // 227 KiB of dynamic shared memory per CTA
 constexpr int kThreads = 192;
+constexpr int kMaxBN = 256;  // the widest tile (the persistent kernel only)
 constexpr uint32_t kTileA = BM * BK * 2;  // 16 KiB
 
 struct Params {
@@ -113,8 +114,8 @@ struct Tail {
     int abort;
     // the tile's bias and channel-scale columns, staged by the epilogue warps
     // while the main loop runs
-    alignas(16) float bias[128];
-    alignas(16) float chan[128];
+    alignas(16) float bias[kMaxBN];
+    alignas(16) float chan[kMaxBN];
 };
 
 template <int BN, int KC = 1, bool kEpi = false>
@@ -223,8 +224,8 @@ __device__ __forceinline__ RowCtx row_ctx(const Params& p, int grow) {
 // epilogue warps (threads 64..191); the caller synchronises them after.
 template <int BN>
 __device__ __forceinline__ void stage_vectors(const Params& p, Tail* tail, int n0) {
-    const int t = static_cast<int>(threadIdx.x) - 64;
-    if (t >= 0 && t < BN) {
+    static_assert(BN <= kMaxBN, "tile wider than the staged vectors");
+    for (int t = static_cast<int>(threadIdx.x) - 64; t >= 0 && t < BN; t += 128) {
         tail->bias[t] = p.bias != nullptr ? __ldg(p.bias + n0 + t) : 0.0f;
         tail->chan[t] = p.chan_scale != nullptr ? __ldg(p.chan_scale + n0 + t) : 1.0f;
     }
@@ -1318,6 +1319,7 @@ int pick_bn(const bl_gemm_args& g) {
     const int mt = static_cast<int>((g.m + BM - 1) / BM);
     const int cands[4] = {128, 96, 64, 32};
     if (g.ln_x == nullptr) {
+        const int wide[5] = {256, 128, 96, 64, 32};  // the persistent kernel's widths
         // Persistent grid: the busiest CTA's tiles times a tile's cost. A
         // k-block is bound by its operand bytes arriving (measured about 45
         // bytes per SM clock from L2); the epilogue costs about 600 clocks
@@ -1327,7 +1329,7 @@ int pick_bn(const bl_gemm_args& g) {
         const long long nk = g.k / BK, sms = sm_count();
         int best = 0;
         long long best_cost = 0;
-        for (int bn : cands) {
+        for (int bn : wide) {
             if (g.n % bn != 0) continue;
             const long long tiles = static_cast<long long>(mt) * (g.n / bn);
             const long long per_cta = (tiles + sms - 1) / sms;
@@ -1371,9 +1373,13 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
             return fail(BL_ERR_UNSUPPORTED, "gemm: the epilogue LayerNorm needs 32-column tiles");
         bn = 32;
     }
-    if (bn == 0 || g.n % bn != 0 || (bn != 32 && bn != 64 && bn != 96 && bn != 128))
-        return fail(BL_ERR_UNSUPPORTED, "gemm: N=%u has no tile width (32/64/96/128)", g.n);
+    if (bn == 0 || g.n % bn != 0 ||
+        (bn != 32 && bn != 64 && bn != 96 && bn != 128 && bn != 256))
+        return fail(BL_ERR_UNSUPPORTED, "gemm: N=%u has no tile width (32/64/96/128/256)", g.n);
     const bool ln = g.ln_x != nullptr;
+    if (bn == 256 && ln)
+        return fail(BL_ERR_UNSUPPORTED, "gemm: 256-column tiles take A loaded by TMA, not a "
+                                        "LayerNorm prologue");
     if (norm) {
         const uint64_t tiles = ((static_cast<uint64_t>(g.m) + BM - 1) / BM) * (g.n / 32);
         if (ln || g.out_dtype != BL_F32 || (g.split_col > 0 && g.split_col < g.n) ||
@@ -1563,6 +1569,7 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
         case 32: return prepare_persistent<32>(ta, tb, to, tn, p, kc, out);
         case 64: return prepare_persistent<64>(ta, tb, to, tn, p, kc, out);
         case 96: return prepare_persistent<96>(ta, tb, to, tn, p, kc, out);
+        case 256: return prepare_persistent<256>(ta, tb, to, tn, p, kc, out);
         default: return prepare_persistent<128>(ta, tb, to, tn, p, kc, out);
     }
 }

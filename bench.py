@@ -2,7 +2,8 @@
 """Benchmark of the ViT attention hot path on B200 (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload encoder|attention|block|vitl|hires|decoder|depth]
+                    [--workload encoder|attention|block|vitl_block|vitl|hires|
+                                decoder|depth]
                     [--no-extra] [--no-cpu-baseline]
 
 Workloads (synthetic data, seeded):
@@ -511,15 +512,16 @@ class BlockWorkload:
     data = "synthetic x ~ N(0,1), N(0,0.02) weights, seeded"
     workload_name = "vit_s_block_fp16 (config 2)"
     scaling = "weak"
+    large, dt, bound = False, "f16", 1e-3
 
     def parallelism(self, world):
         return "replicas x%d (no collective)" % world
 
-    @staticmethod
-    def host_inputs(seed=2):
+    @classmethod
+    def host_inputs(cls, seed=2):
         import numpy as np
         from beatlm_b200.model import ViTConfig, block_weights_normal
-        cfg = ViTConfig.small()
+        cfg = ViTConfig.large() if cls.large else ViTConfig.small()
         rng = np.random.default_rng(seed)
         w = block_weights_normal(rng, cfg.dim, cfg.mlp)
         x = rng.standard_normal(cfg.tokens * cfg.dim, dtype=np.float32)
@@ -532,7 +534,8 @@ class BlockWorkload:
         fn = lambda: oracle.vit_block(x, w, cfg.tokens, cfg.heads, cfg.head_dim, cfg.mlp,
                                       cfg.eps, threads=threads)
         return fn, cfg.flops_per_frame()["linear"] / cfg.layers / 1e12 + \
-            4.0 * cfg.tokens ** 2 * cfg.dim / 1e12, "one ViT-S block per step (oracle, f64)"
+            4.0 * cfg.tokens ** 2 * cfg.dim / 1e12, "one %s block per step (oracle, f64)" % (
+                "ViT-L" if cls.large else "ViT-S")
 
     def __init__(self, rank: int, world: int = 1):
         import torch
@@ -540,8 +543,8 @@ class BlockWorkload:
         from beatlm_b200.runtime import Kernels
         self.cfg, self.w, self.x = self.host_inputs()
         cfg = self.cfg
-        self.blk = DeviceBlock(self.w, cfg.dim, cfg.mlp, "f16")
-        self.buf = Buffers(cfg, 1, "f16", features=False)
+        self.blk = DeviceBlock(self.w, cfg.dim, cfg.mlp, self.dt)
+        self.buf = Buffers(cfg, 1, self.dt, features=False)
         self.host = torch.from_numpy(self.x.reshape(cfg.tokens, cfg.dim)).pin_memory()
         self.out_host = torch.empty((cfg.tokens, cfg.dim), dtype=torch.float32).pin_memory()
         self.buf.x.copy_(self.host)
@@ -556,7 +559,7 @@ class BlockWorkload:
     def config(self):
         c = self.cfg
         return {"workload": self.workload_name, "tokens": c.tokens, "dim": c.dim,
-                "heads": c.heads, "mlp": c.mlp, "dtype": "f16",
+                "heads": c.heads, "mlp": c.mlp, "dtype": self.dt,
                 "weights": "random N(0,0.02), LN gamma=1 beta=0, LayerScale=1",
                 "launch": "one CUDA graph per step (%d kernels)" % self.launches_per_step,
                 "gflop_per_step": round(self.flops / 1e9, 3),
@@ -616,10 +619,10 @@ class BlockWorkload:
         self.buf.x.copy_(self.host)
         self.prog.encode_all(None)
         torch.cuda.synchronize()
-        want = oracle.vit_block(self.x, DeviceBlock.rounded(self.w, "f16"), cfg.tokens, cfg.heads,
-                                64, cfg.mlp, cfg.eps, qkv_round="qk_f16")
+        want = oracle.vit_block(self.x, DeviceBlock.rounded(self.w, self.dt), cfg.tokens,
+                                cfg.heads, 64, cfg.mlp, cfg.eps, qkv_round="qk_" + self.dt)
         rel, mx = _rel(self.buf.x.cpu().numpy(), want)
-        return {"rel_l2": rel, "max_abs": mx, "bound": 1e-3,
+        return {"rel_l2": rel, "max_abs": mx, "bound": self.bound,
                 "sample": "the whole block output vs oracle.vit_block"}
 
     def cpu_baseline(self, threads: int):
@@ -632,6 +635,17 @@ class BlockWorkload:
                 "kind": "port", "sample": "the whole block through oracle.vit_block "
                                           "(reference.rs:520-544), median of %s s"
                                           % [round(x, 2) for x in times]}
+
+
+class VitLBlockWorkload(BlockWorkload):
+    """One block of config 4's ViT-L/14 encoder (dim 1024, 16 heads, MLP
+    4096, 1370 tokens) in bf16, weights N(0, 0.02): the block workload at the
+    large shapes, where the GEMMs carry enough work to study on their own."""
+
+    name = "vitl_block"
+    large, dt, bound = True, "bf16", 4e-3
+    dtype = "bf16 weights and activations, f16 V and P; f32 accumulate and residual"
+    workload_name = "vit_l14_block_bf16 (config 4, one block)"
 
 
 class HiresWorkload:
@@ -972,7 +986,8 @@ class DecoderWorkload:
                 "sample": "%s, median of 3" % sample}
 
 
-WORKLOADS = {"attention": AttentionWorkload, "block": BlockWorkload, "encoder": EncoderWorkload,
+WORKLOADS = {"attention": AttentionWorkload, "block": BlockWorkload,
+             "vitl_block": VitLBlockWorkload, "encoder": EncoderWorkload,
              "vitl": VitLWorkload, "hires": HiresWorkload, "decoder": DecoderWorkload,
              "depth": DepthWorkload}
 # the other configs carried in the default line, by GPU count

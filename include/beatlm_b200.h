@@ -292,8 +292,9 @@ enum { BL_ACT_NONE = 0, BL_ACT_RELU = 1, BL_ACT_GELU_TANH = 2, BL_ACT_GELU_ERF =
  * out_row_offset (out_group_rows = 0: r + out_row_offset), which places the
  * patch tokens of a frame after its class token.
  *
- * k must be a multiple of 64 and n a multiple of the tile width (32, 64, 96 or
- * 128; tile_n = 0 chooses). Pointers 16-byte aligned, row strides 16-byte
+ * k must be a multiple of 64 and n a multiple of the tile width (32, 64, 96,
+ * 128, or 256 with A given as `a`; tile_n = 0 chooses from a per-CTA cost
+ * estimate). Pointers 16-byte aligned, row strides 16-byte
  * multiples. Enqueues on `stream`; allocates nothing.
  */
 typedef struct bl_gemm_args {

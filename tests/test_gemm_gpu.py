@@ -54,7 +54,9 @@ def _check_status():
 @pytest.mark.parametrize("m,n,k,tile", [(1370, 1152, 384, 0), (1370, 384, 384, 32),
                                         (1370, 1536, 384, 128), (1370, 384, 1536, 32),
                                         (200, 192, 128, 96), (1, 64, 64, 64), (129, 128, 640, 64),
-                                        (1370, 4096, 1024, 128), (2740, 1536, 384, 64)])
+                                        (1370, 4096, 1024, 128), (2740, 1536, 384, 64),
+                                        (1370, 3072, 1024, 256), (300, 512, 4096, 256),
+                                        (1370, 4096, 1024, 0)])
 def test_plain_gemm_with_bias(dtype, m, n, k, tile):
     """Shapes from one tile to several tiles per CTA of the persistent grid
     (1370 x 4096 at 128 columns: 352 tiles for 148 CTAs)."""
@@ -73,8 +75,9 @@ def test_plain_gemm_with_bias(dtype, m, n, k, tile):
 
 
 @pytest.mark.parametrize("dtype", ["f16", "bf16"])
-@pytest.mark.parametrize("m,n,k", [(1370, 384, 384), (1370, 1024, 4096)])
-def test_layerscale_residual_epilogue(dtype, m, n, k):
+@pytest.mark.parametrize("m,n,k,tile", [(1370, 384, 384, 0), (1370, 1024, 4096, 0),
+                                        (1370, 1024, 1024, 256)])
+def test_layerscale_residual_epilogue(dtype, m, n, k, tile):
     """x1 = x + ls * (A.W + b): ChannelScale then Add (reference.rs:379, 301),
     in place on the f32 residual stream (ViT-S proj; ViT-L fc2, more than one
     tile per CTA)."""
@@ -86,14 +89,16 @@ def test_layerscale_residual_epilogue(dtype, m, n, k):
     x = oracle.uniform(5, m * n, -2, 2)
     xd = _dev(x.reshape(m, n), "f32")
     bl.ops.linear(_dev(w.reshape(k, n).T, dtype), a=_dev(a.reshape(m, k), dtype),
-                  bias=_dev(b, "f32"), chan_scale=_dev(ls, "f32"), residual=xd, out=xd)
+                  bias=_dev(b, "f32"), chan_scale=_dev(ls, "f32"), residual=xd, out=xd,
+                  tile_n=tile)
     torch.cuda.synchronize()
     _check_status()
     want = oracle.add(x, oracle.channel_scale(oracle.matmul(a, w, b, m, k, n), ls))
     _close(xd.cpu().numpy(), want, "layerscale+residual")
 
 
-def test_gelu_erf_epilogue_and_16bit_store():
+@pytest.mark.parametrize("tile", [0, 256])
+def test_gelu_erf_epilogue_and_16bit_store(tile):
     import torch
     import beatlm_b200 as bl
     m, n, k = 300, 1536, 384
@@ -102,7 +107,7 @@ def test_gelu_erf_epilogue_and_16bit_store():
     b = oracle.uniform(8, n, -0.1, 0.1)
     out = torch.zeros((m, n), dtype=torch.bfloat16, device="cuda")
     bl.ops.linear(_dev(w.reshape(k, n).T, "bf16"), a=_dev(a.reshape(m, k), "bf16"),
-                  bias=_dev(b, "f32"), act="gelu_erf", out=out)
+                  bias=_dev(b, "f32"), act="gelu_erf", out=out, tile_n=tile)
     torch.cuda.synchronize()
     _check_status()
     want = oracle.round_bf16(oracle.gelu_erf(oracle.matmul(a, w, b, m, k, n)))
