@@ -40,6 +40,7 @@ class AttentionArgs(ctypes.Structure):
         ("out_row_stride", ctypes.c_uint64), ("out_head_base", ctypes.c_uint32),
         ("kv_splits", ctypes.c_uint32), ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_uint64), ("trace", ctypes.c_void_p),
+        ("query_tiles", ctypes.c_uint32),
     ]
 
 
@@ -56,6 +57,9 @@ SIGNATURES = {
     "bl_attention": (ctypes.c_int, [ctypes.POINTER(AttentionArgs), ctypes.c_void_p]),
     "bl_attention_workspace_bytes": (ctypes.c_uint64, [ctypes.POINTER(AttentionArgs)]),
     "bl_attention_noalloc": (ctypes.c_int, [ctypes.POINTER(AttentionArgs), ctypes.c_void_p]),
+    "bl_attention_choice": (ctypes.c_int, [ctypes.POINTER(AttentionArgs),
+                                           ctypes.POINTER(ctypes.c_uint32),
+                                           ctypes.POINTER(ctypes.c_uint32)]),
 }
 
 

@@ -4,29 +4,32 @@
 // crates/beatlm-bench/src/reference.rs:437-494) as one kernel with an online
 // softmax, so the [tokens][heads][tokens] scores never reach memory.
 //
-// One CTA computes two 128-row query tiles of one head of one sequence over a
-// range of key tiles (all of them, or one split of them). 12 warps in three
-// warpgroups; the control warpgroup gives registers to the softmax ones
-// (setmaxnreg: 128 x 56 + 256 x 224 = 384 x 168, the launch allocation):
-//   warp 0      TMA producer: Q0 and Q1 once, then K/V tiles of 128 keys into
-//               a 4-stage ring (128-byte swizzle, zero fill past the last key).
+// One CTA computes one or two 128-row query tiles (QT, a template parameter)
+// of one head of one sequence over a range of key tiles (all of them, or one
+// split of them). With QT = 2, 12 warps in three warpgroups, the control
+// warpgroup giving registers to the softmax ones (setmaxnreg); with QT = 1,
+// 8 warps in two:
+//   warp 0      TMA producer: the CTA's Q rows once, then K/V tiles of 128
+//               keys into a 4-stage ring (128-byte swizzle, zero fill past
+//               the last key).
 //   warp 1      MMA issuer (one thread): S = Q_t K^T into TMEM (M=128,
 //               N=128, K=64, f32) and O_t += P V with P read from TMEM
-//               (M=128, N=64, K=128, f16). Three S buffers rotate over the
-//               slots j = 2 i + t (key tile i, query tile t), so the scores
-//               of the next two slots are computed before a softmax needs
-//               them: S_0 S_1 S_2 | PV_0 S_3 | PV_1 S_4 | PV_2 S_5 ...
-//   warps 4..7  softmax of tile 0, warps 8..11 softmax of tile 1: one thread
-//               per query row (TMEM lane) holding its 128 scores in
-//               registers; the running max is updated lazily (O is rescaled
-//               in TMEM only when the max grew by more than 2^8); P is
-//               written as f16 over the consumed S columns; exponentials on
-//               the MUFU ex2 unit.
+//               (M=128, N=64, K=128, f16). S buffers rotate over the slots
+//               j = QT i + t (key tile i, query tile t), so the scores of the
+//               next slots are computed before a softmax needs them (QT = 2,
+//               three buffers: S_0 S_1 S_2 | PV_0 S_3 | PV_1 S_4 ...; QT = 1,
+//               two: S_0 S_1 | PV_0 S_2 | PV_1 S_3 ...).
+//   warps 4..7  softmax of tile 0 (warps 8..11 of tile 1): one thread per
+//               query row (TMEM lane) holding its 128 scores in registers;
+//               the running max is updated lazily (O is rescaled in TMEM
+//               only when the max grew by more than 2^8); P is written as
+//               f16 over the consumed S columns; exponentials on the MUFU
+//               ex2 unit.
 // With more than one key split, the splits of a query group either form a
 // cluster and combine in distributed shared memory, or write their
 // unnormalised O and (max, sum) per row to a workspace where the last CTA
 // of the group (an atomic counter, no waiting) combines them.
-// TMEM: S buffers [0,128) [128,256) [256,384), O0 [384,448), O1 [448,512);
+// TMEM: S buffers at [128 b, 128 b + 128), then O_t (64 columns each);
 // P aliases the S buffer it came from.
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
@@ -40,26 +43,41 @@ namespace bl {
 namespace attn {
 
 constexpr int BM = 128;       // query rows per tile
-constexpr int QT = 2;         // query tiles per CTA
-constexpr int ROWS = BM * QT; // query rows per CTA
 constexpr int BN = 128;       // keys per tile
 constexpr int HD = 64;        // head width
 constexpr int STAGES = 4;     // K/V ring depth
 constexpr int kSoftmaxWarp0 = 4;
-constexpr int kThreads = 32 * (kSoftmaxWarp0 + 4 * QT);  // 384
-// Register split (setmaxnreg): the launch gives every thread kLaunchRegs.
-constexpr int kLaunchRegs = 168;
-constexpr int kControlRegs = 56;
-constexpr int kSoftmaxRegs = 224;
-static_assert(128 * kControlRegs + 32 * 4 * QT * kSoftmaxRegs <= kThreads * kLaunchRegs,
-              "register split exceeds the launch allocation");
 constexpr uint32_t kTileBytes = BM * HD * 2;  // 16 KiB per 128x64 tile
 constexpr uint32_t kTmemCols = 512;
-// Three S buffers of 128 columns rotate over the (key tile, query tile) slots
-// j = 2 i + t (slot j uses buffer j % 3); O_t at kColO + 64 t.
-constexpr int kSBufs = 3;
-constexpr uint32_t kColS = 0, kColO = 128 * kSBufs;
-static_assert(kColO + 64 * QT <= kTmemCols, "TMEM columns");
+constexpr uint32_t kColS = 0;
+// The kernel comes in two shapes, by the query tiles a CTA computes (QT):
+//   QT = 2: 12 warps; the control warpgroup gives registers to the two
+//           softmax warpgroups (setmaxnreg: 128 x 56 + 256 x 224 = 384 x
+//           168, the launch allocation). Three S buffers rotate over the
+//           slots j = 2 i + t (key tile i, query tile t).
+//   QT = 1: 8 warps, one softmax warpgroup, no register split (a thread may
+//           hold up to 255). Two S buffers rotate over the slots j = i.
+// In both the S of slot j + kSBufs reuses slot j's buffer and is issued
+// right after PV(j), so the S of tile t at key tile i is always issued after
+// PV_t(i - 2). O_t lives at kColO + 64 t.
+template <int kQT>
+struct Shape {
+    static_assert(kQT == 1 || kQT == 2, "one or two query tiles per CTA");
+    static constexpr int QT = kQT;
+    static constexpr int ROWS = BM * QT;  // query rows per CTA
+    static constexpr int kThreads = 32 * (kSoftmaxWarp0 + 4 * QT);
+    static constexpr int kSBufs = QT == 2 ? 3 : 2;
+    static constexpr uint32_t kColO = 128 * kSBufs;
+    static_assert(kColO + 64 * QT <= kTmemCols, "TMEM columns");
+    // Register split (QT = 2 only): the launch gives every thread kLaunchRegs.
+    static constexpr bool kRegSplit = QT == 2;
+    static constexpr int kLaunchRegs = 168;
+    static constexpr int kControlRegs = 56;
+    static constexpr int kSoftmaxRegs = 224;
+    static_assert(!kRegSplit ||
+                      128 * kControlRegs + 32 * 4 * QT * kSoftmaxRegs <= kThreads * kLaunchRegs,
+                  "register split exceeds the launch allocation");
+};
 // Lazy rescaling: the max used for exponents may trail the true max by up to
 // this (log2 units), so p <= 2^8, well inside f16.
 constexpr float kRescaleThreshold = 8.0f;
@@ -113,6 +131,7 @@ __device__ __forceinline__ void trace_stamp(unsigned long long* trace, int slot)
     trace[8 * b + slot] = t;
 }
 
+template <int QT>
 struct SmemTail {
     uint64_t q_full;
     uint64_t kv_full[STAGES];
@@ -137,19 +156,25 @@ constexpr int kMaxClusterSplits = 8;  // portable cluster size
 // and the owner's reads are conflict-free. The area holds the splits - 1
 // sources of up to ceil(8 / splits) warps of rows: most at 7 splits.
 constexpr int kPartVecs = HD / 8 + 1;
+template <int ROWS>
 constexpr size_t part_area(int splits) {
     return static_cast<size_t>(splits - 1) * kPartVecs * ((ROWS / 32 + splits - 1) / splits) *
            32 * 16;
 }
+template <int ROWS>
 constexpr size_t max_part_area(int s = 2) {
-    return s > kMaxClusterSplits ? 0
-                                 : (part_area(s) > max_part_area(s + 1) ? part_area(s)
-                                                                        : max_part_area(s + 1));
+    return s > kMaxClusterSplits
+               ? 0
+               : (part_area<ROWS>(s) > max_part_area<ROWS>(s + 1) ? part_area<ROWS>(s)
+                                                                  : max_part_area<ROWS>(s + 1));
 }
-constexpr size_t kPartArea = max_part_area();
+template <int QT>
+constexpr size_t kPartArea = max_part_area<BM * QT>();
+template <int QT>
 constexpr size_t kSmemBytes = 1024 /*align slack*/ + QT * kTileBytes /*Q*/ +
-                              STAGES * 2 * kTileBytes /*K,V*/ + kPartArea + sizeof(SmemTail);
-static_assert(kSmemBytes <= 232448, "shared memory");
+                              STAGES * 2 * kTileBytes /*K,V*/ + kPartArea<QT> +
+                              sizeof(SmemTail<QT>);
+static_assert(kSmemBytes<1> <= 232448 && kSmemBytes<2> <= 232448, "shared memory");
 
 __device__ __forceinline__ uint64_t desc_kmajor(uint32_t addr) {
     return sdesc_sw128(addr, 16, 1024);
@@ -240,17 +265,23 @@ __global__ void __launch_bounds__(32, 1) peer_arrive_kernel(const __grid_constan
     }
 }
 
-// The 256 softmax threads (warps 4..11) only.
+// The softmax threads (warps 4..) only.
+template <int QT>
 __device__ __forceinline__ void softmax_bar() {
     asm volatile("bar.sync 1, %0;" ::"n"(32 * 4 * QT) : "memory");
 }
 
-template <int kOutDtype, bool kPeers = false>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int kQT, int kOutDtype, bool kPeers = false>
+__global__ void __launch_bounds__(Shape<kQT>::kThreads, 1)
     attention_fwd(const __grid_constant__ CUtensorMap tm_q,
                   const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, const Params p,
                   const __grid_constant__ PeerParams peers) {
+    using Sh = Shape<kQT>;
+    constexpr int QT = kQT;
+    constexpr int ROWS = Sh::ROWS;
+    constexpr int kSBufs = Sh::kSBufs;
+    constexpr uint32_t kColO = Sh::kColO;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -258,7 +289,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* sK = smem + QT * kTileBytes;                        // stage s at + s*kTileBytes
     uint8_t* sV = smem + QT * kTileBytes + STAGES * kTileBytes;  // stage s at + s*kTileBytes
     uint8_t* sP = smem + QT * kTileBytes + 2 * STAGES * kTileBytes;  // cluster partials
-    SmemTail* tail = reinterpret_cast<SmemTail*>(sP + kPartArea);
+    SmemTail<QT>* tail = reinterpret_cast<SmemTail<QT>*>(sP + kPartArea<QT>);
     volatile int* abort = &tail->abort;
 
     const int warp = warp_id();
@@ -319,7 +350,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) trace_stamp(p.trace, 1);
 
     if (warp < kSoftmaxWarp0) {
-        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kControlRegs));
+        if constexpr (Sh::kRegSplit)
+            asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Sh::kControlRegs));
         if (warp == 0) {
             // -------------------------------------------------- producer
             // The warp runs the loop in step: lane 0 copies the CTA's Q rows
@@ -387,10 +419,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 return true;
             };
-            // Slot j = 2 i + t is (key tile i, query tile t); its S goes to
-            // buffer j % 3. The S of slot j + 3 reuses the buffer of slot j, so
-            // it is issued right after slot j's PV (the tensor core runs one
-            // thread's MMAs in order); the S of slots j + 1 and j + 2 are
+            // Slot j = QT i + t is (key tile i, query tile t); its S goes to
+            // buffer j % kSBufs. The S of slot j + kSBufs reuses the buffer of
+            // slot j, so it is issued right after slot j's PV (the tensor core
+            // runs one thread's MMAs in order); the S of the slots between are
             // already issued by then, so a softmax warpgroup finds its next
             // scores ready when it finishes its current ones.
             // Descriptors are built once: a tile or stage moves the 14-bit
@@ -401,7 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t dv = desc_v(smem_u32(sV));
             constexpr uint64_t kTileStep = kTileBytes >> 4;
             auto issue_s = [&](int j) {
-                const int t = j & 1, i = j >> 1;
+                const int t = j % QT, i = j / QT;
                 const uint64_t a = dq + t * kTileStep;
                 const uint64_t b = dk + (i % STAGES) * kTileStep;
                 const uint32_t dst = tmem + kColS + 128 * (j % kSBufs);
@@ -414,7 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
             };
             auto issue_pv = [&](int j) -> bool {
-                const int t = j & 1, i = j >> 1;
+                const int t = j % QT, i = j / QT;
                 if (!wait_all(smem_u32(&tail->p_full[t][i & 1]), (i >> 1) & 1,
                               0x10000 | (t << 12) | i))
                     return false;
@@ -427,8 +459,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int k = 1; k < BN / 16; ++k)
                         mma_ts(o, p_col + k * 8, b + 128 * k, idesc_o, 1u);
-                    // The stage is released after its last reader (tile 1's
-                    // PV), and only if the producer will refill it, so no
+                    // The stage is released after its last reader (the last
+                    // tile's PV), and only if the producer will refill it, so no
                     // arrival lands after the CTA has finished.
                     if (t == QT - 1 && i + STAGES < n)
                         mma_commit(smem_u32(&tail->kv_empty[i % STAGES]));
@@ -440,14 +472,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             };
             const int slots = QT * n;
             for (int j = 0; j < kSBufs && j < slots && ok; ++j) {
-                if ((j & 1) == 0) ok = wait_kv(j >> 1);
+                if (j % QT == 0) ok = wait_kv(j / QT);
                 if (ok) issue_s(j);
             }
             for (int j = 0; j < slots && ok; ++j) {
                 ok = issue_pv(j);
                 const int next = j + kSBufs;
                 if (ok && next < slots) {
-                    if ((next & 1) == 0) ok = wait_kv(next >> 1);
+                    if (next % QT == 0) ok = wait_kv(next / QT);
                     if (ok) issue_s(next);
                 }
             }
@@ -467,7 +499,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             cluster_wait();
         }
     } else {
-        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
+        if constexpr (Sh::kRegSplit)
+            asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(Sh::kSoftmaxRegs));
         // ------------------------------------------------------ softmax
         constexpr unsigned kFull = 0xFFFFFFFFu;
         const int t = (warp - kSoftmaxWarp0) / 4;  // query tile of this warpgroup
@@ -482,7 +515,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         float l = 0.0f;
         bool ok = true;
         for (int i = 0; i < n; ++i) {
-            const uint32_t s_col = t_lane + kColS + 128 * ((2 * i + t) % kSBufs);
+            const uint32_t s_col = t_lane + kColS + 128 * ((QT * i + t) % kSBufs);
             const uint32_t b_p = smem_u32(&tail->p_full[t][i & 1]);
             ok = mbar_wait(smem_u32(&tail->s_full[t][i & 1]), (i >> 1) & 1, abort, p.status,
                            ST_TIMEOUT_SOFTMAX, (t << 12) | i);
@@ -590,7 +623,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_ld32(o_col + 32, *reinterpret_cast<uint32_t(*)[32]>(o + 32));
             tmem_wait_ld();
         }
-        const int crow = t * BM + row;  // row within the CTA's 256
+        const int crow = t * BM + row;  // row within the CTA's ROWS
         const int grow = q0 + crow;
         const bool store = grow < p.row_end && grow < p.tokens;
         auto row_offset = [&]() {
@@ -756,12 +789,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int k = 0; k < HD / 8; ++k) po[k] = on[k];
                 *pml = make_float2(mine_m, mine_l);
                 __threadfence();
-                softmax_bar();
+                softmax_bar<QT>();
                 if (threadIdx.x == 32 * kSoftmaxWarp0) {
                     const unsigned prev = atomicAdd(p.counters + unit, 1u);
                     tail->last = prev == static_cast<unsigned>(p.splits) - 1;
                 }
-                softmax_bar();
+                softmax_bar<QT>();
                 if (tail->last) {
                     __threadfence();
                     if (kPeers || store) {
@@ -796,6 +829,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 struct Plan {
+    int qt;      // query tiles per CTA
+    int rows;    // query rows per CTA
     int splits;
     int q_ctas;
     int kv_tiles;
@@ -803,14 +838,16 @@ struct Plan {
     size_t bytes;  // workspace
 };
 
-Plan plan(const bl_attention_args& a, int splits) {
+Plan plan(const bl_attention_args& a, int splits, int qt) {
     Plan pl{};
-    pl.q_ctas = static_cast<int>((a.row_end - a.row_begin + ROWS - 1) / ROWS);
+    pl.qt = qt == 1 ? 1 : 2;
+    pl.rows = BM * pl.qt;
+    pl.q_ctas = static_cast<int>((a.row_end - a.row_begin + pl.rows - 1) / pl.rows);
     pl.kv_tiles = static_cast<int>((a.tokens + BN - 1) / BN);
     pl.units = static_cast<size_t>(a.batch) * (a.head_end - a.head_begin) * pl.q_ctas;
     pl.splits = splits < 1 ? 1 : (splits > pl.kv_tiles ? pl.kv_tiles : splits);
-    // per unit: splits x ROWS rows of f16 O / l (HD x 2 bytes) and (max, sum)
-    pl.bytes = pl.splits > 1 ? pl.units * (static_cast<size_t>(pl.splits) * ROWS *
+    // per unit: splits x rows of f16 O / l (HD x 2 bytes) and (max, sum)
+    pl.bytes = pl.splits > 1 ? pl.units * (static_cast<size_t>(pl.splits) * pl.rows *
                                                (HD * 2 + 2 * sizeof(float)) +
                                            sizeof(unsigned))
                              : 0;
@@ -818,32 +855,131 @@ Plan plan(const bl_attention_args& a, int splits) {
 }
 
 // The workspace: f16 O / l, then (max, sum), then one counter per unit.
-size_t part_o_bytes(const Plan& pl) { return pl.units * pl.splits * ROWS * HD * 2; }
+size_t part_o_bytes(const Plan& pl) { return pl.units * pl.splits * pl.rows * HD * 2; }
 size_t counters_offset(const Plan& pl) {
-    return part_o_bytes(pl) + pl.units * pl.splits * ROWS * 2 * sizeof(float);
+    return part_o_bytes(pl) + pl.units * pl.splits * pl.rows * 2 * sizeof(float);
 }
 
-// Key splits that fill the 148 SMs of a B200 in one wave when the tile grid
-// alone does not: at most one CTA per SM, at least two key tiles per split.
-int auto_splits(const bl_attention_args& a) {
-    const Plan p1 = plan(a, 1);
-    const size_t ctas = p1.units;
-    if (ctas * 2 > 148) return 1;
-    int s = static_cast<int>(148 / ctas);
-    const int max_s = p1.kv_tiles / 2 > 0 ? p1.kv_tiles / 2 : 1;
-    return s > max_s ? max_s : s;
+int max_active_clusters(int qt, int splits);
+
+// Estimated time (us) of one launch: a fixed launch cost plus waves of
+// co-resident CTAs (clusters) times a wave's length, a wave being the key
+// steps of one CTA, its set-up and drain, and the split combine. Unsplit and
+// in the workspace form one CTA per SM. Fitted on B200 to launches replayed
+// back to back in a CUDA graph (T = 1370 with 6 heads, T = 5477 with 2 to 16
+// heads; one or two query tiles, 1 to 8 splits, both combine forms): a
+// 128-key step takes 1.06 us with one query tile and 1.47 us with two; the
+// cluster combine about 1.0 and 2.8 us; the workspace combine, where the
+// last CTA of a group reads every split's partials back, 3.5 us and
+// 6 + 1.5 (splits - 2) us.
+constexpr double kStepUs[2] = {1.06, 1.47};
+constexpr double kLaunchUs = 4.0;
+constexpr double kWaveUs = 1.0;
+double combine_us(const Plan& pl, bool cluster) {
+    if (pl.splits < 2) return 0.0;
+    if (cluster) return pl.qt == 1 ? 1.0 : 2.8;
+    return pl.qt == 1 ? 3.5 : 6.0 + 1.5 * (pl.splits - 2);
+}
+double estimate_us(const Plan& pl, bool cluster) {
+    const long long ctas = static_cast<long long>(pl.units) * pl.splits;
+    long long waves;
+    if (cluster && pl.splits > 1) {
+        const long long per_wave = max_active_clusters(pl.qt, pl.splits);
+        if (per_wave <= 0) return -1.0;
+        waves = (static_cast<long long>(pl.units) + per_wave - 1) / per_wave;
+    } else {
+        waves = (ctas + 147) / 148;
+    }
+    const int steps = (pl.kv_tiles + pl.splits - 1) / pl.splits;
+    return kLaunchUs + static_cast<double>(waves) *
+                           (steps * kStepUs[pl.qt - 1] + kWaveUs + combine_us(pl, cluster));
+}
+
+// Query tiles per CTA and key splits: as asked (nonzero fields), else the
+// pair with the least estimated time. With a workspace (workspace_bytes > 0)
+// the splits combine through it and a split count whose partials do not fit
+// is not considered; without one the splits of a query group form a cluster
+// (at most kMaxClusterSplits). Ties keep the earlier candidate (two query
+// tiles first, fewer splits first), so asking again with a workspace of
+// exactly the size the first answer needs gives the same answer.
+struct Choice {
+    int qt, splits;
+};
+Choice choose(const bl_attention_args& a, uint64_t workspace_bytes) {
+    const int qts[2] = {2, 1};
+    Choice best{a.query_tiles == 1 ? 1 : 2, a.kv_splits > 0 ? static_cast<int>(a.kv_splits) : 1};
+    double best_t = -1.0;
+    const bool cluster = workspace_bytes == 0;
+    for (int qt : qts) {
+        if (a.query_tiles != 0 && static_cast<int>(a.query_tiles) != qt) continue;
+        const Plan p1 = plan(a, 1, qt);
+        int lo = 1, hi = std::max(1, p1.kv_tiles / 2);  // at least two key tiles per split
+        if (cluster) hi = std::min(hi, kMaxClusterSplits);
+        if (a.kv_splits > 0) lo = hi = static_cast<int>(a.kv_splits);
+        for (int sp = lo; sp <= hi; ++sp) {
+            const Plan pl = plan(a, sp, qt);
+            if (!cluster && pl.bytes > workspace_bytes) continue;
+            const double t = estimate_us(pl, cluster);
+            if (t < 0.0) continue;
+            if (best_t < 0.0 || t < best_t) best = Choice{qt, pl.splits}, best_t = t;
+        }
+    }
+    return best;
 }
 
 int validate(const bl_attention_args& a) {
     if (a.head_dim != HD) return fail(BL_ERR_UNSUPPORTED, "attention: head_dim %u (only 64)", a.head_dim);
     if (a.batch == 0 || a.tokens == 0 || a.heads == 0)
         return fail(BL_ERR_INVALID, "attention: zero dimension");
+    if (a.query_tiles > 2)
+        return fail(BL_ERR_INVALID, "attention: %u query tiles per CTA (0, 1 or 2)", a.query_tiles);
     if (a.head_begin >= a.head_end || a.head_end > a.heads)
         return fail(BL_ERR_INVALID, "attention: heads [%u, %u) outside [0, %u)", a.head_begin,
                     a.head_end, a.heads);
     if (a.row_begin >= a.row_end || a.row_end > a.tokens)
         return fail(BL_ERR_INVALID, "attention: rows [%u, %u) outside [0, %u)", a.row_begin,
                     a.row_end, a.tokens);
+    return BL_OK;
+}
+
+template <int QT>
+int make_launch(int out_dtype, bool peers, dim3 grid, const Plan& pl, bool cluster,
+                const CUtensorMap& tm_q, const CUtensorMap& tm, const Params& p,
+                const PeerParams& pq, Launch* out) {
+    using Sh = Shape<QT>;
+    auto kern = peers ? (out_dtype == BL_F16 ? attention_fwd<QT, BL_F16, true>
+                                             : attention_fwd<QT, BL_BF16, true>)
+              : out_dtype == BL_F32 ? attention_fwd<QT, BL_F32>
+              : out_dtype == BL_F16 ? attention_fwd<QT, BL_F16>
+                                    : attention_fwd<QT, BL_BF16>;
+    constexpr size_t smem = kSmemBytes<QT>;
+    BL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(smem)));
+    BL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0));
+    if constexpr (Sh::kRegSplit) {
+        // setmaxnreg.inc draws on the block's launch allocation: the split is
+        // sized for exactly kLaunchRegs per thread, so refuse any other build.
+        cudaFuncAttributes fa{};
+        BL_CUDA_TRY(cudaFuncGetAttributes(&fa, kern));
+        if (fa.numRegs != Sh::kLaunchRegs)
+            return fail(BL_ERR_UNSUPPORTED,
+                        "attention: kernel built with %d registers per thread, the register "
+                        "split needs exactly %d",
+                        fa.numRegs, Sh::kLaunchRegs);
+    }
+    out->op = 1;
+    const CUtensorMap tq = tm_q, tk = tm;
+    if (cluster) {
+        const dim3 cdim(1, 1, pl.splits);
+        out->run = [=](cudaStream_t s) {
+            return launch_k_cluster(kern, grid, dim3(Sh::kThreads), cdim, smem, s, tq, tk, tk, p,
+                                    pq);
+        };
+    } else {
+        out->run = [=](cudaStream_t s) {
+            return launch_k(kern, grid, dim3(Sh::kThreads), smem, s, tq, tk, tk, p, pq);
+        };
+    }
     return BL_OK;
 }
 
@@ -881,21 +1017,12 @@ int prepare(const bl_attention_args& a, void* workspace, uint64_t workspace_byte
                 return fail(BL_ERR_INVALID, "attention: peer %d has no aligned output", r);
     }
 
-    auto kern = peers != nullptr       ? (a.out_dtype == BL_F16 ? attention_fwd<BL_F16, true>
-                                                                : attention_fwd<BL_BF16, true>)
-                : a.out_dtype == BL_F32 ? attention_fwd<BL_F32>
-                : a.out_dtype == BL_F16 ? attention_fwd<BL_F16>
-                                        : attention_fwd<BL_BF16>;
-    BL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(kSmemBytes)));
-    BL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0));
-
-    // Key splits: as asked, or automatic (0). With a workspace the partials
-    // go through it (global combine); without one the splits of a query group
-    // form a thread-block cluster that combines in distributed shared memory.
-    int want = static_cast<int>(a.kv_splits);
-    if (want == 0) want = attention_auto_splits(a, workspace != nullptr ? workspace_bytes : 0);
-    const Plan pl = plan(a, want);
+    // Query tiles per CTA and key splits: as asked, or automatic (0). With
+    // a workspace the partials go through it (global combine); without one
+    // the splits of a query group form a thread-block cluster that combines
+    // in distributed shared memory.
+    const Choice ch = choose(a, workspace != nullptr ? workspace_bytes : 0);
+    const Plan pl = plan(a, ch.splits, ch.qt);
     const bool cluster = pl.splits > 1 && workspace == nullptr;
     if (cluster && pl.splits > kMaxClusterSplits)
         return fail(BL_ERR_CAPACITY,
@@ -909,13 +1036,13 @@ int prepare(const bl_attention_args& a, void* workspace, uint64_t workspace_byte
             return fail(BL_ERR_INVALID, "attention: workspace must be 256-byte aligned");
     }
 
-    CUtensorMap tm, tm_q;  // K / V tiles; the CTA's QT query tiles as one box
+    CUtensorMap tm, tm_q;  // K / V tiles; the CTA's query tiles as one box
     const uint64_t dims[3] = {row, a.tokens, a.batch};
     const uint64_t strides[2] = {row * 2, row * 2 * a.tokens};
     const uint32_t box[3] = {HD, BM, 1};
     rc = make_tmap_16bit_3d(&tm, a.qkv, dims, strides, box);
     if (rc != BL_OK) return rc;
-    const uint32_t qbox[3] = {HD, static_cast<uint32_t>(QT * BM), 1};
+    const uint32_t qbox[3] = {HD, static_cast<uint32_t>(pl.rows), 1};
     rc = make_tmap_16bit_3d(&tm_q, a.qkv, dims, strides, qbox);
     if (rc != BL_OK) return rc;
 
@@ -949,91 +1076,59 @@ int prepare(const bl_attention_args& a, void* workspace, uint64_t workspace_byte
 
     const dim3 grid(pl.q_ctas, a.head_end - a.head_begin, a.batch * pl.splits);
     if (grid.y > 65535 || grid.z > 65535) return fail(BL_ERR_INVALID, "attention: grid too large");
-    // setmaxnreg.inc draws on the block's launch allocation: the split above
-    // is sized for exactly kLaunchRegs per thread, so refuse any other build.
-    cudaFuncAttributes fa{};
-    BL_CUDA_TRY(cudaFuncGetAttributes(&fa, kern));
-    if (fa.numRegs != kLaunchRegs)
-        return fail(BL_ERR_UNSUPPORTED,
-                    "attention: kernel built with %d registers per thread, the register split "
-                    "needs exactly %d",
-                    fa.numRegs, kLaunchRegs);
-    out->op = 1;
-    if (cluster) {
-        const dim3 cdim(1, 1, pl.splits);
-        out->run = [=](cudaStream_t s) {
-            return launch_k_cluster(kern, grid, dim3(kThreads), cdim, kSmemBytes, s, tm_q, tm, tm,
-                                    p, pq);
-        };
-    } else {
-        out->run = [=](cudaStream_t s) {
-            return launch_k(kern, grid, dim3(kThreads), kSmemBytes, s, tm_q, tm, tm, p, pq);
-        };
-    }
-    return BL_OK;
+    return pl.qt == 1 ? make_launch<1>(a.out_dtype, peers != nullptr, grid, pl, cluster, tm_q, tm, p,
+                                       pq, out)
+                      : make_launch<2>(a.out_dtype, peers != nullptr, grid, pl, cluster, tm_q, tm, p,
+                                       pq, out);
 }
 
 // How many clusters of `splits` CTAs (this kernel's shared memory, one CTA
 // per SM) the B200 runs at once; clusters must sit within one GPC, so this
-// is below 148 / splits. Queried once per split count.
-int max_active_clusters(int splits) {
-    static int cache[kMaxClusterSplits + 1] = {};
+// is below 148 / splits. Queried once per (query tiles, split count).
+template <int QT>
+int query_active_clusters(int splits) {
+    auto kern = attention_fwd<QT, BL_F32>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kSmemBytes<QT>)) != cudaSuccess)
+        return 0;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(1, 1, splits);
+    cfg.blockDim = dim3(Shape<QT>::kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes<QT>;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = splits;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
+int max_active_clusters(int qt, int splits) {
+    static int cache[2][kMaxClusterSplits + 1] = {};
     static std::mutex mu;
     std::lock_guard<std::mutex> lk(mu);
-    if (splits < 1 || splits > kMaxClusterSplits) return 0;
-    if (cache[splits] == 0) {
-        auto kern = attention_fwd<BL_F32>;
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(kSmemBytes)) != cudaSuccess)
-            return 0;
-        cudaLaunchConfig_t cfg{};
-        cfg.gridDim = dim3(1, 1, splits);
-        cfg.blockDim = dim3(kThreads);
-        cfg.dynamicSmemBytes = kSmemBytes;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 1;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = splits;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
-            cudaGetLastError();
-            return 0;
-        }
-        cache[splits] = n > 0 ? n : -1;
+    if (splits < 1 || splits > kMaxClusterSplits || qt < 1 || qt > 2) return 0;
+    int& c = cache[qt - 1][splits];
+    if (c == 0) {
+        const int n = qt == 1 ? query_active_clusters<1>(splits) : query_active_clusters<2>(splits);
+        c = n > 0 ? n : -1;
     }
-    return cache[splits] > 0 ? cache[splits] : 0;
+    return c > 0 ? c : 0;
 }
 
 }  // namespace attn
 
-int attention_auto_splits(const bl_attention_args& a, uint64_t workspace_bytes) {
-    using namespace attn;
-    const Plan p1 = plan(a, 1);
-    if (workspace_bytes > 0) {  // global combine: fill the SMs within the workspace
-        int want = auto_splits(a);
-        while (want > 1 && plan(a, want).bytes > workspace_bytes) --want;
-        return want;
-    }
-    // Cluster combine: the split count with the least estimated time, waves
-    // of co-resident clusters times a wave's length. Measured on B200: a
-    // 128-key step of a CTA takes about 1.8 us, set-up about 0.5 us, the
-    // cluster combine about 3 us. Unsplit, one CTA per SM.
-    const long long units = static_cast<long long>(p1.units);
-    const int max_s = std::min(kMaxClusterSplits, std::max(1, p1.kv_tiles / 2));
-    int best = 1;
-    double best_t = 0.0;
-    for (int s = 1; s <= max_s; ++s) {
-        const long long per_wave = s == 1 ? 148 : max_active_clusters(s);
-        if (per_wave <= 0) continue;
-        const long long waves = (units + per_wave - 1) / per_wave;
-        const int steps = (p1.kv_tiles + s - 1) / s;
-        const double t = static_cast<double>(waves) * (steps * 1.8 + 0.5 + (s > 1 ? 3.0 : 0.0));
-        if (s == 1 || t < best_t) best = s, best_t = t;
-    }
-    return best;
+void attention_resolve(bl_attention_args& a, uint64_t workspace_bytes) {
+    const attn::Choice ch = attn::choose(a, workspace_bytes);
+    a.query_tiles = static_cast<uint32_t>(ch.qt);
+    a.kv_splits = static_cast<uint32_t>(ch.splits);
 }
 
 int prepare_attention(const bl_attention_args& a, Launch* out) {
@@ -1124,13 +1219,9 @@ extern "C" int bl_attention_noalloc(const bl_attention_args* args, void* stream)
     if (args == nullptr) return fail(BL_ERR_INVALID, "no-alloc attention: null args");
     int rc = attn::validate(*args);
     if (rc != BL_OK) return rc;
-    // the split count bl_attention would use with a workspace of this size
-    int want = static_cast<int>(args->kv_splits);
-    if (want == 0) {
-        want = attn::auto_splits(*args);
-        while (want > 1 && attn::plan(*args, want).bytes > kNoAllocScratchBytes) --want;
-    }
-    const attn::Plan pl = attn::plan(*args, want);
+    // the choice bl_attention makes with a workspace of this size
+    const attn::Choice ch = attn::choose(*args, kNoAllocScratchBytes);
+    const attn::Plan pl = attn::plan(*args, ch.splits, ch.qt);
     if (pl.bytes > kNoAllocScratchBytes)
         return fail(BL_ERR_CAPACITY,
                     "no-alloc attention: %d key splits need %zu bytes of scratch, more than "
@@ -1211,9 +1302,22 @@ extern "C" int bl_attention_peers(const bl_attention_args* args, bl_peers* peers
 
 extern "C" uint64_t bl_attention_workspace_bytes(const bl_attention_args* args) {
     if (args == nullptr || bl::attn::validate(*args) != BL_OK) return 0;
-    const int want = args->kv_splits == 0 ? bl::attn::auto_splits(*args)
-                                          : static_cast<int>(args->kv_splits);
-    return bl::attn::plan(*args, want).bytes;
+    const bl::attn::Choice ch = bl::attn::choose(*args, ~0ull);
+    return bl::attn::plan(*args, ch.splits, ch.qt).bytes;
+}
+
+extern "C" int bl_attention_choice(const bl_attention_args* args, uint32_t* query_tiles,
+                                   uint32_t* kv_splits) {
+    using namespace bl;
+    if (args == nullptr || query_tiles == nullptr || kv_splits == nullptr)
+        return fail(BL_ERR_INVALID, "attention choice: null argument");
+    int rc = attn::validate(*args);
+    if (rc != BL_OK) return rc;
+    bl_attention_args a = *args;
+    attention_resolve(a, a.workspace != nullptr ? a.workspace_bytes : 0);
+    *query_tiles = a.query_tiles;
+    *kv_splits = attn::plan(a, static_cast<int>(a.kv_splits), static_cast<int>(a.query_tiles)).splits;
+    return BL_OK;
 }
 
 extern "C" int bl_attention(const bl_attention_args* args, void* stream) {

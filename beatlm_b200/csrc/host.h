@@ -106,7 +106,9 @@ cudaError_t launch_k_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, dim3
 
 // Attention's automatic key-split count for these arguments given a
 // workspace of `workspace_bytes` (0 = none: the cluster combine).
-int attention_auto_splits(const bl_attention_args& a, uint64_t workspace_bytes);
+// Fills in the query tiles per CTA and key splits bl_attention would pick
+// (fields left 0) for a workspace of this size (0 = cluster combine).
+void attention_resolve(bl_attention_args& a, uint64_t workspace_bytes);
 
 inline int enqueue(const Launch& l, cudaStream_t s) {
     if (l.run_status) return l.run_status(s);

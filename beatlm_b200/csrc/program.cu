@@ -342,11 +342,10 @@ int prepare_part(const bl_kernel_spec& s, const std::vector<uint32_t>& edges, ui
         case BL_OP_ATTENTION: {
             bl_attention_args a = *static_cast<const bl_attention_args*>(s.args);
             rebind(a, r);
-            // Every part uses the whole kernel's key-split count, so each
-            // row is computed exactly as the whole kernel computes it.
-            if (a.kv_splits == 0)
-                a.kv_splits = static_cast<uint32_t>(attention_auto_splits(
-                    a, a.workspace != nullptr ? a.workspace_bytes : 0));
+            // Every part uses the whole kernel's key splits (and query
+            // tiles), so each row is computed exactly as the whole kernel
+            // computes it.
+            attention_resolve(a, a.workspace != nullptr ? a.workspace_bytes : 0);
             const uint32_t r0 = a.row_begin;
             a.row_begin = r0 + edges[i];
             a.row_end = r0 + edges[i + 1];

@@ -55,11 +55,12 @@ def pack_qkv(qkv, qk_dtype: str = "f16", device="cuda"):
 def attention_args(qkv, *, tokens, heads, out, head_dim=64, batch=1, qk_dtype="f16",
                    out_dtype=None, scale=None, rows=None, head_range=None, out_head_base=0,
                    qkv_row_stride=0, out_row_stride=None, workspace=None, kv_splits=0,
-                   trace=None):
+                   trace=None, query_tiles=0):
     """``kv_splits`` 0 picks the key-split count. Without ``workspace`` the
     splits of a query group combine in distributed shared memory (a cluster);
     with one (a zero-filled device buffer of at least
     ``attention_workspace_bytes`` bytes) they combine through it.
+    ``query_tiles``: 128-row query tiles per CTA (1 or 2; 0 picks).
     ``trace``: optional int64 device buffer for 8 timestamps per CTA."""
     if scale is None:
         scale = 1.0 / math.sqrt(head_dim)
@@ -76,13 +77,21 @@ def attention_args(qkv, *, tokens, heads, out, head_dim=64, batch=1, qk_dtype="f
                            kv_splits=kv_splits,
                            workspace=None if workspace is None else workspace.data_ptr(),
                            workspace_bytes=0 if workspace is None else workspace.numel(),
-                           trace=None if trace is None else trace.data_ptr())
+                           trace=None if trace is None else trace.data_ptr(),
+                           query_tiles=query_tiles)
 
 
 def attention_workspace_bytes(args) -> int:
     """Bytes of workspace ``bl_attention`` wants for these arguments (with
     ``kv_splits`` 0 it reports what the automatic choice would use)."""
     return N.lib().bl_attention_workspace_bytes(ctypes.byref(args))
+
+
+def attention_choice(args) -> tuple[int, int]:
+    """(query tiles per CTA, key splits) ``bl_attention`` takes for ``args``."""
+    qt, sp = ctypes.c_uint32(0), ctypes.c_uint32(0)
+    N.check(N.lib().bl_attention_choice(ctypes.byref(args), ctypes.byref(qt), ctypes.byref(sp)))
+    return qt.value, sp.value
 
 
 def attention_workspace(nbytes: int, device="cuda"):
@@ -95,7 +104,8 @@ def attention_workspace(nbytes: int, device="cuda"):
 def attention(qkv, *, tokens: int, heads: int, head_dim: int = 64, batch: int = 1,
               qk_dtype: str = "f16", out=None, out_dtype: str = "f32", scale: float | None = None,
               rows: tuple[int, int] | None = None, head_range: tuple[int, int] | None = None,
-              out_head_base: int = 0, stream=None, workspace=None, kv_splits: int = 0):
+              out_head_base: int = 0, stream=None, workspace=None, kv_splits: int = 0,
+              query_tiles: int = 0):
     """The fused scores -> scale -> softmax -> values chain of one layer
     (reference kernel.rs:722-777) on packed ``[batch][tokens][3][heads][64]``
     16-bit ``qkv``; returns ``out`` ``[batch][tokens][heads * 64]``."""
@@ -111,7 +121,7 @@ def attention(qkv, *, tokens: int, heads: int, head_dim: int = 64, batch: int = 
     a = attention_args(qkv, tokens=tokens, heads=heads, out=out, head_dim=head_dim, batch=batch,
                        qk_dtype=qk_dtype, out_dtype=odt, scale=scale, rows=rows,
                        head_range=head_range, out_head_base=out_head_base,
-                       workspace=workspace, kv_splits=kv_splits)
+                       workspace=workspace, kv_splits=kv_splits, query_tiles=query_tiles)
     N.check(N.lib().bl_attention(ctypes.byref(a), _stream_ptr(stream)))
     return out
 

@@ -126,7 +126,7 @@ typedef struct bl_attention_args {
     void* out;
     uint64_t out_row_stride; /* 0 = heads * head_dim */
     uint32_t out_head_base;
-    uint32_t kv_splits;      /* 0 = automatic, 1 = none */
+    uint32_t kv_splits;      /* 0 = automatic (with query_tiles), 1 = none */
     void* workspace;
     uint64_t workspace_bytes;
     /* Optional per-CTA timeline (NULL = off): CTA b writes %globaltimer
@@ -136,12 +136,25 @@ typedef struct bl_attention_args {
      * path does not reach stay as they were). CTAs are numbered x-fastest over the grid (query groups, heads,
      * batch x splits); the buffer holds 8 * CTAs uint64 values. */
     uint64_t* trace;
+    /* 128-row query tiles per CTA: 2 (a CTA of 12 warps, two softmax
+     * warpgroups), 1 (8 warps, one softmax warpgroup: twice the CTAs, for
+     * launches too small to fill the GPU), or 0 = automatic. With kv_splits
+     * also 0 the pair with the least estimated time is taken. Every row's
+     * result depends on the key splits only, never on this choice. */
+    uint32_t query_tiles;
 } bl_attention_args;
 
 int bl_attention(const bl_attention_args* args, void* stream);
 
 /* Workspace bytes bl_attention needs for these arguments (0: no split). */
 uint64_t bl_attention_workspace_bytes(const bl_attention_args* args);
+
+/* The query tiles per CTA and key splits bl_attention takes for these
+ * arguments (its automatic choice for fields left 0; with args->workspace
+ * NULL the cluster combine, else the workspace combine within
+ * args->workspace_bytes). Queries the current device's cluster occupancy. */
+int bl_attention_choice(const bl_attention_args* args, uint32_t* query_tiles,
+                        uint32_t* kv_splits);
 
 /*
  * bl_attention for callers that cannot allocate device memory. No counterpart

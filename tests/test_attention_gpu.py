@@ -55,12 +55,13 @@ def test_attention_matches_the_oracle(t, qk_dtype):
     assert rel <= REL_L2 and mx < 5e-3
 
 
-@pytest.mark.parametrize("t,splits", [(300, 2), (1370, 3), (1370, 0), (1370, 11), (129, 2),
-                                      (5477, 0)])
-def test_key_splits_match_the_oracle(t, splits):
+@pytest.mark.parametrize("t,splits,qt", [(300, 2, 2), (1370, 3, 2), (1370, 0, 2), (1370, 11, 2),
+                                         (129, 2, 2), (5477, 0, 2), (1370, 3, 1), (1370, 0, 1),
+                                         (5477, 0, 1)])
+def test_key_splits_match_the_oracle(t, splits, qt):
     """Keys split across CTAs, combined by the last CTA of each tile group
     through a caller-owned workspace; repeated calls reuse it (its counters
-    return to zero)."""
+    return to zero). ``qt`` query tiles of 128 rows per CTA."""
     import torch
     import beatlm_b200 as bl
     from beatlm_b200 import ops
@@ -69,16 +70,16 @@ def test_key_splits_match_the_oracle(t, splits):
     dev = bl.pack_qkv(qkv, "bf16")
     out = torch.zeros((1, t, h * 64), dtype=torch.float32, device="cuda")
     args = ops.attention_args(dev, tokens=t, heads=h, out=out, qk_dtype="bf16",
-                              kv_splits=splits)
+                              kv_splits=splits, query_tiles=qt)
     nbytes = ops.attention_workspace_bytes(args)
     ws = ops.attention_workspace(nbytes)
     for _ in range(2):
         out.zero_()
         bl.attention(dev, tokens=t, heads=h, qk_dtype="bf16", out=out, workspace=ws,
-                     kv_splits=splits)
+                     kv_splits=splits, query_tiles=qt)
     torch.cuda.synchronize()
     assert bl.status(reset=True).code == 0
-    units = h * -(-t // 256)  # one counter per (head, 256-row query group), at the end
+    units = h * -(-t // (128 * qt))  # one counter per (head, query group), at the end
     assert nbytes == 0 or not ws[nbytes - 4 * units:nbytes].any()  # counters back at zero
     rows = (0, t) if t < 2000 else (1000, 1130)
     want = oracle.attention(_rounded(qkv, "bf16")[0].reshape(t, -1), t, h, 64, rows=rows)
@@ -181,3 +182,45 @@ def test_hires_rows_sample():
     want = oracle.attention(ref_in[0].reshape(t, -1), t, h, 64, rows=(2048, 2048 + 130))
     rel, mx = _errors(got[0][2048:2048 + 130], want)
     assert rel <= REL_L2, rel
+
+
+@pytest.mark.parametrize("t,splits,std,out_dtype", [
+    (1, 1, 1.0, "f32"), (129, 1, 1.0, "f32"), (300, 2, 1.0, "bf16"), (700, 1, 2.0, "f32"),
+    (1370, 1, 1.0, "f32"), (1370, 2, 1.0, "bf16"), (1370, 3, 1.0, "f16"), (1370, 8, 1.0, "f32")])
+def test_one_query_tile_per_cta_equals_two(t, splits, std, out_dtype):
+    """One 128-row query tile per CTA (8 warps, two S buffers) against two
+    (12 warps, three S buffers): a row's arithmetic depends on the key splits
+    only, so with the same splits the outputs are the same bits, in both
+    combine forms; and the one-tile kernel meets the oracle."""
+    import torch
+    import beatlm_b200 as bl
+    from beatlm_b200 import ops
+    h = 6
+    qkv = oracle.normal(900 + t + splits, t * 3 * h * 64, 0.0, std).reshape(1, t, 3, h, 64)
+    dev = bl.pack_qkv(qkv, "bf16")
+    run = lambda qt, ws=None: bl.attention(dev, tokens=t, heads=h, qk_dtype="bf16",
+                                           out_dtype=out_dtype, kv_splits=splits,
+                                           query_tiles=qt, workspace=ws)
+    two, one = run(2), run(1)
+    torch.cuda.synchronize()
+    assert bl.status(reset=True).code == 0
+    assert torch.equal(one, two)
+    if splits > 1:
+        a = ops.attention_args(dev, tokens=t, heads=h, out=one, qk_dtype="bf16",
+                               kv_splits=splits, query_tiles=1)
+        one_ws = run(1, ops.attention_workspace(ops.attention_workspace_bytes(a)))
+        torch.cuda.synchronize()
+        assert bl.status(reset=True).code == 0
+        assert torch.equal(one_ws, one)
+    want = oracle.attention(_rounded(qkv, "bf16")[0].reshape(t, -1), t, h, 64)
+    rel, mx = _errors(one.float().cpu().numpy()[0], want)
+    print("T=%d splits=%d std=%g %s: QT=1 rel-L2 %.3e max-abs %.3e" % (t, splits, std, out_dtype,
+                                                                      rel, mx))
+    assert rel <= (4e-3 if out_dtype == "bf16" else REL_L2), rel
+
+
+def test_query_tiles_beyond_two_are_rejected():
+    import beatlm_b200 as bl
+    dev = bl.pack_qkv(np.zeros((1, 64, 3, 2, 64), np.float32), "f16")
+    with pytest.raises(bl.BackendError, match="query tiles"):
+        bl.attention(dev, tokens=64, heads=2, query_tiles=3)
