@@ -59,6 +59,7 @@ SIGNATURES = {
     "bl_attention_noalloc": (ctypes.c_int, [ctypes.POINTER(AttentionArgs), ctypes.c_void_p]),
     "bl_attention_choice": (ctypes.c_int, [ctypes.POINTER(AttentionArgs),
                                            ctypes.POINTER(ctypes.c_uint32),
+                                           ctypes.POINTER(ctypes.c_uint32),
                                            ctypes.POINTER(ctypes.c_uint32)]),
 }
 

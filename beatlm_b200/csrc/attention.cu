@@ -112,8 +112,15 @@ struct Params {
     long long out_row_stride;    // elements
     long long out_batch_stride;  // elements
     int out_head_base;
-    int splits;       // key splits; gridDim.z = batch * splits
+    int splits;       // key splits; gridDim.z = batch * splits (uniform grid)
     int cluster;      // 1: the splits of a query group are one cluster, combined in DSMEM
+    // Mixed grid (cluster form only): a 1-D grid of clusters of `splits`
+    // CTAs over the query groups u = (batch * heads_rel + head) * q_ctas +
+    // tile; groups [0, head_units) run unsplit (a cluster then holds
+    // `splits` different groups, which do not combine), the rest split
+    // `splits` ways, one cluster each. 0 = the uniform grid.
+    int head_units;
+    int q_ctas;       // query groups per head
     int kv_tiles;     // ceil(tokens / BN)
     uint4* part_o;    // [unit][split][ROWS][HD / 8]: f16 O / l of each row
     float2* part_ml;  // [unit][split][ROWS]: (max, sum)
@@ -147,6 +154,9 @@ struct SmemTail {
     uint32_t tmem_base;
     int abort;
     unsigned last;  // this CTA combines the splits
+    // this CTA's query group, key split and the group's split count (written
+    // once at set-up and read where needed, so no role keeps them live)
+    int unit, split, nsplit;
 };
 
 constexpr int kMaxClusterSplits = 8;  // portable cluster size
@@ -294,17 +304,36 @@ __global__ void __launch_bounds__(Shape<kQT>::kThreads, 1)
 
     const int warp = warp_id();
     const int lane = lane_id();
-    const int head = p.head_begin + blockIdx.y;
-    const int batch = blockIdx.z / p.splits;
-    const int split = blockIdx.z % p.splits;
-    const int q0 = p.row_begin + blockIdx.x * ROWS;
-    // this CTA's key tiles [t0, t1)
-    const int t0 = p.kv_tiles * split / p.splits;
-    const int t1 = p.kv_tiles * (split + 1) / p.splits;
-    const int n = t1 - t0;
+    // This CTA's place, from the shared copy: its query group (unit), key
+    // split and the group's split count; the group's head, sequence and
+    // first query row; its key tiles [t0, t0 + n).
+    const volatile int* coord = &tail->unit;
+    auto c_unit = [&]() { return coord[0]; };
+    auto c_split = [&]() { return coord[1]; };
+    auto c_nsplit = [&]() { return coord[2]; };
+    auto c_head = [&](int unit) { return p.head_begin + (unit / p.q_ctas) % p.heads_rel; };
+    auto c_batch = [&](int unit) { return unit / (p.q_ctas * p.heads_rel); };
+    auto c_q0 = [&](int unit) { return p.row_begin + (unit % p.q_ctas) * ROWS; };
+    auto c_t0 = [&]() { return p.kv_tiles * c_split() / c_nsplit(); };
+    auto c_n = [&]() { return p.kv_tiles * (c_split() + 1) / c_nsplit() - c_t0(); };
 
     if (threadIdx.x == 0) {
         trace_stamp(p.trace, 0);
+        int unit, split, nsplit = p.splits;
+        if (p.head_units > 0) {
+            const int b = static_cast<int>(blockIdx.x);
+            if (b < p.head_units) {
+                unit = b, split = 0, nsplit = 1;
+            } else {
+                unit = p.head_units + (b - p.head_units) / p.splits;
+                split = (b - p.head_units) % p.splits;
+            }
+        } else {
+            unit = (static_cast<int>(blockIdx.z / p.splits) * p.heads_rel +
+                    static_cast<int>(blockIdx.y)) * p.q_ctas + static_cast<int>(blockIdx.x);
+            split = static_cast<int>(blockIdx.z % p.splits);
+        }
+        tail->unit = unit, tail->split = split, tail->nsplit = nsplit;
         mbar_init(smem_u32(&tail->q_full), 1);
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(smem_u32(&tail->kv_full[s]), 1);
@@ -319,12 +348,13 @@ __global__ void __launch_bounds__(Shape<kQT>::kThreads, 1)
             mbar_init(smem_u32(&tail->o_final[t]), 1);
         }
         mbar_init(smem_u32(&tail->drain), 1);
-        if (p.cluster) {
+        if (p.cluster && nsplit > 1) {
             // one arrival per pushing warp: the warps w = rank (mod splits) of
-            // each other CTA of the cluster
+            // each other CTA of the cluster (the mixed grid's unsplit groups
+            // never combine and leave it uninitialised)
             const int me = static_cast<int>(cluster_rank());
-            const int nw = (ROWS / 32 - me + p.splits - 1) / p.splits;
-            mbar_init(smem_u32(&tail->parts_full), static_cast<uint32_t>(nw * (p.splits - 1)));
+            const int nw = (ROWS / 32 - me + nsplit - 1) / nsplit;
+            mbar_init(smem_u32(&tail->parts_full), static_cast<uint32_t>(nw * (nsplit - 1)));
         }
         tail->abort = 0;
         tail->last = 0;
@@ -360,9 +390,11 @@ __global__ void __launch_bounds__(Shape<kQT>::kThreads, 1)
             // bulk copies complete one after another). Lane 0 alone waits
             // for a free stage and the vote hands the outcome to the warp.
             const uint32_t b_q = smem_u32(&tail->q_full);
+            const int unit = c_unit(), head = c_head(unit), batch = c_batch(unit);
+            const int t0 = c_t0(), n = c_n();
             if (lane == 0) {
                 mbar_arrive_expect_tx(b_q, QT * kTileBytes);
-                tma_load_3d(smem_u32(sQ), &tm_q, p.q_col0 + head * HD, q0, batch, b_q);
+                tma_load_3d(smem_u32(sQ), &tm_q, p.q_col0 + head * HD, c_q0(unit), batch, b_q);
             }
             int loaded = 0;  // key tiles whose loads were started
             for (int i = 0; i < n; ++i) {
@@ -411,6 +443,7 @@ __global__ void __launch_bounds__(Shape<kQT>::kThreads, 1)
             };
             const uint32_t idesc_s = idesc_f16(BM, BN, p.qk_fmt, p.qk_fmt, 0, 0);
             const uint32_t idesc_o = idesc_f16(BM, HD, 0, 0, 0, 1);
+            const int n = c_n();
             bool ok = wait_all(smem_u32(&tail->q_full), 0, 0xFFFF);
             tc_fence_after();
             auto wait_kv = [&](int i) -> bool {
@@ -514,6 +547,7 @@ __global__ void __launch_bounds__(Shape<kQT>::kThreads, 1)
         float m_used = -INFINITY;
         float l = 0.0f;
         bool ok = true;
+        const int t0 = c_t0(), n = c_n();
         for (int i = 0; i < n; ++i) {
             const uint32_t s_col = t_lane + kColS + 128 * ((QT * i + t) % kSBufs);
             const uint32_t b_p = smem_u32(&tail->p_full[t][i & 1]);
@@ -624,7 +658,9 @@ __global__ void __launch_bounds__(Shape<kQT>::kThreads, 1)
             tmem_wait_ld();
         }
         const int crow = t * BM + row;  // row within the CTA's ROWS
-        const int grow = q0 + crow;
+        const int unit = c_unit(), split = c_split(), nsplit = c_nsplit();
+        const int head = c_head(unit), batch = c_batch(unit);
+        const int grow = c_q0(unit) + crow;
         const bool store = grow < p.row_end && grow < p.tokens;
         auto row_offset = [&]() {
             const size_t esz = kOutDtype == BL_F32 ? 4 : 2;
@@ -676,7 +712,7 @@ __global__ void __launch_bounds__(Shape<kQT>::kThreads, 1)
         };
         bool do_store = ok && store;
         float inv_l = 1.0f / l;
-        if (p.splits > 1) {
+        if (nsplit > 1) {
             // ---------------------------------------------- split-key combine
             // Every split's partial for a row is O / l rounded to f16 (a
             // convex combination of f16 V rows, so within f16 range) and
@@ -696,13 +732,13 @@ __global__ void __launch_bounds__(Shape<kQT>::kThreads, 1)
                                    pack_f16x2(o[8 * k + 6] * il, o[8 * k + 7] * il));
             auto combine = [&](auto&& part_on, auto&& part_ml, bool valid) {
                 float mxs = -INFINITY;
-                for (int sp = 0; sp < p.splits; ++sp) mxs = fmaxf(mxs, part_ml(sp).x);
+                for (int sp = 0; sp < nsplit; ++sp) mxs = fmaxf(mxs, part_ml(sp).x);
                 float acc[HD];
 #pragma unroll
                 for (int k = 0; k < HD; ++k) acc[k] = 0.0f;
                 float wsum = 0.0f;
 #pragma unroll 1
-                for (int sp = 0; sp < p.splits; ++sp) {
+                for (int sp = 0; sp < nsplit; ++sp) {
                     const float2 ml = part_ml(sp);
                     const float w = ml.y > 0.0f ? ex2(ml.x - mxs) * ml.y : 0.0f;
                     wsum += w;
@@ -735,9 +771,9 @@ __global__ void __launch_bounds__(Shape<kQT>::kThreads, 1)
                 cluster_wait();  // every barrier of the cluster is initialised
                 if (threadIdx.x == 32 * kSoftmaxWarp0) trace_stamp(p.trace, 4);
                 const int me = static_cast<int>(cluster_rank());
-                const int owner = (crow >> 5) % p.splits;
-                const int slot = ((crow >> 5) / p.splits) * 32 + (crow & 31);
-                const int slots = ((ROWS / 32 + p.splits - 1) / p.splits) * 32;
+                const int owner = (crow >> 5) % nsplit;
+                const int slot = ((crow >> 5) / nsplit) * 32 + (crow & 31);
+                const int slots = ((ROWS / 32 + nsplit - 1) / nsplit) * 32;
                 const uint32_t vstep = static_cast<uint32_t>(slots * 16);
                 if (owner != me) {
                     const int src = me < owner ? me : me - 1;
@@ -781,41 +817,47 @@ __global__ void __launch_bounds__(Shape<kQT>::kThreads, 1)
                 // ------------------------------ workspace form: partials in
                 // the caller's buffer, the last CTA of the group combines (an
                 // atomic counter; nothing waits)
-                const size_t unit = (static_cast<size_t>(batch) * p.heads_rel + blockIdx.y) *
-                                        gridDim.x + blockIdx.x;
-                uint4* po = p.part_o + ((unit * p.splits + split) * ROWS + crow) * (HD / 8);
-                float2* pml = p.part_ml + (unit * p.splits + split) * ROWS + crow;
+                // (the uniform grid: every group has p.splits splits)
+                const size_t u = static_cast<size_t>(unit);
+                uint4* po = p.part_o + ((u * p.splits + split) * ROWS + crow) * (HD / 8);
+                float2* pml = p.part_ml + (u * p.splits + split) * ROWS + crow;
 #pragma unroll
                 for (int k = 0; k < HD / 8; ++k) po[k] = on[k];
                 *pml = make_float2(mine_m, mine_l);
                 __threadfence();
                 softmax_bar<QT>();
                 if (threadIdx.x == 32 * kSoftmaxWarp0) {
-                    const unsigned prev = atomicAdd(p.counters + unit, 1u);
+                    const unsigned prev = atomicAdd(p.counters + u, 1u);
                     tail->last = prev == static_cast<unsigned>(p.splits) - 1;
                 }
                 softmax_bar<QT>();
                 if (tail->last) {
                     __threadfence();
                     if (kPeers || store) {
-                        const uint4* bo = p.part_o + (unit * p.splits * ROWS + crow) * (HD / 8);
-                        const float2* bml = p.part_ml + unit * p.splits * ROWS + crow;
+                        const uint4* bo = p.part_o + (u * p.splits * ROWS + crow) * (HD / 8);
+                        const float2* bml = p.part_ml + u * p.splits * ROWS + crow;
                         combine([&](int sp, int k) { return __ldcg(bo + static_cast<size_t>(sp) * ROWS * (HD / 8) + k); },
                                 [&](int sp) { return __ldcg(bml + static_cast<size_t>(sp) * ROWS); },
                                 store);
                     }
-                    if (threadIdx.x == 32 * kSoftmaxWarp0) p.counters[unit] = 0u;  // self-cleaning
+                    if (threadIdx.x == 32 * kSoftmaxWarp0) p.counters[u] = 0u;  // self-cleaning
                 }
             }
         }
         if (kPeers) {
-            if (p.splits == 1) store_out(o, inv_l, do_store);  // warp-collective
+            if (nsplit == 1) store_out(o, inv_l, do_store);  // warp-collective
         } else if (do_store) {
             store_out(o, inv_l, true);
         }
         // head-parallel exchange: trace slot 6 is the first softmax warp
         // past its row stores
         if (kPeers && threadIdx.x == 32 * kSoftmaxWarp0) trace_stamp(p.trace, 6);
+        // an unsplit group in a cluster of a mixed grid: the wait of the
+        // cluster barrier arrived on at set-up (no remote access follows)
+        if (p.cluster && nsplit == 1) {
+            __syncwarp();
+            cluster_wait();
+        }
     }
 
     tc_fence_before();
@@ -835,7 +877,8 @@ struct Plan {
     int q_ctas;
     int kv_tiles;
     size_t units;
-    size_t bytes;  // workspace
+    size_t bytes;    // workspace
+    int head_units;  // mixed grid: the unsplit groups before the split ones (0: uniform)
 };
 
 Plan plan(const bl_attention_args& a, int splits, int qt) {
@@ -881,6 +924,20 @@ double combine_us(const Plan& pl, bool cluster) {
     return pl.qt == 1 ? 3.5 : 6.0 + 1.5 * (pl.splits - 2);
 }
 double estimate_us(const Plan& pl, bool cluster) {
+    if (pl.head_units > 0) {
+        // mixed grid: full waves of unsplit groups in clusters, then the
+        // remaining groups split, one cluster each
+        const long long per_wave = max_active_clusters(pl.qt, pl.splits);
+        if (per_wave <= 0) return -1.0;
+        const long long head_waves = pl.head_units / (per_wave * pl.splits);
+        const long long rest = static_cast<long long>(pl.units) - pl.head_units;
+        const long long tail_waves = (rest + per_wave - 1) / per_wave;
+        const int steps = (pl.kv_tiles + pl.splits - 1) / pl.splits;
+        return kLaunchUs +
+               static_cast<double>(head_waves) * (pl.kv_tiles * kStepUs[pl.qt - 1] + kWaveUs) +
+               static_cast<double>(tail_waves) *
+                   (steps * kStepUs[pl.qt - 1] + kWaveUs + combine_us(pl, true));
+    }
     const long long ctas = static_cast<long long>(pl.units) * pl.splits;
     long long waves;
     if (cluster && pl.splits > 1) {
@@ -902,12 +959,16 @@ double estimate_us(const Plan& pl, bool cluster) {
 // (at most kMaxClusterSplits). Ties keep the earlier candidate (two query
 // tiles first, fewer splits first), so asking again with a workspace of
 // exactly the size the first answer needs gives the same answer.
+// With `mixed` (the cluster form with the split count left automatic) the
+// candidates also include mixed grids: as many groups as fill whole waves of
+// clusters run unsplit and only the remainder is split, so the last wave is
+// short instead of a third full.
 struct Choice {
-    int qt, splits;
+    int qt, splits, head_units;
 };
-Choice choose(const bl_attention_args& a, uint64_t workspace_bytes) {
+Choice choose(const bl_attention_args& a, uint64_t workspace_bytes, bool mixed = false) {
     const int qts[2] = {2, 1};
-    Choice best{a.query_tiles == 1 ? 1 : 2, a.kv_splits > 0 ? static_cast<int>(a.kv_splits) : 1};
+    Choice best{a.query_tiles == 1 ? 1 : 2, a.kv_splits > 0 ? static_cast<int>(a.kv_splits) : 1, 0};
     double best_t = -1.0;
     const bool cluster = workspace_bytes == 0;
     for (int qt : qts) {
@@ -921,7 +982,18 @@ Choice choose(const bl_attention_args& a, uint64_t workspace_bytes) {
             if (!cluster && pl.bytes > workspace_bytes) continue;
             const double t = estimate_us(pl, cluster);
             if (t < 0.0) continue;
-            if (best_t < 0.0 || t < best_t) best = Choice{qt, pl.splits}, best_t = t;
+            if (best_t < 0.0 || t < best_t) best = Choice{qt, pl.splits, 0}, best_t = t;
+        }
+        if (!(mixed && cluster && a.kv_splits == 0)) continue;
+        for (int sp = 2; sp <= hi; ++sp) {
+            Plan pl = plan(a, sp, qt);
+            if (pl.splits != sp) continue;
+            const long long wave = static_cast<long long>(max_active_clusters(qt, sp)) * sp;
+            if (wave <= 0) continue;
+            pl.head_units = static_cast<int>(static_cast<long long>(pl.units) / wave * wave);
+            if (pl.head_units == 0 || static_cast<size_t>(pl.head_units) == pl.units) continue;
+            const double t = estimate_us(pl, true);
+            if (t >= 0.0 && t < best_t) best = Choice{qt, sp, pl.head_units}, best_t = t;
         }
     }
     return best;
@@ -970,7 +1042,7 @@ int make_launch(int out_dtype, bool peers, dim3 grid, const Plan& pl, bool clust
     out->op = 1;
     const CUtensorMap tq = tm_q, tk = tm;
     if (cluster) {
-        const dim3 cdim(1, 1, pl.splits);
+        const dim3 cdim = pl.head_units > 0 ? dim3(pl.splits, 1, 1) : dim3(1, 1, pl.splits);
         out->run = [=](cudaStream_t s) {
             return launch_k_cluster(kern, grid, dim3(Sh::kThreads), cdim, smem, s, tq, tk, tk, p,
                                     pq);
@@ -1021,8 +1093,9 @@ int prepare(const bl_attention_args& a, void* workspace, uint64_t workspace_byte
     // a workspace the partials go through it (global combine); without one
     // the splits of a query group form a thread-block cluster that combines
     // in distributed shared memory.
-    const Choice ch = choose(a, workspace != nullptr ? workspace_bytes : 0);
-    const Plan pl = plan(a, ch.splits, ch.qt);
+    const Choice ch = choose(a, workspace != nullptr ? workspace_bytes : 0, true);
+    Plan pl = plan(a, ch.splits, ch.qt);
+    pl.head_units = ch.head_units;
     const bool cluster = pl.splits > 1 && workspace == nullptr;
     if (cluster && pl.splits > kMaxClusterSplits)
         return fail(BL_ERR_CAPACITY,
@@ -1064,6 +1137,8 @@ int prepare(const bl_attention_args& a, void* workspace, uint64_t workspace_byte
     p.splits = pl.splits;
     p.cluster = cluster ? 1 : 0;
     p.kv_tiles = pl.kv_tiles;
+    p.head_units = cluster ? pl.head_units : 0;
+    p.q_ctas = pl.q_ctas;
     if (pl.splits > 1 && !cluster) {
         uint8_t* ws = static_cast<uint8_t*>(workspace);
         p.part_o = reinterpret_cast<uint4*>(ws);
@@ -1074,8 +1149,14 @@ int prepare(const bl_attention_args& a, void* workspace, uint64_t workspace_byte
     p.status = status_ptr();
     const PeerParams pq = peers != nullptr ? *peers : PeerParams{};
 
-    const dim3 grid(pl.q_ctas, a.head_end - a.head_begin, a.batch * pl.splits);
-    if (grid.y > 65535 || grid.z > 65535) return fail(BL_ERR_INVALID, "attention: grid too large");
+    // the uniform grid: (query groups, heads, batch x splits); the mixed
+    // grid: the unsplit groups, then `splits` CTAs for each remaining group
+    const dim3 grid = p.head_units > 0
+                          ? dim3(static_cast<unsigned>(p.head_units +
+                                                       (pl.units - p.head_units) * pl.splits))
+                          : dim3(pl.q_ctas, a.head_end - a.head_begin, a.batch * pl.splits);
+    if (grid.y > 65535 || grid.z > 65535 || pl.units * pl.splits >= (1u << 31))
+        return fail(BL_ERR_INVALID, "attention: grid too large");
     return pl.qt == 1 ? make_launch<1>(a.out_dtype, peers != nullptr, grid, pl, cluster, tm_q, tm, p,
                                        pq, out)
                       : make_launch<2>(a.out_dtype, peers != nullptr, grid, pl, cluster, tm_q, tm, p,
@@ -1307,16 +1388,18 @@ extern "C" uint64_t bl_attention_workspace_bytes(const bl_attention_args* args) 
 }
 
 extern "C" int bl_attention_choice(const bl_attention_args* args, uint32_t* query_tiles,
-                                   uint32_t* kv_splits) {
+                                   uint32_t* kv_splits, uint32_t* unsplit_groups) {
     using namespace bl;
-    if (args == nullptr || query_tiles == nullptr || kv_splits == nullptr)
+    if (args == nullptr || query_tiles == nullptr || kv_splits == nullptr ||
+        unsplit_groups == nullptr)
         return fail(BL_ERR_INVALID, "attention choice: null argument");
     int rc = attn::validate(*args);
     if (rc != BL_OK) return rc;
-    bl_attention_args a = *args;
-    attention_resolve(a, a.workspace != nullptr ? a.workspace_bytes : 0);
-    *query_tiles = a.query_tiles;
-    *kv_splits = attn::plan(a, static_cast<int>(a.kv_splits), static_cast<int>(a.query_tiles)).splits;
+    const attn::Choice ch =
+        attn::choose(*args, args->workspace != nullptr ? args->workspace_bytes : 0, true);
+    *query_tiles = static_cast<uint32_t>(ch.qt);
+    *kv_splits = static_cast<uint32_t>(attn::plan(*args, ch.splits, ch.qt).splits);
+    *unsplit_groups = static_cast<uint32_t>(ch.head_units);
     return BL_OK;
 }
 

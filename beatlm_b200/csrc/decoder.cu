@@ -83,6 +83,29 @@ __global__ void blocks_to_map_kernel(const float* __restrict__ blocks, const flo
     }
 }
 
+// cout a multiple of 4 (every DPT width) and every index below 2^31: a thread
+// moves 4 consecutive channels of one output pixel with 16-byte loads and
+// stores and 32-bit index arithmetic (the 64-bit per-element divisions of the
+// kernel above bound it, not its memory traffic).
+__global__ void blocks_to_map_vec4_kernel(const float4* __restrict__ blocks,
+                                          const float4* __restrict__ bias, float4* __restrict__ out,
+                                          int w, int f, int c4, unsigned total) {
+    const int ow = w * f;
+    for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const unsigned p = i / static_cast<unsigned>(c4);
+        const int ch = static_cast<int>(i - p * static_cast<unsigned>(c4));
+        const int oy = static_cast<int>(p / static_cast<unsigned>(ow));
+        const int ox = static_cast<int>(p - static_cast<unsigned>(oy) * static_cast<unsigned>(ow));
+        const int y = oy / f, ky = oy - y * f, x = ox / f, kx = ox - x * f;
+        float4 v = __ldg(blocks + ((y * w + x) * f * f + ky * f + kx) * c4 + ch);
+        if (bias != nullptr) {
+            const float4 b = __ldg(bias + ch);
+            v.x += b.x, v.y += b.y, v.z += b.z, v.w += b.w;
+        }
+        out[i] = v;
+    }
+}
+
 // Corners aligned: output row oy reads position oy (ih-1)/(oh-1) (0 for one
 // row) between its floor and the next row, clamped; columns likewise.
 __device__ __forceinline__ void axis(int o, int in, int outn, int* i0, int* i1, float* l) {
@@ -238,8 +261,19 @@ int bl_blocks_to_map(const float* blocks, const float* bias, float* out, uint32_
     if (blocks == nullptr || out == nullptr) return fail(BL_ERR_INVALID, "blocks_to_map: null argument");
     if (h == 0 || w == 0 || f == 0 || cout == 0) return fail(BL_ERR_INVALID, "blocks_to_map: zero dimension");
     const long long work = 1ll * h * f * w * f * cout;
-    dec::blocks_to_map_kernel<<<dec::grid_for(work), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        blocks, bias, out, h, w, f, cout);
+    const bool vec = cout % 4 == 0 &&
+                     ((reinterpret_cast<uintptr_t>(blocks) | reinterpret_cast<uintptr_t>(bias) |
+                       reinterpret_cast<uintptr_t>(out)) & 15u) == 0 &&
+                     work < (1ll << 31) - 2ll * 256 * 8 * 148;
+    if (vec)
+        dec::blocks_to_map_vec4_kernel<<<dec::grid_for(work / 4), 256, 0,
+                                         static_cast<cudaStream_t>(stream)>>>(
+            reinterpret_cast<const float4*>(blocks), reinterpret_cast<const float4*>(bias),
+            reinterpret_cast<float4*>(out), static_cast<int>(w), static_cast<int>(f),
+            static_cast<int>(cout / 4), static_cast<unsigned>(work / 4));
+    else
+        dec::blocks_to_map_kernel<<<dec::grid_for(work), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+            blocks, bias, out, h, w, f, cout);
     BL_CUDA_TRY(cudaGetLastError());
     return BL_OK;
 }

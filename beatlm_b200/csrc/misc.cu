@@ -144,30 +144,38 @@ __global__ void __launch_bounds__(128) layernorm_vec_kernel(bl_layernorm_args a,
 // Patch matrix: one thread per (patch, 8 consecutive taps). Tap t of a patch
 // is (ky, kx, ci) = (t / (p*cin), (t / cin) % p, t % cin), the HWIO order of
 // the reference's patch weights, so row . weight[cout][t] is its patch_embed.
+// Index arithmetic in 32 bits (the host checks that every index fits): the
+// divisions happen once per thread, and the 8 taps step (ky, kx, ci) by
+// increments, since run-time integer divisions dominated the kernel.
 __global__ void patchify_kernel(bl_patchify_args a, int grid_side, int taps) {
     pdl_trigger();
     pdl_wait();
-    const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-    const int groups = static_cast<int>(a.k_pad / 8);
-    const long long patches = static_cast<long long>(a.frames) * grid_side * grid_side;
-    if (idx >= patches * groups) return;
-    const long long patch = idx / groups;
-    const int g = static_cast<int>(idx % groups);
-    const int f = static_cast<int>(patch / (grid_side * grid_side));
-    const int pp = static_cast<int>(patch % (grid_side * grid_side));
-    const int gy = pp / grid_side, gx = pp % grid_side;
+    const unsigned idx = blockIdx.x * blockDim.x + threadIdx.x;
+    const unsigned groups = a.k_pad / 8;
+    const unsigned per_frame = static_cast<unsigned>(grid_side * grid_side);
+    if (idx >= a.frames * per_frame * groups) return;
+    const unsigned patch = idx / groups;
+    const int g = static_cast<int>(idx - patch * groups);
+    const unsigned f = patch / per_frame;
+    const int pp = static_cast<int>(patch - f * per_frame);
+    const int gy = pp / grid_side, gx = pp - (pp / grid_side) * grid_side;
     const int P = static_cast<int>(a.patch), C = static_cast<int>(a.cin);
-    const float* img = a.image + static_cast<long long>(f) * a.side * a.side * C;
+    const int side = static_cast<int>(a.side);
+    const float* img = a.image + static_cast<size_t>(f) * side * side * C;
+    int t = g * 8;
+    int ky = t / (P * C);
+    int kx = (t - ky * P * C) / C;
+    int ci = t - ky * P * C - kx * C;
     uint16_t h[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const int t = g * 8 + j;
+    for (int j = 0; j < 8; ++j, ++t) {
         float v = 0.0f;
-        if (t < taps) {
-            const int ky = t / (P * C), kx = (t / C) % P, ci = t % C;
-            v = img[(static_cast<long long>(gy * P + ky) * a.side + gx * P + kx) * C + ci];
-        }
+        if (t < taps) v = img[((gy * P + ky) * side + gx * P + kx) * C + ci];
         h[j] = to16(v, a.a_dtype);
+        if (++ci == C) {
+            ci = 0;
+            if (++kx == P) kx = 0, ++ky;
+        }
     }
     uint4 w;
     w.x = h[0] | (static_cast<uint32_t>(h[1]) << 16);
@@ -254,6 +262,9 @@ int prepare_patchify(const bl_patchify_args& a, Launch* out) {
         return fail(BL_ERR_INVALID, "patchify: class-token rows need cls, pos and dim");
     const int g = static_cast<int>(a.side / a.patch);
     const long long work = static_cast<long long>(a.frames) * g * g * (a.k_pad / 8);
+    if (work >= (1ll << 31) || 1ll * a.side * a.side * a.cin >= (1ll << 31))
+        return fail(BL_ERR_UNSUPPORTED, "patchify: %u frames of %u px exceed 32-bit indexing",
+                    a.frames, a.side);
     const unsigned blocks = static_cast<unsigned>((work + 255) / 256);
     out->op = 4;
     out->run = [=](cudaStream_t s) {

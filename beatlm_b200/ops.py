@@ -87,11 +87,14 @@ def attention_workspace_bytes(args) -> int:
     return N.lib().bl_attention_workspace_bytes(ctypes.byref(args))
 
 
-def attention_choice(args) -> tuple[int, int]:
-    """(query tiles per CTA, key splits) ``bl_attention`` takes for ``args``."""
-    qt, sp = ctypes.c_uint32(0), ctypes.c_uint32(0)
-    N.check(N.lib().bl_attention_choice(ctypes.byref(args), ctypes.byref(qt), ctypes.byref(sp)))
-    return qt.value, sp.value
+def attention_choice(args) -> tuple[int, int, int]:
+    """(query tiles per CTA, key splits, unsplit query groups) ``bl_attention``
+    takes for ``args`` (the last nonzero for a mixed grid: that many groups
+    unsplit, the rest split)."""
+    qt, sp, un = ctypes.c_uint32(0), ctypes.c_uint32(0), ctypes.c_uint32(0)
+    N.check(N.lib().bl_attention_choice(ctypes.byref(args), ctypes.byref(qt), ctypes.byref(sp),
+                                        ctypes.byref(un)))
+    return qt.value, sp.value, un.value
 
 
 def attention_workspace(nbytes: int, device="cuda"):

@@ -152,9 +152,15 @@ uint64_t bl_attention_workspace_bytes(const bl_attention_args* args);
 /* The query tiles per CTA and key splits bl_attention takes for these
  * arguments (its automatic choice for fields left 0; with args->workspace
  * NULL the cluster combine, else the workspace combine within
- * args->workspace_bytes). Queries the current device's cluster occupancy. */
+ * args->workspace_bytes). Queries the current device's cluster occupancy.
+ * With kv_splits left 0 and no workspace the launch may be a mixed grid:
+ * *unsplit_groups query groups (128 x query_tiles rows of one head), as many
+ * as fill whole waves of clusters, run unsplit and the remaining groups are
+ * split kv_splits ways, so the last wave is short; 0 = every group split
+ * kv_splits ways. Rows of the unsplit groups are computed as with
+ * kv_splits = 1, the others as with kv_splits = *kv_splits. */
 int bl_attention_choice(const bl_attention_args* args, uint32_t* query_tiles,
-                        uint32_t* kv_splits);
+                        uint32_t* kv_splits, uint32_t* unsplit_groups);
 
 /*
  * bl_attention for callers that cannot allocate device memory. No counterpart

@@ -224,3 +224,43 @@ def test_query_tiles_beyond_two_are_rejected():
     dev = bl.pack_qkv(np.zeros((1, 64, 3, 2, 64), np.float32), "f16")
     with pytest.raises(bl.BackendError, match="query tiles"):
         bl.attention(dev, tokens=64, heads=2, query_tiles=3)
+
+
+def test_mixed_grid_rows_equal_their_uniform_launches():
+    """Config 5's shape (T=5477, H=16): the automatic choice is a mixed grid
+    (the query groups that fill whole waves of clusters unsplit, the rest
+    split), so the last wave is short. Each row must then equal, bit for bit,
+    the uniform launch with its own group's split count (1 or the tail's),
+    and the output meets the oracle on sampled rows of both kinds."""
+    import torch
+    import beatlm_b200 as bl
+    from beatlm_b200 import ops
+    t, h = 5477, 16
+    qkv = oracle.normal(4242, t * 3 * h * 64).reshape(1, t, 3, h, 64)
+    dev = bl.pack_qkv(qkv, "bf16")
+    out = torch.zeros((1, t, h * 64), dtype=torch.float32, device="cuda")
+    qt, splits, unsplit = ops.attention_choice(
+        ops.attention_args(dev, tokens=t, heads=h, out=out, qk_dtype="bf16"))
+    print("T=%d H=%d: %d query tiles per CTA, %d groups unsplit, the rest split %d ways"
+          % (t, h, qt, unsplit, splits))
+    assert unsplit > 0 and splits > 1  # the tail of 352 groups on 148 SMs
+    mixed = bl.attention(dev, tokens=t, heads=h, qk_dtype="bf16", out=out)
+    one = bl.attention(dev, tokens=t, heads=h, qk_dtype="bf16", kv_splits=1, query_tiles=qt)
+    many = bl.attention(dev, tokens=t, heads=h, qk_dtype="bf16", kv_splits=splits,
+                        query_tiles=qt)
+    torch.cuda.synchronize()
+    assert bl.status(reset=True).code == 0
+    rows = 128 * qt
+    groups = -(-t // rows)
+    got = mixed.view(t, h, 64)
+    for u in range(groups * h):
+        head, g = divmod(u, groups)
+        r0, r1 = g * rows, min(t, (g + 1) * rows)
+        want = (one if u < unsplit else many).view(t, h, 64)[r0:r1, head]
+        assert torch.equal(got[r0:r1, head], want), u
+    first_split_head, g = divmod(unsplit, groups)  # the first split group
+    for head, (r0, r1) in ((0, (0, 64)), (first_split_head, (g * rows, g * rows + 64))):
+        ref = oracle.attention(_rounded(qkv, "bf16")[0].reshape(t, -1), t, h, 64, rows=(r0, r1))
+        rel, _ = _errors(got[r0:r1, head].cpu().numpy(),
+                         ref.reshape(r1 - r0, h, 64)[:, head])
+        assert rel <= REL_L2, (head, rel)

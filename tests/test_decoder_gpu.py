@@ -183,3 +183,26 @@ def test_the_head_on_a_side_stream_equals_the_current_stream():
     got = dec.forward(feats, stream=side)
     side.synchronize()
     assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize("h,w,f,cout,bias", [(5, 3, 2, 6, True), (4, 7, 3, 8, True),
+                                             (37, 37, 4, 48, False)])
+def test_blocks_to_map_scatters_every_block(h, w, f, cout, bias):
+    """bl_blocks_to_map, both forms (4-channel vectors when cout is a multiple
+    of 4, else per element): out[y f + ky][x f + kx][co] = blocks[y w + x]
+    [(ky f + kx) cout + co] + bias[co], exactly."""
+    import ctypes
+    import torch
+    from beatlm_b200 import _native as N
+    blocks = _data(20, h * w * f * f * cout)
+    b = _data(21, cout, 0.1)
+    dev_b = torch.from_numpy(b).cuda() if bias else None
+    dev = torch.from_numpy(blocks).cuda()
+    out = torch.full((h * f, w * f, cout), float("nan"), device="cuda")
+    N.check(N.lib().bl_blocks_to_map(dev.data_ptr(), None if dev_b is None else dev_b.data_ptr(),
+                                     out.data_ptr(), h, w, f, cout, None))
+    torch.cuda.synchronize()
+    want = blocks.reshape(h, w, f, f, cout).transpose(0, 2, 1, 3, 4).reshape(h * f, w * f, cout)
+    if bias:
+        want = want + b
+    assert np.array_equal(out.cpu().numpy(), want.astype(np.float32))
