@@ -117,7 +117,7 @@ class GemmArgs(ctypes.Structure):
         ("norm_out_ld", ctypes.c_uint64), ("norm_gamma", ctypes.c_void_p),
         ("norm_beta", ctypes.c_void_p), ("norm_eps", ctypes.c_float),
         ("norm_sync", ctypes.c_void_p), ("norm_sync_bytes", ctypes.c_uint64),
-        ("weights_static", ctypes.c_uint32),
+        ("weights_static", ctypes.c_uint32), ("trace", ctypes.c_void_p),
     ]
 
 

@@ -129,15 +129,6 @@ struct Params {
     Status* status;
 };
 
-__device__ __forceinline__ void trace_stamp(unsigned long long* trace, int slot) {
-    if (trace == nullptr) return;
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    const size_t b = blockIdx.x + gridDim.x * (blockIdx.y + static_cast<size_t>(gridDim.y) *
-                                                               blockIdx.z);
-    trace[8 * b + slot] = t;
-}
-
 template <int QT>
 struct SmemTail {
     uint64_t q_full;

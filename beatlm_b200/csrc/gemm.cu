@@ -75,6 +75,7 @@ struct Params {
     float norm_eps;
     unsigned* norm_ctr;
     float2* norm_stats;
+    unsigned long long* trace;  // optional per-CTA timeline (persistent kernel)
     Status* status;
 };
 
@@ -779,6 +780,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
 
     if (threadIdx.x == 0) {
+        trace_stamp(p.trace, 0);
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(smem_u32(&tail->full[s]), 1);
             mbar_init(smem_u32(&tail->empty[s]), 1);
@@ -803,6 +805,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tail->tmem_base;
+    if (threadIdx.x == 0) trace_stamp(p.trace, 1);
     // Programmatic dependent launch: with weights_static, B and the epilogue
     // vectors do not depend on the previous kernel, so the first stages' B
     // copies and the vector staging start before the wait; A, the residual
@@ -824,6 +827,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tma_load_3d(smem_u32(sB(g)), &tm_b, 0, tile_n0(g / nk), (g % nk) * KC, bar);
         }
         pdl_wait();
+        if (lane == 0) trace_stamp(p.trace, 2);
         int g = 0;  // stages whose loads were started, over all tiles
         bool ok = true;
         for (int j = 0; j < mine && ok; ++j) {
@@ -880,6 +884,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int s = g % STAGES;
                 ok = wait_all(smem_u32(&tail->full[s]), (g / STAGES) & 1, g);
                 if (!ok) break;
+                if (g == 0 && elected) trace_stamp(p.trace, 3);
                 tc_fence_after();
                 const uint32_t a = smem_u32(sA(s)), bb = smem_u32(sB(s));
                 if (elected) {
@@ -897,6 +902,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
             }
             if (ok && elected) mma_commit(smem_u32(&tail->acc_full[b]));
+            if (j == 0 && elected) trace_stamp(p.trace, 4);
             __syncwarp();
         }
         if (!ok && elected) {
@@ -920,6 +926,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             prefetch_residual(p, rc, n0, rv0);
             bool ok = mbar_wait(smem_u32(&tail->acc_full[b]), use & 1, abort, p.status,
                                 ST_TIMEOUT_SOFTMAX, 0x200 + j);
+            if (j == 0 && threadIdx.x == 64) trace_stamp(p.trace, 5);
             if (!epilogue_all(ok)) break;
             tc_fence_after();
             float keep[32];
@@ -939,6 +946,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // stores complete before the staging is released and the kernel ends
         if (p.tma_store && lane == 0) bulk_wait_all();
         __syncwarp();
+        if (threadIdx.x == 64) trace_stamp(p.trace, 6);
     }
 
     tc_fence_before();
@@ -948,6 +956,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         tmem_dealloc(tmem, kCols);
     }
+    if (threadIdx.x == 0) trace_stamp(p.trace, 7);
 }
 
 // The LayerNorm prologue with its rows brought by TMA (one tile per CTA):
@@ -1521,6 +1530,7 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
     if (row_begin % BM != 0 || row_begin >= row_end || p.m_tiles <= 0)
         return fail(BL_ERR_INVALID, "gemm: row part [%u, %u) is not whole 128-row tiles", row_begin, row_end);
     p.status = status_ptr();
+    p.trace = reinterpret_cast<unsigned long long*>(g.trace);
     if (ln && !staged) {
         switch (bn) {
             case 32: return prepare_t<32, true>(ta, tb, p, out);

@@ -478,4 +478,15 @@ __device__ __forceinline__ bool elect_one() {
 __device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
 
+// Optional per-CTA timeline: CTA b (x fastest over the grid) writes the
+// %globaltimer (ns) at trace[8 b + slot]; nothing when trace is null.
+__device__ __forceinline__ void trace_stamp(unsigned long long* trace, int slot) {
+    if (trace == nullptr) return;
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    const size_t b = blockIdx.x + gridDim.x * (blockIdx.y + static_cast<size_t>(gridDim.y) *
+                                                               blockIdx.z);
+    trace[8 * b + slot] = t;
+}
+
 }  // namespace bl

@@ -381,6 +381,13 @@ typedef struct bl_gemm_args {
      * kernel has finished (programmatic dependent launch; a, residual and the
      * outputs always wait for it). Model weights qualify. */
     uint32_t weights_static;
+    /* Optional per-CTA timeline of the persistent kernel (NULL = off): CTA b
+     * writes %globaltimer stamps (ns) at trace[8b..8b+7]: entry, set-up done,
+     * first A load issued (past the dependency wait), first stage landed at
+     * the MMA issuer, first tile's last MMA issued, first tile's accumulator
+     * seen by the epilogue, last tile stored, exit. 8 * grid uint64 values
+     * (the grid is min(tiles, SMs) CTAs). */
+    uint64_t* trace;
 } bl_gemm_args;
 
 int bl_gemm(const bl_gemm_args* args, void* stream);
