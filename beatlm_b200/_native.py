@@ -249,6 +249,11 @@ class Im2colArgs(ctypes.Structure):
                 ("k_pad", ctypes.c_uint32)]
 
 
+class Conv3x3Args(ctypes.Structure):
+    _fields_ = [("input", ctypes.c_void_p), ("h", ctypes.c_uint32), ("w", ctypes.c_uint32),
+                ("cin", ctypes.c_uint32), ("relu", ctypes.c_uint32)]
+
+
 class PassCostArgs(ctypes.Structure):
     _fields_ = [("variant", ctypes.c_int32), ("passes", ctypes.c_uint32),
                 ("every", ctypes.c_uint32), ("groups", ctypes.c_uint32),
@@ -283,6 +288,7 @@ SIGNATURES.update({
     "bl_micros_nearest": (_u64, [ctypes.c_double]),
     "bl_kernel_spec_max_parts": (_u32, [ctypes.POINTER(KernelSpec)]),
     "bl_im2col": (ctypes.c_int, [ctypes.POINTER(Im2colArgs), _vp]),
+    "bl_conv3x3": (ctypes.c_int, [ctypes.POINTER(GemmArgs), ctypes.POINTER(Conv3x3Args), _vp]),
     "bl_blocks_to_map": (ctypes.c_int, [_vp, _vp, _vp, _u32, _u32, _u32, _u32, _vp]),
     "bl_resize_bilinear": (ctypes.c_int, [_vp, _vp, _u32, _u32, _u32, _u32, _u32, _vp]),
     "bl_budget_for_frame": (_u64, [_u64, _u64, _u64]),

@@ -76,6 +76,10 @@ struct Params {
     unsigned* norm_ctr;
     float2* norm_stats;
     unsigned long long* trace;  // optional per-CTA timeline (persistent kernel)
+    // implicit 3x3 convolution (gemm_conv): an NHWC f32 image of conv_w
+    // columns and conv_pix pixels, conv_cin channels; K columns past conv_k
+    // (9 cin) are zero; conv_relu: max(x, 0) on every input value
+    int conv_w, conv_pix, conv_cin, conv_k, conv_relu;
     Status* status;
 };
 
@@ -1214,6 +1218,277 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// The 3x3 convolution (stride 1, zero padding 1) of an NHWC f32 image as an
+// implicit GEMM: row m of A is output pixel m, and K column (ky 3 + kx) cin +
+// ci holds input pixel (y + ky - 1, x + kx - 1), channel ci (the tap-major
+// order of the weights). Nothing is gathered in memory. A k-block of 64
+// columns is two halves of 32 channels of one tap each (cin a multiple of
+// 32); for each half the producer copies, by TMA, the 128 input pixels that
+// the tile's rows read through that tap: a 128 x 32 f32 box starting at
+// pixel m0 + (ky - 1) w + (kx - 1), rows before the image or past its end
+// zero-filled by the copy. The four epilogue warps, idle until the
+// accumulator is ready, turn the two halves into the 16-bit A tile in the
+// MMA's swizzled layout, applying the optional ReLU and zeroing the pixels
+// whose tap column falls outside the image (x + kx - 1 < 0 or >= w, which
+// the flat copy wraps into the neighbouring row), then run the epilogue.
+// One tile per CTA.
+// A stage: the two f32 halves (TMA destinations, 128-byte aligned), the A
+// tile (1024-byte aligned for the 128-byte swizzle), the B tile. A warp's
+// 8-byte reads of a row are served per half-warp, 128 contiguous bytes of
+// one half each, so the halves need no offset against bank conflicts.
+constexpr uint32_t kConvHalf = BM * 32 * 4;  // 16 KiB: 128 pixels x 32 f32 channels
+constexpr uint32_t kConvX1 = kConvHalf;
+constexpr uint32_t kConvA = 2 * kConvHalf;
+static_assert(kConvX1 % 128 == 0 && kConvA % 1024 == 0, "TMA and swizzle alignment");
+
+template <int BN>
+struct ConvLayout {
+    static constexpr uint32_t kTileB = BN * BK * 2;
+    static constexpr uint32_t kB = kConvA + kTileA;
+    static constexpr uint32_t kStage = (kB + kTileB + 1023) / 1024 * 1024;
+    static_assert(kB % 1024 == 0, "B tile alignment");
+    static constexpr int kStages =
+        static_cast<int>((kSmemLimit - 4096 - kEpiBytes) / kStage) < kMaxStages
+            ? static_cast<int>((kSmemLimit - 4096 - kEpiBytes) / kStage)
+            : kMaxStages;
+};
+
+template <int BN>
+constexpr size_t conv_smem_bytes() {
+    return 1024 + ConvLayout<BN>::kStages * ConvLayout<BN>::kStage + kEpiBytes + sizeof(Tail);
+}
+
+// Half h of k-block kb: K columns [64 kb + 32 h, + 32), or none past conv_k.
+struct ConvHalf {
+    bool live;
+    int kx, x, y;  // tap column; the copy's start (channel, pixel)
+};
+__device__ __forceinline__ ConvHalf conv_half(const Params& p, int kb, int h, int m0) {
+    ConvHalf c{};
+    const int kk = kb * BK + 32 * h;
+    c.live = kk < p.conv_k;
+    if (c.live) {
+        const int tap = kk / p.conv_cin;
+        const int ky = tap / 3;
+        c.kx = tap - 3 * ky;
+        c.x = kk - tap * p.conv_cin;
+        c.y = m0 + (ky - 1) * p.conv_w + (c.kx - 1);
+    }
+    return c;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_conv(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_b,
+              const __grid_constant__ CUtensorMap tm_o, const Params p) {
+    using L = ConvLayout<BN>;
+    constexpr int STAGES = L::kStages;
+    static_assert(STAGES >= 2, "a stage ring needs two stages");
+    constexpr uint32_t kCols = Layout<BN>::kTmemCols;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint8_t* epi = smem + STAGES * L::kStage;
+    Tail* tail = reinterpret_cast<Tail*>(epi + kEpiBytes);
+    volatile int* abort = &tail->abort;
+    auto sX = [&](int s, int h) { return smem + s * L::kStage + (h ? kConvX1 : 0u); };
+    auto sA = [&](int s) { return smem + s * L::kStage + kConvA; };
+    auto sB = [&](int s) { return smem + s * L::kStage + L::kB; };
+
+    const int warp = warp_id();
+    const int lane = lane_id();
+    const int nk = p.K / BK;
+    const int t = static_cast<int>(blockIdx.x);  // the grid has one CTA per tile
+    const int m0 = (p.m_tile0 + t % p.m_tiles) * BM;
+    const int n0 = (t / p.m_tiles) * BN;
+    // bytes a stage's copies bring: B and the live halves
+    auto stage_bytes = [&](int kb) {
+        return L::kTileB + (conv_half(p, kb, 0, m0).live ? kConvHalf : 0u) +
+               (conv_half(p, kb, 1, m0).live ? kConvHalf : 0u);
+    };
+
+    if (threadIdx.x == 0) {
+        trace_stamp(p.trace, 0);
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(smem_u32(&tail->full[s]), 1);
+            mbar_init(smem_u32(&tail->conv[s]), 4);
+            mbar_init(smem_u32(&tail->empty[s]), 1);
+        }
+        mbar_init(smem_u32(&tail->acc_full[0]), 1);
+        mbar_init(smem_u32(&tail->drain), 1);
+        tail->abort = 0;
+        fence_barrier_init();
+        fence_proxy_async_smem();
+        tma_prefetch_desc(&tm_x);
+        tma_prefetch_desc(&tm_b);
+        if (p.tma_store) tma_prefetch_desc(&tm_o);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(&tail->tmem_base), kCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tail->tmem_base;
+    if (threadIdx.x == 0) trace_stamp(p.trace, 1);
+    pdl_trigger();
+
+    if (warp == 0) {
+        // lane 0 arms each stage and copies input half 0, lane 2 copies half
+        // 1 and lane 1 copies B (with weights_static the first stages' B
+        // before the dependency wait): a thread's bulk copies complete one
+        // after another, so the three are issued by three threads
+        const int first = !p.weights_static ? 0 : (STAGES < nk ? STAGES : nk);
+        for (int g = 0; g < first; ++g) {
+            const uint32_t bar = smem_u32(&tail->full[g]);
+            if (lane == 0) mbar_arrive_expect_tx(bar, stage_bytes(g));
+            if (lane == 1) tma_load_3d(smem_u32(sB(g)), &tm_b, 0, n0, g, bar);
+        }
+        pdl_wait();
+        if (lane == 0) trace_stamp(p.trace, 2);
+        int g = 0;
+        for (; g < nk; ++g) {
+            const int s = g % STAGES;
+            bool r = true;
+            if (lane == 0 && g >= STAGES)
+                r = mbar_wait(smem_u32(&tail->empty[s]), ((g / STAGES) - 1) & 1, abort, p.status,
+                              ST_TIMEOUT_TMA, g);
+            if (!__all_sync(0xFFFFFFFFu, r)) break;
+            const uint32_t bar = smem_u32(&tail->full[s]);
+            if (lane == 0 && g >= first) mbar_arrive_expect_tx(bar, stage_bytes(g));
+            __syncwarp();  // the stage is armed before any of its copies can land
+            if (lane == 0 || lane == 2) {
+                const int h = lane >> 1;
+                const ConvHalf c = conv_half(p, g, h, m0);
+                if (c.live) tma_load_2d(smem_u32(sX(s, h)), &tm_x, c.x, c.y, bar);
+            } else if (lane == 1 && g >= first) {
+                tma_load_3d(smem_u32(sB(s)), &tm_b, 0, n0, g, bar);
+            }
+            __syncwarp();
+        }
+        if (lane == 0 && *abort) {
+            for (int s = 0; s < STAGES && s < g; ++s) {
+                const int uses = (g - s - 1) / STAGES + 1;
+                mbar_wait(smem_u32(&tail->full[s]), (uses - 1) & 1, nullptr, p.status,
+                          ST_TIMEOUT_DRAIN, s);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        const bool elected = elect_one();
+        const uint32_t idesc = idesc_f16(BM, BN, p.ab_fmt, p.ab_fmt, 0, 0);
+        bool ok = true;
+        for (int kb = 0; kb < nk; ++kb) {
+            const int s = kb % STAGES;
+            bool r = true;
+            if (elected)
+                r = mbar_wait(smem_u32(&tail->conv[s]), (kb / STAGES) & 1, abort, p.status,
+                              ST_TIMEOUT_MMA, kb);
+            ok = __all_sync(0xFFFFFFFFu, r);
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t a = smem_u32(sA(s)), b = smem_u32(sB(s));
+            if (elected) {
+#pragma unroll
+                for (int k = 0; k < BK / 16; ++k)
+                    mma_ss(tmem, desc_k(a + 32 * k), desc_k(b + 32 * k), idesc,
+                           (kb > 0 || k > 0) ? 1u : 0u);
+                if (kb + STAGES < nk) mma_commit(smem_u32(&tail->empty[s]));
+            }
+            __syncwarp();
+        }
+        if (elected) {
+            if (ok) {
+                mma_commit(smem_u32(&tail->acc_full[0]));
+            } else {
+                mma_commit(smem_u32(&tail->drain));
+                mbar_wait(smem_u32(&tail->drain), 0, nullptr, p.status, ST_TIMEOUT_DRAIN, 0xD);
+            }
+        }
+        __syncwarp();
+    } else {
+        constexpr unsigned kFull = 0xFFFFFFFFu;
+        const int sub = warp & 3;
+        const int row = sub * 32 + lane;
+        const int dt = p.ab_fmt ? BL_BF16 : BL_F16;
+        pdl_wait();  // the residual read by the epilogue comes from the previous kernels
+        // Pixels of this warp's 32 rows in the image's first and last column
+        // (bit r: row sub * 32 + r): their left / right taps are outside.
+        const int col = (m0 + row) % p.conv_w;
+        const unsigned left = __ballot_sync(kFull, col == 0);
+        const unsigned right = __ballot_sync(kFull, col == p.conv_w - 1);
+        // lane L converts K columns 2L and 2L + 1 of each row: half L / 16,
+        // channels 2 (L % 16) and the next
+        const int h = lane >> 4;
+        const int chunk = lane >> 2, off = (lane & 3) * 4;
+        bool ok = true;
+        for (int kb = 0; kb < nk; ++kb) {
+            const int s = kb % STAGES;
+            const ConvHalf c = conv_half(p, kb, h, m0);
+            const unsigned zero = !c.live ? ~0u : c.kx == 0 ? left : c.kx == 2 ? right : 0u;
+            bool r = true;
+            if (lane == 0)
+                r = mbar_wait(smem_u32(&tail->full[s]), (kb / STAGES) & 1, abort, p.status,
+                              ST_TIMEOUT_SOFTMAX, 0x400 + kb);
+            ok = __all_sync(kFull, r);
+            if (!ok) break;
+            if (kb == 0 && threadIdx.x == 64) trace_stamp(p.trace, 3);
+            const uint8_t* xs = sX(s, h) + sub * 32 * 128 + (lane & 15) * 8;
+            uint8_t* tile = sA(s) + sub * 32 * 128 + off;
+            // sixteen rows read before any is written (the stores may alias
+            // the loads as far as the compiler knows)
+#pragma unroll
+            for (int h2 = 0; h2 < 32; h2 += 16) {
+                float2 xv[16];
+#pragma unroll
+                for (int r2 = 0; r2 < 16; ++r2)
+                    xv[r2] = *reinterpret_cast<const float2*>(xs + (h2 + r2) * 128);
+#pragma unroll
+                for (int r2 = 0; r2 < 16; ++r2) {
+                    const int rr = h2 + r2;
+                    float y0 = xv[r2].x, y1 = xv[r2].y;
+                    if (p.conv_relu) y0 = fmaxf(y0, 0.0f), y1 = fmaxf(y1, 0.0f);
+                    if ((zero >> rr) & 1u) y0 = 0.0f, y1 = 0.0f;
+                    *reinterpret_cast<uint32_t*>(tile + rr * 128 + ((chunk ^ (rr & 7)) << 4)) =
+                        pack2(y0, y1, dt);
+                }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&tail->conv[s]));
+        }
+        if (threadIdx.x == 64) trace_stamp(p.trace, 4);
+        // ------------------------------------------------------ epilogue
+        const RowCtx rc = row_ctx(p, m0 + row);
+        stage_vectors<BN>(p, tail, n0);
+        epilogue_all(true);
+        float rv0[32];
+        prefetch_residual(p, rc, n0, rv0);
+        if (ok) ok = mbar_wait(smem_u32(&tail->acc_full[0]), 0, abort, p.status,
+                               ST_TIMEOUT_SOFTMAX, 0xE);
+        if (threadIdx.x == 64) trace_stamp(p.trace, 5);
+        if (epilogue_all(ok)) {
+            tc_fence_after();
+            store_tile<BN>(p, tail, tmem + (static_cast<uint32_t>(sub * 32) << 16), n0, rc, rv0,
+                           p.tma_store ? &tm_o : nullptr, epi + sub * kEpiBlock,
+                           m0 + sub * 32 + p.out_row_offset);
+        }
+        if (p.tma_store && lane == 0) bulk_wait_all();
+        __syncwarp();
+        if (threadIdx.x == 64) trace_stamp(p.trace, 6);
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, kCols);
+    }
+    if (threadIdx.x == 0) trace_stamp(p.trace, 7);
+}
+
 int sm_count() {
     static int n = 0;
     if (n == 0) {
@@ -1303,6 +1578,21 @@ int prepare_ln_staged(const CUtensorMap& tx, const CUtensorMap& tb, const CUtens
     return BL_OK;
 }
 
+template <int BN>
+int prepare_conv(const CUtensorMap& tx, const CUtensorMap& tb, const CUtensorMap& to,
+                 const Params& p, Launch* out) {
+    constexpr size_t smem = conv_smem_bytes<BN>();
+    out->op = 2;
+    auto kern = gemm_conv<BN>;
+    BL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(smem)));
+    const dim3 grid(p.m_tiles * (p.N / BN));
+    out->run = [=](cudaStream_t s) {
+        return launch_k(kern, grid, dim3(kThreads), smem, s, tx, tb, to, p);
+    };
+    return BL_OK;
+}
+
 template <int BN, bool kLn>
 int prepare_t(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, Launch* out) {
     constexpr size_t smem = smem_bytes<BN>();
@@ -1356,12 +1646,36 @@ int pick_bn(const bl_gemm_args& g) {
     return 0;
 }
 
-int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch* out) {
+int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch* out,
+            const bl_conv3x3_args* conv = nullptr) {
     if (g.m == 0 || g.n == 0 || g.k == 0) return fail(BL_ERR_INVALID, "gemm: zero dimension");
     if (g.k % BK != 0) return fail(BL_ERR_UNSUPPORTED, "gemm: K=%u is not a multiple of 64", g.k);
     if (g.ab_dtype != BL_F16 && g.ab_dtype != BL_BF16)
         return fail(BL_ERR_UNSUPPORTED, "gemm: operand dtype %d (f16 or bf16)", g.ab_dtype);
     int bn = pick_bn(g);
+    if (conv != nullptr) {
+        // implicit 3x3 convolution: A is the image, tiles of at most 128 columns
+        if (conv->input == nullptr || conv->h == 0 || conv->w == 0 || conv->cin == 0)
+            return fail(BL_ERR_INVALID, "conv3x3: empty image or null input");
+        if (conv->cin % 32 != 0)
+            return fail(BL_ERR_UNSUPPORTED, "conv3x3: %u channels (a multiple of 32)", conv->cin);
+        if (1ull * conv->h * conv->w != g.m)
+            return fail(BL_ERR_INVALID, "conv3x3: m=%u is not h * w = %u x %u", g.m, conv->h,
+                        conv->w);
+        if (g.k != (9 * conv->cin + BK - 1) / BK * BK)
+            return fail(BL_ERR_INVALID, "conv3x3: k=%u is not 9 x %u channels rounded up to 64",
+                        g.k, conv->cin);
+        if (reinterpret_cast<uintptr_t>(conv->input) & 15)
+            return fail(BL_ERR_INVALID, "conv3x3: input must be 16-byte aligned");
+        if (g.a != nullptr || g.ln_x != nullptr || g.norm_out != nullptr || g.stats_out != nullptr)
+            return fail(BL_ERR_INVALID, "conv3x3: the image is A (no a, LayerNorm or statistics)");
+        if (1ull * g.m + conv->w + 1 >= (1ull << 31))
+            return fail(BL_ERR_UNSUPPORTED, "conv3x3: %u pixels exceed 32-bit coordinates", g.m);
+        bn = g.tile_n ? static_cast<int>(g.tile_n)
+                      : g.n % 128 == 0 ? 128 : g.n % 96 == 0 ? 96 : g.n % 64 == 0 ? 64 : 32;
+        if (bn > 128)
+            return fail(BL_ERR_UNSUPPORTED, "conv3x3: tile width %d (at most 128)", bn);
+    }
     if (g.stats_out != nullptr) {
         // one stats slice per column tile
         if (g.stats_parts == 0 || g.n % g.stats_parts != 0)
@@ -1426,7 +1740,7 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
         return fail(BL_ERR_INVALID,
                     "gemm: LayerNorm statistics need the LayerNorm prologue, parts dividing K=%u "
                     "and 8-byte alignment", g.k);
-    if (!ln && g.a == nullptr) return fail(BL_ERR_INVALID, "gemm: no A operand");
+    if (!ln && g.a == nullptr && conv == nullptr) return fail(BL_ERR_INVALID, "gemm: no A operand");
     if (ln && (g.ln_gamma == nullptr || g.ln_beta == nullptr || !(g.ln_eps > 0.0f)))
         return fail(BL_ERR_INVALID, "gemm: LayerNorm prologue needs gamma, beta and eps > 0");
     if (ln && ((reinterpret_cast<uintptr_t>(g.ln_x) & 15) || (g.ln_ldx % 4) || g.ln_ldx < g.k))
@@ -1471,7 +1785,16 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
                         (ldx * 4) % 16 == 0 && (reinterpret_cast<uintptr_t>(g.ln_x) & 15) == 0;
     const int kc = ln ? 1 : pick_kc(bn, g.k);
     const uint64_t ldb = g.ldb ? g.ldb : g.k;
-    if (staged) {
+    if (conv != nullptr) {
+        // the image as [pixels][channels] f32 rows, boxes of 32 channels x 128 pixels
+        const uint64_t dx[2] = {conv->cin, g.m};
+        const uint32_t bx[2] = {32, BM};
+        if ((rc = make_tmap_2d(&ta, conv->input, 4, dx, 4ull * conv->cin, bx, 0)) != BL_OK)
+            return rc;
+        const uint64_t db[3] = {BK, g.n, g.k / BK}, sb[2] = {ldb * 2, BK * 2};
+        const uint32_t bb[3] = {BK, static_cast<uint32_t>(bn), 1};
+        if ((rc = make_tmap_16bit_3d(&tb, g.b, db, sb, bb)) != BL_OK) return rc;
+    } else if (staged) {
         const uint64_t dx[2] = {g.k, g.m};
         const uint32_t bx[2] = {BK, BM};
         if ((rc = make_tmap_2d(&ta, g.ln_x, 4, dx, ldx * 4, bx, 0)) != BL_OK) return rc;
@@ -1531,6 +1854,13 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
         return fail(BL_ERR_INVALID, "gemm: row part [%u, %u) is not whole 128-row tiles", row_begin, row_end);
     p.status = status_ptr();
     p.trace = reinterpret_cast<unsigned long long*>(g.trace);
+    if (conv != nullptr) {
+        p.conv_w = static_cast<int>(conv->w);
+        p.conv_pix = static_cast<int>(g.m);
+        p.conv_cin = static_cast<int>(conv->cin);
+        p.conv_k = static_cast<int>(9 * conv->cin);
+        p.conv_relu = conv->relu ? 1 : 0;
+    }
     if (ln && !staged) {
         switch (bn) {
             case 32: return prepare_t<32, true>(ta, tb, p, out);
@@ -1567,6 +1897,14 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
             return rc;
         p.tma_store = 1;
     }
+    if (conv != nullptr) {
+        switch (bn) {
+            case 32: return prepare_conv<32>(ta, tb, to, p, out);
+            case 64: return prepare_conv<64>(ta, tb, to, p, out);
+            case 96: return prepare_conv<96>(ta, tb, to, p, out);
+            default: return prepare_conv<128>(ta, tb, to, p, out);
+        }
+    }
     if (staged) {
         switch (bn) {
             case 32: return prepare_ln_staged<32>(ta, tb, to, p, out);
@@ -1595,6 +1933,13 @@ int prepare_gemm_rows(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_en
 
 extern "C" size_t bl_gemm_norm_sync_bytes(const bl_gemm_args* args) {
     return args == nullptr ? 0 : static_cast<size_t>(bl::gemm::norm_sync_bytes(args->m, args->n));
+}
+
+extern "C" int bl_conv3x3(const bl_gemm_args* args, const bl_conv3x3_args* conv, void* stream) {
+    if (args == nullptr || conv == nullptr) return bl::fail(BL_ERR_INVALID, "conv3x3: null args");
+    bl::Launch l;
+    int rc = bl::gemm::prepare(*args, 0, args->m, &l, conv);
+    return rc != BL_OK ? rc : bl::enqueue(l, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int bl_gemm(const bl_gemm_args* args, void* stream) {

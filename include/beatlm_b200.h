@@ -381,12 +381,14 @@ typedef struct bl_gemm_args {
      * kernel has finished (programmatic dependent launch; a, residual and the
      * outputs always wait for it). Model weights qualify. */
     uint32_t weights_static;
-    /* Optional per-CTA timeline of the persistent kernel (NULL = off): CTA b
-     * writes %globaltimer stamps (ns) at trace[8b..8b+7]: entry, set-up done,
-     * first A load issued (past the dependency wait), first stage landed at
-     * the MMA issuer, first tile's last MMA issued, first tile's accumulator
-     * seen by the epilogue, last tile stored, exit. 8 * grid uint64 values
-     * (the grid is min(tiles, SMs) CTAs). */
+    /* Optional per-CTA timeline (NULL = off) of the persistent kernel and of
+     * bl_conv3x3's: CTA b writes %globaltimer stamps (ns) at trace[8b..8b+7]:
+     * entry, set-up done, first A load issued (past the dependency wait),
+     * first stage landed (at the MMA issuer; bl_conv3x3: at the converting
+     * warps), first tile's last MMA issued (bl_conv3x3: last A tile
+     * written), first tile's accumulator seen by the epilogue, last tile
+     * stored, exit. 8 * grid uint64 values (the persistent grid is
+     * min(tiles, SMs) CTAs; bl_conv3x3's one CTA per tile). */
     uint64_t* trace;
 } bl_gemm_args;
 
@@ -646,6 +648,22 @@ typedef struct bl_im2col_args {
     uint32_t k_pad;      /* multiple of 64, >= ksize * ksize * cin; columns past it are 0 */
 } bl_im2col_args;
 int bl_im2col(const bl_im2col_args* args, void* stream);
+/* A 3x3 convolution, stride 1, zero padding 1, of an NHWC f32 image as an
+ * implicit GEMM (no counterpart in the reference, whose conv kernel gathers
+ * per output value, reference.rs:40-101): the tcgen05 GEMM of `gemm` whose A
+ * operand is the image read through the nine taps, the rows of each tap's
+ * 128 pixels copied by TMA and turned into the 16-bit A tile on chip, so no
+ * [h w][9 cin] matrix reaches memory. `gemm` is filled as for bl_gemm with
+ * a = NULL, m = h * w, k = 9 * cin rounded up to 64, b the weights from the
+ * same [cout][k] tap-major layout bl_im2col's columns use, and any epilogue
+ * (bias, activation, residual, output) but no LayerNorm or statistics; the
+ * tile width is at most 128 columns. cin must be a multiple of 32. */
+typedef struct bl_conv3x3_args {
+    const float* input;  /* [h][w][cin] f32, 16-byte aligned */
+    uint32_t h, w, cin;
+    uint32_t relu;       /* non-zero: max(x, 0) applied to every input value */
+} bl_conv3x3_args;
+int bl_conv3x3(const bl_gemm_args* gemm, const bl_conv3x3_args* conv, void* stream);
 /* out[(y f + ky)][(x f + kx)][co] = blocks[y * w + x][(ky f + kx) cout + co] + bias[co]
  * (bias may be NULL): the f x f block each input pixel of a transposed
  * convolution writes (reference.rs:103-140). */

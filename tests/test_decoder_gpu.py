@@ -206,3 +206,41 @@ def test_blocks_to_map_scatters_every_block(h, w, f, cout, bias):
     if bias:
         want = want + b
     assert np.array_equal(out.cpu().numpy(), want.astype(np.float32))
+
+
+@pytest.mark.parametrize("h,w,cin,cout,relu,act,res", [
+    (37, 37, 64, 64, True, None, True),     # a fusion unit's second convolution
+    (148, 148, 64, 32, False, None, False),  # the head's first convolution
+    (74, 74, 96, 64, False, "relu", False),  # k-blocks straddling taps (96 channels)
+    (23, 1, 32, 32, True, None, False),      # one column: both side taps outside
+    (1, 40, 32, 64, False, None, True),      # one row: the vertical taps outside
+    (5, 7, 192, 128, True, "relu", False),   # fewer pixels than one tile
+    (518, 518, 32, 32, False, "relu", False),  # the depth head's full-resolution convolution
+])
+def test_implicit_conv3x3_equals_the_gathered_one(h, w, cin, cout, relu, act, res):
+    """bl_conv3x3 (the image read through the taps on chip) against im2col +
+    bl_gemm: the same 16-bit A values, the same k-block order and the same
+    epilogue, so the same bits; and both against the oracle."""
+    import torch
+    import beatlm_b200 as bl
+    from beatlm_b200 import ops
+    x = _data(40 + cin, h * w * cin)
+    wt = _data(41, 9 * cin * cout, 1.0 / np.sqrt(9 * cin))
+    b = torch.from_numpy(_data(42, cout, 0.1)).cuda()
+    dev = torch.from_numpy(x).cuda()
+    r = torch.from_numpy(_data(43, h * w * cout)).cuda().reshape(h * w, cout) if res else None
+    wdev = ops.conv_weights(wt, 3, cin, cout)
+    run = lambda implicit: ops.conv2d(dev, wdev, b, h, w, cin, cout, relu_input=relu, act=act,
+                                      residual=r, implicit=implicit)
+    got, gathered = run(True), run(False)
+    torch.cuda.synchronize()
+    assert bl.status(reset=True).code == 0
+    assert torch.equal(got, gathered)
+    if h * w <= 40000:
+        xin = oracle.relu(x) if relu else x
+        want = oracle.conv3x3(xin, wt, b.cpu().numpy(), h, w, cin, cout, 1)
+        if act == "relu":
+            want = oracle.relu(want)
+        if res:
+            want = want + r.cpu().numpy().ravel()
+        assert _rel(got.cpu().numpy(), want) <= REL
