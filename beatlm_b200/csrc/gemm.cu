@@ -747,16 +747,28 @@ __device__ bool norm_tile(const Params& p, const CUtensorMap* tmn, const float* 
 // epilogue warps drain tile j from one while the MMA thread fills tile j + 1
 // in the other, and the TMA ring runs on across tiles, so the epilogue and the
 // CTA's set-up leave the critical path once a CTA has more than one tile.
-template <int BN, int KC, int EPI>
+// kPair: the CTA-pair form (a cluster of two CTAs, cta_group::2). A tile is
+// 256 x BN: each CTA copies its own 128 rows of A and BN / 2 rows of B into
+// its shared memory (so it holds the stage of a 128 x BN/2 tile), the even
+// CTA's MMA warp issues M = 256 MMAs that read both CTAs' tiles and write
+// each CTA's 128 x BN accumulator, and each CTA's epilogue stores its own
+// 128 rows. Per MMA each SM then brings in half the B bytes of a 128 x BN
+// tile. The stage barriers that the MMA waits on are the even CTA's (both
+// CTAs' copies count on them); the MMA's completions arrive on both CTAs'
+// barriers; the epilogues of both free an accumulator on the even CTA's
+// barrier. No copy is multicast.
+template <int BN, int KC, int EPI, bool kPair>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_persistent(const __grid_constant__ CUtensorMap tm_a,
                     const __grid_constant__ CUtensorMap tm_b,
                     const __grid_constant__ CUtensorMap tm_o,
                     const __grid_constant__ CUtensorMap tm_n, const Params p) {
-    using L = Layout<BN, KC, true>;
+    using L = Layout<kPair ? BN / 2 : BN, KC, true>;
     constexpr int STAGES = L::kStages;
     static_assert(STAGES >= 2, "a stage ring needs two stages");
-    constexpr uint32_t kCols = 2 * L::kTmemCols;
+    constexpr uint32_t kAccCols = Layout<BN>::kTmemCols;  // one accumulator
+    constexpr uint32_t kCols = 2 * kAccCols;
+    constexpr int TM = kPair ? 2 * BM : BM;  // rows of a tile
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -769,18 +781,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int warp = warp_id();
     const int lane = lane_id();
     const int nk = p.K / (BK * KC);  // stages per tile (the host makes KC divide K / 64)
+    // tiles are walked by CTA (one CTA) or by pair (kPair; p.m_tiles then
+    // counts 256-row tiles)
+    const int rank = kPair ? static_cast<int>(cluster_rank()) : 0;
+    const int unit = kPair ? static_cast<int>(blockIdx.x) / 2 : static_cast<int>(blockIdx.x);
+    const int units = kPair ? static_cast<int>(gridDim.x) / 2 : static_cast<int>(gridDim.x);
+    const bool leader = rank == 0;
     const int total = p.m_tiles * (p.N / BN);
-    const int mine = static_cast<int>(blockIdx.x) < total
-                         ? (total - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
-                               static_cast<int>(gridDim.x)
-                         : 0;
-    auto tile_m0 = [&](int j) {
-        const int t = static_cast<int>(blockIdx.x) + j * static_cast<int>(gridDim.x);
-        return (p.m_tile0 + t % p.m_tiles) * BM;
+    const int mine = unit < total ? (total - unit + units - 1) / units : 0;
+    auto tile_m0 = [&](int j) {  // this CTA's first row of tile j
+        const int t = unit + j * units;
+        return (p.m_tile0 + t % p.m_tiles) * TM + rank * BM;
     };
     auto tile_n0 = [&](int j) {
-        const int t = static_cast<int>(blockIdx.x) + j * static_cast<int>(gridDim.x);
+        const int t = unit + j * units;
         return (t / p.m_tiles) * BN;
+    };
+    // the barrier the MMA waits on for stage s: the even CTA's
+    auto full_bar = [&](int s) {
+        const uint32_t b = smem_u32(&tail->full[s]);
+        return kPair ? dsmem_addr(b, 0) : b;
     };
 
     if (threadIdx.x == 0) {
@@ -791,7 +811,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(smem_u32(&tail->acc_full[b]), 1);
-            mbar_init(smem_u32(&tail->acc_empty[b]), 4);
+            mbar_init(smem_u32(&tail->acc_empty[b]), kPair ? 8 : 4);
         }
         mbar_init(smem_u32(&tail->drain), 1);
         tail->abort = 0;
@@ -802,11 +822,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (p.tma_store) tma_prefetch_desc(&tm_o);
     }
     if (warp == 1) {
-        tmem_alloc(smem_u32(&tail->tmem_base), kCols);
-        tmem_relinquish();
+        if constexpr (kPair) {
+            tmem_alloc_pair(smem_u32(&tail->tmem_base), kCols);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(smem_u32(&tail->tmem_base), kCols);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    // the pair: both CTAs' barriers and tensor memory exist before either
+    // CTA's copies or MMAs can signal or write the other's
+    if constexpr (kPair) cluster_sync();
     tc_fence_after();
     const uint32_t tmem = tail->tmem_base;
     if (threadIdx.x == 0) trace_stamp(p.trace, 1);
@@ -823,12 +851,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         // are in flight together (each thread's copies are serial). Lane 0
         // alone waits for the stage to be free; the vote hands the outcome
         // to the warp, so both lanes start the same stages.
+        // kPair: the even CTA arms its barrier for both CTAs' bytes; B rows
+        // of this CTA's half start BN / 2 further in the odd CTA
+        constexpr uint32_t kArm = kPair ? 2 * L::kStage : L::kStage;
+        const int b_off = kPair ? rank * (BN / 2) : 0;
+        auto load = [&](uint32_t dst, const CUtensorMap* map, int y, int z, uint32_t bar) {
+            if constexpr (kPair) tma_load_3d_pair(dst, map, 0, y, z, bar);
+            else tma_load_3d(dst, map, 0, y, z, bar);
+        };
         const int first = !p.weights_static ? 0 : STAGES < mine * nk ? STAGES : mine * nk;
         for (int g = 0; g < first; ++g) {  // stages whose B is fetched up front
-            const uint32_t bar = smem_u32(&tail->full[g]);
-            if (lane == 0) mbar_arrive_expect_tx(bar, L::kStage);
+            if (lane == 0 && leader) mbar_arrive_expect_tx(smem_u32(&tail->full[g]), kArm);
             if (lane == 1)
-                tma_load_3d(smem_u32(sB(g)), &tm_b, 0, tile_n0(g / nk), (g % nk) * KC, bar);
+                load(smem_u32(sB(g)), &tm_b, tile_n0(g / nk) + b_off, (g % nk) * KC, full_bar(g));
         }
         pdl_wait();
         if (lane == 0) trace_stamp(p.trace, 2);
@@ -844,18 +879,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                                   p.status, ST_TIMEOUT_TMA, g);
                 ok = __all_sync(0xFFFFFFFFu, r);
                 if (!ok) break;
-                const uint32_t bar = smem_u32(&tail->full[s]);
+                const uint32_t bar = full_bar(s);  // the copies' (kPair: the even CTA's)
                 if (lane == 0) {
-                    if (g >= first) mbar_arrive_expect_tx(bar, L::kStage);
-                    tma_load_3d(smem_u32(sA(s)), &tm_a, 0, m0, kb * KC, bar);
+                    if (g >= first && leader)
+                        mbar_arrive_expect_tx(smem_u32(&tail->full[s]), kArm);
+                    load(smem_u32(sA(s)), &tm_a, m0, kb * KC, bar);
                 } else if (lane == 1 && g >= first) {
-                    tma_load_3d(smem_u32(sB(s)), &tm_b, 0, n0, kb * KC, bar);
+                    load(smem_u32(sB(s)), &tm_b, n0 + b_off, kb * KC, bar);
                 }
                 __syncwarp();
             }
         }
-        if (lane == 0 && *abort) {
+        if (lane == 0 && *abort && leader) {
             // let every started copy land before shared memory is released
+            // (the pair's copies, both CTAs', count on the even CTA's
+            // barriers, and the pair leaves together after the closing
+            // cluster barrier)
             for (int s = 0; s < STAGES && s < g; ++s) {
                 const int uses = (g - s - 1) / STAGES + 1;
                 mbar_wait(smem_u32(&tail->full[s]), (uses - 1) & 1, nullptr, p.status,
@@ -863,16 +902,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
         __syncwarp();
-    } else if (warp == 1) {
+    } else if (warp == 1 && !(kPair && !leader)) {
         // whole-warp issuer loop, one elected lane issues and waits (see
         // gemm_kernel)
         const bool elected = elect_one();
         auto wait_all = [&](uint32_t bar, uint32_t parity, uint32_t where) -> bool {
             bool r = true;
-            if (elected) r = mbar_wait(bar, parity, abort, p.status, ST_TIMEOUT_MMA, where);
+            if (elected)
+                r = kPair ? mbar_wait_cluster(bar, parity, abort, p.status, ST_TIMEOUT_MMA, where)
+                          : mbar_wait(bar, parity, abort, p.status, ST_TIMEOUT_MMA, where);
             return __all_sync(0xFFFFFFFFu, r);
         };
-        const uint32_t idesc = idesc_f16(BM, BN, p.ab_fmt, p.ab_fmt, 0, 0);
+        auto commit = [&](uint32_t bar) {
+            if constexpr (kPair) mma_commit_pair(bar);
+            else mma_commit(bar);
+        };
+        const uint32_t idesc = idesc_f16(TM, BN, p.ab_fmt, p.ab_fmt, 0, 0);
         const int total_g = mine * nk;
         int g = 0;
         bool ok = true;
@@ -883,10 +928,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             tc_fence_after();
-            const uint32_t acc = tmem + static_cast<uint32_t>(b) * L::kTmemCols;
+            const uint32_t acc = tmem + static_cast<uint32_t>(b) * kAccCols;
             for (int kb = 0; kb < nk; ++kb, ++g) {
                 const int s = g % STAGES;
-                ok = wait_all(smem_u32(&tail->full[s]), (g / STAGES) & 1, g);
+                ok = wait_all(smem_u32(&tail->full[s]), (g / STAGES) & 1, g);  // the even CTA's own
                 if (!ok) break;
                 if (g == 0 && elected) trace_stamp(p.trace, 3);
                 tc_fence_after();
@@ -895,26 +940,29 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int c = 0; c < KC; ++c)
 #pragma unroll
-                        for (int k = 0; k < BK / 16; ++k)
-                            mma_ss(acc, desc_k(a + c * kTileA + 32 * k),
-                                   desc_k(bb + c * L::kTileB + 32 * k), idesc,
-                                   (kb > 0 || c > 0 || k > 0) ? 1u : 0u);
+                        for (int k = 0; k < BK / 16; ++k) {
+                            const uint64_t da = desc_k(a + c * kTileA + 32 * k);
+                            const uint64_t db = desc_k(bb + c * L::kTileB + 32 * k);
+                            const uint32_t acc_in = (kb > 0 || c > 0 || k > 0) ? 1u : 0u;
+                            if constexpr (kPair) mma_ss_pair(acc, da, db, idesc, acc_in);
+                            else mma_ss(acc, da, db, idesc, acc_in);
+                        }
                     // release the stage only if the producer will refill it,
                     // so no arrival lands after the CTA has finished
-                    if (g + STAGES < total_g) mma_commit(smem_u32(&tail->empty[s]));
+                    if (g + STAGES < total_g) commit(smem_u32(&tail->empty[s]));
                 }
                 __syncwarp();
             }
-            if (ok && elected) mma_commit(smem_u32(&tail->acc_full[b]));
+            if (ok && elected) commit(smem_u32(&tail->acc_full[b]));
             if (j == 0 && elected) trace_stamp(p.trace, 4);
             __syncwarp();
         }
         if (!ok && elected) {
-            mma_commit(smem_u32(&tail->drain));
+            commit(smem_u32(&tail->drain));
             mbar_wait(smem_u32(&tail->drain), 0, nullptr, p.status, ST_TIMEOUT_DRAIN, 0xD);
         }
         __syncwarp();
-    } else {
+    } else if (warp >= 2) {
         const int sub = warp & 3;
         const int row = sub * 32 + lane;
         for (int j = 0; j < mine; ++j) {
@@ -935,14 +983,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             float keep[32];
             store_tile<BN, EPI>(p, tail,
-                           tmem + static_cast<uint32_t>(b) * L::kTmemCols +
+                           tmem + static_cast<uint32_t>(b) * kAccCols +
                                (static_cast<uint32_t>(sub * 32) << 16),
                            n0, rc, rv0, p.tma_store ? &tm_o : nullptr, epi + sub * kEpiBlock,
                            m0 + sub * 32 + p.out_row_offset,
                            p.norm_out != nullptr ? keep : nullptr);
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&tail->acc_empty[b]));
+            if (lane == 0) {
+                if (kPair && !leader)
+                    mbar_arrive_remote(dsmem_addr(smem_u32(&tail->acc_empty[b]), 0));
+                else
+                    mbar_arrive(smem_u32(&tail->acc_empty[b]));
+            }
             if (p.norm_out != nullptr &&
                 !norm_tile(p, &tm_n, keep, rc.live, m0, n0, row, epi + sub * kEpiBlock, abort))
                 break;
@@ -955,10 +1008,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     tc_fence_before();
     __syncthreads();
+    // the pair leaves together: no arrival or MMA read of one CTA's memory
+    // is outstanding when the other exits
+    if constexpr (kPair) cluster_sync();
     if (warp == 1) {
         __syncwarp();
         tc_fence_after();
-        tmem_dealloc(tmem, kCols);
+        if constexpr (kPair) tmem_dealloc_pair(tmem, kCols);
+        else tmem_dealloc(tmem, kCols);
     }
     if (threadIdx.x == 0) trace_stamp(p.trace, 7);
 }
@@ -1500,32 +1557,67 @@ int sm_count() {
     return n;
 }
 
-template <int BN, int KC, int EPI>
+// How many clusters of two persistent CTAs (this kernel's shared memory)
+// the device runs at once, queried once per kernel.
+template <typename K>
+int pair_clusters(K kern, size_t smem) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(2);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
+template <int BN, int KC, int EPI, bool kPair>
 int prepare_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
                        const CUtensorMap& tn, const Params& p, Launch* out) {
-    constexpr size_t smem = smem_bytes<BN, KC, true>();
+    constexpr size_t smem = smem_bytes<kPair ? BN / 2 : BN, KC, true>();
     out->op = 2;
-    auto kern = gemm_persistent<BN, KC, EPI>;
+    auto kern = gemm_persistent<BN, KC, EPI, kPair>;
     BL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(smem)));
     const int tiles = p.m_tiles * (p.N / BN);
-    const dim3 grid(std::min(tiles, sm_count()));
-    out->run = [=](cudaStream_t s) {
-        return launch_k(kern, grid, dim3(kThreads), smem, s, ta, tb, to, tn, p);
-    };
+    if constexpr (kPair) {
+        static int clusters = 0;  // per kernel; the same on every B200
+        if (clusters == 0) clusters = pair_clusters(kern, smem);
+        if (clusters <= 0) return fail(BL_ERR_UNSUPPORTED, "gemm: no CTA pair fits an SM pair");
+        const dim3 grid(2 * std::min(tiles, clusters));
+        out->run = [=](cudaStream_t s) {
+            return launch_k_cluster(kern, grid, dim3(kThreads), dim3(2, 1, 1), smem, s, ta, tb, to,
+                                    tn, p);
+        };
+    } else {
+        const dim3 grid(std::min(tiles, sm_count()));
+        out->run = [=](cudaStream_t s) {
+            return launch_k(kern, grid, dim3(kThreads), smem, s, ta, tb, to, tn, p);
+        };
+    }
     return BL_OK;
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool kPair>
 int prepare_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
                        const CUtensorMap& tn, const Params& p, int kc, Launch* out) {
     // only the depths whose ring holds two stages are built
-    if constexpr (Layout<BN, 4, true>::kStages >= 2)
-        if (kc == 4) return prepare_persistent<BN, 4, EPI>(ta, tb, to, tn, p, out);
-    if constexpr (Layout<BN, 2, true>::kStages >= 2)
-        if (kc == 2) return prepare_persistent<BN, 2, EPI>(ta, tb, to, tn, p, out);
+    constexpr int SB = kPair ? BN / 2 : BN;  // B rows a CTA holds
+    if constexpr (Layout<SB, 4, true>::kStages >= 2)
+        if (kc == 4) return prepare_persistent<BN, 4, EPI, kPair>(ta, tb, to, tn, p, out);
+    if constexpr (Layout<SB, 2, true>::kStages >= 2)
+        if (kc == 2) return prepare_persistent<BN, 2, EPI, kPair>(ta, tb, to, tn, p, out);
     if (kc != 1) return fail(BL_ERR_UNSUPPORTED, "gemm: no kernel for %d k-blocks per stage", kc);
-    return prepare_persistent<BN, 1, EPI>(ta, tb, to, tn, p, out);
+    return prepare_persistent<BN, 1, EPI, kPair>(ta, tb, to, tn, p, out);
 }
 
 // The epilogue form (store_tile's EPI) these arguments match exactly, or -1.
@@ -1541,14 +1633,14 @@ int epilogue_form(const Params& p) {
     return -1;
 }
 
-template <int BN>
+template <int BN, bool kPair = false>
 int prepare_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
                        const CUtensorMap& tn, const Params& p, int kc, Launch* out) {
     switch (epilogue_form(p)) {
-        case 0: return prepare_persistent<BN, 0>(ta, tb, to, tn, p, kc, out);
-        case 1: return prepare_persistent<BN, 1>(ta, tb, to, tn, p, kc, out);
-        case 2: return prepare_persistent<BN, 2>(ta, tb, to, tn, p, kc, out);
-        default: return prepare_persistent<BN, -1>(ta, tb, to, tn, p, kc, out);
+        case 0: return prepare_persistent<BN, 0, kPair>(ta, tb, to, tn, p, kc, out);
+        case 1: return prepare_persistent<BN, 1, kPair>(ta, tb, to, tn, p, kc, out);
+        case 2: return prepare_persistent<BN, 2, kPair>(ta, tb, to, tn, p, kc, out);
+        default: return prepare_persistent<BN, -1, kPair>(ta, tb, to, tn, p, kc, out);
     }
 }
 
@@ -1783,7 +1875,23 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
     const bool staged = ln && g.ln_stats != nullptr && g.ln_stats_parts <= kMaxNormParts &&
                         row_tiles * (g.n / bn) <= static_cast<uint64_t>(sm_count()) &&
                         (ldx * 4) % 16 == 0 && (reinterpret_cast<uintptr_t>(g.ln_x) & 15) == 0;
-    const int kc = ln ? 1 : pick_kc(bn, g.k);
+    // 256-row tiles over CTA pairs (pair_tiles 2): whole launches with A
+    // loaded by TMA, tiles 128 or 256 columns wide; 0 and 1 keep one CTA
+    // per tile.
+    if (g.pair_tiles > 2) return fail(BL_ERR_INVALID, "gemm: pair_tiles %u (0, 1 or 2)", g.pair_tiles);
+    const bool pair = g.pair_tiles == 2;
+    if (pair) {
+        if (ln || norm || conv != nullptr || g.a == nullptr)
+            return fail(BL_ERR_UNSUPPORTED, "gemm: CTA pairs take A loaded by TMA (no LayerNorm "
+                                            "prologue, epilogue LayerNorm or convolution)");
+        if (row_begin != 0 || row_end < g.m)
+            return fail(BL_ERR_UNSUPPORTED, "gemm: CTA pairs cover whole launches");
+        if (!g.tile_n) bn = g.n % 256 == 0 ? 256 : 128;
+        if ((bn != 128 && bn != 256) || g.n % bn != 0)
+            return fail(BL_ERR_UNSUPPORTED, "gemm: CTA pairs take 128- or 256-column tiles (N=%u)",
+                        g.n);
+    }
+    const int kc = ln ? 1 : pick_kc(pair ? bn / 2 : bn, g.k);
     const uint64_t ldb = g.ldb ? g.ldb : g.k;
     if (conv != nullptr) {
         // the image as [pixels][channels] f32 rows, boxes of 32 channels x 128 pixels
@@ -1810,7 +1918,8 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
         const uint32_t ba[3] = {BK, BM, static_cast<uint32_t>(kc)};
         if ((rc = make_tmap_16bit_3d(&ta, g.a, da, sa, ba)) != BL_OK) return rc;
         const uint64_t db[3] = {BK, g.n, g.k / BK}, sb[2] = {ldb * 2, BK * 2};
-        const uint32_t bb[3] = {BK, static_cast<uint32_t>(bn), static_cast<uint32_t>(kc)};
+        const uint32_t bb[3] = {BK, static_cast<uint32_t>(pair ? bn / 2 : bn),
+                                static_cast<uint32_t>(kc)};
         if ((rc = make_tmap_16bit_3d(&tb, g.b, db, sb, bb)) != BL_OK) return rc;
     } else {
         const uint64_t dims[2] = {g.k, g.n};
@@ -1850,6 +1959,7 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
     p.weights_static = g.weights_static ? 1 : 0;
     p.m_tile0 = static_cast<int>(row_begin / BM);
     p.m_tiles = static_cast<int>((std::min(row_end, g.m) + BM - 1) / BM) - p.m_tile0;
+    if (pair) p.m_tiles = static_cast<int>((g.m + 2 * BM - 1) / (2 * BM));  // 256-row tiles
     if (row_begin % BM != 0 || row_begin >= row_end || p.m_tiles <= 0)
         return fail(BL_ERR_INVALID, "gemm: row part [%u, %u) is not whole 128-row tiles", row_begin, row_end);
     p.status = status_ptr();
@@ -1913,6 +2023,9 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
             default: return prepare_ln_staged<128>(ta, tb, to, p, out);
         }
     }
+    if (pair)
+        return bn == 256 ? prepare_persistent<256, true>(ta, tb, to, tn, p, kc, out)
+                         : prepare_persistent<128, true>(ta, tb, to, tn, p, kc, out);
     switch (bn) {
         case 32: return prepare_persistent<32>(ta, tb, to, tn, p, kc, out);
         case 64: return prepare_persistent<64>(ta, tb, to, tn, p, kc, out);

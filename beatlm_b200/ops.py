@@ -134,7 +134,7 @@ def attention(qkv, *, tokens: int, heads: int, head_dim: int = 64, batch: int = 
 def gemm_args(w, *, a=None, ln=None, bias=None, act=None, scale=None, chan_scale=None,
               residual=None, res_period=0, out, out_dtype=None, out_split=None, m=None,
               out_row_offset=0, out_group=(0, 0), tile_n=0, stats_out=None, ln_stats=None,
-              norm=None, norm_sync=None, weights_static=False):
+              norm=None, norm_sync=None, weights_static=False, pair_tiles=0):
     """``stats_out``: a float32 ``[rows][parts][2]`` tensor the epilogue fills
     with per-slice (mean, M2) of each stored row (``parts`` = n / tile width).
     ``ln_stats``: such a tensor for ``ln``'s input, used instead of a pass
@@ -143,7 +143,8 @@ def gemm_args(w, *, a=None, ln=None, bias=None, act=None, scale=None, chan_scale
     its zero-filled exchange buffer (``gemm_norm_sync_bytes``).
     ``weights_static``: ``w``, ``bias`` and ``chan_scale`` are not written by
     the kernel launched just before on the stream (model weights), so the
-    GEMM may fetch them while that kernel finishes."""
+    GEMM may fetch them while that kernel finishes. ``pair_tiles=2``: 256-row
+    tiles over CTA pairs (``bl_gemm_args.pair_tiles``)."""
     import torch
     n, k = w.shape
     ab = {torch.float16: "f16", torch.bfloat16: "bf16"}[w.dtype]
@@ -162,7 +163,7 @@ def gemm_args(w, *, a=None, ln=None, bias=None, act=None, scale=None, chan_scale
                    out=out.data_ptr(), out_dtype=odt, out_ld=out.stride(0),
                    out_row_offset=out_row_offset, out_group_rows=out_group[0],
                    out_group_gap=out_group[1], tile_n=tile_n,
-                   weights_static=1 if weights_static else 0)
+                   weights_static=1 if weights_static else 0, pair_tiles=pair_tiles)
     if out_split is not None:
         g.split_col, g.out_dtype_hi = out_split[0], _TD[out_split[1]]
     if ln is not None:

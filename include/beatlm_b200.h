@@ -390,6 +390,13 @@ typedef struct bl_gemm_args {
      * stored, exit. 8 * grid uint64 values (the persistent grid is
      * min(tiles, SMs) CTAs; bl_conv3x3's one CTA per tile). */
     uint64_t* trace;
+    /* 2: 256-row tiles computed by CTA pairs (a cluster of two CTAs, one
+     * cta_group::2 MMA per step: each CTA copies its 128 rows of A and half
+     * of the tile's B, so each SM brings in half the B bytes per MMA of a
+     * one-CTA tile); whole launches with A given as `a`, no LayerNorm
+     * prologue or epilogue LayerNorm, 128- or 256-column tiles. 0 or 1: one
+     * CTA per 128-row tile. */
+    uint32_t pair_tiles;
 } bl_gemm_args;
 
 int bl_gemm(const bl_gemm_args* args, void* stream);

@@ -8,6 +8,7 @@ the reference's own per-element tolerance |d| <= 1e-4 + 1e-4 |ref|
 computed in f32 on the GPU and in f64 in the oracle before both round to 16
 bits, so a few elements round to neighbouring 16-bit values: there the bound
 is relative L2 <= 1e-3 (bf16) / 2e-4 (f16)."""
+import ctypes
 import math
 
 import numpy as np
@@ -317,3 +318,72 @@ def test_bad_shapes_are_errors():
     with pytest.raises(bl.BackendError, match="tile width"):
         bl.ops.linear(w, a=torch.zeros((4, 64), dtype=torch.float16, device="cuda"),
                       out=torch.zeros((4, 40), device="cuda"))
+
+
+@pytest.mark.parametrize("m,n,k,tile,form", [
+    (1370, 3072, 1024, 256, "bias"),      # ViT-L qkv
+    (1370, 4096, 1024, 256, "gelu"),      # ViT-L fc1 (several tiles per pair)
+    (1370, 1024, 1024, 128, "residual"),  # ViT-L proj
+    (1370, 1024, 4096, 128, "residual"),  # ViT-L fc2
+    (100, 256, 128, 256, "bias"),         # one pair tile, the odd CTA's rows all past M
+    (700, 384, 384, 128, "generic"),      # generic epilogue (scale), f16
+])
+def test_cta_pair_tiles_equal_one_cta_tiles(m, n, k, tile, form):
+    """256-row tiles over CTA pairs (cta_group::2 MMAs reading both CTAs'
+    operands) give the same bits as 128-row tiles of one CTA with the same
+    epilogue, and meet the oracle."""
+    import torch
+    import beatlm_b200 as bl
+    from beatlm_b200 import ops
+    dtype = "f16" if form == "generic" else "bf16"
+    a = _rnd(oracle.normal(7 * m + n, m * k), dtype)
+    w = _rnd(oracle.uniform(k + 1, k * n, -1 / math.sqrt(k), 1 / math.sqrt(k)), dtype)
+    b = oracle.uniform(n + 2, n, -0.1, 0.1)
+    wd, ad, bd = _dev(w.reshape(k, n).T, dtype), _dev(a.reshape(m, k), dtype), _dev(b, "f32")
+    x0 = oracle.uniform(n + 3, m * n, -1.0, 1.0).reshape(m, n)
+    ls = oracle.uniform(n + 4, n, 0.1, 1.0)
+    outs = []
+    for pair in (0, 2):
+        kw = dict(bias=bd, tile_n=tile, weights_static=True, pair_tiles=pair)
+        if form == "residual":
+            x = _dev(x0, "f32")
+            kw.update(chan_scale=_dev(ls, "f32"), residual=x, out=x)
+        elif form == "gelu":
+            kw.update(act="gelu_erf", out=torch.zeros((m, n), dtype=torch.bfloat16, device="cuda"))
+        elif form == "generic":
+            kw.update(scale=0.5, out=torch.zeros((m, n), dtype=torch.float32, device="cuda"))
+        else:
+            kw.update(out=torch.zeros((m, n), dtype=torch.bfloat16, device="cuda"))
+        g = ops.gemm_args(wd, a=ad, **kw)
+        N = bl.ops.N
+        N.check(N.lib().bl_gemm(ctypes.byref(g), None))
+        torch.cuda.synchronize()
+        _check_status()
+        outs.append(kw["out"].float().cpu().numpy())
+    assert np.array_equal(outs[0], outs[1]), form
+    want = oracle.matmul(a, w, b, m, k, n)
+    if form == "residual":
+        want = x0.ravel() + want * np.tile(ls, m)
+        _close(outs[1], want, "pair residual")
+    elif form == "generic":
+        _close(outs[1], 0.5 * want, "pair generic")
+    else:
+        if form == "gelu":
+            want = oracle.gelu_erf(want)
+        assert _rel(outs[1], want) <= 4e-3
+
+
+def test_cta_pairs_reject_row_parts_and_prologues():
+    import torch
+    import beatlm_b200 as bl
+    from beatlm_b200 import ops
+    m, n, k = 512, 256, 128
+    w = torch.zeros((n, k), dtype=torch.bfloat16, device="cuda")
+    a = torch.zeros((m, k), dtype=torch.bfloat16, device="cuda")
+    out = torch.zeros((m, n), dtype=torch.float32, device="cuda")
+    g = ops.gemm_args(w, a=a, out=out, pair_tiles=3)
+    with pytest.raises(bl.BackendError, match="pair_tiles"):
+        bl.ops.N.check(bl.ops.N.lib().bl_gemm(ctypes.byref(g), None))
+    g = ops.gemm_args(w, a=a, out=out, pair_tiles=2, tile_n=64)
+    with pytest.raises(bl.BackendError, match="CTA pairs"):
+        bl.ops.N.check(bl.ops.N.lib().bl_gemm(ctypes.byref(g), None))
