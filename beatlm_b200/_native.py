@@ -118,7 +118,7 @@ class GemmArgs(ctypes.Structure):
         ("norm_beta", ctypes.c_void_p), ("norm_eps", ctypes.c_float),
         ("norm_sync", ctypes.c_void_p), ("norm_sync_bytes", ctypes.c_uint64),
         ("weights_static", ctypes.c_uint32), ("trace", ctypes.c_void_p),
-        ("pair_tiles", ctypes.c_uint32),
+        ("pair_tiles", ctypes.c_uint32), ("split_k", ctypes.c_uint32),
     ]
 
 

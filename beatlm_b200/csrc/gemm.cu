@@ -1020,6 +1020,261 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) trace_stamp(p.trace, 7);
 }
 
+// The K range split over a cluster of two CTAs (one tile per cluster): CTA
+// r of the pair accumulates the tile's stages [r S / 2, (r + 1) S / 2) into
+// its own tensor memory, then owns columns [r BN / 2, (r + 1) BN / 2) of the
+// tile. Each epilogue warp writes the partner's half of its 32 rows' partial
+// sums into its block of the output staging (128-byte rows swizzled by
+// 16-byte chunk) and one lane copies the block into the partner's receive
+// buffer with one bulk copy that completes on the partner's barrier (armed
+// at set-up for the four blocks); each warp then waits for the partner's
+// blocks, adds them to its own half (two addends, so either order gives the
+// same bits), writes the sum back to tensor memory and runs the ordinary
+// epilogue on its half. For K-heavy
+// launches with few tiles (ViT-S fc2: K = 1536 on 66 tiles of 64 columns),
+// which a CTA per tile leaves bound by the operand feed of half the SMs.
+template <int BN, int KC>
+struct SplitLayout {
+    static constexpr uint32_t kTileB = BN * BK * 2;
+    static constexpr uint32_t kStage = KC * (kTileA + kTileB);
+    static constexpr uint32_t kRecv = BM * (BN / 2) * 4;
+    static constexpr int kStages =
+        static_cast<int>((kSmemLimit - 4096 - kEpiBytes - kRecv) / kStage) < kMaxStages
+            ? static_cast<int>((kSmemLimit - 4096 - kEpiBytes - kRecv) / kStage)
+            : kMaxStages;
+};
+
+template <int BN, int KC>
+constexpr size_t split_smem_bytes() {
+    using L = SplitLayout<BN, KC>;
+    return 1024 + L::kStages * L::kStage + L::kRecv + kEpiBytes + sizeof(Tail);
+}
+
+template <int BN, int KC, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_split2(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                const __grid_constant__ CUtensorMap tm_o, const Params p) {
+    using L = SplitLayout<BN, KC>;
+    constexpr int STAGES = L::kStages;
+    static_assert(STAGES >= 2, "a stage ring needs two stages");
+    constexpr int HALF = BN / 2;
+    constexpr uint32_t kCols = Layout<BN>::kTmemCols;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint8_t* recv = smem + STAGES * L::kStage;  // the partner's partials of this CTA's half
+    uint8_t* epi = recv + L::kRecv;
+    Tail* tail = reinterpret_cast<Tail*>(epi + kEpiBytes);
+    volatile int* abort = &tail->abort;
+    auto sA = [&](int s) { return smem + s * L::kStage; };
+    auto sB = [&](int s) { return smem + s * L::kStage + KC * kTileA; };
+
+    const int warp = warp_id();
+    const int lane = lane_id();
+    const int rank = static_cast<int>(cluster_rank());
+    const int t = static_cast<int>(blockIdx.x) / 2;  // the cluster's tile
+    const int m0 = (p.m_tile0 + t % p.m_tiles) * BM;
+    const int n0 = (t / p.m_tiles) * BN;
+    const int all = p.K / (BK * KC);  // stages of the whole K
+    const int s0 = all * rank / 2;    // this CTA's stages [s0, s0 + nk)
+    const int nk = all * (rank + 1) / 2 - s0;
+    // the tail's drain barrier doubles as the receive barrier: armed here for
+    // the partner's four 32-row blocks, completed by their bulk copies
+    const uint32_t b_recv = smem_u32(&tail->drain);
+
+    if (threadIdx.x == 0) {
+        trace_stamp(p.trace, 0);
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(smem_u32(&tail->full[s]), 1);
+            mbar_init(smem_u32(&tail->empty[s]), 1);
+        }
+        mbar_init(smem_u32(&tail->acc_full[0]), 1);
+        mbar_init(smem_u32(&tail->acc_full[1]), 1);  // the MMA's unwinding
+        mbar_init(b_recv, 1);
+        tail->abort = 0;
+        fence_barrier_init();
+        fence_proxy_async_smem();
+        tma_prefetch_desc(&tm_a);
+        tma_prefetch_desc(&tm_b);
+        if (p.tma_store) tma_prefetch_desc(&tm_o);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(&tail->tmem_base), kCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (threadIdx.x == 0) mbar_arrive_expect_tx(b_recv, L::kRecv);
+    cluster_sync();  // the partner's barrier and receive buffer exist before any push
+    tc_fence_after();
+    const uint32_t tmem = tail->tmem_base;
+    if (threadIdx.x == 0) trace_stamp(p.trace, 1);
+    pdl_trigger();
+
+    if (warp == 0) {
+        const int first = !p.weights_static ? 0 : STAGES < nk ? STAGES : nk;
+        for (int g = 0; g < first; ++g) {
+            const uint32_t bar = smem_u32(&tail->full[g]);
+            if (lane == 0) mbar_arrive_expect_tx(bar, L::kStage);
+            if (lane == 1) tma_load_3d(smem_u32(sB(g)), &tm_b, 0, n0, (s0 + g) * KC, bar);
+        }
+        pdl_wait();
+        if (lane == 0) trace_stamp(p.trace, 2);
+        int g = 0;
+        for (; g < nk; ++g) {
+            const int s = g % STAGES;
+            bool r = true;
+            if (lane == 0 && g >= STAGES)
+                r = mbar_wait(smem_u32(&tail->empty[s]), ((g / STAGES) - 1) & 1, abort, p.status,
+                              ST_TIMEOUT_TMA, g);
+            if (!__all_sync(0xFFFFFFFFu, r)) break;
+            const uint32_t bar = smem_u32(&tail->full[s]);
+            if (lane == 0) {
+                if (g >= first) mbar_arrive_expect_tx(bar, L::kStage);
+                tma_load_3d(smem_u32(sA(s)), &tm_a, 0, m0, (s0 + g) * KC, bar);
+            } else if (lane == 1 && g >= first) {
+                tma_load_3d(smem_u32(sB(s)), &tm_b, 0, n0, (s0 + g) * KC, bar);
+            }
+            __syncwarp();
+        }
+        if (lane == 0 && *abort) {
+            for (int s = 0; s < STAGES && s < g; ++s) {
+                const int uses = (g - s - 1) / STAGES + 1;
+                mbar_wait(smem_u32(&tail->full[s]), (uses - 1) & 1, nullptr, p.status,
+                          ST_TIMEOUT_DRAIN, s);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        const bool elected = elect_one();
+        const uint32_t idesc = idesc_f16(BM, BN, p.ab_fmt, p.ab_fmt, 0, 0);
+        bool ok = true;
+        for (int g = 0; g < nk && ok; ++g) {
+            const int s = g % STAGES;
+            bool r = true;
+            if (elected)
+                r = mbar_wait(smem_u32(&tail->full[s]), (g / STAGES) & 1, abort, p.status,
+                              ST_TIMEOUT_MMA, g);
+            ok = __all_sync(0xFFFFFFFFu, r);
+            if (!ok) break;
+            if (g == 0 && elected) trace_stamp(p.trace, 3);
+            tc_fence_after();
+            const uint32_t a = smem_u32(sA(s)), bb = smem_u32(sB(s));
+            if (elected) {
+#pragma unroll
+                for (int c = 0; c < KC; ++c)
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k)
+                        mma_ss(tmem, desc_k(a + c * kTileA + 32 * k),
+                               desc_k(bb + c * L::kTileB + 32 * k), idesc,
+                               (g > 0 || c > 0 || k > 0) ? 1u : 0u);
+                if (g + STAGES < nk) mma_commit(smem_u32(&tail->empty[s]));
+            }
+            __syncwarp();
+        }
+        if (elected) {
+            if (ok) {
+                mma_commit(smem_u32(&tail->acc_full[0]));
+                trace_stamp(p.trace, 4);
+            } else {
+                mma_commit(smem_u32(&tail->acc_full[1]));
+                mbar_wait(smem_u32(&tail->acc_full[1]), 0, nullptr, p.status, ST_TIMEOUT_DRAIN,
+                          0xD);
+            }
+        }
+        __syncwarp();
+    } else {
+        const int sub = warp & 3;
+        const int row = sub * 32 + lane;
+        const uint32_t t_lane = tmem + (static_cast<uint32_t>(sub * 32) << 16);
+        const int mine = rank * HALF, theirs = (1 - rank) * HALF;  // column offsets
+        const RowCtx rc = row_ctx(p, m0 + row);
+        if (!p.weights_static) pdl_wait();
+        stage_vectors<HALF>(p, tail, n0 + mine);
+        epilogue_all(true);
+        pdl_wait();  // the residual and the outputs belong to the previous kernels
+        float rv0[32];
+        prefetch_residual(p, rc, n0 + mine, rv0);
+        bool ok = mbar_wait(smem_u32(&tail->acc_full[0]), 0, abort, p.status, ST_TIMEOUT_SOFTMAX,
+                            0x200);
+        if (threadIdx.x == 64) trace_stamp(p.trace, 5);
+        ok = epilogue_all(ok);
+        tc_fence_after();
+        // the partner's half of this warp's 32 rows, 32 columns at a time,
+        // staged in the warp's 4 KiB block and copied into the partner's
+        // receive buffer (block c of warp sub at (c * 4 + sub) * 4 KiB)
+        const uint32_t peer = static_cast<uint32_t>(1 - rank);
+        uint8_t* blk = epi + sub * kEpiBlock;
+#pragma unroll 1
+        for (int c = 0; c < HALF / 32; ++c) {
+            uint32_t r[32];
+            if (ok) {
+                tmem_ld32(t_lane + theirs + 32 * c, r);
+                tmem_wait_ld();
+            }
+            if (c > 0) {  // the previous block has left the staging
+                if (lane == 0) bulk_wait_read();
+                __syncwarp();
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                *reinterpret_cast<uint4*>(blk + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+                    make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                const uint32_t off = static_cast<uint32_t>((c * 4 + sub) * kEpiBlock);
+                bulk_copy_to_peer(dsmem_addr(smem_u32(recv) + off, peer), smem_u32(blk),
+                                  kEpiBlock, dsmem_addr(b_recv, peer));
+                bulk_commit();
+            }
+        }
+        if (lane == 0) bulk_wait_read();  // the staging is free for the output blocks
+        __syncwarp();
+        // the partner's partials of this CTA's half, added to its own and
+        // written back for the ordinary epilogue
+        if (ok) ok = mbar_wait_cluster(b_recv, 0, abort, p.status, ST_TIMEOUT_SOFTMAX, 0x210);
+        ok = epilogue_all(ok);
+        if (ok) {
+#pragma unroll 1
+            for (int c = 0; c < HALF / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld32(t_lane + mine + 32 * c, r);
+                tmem_wait_ld();
+                const uint8_t* src = recv + (c * 4 + sub) * kEpiBlock + lane * 128;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const uint4 q = *reinterpret_cast<const uint4*>(src + ((j ^ (lane & 7)) << 4));
+                    r[4 * j] = __float_as_uint(__uint_as_float(r[4 * j]) + __uint_as_float(q.x));
+                    r[4 * j + 1] =
+                        __float_as_uint(__uint_as_float(r[4 * j + 1]) + __uint_as_float(q.y));
+                    r[4 * j + 2] =
+                        __float_as_uint(__uint_as_float(r[4 * j + 2]) + __uint_as_float(q.z));
+                    r[4 * j + 3] =
+                        __float_as_uint(__uint_as_float(r[4 * j + 3]) + __uint_as_float(q.w));
+                }
+                tmem_st32(t_lane + mine + 32 * c, r);
+            }
+            tmem_wait_st();
+            store_tile<HALF, EPI>(p, tail, t_lane + mine, n0 + mine, rc, rv0,
+                                  p.tma_store ? &tm_o : nullptr, epi + sub * kEpiBlock,
+                                  m0 + sub * 32 + p.out_row_offset);
+        }
+        if (p.tma_store && lane == 0) bulk_wait_all();
+        __syncwarp();
+        if (threadIdx.x == 64) trace_stamp(p.trace, 6);
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, kCols);
+    }
+    if (threadIdx.x == 0) trace_stamp(p.trace, 7);
+}
+
 // The LayerNorm prologue with its rows brought by TMA (one tile per CTA):
 // A = LayerNorm(x) for f32 rows x whose per-row statistics the GEMM that
 // wrote x left as (mean, M2) per column slice. A stage holds a k-block of x
@@ -1620,6 +1875,21 @@ int prepare_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
     return prepare_persistent<BN, 1, EPI, kPair>(ta, tb, to, tn, p, out);
 }
 
+template <int BN, int KC, int EPI>
+int prepare_split2(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+                   const Params& p, Launch* out) {
+    constexpr size_t smem = split_smem_bytes<BN, KC>();
+    out->op = 2;
+    auto kern = gemm_split2<BN, KC, EPI>;
+    BL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(smem)));
+    const dim3 grid(2 * p.m_tiles * (p.N / BN));
+    out->run = [=](cudaStream_t s) {
+        return launch_k_cluster(kern, grid, dim3(kThreads), dim3(2, 1, 1), smem, s, ta, tb, to, p);
+    };
+    return BL_OK;
+}
+
 // The epilogue form (store_tile's EPI) these arguments match exactly, or -1.
 int epilogue_form(const Params& p) {
     if (!p.tma_store || p.scale != 1.0f || p.stats_out != nullptr || p.norm_out != nullptr)
@@ -1631,6 +1901,29 @@ int epilogue_form(const Params& p) {
     if (p.act == 0 && p.chan_scale != nullptr && p.residual != nullptr && wide && one_type)
         return 2;
     return -1;
+}
+
+// The split form's stages: the most k-blocks (4, 2, 1) that divide K / 64
+// and leave a ring of two stages beside the receive buffer and the staging.
+int pick_kc_split(int bn, uint32_t k) {
+    const uint32_t nk = k / BK;
+    for (int kc : {4, 2}) {
+        const uint32_t stage = kc * (kTileA + bn * BK * 2);
+        if (nk % kc == 0 && (kSmemLimit - 4096 - kEpiBytes - BM * (bn / 2) * 4) / stage >= 2)
+            return kc;
+    }
+    return 1;
+}
+
+template <int BN, int KC>
+int prepare_split2(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+                   const Params& p, Launch* out) {
+    switch (epilogue_form(p)) {
+        case 0: return prepare_split2<BN, KC, 0>(ta, tb, to, p, out);
+        case 1: return prepare_split2<BN, KC, 1>(ta, tb, to, p, out);
+        case 2: return prepare_split2<BN, KC, 2>(ta, tb, to, p, out);
+        default: return prepare_split2<BN, KC, -1>(ta, tb, to, p, out);
+    }
 }
 
 template <int BN, bool kPair = false>
@@ -1891,7 +2184,27 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
             return fail(BL_ERR_UNSUPPORTED, "gemm: CTA pairs take 128- or 256-column tiles (N=%u)",
                         g.n);
     }
-    const int kc = ln ? 1 : pick_kc(pair ? bn / 2 : bn, g.k);
+    // The K range split over a cluster of two CTAs (split_k 2, or 0 for
+    // K >= 1024 with N <= 512 in 64-column tiles, a rule of the shape alone so
+    // row parts split exactly as their whole launch): 64-column tiles.
+    if (g.split_k > 2) return fail(BL_ERR_INVALID, "gemm: split_k %u (0, 1 or 2)", g.split_k);
+    const bool split_ok = !ln && !norm && conv == nullptr && g.a != nullptr &&
+                          g.stats_out == nullptr && !pair && g.n % 64 == 0 &&
+                          (g.tile_n == 0 || g.tile_n == 64) && g.k / BK >= 4;
+    // (the automatic rule also asks that both CTAs of every tile of the whole
+    // launch, m rows, fit one wave; m is the whole launch's for a row part)
+    const bool ksplit =
+        g.split_k == 2 ||
+        (g.split_k == 0 && split_ok && g.k >= 1024 && g.n <= 512 &&
+         2ull * ((g.m + BM - 1) / BM) * (g.n / 64) <= static_cast<uint64_t>(sm_count()));
+    if (ksplit) {
+        if (!split_ok)
+            return fail(BL_ERR_UNSUPPORTED, "gemm: the K split takes A loaded by TMA, N a multiple "
+                                            "of 64, 64-column tiles, K >= 256, no LayerNorm, "
+                                            "statistics, CTA pairs or convolution");
+        bn = 64;
+    }
+    const int kc = ln ? 1 : ksplit ? pick_kc_split(bn, g.k) : pick_kc(pair ? bn / 2 : bn, g.k);
     const uint64_t ldb = g.ldb ? g.ldb : g.k;
     if (conv != nullptr) {
         // the image as [pixels][channels] f32 rows, boxes of 32 channels x 128 pixels
@@ -2026,6 +2339,13 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
     if (pair)
         return bn == 256 ? prepare_persistent<256, true>(ta, tb, to, tn, p, kc, out)
                          : prepare_persistent<128, true>(ta, tb, to, tn, p, kc, out);
+    if (ksplit) {
+        // pick_kc_split keeps two stages: only those depths are built
+        if constexpr (SplitLayout<64, 4>::kStages >= 2)
+            if (kc == 4) return prepare_split2<64, 4>(ta, tb, to, p, out);
+        if (kc == 2) return prepare_split2<64, 2>(ta, tb, to, p, out);
+        return prepare_split2<64, 1>(ta, tb, to, p, out);
+    }
     switch (bn) {
         case 32: return prepare_persistent<32>(ta, tb, to, tn, p, kc, out);
         case 64: return prepare_persistent<64>(ta, tb, to, tn, p, kc, out);

@@ -163,6 +163,17 @@ __device__ __forceinline__ void tma_store_2d(const void* tmap, uint32_t src, int
         "r"(src), "r"(x), "r"(y)
         : "memory");
 }
+// Copy `bytes` (a multiple of 16, both addresses 16-byte aligned) from this
+// CTA's shared memory to another CTA's of the cluster (`dst` and `bar`
+// shared::cluster addresses from mapa); the copy's completion is counted on
+// that CTA's barrier (complete_tx). Not a multicast.
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst, uint32_t src, uint32_t bytes,
+                                                  uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(dst), "r"(src), "r"(bytes), "r"(bar)
+        : "memory");
+}
 __device__ __forceinline__ void bulk_commit() {
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }

@@ -134,7 +134,7 @@ def attention(qkv, *, tokens: int, heads: int, head_dim: int = 64, batch: int = 
 def gemm_args(w, *, a=None, ln=None, bias=None, act=None, scale=None, chan_scale=None,
               residual=None, res_period=0, out, out_dtype=None, out_split=None, m=None,
               out_row_offset=0, out_group=(0, 0), tile_n=0, stats_out=None, ln_stats=None,
-              norm=None, norm_sync=None, weights_static=False, pair_tiles=0):
+              norm=None, norm_sync=None, weights_static=False, pair_tiles=0, split_k=0):
     """``stats_out``: a float32 ``[rows][parts][2]`` tensor the epilogue fills
     with per-slice (mean, M2) of each stored row (``parts`` = n / tile width).
     ``ln_stats``: such a tensor for ``ln``'s input, used instead of a pass
@@ -144,7 +144,8 @@ def gemm_args(w, *, a=None, ln=None, bias=None, act=None, scale=None, chan_scale
     ``weights_static``: ``w``, ``bias`` and ``chan_scale`` are not written by
     the kernel launched just before on the stream (model weights), so the
     GEMM may fetch them while that kernel finishes. ``pair_tiles=2``: 256-row
-    tiles over CTA pairs (``bl_gemm_args.pair_tiles``)."""
+    tiles over CTA pairs (``bl_gemm_args.pair_tiles``); ``split_k``: the K
+    split over a two-CTA cluster (0 automatic, 1 off, 2 on)."""
     import torch
     n, k = w.shape
     ab = {torch.float16: "f16", torch.bfloat16: "bf16"}[w.dtype]
@@ -163,7 +164,8 @@ def gemm_args(w, *, a=None, ln=None, bias=None, act=None, scale=None, chan_scale
                    out=out.data_ptr(), out_dtype=odt, out_ld=out.stride(0),
                    out_row_offset=out_row_offset, out_group_rows=out_group[0],
                    out_group_gap=out_group[1], tile_n=tile_n,
-                   weights_static=1 if weights_static else 0, pair_tiles=pair_tiles)
+                   weights_static=1 if weights_static else 0, pair_tiles=pair_tiles,
+                   split_k=split_k)
     if out_split is not None:
         g.split_col, g.out_dtype_hi = out_split[0], _TD[out_split[1]]
     if ln is not None:
@@ -275,7 +277,7 @@ def im2col(x, h: int, w: int, cin: int, ksize: int = 3, stride: int = 1, relu: b
 
 def conv2d(x, weights, bias, h: int, w: int, cin: int, cout: int, *, ksize: int = 3,
            stride: int = 1, relu_input: bool = False, act=None, residual=None, stream=None,
-           implicit: bool | None = None):
+           implicit: bool | None = None, split_k: int = 0):
     """A 3x3 (zero padding 1) or 1x1 convolution of the NHWC f32 map ``x``:
     ``weights`` from ``conv_weights``, ``bias`` f32 [cout] or None, ``act``
     "relu" on the result, ``residual`` an f32 [oh * ow][cout] map added last
@@ -289,7 +291,8 @@ def conv2d(x, weights, bias, h: int, w: int, cin: int, cout: int, *, ksize: int 
     (148 x 148 x 64: 23 against 27 us; 518 x 518 x 32: 105 against 122 us),
     since the implicit kernel's f32 image tiles take about 1 us per TMA round
     trip, more than a three-stage ring hides, and are converted to 16 bits
-    on chip for every tap."""
+    on chip for every tap. ``split_k``: as ``gemm_args`` (the gathered
+    form's GEMM)."""
     import torch
     dt = "f16" if weights.dtype == torch.float16 else "bf16"
     can = (ksize == 3 and stride == 1 and cin % 32 == 0 and x.dtype == torch.float32
@@ -319,7 +322,7 @@ def conv2d(x, weights, bias, h: int, w: int, cin: int, cout: int, *, ksize: int 
         bias_pad[:cout] = bias.reshape(-1)[:cout].to(device=x.device, dtype=torch.float32)
     out = torch.empty((oh * ow, n_pad), dtype=torch.float32, device=x.device)
     g = gemm_args(weights, a=cols, m=oh * ow, bias=bias_pad, act=act, residual=residual,
-                  out=out)
+                  out=out, split_k=split_k)
     if implicit:
         c = N.Conv3x3Args(input=x.data_ptr(), h=h, w=w, cin=cin, relu=1 if relu_input else 0)
         N.check(N.lib().bl_conv3x3(ctypes.byref(g), ctypes.byref(c), _stream_ptr(stream)))

@@ -397,6 +397,14 @@ typedef struct bl_gemm_args {
      * prologue or epilogue LayerNorm, 128- or 256-column tiles. 0 or 1: one
      * CTA per 128-row tile. */
     uint32_t pair_tiles;
+    /* 2: the K range split over a cluster of two CTAs per 64-column tile,
+     * each CTA adding the other's partial sums for its half of the columns
+     * (distributed shared memory) and running the epilogue on that half;
+     * for A given as `a`, N a multiple of 64, no LayerNorm or statistics.
+     * 0: automatic, which takes it for K >= 1024 with N <= 512 when both
+     * CTAs of every 64-column tile fit one wave (a rule of the whole
+     * launch's shape, so row parts compute as their whole launch). 1: off. */
+    uint32_t split_k;
 } bl_gemm_args;
 
 int bl_gemm(const bl_gemm_args* args, void* stream);

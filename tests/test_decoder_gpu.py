@@ -219,8 +219,9 @@ def test_blocks_to_map_scatters_every_block(h, w, f, cout, bias):
 ])
 def test_implicit_conv3x3_equals_the_gathered_one(h, w, cin, cout, relu, act, res):
     """bl_conv3x3 (the image read through the taps on chip) against im2col +
-    bl_gemm: the same 16-bit A values, the same k-block order and the same
-    epilogue, so the same bits; and both against the oracle."""
+    bl_gemm with K in one chain (split_k 1): the same 16-bit A values, the
+    same k-block order and the same epilogue, so the same bits; and both
+    against the oracle."""
     import torch
     import beatlm_b200 as bl
     from beatlm_b200 import ops
@@ -231,7 +232,7 @@ def test_implicit_conv3x3_equals_the_gathered_one(h, w, cin, cout, relu, act, re
     r = torch.from_numpy(_data(43, h * w * cout)).cuda().reshape(h * w, cout) if res else None
     wdev = ops.conv_weights(wt, 3, cin, cout)
     run = lambda implicit: ops.conv2d(dev, wdev, b, h, w, cin, cout, relu_input=relu, act=act,
-                                      residual=r, implicit=implicit)
+                                      residual=r, implicit=implicit, split_k=1)
     got, gathered = run(True), run(False)
     torch.cuda.synchronize()
     assert bl.status(reset=True).code == 0

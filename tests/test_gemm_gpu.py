@@ -387,3 +387,67 @@ def test_cta_pairs_reject_row_parts_and_prologues():
     g = ops.gemm_args(w, a=a, out=out, pair_tiles=2, tile_n=64)
     with pytest.raises(bl.BackendError, match="CTA pairs"):
         bl.ops.N.check(bl.ops.N.lib().bl_gemm(ctypes.byref(g), None))
+
+
+@pytest.mark.parametrize("m,n,k,form", [
+    (1370, 384, 1536, "residual"),  # ViT-S fc2 (the automatic choice)
+    (1370, 384, 1024, "bias"),
+    (129, 128, 256, "gelu"),        # the shortest K the split takes: two stages per CTA
+    (300, 64, 3456, "bias"),        # a single column tile, K of the DPT neck convolution
+    (1370, 512, 1600, "generic"),   # K / 64 = 25: unequal halves
+])
+def test_k_split_over_a_cluster_meets_the_oracle(m, n, k, form):
+    """The K range split over two CTAs of a cluster, each adding the other's
+    partial sums for its half of the columns (distributed shared memory)
+    before the epilogue: within the reference's GEMM tolerance of the oracle,
+    and close to the unsplit kernel (which sums K in one chain)."""
+    import torch
+    import beatlm_b200 as bl
+    from beatlm_b200 import ops
+    dtype = "bf16"
+    a = _rnd(oracle.normal(11 * m + k, m * k), dtype)
+    w = _rnd(oracle.uniform(k + 5, k * n, -1 / math.sqrt(k), 1 / math.sqrt(k)), dtype)
+    b = oracle.uniform(n + 6, n, -0.1, 0.1)
+    wd, ad, bd = _dev(w.reshape(k, n).T, dtype), _dev(a.reshape(m, k), dtype), _dev(b, "f32")
+    x0 = oracle.uniform(n + 7, m * n, -1.0, 1.0).reshape(m, n)
+    ls = oracle.uniform(n + 8, n, 0.1, 1.0)
+    outs = []
+    for split in (1, 2):
+        kw = dict(bias=bd, weights_static=True, split_k=split)
+        if form == "residual":
+            x = _dev(x0, "f32")
+            kw.update(chan_scale=_dev(ls, "f32"), residual=x, out=x)
+        elif form == "gelu":
+            kw.update(act="gelu_erf", out=torch.zeros((m, n), dtype=torch.float32, device="cuda"))
+        elif form == "generic":
+            kw.update(scale=0.25, out=torch.zeros((m, n), dtype=torch.float32, device="cuda"))
+        else:
+            kw.update(out=torch.zeros((m, n), dtype=torch.float32, device="cuda"))
+        g = ops.gemm_args(wd, a=ad, **kw)
+        bl.ops.N.check(bl.ops.N.lib().bl_gemm(ctypes.byref(g), None))
+        torch.cuda.synchronize()
+        _check_status()
+        outs.append(kw["out"].float().cpu().numpy())
+    want = oracle.matmul(a, w, b, m, k, n)
+    if form == "residual":
+        want = x0.ravel() + want * np.tile(ls, m)
+    elif form == "gelu":
+        want = oracle.gelu_erf(want)
+    elif form == "generic":
+        want = 0.25 * want
+    _close(outs[1], want, "K split %s" % form)
+    # two f32 partial sums added instead of one chain: a few ulps over long K
+    assert _rel(outs[1], outs[0]) < 1e-5
+
+
+def test_k_split_rejects_what_it_cannot_take():
+    import torch
+    import beatlm_b200 as bl
+    from beatlm_b200 import ops
+    w = torch.zeros((96, 1024), dtype=torch.bfloat16, device="cuda")
+    a = torch.zeros((256, 1024), dtype=torch.bfloat16, device="cuda")
+    out = torch.zeros((256, 96), dtype=torch.float32, device="cuda")
+    for bad, match in ((dict(split_k=3), "split_k"), (dict(split_k=2), "K split")):
+        g = ops.gemm_args(w, a=a, out=out, **bad)
+        with pytest.raises(bl.BackendError, match=match):
+            bl.ops.N.check(bl.ops.N.lib().bl_gemm(ctypes.byref(g), None))
