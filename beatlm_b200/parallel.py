@@ -200,6 +200,17 @@ class HeadParallelAttention:
                                   qk_dtype=self.qk_dtype, out_dtype=self.out_dtype,
                                   out_row_stride=out_row_stride)
 
+    def launch_shape(self, qkv_local) -> dict:
+        """The attention launch this rank runs: query tiles per CTA, key
+        splits and the unsplit query groups of a mixed grid (the peer
+        exchange takes two query tiles)."""
+        from . import ops
+        a = self._args(qkv_local, self.local)
+        if self.exchange == "peers":
+            a.query_tiles = 2
+        qt, splits, unsplit = ops.attention_choice(a)
+        return {"query_tiles": qt, "kv_splits": splits, "unsplit_groups": unsplit}
+
     def compute_local(self, qkv_local, stream=None):
         """This rank's heads into a local [T][H/g * 64] buffer, no exchange
         (the attention alone, for timing)."""

@@ -198,8 +198,13 @@ class AttentionWorkload:
         self.launches_per_step = 1
 
     def config(self):
+        from beatlm_b200 import ops
+        qt, splits, unsplit = ops.attention_choice(
+            ops.attention_args(self.dev, tokens=self.t, heads=self.h, out=self.out))
         return {"workload": self.workload_name, "batch": 1, "tokens": self.t, "heads": self.h,
                 "head_dim": 64, "qkv_dtype": "f16", "out_dtype": "f32",
+                "attention_launch": {"query_tiles": qt, "kv_splits": splits,
+                                     "unsplit_groups": unsplit},
                 "l2": "flushed before every timed launch (256 MiB write)"}
 
     def step(self, stream):
@@ -716,6 +721,7 @@ class HiresWorkload:
                 "head_dim": 64, "heads_per_gpu": self.op.local_heads,
                 "qkv_dtype": "bf16 Q/K, f16 V", "out_dtype": "f16",
                 "exchange": self.op.exchange_name(),
+                "attention_launch": self.op.launch_shape(self.dev),
                 "l2": "flushed before every timed step (256 MiB write)"}
 
     def step(self, stream):
