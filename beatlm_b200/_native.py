@@ -119,6 +119,8 @@ class GemmArgs(ctypes.Structure):
         ("norm_sync", ctypes.c_void_p), ("norm_sync_bytes", ctypes.c_uint64),
         ("weights_static", ctypes.c_uint32), ("trace", ctypes.c_void_p),
         ("pair_tiles", ctypes.c_uint32), ("split_k", ctypes.c_uint32),
+        ("stream_k", ctypes.c_uint32), ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_uint64),
     ]
 
 
@@ -196,6 +198,7 @@ SIGNATURES.update({
     "bl_timer_get_stats": (ctypes.c_int, [_vp, ctypes.POINTER(TimerStats)]),
     "bl_gemm": (ctypes.c_int, [ctypes.POINTER(GemmArgs), ctypes.c_void_p]),
     "bl_gemm_norm_sync_bytes": (ctypes.c_uint64, [ctypes.POINTER(GemmArgs)]),
+    "bl_gemm_workspace_bytes": (ctypes.c_uint64, [ctypes.POINTER(GemmArgs)]),
     "bl_layernorm": (ctypes.c_int, [ctypes.POINTER(LayerNormArgs), ctypes.c_void_p]),
     "bl_patchify": (ctypes.c_int, [ctypes.POINTER(PatchifyArgs), ctypes.c_void_p]),
 })

@@ -76,6 +76,17 @@ struct Params {
     unsigned* norm_ctr;
     float2* norm_stats;
     unsigned long long* trace;  // optional per-CTA timeline (persistent kernel)
+    // Stream-K (persistent kernel, sk_pieces > 1): every tile's stages are
+    // cut into sk_pieces pieces, accumulated separately; slot t * sk_pieces
+    // + i of sk_part holds the f32 partial sums of piece i < sk_pieces - 1
+    // of tile t and sk_flag marks it written; the CTA that computes the
+    // last piece adds them to its own in piece order. A slot is laid out
+    // [32-column chunk][32-row quarter][4-column group][row in quarter] of
+    // float4, so the 32 rows (one per lane) of a warp's access to one
+    // column group are 512 contiguous bytes.
+    int sk_pieces;
+    float* sk_part;
+    unsigned* sk_flag;
     // implicit 3x3 convolution (gemm_conv): an NHWC f32 image of conv_w
     // columns and conv_pix pixels, conv_cin channels; K columns past conv_k
     // (9 cin) are zero; conv_relu: max(x, 0) on every input value
@@ -91,6 +102,18 @@ struct Params {
 // Output staging of the persistent kernel's epilogue: one 32 x 32 block of
 // up to 4-byte values per epilogue warp, stored to global memory by TMA.
 constexpr uint32_t kEpiBlock = 32 * 32 * 4;
+// Stream-K partial slot: floats per 32-column chunk of 128 rows
+constexpr uint32_t kSkChunk = BM * 32;
+// a row's float4 of column group k (0..7) in its chunk, from its row base
+// (sk_row_base): 32 float4 (one per row of the quarter) per column group
+constexpr uint32_t kSkGroup = 32;
+__device__ __forceinline__ uint32_t sk_row_base(int row) {
+    return static_cast<uint32_t>((row >> 5) * 8 * 32 + (row & 31)) * 4;  // floats
+}
+// At most three pieces per tile: the finishing piece loads the other two
+// pieces' values of a chunk at once (registers), one L2 round trip a chunk
+constexpr int kMaxSkPieces = 3;
+constexpr int kMaxSkParts = kMaxSkPieces - 1;
 constexpr uint32_t kEpiBytes = 4 * kEpiBlock;
 
 template <int BN, int KC = 1, bool kEpi = false>
@@ -259,27 +282,81 @@ __device__ __forceinline__ void prefetch_residual(const Params& p, const RowCtx&
 // generic (everything decided at run time); 0 plain (bias only, 16-bit out);
 // 1 bias + GELU-erf, 16-bit out; 2 bias, LayerScale and f32 residual. The
 // host picks a fixed form only where the arguments match it exactly.
-template <int BN, int EPI = -1>
+// kParts > 0 (stream-K): `parts` is this row's partial sums of the tile's
+// other pieces, `nparts` (at most kParts) slots `part_stride` floats apart,
+// added to the accumulator in slot order before anything else; a chunk's
+// partials and residual are then loaded together while its accumulator
+// comes (one round trip a chunk).
+template <int BN, int EPI = -1, int kParts = 0>
 __device__ __forceinline__ void store_tile(const Params& p, const Tail* tail, uint32_t t_lane,
                                            int n0, const RowCtx& rc, const float* rv0,
                                            const CUtensorMap* tmo = nullptr,
                                            uint8_t* buf = nullptr, int box_row = 0,
-                                           float* keep = nullptr) {
+                                           float* keep = nullptr, const float* parts = nullptr,
+                                           int nparts = 0, size_t part_stride = 0) {
     const bool live = rc.live;
     const long long orow = rc.orow, res_row = rc.res_row;
     const size_t res_esz = p.res_dtype == BL_F32 ? 4 : 2;
     const int lane = lane_id();
     float run_mean = 0.0f, run_m2 = 0.0f;  // row statistics of the stored slice
+    const bool add_res = (EPI < 0 ? p.residual != nullptr : EPI == 2) && live;
+    // stream-K: the chunk's residual, the first chunk's from the caller (so
+    // rv0 is not live across the loop), later ones loaded with the partials
+    float rvc[kParts > 0 ? 32 : 1];
+    if constexpr (kParts > 0) {
+        if (add_res) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) rvc[i] = rv0[i];
+        }
+    }
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
+        const int col = n0 + c * 32;
+        // stream-K: the chunk's other addends, loaded together: the other
+        // pieces' partial sums (written by other CTAs in this launch: through
+        // L2 only) and, past the first chunk, whose residual the caller
+        // loaded, the residual
+        float4 pf[kParts > 0 ? kParts : 1][8];
+        if constexpr (kParts > 0) {
+#pragma unroll
+            for (int q = 0; q < kParts; ++q) {
+                if (q < nparts) {
+                    const float4* src =
+                        reinterpret_cast<const float4*>(parts + q * part_stride + c * kSkChunk);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) pf[q][i] = __ldcg(src + i * kSkGroup);
+                }
+            }
+        }
+        if constexpr (kParts > 0) {
+            if (add_res && c > 0) {
+                const uint8_t* rb = static_cast<const uint8_t*>(p.residual) +
+                                    res_esz * (res_row * p.res_ld + col);
+                load16(rb, p.res_dtype, rvc);
+                load16(rb + res_esz * 16, p.res_dtype, rvc + 16);
+            }
+        }
         uint32_t r[32];
         tmem_ld32(t_lane + c * 32, r);
         tmem_wait_ld();
         if (!live && tmo == nullptr) continue;
-        const int col = n0 + c * 32;
         float v[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+        if constexpr (kParts > 0) {
+#pragma unroll
+            for (int q = 0; q < kParts; ++q) {
+                if (q < nparts) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        v[4 * i] += pf[q][i].x;
+                        v[4 * i + 1] += pf[q][i].y;
+                        v[4 * i + 2] += pf[q][i].z;
+                        v[4 * i + 3] += pf[q][i].w;
+                    }
+                }
+            }
+        }
         if (p.bias != nullptr) {
 #pragma unroll
             for (int i = 0; i < 32; i += 4) {
@@ -309,8 +386,11 @@ __device__ __forceinline__ void store_tile(const Params& p, const Tail* tail, ui
                 v[i] *= s.x; v[i + 1] *= s.y; v[i + 2] *= s.z; v[i + 3] *= s.w;
             }
         }
-        if ((EPI < 0 ? p.residual != nullptr : EPI == 2) && live) {
-            if (c == 0) {
+        if (add_res) {
+            if constexpr (kParts > 0) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] += rvc[i];
+            } else if (c == 0) {
 #pragma unroll
                 for (int i = 0; i < 32; ++i) v[i] += rv0[i];
             } else {
@@ -644,6 +724,9 @@ __device__ __forceinline__ bool epilogue_all(bool ok) {
 
 constexpr int kMaxNormParts = 16;  // epilogue LayerNorm rows of at most 512 columns
 
+__device__ __forceinline__ void st_release_gpu(unsigned* p, unsigned v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
     unsigned v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -757,7 +840,7 @@ __device__ bool norm_tile(const Params& p, const CUtensorMap* tmn, const float* 
 // CTAs' copies count on them); the MMA's completions arrive on both CTAs'
 // barriers; the epilogues of both free an accumulator on the even CTA's
 // barrier. No copy is multicast.
-template <int BN, int KC, int EPI, bool kPair>
+template <int BN, int KC, int EPI, bool kPair, bool kSk>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_persistent(const __grid_constant__ CUtensorMap tm_a,
                     const __grid_constant__ CUtensorMap tm_b,
@@ -787,16 +870,68 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int unit = kPair ? static_cast<int>(blockIdx.x) / 2 : static_cast<int>(blockIdx.x);
     const int units = kPair ? static_cast<int>(gridDim.x) / 2 : static_cast<int>(gridDim.x);
     const bool leader = rank == 0;
-    const int total = p.m_tiles * (p.N / BN);
-    const int mine = unit < total ? (total - unit + units - 1) / units : 0;
-    auto tile_m0 = [&](int j) {  // this CTA's first row of tile j
-        const int t = unit + j * units;
+    const int total = p.m_tiles * (p.N / BN);  // tiles of this launch
+    // The CTA's segments: stage ranges [s0, s1) of a tile, each accumulated
+    // from zero. Without stream-K: tiles unit, unit + units, ... whole. With
+    // it (S = p.sk_pieces > 1, one CTA per unit): the launch's total x S
+    // pieces (piece i of a tile: stages [i nk / S, (i + 1) nk / S)) dealt in
+    // contiguous ranges. The CTA holding a tile's last piece finishes the
+    // tile. A CTA takes its tiles from the last to the first and each tile's
+    // pieces in order, so a finishing piece comes after the CTA's own
+    // earlier pieces of that tile, and the pieces it waits for from other
+    // CTAs are the first work of lower-numbered CTAs, which the block
+    // scheduler starts no later than this one.
+    static_assert(!(kSk && kPair), "stream-K takes one CTA per tile");
+    const int S = !kSk || p.sk_pieces <= 1 ? 1 : p.sk_pieces;
+    int u0 = 0, u1 = 0, nseg;
+    if (S > 1) {
+        const long long U = static_cast<long long>(total) * S;
+        u0 = static_cast<int>(U * unit / units);
+        u1 = static_cast<int>(U * (unit + 1) / units);
+        nseg = u1 - u0;
+    } else {
+        nseg = unit < total ? (total - unit + units - 1) / units : 0;
+    }
+    struct Seg {
+        int t, piece, s0, s1;
+    };
+    auto seg = [&](int j) {
+        Seg q;
+        if (S > 1) {
+            int t = (u1 - 1) / S, rem = j;
+            for (;;) {
+                const int lo = u0 > t * S ? u0 : t * S;
+                const int hi = u1 < (t + 1) * S ? u1 : (t + 1) * S;
+                if (rem < hi - lo) {
+                    q.t = t;
+                    q.piece = lo + rem - t * S;
+                    break;
+                }
+                rem -= hi - lo;
+                --t;
+            }
+            q.s0 = q.piece * nk / S;
+            q.s1 = (q.piece + 1) * nk / S;
+        } else {
+            q.t = unit + j * units;
+            q.piece = 0;
+            q.s0 = 0;
+            q.s1 = nk;
+        }
+        return q;
+    };
+    auto count_stages = [&]() {
+        int n = 0;
+        for (int j = 0; j < nseg; ++j) {
+            const Seg q = seg(j);
+            n += q.s1 - q.s0;
+        }
+        return n;
+    };
+    auto tile_m0 = [&](int t) {  // this CTA's first row of tile t
         return (p.m_tile0 + t % p.m_tiles) * TM + rank * BM;
     };
-    auto tile_n0 = [&](int j) {
-        const int t = unit + j * units;
-        return (t / p.m_tiles) * BN;
-    };
+    auto tile_n0 = [&](int t) { return (t / p.m_tiles) * BN; };
     // the barrier the MMA waits on for stage s: the even CTA's
     auto full_bar = [&](int s) {
         const uint32_t b = smem_u32(&tail->full[s]);
@@ -859,19 +994,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             if constexpr (kPair) tma_load_3d_pair(dst, map, 0, y, z, bar);
             else tma_load_3d(dst, map, 0, y, z, bar);
         };
-        const int first = !p.weights_static ? 0 : STAGES < mine * nk ? STAGES : mine * nk;
-        for (int g = 0; g < first; ++g) {  // stages whose B is fetched up front
-            if (lane == 0 && leader) mbar_arrive_expect_tx(smem_u32(&tail->full[g]), kArm);
-            if (lane == 1)
-                load(smem_u32(sB(g)), &tm_b, tile_n0(g / nk) + b_off, (g % nk) * KC, full_bar(g));
+        const int total_g = count_stages();
+        const int first = !p.weights_static ? 0 : STAGES < total_g ? STAGES : total_g;
+        for (int j = 0, g = 0; j < nseg && g < first; ++j) {  // stages whose B is fetched up front
+            const Seg q = seg(j);
+            for (int kb = q.s0; kb < q.s1 && g < first; ++kb, ++g) {
+                if (lane == 0 && leader) mbar_arrive_expect_tx(smem_u32(&tail->full[g]), kArm);
+                if (lane == 1)
+                    load(smem_u32(sB(g)), &tm_b, tile_n0(q.t) + b_off, kb * KC, full_bar(g));
+            }
         }
         pdl_wait();
         if (lane == 0) trace_stamp(p.trace, 2);
         int g = 0;  // stages whose loads were started, over all tiles
         bool ok = true;
-        for (int j = 0; j < mine && ok; ++j) {
-            const int m0 = tile_m0(j), n0 = tile_n0(j);
-            for (int kb = 0; kb < nk; ++kb, ++g) {
+        for (int j = 0; j < nseg && ok; ++j) {
+            const Seg q = seg(j);
+            const int m0 = tile_m0(q.t), n0 = tile_n0(q.t);
+            for (int kb = q.s0; kb < q.s1; ++kb, ++g) {
                 const int s = g % STAGES;
                 bool r = true;
                 if (lane == 0 && g >= STAGES)
@@ -918,10 +1058,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             else mma_commit(bar);
         };
         const uint32_t idesc = idesc_f16(TM, BN, p.ab_fmt, p.ab_fmt, 0, 0);
-        const int total_g = mine * nk;
+        const int total_g = count_stages();
         int g = 0;
         bool ok = true;
-        for (int j = 0; j < mine && ok; ++j) {
+        for (int j = 0; j < nseg && ok; ++j) {
+            const Seg q = seg(j);
             const int b = j & 1, use = j >> 1;
             if (use > 0 && !wait_all(smem_u32(&tail->acc_empty[b]), (use - 1) & 1, 0x100 + j)) {
                 ok = false;
@@ -929,7 +1070,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tc_fence_after();
             const uint32_t acc = tmem + static_cast<uint32_t>(b) * kAccCols;
-            for (int kb = 0; kb < nk; ++kb, ++g) {
+            for (int kb = q.s0; kb < q.s1; ++kb, ++g) {
                 const int s = g % STAGES;
                 ok = wait_all(smem_u32(&tail->full[s]), (g / STAGES) & 1, g);  // the even CTA's own
                 if (!ok) break;
@@ -943,7 +1084,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int k = 0; k < BK / 16; ++k) {
                             const uint64_t da = desc_k(a + c * kTileA + 32 * k);
                             const uint64_t db = desc_k(bb + c * L::kTileB + 32 * k);
-                            const uint32_t acc_in = (kb > 0 || c > 0 || k > 0) ? 1u : 0u;
+                            const uint32_t acc_in = (kb > q.s0 || c > 0 || k > 0) ? 1u : 0u;
                             if constexpr (kPair) mma_ss_pair(acc, da, db, idesc, acc_in);
                             else mma_ss(acc, da, db, idesc, acc_in);
                         }
@@ -965,29 +1106,89 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp >= 2) {
         const int sub = warp & 3;
         const int row = sub * 32 + lane;
-        for (int j = 0; j < mine; ++j) {
+        constexpr size_t kSlot = static_cast<size_t>(BN / 32) * kSkChunk;  // floats per slot
+        for (int j = 0; j < nseg; ++j) {
+            const Seg q = seg(j);
             const int b = j & 1, use = j >> 1;
-            const int m0 = tile_m0(j), n0 = tile_n0(j);
+            const int m0 = tile_m0(q.t), n0 = tile_n0(q.t);
             const RowCtx rc = row_ctx(p, m0 + row);
             epilogue_all(true);  // the previous tile's staged vectors are no longer read
             if (!p.weights_static) pdl_wait();
             stage_vectors<BN>(p, tail, n0);
             epilogue_all(true);
             pdl_wait();  // the residual and the outputs belong to the previous kernels
+            const bool finish = q.piece == S - 1;  // this CTA finishes the tile
+            const size_t slot0 = static_cast<size_t>(q.t) * S;  // the tile's first slot
+            const float* parts = nullptr;
+            if (finish && S > 1) {
+                // the last piece finishes the tile: wait (bounded) until the
+                // earlier pieces are stored (before its own accumulator, so
+                // their first chunk loads beside the residual's), clear their
+                // flags for the next launch, and add them in piece order
+                bool fine = true;
+                if (threadIdx.x == 64) {
+                    const long long t0 = clock64();
+                    const long long limit = wait_limit(p.status);
+                    for (int i = 0; i < S - 1 && fine; ++i) {
+                        while (ld_acquire_gpu(p.sk_flag + slot0 + i) == 0u) {
+                            if (*abort || clock64() - t0 > limit) {
+                                if (!*abort)
+                                    record_status(p.status, ST_TIMEOUT_SOFTMAX, 0x400 + q.t);
+                                *abort = 1;
+                                fine = false;
+                                break;
+                            }
+                            __nanosleep(32);
+                        }
+                    }
+                }
+                if (!epilogue_all(fine)) break;
+                if (threadIdx.x == 64)
+                    for (int i = 0; i < S - 1; ++i) p.sk_flag[slot0 + i] = 0u;
+                parts = p.sk_part + kSlot * slot0 + sk_row_base(row);
+            }
             float rv0[32];
-            prefetch_residual(p, rc, n0, rv0);
+            if (finish) prefetch_residual(p, rc, n0, rv0);
             bool ok = mbar_wait(smem_u32(&tail->acc_full[b]), use & 1, abort, p.status,
                                 ST_TIMEOUT_SOFTMAX, 0x200 + j);
             if (j == 0 && threadIdx.x == 64) trace_stamp(p.trace, 5);
             if (!epilogue_all(ok)) break;
             tc_fence_after();
+            const uint32_t t_acc = tmem + static_cast<uint32_t>(b) * kAccCols +
+                                   (static_cast<uint32_t>(sub * 32) << 16);
+            if (!finish) {
+                // an earlier piece of a stream-K tile: its partial sums into its
+                // slot (a warp's stores of one column group contiguous), then
+                // its flag, once every row is stored
+                float* dst = p.sk_part + kSlot * (slot0 + q.piece) + sk_row_base(row);
+#pragma unroll 1
+                for (int c = 0; c < BN / 32; ++c) {
+                    uint32_t r[32];
+                    tmem_ld32(t_acc + c * 32, r);
+                    tmem_wait_ld();
+                    float4* d = reinterpret_cast<float4*>(dst + c * kSkChunk);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        __stcg(d + i * kSkGroup, make_float4(__uint_as_float(r[4 * i]),
+                                                  __uint_as_float(r[4 * i + 1]),
+                                                  __uint_as_float(r[4 * i + 2]),
+                                                  __uint_as_float(r[4 * i + 3])));
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&tail->acc_empty[b]));
+                epilogue_all(true);  // every row of the slot is stored
+                if (threadIdx.x == 64) {
+                    __threadfence();  // ... and published (cumulative over the barrier)
+                    st_release_gpu(p.sk_flag + slot0 + q.piece, 1u);
+                }
+                continue;
+            }
             float keep[32];
-            store_tile<BN, EPI>(p, tail,
-                           tmem + static_cast<uint32_t>(b) * kAccCols +
-                               (static_cast<uint32_t>(sub * 32) << 16),
-                           n0, rc, rv0, p.tma_store ? &tm_o : nullptr, epi + sub * kEpiBlock,
-                           m0 + sub * 32 + p.out_row_offset,
-                           p.norm_out != nullptr ? keep : nullptr);
+            store_tile<BN, EPI, kSk ? kMaxSkParts : 0>(
+                p, tail, t_acc, n0, rc, rv0, p.tma_store ? &tm_o : nullptr, epi + sub * kEpiBlock,
+                m0 + sub * 32 + p.out_row_offset, p.norm_out != nullptr ? keep : nullptr, parts,
+                S - 1, kSlot);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
@@ -1835,12 +2036,12 @@ int pair_clusters(K kern, size_t smem) {
     return n;
 }
 
-template <int BN, int KC, int EPI, bool kPair>
+template <int BN, int KC, int EPI, bool kPair, bool kSk>
 int prepare_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
                        const CUtensorMap& tn, const Params& p, Launch* out) {
     constexpr size_t smem = smem_bytes<kPair ? BN / 2 : BN, KC, true>();
     out->op = 2;
-    auto kern = gemm_persistent<BN, KC, EPI, kPair>;
+    auto kern = gemm_persistent<BN, KC, EPI, kPair, kSk>;
     BL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(smem)));
     const int tiles = p.m_tiles * (p.N / BN);
@@ -1854,7 +2055,9 @@ int prepare_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
                                     tn, p);
         };
     } else {
-        const dim3 grid(std::min(tiles, sm_count()));
+        // stream-K: one CTA per piece up to one per SM
+        const int work = p.sk_pieces > 1 ? tiles * p.sk_pieces : tiles;
+        const dim3 grid(std::min(work, sm_count()));
         out->run = [=](cudaStream_t s) {
             return launch_k(kern, grid, dim3(kThreads), smem, s, ta, tb, to, tn, p);
         };
@@ -1862,17 +2065,17 @@ int prepare_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
     return BL_OK;
 }
 
-template <int BN, int EPI, bool kPair>
+template <int BN, int EPI, bool kPair, bool kSk>
 int prepare_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
                        const CUtensorMap& tn, const Params& p, int kc, Launch* out) {
     // only the depths whose ring holds two stages are built
     constexpr int SB = kPair ? BN / 2 : BN;  // B rows a CTA holds
     if constexpr (Layout<SB, 4, true>::kStages >= 2)
-        if (kc == 4) return prepare_persistent<BN, 4, EPI, kPair>(ta, tb, to, tn, p, out);
+        if (kc == 4) return prepare_persistent<BN, 4, EPI, kPair, kSk>(ta, tb, to, tn, p, out);
     if constexpr (Layout<SB, 2, true>::kStages >= 2)
-        if (kc == 2) return prepare_persistent<BN, 2, EPI, kPair>(ta, tb, to, tn, p, out);
+        if (kc == 2) return prepare_persistent<BN, 2, EPI, kPair, kSk>(ta, tb, to, tn, p, out);
     if (kc != 1) return fail(BL_ERR_UNSUPPORTED, "gemm: no kernel for %d k-blocks per stage", kc);
-    return prepare_persistent<BN, 1, EPI, kPair>(ta, tb, to, tn, p, out);
+    return prepare_persistent<BN, 1, EPI, kPair, kSk>(ta, tb, to, tn, p, out);
 }
 
 template <int BN, int KC, int EPI>
@@ -1926,14 +2129,14 @@ int prepare_split2(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
     }
 }
 
-template <int BN, bool kPair = false>
+template <int BN, bool kPair = false, bool kSk = false>
 int prepare_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
                        const CUtensorMap& tn, const Params& p, int kc, Launch* out) {
     switch (epilogue_form(p)) {
-        case 0: return prepare_persistent<BN, 0, kPair>(ta, tb, to, tn, p, kc, out);
-        case 1: return prepare_persistent<BN, 1, kPair>(ta, tb, to, tn, p, kc, out);
-        case 2: return prepare_persistent<BN, 2, kPair>(ta, tb, to, tn, p, kc, out);
-        default: return prepare_persistent<BN, -1, kPair>(ta, tb, to, tn, p, kc, out);
+        case 0: return prepare_persistent<BN, 0, kPair, kSk>(ta, tb, to, tn, p, kc, out);
+        case 1: return prepare_persistent<BN, 1, kPair, kSk>(ta, tb, to, tn, p, kc, out);
+        case 2: return prepare_persistent<BN, 2, kPair, kSk>(ta, tb, to, tn, p, kc, out);
+        default: return prepare_persistent<BN, -1, kPair, kSk>(ta, tb, to, tn, p, kc, out);
     }
 }
 
@@ -1946,6 +2149,75 @@ int pick_kc(int bn, uint32_t k) {
         if (nk % kc == 0 && (kSmemLimit - 4096 - kEpiBytes) / stage >= 2) return kc;
     }
     return 1;
+}
+
+// Stream-K pieces per tile for `tiles` tiles (the whole launch's) of `nk`
+// stages of kc k-blocks, bn columns wide, on `sms` SMs: the count S (1 =
+// whole tiles) that minimises an estimate of the busiest CTA's time in SM
+// clocks: its pieces' stages (operand bytes at about 45 bytes per clock, as
+// for the tile width), one slot's partial sums stored or loaded per piece at
+// the same rate, and half of the finishing piece's S - 1 loads exposed. A
+// split must beat whole tiles by a tenth.
+int sk_pieces(long long tiles, int nk, int bn, int kc, int sms) {
+    const double stage = kc * (kTileA + bn * BK * 2.0) / 45.0;
+    const double slot = BM * bn * 4.0 / 45.0;
+    auto cost = [&](int S) {
+        const long long units = tiles * S;
+        const long long grid = std::min<long long>(units, sms);
+        const long long per = (units + grid - 1) / grid;
+        const long long piece = (nk + S - 1) / S;
+        return static_cast<double>(per * piece) * stage +
+               (S > 1 ? static_cast<double>(per) * slot + 0.5 * (S - 1) * slot : 0.0);
+    };
+    const double whole = cost(1);
+    int best = 1;
+    double best_cost = whole;
+    for (int S = 2; S <= std::min(nk, kMaxSkPieces); ++S)
+        if (cost(S) < best_cost) best = S, best_cost = cost(S);
+    return best_cost < 0.9 * whole ? best : 1;
+}
+
+// The workspace of a stream-K launch: a flag per (tile, piece) slot, padded
+// to 256 bytes, then the slots' partial sums (128 x bn f32 each).
+uint64_t sk_flag_bytes(long long slots) { return (4ull * slots + 255) / 256 * 256; }
+uint64_t sk_workspace_bytes(long long tiles, int pieces, int bn) {
+    const long long slots = tiles * pieces;
+    return sk_flag_bytes(slots) + 4ull * BM * bn * slots;
+}
+
+int pick_bn(const bl_gemm_args& g);
+
+// The form a launch takes when it can take stream-K: A by TMA into the
+// one-CTA persistent kernel, no LayerNorm, epilogue LayerNorm, statistics,
+// CTA pairs or K split. Returns the piece count from the whole launch's
+// shape (1: whole tiles) and the tile width and stage depth.
+int sk_form(const bl_gemm_args& g, int* bn_out, int* kc_out) {
+    if (g.stream_k != 2 || g.ln_x != nullptr || g.norm_out != nullptr || g.stats_out != nullptr ||
+        g.pair_tiles == 2 || g.k % BK != 0 || g.m == 0 || g.n == 0)
+        return 1;
+    const int bn = pick_bn(g);
+    if ((bn != 128 && bn != 256) || g.n % bn != 0) return 1;
+    const bool split_ok = g.n % 64 == 0 && (g.tile_n == 0 || g.tile_n == 64) && g.k / BK >= 4;
+    const bool ksplit =
+        g.split_k == 2 ||
+        (g.split_k == 0 && split_ok && g.k >= 1024 && g.n <= 512 &&
+         2ull * ((g.m + BM - 1) / BM) * (g.n / 64) <= static_cast<uint64_t>(sm_count()));
+    if (ksplit) return 1;
+    const int kc = pick_kc(bn, g.k);
+    const int nk = static_cast<int>(g.k / (BK * kc));
+    const long long tiles = static_cast<long long>((g.m + BM - 1) / BM) * (g.n / bn);
+    int pieces = sk_pieces(tiles, nk, bn, kc, sm_count());
+    if (pieces <= 1 && nk >= 2) pieces = 2;
+    *bn_out = bn;
+    *kc_out = kc;
+    return pieces;
+}
+
+uint64_t sk_bytes(const bl_gemm_args& g) {
+    int bn = 0, kc = 0;
+    const int pieces = sk_form(g, &bn, &kc);
+    if (pieces <= 1) return 0;
+    return sk_workspace_bytes(static_cast<long long>((g.m + BM - 1) / BM) * (g.n / bn), pieces, bn);
 }
 
 template <int BN>
@@ -2205,6 +2477,32 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
         bn = 64;
     }
     const int kc = ln ? 1 : ksplit ? pick_kc_split(bn, g.k) : pick_kc(pair ? bn / 2 : bn, g.k);
+    // Stream-K on request (sk_form: pieces from the whole launch's shape) on
+    // the persistent path
+    if (g.stream_k > 2) return fail(BL_ERR_INVALID, "gemm: stream_k %u (0, 1 or 2)", g.stream_k);
+    int pieces = 1;
+    const long long whole_tiles = static_cast<long long>((g.m + BM - 1) / BM) * (g.n / bn);
+    {
+        const bool sk_path = !ln && !norm && conv == nullptr && !pair && !ksplit && !staged &&
+                             g.a != nullptr && g.stats_out == nullptr;
+        int sbn = 0, skc = 0;
+        int want = sk_path ? sk_form(g, &sbn, &skc) : 1;
+        if (want > 1 && (sbn != bn || skc != kc)) want = 1;
+        if (g.stream_k == 2 && want <= 1)
+            return fail(BL_ERR_UNSUPPORTED,
+                        "gemm: stream-K takes A loaded by TMA into one CTA per 128- or "
+                        "256-column tile (no LayerNorm, statistics, CTA pairs, K split or "
+                        "convolution) and at least two stages of K");
+        if (want > 1) {
+            const uint64_t need = sk_workspace_bytes(whole_tiles, want, bn);
+            if (g.workspace == nullptr || g.workspace_bytes < need ||
+                (reinterpret_cast<uintptr_t>(g.workspace) & 15) != 0)
+                return fail(BL_ERR_INVALID,
+                            "gemm: stream-K needs a 16-byte aligned workspace of %llu bytes",
+                            (unsigned long long)need);
+            pieces = want;
+        }
+    }
     const uint64_t ldb = g.ldb ? g.ldb : g.k;
     if (conv != nullptr) {
         // the image as [pixels][channels] f32 rows, boxes of 32 channels x 128 pixels
@@ -2277,6 +2575,12 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
         return fail(BL_ERR_INVALID, "gemm: row part [%u, %u) is not whole 128-row tiles", row_begin, row_end);
     p.status = status_ptr();
     p.trace = reinterpret_cast<unsigned long long*>(g.trace);
+    if (pieces > 1) {
+        p.sk_pieces = pieces;
+        p.sk_flag = static_cast<unsigned*>(g.workspace);
+        p.sk_part = reinterpret_cast<float*>(static_cast<uint8_t*>(g.workspace) +
+                                             sk_flag_bytes(whole_tiles * pieces));
+    }
     if (conv != nullptr) {
         p.conv_w = static_cast<int>(conv->w);
         p.conv_pix = static_cast<int>(g.m);
@@ -2346,6 +2650,9 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
         if (kc == 2) return prepare_split2<64, 2>(ta, tb, to, p, out);
         return prepare_split2<64, 1>(ta, tb, to, p, out);
     }
+    if (pieces > 1)  // sk_form takes stream-K for 128- and 256-column tiles only
+        return bn == 256 ? prepare_persistent<256, false, true>(ta, tb, to, tn, p, kc, out)
+                         : prepare_persistent<128, false, true>(ta, tb, to, tn, p, kc, out);
     switch (bn) {
         case 32: return prepare_persistent<32>(ta, tb, to, tn, p, kc, out);
         case 64: return prepare_persistent<64>(ta, tb, to, tn, p, kc, out);
@@ -2363,6 +2670,10 @@ int prepare_gemm_rows(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_en
 }
 
 }  // namespace bl
+
+extern "C" size_t bl_gemm_workspace_bytes(const bl_gemm_args* args) {
+    return args == nullptr ? 0 : static_cast<size_t>(bl::gemm::sk_bytes(*args));
+}
 
 extern "C" size_t bl_gemm_norm_sync_bytes(const bl_gemm_args* args) {
     return args == nullptr ? 0 : static_cast<size_t>(bl::gemm::norm_sync_bytes(args->m, args->n));

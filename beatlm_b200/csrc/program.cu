@@ -325,7 +325,7 @@ void rebind(bl_attention_args& a, Rebind& r) { r(a.qkv), r(a.out), r(a.workspace
 void rebind(bl_gemm_args& g, Rebind& r) {
     r(g.a), r(g.b), r(g.ln_x), r(g.ln_gamma), r(g.ln_beta), r(g.bias), r(g.chan_scale);
     r(g.residual), r(g.out), r(g.stats_out), r(g.ln_stats), r(g.norm_out), r(g.norm_gamma);
-    r(g.norm_beta), r(g.norm_sync);
+    r(g.norm_beta), r(g.norm_sync), r(g.workspace);
 }
 void rebind(bl_layernorm_args& a, Rebind& r) { r(a.x), r(a.gamma), r(a.beta), r(a.out); }
 void rebind(bl_patchify_args& a, Rebind& r) { r(a.image), r(a.a), r(a.cls), r(a.pos), r(a.x); }

@@ -134,7 +134,8 @@ def attention(qkv, *, tokens: int, heads: int, head_dim: int = 64, batch: int = 
 def gemm_args(w, *, a=None, ln=None, bias=None, act=None, scale=None, chan_scale=None,
               residual=None, res_period=0, out, out_dtype=None, out_split=None, m=None,
               out_row_offset=0, out_group=(0, 0), tile_n=0, stats_out=None, ln_stats=None,
-              norm=None, norm_sync=None, weights_static=False, pair_tiles=0, split_k=0):
+              norm=None, norm_sync=None, weights_static=False, pair_tiles=0, split_k=0,
+              stream_k=0, workspace=None):
     """``stats_out``: a float32 ``[rows][parts][2]`` tensor the epilogue fills
     with per-slice (mean, M2) of each stored row (``parts`` = n / tile width).
     ``ln_stats``: such a tensor for ``ln``'s input, used instead of a pass
@@ -145,7 +146,11 @@ def gemm_args(w, *, a=None, ln=None, bias=None, act=None, scale=None, chan_scale
     the kernel launched just before on the stream (model weights), so the
     GEMM may fetch them while that kernel finishes. ``pair_tiles=2``: 256-row
     tiles over CTA pairs (``bl_gemm_args.pair_tiles``); ``split_k``: the K
-    split over a two-CTA cluster (0 automatic, 1 off, 2 on)."""
+    split over a two-CTA cluster (0 automatic, 1 off, 2 on). ``stream_k=2``:
+    tiles' k-stages cut into pieces dealt over the SMs (0 or 1: whole
+    tiles); ``workspace``: its zero-filled device tensor of at least
+    ``gemm_workspace_bytes(args)`` bytes, which each launch leaves
+    zero-filled."""
     import torch
     n, k = w.shape
     ab = {torch.float16: "f16", torch.bfloat16: "bf16"}[w.dtype]
@@ -165,7 +170,10 @@ def gemm_args(w, *, a=None, ln=None, bias=None, act=None, scale=None, chan_scale
                    out_row_offset=out_row_offset, out_group_rows=out_group[0],
                    out_group_gap=out_group[1], tile_n=tile_n,
                    weights_static=1 if weights_static else 0, pair_tiles=pair_tiles,
-                   split_k=split_k)
+                   split_k=split_k, stream_k=stream_k)
+    if workspace is not None:
+        g.workspace = workspace.data_ptr()
+        g.workspace_bytes = workspace.numel() * workspace.element_size()
     if out_split is not None:
         g.split_col, g.out_dtype_hi = out_split[0], _TD[out_split[1]]
     if ln is not None:
@@ -182,6 +190,12 @@ def gemm_args(w, *, a=None, ln=None, bias=None, act=None, scale=None, chan_scale
         g.norm_gamma, g.norm_beta, g.norm_eps = gamma.data_ptr(), beta.data_ptr(), eps
         g.norm_sync, g.norm_sync_bytes = norm_sync.data_ptr(), norm_sync.numel()
     return g
+
+
+def gemm_workspace_bytes(args) -> int:
+    """Bytes of workspace the stream-K form needs for these ``gemm_args``
+    (0 where the launch keeps whole tiles; ``bl_gemm_workspace_bytes``)."""
+    return int(N.lib().bl_gemm_workspace_bytes(ctypes.byref(args)))
 
 
 def gemm_norm_sync_bytes(m: int, n: int) -> int:

@@ -405,9 +405,33 @@ typedef struct bl_gemm_args {
      * CTAs of every 64-column tile fit one wave (a rule of the whole
      * launch's shape, so row parts compute as their whole launch). 1: off. */
     uint32_t split_k;
+    /* Stream-K: every tile's k-stages cut into S pieces that are dealt to
+     * the CTAs in contiguous ranges, so a launch with fewer tiles than SMs,
+     * or a short last wave, keeps every SM on its k-loop. Each piece is
+     * accumulated on its own; the CTA that computes a tile's last piece
+     * adds the others' f32 partial sums in piece order before its epilogue,
+     * so the bits depend on the shape alone (S comes from the whole
+     * launch's m, n and k: row parts compute as their whole launch). The
+     * partials and their flags live in `workspace`: a zero-filled device
+     * buffer of at least bl_gemm_workspace_bytes() bytes, 16-byte aligned,
+     * that each launch leaves zero-filled again (one launch at a time per
+     * buffer). For A given as `a`, one CTA per 128- or 256-column tile, no
+     * LayerNorm, epilogue LayerNorm, statistics, K split or convolution; two
+     * or three pieces, by an estimate of the busiest CTA's time. 2: on; 0 or
+     * 1: whole tiles. Not automatic: at the ViT-L fc2 shape (88 tiles of
+     * 4096-deep K) it measured no faster than whole tiles, the full grid's
+     * operand reads meeting the L2's delivery rate. */
+    uint32_t stream_k;
+    void* workspace;
+    uint64_t workspace_bytes;
 } bl_gemm_args;
 
 int bl_gemm(const bl_gemm_args* args, void* stream);
+
+/* Bytes of workspace that bl_gemm's stream-K form needs for these arguments
+ * (0 where the launch does not take it: stream_k other than 2, or a form it
+ * does not apply to). */
+size_t bl_gemm_workspace_bytes(const bl_gemm_args* args);
 
 /* Bytes of norm_sync that bl_gemm needs for these arguments (m and n). */
 size_t bl_gemm_norm_sync_bytes(const bl_gemm_args* args);

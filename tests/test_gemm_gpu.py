@@ -451,3 +451,147 @@ def test_k_split_rejects_what_it_cannot_take():
         g = ops.gemm_args(w, a=a, out=out, **bad)
         with pytest.raises(bl.BackendError, match=match):
             bl.ops.N.check(bl.ops.N.lib().bl_gemm(ctypes.byref(g), None))
+
+
+def _sk_case(m, n, k, form, seed, tile_n=0):
+    """Operands, host expectation and a kwargs builder for a stream-K case."""
+    import torch
+    dtype = "bf16"
+    a = _rnd(oracle.normal(13 * m + k + seed, m * k), dtype)
+    w = _rnd(oracle.uniform(k + 9 + seed, k * n, -1 / math.sqrt(k), 1 / math.sqrt(k)), dtype)
+    b = oracle.uniform(n + 10 + seed, n, -0.1, 0.1)
+    wd, ad, bd = _dev(w.reshape(k, n).T, dtype), _dev(a.reshape(m, k), dtype), _dev(b, "f32")
+    x0 = oracle.uniform(n + 11 + seed, m * n, -1.0, 1.0).reshape(m, n)
+    ls = oracle.uniform(n + 12 + seed, n, 0.1, 1.0)
+
+    def kwargs():
+        kw = dict(a=ad, bias=bd, weights_static=True, split_k=1, tile_n=tile_n)
+        if form == "residual":
+            x = _dev(x0, "f32")
+            kw.update(chan_scale=_dev(ls, "f32"), residual=x, out=x)
+        elif form == "gelu":
+            kw.update(act="gelu_erf", out=torch.zeros((m, n), dtype=torch.float32, device="cuda"))
+        elif form == "generic":
+            kw.update(scale=0.25, out=torch.zeros((m, n), dtype=torch.float32, device="cuda"))
+        else:
+            kw.update(out=torch.zeros((m, n), dtype=torch.float32, device="cuda"))
+        return kw
+
+    want = oracle.matmul(a, w, b, m, k, n)
+    if form == "residual":
+        want = x0.ravel() + want * np.tile(ls, m)
+    elif form == "gelu":
+        want = oracle.gelu_erf(want)
+    elif form == "generic":
+        want = 0.25 * want
+    return wd, kwargs, want
+
+
+def _sk_flag_bytes(m, n, args):
+    """The flag area at the head of a stream-K workspace: one word per
+    (tile, piece) slot padded to 256 bytes; tiles and pieces follow from the
+    workspace size, whose rest is 128 x bn f32 per slot."""
+    from beatlm_b200 import ops
+    total = ops.gemm_workspace_bytes(args)
+    for bn in (128, 256):
+        for pieces in (2, 3):
+            slots = ((m + 127) // 128) * (n // bn) * pieces
+            flags = (4 * slots + 255) // 256 * 256
+            if n % bn == 0 and flags + 4 * 128 * bn * slots == total:
+                return flags
+    raise AssertionError("no (tile width, pieces) gives %d bytes" % total)
+
+
+@pytest.mark.parametrize("m,n,k,form,tile", [
+    (1370, 1024, 4096, "residual", 0),  # ViT-L fc2 (128-column tiles, three pieces)
+    (300, 1024, 2048, "generic", 128),  # ragged last row tile
+    (129, 256, 1024, "gelu", 256),      # 256-column tiles, one row past a tile
+    (384, 512, 2048, "bias", 128),
+])
+def test_stream_k_meets_the_oracle(m, n, k, form, tile):
+    """Stream-K (stream_k 2): every tile's k-stages cut into pieces dealt
+    over the SMs, each accumulated on its own and added in piece order by the
+    CTA holding the last piece. Within the reference's GEMM tolerance of the
+    oracle, close to whole tiles (a few partial sums instead of one chain),
+    the same bits on a second launch through the same workspace, whose flags
+    the launches leave at zero."""
+    import torch
+    import beatlm_b200 as bl
+    from beatlm_b200 import ops
+    mode = 2
+    wd, kwargs, want = _sk_case(m, n, k, form, 0, tile)
+    whole_kw = kwargs()
+    g = ops.gemm_args(wd, stream_k=1, **whole_kw)
+    bl.ops.N.check(bl.ops.N.lib().bl_gemm(ctypes.byref(g), None))
+    probe_kw = kwargs()
+    probe = ops.gemm_args(wd, stream_k=mode, **probe_kw)
+    nbytes = ops.gemm_workspace_bytes(probe)
+    assert nbytes > 0, "stream-K not taken"
+    flags = _sk_flag_bytes(m, n, probe)
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    outs = []
+    for _ in range(2):
+        kw = kwargs()
+        g = ops.gemm_args(wd, stream_k=mode, workspace=ws, **kw)
+        bl.ops.N.check(bl.ops.N.lib().bl_gemm(ctypes.byref(g), None))
+        torch.cuda.synchronize()
+        _check_status()
+        assert int(ws[:flags].count_nonzero()) == 0, "flags left set"
+        outs.append(kw["out"].float().cpu().numpy())
+    torch.cuda.synchronize()
+    whole = whole_kw["out"].float().cpu().numpy()
+    _close(outs[0], want, "stream-K %s" % form)
+    assert np.array_equal(outs[0], outs[1])
+    assert _rel(outs[0], whole) < 1e-5
+
+
+def test_stream_k_row_parts_compute_as_the_whole_launch():
+    """The pieces come from the whole launch's shape, so a program that
+    splits the GEMM into row parts (each a launch of its own) gives the same
+    bits as the unsplit launch."""
+    import torch
+    from beatlm_b200 import ops
+    from beatlm_b200.runtime import Kernels, Spec
+    m, n, k = 1370, 1024, 4096
+    wd, kwargs, _ = _sk_case(m, n, k, "residual", 3)
+    res = []
+    for parts in (1, 3, 5):
+        kw = kwargs()
+        probe = ops.gemm_args(wd, stream_k=2, **kw)
+        ws = torch.zeros(ops.gemm_workspace_bytes(probe), dtype=torch.uint8, device="cuda")
+        assert ws.numel() > 0
+        prog = Kernels([Spec(ops.gemm_args(wd, stream_k=2, workspace=ws, **kw), "fc2", parts)])
+        prog.encode_all(None)
+        torch.cuda.synchronize()
+        _check_status()
+        res.append(kw["out"].cpu())
+        prog.close()
+    assert torch.equal(res[0], res[1]) and torch.equal(res[0], res[2])
+
+
+def test_stream_k_workspace_query_and_rejects():
+    import torch
+    import beatlm_b200 as bl
+    from beatlm_b200 import ops
+
+    def args(m, n, k, **kw):
+        w = torch.zeros((n, k), dtype=torch.bfloat16, device="cuda")
+        a = torch.zeros((m, k), dtype=torch.bfloat16, device="cuda")
+        out = torch.zeros((m, n), dtype=torch.float32, device="cuda")
+        return ops.gemm_args(w, a=a, out=out, **kw), (w, a, out)
+
+    # only on request: 0 and 1 keep whole tiles and need no workspace
+    for mode in (0, 1):
+        g, keep = args(1370, 1024, 4096, stream_k=mode)
+        assert ops.gemm_workspace_bytes(g) == 0
+    # ViT-L fc2: 88 tiles of 32 stages in three pieces, a 128 x 128 slot each
+    g, keep = args(1370, 1024, 4096, stream_k=2)
+    slots = 88 * 3
+    assert ops.gemm_workspace_bytes(g) == (4 * slots + 255) // 256 * 256 + slots * 128 * 128 * 4
+    for bad, match in ((dict(stream_k=3), "stream_k"),
+                       (dict(stream_k=2), "workspace"),
+                       (dict(stream_k=2, tile_n=32), "stream-K takes"),
+                       (dict(stream_k=2, split_k=2), "stream-K takes")):
+        g, keep = args(1370, 1024, 4096, **bad)
+        with pytest.raises(bl.BackendError, match=match):
+            bl.ops.N.check(bl.ops.N.lib().bl_gemm(ctypes.byref(g), None))
