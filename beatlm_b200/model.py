@@ -739,18 +739,21 @@ class Encoder:
             self.program(frames, layers).encode_all(None)
         return self.features(frames, layers)
 
-    def capture_host(self, frames: int, host_image, host_features: list, stream=None):
+    def capture_host(self, frames: int, host_image, host_features: list, stream=None,
+                     slot: int = 0):
         """One CUDA graph of a whole host-to-host pass over `frames` frames:
-        the pinned ``host_image`` (f32 NHWC) copied in, the encoder program,
-        and each feature map copied out to its pinned ``host_features[j]`` on
-        a second stream as soon as its LayerNorm has run, so the copies of
-        the early features overlap the later blocks. Returns the
-        ``torch.cuda.CUDAGraph``; ``replay()`` on a stream runs one pass."""
+        the pinned ``host_image`` (f32 NHWC) copied in (None: the slot's image
+        is already on the device), the encoder program over slot ``slot``
+        (its binding set), and each feature map copied out to its pinned
+        ``host_features[j]`` on a second stream as soon as its LayerNorm has
+        run, so the copies of the early features overlap the later blocks.
+        Returns the ``torch.cuda.CUDAGraph``; ``replay()`` on a stream runs
+        one pass."""
         import torch
         prog = self.program(frames)
         buf = self.buffers(frames)
         cuts = [i + 1 for i in range(len(prog)) if prog.label(i).startswith("features.")]
-        feats = self.features(frames)
+        feats = self.features(frames, slot=slot)
         if len(host_features) != len(feats):
             raise ValueError("%d host feature buffers for %d feature maps"
                              % (len(host_features), len(feats)))
@@ -758,10 +761,11 @@ class Encoder:
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
             s = torch.cuda.current_stream()
-            buf.image.copy_(host_image, non_blocking=True)
+            if host_image is not None:
+                buf.images[slot].copy_(host_image, non_blocking=True)
             begin = 0
             for j, end in enumerate(cuts):
-                prog.encode_all(s, begin=begin, end=end)
+                prog.encode_all(s, begin=begin, end=end, set=slot)
                 ready = torch.cuda.Event()
                 ready.record(s)
                 side.wait_event(ready)
@@ -769,9 +773,16 @@ class Encoder:
                     host_features[j].copy_(feats[j], non_blocking=True)
                 begin = end
             if begin < len(prog):
-                prog.encode_all(s, begin=begin)
+                prog.encode_all(s, begin=begin, set=slot)
             s.wait_stream(side)
         return g
+
+    def host_pipeline(self, frames: int, host_images: list, host_features: list):
+        """Frames host to host with each frame's image copy overlapping the
+        previous frame's pass (``HostPipeline``): needs ``slots >= 2``;
+        ``host_images[s]`` (pinned f32 NHWC) and ``host_features[s]`` (pinned,
+        one per feature map) are slot s's host buffers."""
+        return HostPipeline(self, frames, host_images, host_features)
 
     def launches_per_frame_batch(self, layers: int | None = None, frames: int = 1) -> int:
         """Kernels launched per pass: the program's specs, with the patch
@@ -779,6 +790,68 @@ class Encoder:
         from .graph import PatchEmbed
         prog, _, _ = self.lowered(frames, layers)
         return sum(3 if isinstance(k.main, PatchEmbed) else 1 for k in prog.kernels)
+
+
+class HostPipeline:
+    """Frames from pinned host memory to pinned host memory over two input/
+    output slots (the reference keeps jobs in flight through its Net slots,
+    crates/beatlm-host/src/slots.rs:1-60): frame k runs in slot k % 2 as one
+    ``Encoder.capture_host`` graph of that slot (the encoder, each feature map
+    copied out right after its LayerNorm), and at the start of frame k the
+    image of frame k + 1 is copied into the other slot on a stream of its own
+    once frame k - 1, which read that slot, has finished. Frame k + 1 waits
+    for that copy. So a frame's image copy overlaps the previous frame's pass
+    and leaves the critical path; its feature copies stay inside its own
+    pass. ``step(stream, fill)`` runs the next frame on ``stream``;
+    ``fill(slot)`` (optional) writes the next frame's pixels into
+    ``host_images[slot]`` before its copy is issued, after the previous copy
+    from that buffer has completed."""
+
+    def __init__(self, enc: "Encoder", frames: int, host_images: list, host_features: list):
+        import torch
+        if enc.slots < 2:
+            raise ValueError("a host pipeline needs an encoder with two slots (slots=2)")
+        if len(host_images) < 2 or len(host_features) < 2:
+            raise ValueError("host buffers for two slots")
+        self.enc, self.frames = enc, frames
+        self.host_images, self.host_features = host_images, host_features
+        self.images = enc.buffers(frames).images
+        self.copy_in = torch.cuda.Stream()
+        self.graphs = {}
+        self.ev_in = [torch.cuda.Event() for _ in range(2)]   # slot's image landed
+        self.ev_done = [torch.cuda.Event() for _ in range(2)]  # slot's last pass ended
+        self.used = [False, False]
+        self.k = 0
+        self._primed = False
+
+    def _copy_in(self, slot, fill):
+        import torch
+        if fill is not None:
+            self.ev_in[slot].synchronize()  # the previous copy from that buffer is done
+            fill(slot)
+        if self.used[slot]:
+            self.copy_in.wait_event(self.ev_done[slot])
+        with torch.cuda.stream(self.copy_in):
+            self.images[slot].copy_(self.host_images[slot], non_blocking=True)
+        self.ev_in[slot].record(self.copy_in)
+
+    def step(self, stream, fill=None):
+        import torch
+        s = self.k % 2
+        if s not in self.graphs:
+            self.graphs[s] = self.enc.capture_host(self.frames, None, self.host_features[s],
+                                                   stream, slot=s)
+        if not self._primed:
+            self._copy_in(s, fill)
+            self._primed = True
+        self._copy_in(1 - s, fill)  # the next frame's image, beside this pass
+        stream.wait_event(self.ev_in[s])
+        with torch.cuda.stream(stream):
+            self.graphs[s].replay()
+        self.ev_done[s].record(stream)
+        self.used[s] = True
+        self.k += 1
+        return s
 
 
 # ------------------------------------------------------------------ DPT head

@@ -380,3 +380,48 @@ def test_jobs_in_flight_keep_their_own_input_and_output_slots():
     for j, f in got.items():
         assert torch.equal(f, want[j]), j
     assert bl.status(reset=True).code == 0
+
+
+def test_host_pipeline_frames_equal_direct_passes():
+    """Encoder.host_pipeline: frames from pinned host memory to pinned host
+    memory over two slots, each frame's image copied in beside the previous
+    frame's pass and its feature maps copied out inside its own. Six frames,
+    each a different image written by the fill callback: every frame's host
+    features equal a direct pass over its image, bit for bit, and nothing
+    records a device error."""
+    import torch
+    import beatlm_b200 as bl
+    from beatlm_b200.model import Encoder, ViTConfig, block_weights_normal
+    cfg = ViTConfig.small(layers=2, out_indices=(1, 2))
+    rng = np.random.default_rng(23)
+    n = lambda *s: rng.standard_normal(int(np.prod(s)), dtype=np.float32) * 0.02
+    w = {"blocks": [block_weights_normal(rng, cfg.dim, cfg.mlp) for _ in range(2)],
+         "patch_w": n(cfg.patch, cfg.patch, cfg.cin, cfg.dim), "patch_b": n(cfg.dim),
+         "cls": n(cfg.dim), "pos": n(cfg.tokens, cfg.dim),
+         "norm_g": np.ones(cfg.dim, np.float32), "norm_b": np.zeros(cfg.dim, np.float32)}
+    enc = Encoder(cfg, w, "bf16", planned_frames=1, slots=2)
+    images = [rng.random((1, cfg.side, cfg.side, cfg.cin), dtype=np.float32) for _ in range(6)]
+    want = [[f.cpu().clone() for f in enc.forward(torch.from_numpy(img).cuda(), frames=1)]
+            for img in images]
+    torch.cuda.synchronize()
+    hosts = [torch.empty((1, cfg.side, cfg.side, cfg.cin)).pin_memory() for _ in range(2)]
+    feats = [[torch.empty(f.shape, dtype=f.dtype).pin_memory() for f in enc.features(1)]
+             for _ in range(2)]
+    pipe = enc.host_pipeline(1, hosts, feats)
+    fed = [0]
+
+    def fill(slot):  # the next frame's pixels into that slot's host buffer
+        if fed[0] < len(images):
+            hosts[slot].copy_(torch.from_numpy(images[fed[0]]))
+        fed[0] += 1
+
+    stream = torch.cuda.Stream()
+    got = []
+    for k in range(len(images)):
+        slot = pipe.step(stream, fill)
+        stream.synchronize()
+        got.append([f.clone() for f in feats[slot]])
+    assert bl.status(reset=True).code == 0
+    for k in range(len(images)):
+        for g, w_ in zip(got[k], want[k]):
+            assert torch.equal(g, w_), k
