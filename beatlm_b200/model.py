@@ -797,60 +797,36 @@ class HostPipeline:
     output slots (the reference keeps jobs in flight through its Net slots,
     crates/beatlm-host/src/slots.rs:1-60): frame k runs in slot k % 2 as one
     ``Encoder.capture_host`` graph of that slot (the encoder, each feature map
-    copied out right after its LayerNorm), and at the start of frame k the
-    image of frame k + 1 is copied into the other slot on a stream of its own
-    once frame k - 1, which read that slot, has finished. Frame k + 1 waits
-    for that copy. So a frame's image copy overlaps the previous frame's pass
-    and leaves the critical path; its feature copies stay inside its own
-    pass. ``step(stream, fill)`` runs the next frame on ``stream``;
-    ``fill(slot)`` (optional) writes the next frame's pixels into
-    ``host_images[slot]`` before its copy is issued, after the previous copy
-    from that buffer has completed."""
+    copied out right after its LayerNorm), and its image reaches that slot's
+    device buffer through ``runtime.InputPipeline``: copied at the start of
+    frame k - 1, beside that frame's pass, once frame k - 2 (which read the
+    slot) has finished. So a frame's image copy leaves the critical path; its
+    feature copies stay inside its own pass. ``step(stream, fill)`` runs the
+    next frame on ``stream`` and returns its slot; ``fill(slot)`` (optional)
+    writes the next frame's pixels into ``host_images[slot]`` before its copy
+    is issued."""
 
     def __init__(self, enc: "Encoder", frames: int, host_images: list, host_features: list):
-        import torch
+        from .runtime import InputPipeline
         if enc.slots < 2:
             raise ValueError("a host pipeline needs an encoder with two slots (slots=2)")
         if len(host_images) < 2 or len(host_features) < 2:
             raise ValueError("host buffers for two slots")
         self.enc, self.frames = enc, frames
-        self.host_images, self.host_features = host_images, host_features
-        self.images = enc.buffers(frames).images
-        self.copy_in = torch.cuda.Stream()
+        self.host_features = host_features
+        self.inputs = InputPipeline(list(host_images[:2]), enc.buffers(frames).images[:2])
         self.graphs = {}
-        self.ev_in = [torch.cuda.Event() for _ in range(2)]   # slot's image landed
-        self.ev_done = [torch.cuda.Event() for _ in range(2)]  # slot's last pass ended
-        self.used = [False, False]
-        self.k = 0
-        self._primed = False
-
-    def _copy_in(self, slot, fill):
-        import torch
-        if fill is not None:
-            self.ev_in[slot].synchronize()  # the previous copy from that buffer is done
-            fill(slot)
-        if self.used[slot]:
-            self.copy_in.wait_event(self.ev_done[slot])
-        with torch.cuda.stream(self.copy_in):
-            self.images[slot].copy_(self.host_images[slot], non_blocking=True)
-        self.ev_in[slot].record(self.copy_in)
 
     def step(self, stream, fill=None):
         import torch
-        s = self.k % 2
+        s = self.inputs.slot()
         if s not in self.graphs:
             self.graphs[s] = self.enc.capture_host(self.frames, None, self.host_features[s],
                                                    stream, slot=s)
-        if not self._primed:
-            self._copy_in(s, fill)
-            self._primed = True
-        self._copy_in(1 - s, fill)  # the next frame's image, beside this pass
-        stream.wait_event(self.ev_in[s])
+        self.inputs.acquire(stream, fill)
         with torch.cuda.stream(stream):
             self.graphs[s].replay()
-        self.ev_done[s].record(stream)
-        self.used[s] = True
-        self.k += 1
+        self.inputs.release(stream)
         return s
 
 

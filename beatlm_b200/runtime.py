@@ -254,3 +254,59 @@ class SliceTimer:
             self.close()
         except Exception:
             pass
+
+
+class InputPipeline:
+    """Host-to-device copies of one input a step ahead, over two device
+    buffers (input slots, as the reference's Net keeps jobs in flight,
+    crates/beatlm-host/src/slots.rs:1-60). ``acquire(stream)`` returns this
+    step's device buffer, whose copy was issued a step earlier beside the
+    previous step's work (``stream`` waits for it), and issues the copy of
+    the next step's input into the other buffer on a copy stream of its own,
+    once the step that last read that buffer has ended. ``release(stream)``
+    marks the end of this step's reads (on ``stream``, after its work).
+    ``hosts[i]`` (pinned) is copied into ``devices[i]``; ``fill(i)``, when
+    given, writes the next input into ``hosts[i]`` first, after the previous
+    copy from it has completed."""
+
+    def __init__(self, hosts: list, devices: list):
+        import torch
+        if len(hosts) != 2 or len(devices) != 2:
+            raise ValueError("an input pipeline has two host and two device buffers")
+        self.hosts, self.devices = hosts, devices
+        self.copy = torch.cuda.Stream()
+        self._in = [torch.cuda.Event() for _ in range(2)]    # the buffer's copy landed
+        self._done = [torch.cuda.Event() for _ in range(2)]  # its last reader ended
+        self._used = [False, False]
+        self._primed = False
+        self.k = 0
+
+    def _issue(self, i, fill):
+        import torch
+        if fill is not None:
+            self._in[i].synchronize()
+            fill(i)
+        if self._used[i]:
+            self.copy.wait_event(self._done[i])
+        with torch.cuda.stream(self.copy):
+            self.devices[i].copy_(self.hosts[i], non_blocking=True)
+        self._in[i].record(self.copy)
+
+    def slot(self) -> int:
+        """This step's buffer index."""
+        return self.k % 2
+
+    def acquire(self, stream, fill=None):
+        i = self.slot()
+        if not self._primed:
+            self._issue(i, fill)
+            self._primed = True
+        self._issue(1 - i, fill)  # the next step's input, beside this step
+        stream.wait_event(self._in[i])
+        return self.devices[i]
+
+    def release(self, stream):
+        i = self.slot()
+        self._done[i].record(stream)
+        self._used[i] = True
+        self.k += 1
