@@ -329,11 +329,51 @@ class EncoderWorkload:
         from beatlm_b200.model import ViTConfig
         return ViTConfig.large() if cls.large else ViTConfig.small()
 
+    def attention_marginal_us(self, stream, frames: int = 30):
+        """What one attention launch costs inside the graphed frame: the frame
+        graph against the same graph without its attention launches (their
+        outputs then stale), each timed with CUDA events over `frames` frames,
+        interleaved, L2 flushed before each; the median difference over the
+        frame's attention launches."""
+        import numpy as np
+        import torch
+        from beatlm_b200.runtime import Kernels
+        specs = self.enc.specs(self.frames)
+        keep = [sp for sp in specs if not sp.label.endswith(".attention")]
+        cut = len(specs) - len(keep)
+        if cut == 0:
+            return None
+        without = Kernels(keep)
+        graphs = [self.prog.capture(stream), without.capture(stream)]
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+        times = [[], []]
+        with torch.cuda.stream(stream):
+            for rep in range(frames + 3):
+                for i, g in enumerate(graphs):
+                    flush.zero_()
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                    g.launch(stream)
+                    e1.record(stream)
+                    e1.synchronize()
+                    if rep >= 3:
+                        times[i].append(e0.elapsed_time(e1) * 1e3)
+        without.close()
+        return (float(np.median(times[0])) - float(np.median(times[1]))) / cut
+
     def roofline(self, stream, avg_ms):
         prof = self.slice_profile(stream)
         n, tot, avg_us = prof["attention"]
         steps = n / self.cfg.layers
+        marginal = self.attention_marginal_us(stream)
         return {"achieved_tflops": self.attn_flops / (avg_us / 1e6) / 1e12,
+                "in_frame": None if marginal is None else {
+                    "us_per_launch": round(marginal, 2),
+                    "tflops": round(self.attn_flops / (marginal / 1e6) / 1e12, 2),
+                    "how": "the frame's CUDA graph against the same graph without its attention "
+                           "launches, CUDA events, L2 flushed before each frame, medians over 30 "
+                           "frames each; the difference over the launches left out"},
                 "kernel": "bl::attn::attention_fwd (%d launches per frame)" % self.cfg.layers,
                 "how": "cudaEvent slice timer (bl_timer) around every kernel of 5 direct "
                        "(non-graph) encodes after the timed region, each queued behind a "
@@ -597,8 +637,21 @@ class BlockWorkload:
             self.graph = self.prog.capture(stream)
         self.graph.launch(stream)
 
+    e2e_how = ("each step: the block's input rows, whose host-to-device copy was issued beside "
+               "the previous step's block into one of two staging buffers "
+               "(runtime.InputPipeline), copied into the residual stream on the device, the "
+               "block's graph, its output copied to pinned host memory inside the step; L2 "
+               "flushed between steps")
+
     def step_e2e(self, stream):
-        self.buf.x.copy_(self.host, non_blocking=True)
+        import torch
+        from beatlm_b200.runtime import InputPipeline
+        if getattr(self, "inputs", None) is None:
+            self.inputs = InputPipeline([self.host, self.host],
+                                        [torch.empty_like(self.buf.x), torch.empty_like(self.buf.x)])
+        staged = self.inputs.acquire(stream)
+        self.buf.x.copy_(staged, non_blocking=True)
+        self.inputs.release(stream)
         self.step(stream)
         self.out_host.copy_(self.buf.x, non_blocking=True)
 
