@@ -739,43 +739,76 @@ class Encoder:
             self.program(frames, layers).encode_all(None)
         return self.features(frames, layers)
 
-    def capture_host(self, frames: int, host_image, host_features: list, stream=None,
-                     slot: int = 0):
-        """One CUDA graph of a whole host-to-host pass over `frames` frames:
-        the pinned ``host_image`` (f32 NHWC) copied in (None: the slot's image
-        is already on the device), the encoder program over slot ``slot``
-        (its binding set), and each feature map copied out to its pinned
-        ``host_features[j]`` on a second stream as soon as its LayerNorm has
-        run, so the copies of the early features overlap the later blocks.
-        Returns the ``torch.cuda.CUDAGraph``; ``replay()`` on a stream runs
+    def capture(self, frames: int, stream, slot: int = 0, host_features: list | None = None,
+                host_image=None):
+        """One CUDA graph of the encoder over `frames` frames in slot ``slot``
+        (its binding set), with each feature-map LayerNorm on a second stream:
+        it forks after the block whose output it reads and joins before the
+        next kernel that writes the residual stream (the next block's
+        out-projection), so it leaves the chain of dependent launches. With
+        ``host_features`` each map is also copied out to its pinned buffer on
+        that stream right after its LayerNorm; with ``host_image`` the pinned
+        image is first copied into the slot. Returns the
+        ``torch.cuda.CUDAGraph``; ``replay()`` on the current stream runs
         one pass."""
         import torch
         prog = self.program(frames)
         buf = self.buffers(frames)
-        cuts = [i + 1 for i in range(len(prog)) if prog.label(i).startswith("features.")]
+        n = len(prog)
+        base = [prog.label(i).split(" ")[0] for i in range(n)]
         feats = self.features(frames, slot=slot)
-        if len(host_features) != len(feats):
+        fidx = [i for i in range(n) if base[i].startswith("features.")]
+        if host_features is not None and len(host_features) != len(feats):
             raise ValueError("%d host feature buffers for %d feature maps"
                              % (len(host_features), len(feats)))
+        # the residual stream's next writer after each feature LayerNorm
+        writes_x = [i for i in range(n) if base[i].endswith(".proj") or base[i].endswith(".fc2")
+                    or base[i] == "embed.patch"]
+        joins = {}
+        for j, f in enumerate(fidx):
+            nxt = [i for i in writes_x if i > f]
+            joins.setdefault(nxt[0] if nxt else n, []).append(j)
         side = torch.cuda.Stream()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
             s = torch.cuda.current_stream()
             if host_image is not None:
                 buf.images[slot].copy_(host_image, non_blocking=True)
+            done = {}
             begin = 0
-            for j, end in enumerate(cuts):
-                prog.encode_all(s, begin=begin, end=end, set=slot)
-                ready = torch.cuda.Event()
-                ready.record(s)
-                side.wait_event(ready)
-                with torch.cuda.stream(side):
-                    host_features[j].copy_(feats[j], non_blocking=True)
-                begin = end
-            if begin < len(prog):
-                prog.encode_all(s, begin=begin, set=slot)
+            for i in range(n + 1):
+                if i in joins or i in fidx or i == n:
+                    if begin < i:
+                        prog.encode_all(s, begin=begin, end=i, set=slot)
+                    begin = i
+                for j in joins.get(i, []):
+                    s.wait_event(done[j])
+                if i < n and i in fidx:
+                    j = fidx.index(i)
+                    fork = torch.cuda.Event()
+                    fork.record(s)
+                    side.wait_event(fork)
+                    prog.encode(i, side, set=slot)
+                    # the join waits for the LayerNorm, not for its copy out
+                    done[j] = torch.cuda.Event()
+                    done[j].record(side)
+                    if host_features is not None:
+                        with torch.cuda.stream(side):
+                            host_features[j].copy_(feats[j], non_blocking=True)
+                    begin = i + 1
             s.wait_stream(side)
         return g
+
+    def capture_host(self, frames: int, host_image, host_features: list, stream=None,
+                     slot: int = 0):
+        """One CUDA graph of a whole host-to-host pass over `frames` frames:
+        the pinned ``host_image`` (f32 NHWC) copied in (None: the slot's image
+        is already on the device), the encoder over slot ``slot``, and each
+        feature map copied out to its pinned ``host_features[j]`` right after
+        its LayerNorm, both on a second stream beside the later blocks
+        (``capture``). ``replay()`` on a stream runs one pass."""
+        return self.capture(frames, stream, slot=slot, host_features=host_features,
+                            host_image=host_image)
 
     def host_pipeline(self, frames: int, host_images: list, host_features: list):
         """Frames host to host with each frame's image copy overlapping the

@@ -445,8 +445,10 @@ class EncoderWorkload:
             self.prog.encode_all(stream)
             return
         if self.graph is None:
-            self.graph = self.prog.capture(stream)
-        self.graph.launch(stream)
+            # the frame's kernels, the feature LayerNorms on a second stream
+            # (Encoder.capture)
+            self.graph = self.enc.capture(self.frames, stream)
+        self.graph.replay()
 
     def step_e2e(self, stream):
         # Encoder.host_pipeline: each step one frame host to host, its

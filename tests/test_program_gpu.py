@@ -425,3 +425,42 @@ def test_host_pipeline_frames_equal_direct_passes():
     for k in range(len(images)):
         for g, w_ in zip(got[k], want[k]):
             assert torch.equal(g, w_), k
+
+
+def test_forked_capture_equals_direct_passes():
+    """Encoder.capture: the frame's graph with the feature LayerNorms forked
+    onto a second stream and joined before the next write of the residual
+    stream gives the same bits as encoding the program directly, for both
+    slots and over repeated replays."""
+    import torch
+    import beatlm_b200 as bl
+    from beatlm_b200.model import Encoder, ViTConfig, block_weights_normal
+    cfg = ViTConfig.small(layers=4, out_indices=(1, 2, 4))
+    rng = np.random.default_rng(29)
+    n = lambda *s: rng.standard_normal(int(np.prod(s)), dtype=np.float32) * 0.02
+    w = {"blocks": [block_weights_normal(rng, cfg.dim, cfg.mlp) for _ in range(cfg.layers)],
+         "patch_w": n(cfg.patch, cfg.patch, cfg.cin, cfg.dim), "patch_b": n(cfg.dim),
+         "cls": n(cfg.dim), "pos": n(cfg.tokens, cfg.dim),
+         "norm_g": np.ones(cfg.dim, np.float32), "norm_b": np.zeros(cfg.dim, np.float32)}
+    enc = Encoder(cfg, w, "bf16", planned_frames=1, slots=2)
+    buf = enc.buffers(1)
+    prog = enc.program(1)
+    stream = torch.cuda.Stream()
+    for slot in (0, 1):
+        img = torch.from_numpy(rng.random((1, cfg.side, cfg.side, cfg.cin), dtype=np.float32))
+        buf.images[slot].copy_(img.cuda())
+        torch.cuda.synchronize()
+        prog.encode_all(stream, set=slot)
+        stream.synchronize()
+        want = [f.clone() for f in enc.features(1, slot=slot)]
+        for f in enc.features(1, slot=slot):
+            f.zero_()
+        torch.cuda.synchronize()
+        g = enc.capture(1, stream, slot=slot)
+        for _ in range(3):
+            with torch.cuda.stream(stream):
+                g.replay()
+        stream.synchronize()
+        for got, w_ in zip(enc.features(1, slot=slot), want):
+            assert torch.equal(got, w_), slot
+    assert bl.status(reset=True).code == 0
