@@ -169,28 +169,48 @@ __global__ void resize_bilinear_vec4_kernel(const float4* __restrict__ in, float
 }
 
 // cin a multiple of 8 (every DPT width): a thread's 8 columns are 8
-// consecutive channels of one tap, read as two 16-byte loads; one division
-// per thread instead of one per column.
+// consecutive channels of one tap, read as two 16-byte loads. No division in
+// the loop: each block first tabulates, per 8-column vector j of an output
+// row, its tap (ky, kx) and first channel (or -1 past the taps) in shared
+// memory (k_pad / 8 words), and each thread steps its (pixel, vector) pair
+// and the pixel's (y, x) by the grid stride with carries. Consecutive
+// threads still write consecutive 16-byte vectors.
 // Index arithmetic in 32 bits (the host launches it only when every index
-// fits): 64-bit divisions cost several times more than the copy itself.
+// fits).
 template <typename T>
 __global__ void im2col_vec8_kernel(const float* __restrict__ in, uint4* __restrict__ out, int h,
                                    int w, int cin, int ks, int stride, int relu, int oh, int ow,
                                    int k_pad) {
+    extern __shared__ int vec_tap[];
     const unsigned vecs = static_cast<unsigned>(k_pad) / 8u;
     const unsigned total = static_cast<unsigned>(oh) * static_cast<unsigned>(ow) * vecs;
     const int taps = ks * ks * cin;
     const int pad = ks / 2;
-    for (unsigned v = blockIdx.x * blockDim.x + threadIdx.x; v < total; v += gridDim.x * blockDim.x) {
-        const unsigned pix = v / vecs;
-        const int k0 = static_cast<int>(v - pix * vecs) * 8;
-        const int y = static_cast<int>(pix / static_cast<unsigned>(ow));
-        const int x = static_cast<int>(pix - static_cast<unsigned>(y) * static_cast<unsigned>(ow));
-        float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
+    for (unsigned j = threadIdx.x; j < vecs; j += blockDim.x) {
+        const int k0 = static_cast<int>(j) * 8;
+        int e = -1;
         if (k0 < taps) {
             const int tap = k0 / cin, ci = k0 - tap * cin;
             const int ky = tap / ks, kx = tap - ky * ks;
-            const int iy = y * stride + ky - pad, ix = x * stride + kx - pad;
+            e = (ky << 28) | (kx << 24) | ci;
+        }
+        vec_tap[j] = e;
+    }
+    __syncthreads();
+    const unsigned step = gridDim.x * blockDim.x;
+    const unsigned step_p = step / vecs, step_j = step - step_p * vecs;
+    const unsigned step_y = step_p / static_cast<unsigned>(ow);
+    const unsigned step_x = step_p - step_y * static_cast<unsigned>(ow);
+    unsigned v = blockIdx.x * blockDim.x + threadIdx.x;
+    unsigned pix = v / vecs, j = v - pix * vecs;
+    unsigned y = pix / static_cast<unsigned>(ow), x = pix - y * static_cast<unsigned>(ow);
+    for (; v < total; v += step) {
+        float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
+        const int e = vec_tap[j];
+        if (e >= 0) {
+            const int ky = e >> 28, kx = (e >> 24) & 15, ci = e & 0xFFFFFF;
+            const int iy = static_cast<int>(y) * stride + ky - pad;
+            const int ix = static_cast<int>(x) * stride + kx - pad;
             if (iy >= 0 && iy < h && ix >= 0 && ix < w) {
                 const float4* src = reinterpret_cast<const float4*>(
                     in + (static_cast<long long>(iy) * w + ix) * cin + ci);
@@ -206,6 +226,19 @@ __global__ void im2col_vec8_kernel(const float* __restrict__ in, uint4* __restri
                             to16<T>(lo.z) | (uint32_t(to16<T>(lo.w)) << 16),
                             to16<T>(hi.x) | (uint32_t(to16<T>(hi.y)) << 16),
                             to16<T>(hi.z) | (uint32_t(to16<T>(hi.w)) << 16));
+        // the next (pixel, vector) and the pixel's (y, x), with carries
+        j += step_j;
+        unsigned carry = 0;
+        if (j >= vecs) {
+            j -= vecs;
+            carry = 1;
+        }
+        x += step_x + carry;
+        y += step_y;
+        if (x >= static_cast<unsigned>(ow)) {
+            x -= static_cast<unsigned>(ow);
+            y += 1;
+        }
     }
 }
 
@@ -241,16 +274,20 @@ int bl_im2col(const bl_im2col_args* a, void* stream) {
     const long long work = 1ll * oh * ow * (a->k_pad / 8);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     // the vector path indexes in 32 bits: outputs and inputs below 2^31 elements
+    // (and its tap table, k_pad / 8 words, fits the default 48 KiB of shared memory)
     const bool vec = a->cin % 8 == 0 && (reinterpret_cast<uintptr_t>(a->input) & 15u) == 0 &&
+                     a->k_pad / 8 * sizeof(int) <= 48u * 1024u &&
                      work < (1ll << 31) - 2ll * 256 * 8 * 148 &&
                      1ll * a->h * a->w * a->cin < (1ll << 31);
     auto kern = vec ? (a->out_dtype == BL_F16 ? dec::im2col_vec8_kernel<__half>
                                               : dec::im2col_vec8_kernel<__nv_bfloat16>)
                     : (a->out_dtype == BL_F16 ? dec::im2col_kernel<__half>
                                               : dec::im2col_kernel<__nv_bfloat16>);
-    kern<<<dec::grid_for(work), 256, 0, s>>>(a->input, static_cast<uint4*>(a->out), a->h, a->w,
-                                            a->cin, a->ksize, a->stride, a->relu ? 1 : 0, oh, ow,
-                                            a->k_pad);
+    // the vector path's tap table: one word per 8 columns of an output row
+    const size_t table = vec ? sizeof(int) * (a->k_pad / 8) : 0;
+    kern<<<dec::grid_for(work), 256, table, s>>>(a->input, static_cast<uint4*>(a->out), a->h,
+                                                a->w, a->cin, a->ksize, a->stride,
+                                                a->relu ? 1 : 0, oh, ow, a->k_pad);
     BL_CUDA_TRY(cudaGetLastError());
     return BL_OK;
 }

@@ -245,3 +245,47 @@ def test_implicit_conv3x3_equals_the_gathered_one(h, w, cin, cout, relu, act, re
         if res:
             want = want + r.cpu().numpy().ravel()
         assert _rel(got.cpu().numpy(), want) <= REL
+
+
+def _im2col_host(x, h, w, cin, ks, stride, relu, k_pad, dtype):
+    """The reference's im2col order (K = taps x cin, tap = ky * ks + kx), zero
+    border, ReLU on the way in, rounded to the 16-bit type."""
+    pad = ks // 2
+    oh, ow = (h + 2 * pad - ks) // stride + 1, (w + 2 * pad - ks) // stride + 1
+    img = x.reshape(h, w, cin)
+    if relu:
+        img = np.maximum(img, 0.0)
+    padded = np.zeros((h + 2 * pad, w + 2 * pad, cin), np.float32)
+    padded[pad:pad + h, pad:pad + w] = img
+    out = np.zeros((oh, ow, k_pad), np.float32)
+    for ky in range(ks):
+        for kx in range(ks):
+            t = (ky * ks + kx) * cin
+            out[:, :, t:t + cin] = padded[ky:ky + stride * oh:stride, kx:kx + stride * ow:stride]
+    out = out.reshape(oh * ow, k_pad)
+    return oracle.round_f16(out) if dtype == "f16" else oracle.round_bf16(out)
+
+
+@pytest.mark.parametrize("h,w,cin,ks,stride,relu,dtype", [
+    (37, 37, 64, 3, 1, True, "f16"),      # a fusion unit at 37 px
+    (148, 148, 64, 3, 1, False, "f16"),
+    (518, 518, 32, 3, 1, True, "f16"),    # the head's full-resolution convolution
+    (74, 74, 96, 3, 2, False, "bf16"),    # stride 2, 96 channels: vectors straddle taps
+    (23, 1, 32, 3, 1, True, "f16"),       # one column
+    (5, 7, 384, 3, 1, False, "f16"),      # K = 3456 (the neck's widest)
+    (300, 11, 40, 1, 1, True, "bf16"),    # 1x1, K padded from 40 to 64
+])
+def test_im2col_gathers_the_reference_order(h, w, cin, ks, stride, relu, dtype):
+    """bl_im2col's vector path (each block's tap table, each thread's
+    (pixel, vector) stepped by the grid stride with carries) against a host
+    gather of the same map: the same 16-bit values in every column, the
+    padding columns zero."""
+    import torch
+    from beatlm_b200 import ops
+    x = _data(70 + cin + h, h * w * cin)
+    got, oh, ow = ops.im2col(torch.from_numpy(x).cuda(), h, w, cin, ksize=ks, stride=stride,
+                             relu=relu, dtype=dtype)
+    torch.cuda.synchronize()
+    k_pad = got.shape[1]
+    want = _im2col_host(x, h, w, cin, ks, stride, relu, k_pad, dtype)
+    assert np.array_equal(got.float().cpu().numpy(), want)
