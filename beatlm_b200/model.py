@@ -914,10 +914,18 @@ class Decoder:
         import torch
         self.cfg, self.dcfg = cfg, dcfg
         dev = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(device)
+
+        def padded(b, wts):
+            # a bias zero-padded to the weights' padded output channels, so
+            # the convolution reads it in place (no per-call padding)
+            out = np.zeros(wts.shape[0], np.float32)
+            out[:len(b)] = np.asarray(b, np.float32).reshape(-1)
+            return dev(out)
         F = dcfg.fusion
         self.stages = []
         for c, rs, w in zip(dcfg.neck, dcfg.reassemble, weights["stages"]):
-            st = {"proj": (ops.conv_weights(w["proj_w"], 1, cfg.dim, c), dev(w["proj_b"])),
+            pw = ops.conv_weights(w["proj_w"], 1, cfg.dim, c)
+            st = {"proj": (pw, padded(w["proj_b"], pw)),
                   "neck": ops.conv_weights(w["neck_w"], 3, c, F), "resample": rs, "c": c}
             if rs[0] == "down":
                 st["resize"] = (ops.conv_weights(w["resize_w"], 3, c, c), dev(w["resize_b"]))
@@ -931,9 +939,10 @@ class Decoder:
                         "proj": (ops.conv_weights(f["proj_w"], 1, F, F), dev(f["proj_b"]))}
                        for f in weights["fusion"]]
         h = weights["head"]
+        w3 = ops.conv_weights(h["w3"], 1, dcfg.head, 1)
         self.head = {"c1": (ops.conv_weights(h["w1"], 3, F, F // 2), dev(h["b1"])),
                      "c2": (ops.conv_weights(h["w2"], 3, F // 2, dcfg.head), dev(h["b2"])),
-                     "c3": (ops.conv_weights(h["w3"], 1, dcfg.head, 1), dev(h["b3"]))}
+                     "c3": (w3, padded(h["b3"], w3))}
 
     def _unit(self, x, u, side, residual=None):
         F = self.dcfg.fusion
@@ -974,11 +983,15 @@ class Decoder:
             f = self.fusion[layer]
             if fused is None:
                 x = stage
-            else:  # unit1(stage) + previous: the previous map joins the unit's residual
-                x = self._unit(stage, f["unit1"], s, residual=stage + fused)
+            else:  # unit1(stage) + previous: `fused` already holds stage + previous
+                x = self._unit(stage, f["unit1"], s, residual=fused)
             x = self._unit(x, f["unit2"], s)
             x = ops.resize_bilinear(x, s, s, out_side, out_side, F, stream)
-            fused = ops.conv2d(x, f["proj"][0], f["proj"][1], out_side, out_side, F, F, ksize=1)
+            # the projection's epilogue adds the next layer's stage map (the
+            # residual of that layer's first unit): the same f32 addition as
+            # a separate pass, one launch fewer
+            fused = ops.conv2d(x, f["proj"][0], f["proj"][1], out_side, out_side, F, F, ksize=1,
+                               residual=maps[nxt][0] if nxt >= 0 else None)
             side = out_side
         out_side = g * cfg.patch
         h = self.head
