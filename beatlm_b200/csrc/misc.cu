@@ -147,9 +147,20 @@ __global__ void __launch_bounds__(128) layernorm_vec_kernel(bl_layernorm_args a,
 // Index arithmetic in 32 bits (the host checks that every index fits): the
 // divisions happen once per thread, and the 8 taps step (ky, kx, ci) by
 // increments, since run-time integer divisions dominated the kernel.
-__global__ void patchify_kernel(bl_patchify_args a, int grid_side, int taps) {
+// Blocks past `patch_blocks` (one per frame, when a.x is set) write the
+// frame's class-token row: x[f][0][c] = cls[c] + pos[0][c] (an f32 add, as a
+// fused epilogue Add would do), so the rows need no launch of their own.
+__global__ void patchify_kernel(bl_patchify_args a, int grid_side, int taps,
+                                unsigned patch_blocks) {
     pdl_trigger();
     pdl_wait();
+    if (blockIdx.x >= patch_blocks) {
+        const long long f = blockIdx.x - patch_blocks;
+        const long long tokens = static_cast<long long>(grid_side) * grid_side + 1;
+        for (int c = threadIdx.x; c < static_cast<int>(a.dim); c += blockDim.x)
+            a.x[f * tokens * a.dim + c] = a.cls[c] + a.pos[c];
+        return;
+    }
     const unsigned idx = blockIdx.x * blockDim.x + threadIdx.x;
     const unsigned groups = a.k_pad / 8;
     const unsigned per_frame = static_cast<unsigned>(grid_side * grid_side);
@@ -183,16 +194,6 @@ __global__ void patchify_kernel(bl_patchify_args a, int grid_side, int taps) {
     w.z = h[4] | (static_cast<uint32_t>(h[5]) << 16);
     w.w = h[6] | (static_cast<uint32_t>(h[7]) << 16);
     reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.a) + patch * a.k_pad)[g] = w;
-}
-
-// Class-token rows: x[f][0][c] = cls[c] + pos[0][c] (f64-free f32 add, as a
-// fused epilogue Add would do).
-__global__ void cls_rows_kernel(bl_patchify_args a, int tokens) {
-    pdl_trigger();
-    pdl_wait();
-    const int f = blockIdx.x;
-    for (int c = threadIdx.x; c < static_cast<int>(a.dim); c += blockDim.x)
-        a.x[static_cast<long long>(f) * tokens * a.dim + c] = a.cls[c] + a.pos[c];
 }
 
 }  // namespace misc
@@ -268,11 +269,9 @@ int prepare_patchify(const bl_patchify_args& a, Launch* out) {
     const unsigned blocks = static_cast<unsigned>((work + 255) / 256);
     out->op = 4;
     out->run = [=](cudaStream_t s) {
-        cudaError_t e = launch_k(misc::patchify_kernel, dim3(blocks), dim3(256), 0, s, a, g,
-                                 static_cast<int>(taps));
-        if (e == cudaSuccess && a.x != nullptr)
-            e = launch_k(misc::cls_rows_kernel, dim3(a.frames), dim3(128), 0, s, a, g * g + 1);
-        return e;
+        // the patch matrix, and one block per frame for its class-token row
+        return launch_k(misc::patchify_kernel, dim3(blocks + (a.x != nullptr ? a.frames : 0)),
+                        dim3(256), 0, s, a, g, static_cast<int>(taps), blocks);
     };
     return BL_OK;
 }

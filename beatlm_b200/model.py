@@ -819,10 +819,11 @@ class Encoder:
 
     def launches_per_frame_batch(self, layers: int | None = None, frames: int = 1) -> int:
         """Kernels launched per pass: the program's specs, with the patch
-        matrix and its class rows counted as two."""
+        embedding counted as two (the patch matrix, whose launch also writes
+        the class-token rows, and its GEMM)."""
         from .graph import PatchEmbed
         prog, _, _ = self.lowered(frames, layers)
-        return sum(3 if isinstance(k.main, PatchEmbed) else 1 for k in prog.kernels)
+        return sum(2 if isinstance(k.main, PatchEmbed) else 1 for k in prog.kernels)
 
 
 class HostPipeline:

@@ -295,7 +295,7 @@ def test_the_generated_encoder_program_is_the_listed_one(fused_ln):
     assert [g[0] for g in got] == [w_[0] for w_ in want]
     assert got == want
     assert enc.specs_layout(1) == [g[0] for g in got]
-    assert enc.launches_per_frame_batch(frames=1) == len(got) + 1
+    assert enc.launches_per_frame_batch(frames=1) == len(got)
 
 
 def test_buffer_lifetimes_come_from_the_launches():

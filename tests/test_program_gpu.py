@@ -140,7 +140,7 @@ def test_encoder_program_graph_equals_direct():
     torch.cuda.synchronize()
     want = feats[0].clone()
     prog = enc.program(1)
-    assert len(prog) == enc.launches_per_frame_batch() - 1  # patchify is one launch record
+    assert len(prog) == enc.launches_per_frame_batch()  # one launch record per launch
     s = torch.cuda.Stream()
     g = prog.capture(s)
     enc.buffers(1).features[0].zero_()
