@@ -242,6 +242,51 @@ __global__ void im2col_vec8_kernel(const float* __restrict__ in, uint4* __restri
     }
 }
 
+// One output channel of a 1x1 convolution over NHWC f32 rows of 4 * c4
+// values: out[p] = act(sum_i in[p][i] w[i] + b). A warp step covers 16
+// pixels as four 4-pixel loads (lane l: pixel 4 k + l / 8, float4 l % 8 of
+// each 32 channels, so a load is 512 contiguous bytes at 32 channels); each
+// lane sums its float4s in channel order, an xor-shuffle tree within the
+// pixel's 8 lanes completes the sum (the same bits whichever lane reads it),
+// and the group's first lane stores the pixel.
+__global__ void conv1x1_one_kernel(const float4* __restrict__ in, const float4* __restrict__ w,
+                                   float b, float* __restrict__ out, unsigned pixels, int c4,
+                                   int relu) {
+    const int lane = threadIdx.x & 31, sub = lane & 7, grp = lane >> 3;
+    const unsigned warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const unsigned warps = (gridDim.x * blockDim.x) >> 5;
+    for (unsigned p0 = warp * 16u; p0 < pixels; p0 += warps * 16u) {  // warp-uniform
+        float acc[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const unsigned p = p0 + 4u * k + grp;
+            acc[k] = 0.0f;
+            if (p < pixels) {
+                const float4* row = in + static_cast<size_t>(p) * c4;
+                for (int i = sub; i < c4; i += 8) {
+                    const float4 v = __ldg(row + i), q = __ldg(w + i);
+                    acc[k] = fmaf(v.x, q.x, acc[k]);
+                    acc[k] = fmaf(v.y, q.y, acc[k]);
+                    acc[k] = fmaf(v.z, q.z, acc[k]);
+                    acc[k] = fmaf(v.w, q.w, acc[k]);
+                }
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            float a = acc[k];
+            a += __shfl_xor_sync(0xFFFFFFFFu, a, 1);
+            a += __shfl_xor_sync(0xFFFFFFFFu, a, 2);
+            a += __shfl_xor_sync(0xFFFFFFFFu, a, 4);
+            const unsigned p = p0 + 4u * k + grp;
+            if (sub == 0 && p < pixels) {
+                const float y = a + b;
+                out[p] = relu ? fmaxf(y, 0.0f) : y;
+            }
+        }
+    }
+}
+
 // blocks of 256 threads, up to 8 per SM, never more than the work needs
 unsigned grid_for(long long work) {
     const long long blocks = (work + 255) / 256;
@@ -311,6 +356,29 @@ int bl_blocks_to_map(const float* blocks, const float* bias, float* out, uint32_
     else
         dec::blocks_to_map_kernel<<<dec::grid_for(work), 256, 0, static_cast<cudaStream_t>(stream)>>>(
             blocks, bias, out, h, w, f, cout);
+    BL_CUDA_TRY(cudaGetLastError());
+    return BL_OK;
+}
+
+int bl_conv1x1_one(const float* in, const float* w, float bias, float* out, uint32_t pixels,
+                   uint32_t c, int32_t relu, void* stream) {
+    using namespace bl;
+    if (in == nullptr || w == nullptr || out == nullptr)
+        return fail(BL_ERR_INVALID, "conv1x1_one: null argument");
+    if (pixels == 0 || c == 0) return fail(BL_ERR_INVALID, "conv1x1_one: zero dimension");
+    if (c % 4 != 0 || c > 1024)
+        return fail(BL_ERR_UNSUPPORTED, "conv1x1_one: %u channels (a multiple of 4, at most 1024)", c);
+    if (((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(w)) & 15u) ||
+        (reinterpret_cast<uintptr_t>(out) & 3u))
+        return fail(BL_ERR_INVALID, "conv1x1_one: in and w must be 16-byte aligned, out 4-byte");
+    if (1ull * pixels + 16ull * 8 * 256 * 8 * 148 >= (1ull << 32))
+        return fail(BL_ERR_UNSUPPORTED, "conv1x1_one: %u pixels exceed 32-bit indexing", pixels);
+    // one warp step per 16 pixels, 8 warps a block
+    const long long steps = (static_cast<long long>(pixels) + 15) / 16;
+    const unsigned blocks = dec::grid_for(steps * 32);
+    dec::conv1x1_one_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        reinterpret_cast<const float4*>(in), reinterpret_cast<const float4*>(w), bias, out, pixels,
+        static_cast<int>(c / 4), relu ? 1 : 0);
     BL_CUDA_TRY(cudaGetLastError());
     return BL_OK;
 }

@@ -940,10 +940,12 @@ class Decoder:
                         "proj": (ops.conv_weights(f["proj_w"], 1, F, F), dev(f["proj_b"]))}
                        for f in weights["fusion"]]
         h = weights["head"]
-        w3 = ops.conv_weights(h["w3"], 1, dcfg.head, 1)
+        # the last convolution (head width -> 1 channel, 1x1) as a per-pixel
+        # dot product in f32 (bl_conv1x1_one): its weights as a vector
         self.head = {"c1": (ops.conv_weights(h["w1"], 3, F, F // 2), dev(h["b1"])),
                      "c2": (ops.conv_weights(h["w2"], 3, F // 2, dcfg.head), dev(h["b2"])),
-                     "c3": (w3, padded(h["b3"], w3))}
+                     "c3": (dev(np.asarray(h["w3"], np.float32).reshape(dcfg.head)),
+                            float(np.asarray(h["b3"], np.float32).reshape(-1)[0]))}
 
     def _unit(self, x, u, side, residual=None):
         F = self.dcfg.fusion
@@ -1000,8 +1002,8 @@ class Decoder:
         x = ops.resize_bilinear(x, side, side, out_side, out_side, F // 2, stream)
         x = ops.conv2d(x, h["c2"][0], h["c2"][1], out_side, out_side, F // 2, self.dcfg.head,
                        act="relu")
-        x = ops.conv2d(x, h["c3"][0], h["c3"][1], out_side, out_side, self.dcfg.head, 1,
-                       ksize=1, act="relu")
+        x = ops.conv1x1_one(x, h["c3"][0], h["c3"][1], out_side * out_side, self.dcfg.head,
+                            relu=True)
         return x.reshape(out_side, out_side)
 
     def capture(self, features: list, stream):

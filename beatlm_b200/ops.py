@@ -383,6 +383,17 @@ def conv_transpose(x, hwio, bias, h: int, w: int, cin: int, cout: int, f: int,
     return out
 
 
+def conv1x1_one(x, w, bias: float, pixels: int, c: int, relu: bool = False, stream=None):
+    """``bl_conv1x1_one``: one output channel of a 1x1 convolution of the
+    NHWC f32 map ``x`` ([pixels][c]) by the f32 device vector ``w`` [c],
+    plus ``bias``, ReLU when asked; returns f32 [pixels]."""
+    import torch
+    out = torch.empty(pixels, dtype=torch.float32, device=x.device)
+    N.check(N.lib().bl_conv1x1_one(x.data_ptr(), w.data_ptr(), float(bias), out.data_ptr(),
+                                   pixels, c, 1 if relu else 0, _stream_ptr(stream)))
+    return out
+
+
 def resize_bilinear(x, ih: int, iw: int, oh: int, ow: int, c: int, stream=None):
     """``bl_resize_bilinear``: corners aligned, f32 NHWC."""
     import torch

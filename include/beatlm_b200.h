@@ -708,6 +708,13 @@ int bl_conv3x3(const bl_gemm_args* gemm, const bl_conv3x3_args* conv, void* stre
  * convolution writes (reference.rs:103-140). */
 int bl_blocks_to_map(const float* blocks, const float* bias, float* out, uint32_t h, uint32_t w,
                      uint32_t f, uint32_t cout, void* stream);
+/* One output channel of a 1x1 convolution (reference.rs:79-101 with cout 1;
+ * the depth head's last convolution, model/depth_anything_v2.rs:680-982):
+ * out[p] = act(sum_i in[p][i] * w[i] + bias) over NHWC f32 rows of c values
+ * (c a multiple of 4, at most 1024; in and w 16-byte aligned), act = max(x, 0)
+ * when relu != 0, in f32 without a GEMM's padded output channels. */
+int bl_conv1x1_one(const float* in, const float* w, float bias, float* out, uint32_t pixels,
+                   uint32_t c, int32_t relu, void* stream);
 /* Bilinear resampling with corners aligned, [ih][iw][c] -> [oh][ow][c]
  * (reference.rs:142-175), in f32. */
 int bl_resize_bilinear(const float* in, float* out, uint32_t ih, uint32_t iw, uint32_t oh,

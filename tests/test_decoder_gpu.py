@@ -289,3 +289,34 @@ def test_im2col_gathers_the_reference_order(h, w, cin, ks, stride, relu, dtype):
     k_pad = got.shape[1]
     want = _im2col_host(x, h, w, cin, ks, stride, relu, k_pad, dtype)
     assert np.array_equal(got.float().cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("pixels,c,relu", [
+    (518 * 518, 32, True),  # the depth head's last convolution
+    (1001, 4, False),       # pixels not a multiple of a warp step
+    (37, 64, True),
+    (17, 256, False),
+    (5, 1024, True),        # the widest row it takes
+])
+def test_conv1x1_one_matches_the_oracle(pixels, c, relu):
+    """bl_conv1x1_one (one output channel of a 1x1 convolution, summed in f32
+    by a fixed shuffle order) against the oracle's conv1x1 with one output
+    channel (f64 sums): within 1e-5 relative L2, and two calls give the same
+    bits."""
+    import torch
+    from beatlm_b200 import ops
+    x = _data(90 + c, pixels * c)
+    w = _data(91 + c, c, 1.0 / np.sqrt(c))
+    b = 0.05
+    xd, wd = torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda()
+    got = ops.conv1x1_one(xd, wd, b, pixels, c, relu=relu)
+    again = ops.conv1x1_one(xd, wd, b, pixels, c, relu=relu)
+    torch.cuda.synchronize()
+    want = oracle.conv1x1(x, w.reshape(c, 1), np.array([b], np.float32), pixels, c, 1)
+    if relu:
+        want = np.maximum(want, 0.0)
+    got = got.cpu().numpy()
+    assert np.array_equal(got, again.cpu().numpy())
+    assert _rel(got, want) < 1e-5
+    if relu:
+        assert (got >= 0).all()
