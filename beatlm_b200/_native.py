@@ -295,6 +295,8 @@ SIGNATURES.update({
     "bl_conv3x3": (ctypes.c_int, [ctypes.POINTER(GemmArgs), ctypes.POINTER(Conv3x3Args), _vp]),
     "bl_blocks_to_map": (ctypes.c_int, [_vp, _vp, _vp, _u32, _u32, _u32, _u32, _vp]),
     "bl_resize_bilinear": (ctypes.c_int, [_vp, _vp, _u32, _u32, _u32, _u32, _u32, _vp]),
+    "bl_resize_bilinear_rows16": (ctypes.c_int, [_vp, _vp, _u32, _u32, _u32, _u32, _u32, _u32,
+                                                 ctypes.c_int32, _vp]),
     "bl_conv1x1_one": (ctypes.c_int, [_vp, _vp, ctypes.c_float, _vp, _u32, _u32, ctypes.c_int32,
                                       _vp]),
     "bl_budget_for_frame": (_u64, [_u64, _u64, _u64]),

@@ -119,6 +119,16 @@ __device__ __forceinline__ void axis(int o, int in, int outn, int* i0, int* i1, 
     *l = pos - static_cast<float>(a);
 }
 
+// The four corners mixed along x, then y, each product and sum rounded as
+// written (no contraction left to the compiler), so every resampling kernel
+// below gives the same f32 bits for the same pixel.
+__device__ __forceinline__ float bilerp(float v00, float v01, float v10, float v11, float lx,
+                                        float ly) {
+    const float top = __fadd_rn(__fmul_rn(1.0f - lx, v00), __fmul_rn(lx, v01));
+    const float bottom = __fadd_rn(__fmul_rn(1.0f - lx, v10), __fmul_rn(lx, v11));
+    return __fadd_rn(__fmul_rn(1.0f - ly, top), __fmul_rn(ly, bottom));
+}
+
 __global__ void resize_bilinear_kernel(const float* __restrict__ in, float* __restrict__ out, int ih,
                                        int iw, int oh, int ow, int c) {
     const long long total = static_cast<long long>(oh) * ow * c;
@@ -135,9 +145,7 @@ __global__ void resize_bilinear_kernel(const float* __restrict__ in, float* __re
         const float a01 = __ldg(in + (static_cast<long long>(y0) * iw + x1) * c + ch);
         const float a10 = __ldg(in + (static_cast<long long>(y1) * iw + x0) * c + ch);
         const float a11 = __ldg(in + (static_cast<long long>(y1) * iw + x1) * c + ch);
-        const float top = (1.0f - lx) * a00 + lx * a01;
-        const float bottom = (1.0f - lx) * a10 + lx * a11;
-        out[i] = (1.0f - ly) * top + ly * bottom;
+        out[i] = bilerp(a00, a01, a10, a11, lx, ly);
     }
 }
 
@@ -158,13 +166,54 @@ __global__ void resize_bilinear_vec4_kernel(const float4* __restrict__ in, float
         axis(ox, iw, ow, &x0, &x1, &lx);
         const float4 a00 = __ldg(in + (y0 * iw + x0) * c4 + ch), a01 = __ldg(in + (y0 * iw + x1) * c4 + ch);
         const float4 a10 = __ldg(in + (y1 * iw + x0) * c4 + ch), a11 = __ldg(in + (y1 * iw + x1) * c4 + ch);
-        auto mix = [&](float v00, float v01, float v10, float v11) {
-            const float top = (1.0f - lx) * v00 + lx * v01;
-            const float bottom = (1.0f - lx) * v10 + lx * v11;
-            return (1.0f - ly) * top + ly * bottom;
-        };
-        out[i] = make_float4(mix(a00.x, a01.x, a10.x, a11.x), mix(a00.y, a01.y, a10.y, a11.y),
-                             mix(a00.z, a01.z, a10.z, a11.z), mix(a00.w, a01.w, a10.w, a11.w));
+        out[i] = make_float4(bilerp(a00.x, a01.x, a10.x, a11.x, lx, ly),
+                             bilerp(a00.y, a01.y, a10.y, a11.y, lx, ly),
+                             bilerp(a00.z, a01.z, a10.z, a11.z, lx, ly),
+                             bilerp(a00.w, a01.w, a10.w, a11.w, lx, ly));
+    }
+}
+
+// The same resampling written as 16-bit rows of ld8 * 8 values, the A operand
+// of a 1x1 convolution's GEMM (what a gather of the f32 map would store, with
+// no f32 map in between): a thread makes 8 consecutive channels of one output
+// pixel from two float4 loads at each corner and stores them as one 16-byte
+// vector; vectors past the c4 * 4 channels are zeros. c4 even; 32-bit index
+// arithmetic (the host launches it only when every index fits).
+template <typename T>
+__global__ void resize_bilinear_rows16_kernel(const float4* __restrict__ in, uint4* __restrict__ out,
+                                              int ih, int iw, int oh, int ow, int c4, int ld8) {
+    const unsigned total = static_cast<unsigned>(oh) * static_cast<unsigned>(ow) * static_cast<unsigned>(ld8);
+    for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const unsigned p = i / static_cast<unsigned>(ld8);
+        const int v = static_cast<int>(i - p * static_cast<unsigned>(ld8));
+        uint4 r = make_uint4(0u, 0u, 0u, 0u);
+        if (2 * v < c4) {
+            const int oy = static_cast<int>(p / static_cast<unsigned>(ow));
+            const int ox = static_cast<int>(p - static_cast<unsigned>(oy) * static_cast<unsigned>(ow));
+            int y0, y1, x0, x1;
+            float ly, lx;
+            axis(oy, ih, oh, &y0, &y1, &ly);
+            axis(ox, iw, ow, &x0, &x1, &lx);
+            const float4* c00 = in + (y0 * iw + x0) * c4 + 2 * v;
+            const float4* c01 = in + (y0 * iw + x1) * c4 + 2 * v;
+            const float4* c10 = in + (y1 * iw + x0) * c4 + 2 * v;
+            const float4* c11 = in + (y1 * iw + x1) * c4 + 2 * v;
+            float f[8];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const float4 a00 = __ldg(c00 + h), a01 = __ldg(c01 + h);
+                const float4 a10 = __ldg(c10 + h), a11 = __ldg(c11 + h);
+                f[4 * h + 0] = bilerp(a00.x, a01.x, a10.x, a11.x, lx, ly);
+                f[4 * h + 1] = bilerp(a00.y, a01.y, a10.y, a11.y, lx, ly);
+                f[4 * h + 2] = bilerp(a00.z, a01.z, a10.z, a11.z, lx, ly);
+                f[4 * h + 3] = bilerp(a00.w, a01.w, a10.w, a11.w, lx, ly);
+            }
+            r = make_uint4(to16<T>(f[0]) | (uint32_t(to16<T>(f[1])) << 16),
+                           to16<T>(f[2]) | (uint32_t(to16<T>(f[3])) << 16),
+                           to16<T>(f[4]) | (uint32_t(to16<T>(f[5])) << 16),
+                           to16<T>(f[6]) | (uint32_t(to16<T>(f[7])) << 16));
+        }
+        out[i] = r;
     }
 }
 
@@ -398,6 +447,36 @@ int bl_resize_bilinear(const float* in, float* out, uint32_t ih, uint32_t iw, ui
     else
         dec::resize_bilinear_kernel<<<dec::grid_for(work), 256, 0, static_cast<cudaStream_t>(stream)>>>(
             in, out, ih, iw, oh, ow, c);
+    BL_CUDA_TRY(cudaGetLastError());
+    return BL_OK;
+}
+
+int bl_resize_bilinear_rows16(const float* in, void* out, uint32_t ih, uint32_t iw, uint32_t oh,
+                              uint32_t ow, uint32_t c, uint32_t ld, int32_t out_dtype,
+                              void* stream) {
+    using namespace bl;
+    if (in == nullptr || out == nullptr) return fail(BL_ERR_INVALID, "resize rows16: null argument");
+    if (ih == 0 || iw == 0 || oh == 0 || ow == 0 || c == 0)
+        return fail(BL_ERR_INVALID, "resize rows16: zero dimension");
+    if (c % 8 != 0 || ld % 8 != 0 || ld < c)
+        return fail(BL_ERR_UNSUPPORTED,
+                    "resize rows16: %u channels into rows of %u (both multiples of 8, rows >= channels)",
+                    c, ld);
+    if (out_dtype != BL_F16 && out_dtype != BL_BF16)
+        return fail(BL_ERR_UNSUPPORTED, "resize rows16: out dtype %d (f16 or bf16)", out_dtype);
+    if (((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 15u) != 0)
+        return fail(BL_ERR_INVALID, "resize rows16: in and out must be 16-byte aligned");
+    const long long work = 1ll * oh * ow * (ld / 8);
+    if (work >= (1ll << 31) - 2ll * 256 * 8 * 148 || 1ll * ih * iw * c >= (1ll << 31))
+        return fail(BL_ERR_UNSUPPORTED, "resize rows16: sizes exceed 32-bit indexing");
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const unsigned grid = dec::grid_for(work);
+    if (out_dtype == BL_F16)
+        dec::resize_bilinear_rows16_kernel<__half><<<grid, 256, 0, st>>>(
+            reinterpret_cast<const float4*>(in), static_cast<uint4*>(out), ih, iw, oh, ow, c / 4, ld / 8);
+    else
+        dec::resize_bilinear_rows16_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
+            reinterpret_cast<const float4*>(in), static_cast<uint4*>(out), ih, iw, oh, ow, c / 4, ld / 8);
     BL_CUDA_TRY(cudaGetLastError());
     return BL_OK;
 }

@@ -963,6 +963,7 @@ class Decoder:
             return self._forward(features)
 
     def _forward(self, features: list):
+        import torch
         stream = None  # the current stream, for every op
         cfg, F = self.cfg, self.dcfg.fusion
         g = cfg.grid
@@ -989,11 +990,16 @@ class Decoder:
             else:  # unit1(stage) + previous: `fused` already holds stage + previous
                 x = self._unit(stage, f["unit1"], s, residual=fused)
             x = self._unit(x, f["unit2"], s)
-            x = ops.resize_bilinear(x, s, s, out_side, out_side, F, stream)
+            # the resampling writes the projection's 16-bit GEMM rows itself
+            # (the same values a gather of its f32 output would store), and
             # the projection's epilogue adds the next layer's stage map (the
-            # residual of that layer's first unit): the same f32 addition as
-            # a separate pass, one launch fewer
-            fused = ops.conv2d(x, f["proj"][0], f["proj"][1], out_side, out_side, F, F, ksize=1,
+            # residual of that layer's first unit): the same arithmetic as
+            # separate passes, two launches fewer
+            pw = f["proj"][0]
+            x = ops.resize_bilinear_rows16(x, s, s, out_side, out_side, F, pw.shape[1],
+                                           "f16" if pw.dtype == torch.float16 else "bf16",
+                                           stream)
+            fused = ops.conv2d(x, pw, f["proj"][1], out_side, out_side, F, F, ksize=1,
                                residual=maps[nxt][0] if nxt >= 0 else None)
             side = out_side
         out_side = g * cfg.patch

@@ -295,7 +295,9 @@ def conv2d(x, weights, bias, h: int, w: int, cin: int, cout: int, *, ksize: int 
     """A 3x3 (zero padding 1) or 1x1 convolution of the NHWC f32 map ``x``:
     ``weights`` from ``conv_weights``, ``bias`` f32 [cout] or None, ``act``
     "relu" on the result, ``residual`` an f32 [oh * ow][cout] map added last
-    (cout a multiple of 32). Returns f32 [oh * ow][cout].
+    (cout a multiple of 32). Returns f32 [oh * ow][cout]. A 1x1 convolution
+    also takes ``x`` as 16-bit rows [h * w][k_pad] of the weights' dtype
+    (``resize_bilinear_rows16``), multiplied as they are.
 
     ``implicit=True``: a 3x3 stride-1 convolution of a multiple of 32
     channels runs as an implicit GEMM (``bl_conv3x3``, the image read
@@ -309,6 +311,17 @@ def conv2d(x, weights, bias, h: int, w: int, cin: int, cout: int, *, ksize: int 
     form's GEMM)."""
     import torch
     dt = "f16" if weights.dtype == torch.float16 else "bf16"
+    if x.dtype in (torch.float16, torch.bfloat16):
+        # 16-bit rows already in the GEMM's layout (resize_bilinear_rows16):
+        # a 1x1 convolution of them is the GEMM alone
+        if ksize != 1 or stride != 1 or relu_input or implicit:
+            raise ValueError("conv2d: 16-bit rows take a 1x1, stride-1 convolution without "
+                             "an input ReLU")
+        if (x.dtype != weights.dtype or tuple(x.shape) != (h * w, weights.shape[1])
+                or not x.is_contiguous() or cin > weights.shape[1]):
+            raise ValueError("conv2d: 16-bit rows must be [h * w][k_pad] of the weights' dtype, "
+                             "contiguous")
+        implicit = False
     can = (ksize == 3 and stride == 1 and cin % 32 == 0 and x.dtype == torch.float32
            and x.is_contiguous() and x.data_ptr() % 16 == 0)
     if implicit is None:
@@ -317,6 +330,8 @@ def conv2d(x, weights, bias, h: int, w: int, cin: int, cout: int, *, ksize: int 
         raise ValueError("conv2d: the implicit form takes 3x3, stride 1, channels a multiple of 32")
     if implicit:
         cols, oh, ow = None, h, w
+    elif x.dtype in (torch.float16, torch.bfloat16):
+        cols, oh, ow = x, h, w
     else:
         cols, oh, ow = im2col(x, h, w, cin, ksize, stride, relu_input, weights.shape[1], dt,
                               stream)
@@ -400,4 +415,18 @@ def resize_bilinear(x, ih: int, iw: int, oh: int, ow: int, c: int, stream=None):
     out = torch.empty((oh * ow, c), dtype=torch.float32, device=x.device)
     N.check(N.lib().bl_resize_bilinear(x.data_ptr(), out.data_ptr(), ih, iw, oh, ow, c,
                                        _stream_ptr(stream)))
+    return out
+
+
+def resize_bilinear_rows16(x, ih: int, iw: int, oh: int, ow: int, c: int, ld: int | None = None,
+                           dtype: str = "f16", stream=None):
+    """``bl_resize_bilinear_rows16``: the resampling of ``resize_bilinear``
+    written as 16-bit rows [oh * ow][ld] (channels past ``c`` zero), the
+    operand ``conv2d`` takes for a 1x1 convolution without a gather."""
+    import torch
+    ld = c if ld is None else ld
+    out = torch.empty((oh * ow, ld), dtype=torch.float16 if dtype == "f16" else torch.bfloat16,
+                      device=x.device)
+    N.check(N.lib().bl_resize_bilinear_rows16(x.data_ptr(), out.data_ptr(), ih, iw, oh, ow, c, ld,
+                                              _TD[dtype], _stream_ptr(stream)))
     return out

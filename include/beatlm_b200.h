@@ -719,6 +719,15 @@ int bl_conv1x1_one(const float* in, const float* w, float bias, float* out, uint
  * (reference.rs:142-175), in f32. */
 int bl_resize_bilinear(const float* in, float* out, uint32_t ih, uint32_t iw, uint32_t oh,
                        uint32_t ow, uint32_t c, void* stream);
+/* The same resampling written as 16-bit rows (out_dtype BL_F16 or BL_BF16)
+ * of ld values, channels c..ld-1 zero: the A operand of the 1x1 convolution
+ * that follows each DPT fusion layer's resampling
+ * (model/depth_anything_v2.rs:680-982), the f32 values of bl_resize_bilinear
+ * rounded once to 16 bits, with no f32 map in between. c and ld multiples of
+ * 8, ld >= c, in and out 16-byte aligned. */
+int bl_resize_bilinear_rows16(const float* in, void* out, uint32_t ih, uint32_t iw, uint32_t oh,
+                              uint32_t ow, uint32_t c, uint32_t ld, int32_t out_dtype,
+                              void* stream);
 
 /* ------------------------------------------------------------- pass cost */
 

@@ -320,3 +320,56 @@ def test_conv1x1_one_matches_the_oracle(pixels, c, relu):
     assert _rel(got, want) < 1e-5
     if relu:
         assert (got >= 0).all()
+
+
+@pytest.mark.parametrize("ih,iw,oh,ow,c,ld", [
+    (148, 148, 296, 296, 64, 64),  # the last fusion layer's resampling before its projection
+    (19, 19, 37, 37, 64, 64),      # the deepest layer's
+    (37, 37, 74, 74, 48, 64),      # channels padded to the row width with zeros
+    (2, 3, 5, 4, 8, 16),
+    (1, 1, 1, 1, 8, 8),
+])
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+def test_resize_rows16_is_the_rounded_f32_resampling(ih, iw, oh, ow, c, ld, dt):
+    """bl_resize_bilinear_rows16 writes exactly the f32 resampling of
+    bl_resize_bilinear rounded once to 16 bits (to nearest even), zeros in the
+    padded channels, and stays within the oracle's tolerance."""
+    import torch
+    from beatlm_b200 import ops
+    x = _data(70 + c, ih * iw * c)
+    xd = torch.from_numpy(x).cuda()
+    got = ops.resize_bilinear_rows16(xd, ih, iw, oh, ow, c, ld, dt)
+    f32 = ops.resize_bilinear(xd, ih, iw, oh, ow, c)
+    torch.cuda.synchronize()
+    td = torch.float16 if dt == "f16" else torch.bfloat16
+    assert got.dtype == td and tuple(got.shape) == (oh * ow, ld)
+    want = f32.to(td)
+    assert torch.equal(got[:, :c].view(torch.int16), want.view(torch.int16))
+    assert not got[:, c:].float().abs().sum().item()
+    ref = oracle.resize_bilinear(x, ih, iw, oh, ow, c)
+    rel16 = 1e-2 if dt == "bf16" else 1e-3
+    assert np.abs(got[:, :c].float().cpu().numpy().ravel() - ref).max() <= \
+        rel16 * max(1.0, np.abs(ref).max())
+
+
+@pytest.mark.parametrize("side,out_side,c", [(74, 148, 64), (148, 296, 64)])
+def test_projection_of_the_16bit_resampling_equals_the_gathered_one(side, out_side, c):
+    """A fusion layer's resampling + 1x1 projection + the next stage map:
+    from the 16-bit rows of bl_resize_bilinear_rows16 the GEMM alone gives
+    the same bits as the f32 resampling followed by the 1x1 gather."""
+    import torch
+    from beatlm_b200 import ops
+    x = torch.from_numpy(_data(80, side * side * c)).cuda()
+    w = ops.conv_weights(_data(81, c * c, 1.0 / np.sqrt(c)), 1, c, c)
+    b = torch.from_numpy(_data(82, c, 0.1)).cuda()
+    res = torch.from_numpy(_data(83, out_side * out_side * c)).cuda().reshape(-1, c)
+    rows = ops.resize_bilinear_rows16(x, side, side, out_side, out_side, c, w.shape[1])
+    got = ops.conv2d(rows, w, b, out_side, out_side, c, c, ksize=1, residual=res)
+    mid = ops.resize_bilinear(x, side, side, out_side, out_side, c)
+    want = ops.conv2d(mid, w, b, out_side, out_side, c, c, ksize=1, residual=res)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+    with pytest.raises(ValueError):
+        ops.conv2d(rows, w, b, out_side, out_side, c, c, ksize=3)
+    with pytest.raises(ValueError):
+        ops.conv2d(rows[:-1], w, b, out_side, out_side, c, c, ksize=1)
