@@ -250,7 +250,7 @@ class Im2colArgs(ctypes.Structure):
     _fields_ = [("input", ctypes.c_void_p), ("h", ctypes.c_uint32), ("w", ctypes.c_uint32),
                 ("cin", ctypes.c_uint32), ("ksize", ctypes.c_uint32), ("stride", ctypes.c_uint32),
                 ("relu", ctypes.c_uint32), ("out", ctypes.c_void_p), ("out_dtype", ctypes.c_int32),
-                ("k_pad", ctypes.c_uint32)]
+                ("k_pad", ctypes.c_uint32), ("in_dtype", ctypes.c_int32)]
 
 
 class Conv3x3Args(ctypes.Structure):

@@ -225,9 +225,11 @@ __global__ void resize_bilinear_rows16_kernel(const float4* __restrict__ in, uin
 // and the pixel's (y, x) by the grid stride with carries. Consecutive
 // threads still write consecutive 16-byte vectors.
 // Index arithmetic in 32 bits (the host launches it only when every index
-// fits).
-template <typename T>
-__global__ void im2col_vec8_kernel(const float* __restrict__ in, uint4* __restrict__ out, int h,
+// fits). kIn16: the map is already 16-bit of the output's type, and each
+// vector is one 16-byte load copied as it is (ReLU clears the values whose
+// sign bit is set: the bits the f32 path stores for the same rounded map).
+template <typename T, bool kIn16>
+__global__ void im2col_vec8_kernel(const void* __restrict__ in_, uint4* __restrict__ out, int h,
                                    int w, int cin, int ks, int stride, int relu, int oh, int ow,
                                    int k_pad) {
     extern __shared__ int vec_tap[];
@@ -254,27 +256,36 @@ __global__ void im2col_vec8_kernel(const float* __restrict__ in, uint4* __restri
     unsigned pix = v / vecs, j = v - pix * vecs;
     unsigned y = pix / static_cast<unsigned>(ow), x = pix - y * static_cast<unsigned>(ow);
     for (; v < total; v += step) {
-        float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
+        uint4 r = make_uint4(0u, 0u, 0u, 0u);  // the zero border and the padded columns
         const int e = vec_tap[j];
         if (e >= 0) {
             const int ky = e >> 28, kx = (e >> 24) & 15, ci = e & 0xFFFFFF;
             const int iy = static_cast<int>(y) * stride + ky - pad;
             const int ix = static_cast<int>(x) * stride + kx - pad;
             if (iy >= 0 && iy < h && ix >= 0 && ix < w) {
-                const float4* src = reinterpret_cast<const float4*>(
-                    in + (static_cast<long long>(iy) * w + ix) * cin + ci);
-                lo = __ldg(src);
-                hi = __ldg(src + 1);
-                if (relu) {
-                    lo = make_float4(fmaxf(lo.x, 0.f), fmaxf(lo.y, 0.f), fmaxf(lo.z, 0.f), fmaxf(lo.w, 0.f));
-                    hi = make_float4(fmaxf(hi.x, 0.f), fmaxf(hi.y, 0.f), fmaxf(hi.z, 0.f), fmaxf(hi.w, 0.f));
+                const long long off = (static_cast<long long>(iy) * w + ix) * cin + ci;
+                if constexpr (kIn16) {
+                    r = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(in_) + off));
+                    if (relu) {
+                        // a 0xFFFF mask on each 16-bit half whose sign bit is set
+                        auto clear = [](uint32_t u) { return u & ~(((u >> 15) & 0x00010001u) * 0xFFFFu); };
+                        r = make_uint4(clear(r.x), clear(r.y), clear(r.z), clear(r.w));
+                    }
+                } else {
+                    const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(in_) + off);
+                    float4 lo = __ldg(src), hi = __ldg(src + 1);
+                    if (relu) {
+                        lo = make_float4(fmaxf(lo.x, 0.f), fmaxf(lo.y, 0.f), fmaxf(lo.z, 0.f), fmaxf(lo.w, 0.f));
+                        hi = make_float4(fmaxf(hi.x, 0.f), fmaxf(hi.y, 0.f), fmaxf(hi.z, 0.f), fmaxf(hi.w, 0.f));
+                    }
+                    r = make_uint4(to16<T>(lo.x) | (uint32_t(to16<T>(lo.y)) << 16),
+                                   to16<T>(lo.z) | (uint32_t(to16<T>(lo.w)) << 16),
+                                   to16<T>(hi.x) | (uint32_t(to16<T>(hi.y)) << 16),
+                                   to16<T>(hi.z) | (uint32_t(to16<T>(hi.w)) << 16));
                 }
             }
         }
-        out[v] = make_uint4(to16<T>(lo.x) | (uint32_t(to16<T>(lo.y)) << 16),
-                            to16<T>(lo.z) | (uint32_t(to16<T>(lo.w)) << 16),
-                            to16<T>(hi.x) | (uint32_t(to16<T>(hi.y)) << 16),
-                            to16<T>(hi.z) | (uint32_t(to16<T>(hi.w)) << 16));
+        out[v] = r;
         // the next (pixel, vector) and the pixel's (y, x), with carries
         j += step_j;
         unsigned carry = 0;
@@ -362,6 +373,10 @@ int bl_im2col(const bl_im2col_args* a, void* stream) {
     if (a->out_dtype != BL_F16 && a->out_dtype != BL_BF16)
         return fail(BL_ERR_UNSUPPORTED, "im2col: out dtype %d (f16 or bf16)", a->out_dtype);
     if (reinterpret_cast<uintptr_t>(a->out) & 15u) return fail(BL_ERR_INVALID, "im2col: out must be 16-byte aligned");
+    const bool in16 = a->in_dtype != BL_F32;
+    if (in16 && a->in_dtype != a->out_dtype)
+        return fail(BL_ERR_UNSUPPORTED, "im2col: in dtype %d (f32 or the out dtype %d)", a->in_dtype,
+                    a->out_dtype);
     const int pad = static_cast<int>(a->ksize / 2);
     const int oh = static_cast<int>((a->h + 2 * pad - a->ksize) / a->stride + 1);
     const int ow = static_cast<int>((a->w + 2 * pad - a->ksize) / a->stride + 1);
@@ -373,15 +388,29 @@ int bl_im2col(const bl_im2col_args* a, void* stream) {
                      a->k_pad / 8 * sizeof(int) <= 48u * 1024u &&
                      work < (1ll << 31) - 2ll * 256 * 8 * 148 &&
                      1ll * a->h * a->w * a->cin < (1ll << 31);
-    auto kern = vec ? (a->out_dtype == BL_F16 ? dec::im2col_vec8_kernel<__half>
-                                              : dec::im2col_vec8_kernel<__nv_bfloat16>)
-                    : (a->out_dtype == BL_F16 ? dec::im2col_kernel<__half>
-                                              : dec::im2col_kernel<__nv_bfloat16>);
+    if (in16 && !vec)
+        return fail(BL_ERR_UNSUPPORTED,
+                    "im2col: a 16-bit map needs cin a multiple of 8, a 16-byte aligned input and "
+                    "32-bit indices");
     // the vector path's tap table: one word per 8 columns of an output row
     const size_t table = vec ? sizeof(int) * (a->k_pad / 8) : 0;
-    kern<<<dec::grid_for(work), 256, table, s>>>(a->input, static_cast<uint4*>(a->out), a->h,
-                                                a->w, a->cin, a->ksize, a->stride,
-                                                a->relu ? 1 : 0, oh, ow, a->k_pad);
+    const unsigned grid = dec::grid_for(work);
+    const int relu = a->relu ? 1 : 0;
+    uint4* out = static_cast<uint4*>(a->out);
+    if (!vec) {
+        auto kern = a->out_dtype == BL_F16 ? dec::im2col_kernel<__half>
+                                           : dec::im2col_kernel<__nv_bfloat16>;
+        kern<<<grid, 256, 0, s>>>(static_cast<const float*>(a->input), out, a->h, a->w, a->cin,
+                                  a->ksize, a->stride, relu, oh, ow, a->k_pad);
+    } else {
+        auto kern = a->out_dtype == BL_F16
+                        ? (in16 ? dec::im2col_vec8_kernel<__half, true>
+                                : dec::im2col_vec8_kernel<__half, false>)
+                        : (in16 ? dec::im2col_vec8_kernel<__nv_bfloat16, true>
+                                : dec::im2col_vec8_kernel<__nv_bfloat16, false>);
+        kern<<<grid, 256, table, s>>>(a->input, out, a->h, a->w, a->cin, a->ksize, a->stride,
+                                      relu, oh, ow, a->k_pad);
+    }
     BL_CUDA_TRY(cudaGetLastError());
     return BL_OK;
 }

@@ -901,6 +901,12 @@ def decoder_weights_random(cfg: ViTConfig, dcfg: DecoderConfig, seed: int = 0) -
     return out
 
 
+def _dt_name(weights) -> str:
+    """The 16-bit operand type of a convolution's weights, by name."""
+    import torch
+    return "f16" if weights.dtype == torch.float16 else "bf16"
+
+
 class Decoder:
     """The DPT head on NHWC f32 maps (model/depth_anything_v2.rs:680-982): per
     stage a 1x1 reassembly convolution and its resampling, a 3x3 convolution
@@ -949,7 +955,11 @@ class Decoder:
 
     def _unit(self, x, u, side, residual=None):
         F = self.dcfg.fusion
-        first = ops.conv2d(x, u[0], u[1], side, side, F, F, relu_input=True)
+        # the first convolution's only reader is the second one's gather: its
+        # map is stored in the operands' 16 bits (the one rounding the gather
+        # of an f32 map would make), half the bytes written and read
+        first = ops.conv2d(x, u[0], u[1], side, side, F, F, relu_input=True,
+                           out_dtype=_dt_name(u[0]))
         return ops.conv2d(first, u[2], u[3], side, side, F, F, relu_input=True,
                           residual=x if residual is None else residual)
 
@@ -963,7 +973,6 @@ class Decoder:
             return self._forward(features)
 
     def _forward(self, features: list):
-        import torch
         stream = None  # the current stream, for every op
         cfg, F = self.cfg, self.dcfg.fusion
         g = cfg.grid
@@ -997,15 +1006,20 @@ class Decoder:
             # separate passes, two launches fewer
             pw = f["proj"][0]
             x = ops.resize_bilinear_rows16(x, s, s, out_side, out_side, F, pw.shape[1],
-                                           "f16" if pw.dtype == torch.float16 else "bf16",
-                                           stream)
+                                           _dt_name(pw), stream)
+            # the last layer's map feeds only the head's first convolution:
+            # 16 bits, as for a unit's first convolution
             fused = ops.conv2d(x, pw, f["proj"][1], out_side, out_side, F, F, ksize=1,
-                               residual=maps[nxt][0] if nxt >= 0 else None)
+                               residual=maps[nxt][0] if nxt >= 0 else None,
+                               out_dtype="f32" if nxt >= 0 else _dt_name(pw))
             side = out_side
         out_side = g * cfg.patch
         h = self.head
         x = ops.conv2d(fused, h["c1"][0], h["c1"][1], side, side, F, F // 2)
-        x = ops.resize_bilinear(x, side, side, out_side, out_side, F // 2, stream)
+        # the resampling to full size stored in 16 bits, gathered as it is by
+        # the next convolution (the same bits as an f32 map gathered)
+        x = ops.resize_bilinear_rows16(x, side, side, out_side, out_side, F // 2, F // 2,
+                                       _dt_name(h["c2"][0]), stream)
         x = ops.conv2d(x, h["c2"][0], h["c2"][1], out_side, out_side, F // 2, self.dcfg.head,
                        act="relu")
         x = ops.conv1x1_one(x, h["c3"][0], h["c3"][1], out_side * out_side, self.dcfg.head,

@@ -276,27 +276,32 @@ def conv_weights(hwio, ksize: int, cin: int, cout: int, dtype: str = "f16", devi
 
 def im2col(x, h: int, w: int, cin: int, ksize: int = 3, stride: int = 1, relu: bool = False,
            k_pad: int | None = None, dtype: str = "f16", stream=None):
-    """``bl_im2col``: the [oh * ow][k_pad] 16-bit rows of an NHWC f32 map."""
+    """``bl_im2col``: the [oh * ow][k_pad] 16-bit rows of an NHWC map, f32 or
+    already 16-bit of ``dtype`` (copied as it is)."""
     import torch
     pad = ksize // 2
     oh, ow = (h + 2 * pad - ksize) // stride + 1, (w + 2 * pad - ksize) // stride + 1
     k_pad = k_pad or _round_up(ksize * ksize * cin, 64)
     td = torch.float16 if dtype == "f16" else torch.bfloat16
+    if x.dtype != torch.float32 and x.dtype != td:
+        raise ValueError("im2col: the map is f32 or of the output dtype")
     out = torch.empty((oh * ow, k_pad), dtype=td, device=x.device)
     a = N.Im2colArgs(input=x.data_ptr(), h=h, w=w, cin=cin, ksize=ksize, stride=stride,
-                     relu=1 if relu else 0, out=out.data_ptr(), out_dtype=_TD[dtype], k_pad=k_pad)
+                     relu=1 if relu else 0, out=out.data_ptr(), out_dtype=_TD[dtype], k_pad=k_pad,
+                     in_dtype=N.BL_F32 if x.dtype == torch.float32 else _TD[dtype])
     N.check(N.lib().bl_im2col(ctypes.byref(a), _stream_ptr(stream)))
     return out, oh, ow
 
 
 def conv2d(x, weights, bias, h: int, w: int, cin: int, cout: int, *, ksize: int = 3,
            stride: int = 1, relu_input: bool = False, act=None, residual=None, stream=None,
-           implicit: bool | None = None, split_k: int = 0):
+           implicit: bool | None = None, split_k: int = 0, out_dtype: str = "f32"):
     """A 3x3 (zero padding 1) or 1x1 convolution of the NHWC f32 map ``x``:
     ``weights`` from ``conv_weights``, ``bias`` f32 [cout] or None, ``act``
     "relu" on the result, ``residual`` an f32 [oh * ow][cout] map added last
-    (cout a multiple of 32). Returns f32 [oh * ow][cout]. A 1x1 convolution
-    also takes ``x`` as 16-bit rows [h * w][k_pad] of the weights' dtype
+    (cout a multiple of 32). Returns f32 [oh * ow][cout]. ``x`` may also be a
+    16-bit map of the weights' dtype (gathered without a rounding), and for a
+    1x1 convolution the GEMM's 16-bit rows [h * w][k_pad]
     (``resize_bilinear_rows16``), multiplied as they are.
 
     ``implicit=True``: a 3x3 stride-1 convolution of a multiple of 32
@@ -308,19 +313,23 @@ def conv2d(x, weights, bias, h: int, w: int, cin: int, cout: int, *, ksize: int 
     since the implicit kernel's f32 image tiles take about 1 us per TMA round
     trip, more than a three-stage ring hides, and are converted to 16 bits
     on chip for every tap. ``split_k``: as ``gemm_args`` (the gathered
-    form's GEMM)."""
+    form's GEMM). ``out_dtype`` "f16" or "bf16": the result rounded once to
+    16 bits in the epilogue (the bits a gather of the f32 result would
+    store, for a map whose only reader is the next convolution)."""
     import torch
     dt = "f16" if weights.dtype == torch.float16 else "bf16"
+    rows16 = False
     if x.dtype in (torch.float16, torch.bfloat16):
-        # 16-bit rows already in the GEMM's layout (resize_bilinear_rows16):
-        # a 1x1 convolution of them is the GEMM alone
-        if ksize != 1 or stride != 1 or relu_input or implicit:
-            raise ValueError("conv2d: 16-bit rows take a 1x1, stride-1 convolution without "
-                             "an input ReLU")
-        if (x.dtype != weights.dtype or tuple(x.shape) != (h * w, weights.shape[1])
-                or not x.is_contiguous() or cin > weights.shape[1]):
-            raise ValueError("conv2d: 16-bit rows must be [h * w][k_pad] of the weights' dtype, "
-                             "contiguous")
+        if x.dtype != weights.dtype or not x.is_contiguous() or implicit:
+            raise ValueError("conv2d: a 16-bit map must be of the weights' dtype, contiguous, "
+                             "and gathered (not implicit)")
+        # the GEMM's rows already (resize_bilinear_rows16): a 1x1 convolution
+        # of them is the GEMM alone; any other 16-bit map is gathered as it is
+        rows16 = (ksize == 1 and stride == 1 and not relu_input
+                  and tuple(x.shape) == (h * w, weights.shape[1]))
+        if not rows16 and x.numel() != h * w * cin:
+            raise ValueError("conv2d: a 16-bit map must be [h * w][cin], or for a 1x1 "
+                             "convolution the GEMM's [h * w][k_pad] rows")
         implicit = False
     can = (ksize == 3 and stride == 1 and cin % 32 == 0 and x.dtype == torch.float32
            and x.is_contiguous() and x.data_ptr() % 16 == 0)
@@ -330,7 +339,7 @@ def conv2d(x, weights, bias, h: int, w: int, cin: int, cout: int, *, ksize: int 
         raise ValueError("conv2d: the implicit form takes 3x3, stride 1, channels a multiple of 32")
     if implicit:
         cols, oh, ow = None, h, w
-    elif x.dtype in (torch.float16, torch.bfloat16):
+    elif rows16:
         cols, oh, ow = x, h, w
     else:
         cols, oh, ow = im2col(x, h, w, cin, ksize, stride, relu_input, weights.shape[1], dt,
@@ -349,7 +358,8 @@ def conv2d(x, weights, bias, h: int, w: int, cin: int, cout: int, *, ksize: int 
                                  and bias.device == x.device and bias.numel() == n_pad):
         bias_pad = torch.zeros(n_pad, dtype=torch.float32, device=x.device)
         bias_pad[:cout] = bias.reshape(-1)[:cout].to(device=x.device, dtype=torch.float32)
-    out = torch.empty((oh * ow, n_pad), dtype=torch.float32, device=x.device)
+    otd = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[out_dtype]
+    out = torch.empty((oh * ow, n_pad), dtype=otd, device=x.device)
     g = gemm_args(weights, a=cols, m=oh * ow, bias=bias_pad, act=act, residual=residual,
                   out=out, split_k=split_k)
     if implicit:

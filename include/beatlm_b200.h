@@ -677,7 +677,7 @@ int bl_stream_hold(void* stream, uint32_t microseconds);
  * bl_blocks_to_map. Each call enqueues on `stream`.
  */
 typedef struct bl_im2col_args {
-    const float* input;  /* [h][w][cin] f32 */
+    const void* input;   /* [h][w][cin] of in_dtype */
     uint32_t h, w, cin;
     uint32_t ksize;      /* 1 or 3 (3: zero padding 1) */
     uint32_t stride;     /* output pixel (y, x) centred on input (y stride, x stride) */
@@ -685,6 +685,8 @@ typedef struct bl_im2col_args {
     void* out;           /* [oh * ow][k_pad] 16-bit, 16-byte aligned */
     int32_t out_dtype;   /* BL_F16 or BL_BF16 */
     uint32_t k_pad;      /* multiple of 64, >= ksize * ksize * cin; columns past it are 0 */
+    int32_t in_dtype;    /* BL_F32 (0, the default), or out_dtype: a 16-bit map copied as it
+                            is (cin a multiple of 8, input 16-byte aligned) */
 } bl_im2col_args;
 int bl_im2col(const bl_im2col_args* args, void* stream);
 /* A 3x3 convolution, stride 1, zero padding 1, of an NHWC f32 image as an

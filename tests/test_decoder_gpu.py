@@ -370,6 +370,48 @@ def test_projection_of_the_16bit_resampling_equals_the_gathered_one(side, out_si
     torch.cuda.synchronize()
     assert torch.equal(got, want)
     with pytest.raises(ValueError):
-        ops.conv2d(rows, w, b, out_side, out_side, c, c, ksize=3)
-    with pytest.raises(ValueError):
         ops.conv2d(rows[:-1], w, b, out_side, out_side, c, c, ksize=1)
+    with pytest.raises(ValueError):
+        ops.conv2d(rows, w, b, out_side, out_side, c, c, ksize=1, implicit=True)
+
+
+@pytest.mark.parametrize("side,c,relu,dt", [(518, 32, False, "f16"), (74, 64, True, "f16"),
+                                            (37, 48, True, "bf16"), (9, 8, False, "bf16")])
+def test_gather_of_a_16bit_map_equals_the_gather_of_its_f32_map(side, c, relu, dt):
+    """bl_im2col of a 16-bit map (the head's resampling written by
+    bl_resize_bilinear_rows16) gives the same bits as the gather of the same
+    values in f32, ReLU included, and so the same 3x3 convolution."""
+    import torch
+    from beatlm_b200 import ops
+    td = torch.float16 if dt == "f16" else torch.bfloat16
+    m16 = torch.from_numpy(_data(84, side * side * c)).cuda().to(td).reshape(-1, c)
+    m32 = m16.float()
+    got, _, _ = ops.im2col(m16, side, side, c, 3, 1, relu, dtype=dt)
+    want, _, _ = ops.im2col(m32, side, side, c, 3, 1, relu, dtype=dt)
+    torch.cuda.synchronize()
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+    wt = ops.conv_weights(_data(85, 9 * c * 32, 1.0 / np.sqrt(9 * c)), 3, c, 32, dtype=dt)
+    b = torch.from_numpy(_data(86, 32, 0.1)).cuda()
+    y16 = ops.conv2d(m16, wt, b, side, side, c, 32, relu_input=relu, act="relu")
+    y32 = ops.conv2d(m32, wt, b, side, side, c, 32, relu_input=relu, act="relu")
+    torch.cuda.synchronize()
+    assert torch.equal(y16, y32)
+
+
+@pytest.mark.parametrize("side,cin,cout,dt", [(148, 64, 64, "f16"), (37, 64, 48, "bf16")])
+def test_conv_16bit_output_is_the_rounded_f32_output(side, cin, cout, dt):
+    """conv2d(out_dtype=16-bit) (a fusion unit's first convolution, whose only
+    reader is the next gather) stores the f32 result rounded once to nearest
+    even: the bits the gather of the f32 map would store."""
+    import torch
+    from beatlm_b200 import ops
+    td = torch.float16 if dt == "f16" else torch.bfloat16
+    x = torch.from_numpy(_data(87, side * side * cin)).cuda()
+    wt = ops.conv_weights(_data(88, 9 * cin * cout, 1.0 / np.sqrt(9 * cin)), 3, cin, cout,
+                          dtype=dt)
+    b = torch.from_numpy(_data(89, cout, 0.1)).cuda()
+    got = ops.conv2d(x, wt, b, side, side, cin, cout, relu_input=True, out_dtype=dt)
+    want = ops.conv2d(x, wt, b, side, side, cin, cout, relu_input=True)
+    torch.cuda.synchronize()
+    assert got.dtype == td and tuple(got.shape) == (side * side, cout)
+    assert torch.equal(got.view(torch.int16), want.to(td).view(torch.int16))
