@@ -1043,14 +1043,17 @@ class DecoderWorkload:
                   for _ in range(2)]
         k_pad = self.w[0].shape[1]
         self.cols = torch.empty((px, k_pad), dtype=torch.float16, device="cuda")
-        self.mid = torch.empty((px, c), dtype=torch.float32, device="cuda")
+        # the first convolution's map is read only by the second one's gather:
+        # stored in f16 by its epilogue and copied as it is by the gather
+        # (model.Decoder's residual unit; the same bits as an f32 map)
+        self.mid = torch.empty((px, c), dtype=torch.float16, device="cuda")
         self.out = torch.empty((px, c), dtype=torch.float32, device="cuda")
         self.host = self.x.cpu().pin_memory()
         self.out_host = torch.empty((px, c), dtype=torch.float32).pin_memory()
-        mk = lambda src: N.Im2colArgs(input=src.data_ptr(), h=side, w=side, cin=c, ksize=3,
-                                      stride=1, relu=1, out=self.cols.data_ptr(),
-                                      out_dtype=N.BL_F16, k_pad=k_pad)
-        self.i2c = [mk(self.x), mk(self.mid)]
+        mk = lambda src, dt: N.Im2colArgs(input=src.data_ptr(), h=side, w=side, cin=c, ksize=3,
+                                          stride=1, relu=1, out=self.cols.data_ptr(),
+                                          out_dtype=N.BL_F16, k_pad=k_pad, in_dtype=dt)
+        self.i2c = [mk(self.x, N.BL_F32), mk(self.mid, N.BL_F16)]
         self.g = [ops.gemm_args(self.w[0], a=self.cols, bias=self.b[0], out=self.mid),
                   ops.gemm_args(self.w[1], a=self.cols, bias=self.b[1], residual=self.x,
                                 out=self.out)]
