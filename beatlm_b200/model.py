@@ -979,14 +979,22 @@ class Decoder:
         maps = []
         for feat, st in zip(features, self.stages):
             c = st["c"]
-            x = ops.conv2d(feat, st["proj"][0], st["proj"][1], g, g, cfg.dim, c, ksize=1)
+            # the reassembly projection's only reader is the next gather or
+            # GEMM: its map in the operands' 16 bits, with the padded output
+            # channels (zeros), which at 48 channels are the transposed
+            # convolution's GEMM rows (no narrowing copy, no gather)
+            dt = _dt_name(st["proj"][0])
+            x = ops.conv2d(feat, st["proj"][0], st["proj"][1], g, g, cfg.dim, c, ksize=1,
+                           out_dtype=dt, padded=True)
             side = g
             kind = st["resample"]
             if kind[0] == "up":
-                x = ops.conv_transpose(x, st["resize"][0], st["resize"][1], g, g, c, c, kind[1])
+                x = ops.conv_transpose(x, st["resize"][0], st["resize"][1], g, g, c, c, kind[1],
+                                       dtype=dt)
                 side = g * kind[1]
             elif kind[0] == "down":
-                x = ops.conv2d(x, st["resize"][0], st["resize"][1], g, g, c, c, stride=kind[1])
+                x = ops.conv2d(x, st["resize"][0], st["resize"][1], g, g, c, c, stride=kind[1],
+                               out_dtype=dt)
                 side = (g - 1) // kind[1] + 1
             maps.append((ops.conv2d(x, st["neck"], None, side, side, c, F), side))
         fused, side = None, None

@@ -295,7 +295,8 @@ def im2col(x, h: int, w: int, cin: int, ksize: int = 3, stride: int = 1, relu: b
 
 def conv2d(x, weights, bias, h: int, w: int, cin: int, cout: int, *, ksize: int = 3,
            stride: int = 1, relu_input: bool = False, act=None, residual=None, stream=None,
-           implicit: bool | None = None, split_k: int = 0, out_dtype: str = "f32"):
+           implicit: bool | None = None, split_k: int = 0, out_dtype: str = "f32",
+           padded: bool = False):
     """A 3x3 (zero padding 1) or 1x1 convolution of the NHWC f32 map ``x``:
     ``weights`` from ``conv_weights``, ``bias`` f32 [cout] or None, ``act``
     "relu" on the result, ``residual`` an f32 [oh * ow][cout] map added last
@@ -315,7 +316,10 @@ def conv2d(x, weights, bias, h: int, w: int, cin: int, cout: int, *, ksize: int 
     on chip for every tap. ``split_k``: as ``gemm_args`` (the gathered
     form's GEMM). ``out_dtype`` "f16" or "bf16": the result rounded once to
     16 bits in the epilogue (the bits a gather of the f32 result would
-    store, for a map whose only reader is the next convolution)."""
+    store, for a map whose only reader is the next convolution). ``padded``:
+    the result with all the weights' padded output channels (zeros), as
+    [oh * ow][n_pad], which with 16 bits and n_pad = cout rounded up to 64 is
+    the next 1x1 GEMM's rows."""
     import torch
     dt = "f16" if weights.dtype == torch.float16 else "bf16"
     rows16 = False
@@ -367,7 +371,7 @@ def conv2d(x, weights, bias, h: int, w: int, cin: int, cout: int, *, ksize: int 
         N.check(N.lib().bl_conv3x3(ctypes.byref(g), ctypes.byref(c), _stream_ptr(stream)))
     else:
         N.check(N.lib().bl_gemm(ctypes.byref(g), _stream_ptr(stream)))
-    return out if n_pad == cout else out[:, :cout].contiguous()
+    return out if n_pad == cout or padded else out[:, :cout].contiguous()
 
 
 def conv_transpose_weights(hwio, cin: int, cout: int, f: int, dtype: str = "f16",
@@ -389,12 +393,21 @@ def conv_transpose(x, hwio, bias, h: int, w: int, cin: int, cout: int, f: int,
     each pixel by the [(ky f + kx) cout + co][ci] weights, then the f x f
     blocks scattered into the [h f][w f][cout] map with the bias. ``hwio`` is
     the HWIO array, or its device matrix from ``conv_transpose_weights``
-    (which a CUDA graph capture needs: nothing then crosses from the host)."""
+    (which a CUDA graph capture needs: nothing then crosses from the host).
+    ``x`` may also be 16-bit of ``dtype``: a map [h * w][cin] (gathered as it
+    is), or the GEMM's rows [h * w][cin rounded up to 64] (used as they are,
+    e.g. ``conv2d(..., out_dtype=dtype, padded=True)``)."""
     import torch
     n = f * f * cout
     if n % 32 != 0:
         raise ValueError("conv_transpose: f * f * cout must be a multiple of 32")
-    cols, _, _ = im2col(x, h, w, cin, 1, 1, False, None, dtype, stream)
+    k_pad = _round_up(cin, 64)
+    if x.dtype != torch.float32 and tuple(x.shape) == (h * w, k_pad) and x.is_contiguous():
+        if x.dtype != (torch.float16 if dtype == "f16" else torch.bfloat16):
+            raise ValueError("conv_transpose: 16-bit rows must be of the weights' dtype")
+        cols = x
+    else:
+        cols, _, _ = im2col(x, h, w, cin, 1, 1, False, None, dtype, stream)
     if isinstance(hwio, torch.Tensor) and hwio.dim() == 2:
         wdev = hwio
     else:

@@ -415,3 +415,28 @@ def test_conv_16bit_output_is_the_rounded_f32_output(side, cin, cout, dt):
     torch.cuda.synchronize()
     assert got.dtype == td and tuple(got.shape) == (side * side, cout)
     assert torch.equal(got.view(torch.int16), want.to(td).view(torch.int16))
+
+
+@pytest.mark.parametrize("c,f", [(48, 4), (96, 2)])
+def test_reassembly_in_16_bits_equals_the_f32_chain(c, f):
+    """A reassembly stage (1x1 projection, then the transposed convolution):
+    the projection's map stored in f16 with its padded channels (48 -> the
+    64-column GEMM rows, used as they are) or as a 16-bit map (96, gathered as
+    it is) gives the same bits as the f32 map narrowed and gathered."""
+    import torch
+    from beatlm_b200 import ops
+    g, dim = 37, 384
+    feat = torch.from_numpy(_data(92, g * g * dim)).cuda()
+    pw = ops.conv_weights(_data(93, dim * c, 1.0 / np.sqrt(dim)), 1, dim, c)
+    pb = torch.zeros(pw.shape[0], dtype=torch.float32, device="cuda")
+    pb[:c] = torch.from_numpy(_data(94, c, 0.1)).cuda()
+    tw = ops.conv_transpose_weights(_data(95, f * f * c * c, 1.0 / np.sqrt(c)), c, c, f)
+    tb = torch.from_numpy(_data(96, c, 0.1)).cuda()
+    x16 = ops.conv2d(feat, pw, pb, g, g, dim, c, ksize=1, out_dtype="f16", padded=True)
+    x32 = ops.conv2d(feat, pw, pb, g, g, dim, c, ksize=1)
+    got = ops.conv_transpose(x16, tw, tb, g, g, c, c, f)
+    want = ops.conv_transpose(x32, tw, tb, g, g, c, c, f)
+    torch.cuda.synchronize()
+    assert tuple(x16.shape) == (g * g, pw.shape[0]) and tuple(x32.shape) == (g * g, c)
+    assert not x16[:, c:].float().abs().sum().item()
+    assert torch.equal(got, want)
