@@ -953,6 +953,28 @@ class Decoder:
                      "c3": (dev(np.asarray(h["w3"], np.float32).reshape(dcfg.head)),
                             float(np.asarray(h["b3"], np.float32).reshape(-1)[0]))}
 
+    def launches_per_frame(self) -> int:
+        """The kernels one ``forward`` launches: a convolution is a gather and
+        a GEMM, except a 1x1 one of 16-bit GEMM rows (the GEMM alone); a
+        transposed convolution adds its block scatter; a resampling is one
+        launch; the last 1x1 convolution to one channel is one."""
+        n = 0
+        for st in self.stages:
+            n += 2 + 2  # the projection and the neck convolution
+            kind = st["resample"][0]
+            if kind == "up":
+                # the projection's padded 16-bit output is the GEMM's rows
+                # when its width is cin rounded up to 64 (see _forward)
+                rows = st["proj"][0].shape[0] == -(-st["c"] // 64) * 64
+                n += 2 if rows else 3
+            elif kind == "down":
+                n += 2
+        for layer in range(len(self.fusion)):
+            # one residual unit in the deepest layer, two after it; the
+            # resampling writes the projection's rows
+            n += (4 if layer == 0 else 8) + 1 + 1
+        return n + 2 + 1 + 2 + 1  # head: 3x3, resampling, 3x3, 1x1 to one channel
+
     def _unit(self, x, u, side, residual=None):
         F = self.dcfg.fusion
         # the first convolution's only reader is the second one's gather: its
