@@ -16,3 +16,24 @@ def test_head_launch_count_follows_its_structure():
                 for c, rs in zip(dc.neck, dc.reassemble)]
     d.fusion = [None] * len(dc.neck)
     assert d.launches_per_frame() == 65
+
+
+def test_16bit_map_arguments_are_checked_before_any_launch():
+    """Malformed 16-bit maps are errors on the host (no device needed): a map
+    of another dtype than the weights, rows of the wrong shape, a 16-bit map
+    for the implicit convolution, and a gather of a map of a third dtype."""
+    import pytest
+    from beatlm_b200 import ops
+    w = torch.zeros((64, 64), dtype=torch.float16)  # 1x1, 64 -> 64, k_pad 64
+    with pytest.raises(ValueError):
+        ops.conv2d(torch.zeros((16, 64), dtype=torch.bfloat16), w, None, 4, 4, 64, 64, ksize=1)
+    with pytest.raises(ValueError):
+        ops.conv2d(torch.zeros((15, 64), dtype=torch.float16), w, None, 4, 4, 64, 64, ksize=1)
+    with pytest.raises(ValueError):
+        ops.conv2d(torch.zeros((16, 64), dtype=torch.float16), w, None, 4, 4, 64, 64, ksize=1,
+                   implicit=True)
+    with pytest.raises(ValueError):
+        ops.im2col(torch.zeros((16, 64), dtype=torch.bfloat16), 4, 4, 64, 3, dtype="f16")
+    with pytest.raises(ValueError):
+        ops.conv_transpose(torch.zeros((16, 64), dtype=torch.bfloat16),
+                           torch.zeros((16 * 48, 64), dtype=torch.float16), None, 4, 4, 48, 48, 4)
