@@ -120,7 +120,8 @@ class GemmArgs(ctypes.Structure):
         ("weights_static", ctypes.c_uint32), ("trace", ctypes.c_void_p),
         ("pair_tiles", ctypes.c_uint32), ("split_k", ctypes.c_uint32),
         ("stream_k", ctypes.c_uint32), ("workspace", ctypes.c_void_p),
-        ("workspace_bytes", ctypes.c_uint64),
+        ("workspace_bytes", ctypes.c_uint64), ("dot_w", ctypes.c_void_p),
+        ("dot_bias", ctypes.c_float), ("dot_act", ctypes.c_int32),
     ]
 
 

@@ -91,6 +91,11 @@ struct Params {
     // columns and conv_pix pixels, conv_cin channels; K columns past conv_k
     // (9 cin) are zero; conv_relu: max(x, 0) on every input value
     int conv_w, conv_pix, conv_cin, conv_k, conv_relu;
+    // row reduction (generic epilogue, one column tile): out[row] =
+    // act2(sum_c v[c] dot_w[c] + dot_bias), no row stored
+    const float* dot_w;
+    float dot_bias;
+    int dot_act;
     Status* status;
 };
 
@@ -299,6 +304,7 @@ __device__ __forceinline__ void store_tile(const Params& p, const Tail* tail, ui
     const size_t res_esz = p.res_dtype == BL_F32 ? 4 : 2;
     const int lane = lane_id();
     float run_mean = 0.0f, run_m2 = 0.0f;  // row statistics of the stored slice
+    float dacc = 0.0f;                     // row reduction (dot_w), in column order
     const bool add_res = (EPI < 0 ? p.residual != nullptr : EPI == 2) && live;
     // stream-K: the chunk's residual, the first chunk's from the caller (so
     // rv0 is not live across the loop), later ones loaded with the partials
@@ -403,6 +409,26 @@ __device__ __forceinline__ void store_tile(const Params& p, const Tail* tail, ui
 #pragma unroll
                     for (int i = 0; i < 16; ++i) v[16 * h + i] += rv[i];
                 }
+            }
+        }
+        if constexpr (EPI < 0 && kParts == 0) {
+            if (p.dot_w != nullptr) {
+                // the row reduced to one value (the host allows one column
+                // tile, no tensor-map store, no statistics): nothing stored
+                // but the last chunk's sum
+#pragma unroll
+                for (int i = 0; i < 32; i += 4) {
+                    const float4 w = __ldg(reinterpret_cast<const float4*>(p.dot_w + col + i));
+                    dacc = fmaf(v[i], w.x, dacc);
+                    dacc = fmaf(v[i + 1], w.y, dacc);
+                    dacc = fmaf(v[i + 2], w.z, dacc);
+                    dacc = fmaf(v[i + 3], w.w, dacc);
+                }
+                if (c == BN / 32 - 1 && live) {
+                    const float y = dacc + p.dot_bias;
+                    static_cast<float*>(p.out)[orow] = p.dot_act ? fmaxf(y, 0.0f) : y;
+                }
+                continue;
             }
         }
         if (EPI < 0 && p.stats_out != nullptr) {
@@ -2353,6 +2379,23 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
             return fail(BL_ERR_UNSUPPORTED, "gemm: the epilogue LayerNorm needs 32-column tiles");
         bn = 32;
     }
+    const bool dot = g.dot_w != nullptr;
+    if (dot) {
+        if (g.n > 128 || (g.tile_n && g.tile_n != g.n))
+            return fail(BL_ERR_UNSUPPORTED, "gemm: a row reduction takes one column tile (N=%u, "
+                                            "at most 128)", g.n);
+        if (g.out_dtype != BL_F32 || (g.split_col > 0 && g.split_col < g.n) ||
+            g.out_group_rows != 0 || g.out_row_offset != 0 || g.stats_out != nullptr || norm ||
+            g.ln_x != nullptr || g.pair_tiles == 2 || g.split_k == 2 || g.stream_k == 2)
+            return fail(BL_ERR_UNSUPPORTED,
+                        "gemm: a row reduction needs an f32 output of one type without row groups "
+                        "or offset, and no statistics, LayerNorm, CTA pairs, K split or stream-K");
+        if (g.dot_act != 0 && g.dot_act != 1)
+            return fail(BL_ERR_INVALID, "gemm: row reduction activation %d (0 or 1)", g.dot_act);
+        if (reinterpret_cast<uintptr_t>(g.dot_w) & 15)
+            return fail(BL_ERR_INVALID, "gemm: row reduction weights must be 16-byte aligned");
+        bn = static_cast<int>(g.n);
+    }
     if (bn == 0 || g.n % bn != 0 ||
         (bn != 32 && bn != 64 && bn != 96 && bn != 128 && bn != 256))
         return fail(BL_ERR_UNSUPPORTED, "gemm: N=%u has no tile width (32/64/96/128/256)", g.n);
@@ -2460,7 +2503,7 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
     // K >= 1024 with N <= 512 in 64-column tiles, a rule of the shape alone so
     // row parts split exactly as their whole launch): 64-column tiles.
     if (g.split_k > 2) return fail(BL_ERR_INVALID, "gemm: split_k %u (0, 1 or 2)", g.split_k);
-    const bool split_ok = !ln && !norm && conv == nullptr && g.a != nullptr &&
+    const bool split_ok = !ln && !norm && !dot && conv == nullptr && g.a != nullptr &&
                           g.stats_out == nullptr && !pair && g.n % 64 == 0 &&
                           (g.tile_n == 0 || g.tile_n == 64) && g.k / BK >= 4;
     // (the automatic rule also asks that both CTAs of every tile of the whole
@@ -2575,6 +2618,11 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
         return fail(BL_ERR_INVALID, "gemm: row part [%u, %u) is not whole 128-row tiles", row_begin, row_end);
     p.status = status_ptr();
     p.trace = reinterpret_cast<unsigned long long*>(g.trace);
+    if (dot) {
+        p.dot_w = g.dot_w;
+        p.dot_bias = g.dot_bias;
+        p.dot_act = g.dot_act;
+    }
     if (pieces > 1) {
         p.sk_pieces = pieces;
         p.sk_flag = static_cast<unsigned*>(g.workspace);
@@ -2616,7 +2664,7 @@ int prepare(const bl_gemm_args& g, uint32_t row_begin, uint32_t row_end, Launch*
     // array of a single element size (no row groups).
     CUtensorMap to{};
     const int esz = static_cast<int>(dtype_size(dts[0]));
-    if (g.out_group_rows == 0 && dtype_size(dts[1]) == dtype_size(dts[0])) {
+    if (!dot && g.out_group_rows == 0 && dtype_size(dts[1]) == dtype_size(dts[0])) {
         const uint64_t dims[2] = {g.n, static_cast<uint64_t>(g.m) + g.out_row_offset};
         const uint32_t box[2] = {32, 32};
         if ((rc = make_tmap_2d(&to, g.out, esz, dims, out_ld * esz, box,

@@ -947,7 +947,8 @@ class Decoder:
                        for f in weights["fusion"]]
         h = weights["head"]
         # the last convolution (head width -> 1 channel, 1x1) as a per-pixel
-        # dot product in f32 (bl_conv1x1_one): its weights as a vector
+        # dot product in f32 in the epilogue of the one before: its weights
+        # as a vector
         self.head = {"c1": (ops.conv_weights(h["w1"], 3, F, F // 2), dev(h["b1"])),
                      "c2": (ops.conv_weights(h["w2"], 3, F // 2, dcfg.head), dev(h["b2"])),
                      "c3": (dev(np.asarray(h["w3"], np.float32).reshape(dcfg.head)),
@@ -957,7 +958,8 @@ class Decoder:
         """The kernels one ``forward`` launches: a convolution is a gather and
         a GEMM, except a 1x1 one of 16-bit GEMM rows (the GEMM alone); a
         transposed convolution adds its block scatter; a resampling is one
-        launch; the last 1x1 convolution to one channel is one."""
+        launch; the last 1x1 convolution to one channel runs in the epilogue
+        of the convolution before it."""
         n = 0
         for st in self.stages:
             n += 2 + 2  # the projection and the neck convolution
@@ -973,7 +975,7 @@ class Decoder:
             # one residual unit in the deepest layer, two after it; the
             # resampling writes the projection's rows
             n += (4 if layer == 0 else 8) + 1 + 1
-        return n + 2 + 1 + 2 + 1  # head: 3x3, resampling, 3x3, 1x1 to one channel
+        return n + 2 + 1 + 2  # head: 3x3, resampling, 3x3 with the 1x1 to one channel
 
     def _unit(self, x, u, side, residual=None):
         F = self.dcfg.fusion
@@ -1050,10 +1052,12 @@ class Decoder:
         # the next convolution (the same bits as an f32 map gathered)
         x = ops.resize_bilinear_rows16(x, side, side, out_side, out_side, F // 2, F // 2,
                                        _dt_name(h["c2"][0]), stream)
+        # the last 1x1 convolution to one channel (with its ReLU) in this
+        # convolution's epilogue: each pixel's head-width values are one
+        # accumulator row of one tile, reduced there, and the full-size map
+        # of head-width channels never reaches memory
         x = ops.conv2d(x, h["c2"][0], h["c2"][1], out_side, out_side, F // 2, self.dcfg.head,
-                       act="relu")
-        x = ops.conv1x1_one(x, h["c3"][0], h["c3"][1], out_side * out_side, self.dcfg.head,
-                            relu=True)
+                       act="relu", dot=(h["c3"][0], h["c3"][1], True))
         return x.reshape(out_side, out_side)
 
     def capture(self, features: list, stream):

@@ -135,7 +135,7 @@ def gemm_args(w, *, a=None, ln=None, bias=None, act=None, scale=None, chan_scale
               residual=None, res_period=0, out, out_dtype=None, out_split=None, m=None,
               out_row_offset=0, out_group=(0, 0), tile_n=0, stats_out=None, ln_stats=None,
               norm=None, norm_sync=None, weights_static=False, pair_tiles=0, split_k=0,
-              stream_k=0, workspace=None):
+              stream_k=0, workspace=None, dot=None):
     """``stats_out``: a float32 ``[rows][parts][2]`` tensor the epilogue fills
     with per-slice (mean, M2) of each stored row (``parts`` = n / tile width).
     ``ln_stats``: such a tensor for ``ln``'s input, used instead of a pass
@@ -150,7 +150,10 @@ def gemm_args(w, *, a=None, ln=None, bias=None, act=None, scale=None, chan_scale
     tiles' k-stages cut into pieces dealt over the SMs (0 or 1: whole
     tiles); ``workspace``: its zero-filled device tensor of at least
     ``gemm_workspace_bytes(args)`` bytes, which each launch leaves
-    zero-filled."""
+    zero-filled. ``dot=(w, bias, relu)``: each finished row reduced to
+    one f32 value, relu(sum_c row[c] w[c] + bias) when relu, written to
+    ``out`` (an f32 tensor of m values) in place of the row
+    (``bl_gemm_args.dot_w``)."""
     import torch
     n, k = w.shape
     ab = {torch.float16: "f16", torch.bfloat16: "bf16"}[w.dtype]
@@ -171,6 +174,14 @@ def gemm_args(w, *, a=None, ln=None, bias=None, act=None, scale=None, chan_scale
                    out_group_gap=out_group[1], tile_n=tile_n,
                    weights_static=1 if weights_static else 0, pair_tiles=pair_tiles,
                    split_k=split_k, stream_k=stream_k)
+    if dot is not None:
+        dw, db, drelu = dot
+        if (dw.dtype != torch.float32 or not dw.is_contiguous() or dw.numel() != n
+                or out.dtype != torch.float32 or out.numel() != m or not out.is_contiguous()):
+            raise ValueError("gemm_args: a row reduction takes f32 weights of n values and an "
+                             "f32 output of m values")
+        g.dot_w, g.dot_bias, g.dot_act = dw.data_ptr(), float(db), 1 if drelu else 0
+        g.out_ld = 0  # m values, not rows
     if workspace is not None:
         g.workspace = workspace.data_ptr()
         g.workspace_bytes = workspace.numel() * workspace.element_size()
@@ -296,7 +307,7 @@ def im2col(x, h: int, w: int, cin: int, ksize: int = 3, stride: int = 1, relu: b
 def conv2d(x, weights, bias, h: int, w: int, cin: int, cout: int, *, ksize: int = 3,
            stride: int = 1, relu_input: bool = False, act=None, residual=None, stream=None,
            implicit: bool | None = None, split_k: int = 0, out_dtype: str = "f32",
-           padded: bool = False):
+           padded: bool = False, dot=None):
     """A 3x3 (zero padding 1) or 1x1 convolution of the NHWC f32 map ``x``:
     ``weights`` from ``conv_weights``, ``bias`` f32 [cout] or None, ``act``
     "relu" on the result, ``residual`` an f32 [oh * ow][cout] map added last
@@ -319,7 +330,9 @@ def conv2d(x, weights, bias, h: int, w: int, cin: int, cout: int, *, ksize: int 
     store, for a map whose only reader is the next convolution). ``padded``:
     the result with all the weights' padded output channels (zeros), as
     [oh * ow][n_pad], which with 16 bits and n_pad = cout rounded up to 64 is
-    the next 1x1 GEMM's rows."""
+    the next 1x1 GEMM's rows. ``dot=(w, bias, relu)``: a 1x1 convolution to
+    one channel after this one, in its epilogue (``w`` f32 [cout], cout at
+    most 128 and a multiple of 32): returns f32 [oh * ow]."""
     import torch
     dt = "f16" if weights.dtype == torch.float16 else "bf16"
     rows16 = False
@@ -363,15 +376,21 @@ def conv2d(x, weights, bias, h: int, w: int, cin: int, cout: int, *, ksize: int 
         bias_pad = torch.zeros(n_pad, dtype=torch.float32, device=x.device)
         bias_pad[:cout] = bias.reshape(-1)[:cout].to(device=x.device, dtype=torch.float32)
     otd = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[out_dtype]
-    out = torch.empty((oh * ow, n_pad), dtype=otd, device=x.device)
+    if dot is not None:
+        if n_pad != cout or out_dtype != "f32":
+            raise ValueError("conv2d: the one-channel 1x1 convolution after it takes cout a "
+                             "multiple of 32 and an f32 result")
+        out = torch.empty(oh * ow, dtype=torch.float32, device=x.device)
+    else:
+        out = torch.empty((oh * ow, n_pad), dtype=otd, device=x.device)
     g = gemm_args(weights, a=cols, m=oh * ow, bias=bias_pad, act=act, residual=residual,
-                  out=out, split_k=split_k)
+                  out=out, split_k=split_k, dot=dot)
     if implicit:
         c = N.Conv3x3Args(input=x.data_ptr(), h=h, w=w, cin=cin, relu=1 if relu_input else 0)
         N.check(N.lib().bl_conv3x3(ctypes.byref(g), ctypes.byref(c), _stream_ptr(stream)))
     else:
         N.check(N.lib().bl_gemm(ctypes.byref(g), _stream_ptr(stream)))
-    return out if n_pad == cout or padded else out[:, :cout].contiguous()
+    return out if n_pad == cout or padded or dot is not None else out[:, :cout].contiguous()
 
 
 def conv_transpose_weights(hwio, cin: int, cout: int, f: int, dtype: str = "f16",

@@ -919,7 +919,7 @@ class DepthWorkload:
         self.feats = self.enc_wl.enc.features(1)
         side = cfg.grid * cfg.patch
         self.depth_host = torch.empty((side, side), dtype=torch.float32).pin_memory()
-        # ours in the head, counted from its structure (65 at DPT-S)
+        # ours in the head, counted from its structure (64 at DPT-S)
         self.launches_per_step = self.enc_wl.launches_per_step + self.dec.launches_per_frame()
         self.flops = self.enc_wl.flops
 

@@ -424,6 +424,20 @@ typedef struct bl_gemm_args {
     uint32_t stream_k;
     void* workspace;
     uint64_t workspace_bytes;
+    /* Optional row reduction (NULL = off): with dot_w set (n f32 values,
+     * 16-byte aligned), each finished output row v (after bias, act, scale,
+     * chan_scale and residual) is reduced to one f32 value,
+     * out[r] = act2(sum_c v[c] * dot_w[c] + dot_bias) summed in column order
+     * (act2 = max(x, 0) when dot_act is 1, none when 0), written to `out` as
+     * m contiguous f32 values in place of the row: a 1x1 convolution to one
+     * channel after this GEMM's convolution (the DPT head's last two,
+     * model/depth_anything_v2.rs:680-982). Requires one column tile (n at
+     * most 128; tile_n 0 or n), out_dtype BL_F32 with no split column, row
+     * groups or row offset, and no statistics, LayerNorm (prologue or
+     * epilogue), CTA pairs, K split or stream-K; else BL_ERR_UNSUPPORTED. */
+    const float* dot_w;
+    float dot_bias;
+    int32_t dot_act;
 } bl_gemm_args;
 
 int bl_gemm(const bl_gemm_args* args, void* stream);

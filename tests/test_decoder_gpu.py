@@ -440,3 +440,35 @@ def test_reassembly_in_16_bits_equals_the_f32_chain(c, f):
     assert tuple(x16.shape) == (g * g, pw.shape[0]) and tuple(x32.shape) == (g * g, c)
     assert not x16[:, c:].float().abs().sum().item()
     assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize("side,cin,cout,relu", [(518, 32, 32, True), (37, 64, 64, False),
+                                                (20, 32, 96, True), (5, 64, 128, True)])
+def test_one_channel_1x1_in_the_epilogue_matches_the_oracle(side, cin, cout, relu):
+    """The head's last two convolutions as one GEMM (bl_gemm_args.dot_w: the
+    3x3 convolution with ReLU, each finished row reduced to one channel in
+    the epilogue) against the 3x3 convolution followed by bl_conv1x1_one and
+    against the oracle's 1x1 convolution of the same map: within 1e-5
+    relative L2 (the sums run in another order); two launches give the same
+    bits."""
+    import torch
+    from beatlm_b200 import ops
+    x = torch.from_numpy(_data(97, side * side * cin)).cuda()
+    wt = ops.conv_weights(_data(98, 9 * cin * cout, 1.0 / np.sqrt(9 * cin)), 3, cin, cout)
+    b = torch.from_numpy(_data(99, cout, 0.1)).cuda()
+    w3 = _data(100, cout, 1.0 / np.sqrt(cout))
+    w3d, b3 = torch.from_numpy(w3).cuda(), 0.05
+    got = ops.conv2d(x, wt, b, side, side, cin, cout, act="relu", dot=(w3d, b3, relu))
+    again = ops.conv2d(x, wt, b, side, side, cin, cout, act="relu", dot=(w3d, b3, relu))
+    mid = ops.conv2d(x, wt, b, side, side, cin, cout, act="relu")
+    two = ops.conv1x1_one(mid, w3d, b3, side * side, cout, relu=relu)
+    torch.cuda.synchronize()
+    assert got.shape == (side * side,) and torch.equal(got, again)
+    assert _rel(got.cpu().numpy(), two.cpu().numpy()) < 1e-5
+    want = oracle.conv1x1(mid.cpu().numpy(), w3.reshape(cout, 1), np.array([b3], np.float32),
+                          side * side, cout, 1)
+    if relu:
+        want = np.maximum(want, 0.0)
+    assert _rel(got.cpu().numpy(), want) < 1e-5
+    with pytest.raises(ValueError):  # an f32 reduction only
+        ops.conv2d(x, wt, b, side, side, cin, cout, out_dtype="f16", dot=(w3d, b3, relu))
