@@ -37,3 +37,24 @@ def test_16bit_map_arguments_are_checked_before_any_launch():
     with pytest.raises(ValueError):
         ops.conv_transpose(torch.zeros((16, 64), dtype=torch.bfloat16),
                            torch.zeros((16 * 48, 64), dtype=torch.float16), None, 4, 4, 48, 48, 4)
+
+
+def test_row_reduction_arguments_are_checked_on_the_host():
+    """gemm_args(dot=...) takes f32 weights of n values and an f32 output of m
+    values; anything else is an error before any launch, and a valid one
+    sets the reduction's fields with out_ld left to the library."""
+    import pytest
+    from beatlm_b200 import ops
+    w = torch.zeros((32, 64), dtype=torch.float16)  # n = 32, k = 64
+    a = torch.zeros((10, 64), dtype=torch.float16)
+    out = torch.zeros(10, dtype=torch.float32)
+    dw = torch.ones(32)
+    g = ops.gemm_args(w, a=a, out=out, dot=(dw, 0.5, True))
+    assert g.dot_w == dw.data_ptr()
+    assert g.dot_bias == 0.5 and g.dot_act == 1 and g.out_ld == 0
+    with pytest.raises(ValueError):
+        ops.gemm_args(w, a=a, out=out, dot=(torch.ones(31), 0.0, False))
+    with pytest.raises(ValueError):
+        ops.gemm_args(w, a=a, out=torch.zeros(9), dot=(torch.ones(32), 0.0, False))
+    with pytest.raises(ValueError):
+        ops.gemm_args(w, a=a, out=out, dot=(torch.ones(32, dtype=torch.float16), 0.0, False))
