@@ -58,3 +58,34 @@ def test_row_reduction_arguments_are_checked_on_the_host():
         ops.gemm_args(w, a=a, out=torch.zeros(9), dot=(torch.ones(32), 0.0, False))
     with pytest.raises(ValueError):
         ops.gemm_args(w, a=a, out=out, dot=(torch.ones(32, dtype=torch.float16), 0.0, False))
+
+
+def test_head_launch_count_equals_the_launches_a_pass_makes(monkeypatch):
+    """One DPT-S head pass at 518 px with the library replaced by a recorder
+    (CPU tensors, nothing computed): the kernel entry points it calls are
+    exactly launches_per_frame(), the figure the bench reports."""
+    import ctypes
+    import functools
+    from beatlm_b200 import _native, ops
+    launching = {"bl_im2col", "bl_gemm", "bl_blocks_to_map", "bl_resize_bilinear",
+                 "bl_resize_bilinear_rows16", "bl_conv1x1_one", "bl_conv3x3"}
+    calls = []
+
+    class Recorder:
+        def __getattr__(self, name):
+            def call(*args):
+                calls.append(name)
+                return 0
+            return call
+
+    monkeypatch.setattr(_native, "lib", lambda: Recorder())
+    monkeypatch.setattr(ops, "_stream_ptr", lambda stream: ctypes.c_void_p(0))
+    monkeypatch.setattr(ops, "conv_weights", functools.partial(ops.conv_weights, device="cpu"))
+    cfg, dc = model.ViTConfig.small(), model.DecoderConfig()
+    d = model.Decoder(cfg, dc, model.decoder_weights_random(cfg, dc, seed=0), device="cpu")
+    feats = [torch.zeros((cfg.grid * cfg.grid, cfg.dim)) for _ in dc.neck]
+    depth = d.forward(feats)
+    side = cfg.grid * cfg.patch
+    assert tuple(depth.shape) == (side, side)
+    assert sum(1 for c in calls if c in launching) == d.launches_per_frame() == 64
+    assert "bl_conv1x1_one" not in calls  # the last 1x1 runs in the GEMM epilogue
