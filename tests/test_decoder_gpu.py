@@ -1,5 +1,6 @@
 """The DPT decoder's convolutions and resampling on the GPU (bl_im2col +
-the tcgen05 GEMM, bl_blocks_to_map, bl_resize_bilinear) against the oracle
+the tcgen05 GEMM, bl_blocks_to_map, bl_resize_bilinear and its 16-bit rows
+form, bl_conv1x1_one and the GEMM's row reduction) against the oracle
 restatement of the reference's CPU definitions
 (crates/beatlm-bench/src/reference.rs:25-230), at DPT-S shapes on the 37 x 37
 patch grid. f16 operands, f32 accumulation: relative L2 <= 1e-3 against the
